@@ -1,0 +1,306 @@
+// Torch bindings of the lora_kernel_b200 CUDA library (module lora_kernel_b200._C).
+// Each binding checks devices/dtypes/shapes, fills the C descriptor and calls
+// the launcher on the current CUDA stream; launcher errors become Python
+// RuntimeErrors.  No binding falls back to another implementation.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "lk_api.h"
+
+namespace {
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(int rc) { TORCH_CHECK(rc == 0, "lora_kernel_b200: ", lk_last_error()); }
+
+void need(const torch::Tensor& t, const char* name, c10::ScalarType dt) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+void need_contig(const torch::Tensor& t, const char* name, c10::ScalarType dt) {
+  need(t, name, dt);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+template <typename T = void>
+T* optp(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// ----------------------------------------------------------------- GEMM
+struct Operand {
+  const void* base;
+  int64_t rows, cols, ld;
+  int mn;
+};
+
+Operand classify(const torch::Tensor& x, const char* name) {
+  need(x, name, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2, name, " must be 2-D");
+  Operand o;
+  o.base = x.data_ptr();
+  const int64_t r = x.size(0), k = x.size(1);
+  if (x.stride(1) == 1 && (r == 1 || x.stride(0) >= k)) {
+    o.mn = 0;
+    o.rows = r;
+    o.cols = k;
+    o.ld = r == 1 ? ((k + 7) / 8) * 8 : x.stride(0);
+  } else if (x.stride(0) == 1 && (k == 1 || x.stride(1) >= r)) {
+    o.mn = 1;
+    o.rows = k;
+    o.cols = r;
+    o.ld = k == 1 ? ((r + 7) / 8) * 8 : x.stride(1);
+  } else {
+    TORCH_CHECK(false, name, " needs a unit stride in one dimension");
+  }
+  return o;
+}
+
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
+          c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> h, double alpha,
+          torch::Tensor status, int64_t bn) {
+  const c10::cuda::CUDAGuard g(a.device());
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm: K mismatch ", a.sizes(), " vs ", b.sizes());
+  Operand A = classify(a, "a"), B = classify(b, "b");
+  LkGemmDesc d{};
+  d.a = A.base; d.a_rows = A.rows; d.a_cols = A.cols; d.a_ld = A.ld; d.a_mn = A.mn;
+  d.b = B.base; d.b_rows = B.rows; d.b_cols = B.cols; d.b_ld = B.ld; d.b_mn = B.mn;
+  d.M = (int)a.size(0);
+  d.N = (int)b.size(0);
+  d.K = (int)a.size(1);
+  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == d.M && out.size(1) == d.N &&
+                  out.stride(1) == 1,
+              "gemm: out must be row-major [M, N]");
+  const bool f32 = epi == LK_EPI_F32 || epi == LK_EPI_F32_ACC;
+  TORCH_CHECK(out.scalar_type() == (f32 ? torch::kFloat32 : torch::kBFloat16), "gemm: out dtype");
+  d.d = out.data_ptr();
+  d.ldd = out.stride(0);
+  if (resid.has_value()) {
+    need(*resid, "resid", torch::kBFloat16);
+    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == d.N && resid->stride(1) == 1, "gemm: resid shape");
+    d.r = resid->data_ptr();
+    d.ldr = resid->stride(0);
+  }
+  if (h.has_value()) {
+    need(*h, "h", torch::kBFloat16);
+    TORCH_CHECK(h->size(0) == d.M && h->size(1) == d.N / 2 && h->stride(1) == 1, "gemm: h shape");
+    d.h = h->data_ptr();
+    d.ldh = h->stride(0);
+  }
+  d.alpha = (float)alpha;
+  d.epi = (int)epi;
+  d.bn = (int)bn;
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  check(lk_gemm(&d, stream()));
+}
+
+// ------------------------------------------------------------- RMSNorm
+void rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res, torch::Tensor gamma,
+                 torch::Tensor y, c10::optional<torch::Tensor> h_out,
+                 c10::optional<torch::Tensor> rstd, double eps) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(gamma, "gamma", torch::kBFloat16);
+  need_contig(y, "y", torch::kBFloat16);
+  LkNormFwdDesc d{};
+  d.D = (int)x.size(-1);
+  d.M = (int)(x.numel() / d.D);
+  d.x = x.data_ptr();
+  d.res = optp(res);
+  d.gamma = gamma.data_ptr();
+  d.y = y.data_ptr();
+  d.h_out = optp(h_out);
+  d.rstd = optp<float>(rstd);
+  d.eps = (float)eps;
+  check(lk_rmsnorm_fwd(&d, stream()));
+}
+
+void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::Tensor rstd,
+                 c10::optional<torch::Tensor> dres, torch::Tensor dx, torch::Tensor dgamma,
+                 torch::Tensor partial, bool accumulate) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(dy, "dy", torch::kBFloat16);
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(dx, "dx", torch::kBFloat16);
+  need_contig(rstd, "rstd", torch::kFloat32);
+  need_contig(dgamma, "dgamma", torch::kFloat32);
+  need_contig(partial, "partial", torch::kFloat32);
+  LkNormBwdDesc d{};
+  d.D = (int)x.size(-1);
+  d.M = (int)(x.numel() / d.D);
+  d.dy = dy.data_ptr();
+  d.x = x.data_ptr();
+  d.gamma = gamma.data_ptr();
+  d.rstd = rstd.data_ptr<float>();
+  d.dres = optp(dres);
+  d.dx = dx.data_ptr();
+  d.dgamma = dgamma.data_ptr<float>();
+  d.partial = partial.data_ptr<float>();
+  d.partial_rows = (int)(partial.numel() / d.D);
+  d.accumulate = accumulate ? 1 : 0;
+  check(lk_rmsnorm_bwd(&d, stream()));
+}
+
+int64_t rmsnorm_bwd_partial_rows(int64_t M) { return lk_rmsnorm_bwd_partial_rows((int)M); }
+
+// --------------------------------------------------------- RoPE / SwiGLU / emb
+void rope(torch::Tensor x, int64_t col0, int64_t nheads, int64_t Dh, torch::Tensor table,
+          c10::optional<torch::Tensor> pos, int64_t seq_len, int64_t pos_offset, bool inverse) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need(x, "x", torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "rope: x must be a row-major 2-D view");
+  need_contig(table, "table", torch::kFloat32);
+  LkRopeDesc d{};
+  d.x = x.data_ptr();
+  d.ld = x.stride(0);
+  d.T = (int)x.size(0);
+  d.col0 = (int)col0;
+  d.nheads = (int)nheads;
+  d.Dh = (int)Dh;
+  d.table = table.data_ptr();
+  if (pos.has_value()) need_contig(*pos, "pos", torch::kInt32);
+  d.pos = optp<int>(pos);
+  d.seq_len = (int)seq_len;
+  d.pos_offset = (int)pos_offset;
+  d.inverse = inverse ? 1 : 0;
+  TORCH_CHECK(col0 + nheads * Dh <= x.size(1), "rope: heads exceed the row");
+  check(lk_rope(&d, stream()));
+}
+
+void swiglu_fwd(torch::Tensor gu, torch::Tensor h) {
+  const c10::cuda::CUDAGuard g(gu.device());
+  need_contig(gu, "gu", torch::kBFloat16);
+  need_contig(h, "h", torch::kBFloat16);
+  const int F = (int)h.size(-1);
+  check(lk_swiglu_fwd(gu.data_ptr(), h.data_ptr(), (int)(h.numel() / F), F, stream()));
+}
+
+void swiglu_bwd(torch::Tensor gu, torch::Tensor dh, torch::Tensor dgu) {
+  const c10::cuda::CUDAGuard g(gu.device());
+  need_contig(gu, "gu", torch::kBFloat16);
+  need_contig(dh, "dh", torch::kBFloat16);
+  need_contig(dgu, "dgu", torch::kBFloat16);
+  const int F = (int)dh.size(-1);
+  check(lk_swiglu_bwd(gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), (int)(dh.numel() / F), F, stream()));
+}
+
+void embedding_fwd(torch::Tensor ids, torch::Tensor W, torch::Tensor out, torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(W.device());
+  need_contig(ids, "ids", torch::kInt64);
+  need_contig(W, "W", torch::kBFloat16);
+  need_contig(out, "out", torch::kBFloat16);
+  check(lk_embedding_fwd(ids.data_ptr<int64_t>(), W.data_ptr(), out.data_ptr(), (int)ids.numel(),
+                         (int)W.size(1), (int)W.size(0), status.data_ptr<int>(), stream()));
+}
+
+void embedding_bwd(torch::Tensor ids, torch::Tensor dy, torch::Tensor dW) {
+  const c10::cuda::CUDAGuard g(dW.device());
+  need_contig(ids, "ids", torch::kInt64);
+  need_contig(dy, "dy", torch::kBFloat16);
+  need_contig(dW, "dW", torch::kFloat32);
+  check(lk_embedding_bwd(ids.data_ptr<int64_t>(), dy.data_ptr(), dW.data_ptr<float>(),
+                         (int)ids.numel(), (int)dW.size(1), (int)dW.size(0), stream()));
+}
+
+// ----------------------------------------------------------- cross-entropy
+void cross_entropy(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss_acc,
+                   c10::optional<torch::Tensor> row_loss, c10::optional<torch::Tensor> scale,
+                   double scale_mul, double smoothing, double zloss, int64_t ignore_index,
+                   bool write_grad) {
+  const c10::cuda::CUDAGuard g(logits.device());
+  need(logits, "logits", torch::kBFloat16);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "cross_entropy: logits must be row-major 2-D");
+  need_contig(targets, "targets", torch::kInt64);
+  need_contig(loss_acc, "loss_acc", torch::kFloat32);
+  LkCeDesc d{};
+  d.logits = logits.data_ptr();
+  d.ld = logits.stride(0);
+  d.targets = targets.data_ptr<int64_t>();
+  d.T = (int)logits.size(0);
+  d.V = (int)logits.size(1);
+  d.loss_acc = loss_acc.data_ptr<float>();
+  d.row_loss = optp<float>(row_loss);
+  d.scale_ptr = optp<float>(scale);
+  d.scale_mul = (float)scale_mul;
+  d.smoothing = (float)smoothing;
+  d.zloss = (float)zloss;
+  d.ignore_index = ignore_index;
+  d.write_grad = write_grad ? 1 : 0;
+  check(lk_cross_entropy(&d, stream()));
+}
+
+// ------------------------------------------------------------ optimizer
+void adamw(torch::Tensor p32, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
+           c10::optional<torch::Tensor> p16, c10::optional<torch::Tensor> ema,
+           torch::Tensor chunks, torch::Tensor state, double beta1, double beta2, double eps,
+           double wd, double ema_decay, bool zero_grad) {
+  const c10::cuda::CUDAGuard g(p32.device());
+  need_contig(p32, "p32", torch::kFloat32);
+  need_contig(grad, "grad", torch::kFloat32);
+  need_contig(m, "m", torch::kFloat32);
+  need_contig(v, "v", torch::kFloat32);
+  need_contig(chunks, "chunks", torch::kInt32);
+  need_contig(state, "state", torch::kFloat32);
+  LkAdamWDesc d{};
+  d.p32 = p32.data_ptr<float>();
+  d.g = grad.data_ptr<float>();
+  d.m = m.data_ptr<float>();
+  d.v = v.data_ptr<float>();
+  d.p16 = optp(p16);
+  d.ema = optp<float>(ema);
+  d.chunks = chunks.data_ptr<int>();
+  d.nchunks = (int)(chunks.numel() / 4);
+  d.state = state.data_ptr<float>();
+  d.beta1 = (float)beta1;
+  d.beta2 = (float)beta2;
+  d.eps = (float)eps;
+  d.wd = (float)wd;
+  d.ema_decay = (float)ema_decay;
+  d.zero_grad = zero_grad ? 1 : 0;
+  check(lk_adamw(&d, stream()));
+}
+
+void grad_norm_partials(torch::Tensor grad, torch::Tensor partial) {
+  const c10::cuda::CUDAGuard g(grad.device());
+  need_contig(grad, "grad", torch::kFloat32);
+  need_contig(partial, "partial", torch::kFloat32);
+  check(lk_grad_norm_partials(grad.data_ptr<float>(), grad.numel(), partial.data_ptr<float>(),
+                              (int)partial.numel(), stream()));
+}
+
+void optimizer_finalize(torch::Tensor partial, torch::Tensor state, double max_norm, bool dynamic,
+                        double growth, double backoff, int64_t growth_interval, double min_scale) {
+  const c10::cuda::CUDAGuard g(state.device());
+  need_contig(partial, "partial", torch::kFloat32);
+  need_contig(state, "state", torch::kFloat32);
+  check(lk_optimizer_finalize(partial.data_ptr<float>(), (int)partial.numel(), state.data_ptr<float>(),
+                              (float)max_norm, dynamic ? 1 : 0, (float)growth, (float)backoff,
+                              (int)growth_interval, (float)min_scale, stream()));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "lora_kernel_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd_partial_rows", &rmsnorm_bwd_partial_rows);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("adamw", &adamw);
+  m.def("grad_norm_partials", &grad_norm_partials);
+  m.def("optimizer_finalize", &optimizer_finalize);
+  m.attr("EPI_BF16") = (int)LK_EPI_BF16;
+  m.attr("EPI_F32") = (int)LK_EPI_F32;
+  m.attr("EPI_F32_ACC") = (int)LK_EPI_F32_ACC;
+  m.attr("EPI_BF16_RESID") = (int)LK_EPI_BF16_RESID;
+  m.attr("EPI_SWIGLU") = (int)LK_EPI_SWIGLU;
+}

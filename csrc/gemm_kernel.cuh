@@ -1,0 +1,392 @@
+// K1: bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   D[M, N] = alpha * A[M, K] . B[N, K]^T   (+ fused epilogue)
+//
+// A and B are each either K-major (row-major with K contiguous) or MN-major
+// (the transpose view of a row-major [K, M] / [K, N] tensor), which covers the
+// three GEMMs of a linear layer without any transpose copies:
+//   forward  Y  = X  W^T      A K-major,  B K-major
+//   dgrad    dX = dY W        A K-major,  B MN-major (W^T view)
+//   wgrad    dW = dY^T X      A MN-major, B MN-major
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      one thread issues TMA tile loads (128B swizzle, no multicast)
+//               into a STAGES-deep shared-memory ring guarded by mbarriers;
+//   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) into a
+//               double-buffered fp32 TMEM accumulator and tcgen05.commit's the
+//               stage back to the producer;
+//   warps 2..5  the epilogue: tcgen05.ld 32 lanes x 32 columns per warp, apply
+//               the fused epilogue, store to global; overlaps the next tile's
+//               MMAs thanks to the second accumulator buffer.
+// Every wait is bounded (see common.cuh): on timeout the CTA records a status
+// code, drains its in-flight TMA copies and MMAs, frees TMEM and returns.
+//
+// Replaces the reference's scalar/cuBLAS GEMMs: GemmEngine::matmul
+// (include/core/gemm_engine.hpp:30-55), gemm_tiled_kernel
+// (include/hw/cuda_kernels.hpp:18-50) and the matmul loops of
+// src/nn/transformer_blocks.cpp (QKV :22-38, FFN :264-302, LM head :659-667).
+#pragma once
+#include "common.cuh"
+#include "host_util.h"
+#include "lk_api.h"
+
+namespace lk {
+
+enum GemmEpi : int {
+  EPI_BF16 = 0,        // D(bf16) = alpha*acc
+  EPI_F32 = 1,         // D(f32)  = alpha*acc
+  EPI_F32_ACC = 2,     // D(f32) += alpha*acc          (gradient accumulation)
+  EPI_BF16_RESID = 3,  // D(bf16) = alpha*acc + R(bf16) (residual add; D may alias R)
+  EPI_SWIGLU = 4,      // D(bf16) = acc (gate|up), H(bf16) = silu(gate) * up
+};
+
+struct GemmArgs {
+  int M, N, K;
+  void* D;
+  int64_t ldd;
+  const __nv_bfloat16* R;
+  int64_t ldr;
+  __nv_bfloat16* H;
+  int64_t ldh;
+  float alpha;
+  int* status;
+  int tiles_m, tiles_n;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;
+  static constexpr int TMEM_COLS = 2 * BN;
+};
+
+// Grouped tile order: GROUP consecutive M-tiles share each sweep over N so the
+// B panel and the A rows they use stay resident in L2.
+__device__ __forceinline__ void gemm_tile_coords(int t, int tiles_m, int tiles_n, int& tm,
+                                                 int& tn) {
+  constexpr int G = 16;
+  const int group = t / (G * tiles_n);
+  const int first_m = group * G;
+  const int gsz = min(tiles_m - first_m, G);
+  const int r = t - group * G * tiles_n;
+  tm = first_m + r % gsz;
+  tn = r / gsz;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  const uint32_t sbase = smem_u32(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * C::STAGES;
+  const uint32_t tfull0 = empty0 + 8 * C::STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain_bar = tempty0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int T = args.tiles_m * args.tiles_n;
+  const int nk = (args.K + GEMM_BK - 1) / GEMM_BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, pending = 0, parbits = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+        int tm, tn;
+        gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!bounded_wait(empty0 + 8 * s, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY,
+                            abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * s;
+          const uint32_t sa = sbase + s * C::STAGE;
+          const uint32_t sb = sa + C::A_BYTES;
+          mbar_expect_tx(fb, C::STAGE);
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, fb, kb * GEMM_BK, tm * GEMM_BM);
+          } else {
+            tma_load_2d(sa, &tmA, fb, tm * GEMM_BM, kb * GEMM_BK);
+            tma_load_2d(sa + 8192, &tmA, fb, tm * GEMM_BM + 64, kb * GEMM_BK);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, &tmB, fb, kb * GEMM_BK, tn * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + 8192 * j, &tmB, fb, tn * BN + 64 * j, kb * GEMM_BK);
+          }
+          pending |= 1u << s;
+          parbits = (parbits & ~(1u << s)) | (ph << s);
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Abort: let every copy this thread issued land before smem is released.
+        for (int i = 0; i < C::STAGES; ++i)
+          if (pending & (1u << i))
+            bounded_wait(full0 + 8 * i, (parbits >> i) & 1, args.status, LK_ERR_TIMEOUT_DRAIN,
+                         nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(GEMM_BM, BN, A_MN, B_MN);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int local = 0;
+      for (int t = blockIdx.x; t < T && ok; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!bounded_wait(tempty0 + 8 * buf, (use & 1) ^ 1, args.status, LK_ERR_TIMEOUT_ACCUM,
+                          abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!bounded_wait(full0 + 8 * s, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + s * C::STAGE;
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_desc_sw128(sa + kk * 2048, 8192, 1024)
+                                     : make_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_desc_sw128(sb + kk * 2048, 8192, 1024)
+                                     : make_desc_sw128(sb + kk * 32, 16, 1024);
+            tc_mma_f16(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * s);
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (ok) tc_commit(tfull0 + 8 * buf);
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is freed.
+      tc_commit(drain_bar);
+      bounded_wait(drain_bar, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < T; t += gridDim.x, ++local) {
+      int tm, tn;
+      gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      bool ok = bounded_wait(tfull0 + 8 * buf, use & 1, args.status, LK_ERR_TIMEOUT_ACCUM,
+                             abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int row = tm * GEMM_BM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+      const float alpha = args.alpha;
+
+      if constexpr (EPI == EPI_SWIGLU) {
+        // Tile columns [0,128) are gate j, [128,256) are up j, for j in the
+        // tile's 128-wide slice of the intermediate dimension.
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+        __nv_bfloat16* hrow = args.H + (int64_t)row * args.ldh;
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(taddr + c * 32, g);
+          tmem_ld32(taddr + BN / 2 + c * 32, u);
+          tc_wait_ld();
+          if (row_ok) {
+            const int gcol = tn * BN + c * 32;
+            const int ucol = gcol + BN / 2;
+            const int hcol = tn * (BN / 2) + c * 32;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t pg[4], pu[4], ph[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float g0 = __uint_as_float(g[v * 8 + 2 * e]) * alpha;
+                const float g1 = __uint_as_float(g[v * 8 + 2 * e + 1]) * alpha;
+                const float u0 = __uint_as_float(u[v * 8 + 2 * e]) * alpha;
+                const float u1 = __uint_as_float(u[v * 8 + 2 * e + 1]) * alpha;
+                pg[e] = pack_bf16x2(g0, g1);
+                pu[e] = pack_bf16x2(u0, u1);
+                // h from the rounded gate/up so the backward sees consistent values
+                const float2 gr = unpack_bf16x2(pg[e]);
+                const float2 ur = unpack_bf16x2(pu[e]);
+                ph[e] = pack_bf16x2(silu_f(gr.x) * ur.x, silu_f(gr.y) * ur.y);
+              }
+              if (gcol + v * 8 < args.N)
+                *reinterpret_cast<uint4*>(gu + gcol + v * 8) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
+              if (ucol + v * 8 < args.N)
+                *reinterpret_cast<uint4*>(gu + ucol + v * 8) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+              if (ucol + v * 8 < args.N)
+                *reinterpret_cast<uint4*>(hrow + hcol + v * 8) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tc_wait_ld();
+          if (!row_ok) continue;
+          const int col0 = tn * BN + c * 32;
+          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
+            __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = col0 + v * 8;
+              if (col >= args.N) break;
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]) * alpha;
+              if constexpr (EPI == EPI_BF16_RESID) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(args.R + (int64_t)row * args.ldr + col);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 x = unpack_bf16x2(rw[e]);
+                  f[2 * e] += x.x;
+                  f[2 * e + 1] += x.y;
+                }
+              }
+              *reinterpret_cast<uint4*>(drow + col) =
+                  make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                             pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            }
+          } else {
+            float* drow = reinterpret_cast<float*>(args.D) + (int64_t)row * args.ldd;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const int col = col0 + v * 4;
+              if (col >= args.N) break;
+              float4 o = make_float4(__uint_as_float(r[v * 4]) * alpha,
+                                     __uint_as_float(r[v * 4 + 1]) * alpha,
+                                     __uint_as_float(r[v * 4 + 2]) * alpha,
+                                     __uint_as_float(r[v * 4 + 3]) * alpha);
+              if constexpr (EPI == EPI_F32_ACC) {
+                const float4 old = *reinterpret_cast<const float4*>(drow + col);
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+              }
+              *reinterpret_cast<float4*>(drow + col) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  GemmArgs args{};
+  args.M = g.M;
+  args.N = g.N;
+  args.K = g.K;
+  args.D = g.d;
+  args.ldd = g.ldd;
+  args.R = reinterpret_cast<const __nv_bfloat16*>(g.r);
+  args.ldr = g.ldr;
+  args.H = reinterpret_cast<__nv_bfloat16*>(g.h);
+  args.ldh = g.ldh;
+  args.alpha = g.alpha;
+  args.status = g.status;
+  args.tiles_m = cdiv(g.M, GEMM_BM);
+  args.tiles_n = cdiv(g.N, BN);
+  CUtensorMap ta, tb;
+  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap_2d(&ta, g.a, bf, 2, g.a_rows, g.a_cols, g.a_ld, A_MN ? 64 : GEMM_BM, 64)) return -1;
+  if (!make_tmap_2d(&tb, g.b, bf, 2, g.b_rows, g.b_cols, g.b_ld, B_MN ? 64 : BN, 64)) return -1;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  static uint64_t attr_set = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << dev))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr_set |= 1ull << dev;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, args);
+  return check_launch("gemm_tc_kernel");
+}
+
+// Per-epilogue dispatchers (each defined in its own translation unit).
+int gemm_dispatch_bf16(const LkGemmDesc& g, cudaStream_t s);
+int gemm_dispatch_f32(const LkGemmDesc& g, cudaStream_t s);
+int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s);
+
+}  // namespace lk

@@ -1,0 +1,152 @@
+// Plain C ABI of the lora_kernel_b200 CUDA library.
+//
+// Every launcher takes raw device pointers, sizes and strides plus the CUDA
+// stream, enqueues its kernel(s) and returns 0 on success or -1 with a message
+// retrievable through lk_last_error().  The torch bindings (bindings.cpp)
+// validate tensors and call these; C/C++ callers can use them directly.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+const char* lk_last_error(void);
+
+// ------------------------------------------------------------------ K1 GEMM
+// D[M,N] = alpha * A[M,K] . B[N,K]^T with a fused epilogue.  Operands are
+// described by their physical row-major storage: a K-major operand X[rows,K]
+// is stored [rows, K] (x_mn = 0); an MN-major one is stored [K, rows] (x_mn = 1).
+enum LkGemmEpi {
+  LK_EPI_BF16 = 0,
+  LK_EPI_F32 = 1,
+  LK_EPI_F32_ACC = 2,
+  LK_EPI_BF16_RESID = 3,
+  LK_EPI_SWIGLU = 4,
+};
+
+typedef struct LkGemmDesc {
+  const void* a;
+  int64_t a_rows, a_cols, a_ld;
+  int a_mn;
+  const void* b;
+  int64_t b_rows, b_cols, b_ld;
+  int b_mn;
+  int M, N, K;
+  void* d;
+  int64_t ldd;
+  const void* r;  // residual (LK_EPI_BF16_RESID)
+  int64_t ldr;
+  void* h;  // silu(gate)*up output (LK_EPI_SWIGLU)
+  int64_t ldh;
+  float alpha;
+  int epi;
+  int bn;  // 0 = choose, 128 or 256
+  int* status;
+} LkGemmDesc;
+
+int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
+
+// --------------------------------------------------------------- K5 RMSNorm
+typedef struct LkNormFwdDesc {
+  const void* x;    // [M, D] bf16
+  const void* res;  // optional residual [M, D] bf16 (h = x + res)
+  const void* gamma;
+  void* y;          // [M, D] bf16
+  void* h_out;      // [M, D] bf16 when res != NULL (may alias x)
+  float* rstd;      // [M] fp32 (may be NULL)
+  int M, D;
+  float eps;
+} LkNormFwdDesc;
+
+typedef struct LkNormBwdDesc {
+  const void* dy;     // [M, D] bf16
+  const void* x;      // normalised input h [M, D] bf16
+  const void* gamma;  // [D] bf16
+  const float* rstd;  // [M]
+  const void* dres;   // optional gradient to add (may alias dx)
+  void* dx;           // [M, D] bf16
+  float* dgamma;      // [D] fp32
+  float* partial;     // scratch [partial_rows, D] fp32
+  int partial_rows;
+  int M, D;
+  int accumulate;     // dgamma += (1) or = (0)
+} LkNormBwdDesc;
+
+int lk_rmsnorm_fwd(const LkNormFwdDesc* d, cudaStream_t s);
+int lk_rmsnorm_bwd(const LkNormBwdDesc* d, cudaStream_t s);
+int lk_rmsnorm_bwd_partial_rows(int M);
+
+// ------------------------------------------------------------------ K6 RoPE
+typedef struct LkRopeDesc {
+  void* x;            // bf16 [T, ...] row pitch ld
+  int64_t ld;
+  int T, col0, nheads, Dh;
+  const void* table;  // float2 [max_pos, Dh/2] (cos, sin)
+  const int* pos;     // optional per-token positions
+  int seq_len, pos_offset;
+  int inverse;
+} LkRopeDesc;
+int lk_rope(const LkRopeDesc* d, cudaStream_t s);
+
+// ------------------------------------------------------ K7 SwiGLU, K8 embedding
+int lk_swiglu_fwd(const void* gu, void* h, int M, int F, cudaStream_t s);
+int lk_swiglu_bwd(const void* gu, const void* dh, void* dgu, int M, int F, cudaStream_t s);
+int lk_embedding_fwd(const int64_t* ids, const void* W, void* out, int T, int D, int V,
+                     int* status, cudaStream_t s);
+int lk_embedding_bwd(const int64_t* ids, const void* dy, float* dW, int T, int D, int V,
+                     cudaStream_t s);
+
+// ------------------------------------------------------------ K9 cross-entropy
+typedef struct LkCeDesc {
+  void* logits;  // [T, V] bf16, overwritten with the gradient when write_grad
+  int64_t ld;
+  const int64_t* targets;
+  int T, V;
+  float* loss_acc;        // [2]: += sum of losses, += number of counted rows
+  float* row_loss;        // optional [T]
+  const float* scale_ptr; // optional device scalar (loss scale)
+  float scale_mul;
+  float smoothing, zloss;
+  int64_t ignore_index;
+  int write_grad;
+} LkCeDesc;
+int lk_cross_entropy(const LkCeDesc* d, cudaStream_t s);
+
+// ------------------------------------------------------- K11 AdamW + K12 (1 GPU)
+// Device-resident optimizer state vector (fp32) indices.
+enum LkOptState {
+  LK_ST_LOSS_SCALE = 0,
+  LK_ST_GROWTH_TRACKER = 1,
+  LK_ST_STEP = 2,
+  LK_ST_GRAD_MULT = 3,
+  LK_ST_SKIP = 4,
+  LK_ST_LR = 5,
+  LK_ST_GRAD_NORM = 6,
+  LK_ST_NUM_SKIPPED = 7,
+  LK_ST_CONSEC_SKIPS = 8,
+  LK_ST_CLIP_COEF = 9,
+  LK_ST_SIZE = 16,
+};
+
+typedef struct LkAdamWDesc {
+  float *p32, *g, *m, *v;
+  void* p16;        // optional bf16 copy of the params
+  float* ema;       // optional EMA of the params
+  const int* chunks;  // int4 [nchunks]: start, length, wd on/off, 0
+  int nchunks;
+  const float* state;
+  float beta1, beta2, eps, wd, ema_decay;
+  int zero_grad;
+} LkAdamWDesc;
+int lk_adamw(const LkAdamWDesc* d, cudaStream_t s);
+int lk_grad_norm_partials(const float* g, int64_t n, float* partial, int nparts, cudaStream_t s);
+int lk_optimizer_finalize(const float* partial, int nparts, float* state, float max_norm,
+                          int dynamic, float growth, float backoff, int growth_interval,
+                          float min_scale, cudaStream_t s);
+
+#ifdef __cplusplus
+}
+#endif

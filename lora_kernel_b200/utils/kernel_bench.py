@@ -1,0 +1,121 @@
+"""Kernel micro-benchmarks: device-timed (CUDA events) throughput of the
+sm_100a kernels next to the library equivalent (cuBLAS via torch.matmul),
+reported against the measured peaks of this machine when they are available.
+
+    python -m lora_kernel_b200.utils.kernel_bench [--only gemm,norm,...]
+
+Each case runs warm-up iterations, then times `iters` launches between two
+events with an L2 flush (a 256 MiB write, larger than the 126 MB L2) before
+each timed launch, and prints one JSON line per case.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+_flush = None
+
+
+def _l2_flush():
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _flush.zero_()
+
+
+def time_fn(fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
+    """Median milliseconds per call (CUDA events on the current stream)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush:
+            _l2_flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def bench_gemm(shapes, iters):
+    from lora_kernel_b200.ops.gemm import gemm
+    pk = peaks()
+    for (M, N, K, layout) in shapes:
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        if layout == "tn":
+            b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+            A, B = a, b
+        elif layout == "dgrad":
+            b = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+            A, B = a, b.t()
+        else:  # wgrad: A = X1^T (MN-major), B = X2^T
+            a = torch.randn(K, M, device="cuda").to(torch.bfloat16)
+            b = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+            A, B = a.t(), b.t()
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        t_lk = time_fn(lambda: gemm(A, B, out), iters)
+        t_cb = time_fn(lambda: torch.matmul(A, B.t(), out=out), iters)
+        fl = 2.0 * M * N * K
+        print(json.dumps({"kernel": "gemm_tc", "M": M, "N": N, "K": K, "layout": layout,
+                          "ms": round(t_lk, 4), "tflops": round(fl / t_lk / 1e9, 1),
+                          "cublas_ms": round(t_cb, 4), "cublas_tflops": round(fl / t_cb / 1e9, 1),
+                          "frac_of_peak": round(fl / t_lk / 1e9 / pk["bf16_tflops"], 3),
+                          "peak_src": pk["src"]}), flush=True)
+
+
+def bench_norm(iters):
+    from lora_kernel_b200.ops.norm import rmsnorm_fwd
+    pk = peaks()
+    for (M, D) in [(8192, 2048), (16384, 4096)]:
+        x = torch.randn(M, D, device="cuda").to(torch.bfloat16)
+        g = torch.ones(D, device="cuda").to(torch.bfloat16)
+        y = torch.empty_like(x)
+        r = torch.empty(M, device="cuda")
+        t = time_fn(lambda: rmsnorm_fwd(x, g, 1e-5, y=y, rstd=r), iters)
+        by = 2 * M * D * 2
+        print(json.dumps({"kernel": "rmsnorm_fwd", "M": M, "D": D, "ms": round(t, 4),
+                          "gbs": round(by / t / 1e6, 1),
+                          "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,norm")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--small", action="store_true", help="one small GEMM (for profiling)")
+    args = ap.parse_args()
+    which = set(args.only.split(","))
+    if "gemm" in which:
+        if args.small:
+            shapes = [(4096, 4096, 4096, "tn")]
+        else:
+            shapes = [(8192, 8192, 8192, "tn"), (8192, 8192, 8192, "dgrad"),
+                      (8192, 8192, 8192, "wgrad"),
+                      (8192, 2560, 2048, "tn"), (8192, 11264, 2048, "tn"),
+                      (8192, 2048, 5632, "tn"), (8192, 32000, 2048, "tn"),
+                      (8192, 2048, 11264, "dgrad"), (11264, 2048, 8192, "wgrad")]
+        bench_gemm(shapes, args.iters)
+    if "norm" in which:
+        bench_norm(args.iters)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,23 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+    config.addinivalue_line("markers", "multigpu: needs 2 or more GPUs")
+    config.addinivalue_line("markers", "slow: long-running test")
+
+
+def pytest_collection_modifyitems(config, items):
+    import torch
+    have_gpu = torch.cuda.is_available()
+    skip = pytest.mark.skip(reason="no CUDA GPU")
+    for item in items:
+        if "gpu" in item.keywords and not have_gpu:
+            item.add_marker(skip)
