@@ -1,0 +1,467 @@
+// K4: flash-attention backward on tcgen05 (causal / full / sliding window, GQA,
+// head_dim 64/128).
+//
+// One CTA per (128-key tile j, kv head g, batch b).  It loops over every q head
+// of the GQA group and every q tile i that can see key tile j, so dK_j and dV_j
+// accumulate in TMEM for the whole group and are written once (no atomics):
+//
+//   S^T  = K_j Q_i^T            (tcgen05, M = keys, N = queries)
+//   dP^T = V_j dO_i^T
+//   P^T  = exp(S^T * scale - LSE),  dS^T = P^T (dP^T - D) * scale   (registers)
+//   dV  += P^T dO_i,  dK += dS^T Q_i,  dQ_i = dS K_j                 (tcgen05)
+//
+// dQ_i partials are added into an fp32 accumulator with vector reductions
+// (red.global.add.v4.f32) and converted to bf16 by a final kernel.  The same
+// 128B-swizzled shared-memory tiles serve as K-major operands (S^T, dP^T) and
+// as MN-major operands (dV, dK, dQ), so nothing is transposed in memory.
+// D = rowsum(dO * O) is computed by a small pre-pass.
+//
+// Replaces the reference's MultiHeadAttention::backward
+// (src/nn/transformer_blocks.cpp:156-207) and softmax_backward_inplace
+// (include/core/tensor.hpp:380-392).
+#include "common.cuh"
+#include "host_util.h"
+#include "lk_api.h"
+
+namespace lk {
+
+struct AttnBwdArgs {
+  int B, S, Hq, Hkv;
+  int causal, window;
+  float sl2;    // scale * log2(e)
+  float scale;  // softmax scale
+  const float* lse;   // [B, Hq, S] natural log
+  const float* Dvec;  // [B, Hq, S]
+  float* dq_acc;      // [B*S, Hq*Dh] fp32
+  __nv_bfloat16* dqkv;
+  int64_t ld_dqkv;
+  int* status;
+  int n_tiles;
+};
+
+__device__ __forceinline__ uint32_t sw128_off_b(int r, int u) {
+  return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+template <int DH>
+struct BwdCfg {
+  static constexpr int QB = 128 * DH * 2;
+  static constexpr int STAGES = DH == 64 ? 2 : 1;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = QB;
+  static constexpr int OFF_Q = 2 * QB;
+  static constexpr int OFF_DO = OFF_Q + STAGES * QB;
+  static constexpr int OFF_P = OFF_DO + STAGES * QB;
+  static constexpr int OFF_DS = OFF_P + 32768;
+  static constexpr int OFF_BAR = OFF_DS + 32768;
+  static constexpr int SMEM = OFF_BAR + 256;
+  static constexpr int TMEM_COLS = 512;
+};
+
+__device__ __forceinline__ void q_range(const AttnBwdArgs& a, int j, int& i0, int& i1) {
+  const int n = a.n_tiles;
+  i0 = a.causal ? j : 0;
+  i1 = n;
+  if (a.window > 0) {
+    // query q sees keys in (q - window, q]; key tile j is seen by q < j*128 + 127 + window
+    const int qmax = j * 128 + 127 + a.window - 1;
+    i1 = min(n, qmax / 128 + 1);
+  }
+}
+
+template <int DH>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    const AttnBwdArgs args) {
+  using C = BwdCfg<DH>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023) {
+    if (threadIdx.x == 0) atomicCAS(args.status, 0, LK_ERR_BAD_INDEX);
+    return;
+  }
+  const uint32_t bar = sbase + C::OFF_BAR;
+  const uint32_t kv_full = bar, qd_full = bar + 8, qd_empty = bar + 24, sdp_full = bar + 40,
+                 ds_ready = bar + 48, dq_full = bar + 56, dq_free = bar + 64, drain = bar + 72;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 132);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int group = args.Hq / args.Hkv;
+  const int S = args.S;
+  const int row0 = b * S;
+  int i0, i1;
+  q_range(args, j, i0, i1);
+  const int nq = max(0, i1 - i0);
+  const int n_it = group * nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qd_full + 8 * s, 1);
+      mbar_init(qd_empty + 8 * s, 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(ds_ready, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_do);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + DH;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA
+      mbar_expect_tx(kv_full, 2 * C::QB);
+#pragma unroll
+      for (int c = 0; c < DH / 64; ++c) {
+        tma_load_2d(sbase + C::OFF_K + c * 16384, &tm_qkv, kv_full, (args.Hq + g) * DH + c * 64, row0 + j * 128);
+        tma_load_2d(sbase + C::OFF_V + c * 16384, &tm_qkv, kv_full,
+                    (args.Hq + args.Hkv + g) * DH + c * 64, row0 + j * 128);
+      }
+      uint32_t pending = 0, parbits = 0;
+      bool ok = true;
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int h = g * group + it / nq;
+        const int i = i0 + it % nq;
+        const int st = it % C::STAGES;
+        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
+        if (!bounded_wait(qd_empty + 8 * st, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = qd_full + 8 * st;
+        mbar_expect_tx(fb, 2 * C::QB);
+#pragma unroll
+        for (int c = 0; c < DH / 64; ++c) {
+          tma_load_2d(sbase + C::OFF_Q + st * C::QB + c * 16384, &tm_qkv, fb, h * DH + c * 64, row0 + i * 128);
+          tma_load_2d(sbase + C::OFF_DO + st * C::QB + c * 16384, &tm_do, fb, h * DH + c * 64, row0 + i * 128);
+        }
+        pending |= 1u << st;
+        parbits = (parbits & ~(1u << st)) | (ph << st);
+      }
+      if (!ok) {
+        bounded_wait(kv_full, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+        for (int s2 = 0; s2 < C::STAGES; ++s2)
+          if (pending & (1u << s2))
+            bounded_wait(qd_full + 8 * s2, (parbits >> s2) & 1, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA
+      constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);   // K Q^T, V dO^T
+      constexpr uint32_t id_kv = make_idesc_bf16(128, DH, false, true);    // P^T dO, dS^T Q
+      constexpr uint32_t id_q = make_idesc_bf16(128, DH, true, true);      // dS K
+      const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
+      const uint32_t sp = sbase + C::OFF_P, sds = sbase + C::OFF_DS;
+      bool ok = bounded_wait(kv_full, 0, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % C::STAGES;
+        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
+        if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
+            (it > 0 && !bounded_wait(dq_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sq = sbase + C::OFF_Q + st * C::QB, sdo = sbase + C::OFF_DO + st * C::QB;
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          tc_mma_f16(tS, make_desc_sw128(sk + off, 16, 1024), make_desc_sw128(sq + off, 16, 1024), id_s,
+                     kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          tc_mma_f16(tdP, make_desc_sw128(sv + off, 16, 1024), make_desc_sw128(sdo + off, 16, 1024), id_s,
+                     kk > 0 ? 1u : 0u);
+        }
+        tc_commit(sdp_full);
+        if (!bounded_wait(ds_ready, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 queries
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          tc_mma_f16(tdV, make_desc_sw128(sp + aoff, 16, 1024), make_desc_sw128(sdo + kk * 2048, 16384, 1024),
+                     id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16(tdK, make_desc_sw128(sds + aoff, 16, 1024), make_desc_sw128(sq + kk * 2048, 16384, 1024),
+                     id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 keys
+          tc_mma_f16(tS, make_desc_sw128(sds + kk * 2048, 16384, 1024),
+                     make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(dq_full);
+        tc_commit(qd_empty + 8 * st);
+      }
+      tc_commit(drain);
+      bounded_wait(drain, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+    }
+  } else {
+    // ------------------------------------------------- softmax backward
+    const int quarter = warp & 3;
+    const int kr = quarter * 32 + lane;  // key row (S^T/dP^T/dK/dV lane) and q row (dQ lane)
+    const int key = j * 128 + kr;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* sP = smem + C::OFF_P;
+    uint8_t* sDS = smem + C::OFF_DS;
+    const int ldq = args.Hq * DH;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = g * group + it / nq;
+      const int i = i0 + it % nq;
+      bool w_ok = bounded_wait(sdp_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
+      const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
+      const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
+                             args.window > 0;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + lane_off + c * 32, sv);
+        tmem_ld32(tdP + lane_off + c * 32, dv);
+        tc_wait_ld();
+        uint32_t pp[16], pd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const int qi = c * 32 + e;  // query index within the tile
+          float4 L = make_float4(0.f, 0.f, 0.f, 0.f), Dd = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (i * 128 + qi + 3 < S && (S & 3) == 0) {
+            L = *reinterpret_cast<const float4*>(lse_row + qi);
+            Dd = *reinterpret_cast<const float4*>(d_row + qi);
+          } else {
+            float* Lp = &L.x;
+            float* Dp = &Dd.x;
+            for (int t = 0; t < 4; ++t)
+              if (i * 128 + qi + t < S) {
+                Lp[t] = lse_row[qi + t];
+                Dp[t] = d_row[qi + t];
+              }
+          }
+          const float Ls[4] = {L.x, L.y, L.z, L.w};
+          const float Ds[4] = {Dd.x, Dd.y, Dd.z, Dd.w};
+          float p[4], ds[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int q = i * 128 + qi + t;
+            p[t] = exp2f(__uint_as_float(sv[e + t]) * args.sl2 - Ls[t] * 1.4426950408889634f);
+            if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
+                              (args.window > 0 && key <= q - args.window)))
+              p[t] = 0.f;
+          }
+          // round P to bf16 first so dS uses the P the forward's PV used
+          const uint32_t p01 = pack_bf16x2(p[0], p[1]), p23 = pack_bf16x2(p[2], p[3]);
+          const float2 r01 = unpack_bf16x2(p01), r23 = unpack_bf16x2(p23);
+          p[0] = r01.x; p[1] = r01.y; p[2] = r23.x; p[3] = r23.y;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) ds[t] = p[t] * (__uint_as_float(dv[e + t]) - Ds[t]) * args.scale;
+          pp[e / 2] = p01;
+          pp[e / 2 + 1] = p23;
+          pd[e / 2] = pack_bf16x2(ds[0], ds[1]);
+          pd[e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = sw128_off_b(kr, c * 4 + u);
+          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+          *reinterpret_cast<uint4*>(sDS + off) = make_uint4(pd[4 * u], pd[4 * u + 1], pd[4 * u + 2], pd[4 * u + 3]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_ready);
+      // dQ tile (lane = query row) -> fp32 accumulator
+      w_ok = bounded_wait(dq_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q = i * 128 + kr;
+      float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + h * DH;
+#pragma unroll 1
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_off + c * 32, v);
+        tc_wait_ld();
+        if (q < S) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(dqrow + c * 32 + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                       __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    // dK, dV (lane = key row) -> bf16 into dqkv
+    // tcgen05.ld is warp-collective: every lane loads, only in-range keys store.
+    if (__all_sync(0xffffffffu, ok) && n_it > 0) {
+      tc_fence_after();
+      __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
+      __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
+#pragma unroll 1
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t a[32], bb[32];
+        tmem_ld32(tdK + lane_off + c * 32, a);
+        tmem_ld32(tdV + lane_off + c * 32, bb);
+        tc_wait_ld();
+        if (key >= S) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          *reinterpret_cast<uint4*>(dk + c * 32 + e) = make_uint4(
+              pack_bf16x2(__uint_as_float(a[e]), __uint_as_float(a[e + 1])),
+              pack_bf16x2(__uint_as_float(a[e + 2]), __uint_as_float(a[e + 3])),
+              pack_bf16x2(__uint_as_float(a[e + 4]), __uint_as_float(a[e + 5])),
+              pack_bf16x2(__uint_as_float(a[e + 6]), __uint_as_float(a[e + 7])));
+          *reinterpret_cast<uint4*>(dvp + c * 32 + e) = make_uint4(
+              pack_bf16x2(__uint_as_float(bb[e]), __uint_as_float(bb[e + 1])),
+              pack_bf16x2(__uint_as_float(bb[e + 2]), __uint_as_float(bb[e + 3])),
+              pack_bf16x2(__uint_as_float(bb[e + 4]), __uint_as_float(bb[e + 5])),
+              pack_bf16x2(__uint_as_float(bb[e + 6]), __uint_as_float(bb[e + 7])));
+        }
+      }
+    } else if (ok && n_it == 0 && key < S) {
+      // no query sees this key tile: its gradients are zero
+      __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
+      __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
+      for (int e = 0; e < DH; e += 8) {
+        *reinterpret_cast<uint4*>(dk + e) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dvp + e) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// D[b, h, q] = sum_d dO[q, h, d] * O[q, h, d]   (one warp per (row, head))
+template <int DH>
+__global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
+                                    const __nv_bfloat16* __restrict__ dout, int64_t lddo,
+                                    float* __restrict__ Dvec, int B, int S, int Hq) {
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)B * S * Hq;
+  if (w >= total) return;
+  const int h = (int)(w % Hq);
+  const int64_t row = w / Hq;  // b*S + s
+  const __nv_bfloat16* op = o + row * ldo + h * DH;
+  const __nv_bfloat16* dp = dout + row * lddo + h * DH;
+  float s = 0.f;
+  for (int d = lane * 2; d < DH; d += 64) {
+    const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(op + d));
+    const float2 c = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dp + d));
+    s += a.x * c.x + a.y * c.y;
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int bb = (int)(row / S), q = (int)(row % S);
+    Dvec[((int64_t)bb * Hq + h) * S + q] = s;
+  }
+}
+
+__global__ void dq_convert_kernel(const float* __restrict__ acc, int64_t T, int ncols,
+                                  __nv_bfloat16* __restrict__ dqkv, int64_t ld) {
+  const int64_t n4 = T * ncols / 4;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n4;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = idx * 4;
+    const int64_t row = e / ncols;
+    const int col = (int)(e % ncols);
+    const float4 v = *reinterpret_cast<const float4*>(acc + e);
+    *reinterpret_cast<uint2*>(dqkv + row * ld + col) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+template <int DH>
+static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
+  using C = BwdCfg<DH>;
+  const int64_t T = (int64_t)d.B * d.S;
+  const int ncols = (d.Hq + 2 * d.Hkv) * DH;
+  // D = rowsum(dO * O)
+  {
+    const int64_t warps = T * d.Hq;
+    attn_bwd_dot_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
+        (const __nv_bfloat16*)d.o, d.ld_o, (const __nv_bfloat16*)d.dout, d.ld_do, d.dvec, d.B, d.S, d.Hq);
+    if (check_launch("attn_bwd_dot")) return -1;
+  }
+  if (cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * T * d.Hq * DH, s) != cudaSuccess)
+    return fail("attention_bwd: memset failed");
+  CUtensorMap tq, tdo;
+  if (!make_tmap_2d(&tq, d.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, ncols, d.ld_qkv, 128, 64)) return -1;
+  if (!make_tmap_2d(&tdo, d.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (int64_t)d.Hq * DH, d.ld_do, 128, 64))
+    return -1;
+  AttnBwdArgs a{};
+  a.B = d.B;
+  a.S = d.S;
+  a.Hq = d.Hq;
+  a.Hkv = d.Hkv;
+  a.causal = d.causal;
+  a.window = d.window;
+  a.scale = d.scale;
+  a.sl2 = d.scale * 1.4426950408889634f;
+  a.lse = d.lse;
+  a.Dvec = d.dvec;
+  a.dq_acc = d.dq_acc;
+  a.dqkv = (__nv_bfloat16*)d.dqkv;
+  a.ld_dqkv = d.ld_dqkv;
+  a.status = d.status;
+  a.n_tiles = cdiv(d.S, 128);
+  auto k = attn_bwd_kernel<DH>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  dim3 grid(a.n_tiles, d.Hkv, d.B);
+  k<<<grid, 192, C::SMEM, s>>>(tq, tdo, a);
+  if (check_launch("attn_bwd")) return -1;
+  const int64_t n4 = T * d.Hq * DH / 4;
+  int grid_c = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms() * 16);
+  dq_convert_kernel<<<grid_c, 256, 0, s>>>(d.dq_acc, T, d.Hq * DH, (__nv_bfloat16*)d.dqkv, d.ld_dqkv);
+  return check_launch("attn_dq_convert");
+}
+
+}  // namespace lk
+
+extern "C" int lk_attention_bwd(const LkAttnBwdDesc* d, cudaStream_t s) {
+  using namespace lk;
+  LK_REQUIRE(d->Hq % d->Hkv == 0, "attention_bwd: Hq must be a multiple of Hkv");
+  LK_REQUIRE(d->ld_qkv % 8 == 0 && d->ld_do % 8 == 0 && d->ld_dqkv % 8 == 0 && d->ld_o % 8 == 0,
+             "attention_bwd: row pitches must be multiples of 8");
+  if (d->B == 0 || d->S == 0) return 0;
+  if (d->Dh == 64) return launch_bwd<64>(*d, s);
+  if (d->Dh == 128) return launch_bwd<128>(*d, s);
+  return fail("attention_bwd: head_dim must be 64 or 128");
+}

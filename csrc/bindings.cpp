@@ -281,11 +281,70 @@ void optimizer_finalize(torch::Tensor partial, torch::Tensor state, double max_n
                               (int)growth_interval, (float)min_scale, stream()));
 }
 
+// ------------------------------------------------------------- attention
+void attention_fwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
+                   int64_t Hq, int64_t Hkv, int64_t Dh, bool causal, int64_t window, double scale,
+                   torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(qkv.device());
+  need(qkv, "qkv", torch::kBFloat16);
+  need(o, "o", torch::kBFloat16);
+  need_contig(lse, "lse", torch::kFloat32);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(0) == B * S &&
+                  qkv.size(1) >= (Hq + 2 * Hkv) * Dh, "attention: bad qkv shape");
+  TORCH_CHECK(o.dim() == 2 && o.stride(1) == 1 && o.size(0) == B * S && o.size(1) >= Hq * Dh,
+              "attention: bad o shape");
+  TORCH_CHECK(lse.numel() >= B * Hq * S, "attention: lse too small");
+  LkAttnDesc d{};
+  d.qkv = qkv.data_ptr();
+  d.ld_qkv = qkv.stride(0);
+  d.o = o.data_ptr();
+  d.ld_o = o.stride(0);
+  d.lse = lse.data_ptr<float>();
+  d.B = (int)B; d.S = (int)S; d.Hq = (int)Hq; d.Hkv = (int)Hkv; d.Dh = (int)Dh;
+  d.causal = causal ? 1 : 0;
+  d.window = (int)window;
+  d.scale = (float)scale;
+  d.status = status.data_ptr<int>();
+  check(lk_attention_fwd(&d, stream()));
+}
+
+void attention_bwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch::Tensor lse,
+                   torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor dvec, int64_t B,
+                   int64_t S, int64_t Hq, int64_t Hkv, int64_t Dh, bool causal, int64_t window,
+                   double scale, torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(qkv.device());
+  need(qkv, "qkv", torch::kBFloat16);
+  need(o, "o", torch::kBFloat16);
+  need(dout, "dout", torch::kBFloat16);
+  need(dqkv, "dqkv", torch::kBFloat16);
+  need_contig(lse, "lse", torch::kFloat32);
+  need_contig(dq_acc, "dq_acc", torch::kFloat32);
+  need_contig(dvec, "dvec", torch::kFloat32);
+  TORCH_CHECK(dq_acc.numel() >= B * S * Hq * Dh && dvec.numel() >= B * Hq * S, "attention_bwd: scratch too small");
+  for (auto* t : {&qkv, &o, &dout, &dqkv})
+    TORCH_CHECK(t->dim() == 2 && t->stride(1) == 1 && t->size(0) == B * S, "attention_bwd: bad 2-D operand");
+  LkAttnBwdDesc d{};
+  d.qkv = qkv.data_ptr(); d.ld_qkv = qkv.stride(0);
+  d.o = o.data_ptr(); d.ld_o = o.stride(0);
+  d.dout = dout.data_ptr(); d.ld_do = dout.stride(0);
+  d.lse = lse.data_ptr<float>();
+  d.dqkv = dqkv.data_ptr(); d.ld_dqkv = dqkv.stride(0);
+  d.dq_acc = dq_acc.data_ptr<float>();
+  d.dvec = dvec.data_ptr<float>();
+  d.B = (int)B; d.S = (int)S; d.Hq = (int)Hq; d.Hkv = (int)Hkv; d.Dh = (int)Dh;
+  d.causal = causal ? 1 : 0;
+  d.window = (int)window;
+  d.scale = (float)scale;
+  d.status = status.data_ptr<int>();
+  check(lk_attention_bwd(&d, stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lora_kernel_b200 sm_100a kernels";
   m.def("gemm", &gemm);
+  m.def("launch_count", []() { return (int64_t)lk_launch_count(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rmsnorm_bwd_partial_rows", &rmsnorm_bwd_partial_rows);
@@ -298,6 +357,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw);
   m.def("grad_norm_partials", &grad_norm_partials);
   m.def("optimizer_finalize", &optimizer_finalize);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
   m.attr("EPI_BF16") = (int)LK_EPI_BF16;
   m.attr("EPI_F32") = (int)LK_EPI_F32;
   m.attr("EPI_F32_ACC") = (int)LK_EPI_F32_ACC;

@@ -5,6 +5,8 @@
 
 extern "C" const char* lk_last_error(void) { return lk::last_error().c_str(); }
 
+extern "C" unsigned long long lk_launch_count(void) { return lk::launch_counter().load(); }
+
 extern "C" int lk_gemm(const LkGemmDesc* g, cudaStream_t stream) {
   using namespace lk;
   LK_REQUIRE(g != nullptr, "lk_gemm: null descriptor");

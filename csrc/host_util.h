@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -28,7 +29,14 @@ inline int fail(const char* what) {
     if (!(cond)) return ::lk::fail(msg); \
   } while (0)
 
+// Number of kernels this library has enqueued (all devices, all threads).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
 inline int check_launch(const char* name) {
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     last_error() = std::string(name) + ": " + cudaGetErrorString(e);

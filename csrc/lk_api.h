@@ -14,6 +14,8 @@ extern "C" {
 #endif
 
 const char* lk_last_error(void);
+// Kernels enqueued by this library so far (for launch accounting).
+unsigned long long lk_launch_count(void);
 
 // ------------------------------------------------------------------ K1 GEMM
 // D[M,N] = alpha * A[M,K] . B[N,K]^T with a fused epilogue.  Operands are
@@ -146,6 +148,39 @@ int lk_grad_norm_partials(const float* g, int64_t n, float* partial, int nparts,
 int lk_optimizer_finalize(const float* partial, int nparts, float* state, float max_norm,
                           int dynamic, float growth, float backoff, int growth_interval,
                           float min_scale, cudaStream_t s);
+
+// ------------------------------------------------------- K3/K4 flash attention
+typedef struct LkAttnDesc {
+  const void* qkv;  // [B*S, (Hq+2Hkv)*Dh] bf16, row pitch ld_qkv
+  int64_t ld_qkv;
+  void* o;          // [B*S, Hq*Dh] bf16, row pitch ld_o
+  int64_t ld_o;
+  float* lse;       // [B, Hq, S] natural-log LSE
+  int B, S, Hq, Hkv, Dh;
+  int causal, window;
+  float scale;
+  int* status;
+} LkAttnDesc;
+int lk_attention_fwd(const LkAttnDesc* d, cudaStream_t s);
+
+typedef struct LkAttnBwdDesc {
+  const void* qkv;
+  int64_t ld_qkv;
+  const void* o;
+  int64_t ld_o;
+  const void* dout;  // [B*S, Hq*Dh]
+  int64_t ld_do;
+  const float* lse;
+  void* dqkv;        // [B*S, (Hq+2Hkv)*Dh] bf16 output
+  int64_t ld_dqkv;
+  float* dq_acc;     // scratch [B*S, Hq*Dh] fp32
+  float* dvec;       // scratch [B, Hq, S] fp32
+  int B, S, Hq, Hkv, Dh;
+  int causal, window;
+  float scale;
+  int* status;
+} LkAttnBwdDesc;
+int lk_attention_bwd(const LkAttnBwdDesc* d, cudaStream_t s);
 
 #ifdef __cplusplus
 }

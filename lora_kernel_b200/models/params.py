@@ -1,0 +1,207 @@
+"""Flat parameter storage for the Llama decoder.
+
+All weights live in one bf16 buffer (and, for training, one fp32 master buffer,
+one fp32 gradient buffer and the AdamW moments with the same layout); every
+named parameter is a view.  This makes the optimizer one kernel over one
+buffer, lets the weight-gradient GEMMs accumulate straight into the fp32
+gradient views, and makes ZeRO sharding a slice of a flat range.
+
+Layout: parameters are grouped per layer ("embed", "layers.{i}", "head") so a
+ZeRO-3 rank can gather one layer at a time; every tensor starts on a 64-element
+(128-byte) boundary so TMA descriptors over any view are aligned.
+
+Internal orientation is [out, in] (y = x W^T); Wq/Wk/Wv are fused row-wise into
+`wqkv` and Wgate/Wup are interleaved in blocks of 128 rows into `wgu` (the
+gate|up GEMM's SwiGLU epilogue layout).  `to_reference_state_dict` converts to
+the reference's checkpoint names and [in, out] orientation
+(include/io/serialization.hpp:13-44).
+"""
+from __future__ import annotations
+
+import math
+from collections import OrderedDict
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from ..config import TransformerConfig
+
+ALIGN = 64
+
+
+@dataclass
+class ParamSpec:
+    name: str
+    shape: Tuple[int, ...]
+    offset: int
+    group: str
+    decay: bool
+    init: str  # "normal" | "ones" | "zeros"
+
+    @property
+    def numel(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+
+def _round(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+def build_layout(cfg: TransformerConfig) -> Tuple[List[ParamSpec], Dict[str, Tuple[int, int]], int]:
+    """Returns (specs, group ranges {group: (start, end)}, total numel)."""
+    D, V, F = cfg.hidden_dim, cfg.vocab_size, cfg.ff_dim_padded
+    specs: List[ParamSpec] = []
+    groups: Dict[str, Tuple[int, int]] = OrderedDict()
+    off = 0
+
+    def add(name, shape, group, decay, init):
+        nonlocal off
+        s = ParamSpec(name, tuple(shape), off, group, decay, init)
+        specs.append(s)
+        off += _round(s.numel)
+
+    def group(name, items):
+        nonlocal off
+        start = off
+        for it in items:
+            add(*it[:2], name, *it[2:])
+        off = _round(off)
+        groups[name] = (start, off)
+
+    group("embed", [("embed", (V, D), True, "normal")])
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        group(f"layers.{i}", [
+            (p + "attn_norm", (D,), False, "ones"),
+            (p + "wqkv", (cfg.qkv_dim, D), True, "normal"),
+            (p + "wo", (D, cfg.q_dim), True, "normal"),
+            (p + "ffn_norm", (D,), False, "ones"),
+            (p + "wgu", (2 * F, D), True, "normal"),
+            (p + "wdown", (D, F), True, "normal"),
+        ])
+    head = [("final_norm", (D,), False, "ones")]
+    if not cfg.tie_embeddings:
+        head.append(("lm_head", (V, D), True, "normal"))
+    group("head", head)
+    return specs, groups, off
+
+
+class FlatParams:
+    """A flat buffer plus named views following `build_layout(cfg)`."""
+
+    def __init__(self, cfg: TransformerConfig, device, dtype=torch.bfloat16,
+                 buffer: Optional[torch.Tensor] = None):
+        self.cfg = cfg
+        self.specs, self.groups, self.numel = build_layout(cfg)
+        self.by_name = {s.name: s for s in self.specs}
+        if buffer is None:
+            buffer = torch.zeros(self.numel, dtype=dtype, device=device)
+        assert buffer.numel() == self.numel
+        self.flat = buffer
+        self.views: Dict[str, torch.Tensor] = {
+            s.name: self.flat[s.offset:s.offset + s.numel].view(s.shape) for s in self.specs}
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        if name == "lm_head" and self.cfg.tie_embeddings:
+            return self.views["embed"]
+        return self.views[name]
+
+    def like(self, dtype=torch.float32, device=None) -> "FlatParams":
+        return FlatParams(self.cfg, device or self.flat.device, dtype,
+                          torch.zeros(self.numel, dtype=dtype, device=device or self.flat.device))
+
+    def segments(self, decay_norms: bool = False, lo: int = 0, hi: Optional[int] = None):
+        """(start, length, decay) of every parameter clipped to [lo, hi), relative to lo."""
+        hi = self.numel if hi is None else hi
+        out = []
+        for s in self.specs:
+            a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
+            if a < b:
+                out.append((a - lo, b - a, s.decay or decay_norms))
+        return out
+
+    # ------------------------------------------------------------------ init
+    def init_(self, seed: int, std: float) -> None:
+        """Deterministic N(0, std) for matrices, ones for norms; the padded FFN
+        rows/columns are zero so the padding is exact."""
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        cfg = self.cfg
+        F, Fp = cfg.ff_dim, cfg.ff_dim_padded
+        for s in self.specs:
+            v = self.views[s.name]
+            if s.init == "ones":
+                v.fill_(1.0)
+            elif s.init == "zeros":
+                v.zero_()
+            else:
+                t = torch.empty(s.shape, dtype=torch.float32)
+                t.normal_(0.0, std, generator=g)
+                if s.name.endswith("wgu") and Fp != F:
+                    blk = t.view(Fp // 128, 2, 128, -1)
+                    mask = torch.arange(Fp).view(Fp // 128, 128) >= F
+                    blk[:, 0][mask] = 0.0
+                    blk[:, 1][mask] = 0.0
+                if s.name.endswith("wdown") and Fp != F:
+                    t[:, F:] = 0.0
+                v.copy_(t.to(v.dtype))
+
+    # ------------------------------------------------------- checkpoint names
+    def to_reference_state_dict(self) -> "OrderedDict[str, torch.Tensor]":
+        """Reference tensor names, [in, out] orientation, unpadded FFN."""
+        cfg = self.cfg
+        q, kv, F = cfg.q_dim, cfg.kv_dim, cfg.ff_dim
+        out: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+        out["token_embedding.weight"] = self.views["embed"]
+        for i in range(cfg.num_layers):
+            p, r = f"layers.{i}.", f"blocks.{i}."
+            wqkv = self.views[p + "wqkv"]
+            out[r + "attn.Wq.weight"] = wqkv[:q].t()
+            out[r + "attn.Wk.weight"] = wqkv[q:q + kv].t()
+            out[r + "attn.Wv.weight"] = wqkv[q + kv:].t()
+            out[r + "attn.Wo.weight"] = self.views[p + "wo"].t()
+            wgu = self.views[p + "wgu"]
+            Fp = wgu.shape[0] // 2
+            blk = wgu.view(Fp // 128, 2, 128, -1)
+            out[r + "ffn.Wgate.weight"] = blk[:, 0].reshape(Fp, -1)[:F].t()
+            out[r + "ffn.Wup.weight"] = blk[:, 1].reshape(Fp, -1)[:F].t()
+            out[r + "ffn.Wdown.weight"] = self.views[p + "wdown"][:, :F].t()
+            out[r + "rms_norm_attn.weight"] = self.views[p + "attn_norm"]
+            out[r + "rms_norm_ffn.weight"] = self.views[p + "ffn_norm"]
+        out["final_norm.weight"] = self.views["final_norm"]
+        if not cfg.tie_embeddings:
+            out["lm_head.weight"] = self.views["lm_head"].t()
+        return out
+
+    def load_reference_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
+        cfg = self.cfg
+        q, kv, F = cfg.q_dim, cfg.kv_dim, cfg.ff_dim
+        with torch.no_grad():
+            self.views["embed"].copy_(sd["token_embedding.weight"])
+            for i in range(cfg.num_layers):
+                p, r = f"layers.{i}.", f"blocks.{i}."
+                wqkv = self.views[p + "wqkv"]
+                wqkv[:q].copy_(sd[r + "attn.Wq.weight"].t())
+                wqkv[q:q + kv].copy_(sd[r + "attn.Wk.weight"].t())
+                wqkv[q + kv:].copy_(sd[r + "attn.Wv.weight"].t())
+                self.views[p + "wo"].copy_(sd[r + "attn.Wo.weight"].t())
+                wgu = self.views[p + "wgu"]
+                Fp = wgu.shape[0] // 2
+                blk = wgu.view(Fp // 128, 2, 128, -1)
+                g = torch.zeros(Fp, wgu.shape[1], dtype=wgu.dtype, device=wgu.device)
+                u = torch.zeros_like(g)
+                g[:F] = sd[r + "ffn.Wgate.weight"].t()
+                u[:F] = sd[r + "ffn.Wup.weight"].t()
+                blk[:, 0].copy_(g.view(Fp // 128, 128, -1))
+                blk[:, 1].copy_(u.view(Fp // 128, 128, -1))
+                wd = self.views[p + "wdown"]
+                wd.zero_()
+                wd[:, :F].copy_(sd[r + "ffn.Wdown.weight"].t())
+                self.views[p + "attn_norm"].copy_(sd[r + "rms_norm_attn.weight"])
+                self.views[p + "ffn_norm"].copy_(sd[r + "rms_norm_ffn.weight"])
+            self.views["final_norm"].copy_(sd["final_norm.weight"])
+            if not cfg.tie_embeddings:
+                self.views["lm_head"].copy_(sd["lm_head.weight"].t())

@@ -1,0 +1,114 @@
+"""CPU tests: configs, schedules, parameter layout, checkpoint names, oracle."""
+import json
+import math
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from lora_kernel_b200.config import TransformerConfig, get_preset, load_config
+
+
+def test_presets_and_param_counts():
+    c = get_preset("llama-1.1b-zero3").model
+    assert 1.09e9 < c.num_parameters() < 1.11e9
+    c8 = get_preset("llama-8b-tp8-fp8").model
+    assert 8.0e9 < c8.num_parameters() < 8.1e9
+    demo = get_preset("cpu-demo")
+    assert demo.model.hidden_dim == 256 and demo.model.ff_dim == 688
+    assert demo.model.ff_dim_padded == 768
+    assert demo.train.micro_batch == 8 and demo.train.seq_len == 128
+
+
+def test_load_config_overrides(tmp_path):
+    p = tmp_path / "c.yaml"
+    p.write_text("model:\n  num_layers: 3\ntrain:\n  lr: 0.001\n")
+    cfg = load_config(str(p), preset="tiny", overrides={"parallel.zero_stage": 2})
+    assert cfg.model.num_layers == 3 and cfg.train.lr == 0.001 and cfg.parallel.zero_stage == 2
+    with pytest.raises(KeyError):
+        load_config(None, preset="tiny", overrides={"train.nope": 1})
+
+
+def test_lr_schedules():
+    from lora_kernel_b200.train.schedules import lr_at
+    assert lr_at(0, 1.0, "constant") == 1.0
+    assert lr_at(0, 1.0, "cosine", warmup_steps=10, total_steps=100) == pytest.approx(0.1)
+    assert lr_at(10, 1.0, "cosine", warmup_steps=10, total_steps=100) == pytest.approx(1.0)
+    assert lr_at(100, 1.0, "cosine", warmup_steps=10, total_steps=100, min_lr_ratio=0.1) == pytest.approx(0.1)
+    assert lr_at(55, 1.0, "linear", warmup_steps=10, total_steps=100) == pytest.approx(0.5)
+    assert lr_at(50, 1.0, "polynomial", total_steps=100, power=2.0) == pytest.approx(0.25)
+    assert lr_at(25, 1.0, "cosine_restarts", total_steps=100, num_cycles=2) == pytest.approx(0.5, abs=1e-6)
+
+
+def test_flat_layout_alignment_and_names():
+    from lora_kernel_b200.models.params import FlatParams
+    cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=688,
+                            vocab_size=1024, num_layers=2)
+    p = FlatParams(cfg, "cpu", torch.float32)
+    for s in p.specs:
+        assert s.offset % 64 == 0
+    p.init_(0, 0.02)
+    sd = p.to_reference_state_dict()
+    assert sd["blocks.0.attn.Wq.weight"].shape == (256, 256)
+    assert sd["blocks.0.attn.Wk.weight"].shape == (256, 128)
+    assert sd["blocks.1.ffn.Wgate.weight"].shape == (256, 688)
+    assert sd["blocks.1.ffn.Wdown.weight"].shape == (688, 256)
+    assert sd["lm_head.weight"].shape == (256, 1024)
+    # padding rows are exactly zero
+    wgu = p["layers.0.wgu"].view(6, 2, 128, 256)
+    assert torch.count_nonzero(wgu[5, :, 688 - 640:]) == 0
+    q = FlatParams(cfg, "cpu", torch.float32)
+    q.load_reference_state_dict({k: v.clone() for k, v in sd.items()})
+    assert torch.equal(q.flat, p.flat)
+    tot = sum(v.numel() for v in sd.values())
+    assert tot == cfg.num_parameters()
+
+
+def test_oracle_gradcheck_float64():
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.oracle import llama_ref
+    cfg = TransformerConfig(hidden_dim=32, num_heads=2, num_kv_heads=1, head_dim=16, ff_dim=128,
+                            vocab_size=16, num_layers=1)
+    p = FlatParams(cfg, "cpu", torch.float64)
+    p.init_(1, 0.2)
+    ids = torch.randint(0, 16, (1, 6))
+    tgt = torch.randint(0, 16, (1, 6))
+    w = p["layers.0.wo"].detach().clone().requires_grad_(True)
+
+    def f(wo):
+        d = {k: v for k, v in p.views.items()}
+        d["layers.0.wo"] = wo
+        return llama_ref.loss_fn(d, cfg, ids, tgt)
+
+    assert torch.autograd.gradcheck(f, (w,), eps=1e-6, atol=1e-5)
+
+
+def test_oracle_rope_is_rotation():
+    from lora_kernel_b200.oracle.llama_ref import rope
+    x = torch.randn(1, 5, 2, 8, dtype=torch.float64)
+    y = rope(x, 10000.0)
+    assert torch.allclose(x.norm(dim=-1), y.norm(dim=-1))
+    assert torch.allclose(x[:, 0], y[:, 0])
+
+
+def test_oracle_training_decreases_loss():
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.oracle.llama_ref import OracleTrainer
+    cfg = TransformerConfig(hidden_dim=64, num_heads=2, head_dim=32, ff_dim=128, vocab_size=64,
+                            num_layers=1)
+    p = FlatParams(cfg, "cpu", torch.float32)
+    p.init_(0, 0.02)
+    tr = OracleTrainer(dict(p.views), cfg, lr=1e-2)
+    ids = torch.randint(0, 64, (2, 17))
+    l0 = tr.step(ids[:, :-1], ids[:, 1:])
+    for _ in range(20):
+        l = tr.step(ids[:, :-1], ids[:, 1:])
+    assert l < l0 - 0.5
+
+
+def test_bench_reference_arm_reports_unavailable():
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference"], capture_output=True,
+                         text=True, check=True)
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["impl"] == "reference" and "unavailable" in d
