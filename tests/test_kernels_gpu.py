@@ -84,9 +84,10 @@ def test_gemm_swiglu():
     u = x.float() @ wu.float().t()
     _close(h, torch.nn.functional.silu(g) * u, 3e-2, 3e-2)
     from lora_kernel_b200.ops.gemm import split_gate_up
-    gg, uu = split_gate_up(gu)
-    _close(gg, g, 2e-2, 2e-2)
-    _close(uu, u, 2e-2, 2e-2)
+    # gate|up blocks run along the activation's column dimension
+    gg, uu = split_gate_up(gu.t().contiguous())
+    _close(gg.t(), g, 2e-2, 2e-2)
+    _close(uu.t(), u, 2e-2, 2e-2)
 
 
 @pytest.mark.parametrize("D", [256, 2048, 4096])
