@@ -76,10 +76,12 @@ __device__ __forceinline__ void q_range(const AttnBwdArgs& a, int j, int& i0, in
 }
 
 template <int DH>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const AttnBwdArgs args) {
   using C = BwdCfg<DH>;
+  // head_dim 64: dQ has its own TMEM columns; head_dim 128 reuses S^T's.
+  constexpr bool DQ_ALIAS = DH == 128;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023) {
@@ -88,12 +90,16 @@ __global__ void __launch_bounds__(192, 1)
   }
   const uint32_t bar = sbase + C::OFF_BAR;
   const uint32_t kv_full = bar, qd_full = bar + 8, qd_empty = bar + 24, sdp_full = bar + 40,
-                 ds_ready = bar + 48, dq_full = bar + 56, dq_free = bar + 64, drain = bar + 72;
+                 sdp_free = bar + 48, ds_ready = bar + 56, dq_full = bar + 64, dq_free = bar + 72,
+                 drain = bar + 80;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 132);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  // 1-D grid, key tile slowest: all j = 0 CTAs (the most work when causal) first
+  const int gb = args.Hkv * args.B;
+  const int j = (int)(blockIdx.x / gb);
+  const int g = (int)(blockIdx.x % gb) % args.Hkv, b = (int)(blockIdx.x % gb) / args.Hkv;
   const int group = args.Hq / args.Hkv;
   const int S = args.S;
   const int row0 = b * S;
@@ -109,9 +115,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(qd_empty + 8 * s, 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(ds_ready, 4);
+    mbar_init(sdp_free, 8);
+    mbar_init(ds_ready, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, 8);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -124,6 +131,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + DH;
+  const uint32_t tdQ = DQ_ALIAS ? tS : tmem + 256 + 2 * DH;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -175,8 +183,10 @@ __global__ void __launch_bounds__(192, 1)
       for (int it = 0; it < n_it && ok; ++it) {
         const int st = it % C::STAGES;
         const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
+        const uint32_t prev = (uint32_t)(it - 1) & 1;
         if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
-            (it > 0 && !bounded_wait(dq_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+            (it > 0 && !bounded_wait(sdp_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) ||
+            (DQ_ALIAS && it > 0 && !bounded_wait(dq_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
           ok = false;
           break;
         }
@@ -195,7 +205,8 @@ __global__ void __launch_bounds__(192, 1)
                      kk > 0 ? 1u : 0u);
         }
         tc_commit(sdp_full);
-        if (!bounded_wait(ds_ready, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) {
+        if (!bounded_wait(ds_ready, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
+            (!DQ_ALIAS && it > 0 && !bounded_wait(dq_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
           ok = false;
           break;
         }
@@ -210,7 +221,7 @@ __global__ void __launch_bounds__(192, 1)
         }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 keys
-          tc_mma_f16(tS, make_desc_sw128(sds + kk * 2048, 16384, 1024),
+          tc_mma_f16(tdQ, make_desc_sw128(sds + kk * 2048, 16384, 1024),
                      make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
         }
         tc_commit(dq_full);
@@ -221,8 +232,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------- softmax backward
+    // 8 warps: warp w owns TMEM lanes 32*(w%4)..+31 (key rows for S^T/dP^T/dK/dV,
+    // query rows for dQ) and half wg = (w-2)/4 of the columns.
     const int quarter = warp & 3;
-    const int kr = quarter * 32 + lane;  // key row (S^T/dP^T/dK/dV lane) and q row (dQ lane)
+    const int wg = (warp - 2) >> 2;
+    const int kr = quarter * 32 + lane;
     const int key = j * 128 + kr;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* sP = smem + C::OFF_P;
@@ -238,67 +252,68 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
+      uint32_t sv[2][32], dv[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(tS + lane_off + (wg * 2 + c) * 32, sv[c]);
+        tmem_ld32(tdP + lane_off + (wg * 2 + c) * 32, dv[c]);
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sdp_free);  // S^T / dP^T may be overwritten now
       const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
       const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
       const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
                              args.window > 0;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tS + lane_off + c * 32, sv);
-        tmem_ld32(tdP + lane_off + c * 32, dv);
-        tc_wait_ld();
+      const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int cc = wg * 2 + c;  // 32-query chunk index within the tile
         uint32_t pp[16], pd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
-          const int qi = c * 32 + e;  // query index within the tile
-          float4 L = make_float4(0.f, 0.f, 0.f, 0.f), Dd = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (i * 128 + qi + 3 < S && (S & 3) == 0) {
-            L = *reinterpret_cast<const float4*>(lse_row + qi);
-            Dd = *reinterpret_cast<const float4*>(d_row + qi);
+          const int qi = cc * 32 + e;
+          float Ls[4], Ds[4];
+          if (vec_ok) {
+            const float4 L = *reinterpret_cast<const float4*>(lse_row + qi);
+            const float4 Dd = *reinterpret_cast<const float4*>(d_row + qi);
+            Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
+            Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
           } else {
-            float* Lp = &L.x;
-            float* Dp = &Dd.x;
-            for (int t = 0; t < 4; ++t)
-              if (i * 128 + qi + t < S) {
-                Lp[t] = lse_row[qi + t];
-                Dp[t] = d_row[qi + t];
-              }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const bool in = i * 128 + qi + t < S;
+              Ls[t] = in ? lse_row[qi + t] : 0.f;
+              Ds[t] = in ? d_row[qi + t] : 0.f;
+            }
           }
-          const float Ls[4] = {L.x, L.y, L.z, L.w};
-          const float Ds[4] = {Dd.x, Dd.y, Dd.z, Dd.w};
           float p[4], ds[4];
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const int q = i * 128 + qi + t;
-            p[t] = exp2f(__uint_as_float(sv[e + t]) * args.sl2 - Ls[t] * 1.4426950408889634f);
+            p[t] = fast_exp2(__uint_as_float(sv[c][e + t]) * args.sl2 - Ls[t] * 1.4426950408889634f);
             if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
                               (args.window > 0 && key <= q - args.window)))
               p[t] = 0.f;
+            ds[t] = p[t] * (__uint_as_float(dv[c][e + t]) - Ds[t]) * args.scale;
           }
-          // round P to bf16 first so dS uses the P the forward's PV used
-          const uint32_t p01 = pack_bf16x2(p[0], p[1]), p23 = pack_bf16x2(p[2], p[3]);
-          const float2 r01 = unpack_bf16x2(p01), r23 = unpack_bf16x2(p23);
-          p[0] = r01.x; p[1] = r01.y; p[2] = r23.x; p[3] = r23.y;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) ds[t] = p[t] * (__uint_as_float(dv[e + t]) - Ds[t]) * args.scale;
-          pp[e / 2] = p01;
-          pp[e / 2 + 1] = p23;
+          pp[e / 2] = pack_bf16x2(p[0], p[1]);
+          pp[e / 2 + 1] = pack_bf16x2(p[2], p[3]);
           pd[e / 2] = pack_bf16x2(ds[0], ds[1]);
           pd[e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint32_t off = sw128_off_b(kr, c * 4 + u);
+          const uint32_t off = sw128_off_b(kr, cc * 4 + u);
           *reinterpret_cast<uint4*>(sP + off) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
           *reinterpret_cast<uint4*>(sDS + off) = make_uint4(pd[4 * u], pd[4 * u + 1], pd[4 * u + 2], pd[4 * u + 3]);
         }
       }
-      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      // dQ tile (lane = query row) -> fp32 accumulator
+      // dQ tile (lane = query row), this warp group's half of the columns
       w_ok = bounded_wait(dq_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
       if (!__all_sync(0xffffffffu, w_ok)) {
         ok = false;
@@ -308,9 +323,9 @@ __global__ void __launch_bounds__(192, 1)
       const int q = i * 128 + kr;
       float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + h * DH;
 #pragma unroll 1
-      for (int c = 0; c < DH / 32; ++c) {
+      for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
         uint32_t v[32];
-        tmem_ld32(tS + lane_off + c * 32, v);
+        tmem_ld32(tdQ + lane_off + c * 32, v);
         tc_wait_ld();
         if (q < S) {
 #pragma unroll
@@ -323,14 +338,14 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
     }
-    // dK, dV (lane = key row) -> bf16 into dqkv
-    // tcgen05.ld is warp-collective: every lane loads, only in-range keys store.
+    // dK, dV (lane = key row) -> bf16 into dqkv.  tcgen05.ld is warp-collective:
+    // every lane loads, only in-range keys store.
     if (__all_sync(0xffffffffu, ok) && n_it > 0) {
       tc_fence_after();
       __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
       __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
 #pragma unroll 1
-      for (int c = 0; c < DH / 32; ++c) {
+      for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
         uint32_t a[32], bb[32];
         tmem_ld32(tdK + lane_off + c * 32, a);
         tmem_ld32(tdV + lane_off + c * 32, bb);
@@ -354,7 +369,7 @@ __global__ void __launch_bounds__(192, 1)
       // no query sees this key tile: its gradients are zero
       __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
       __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
-      for (int e = 0; e < DH; e += 8) {
+      for (int e = wg * (DH / 2); e < (wg + 1) * (DH / 2); e += 8) {
         *reinterpret_cast<uint4*>(dk + e) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(dvp + e) = make_uint4(0, 0, 0, 0);
       }
@@ -444,8 +459,7 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   a.n_tiles = cdiv(d.S, 128);
   auto k = attn_bwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  dim3 grid(a.n_tiles, d.Hkv, d.B);
-  k<<<grid, 192, C::SMEM, s>>>(tq, tdo, a);
+  k<<<a.n_tiles * d.Hkv * d.B, 320, C::SMEM, s>>>(tq, tdo, a);
   if (check_launch("attn_bwd")) return -1;
   const int64_t n4 = T * d.Hq * DH / 4;
   int grid_c = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms() * 16);

@@ -71,13 +71,15 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
   const uint32_t bar = sbase + C::OFF_BAR;
   const uint32_t q_full = bar, k_full = bar + 8, k_empty = bar + 24, v_full = bar + 40,
                  v_empty = bar + 56, s_full = bar + 72, s_free = bar + 80, p_full = bar + 88,
-                 o_full = bar + 96, o_free = bar + 104, drain = bar + 112;
+                 o_full = bar + 96, drain = bar + 112;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 132);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = args.n_qtiles - 1 - blockIdx.x;  // heaviest causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // 1-D grid, heaviest causal q tiles first across all (head, batch) pairs
+  const int hb = args.Hq * args.B;
+  const int qt = args.n_qtiles - 1 - (int)(blockIdx.x / hb);
+  const int h = (int)(blockIdx.x % hb) % args.Hq, b = (int)(blockIdx.x % hb) / args.Hq;
   const int kvh = h / (args.Hq / args.Hkv);
   const int S = args.S;
   const int nkv_all = (S + 127) / 128;
@@ -98,7 +100,6 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
     mbar_init(s_free, 4);
     mbar_init(p_full, 4);
     mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -192,8 +193,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         }
         const int st = jj & 1;
         if (!bounded_wait(p_full, jj & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
-            !bounded_wait(v_full + 8 * st, (jj >> 1) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
-            (jj > 0 && !bounded_wait(o_free, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+            !bounded_wait(v_full + 8 * st, (jj >> 1) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
           ok = false;
           break;
         }
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         for (int kk = 0; kk < 8; ++kk) {  // 128 keys, 16 per MMA
           const uint64_t ad = make_desc_sw128(sp + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = make_desc_sw128(sv + kk * 2048, 16384, 1024);
-          tc_mma_f16(tO, ad, bd, idesc_o, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tO, ad, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(o_full);
         tc_commit(v_empty + 8 * st);
@@ -213,15 +213,16 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
     }
   } else {
     // ---------------------------------------------------------- softmax
+    // O accumulates in TMEM across key tiles.  Each row keeps the max m_used
+    // its exponentials are taken against and rescales its O row (TMEM
+    // read-modify-write) only when a tile's max exceeds m_used by more than 8
+    // (a factor 256), so P stays <= 256 and most tiles need no O traffic.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
     const int q = qt * 128 + r;         // query position
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* sP = smem + C::OFF_P;
-    float acc[DH];
-#pragma unroll
-    for (int d = 0; d < DH; ++d) acc[d] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, alpha_pending = 0.f;
+    float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int jj = 0; jj < nkv; ++jj) {
       const int j = j_begin + jj;
@@ -231,29 +232,47 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         break;
       }
       tc_fence_after();
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, sv[c]);
+      tc_wait_ld();
+      // S is in registers: release the TMEM buffer so S_{j+1} can start now
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
       const bool need_mask = (args.causal && j == qt) || (j + 1) * 128 > S ||
                              (args.window > 0 && j * 128 <= q - args.window + 127);
-      // pass 1: row max
       float mx = -INFINITY;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_off + c * 32, v);
-        tc_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          float s = __uint_as_float(v[e]);
+          float x = __uint_as_float(sv[c][e]) * args.sl2;
           if (need_mask) {
             const int key = j * 128 + c * 32 + e;
             if (key >= S || (args.causal && key > q) || (args.window > 0 && key <= q - args.window))
-              s = -INFINITY;
+              x = -INFINITY;
           }
-          mx = fmaxf(mx, s);
+          sv[c][e] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
         }
       }
-      const float m_new = fmaxf(m_run, mx * args.sl2);
-      const float alpha = exp2f(m_run - m_new);
-      // deferred accumulation of the previous tile's P V
+      const float m_new = (mx > m_used + 8.f) ? mx : m_used;
+      const float alpha = (m_new != m_used) ? fast_exp2(m_used - m_new) : 1.f;
+      const float mb = (m_new == -INFINITY) ? 0.f : m_new;
+      uint32_t pk[64];
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = fast_exp2(__uint_as_float(sv[c][e]) - mb);
+          const float p1 = fast_exp2(__uint_as_float(sv[c][e + 1]) - mb);
+          rowsum += p0 + p1;
+          pk[c * 16 + e / 2] = pack_bf16x2(p0, p1);
+        }
+      }
+      // PV_{j-1} must be done before O is rescaled and before P is overwritten
       if (jj > 0) {
         w_ok = bounded_wait(o_full, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) {
@@ -261,80 +280,55 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tO + lane_off + c * 32, v);
-          tc_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) acc[c * 32 + e] = acc[c * 32 + e] * alpha_pending + __uint_as_float(v[e]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
-      }
-      // pass 2: P = exp2(s*sl2 - m_new) -> shared memory (bf16, swizzled)
-      float rowsum = 0.f;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_off + c * 32, v);
-        tc_wait_ld();
-        uint32_t pk[16];
+          for (int c = 0; c < DH / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + lane_off + c * 32, ov);
+            tc_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = exp2f(__uint_as_float(v[e]) * args.sl2 - m_new);
-          float p1 = exp2f(__uint_as_float(v[e + 1]) * args.sl2 - m_new);
-          if (need_mask) {
-            const int key = j * 128 + c * 32 + e;
-            if (key >= S || (args.causal && key > q) || (args.window > 0 && key <= q - args.window)) p0 = 0.f;
-            if (key + 1 >= S || (args.causal && key + 1 > q) || (args.window > 0 && key + 1 <= q - args.window)) p1 = 0.f;
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st32(tO + lane_off + c * 32, ov);
           }
-          pk[e / 2] = pack_bf16x2(p0, p1);
-          const float2 pr = unpack_bf16x2(pk[e / 2]);  // sum what the MMA will see
-          rowsum += pr.x + pr.y;
+          tc_wait_st();
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(sP + sw128_off(r, c * 4 + u)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       }
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        *reinterpret_cast<uint4*>(sP + sw128_off(r, u)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(p_full);
       l_run = l_run * alpha + rowsum;
-      m_run = m_new;
-      alpha_pending = alpha;
+      m_used = m_new;
     }
     if (ok && nkv > 0) {
       bool w_ok = bounded_wait(o_full, (nkv - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
       if (__all_sync(0xffffffffu, w_ok)) {
         tc_fence_after();
-#pragma unroll
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = args.o + (int64_t)(row0 + q) * args.ldo + h * DH;
+#pragma unroll 1
         for (int c = 0; c < DH / 32; ++c) {
           uint32_t v[32];
           tmem_ld32(tO + lane_off + c * 32, v);
           tc_wait_ld();
+          if (q < S) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) acc[c * 32 + e] = acc[c * 32 + e] * alpha_pending + __uint_as_float(v[e]);
+            for (int d = 0; d < 32; d += 8)
+              *reinterpret_cast<uint4*>(orow + c * 32 + d) = make_uint4(
+                  pack_bf16x2(__uint_as_float(v[d]) * inv, __uint_as_float(v[d + 1]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 2]) * inv, __uint_as_float(v[d + 3]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 4]) * inv, __uint_as_float(v[d + 5]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 6]) * inv, __uint_as_float(v[d + 7]) * inv));
+          }
         }
-        if (q < S) {
-          const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-          __nv_bfloat16* orow = args.o + (int64_t)(row0 + q) * args.ldo + h * DH;
-#pragma unroll
-          for (int d = 0; d < DH; d += 8)
-            *reinterpret_cast<uint4*>(orow + d) =
-                make_uint4(pack_bf16x2(acc[d] * inv, acc[d + 1] * inv),
-                           pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv),
-                           pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv),
-                           pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv));
-          // natural-log LSE: (m + log2 l) * ln 2
-          args.lse[((int64_t)b * args.Hq + h) * S + q] = (m_run + log2f(l_run)) * 0.69314718055994531f;
-        }
+        // natural-log LSE: (m + log2 l) * ln 2
+        if (q < S)
+          args.lse[((int64_t)b * args.Hq + h) * S + q] =
+              l_run > 0.f ? (m_used + log2f(l_run)) * 0.69314718055994531f : -INFINITY;
       }
     }
   }
@@ -370,8 +364,7 @@ static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
   a.n_qtiles = cdiv(d.S, 128);
   auto k = attn_fwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  dim3 grid(a.n_qtiles, d.Hq, d.B);
-  k<<<grid, 192, C::SMEM, s>>>(tm, a);
+  k<<<a.n_qtiles * d.Hq * d.B, 192, C::SMEM, s>>>(tm, a);
   return check_launch("attn_fwd");
 }
 

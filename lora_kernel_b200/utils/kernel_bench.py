@@ -96,6 +96,27 @@ def bench_norm(iters):
                           "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
 
 
+def bench_attention(iters, B=4, S=2048, Hq=32, Hkv=4, Dh=64):
+    from lora_kernel_b200.ops.attention import attention_bwd, attention_fwd
+    qkv = torch.randn(B * S, (Hq + 2 * Hkv) * Dh, device="cuda").to(torch.bfloat16)
+    o, lse = attention_fwd(qkv, B, S, Hq, Hkv, Dh)
+    dout = torch.randn_like(o)
+    dqkv = torch.empty_like(qkv)
+    t_f = time_fn(lambda: attention_fwd(qkv, B, S, Hq, Hkv, Dh, out=o, lse=lse), iters)
+    t_b = time_fn(lambda: attention_bwd(qkv, o, dout, lse, B, S, Hq, Hkv, Dh, dqkv=dqkv), iters)
+    fl = 4.0 * B * Hq * Dh * S * S / 2  # causal
+    q = qkv[:, :Hq * Dh].view(B, S, Hq, Dh).transpose(1, 2)
+    k = qkv[:, Hq * Dh:(Hq + Hkv) * Dh].view(B, S, Hkv, Dh).transpose(1, 2)
+    v = qkv[:, (Hq + Hkv) * Dh:].view(B, S, Hkv, Dh).transpose(1, 2)
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    t_ref = time_fn(lambda: sdpa(q, k, v, is_causal=True, enable_gqa=True), iters)
+    print(json.dumps({"kernel": "attention", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "Dh": Dh,
+                      "fwd_ms": round(t_f, 4), "fwd_tflops": round(fl / t_f / 1e9, 1),
+                      "bwd_ms": round(t_b, 4), "bwd_tflops": round(2.5 * fl / t_b / 1e9, 1),
+                      "sdpa_fwd_ms": round(t_ref, 4), "sdpa_fwd_tflops": round(fl / t_ref / 1e9, 1)}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,norm")
@@ -105,7 +126,7 @@ def main():
     which = set(args.only.split(","))
     if "gemm" in which:
         if args.small:
-            shapes = [(4096, 4096, 4096, "tn")]
+            shapes = [(8192, 8192, 8192, "tn")]
         else:
             shapes = [(8192, 8192, 8192, "tn"), (8192, 8192, 8192, "dgrad"),
                       (8192, 8192, 8192, "wgrad"),
@@ -115,6 +136,8 @@ def main():
         bench_gemm(shapes, args.iters)
     if "norm" in which:
         bench_norm(args.iters)
+    if "attn" in which:
+        bench_attention(args.iters)
 
 
 if __name__ == "__main__":
