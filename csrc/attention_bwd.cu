@@ -59,7 +59,8 @@ struct BwdCfg {
   static constexpr int OFF_DO = OFF_Q + STAGES * QB;
   static constexpr int OFF_P = OFF_DO + STAGES * QB;
   static constexpr int OFF_DS = OFF_P + 32768;
-  static constexpr int OFF_BAR = OFF_DS + 32768;
+  static constexpr int OFF_LD = OFF_DS + 32768;        // [STAGES][2][128] fp32 LSE, D
+  static constexpr int OFF_BAR = OFF_LD + STAGES * 1024;
   static constexpr int SMEM = OFF_BAR + 256;
   static constexpr int TMEM_COLS = 512;
 };
@@ -107,6 +108,8 @@ __global__ void __launch_bounds__(320, 1)
   q_range(args, j, i0, i1);
   const int nq = max(0, i1 - i0);
   const int n_it = group * nq;
+  // whole 128-query tiles: LSE/D rows arrive by bulk copy with the Q/dO stage
+  const bool bulk_ld = (S & 127) == 0;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -155,7 +158,12 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         const uint32_t fb = qd_full + 8 * st;
-        mbar_expect_tx(fb, 2 * C::QB);
+        mbar_expect_tx(fb, 2 * C::QB + (bulk_ld ? 1024u : 0u));
+        if (bulk_ld) {
+          const int64_t off = ((int64_t)b * args.Hq + h) * S + i * 128;
+          bulk_load(sbase + C::OFF_LD + st * 1024, args.lse + off, 512, fb);
+          bulk_load(sbase + C::OFF_LD + st * 1024 + 512, args.Dvec + off, 512, fb);
+        }
 #pragma unroll
         for (int c = 0; c < DH / 64; ++c) {
           tma_load_2d(sbase + C::OFF_Q + st * C::QB + c * 16384, &tm_qkv, fb, h * DH + c * 64, row0 + i * 128);
@@ -267,6 +275,8 @@ __global__ void __launch_bounds__(320, 1)
       const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
                              args.window > 0;
       const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
+      const int st = it % C::STAGES;
+      const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int cc = wg * 2 + c;  // 32-query chunk index within the tile
@@ -275,7 +285,12 @@ __global__ void __launch_bounds__(320, 1)
         for (int e = 0; e < 32; e += 4) {
           const int qi = cc * 32 + e;
           float Ls[4], Ds[4];
-          if (vec_ok) {
+          if (bulk_ld) {
+            const float4 L = *reinterpret_cast<const float4*>(sL + qi);
+            const float4 Dd = *reinterpret_cast<const float4*>(sL + 128 + qi);
+            Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
+            Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
+          } else if (vec_ok) {
             const float4 L = *reinterpret_cast<const float4*>(lse_row + qi);
             const float4 Dd = *reinterpret_cast<const float4*>(d_row + qi);
             Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;

@@ -242,34 +242,36 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
       if (lane == 0) mbar_arrive(s_free);
       const bool need_mask = (args.causal && j == qt) || (j + 1) * 128 > S ||
                              (args.window > 0 && j * 128 <= q - args.window + 127);
-      float mx = -INFINITY;
+      float mraw = -INFINITY;  // max of the raw scores (scale > 0 commutes with max)
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(sv[c][e]) * args.sl2;
-          if (need_mask) {
+          for (int e = 0; e < 32; ++e) {
             const int key = j * 128 + c * 32 + e;
             if (key >= S || (args.causal && key > q) || (args.window > 0 && key <= q - args.window))
-              x = -INFINITY;
+              sv[c][e] = __float_as_uint(-INFINITY);
           }
-          sv[c][e] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
         }
       }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[c][e]));
+      const float mx = mraw * args.sl2;
       const float m_new = (mx > m_used + 8.f) ? mx : m_used;
       const float alpha = (m_new != m_used) ? fast_exp2(m_used - m_new) : 1.f;
       const float mb = (m_new == -INFINITY) ? 0.f : m_new;
-      uint32_t pk[64];
+      // P packed to bf16 pairs in place: sv[c][0..15] hold chunk c's 32 probabilities
       float rowsum = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = fast_exp2(__uint_as_float(sv[c][e]) - mb);
-          const float p1 = fast_exp2(__uint_as_float(sv[c][e + 1]) - mb);
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][e]), args.sl2, -mb));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][e + 1]), args.sl2, -mb));
           rowsum += p0 + p1;
-          pk[c * 16 + e / 2] = pack_bf16x2(p0, p1);
+          sv[c][e >> 1] = pack_bf16x2(p0, p1);
         }
       }
       // PV_{j-1} must be done before O is rescaled and before P is overwritten
@@ -294,9 +296,10 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         }
       }
 #pragma unroll
-      for (int u = 0; u < 16; ++u)
-        *reinterpret_cast<uint4*>(sP + sw128_off(r, u)) =
-            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      for (int u = 0; u < 16; ++u) {
+        const uint32_t* pk = &sv[u >> 2][(u & 3) * 4];
+        *reinterpret_cast<uint4*>(sP + sw128_off(r, u)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
