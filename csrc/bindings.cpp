@@ -339,6 +339,59 @@ void attention_bwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch
   check(lk_attention_bwd(&d, stream()));
 }
 
+// ------------------------------------------------------ peer collectives
+template <typename T>
+T ptrs(const torch::Tensor& t) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64, "pointer table must be a CUDA int64 tensor");
+  return reinterpret_cast<T>(t.data_ptr());
+}
+
+void signal_barrier(torch::Tensor sig_ptrs, int64_t rank, int64_t world, int64_t slot, int64_t epoch,
+                    torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(sig_ptrs.device());
+  check(lk_signal_barrier(ptrs<int* const*>(sig_ptrs), (int)rank, (int)world, (int)slot, (int)epoch,
+                          status.data_ptr<int>(), stream()));
+}
+
+void allgather_copy(torch::Tensor src_ptrs, int64_t src_off_bytes, int64_t chunk_bytes, torch::Tensor dst,
+                    int64_t world) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  TORCH_CHECK(dst.is_contiguous() && dst.numel() * dst.element_size() >= chunk_bytes * world, "allgather: dst too small");
+  check(lk_allgather_copy(ptrs<const void* const*>(src_ptrs), src_off_bytes, chunk_bytes, dst.data_ptr(),
+                          (int)world, stream()));
+}
+
+void reduce_scatter_sum(torch::Tensor src_ptrs, int64_t src_off, int64_t n, torch::Tensor dst, int64_t world,
+                        bool accumulate, c10::optional<torch::Tensor> partial) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  need_contig(dst, "dst", torch::kFloat32);
+  TORCH_CHECK(dst.numel() >= n, "reduce_scatter: dst too small");
+  check(lk_reduce_scatter_sum(ptrs<const float* const*>(src_ptrs), src_off, n, dst.data_ptr<float>(),
+                              (int)world, accumulate ? 1 : 0, optp<float>(partial),
+                              partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
+void allreduce_sum(torch::Tensor buf_ptrs, int64_t n, int64_t rank, int64_t world,
+                   c10::optional<torch::Tensor> partial) {
+  const c10::cuda::CUDAGuard g(buf_ptrs.device());
+  check(lk_allreduce_sum(ptrs<float* const*>(buf_ptrs), n, (int)rank, (int)world, optp<float>(partial),
+                         partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
+void norm_exchange(torch::Tensor partial, torch::Tensor nbuf_ptrs, torch::Tensor sig_ptrs, int64_t rank,
+                   int64_t world, int64_t slot, int64_t epoch, torch::Tensor state, double max_norm,
+                   bool dynamic, double growth, double backoff, int64_t growth_interval, double min_scale,
+                   torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(state.device());
+  need_contig(partial, "partial", torch::kFloat32);
+  need_contig(state, "state", torch::kFloat32);
+  check(lk_norm_exchange(partial.data_ptr<float>(), (int)partial.numel(), ptrs<double* const*>(nbuf_ptrs),
+                         ptrs<int* const*>(sig_ptrs), (int)rank, (int)world, (int)slot, (int)epoch,
+                         state.data_ptr<float>(), (float)max_norm, dynamic ? 1 : 0, (float)growth,
+                         (float)backoff, (int)growth_interval, (float)min_scale, status.data_ptr<int>(),
+                         stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -358,6 +411,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_norm_partials", &grad_norm_partials);
   m.def("optimizer_finalize", &optimizer_finalize);
   m.def("attention_fwd", &attention_fwd);
+  m.def("signal_barrier", &signal_barrier);
+  m.def("allgather_copy", &allgather_copy);
+  m.def("reduce_scatter_sum", &reduce_scatter_sum);
+  m.def("allreduce_sum", &allreduce_sum);
+  m.def("norm_exchange", &norm_exchange);
+  m.attr("SIG_SLOTS") = (int)LK_SIG_SLOTS;
   m.def("attention_bwd", &attention_bwd);
   m.attr("EPI_BF16") = (int)LK_EPI_BF16;
   m.attr("EPI_F32") = (int)LK_EPI_F32;

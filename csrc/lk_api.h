@@ -182,6 +182,24 @@ typedef struct LkAttnBwdDesc {
 } LkAttnBwdDesc;
 int lk_attention_bwd(const LkAttnBwdDesc* d, cudaStream_t s);
 
+// ---------------------------------------------- peer-memory collectives (comm.cu)
+// Pointer arguments named *_ptrs are DEVICE arrays of `world` peer pointers
+// (rank order) into symmetric (peer-mapped) buffers.  Flag arrays hold
+// LK_SIG_SLOTS * world int32 per rank, zero-initialised; epochs increase.
+#define LK_SIG_SLOTS 16
+int lk_signal_barrier(int* const* sig_ptrs, int rank, int world, int slot, int epoch, int* status,
+                      cudaStream_t s);
+int lk_allgather_copy(const void* const* src_ptrs, int64_t src_off_bytes, int64_t chunk_bytes,
+                      void* dst, int world, cudaStream_t s);
+int lk_reduce_scatter_sum(const float* const* src_ptrs, int64_t src_off, int64_t n, float* dst,
+                          int world, int accumulate, float* partial, int nparts, cudaStream_t s);
+int lk_allreduce_sum(float* const* buf_ptrs, int64_t n, int rank, int world, float* partial,
+                     int nparts, cudaStream_t s);
+int lk_norm_exchange(const float* partial, int nparts, double* const* nbuf_ptrs, int* const* sig_ptrs,
+                     int rank, int world, int slot, int epoch, float* state, float max_norm,
+                     int dynamic, float growth, float backoff, int growth_interval, float min_scale,
+                     int* status, cudaStream_t s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,6 +88,9 @@ class LlamaModel:
         self._ws: Dict[Tuple[int, int, bool], _Workspace] = {}
         self.rope = E.rope_table(max(cfg.max_seq_len, 1), cfg.head_dim, cfg.rope_base, self.device)
         self.attn_window = 0
+        self.hooks = None  # optional: pre_forward / pre_layer_fwd(i) / pre_layer_bwd(i) /
+        #                    post_layer_bwd(i) / post_head_bwd / post_backward (ZeRO-3)
+        self._overwrite = False
 
     # -------------------------------------------------------------- helpers
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
@@ -109,6 +112,14 @@ class LlamaModel:
     def _g(self, name):
         return self.grads[name]
 
+    def _hook(self, name, *a):
+        if self.hooks is not None:
+            getattr(self.hooks, name)(*a)
+
+    def _wgrad(self, dy, x, name):
+        """Weight gradient: stored on the first micro-step of a window, else accumulated."""
+        G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
+
     # -------------------------------------------------------------- forward
     def _layer_fwd(self, i: int, ws: _Workspace, h_in: torch.Tensor, h_out: torch.Tensor, slot: int):
         cfg = self.cfg
@@ -128,8 +139,10 @@ class LlamaModel:
 
     def _forward(self, ids: torch.Tensor, ws: _Workspace, save: bool) -> torch.Tensor:
         cfg = self.cfg
+        self._hook("pre_forward")
         E.embedding_fwd(ids.reshape(-1), self._p("embed"), out=ws.h[0])
         for i in range(cfg.num_layers):
+            self._hook("pre_layer_fwd", i)
             if save:
                 self._layer_fwd(i, ws, ws.h[i], ws.h[i + 1], i)
             else:
@@ -151,12 +164,15 @@ class LlamaModel:
     def forward_backward(self, ids: torch.Tensor, targets: torch.Tensor, *,
                          loss_scale: Optional[torch.Tensor] = None, grad_scale: float = 1.0,
                          label_smoothing: float = 0.0, z_loss: float = 0.0,
-                         loss_acc: Optional[torch.Tensor] = None) -> torch.Tensor:
+                         loss_acc: Optional[torch.Tensor] = None,
+                         overwrite_grads: bool = False) -> torch.Tensor:
         """One micro-batch: forward, fused CE, backward.  Gradients (scaled by
         *loss_scale x grad_scale) accumulate into self.grads.  Returns the
         device tensor [sum of token losses, token count] (accumulated into
-        loss_acc when given)."""
+        loss_acc when given).  overwrite_grads: store instead of accumulate
+        (first micro-step of an accumulation window; no zeroing pass needed)."""
         cfg = self.cfg
+        self._overwrite = overwrite_grads
         B, S = ids.shape
         ws = self.workspace(B, S, save=True)
         acc = ws.loss_acc if loss_acc is None else loss_acc
@@ -169,12 +185,20 @@ class LlamaModel:
         dlogits = ws.logits
         # LM head
         G.linear_dgrad(dlogits, self._p("lm_head"), out=ws.dx)
-        G.linear_wgrad(dlogits, ws.xf, self._g("lm_head"))
+        self._wgrad(dlogits, ws.xf, "lm_head")
         L_ = cfg.num_layers
-        N.rmsnorm_bwd(ws.dx, ws.h[L_], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=ws.dh)
+        N.rmsnorm_bwd(ws.dx, ws.h[L_], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=ws.dh,
+                      accumulate=not overwrite_grads)
+        self._hook("post_head_bwd")
         for i in reversed(range(L_)):
+            self._hook("pre_layer_bwd", i)
             self._layer_bwd(i, ws)
+            self._hook("post_layer_bwd", i)
+        if overwrite_grads and not cfg.tie_embeddings:
+            self._g("embed").zero_()
         E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
+        self._hook("post_backward")
+        self._overwrite = False
         return acc
 
     def _layer_bwd(self, i: int, ws: _Workspace):
@@ -183,21 +207,21 @@ class LlamaModel:
         dh = ws.dh
         # FFN
         G.linear_dgrad(dh, self._p(p + "wdown"), out=ws.dact)
-        G.linear_wgrad(dh, ws.act[i], self._g(p + "wdown"))
+        self._wgrad(dh, ws.act[i], p + "wdown")
         E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
         G.linear_dgrad(ws.dgu, self._p(p + "wgu"), out=ws.dx)
-        G.linear_wgrad(ws.dgu, ws.xn2[i], self._g(p + "wgu"))
+        self._wgrad(ws.dgu, ws.xn2[i], p + "wgu")
         N.rmsnorm_bwd(ws.dx, ws.hmid[i], self._p(p + "ffn_norm"), ws.rstd2[i], self._g(p + "ffn_norm"),
-                      dres=dh, dx=dh)
+                      dres=dh, dx=dh, accumulate=not self._overwrite)
         # attention
         G.linear_dgrad(dh, self._p(p + "wo"), out=ws.do)
-        G.linear_wgrad(dh, ws.o[i], self._g(p + "wo"))
+        self._wgrad(dh, ws.o[i], p + "wo")
         A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, cfg.num_heads,
                         cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
                         dqkv=ws.dqkv)
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
                 inverse=True)
         G.linear_dgrad(ws.dqkv, self._p(p + "wqkv"), out=ws.dx)
-        G.linear_wgrad(ws.dqkv, ws.xn1[i], self._g(p + "wqkv"))
+        self._wgrad(ws.dqkv, ws.xn1[i], p + "wqkv")
         N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[i], self._g(p + "attn_norm"),
-                      dres=dh, dx=dh)
+                      dres=dh, dx=dh, accumulate=not self._overwrite)

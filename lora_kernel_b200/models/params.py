@@ -51,8 +51,12 @@ def _round(n: int) -> int:
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
 
-def build_layout(cfg: TransformerConfig) -> Tuple[List[ParamSpec], Dict[str, Tuple[int, int]], int]:
-    """Returns (specs, group ranges {group: (start, end)}, total numel)."""
+def build_layout(cfg: TransformerConfig, group_align: int = ALIGN
+                 ) -> Tuple[List[ParamSpec], Dict[str, Tuple[int, int]], int]:
+    """Returns (specs, group ranges {group: (start, end)}, total numel).  Every
+    group is padded to a multiple of `group_align` elements (64 x world size for
+    ZeRO sharding, so each rank owns an equal, aligned chunk of every group)."""
+    assert group_align % ALIGN == 0
     D, V, F = cfg.hidden_dim, cfg.vocab_size, cfg.ff_dim_padded
     specs: List[ParamSpec] = []
     groups: Dict[str, Tuple[int, int]] = OrderedDict()
@@ -69,7 +73,7 @@ def build_layout(cfg: TransformerConfig) -> Tuple[List[ParamSpec], Dict[str, Tup
         start = off
         for it in items:
             add(*it[:2], name, *it[2:])
-        off = _round(off)
+        off = (off + group_align - 1) // group_align * group_align
         groups[name] = (start, off)
 
     group("embed", [("embed", (V, D), True, "normal")])
@@ -94,9 +98,10 @@ class FlatParams:
     """A flat buffer plus named views following `build_layout(cfg)`."""
 
     def __init__(self, cfg: TransformerConfig, device, dtype=torch.bfloat16,
-                 buffer: Optional[torch.Tensor] = None):
+                 buffer: Optional[torch.Tensor] = None, group_align: int = ALIGN):
         self.cfg = cfg
-        self.specs, self.groups, self.numel = build_layout(cfg)
+        self.group_align = group_align
+        self.specs, self.groups, self.numel = build_layout(cfg, group_align)
         self.by_name = {s.name: s for s in self.specs}
         if buffer is None:
             buffer = torch.zeros(self.numel, dtype=dtype, device=device)
@@ -112,7 +117,11 @@ class FlatParams:
 
     def like(self, dtype=torch.float32, device=None) -> "FlatParams":
         return FlatParams(self.cfg, device or self.flat.device, dtype,
-                          torch.zeros(self.numel, dtype=dtype, device=device or self.flat.device))
+                          torch.zeros(self.numel, dtype=dtype, device=device or self.flat.device),
+                          self.group_align)
+
+    def group_of(self, name: str) -> str:
+        return self.by_name[name].group
 
     def segments(self, decay_norms: bool = False, lo: int = 0, hi: Optional[int] = None):
         """(start, length, decay) of every parameter clipped to [lo, hi), relative to lo."""
@@ -128,21 +137,24 @@ class FlatParams:
     def init_(self, seed: int, std: float) -> None:
         """Deterministic N(0, std) for matrices, ones for norms; the padded FFN
         rows/columns are zero so the padding is exact."""
-        g = torch.Generator(device="cpu").manual_seed(seed)
         cfg = self.cfg
         F, Fp = cfg.ff_dim, cfg.ff_dim_padded
-        for s in self.specs:
+        dev = self.flat.device
+        for idx, s in enumerate(self.specs):
             v = self.views[s.name]
             if s.init == "ones":
                 v.fill_(1.0)
             elif s.init == "zeros":
                 v.zero_()
             else:
-                t = torch.empty(s.shape, dtype=torch.float32)
+                # one generator per tensor, seeded by (seed, tensor index): every
+                # rank reproduces the same weights for any tensor independently
+                g = torch.Generator(device=dev).manual_seed(seed * 1000003 + idx)
+                t = torch.empty(s.shape, dtype=torch.float32, device=dev)
                 t.normal_(0.0, std, generator=g)
                 if s.name.endswith("wgu") and Fp != F:
                     blk = t.view(Fp // 128, 2, 128, -1)
-                    mask = torch.arange(Fp).view(Fp // 128, 128) >= F
+                    mask = (torch.arange(Fp, device=dev) >= F).view(Fp // 128, 128)
                     blk[:, 0][mask] = 0.0
                     blk[:, 1][mask] = 0.0
                 if s.name.endswith("wdown") and Fp != F:

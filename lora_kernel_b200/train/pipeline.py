@@ -116,10 +116,13 @@ class TrainingPipeline:
         self.engine.forward_backward(ids, targets, loss_scale=self.opt.scaler.scale_tensor(),
                                      grad_scale=1.0 / (n_tok * self.accum_steps),
                                      label_smoothing=self.tc.label_smoothing, z_loss=self.tc.z_loss,
-                                     loss_acc=self.loss_acc)
+                                     loss_acc=self.loss_acc,
+                                     overwrite_grads=(self._micro % self.accum_steps == 0))
         self._micro += 1
         if self._micro % self.accum_steps == 0:
-            self.opt.step(self.engine.grads.flat, self.engine.params.flat)
+            self.opt.norm_partials(self.engine.grads.flat)
+            self.opt.finalize()
+            self.opt.apply(self.engine.grads.flat, self.engine.params.flat, zero_grad=False)
             self._opt_steps += 1
             if self.swa is not None:
                 self.swa.update(self.opt.p32, self._opt_steps)
