@@ -28,7 +28,10 @@
 namespace lk {
 
 struct AttnFwdArgs {
-  int B, S, Hq, Hkv;
+  int B, S, Hq, Hkv;  // S = query length
+  int Skv;            // key length (== S for self-attention over packed QKV)
+  int q_off;          // position of query 0 relative to key 0 (cached prefix length)
+  int kcol0, vcol0;   // first column of key head 0 / value head 0 in the KV map
   int causal;
   int window;      // > 0: sliding window (keys in (q - window, q])
   float sl2;       // softmax scale * log2(e)
@@ -60,7 +63,8 @@ struct FwdCfg {
 
 template <int DH>
 __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs args) {
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_kv,
+                    const AttnFwdArgs args) {
   using C = FwdCfg<DH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -81,11 +85,12 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
   const int qt = args.n_qtiles - 1 - (int)(blockIdx.x / hb);
   const int h = (int)(blockIdx.x % hb) % args.Hq, b = (int)(blockIdx.x % hb) / args.Hq;
   const int kvh = h / (args.Hq / args.Hkv);
-  const int S = args.S;
-  const int nkv_all = (S + 127) / 128;
-  int j_end = args.causal ? min(qt + 1, nkv_all) : nkv_all;
+  const int S = args.S, Skv = args.Skv, q_off = args.q_off;
+  const int nkv_all = (Skv + 127) / 128;
+  const int qpos_max = q_off + qt * 128 + 127;  // largest query position in the tile
+  int j_end = args.causal ? min(qpos_max / 128 + 1, nkv_all) : nkv_all;
   int j_begin = 0;
-  if (args.window > 0) j_begin = max(0, (qt * 128 - args.window + 1) / 128);
+  if (args.window > 0) j_begin = max(0, (q_off + qt * 128 - args.window + 1) / 128);
   const int nkv = j_end - j_begin;
 
   if (threadIdx.x == 0) {
@@ -104,6 +109,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_kv);
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
@@ -111,7 +117,8 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 128;
-  const int row0 = b * S;
+  const int row0 = b * S;      // query rows
+  const int krow0 = b * Skv;   // key / value rows
 
   if (warp == 0) {
     if (lane == 0) {
@@ -134,8 +141,8 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         mbar_expect_tx(k_full + 8 * st, C::QB);
 #pragma unroll
         for (int c = 0; c < DH / 64; ++c)
-          tma_load_2d(sbase + C::OFF_K + st * C::QB + c * 16384, &tm_qkv, k_full + 8 * st,
-                      (args.Hq + kvh) * DH + c * 64, row0 + j * 128);
+          tma_load_2d(sbase + C::OFF_K + st * C::QB + c * 16384, &tm_kv, k_full + 8 * st,
+                      args.kcol0 + kvh * DH + c * 64, krow0 + j * 128);
         pending |= 1u << st;
         parbits = (parbits & ~(1u << st)) | (ph << st);
         if (!bounded_wait(v_empty + 8 * st, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
@@ -145,8 +152,8 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         mbar_expect_tx(v_full + 8 * st, C::QB);
 #pragma unroll
         for (int c = 0; c < DH / 64; ++c)
-          tma_load_2d(sbase + C::OFF_V + st * C::QB + c * 16384, &tm_qkv, v_full + 8 * st,
-                      (args.Hq + args.Hkv + kvh) * DH + c * 64, row0 + j * 128);
+          tma_load_2d(sbase + C::OFF_V + st * C::QB + c * 16384, &tm_kv, v_full + 8 * st,
+                      args.vcol0 + kvh * DH + c * 64, krow0 + j * 128);
         pending |= 4u << st;
         parbits = (parbits & ~(4u << st)) | (ph << (st + 2));
       }
@@ -219,7 +226,8 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
     // (a factor 256), so P stays <= 256 and most tiles need no O traffic.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
-    const int q = qt * 128 + r;         // query position
+    const int ql = qt * 128 + r;        // query row within the sequence
+    const int q = q_off + ql;           // query position (keys are 0..Skv-1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* sP = smem + C::OFF_P;
     float m_used = -INFINITY, l_run = 0.f;
@@ -240,7 +248,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
-      const bool need_mask = (args.causal && j == qt) || (j + 1) * 128 > S ||
+      const bool need_mask = (args.causal && j * 128 + 127 > q_off + qt * 128) || (j + 1) * 128 > Skv ||
                              (args.window > 0 && j * 128 <= q - args.window + 127);
       float mraw = -INFINITY;  // max of the raw scores (scale > 0 commutes with max)
       if (need_mask) {
@@ -249,7 +257,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int key = j * 128 + c * 32 + e;
-            if (key >= S || (args.causal && key > q) || (args.window > 0 && key <= q - args.window))
+            if (key >= Skv || (args.causal && key > q) || (args.window > 0 && key <= q - args.window))
               sv[c][e] = __float_as_uint(-INFINITY);
           }
         }
@@ -312,13 +320,13 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
       if (__all_sync(0xffffffffu, w_ok)) {
         tc_fence_after();
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        __nv_bfloat16* orow = args.o + (int64_t)(row0 + q) * args.ldo + h * DH;
+        __nv_bfloat16* orow = args.o + (int64_t)(row0 + ql) * args.ldo + h * DH;
 #pragma unroll 1
         for (int c = 0; c < DH / 32; ++c) {
           uint32_t v[32];
           tmem_ld32(tO + lane_off + c * 32, v);
           tc_wait_ld();
-          if (q < S) {
+          if (ql < S) {
 #pragma unroll
             for (int d = 0; d < 32; d += 8)
               *reinterpret_cast<uint4*>(orow + c * 32 + d) = make_uint4(
@@ -329,8 +337,8 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
           }
         }
         // natural-log LSE: (m + log2 l) * ln 2
-        if (q < S)
-          args.lse[((int64_t)b * args.Hq + h) * S + q] =
+        if (ql < S)
+          args.lse[((int64_t)b * args.Hq + h) * S + ql] =
               l_run > 0.f ? (m_used + log2f(l_run)) * 0.69314718055994531f : -INFINITY;
       }
     }
@@ -347,14 +355,26 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
 template <int DH>
 static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
   using C = FwdCfg<DH>;
-  const int ncols = (d.Hq + 2 * d.Hkv) * DH;
-  CUtensorMap tm;
-  if (!make_tmap_2d(&tm, d.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (int64_t)d.B * d.S, ncols,
+  const bool packed = d.kv == nullptr;
+  const int Skv = packed ? d.S : d.Skv;
+  const int64_t qcols = packed ? (int64_t)(d.Hq + 2 * d.Hkv) * DH : (int64_t)d.Hq * DH;
+  CUtensorMap tm, tkv;
+  if (!make_tmap_2d(&tm, d.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (int64_t)d.B * d.S, qcols,
                     d.ld_qkv, 128, 64))
     return -1;
+  if (packed) {
+    tkv = tm;
+  } else if (!make_tmap_2d(&tkv, d.kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (int64_t)d.B * Skv,
+                           (int64_t)2 * d.Hkv * DH, d.ld_kv, 128, 64)) {
+    return -1;
+  }
   AttnFwdArgs a{};
   a.B = d.B;
   a.S = d.S;
+  a.Skv = Skv;
+  a.q_off = packed ? 0 : d.q_off;
+  a.kcol0 = packed ? d.Hq * DH : 0;
+  a.vcol0 = packed ? (d.Hq + d.Hkv) * DH : d.Hkv * DH;
   a.Hq = d.Hq;
   a.Hkv = d.Hkv;
   a.causal = d.causal;
@@ -367,7 +387,7 @@ static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
   a.n_qtiles = cdiv(d.S, 128);
   auto k = attn_fwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  k<<<a.n_qtiles * d.Hq * d.B, 192, C::SMEM, s>>>(tm, a);
+  k<<<a.n_qtiles * d.Hq * d.B, 192, C::SMEM, s>>>(tm, tkv, a);
   return check_launch("attn_fwd");
 }
 

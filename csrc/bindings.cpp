@@ -284,13 +284,14 @@ void optimizer_finalize(torch::Tensor partial, torch::Tensor state, double max_n
 // ------------------------------------------------------------- attention
 void attention_fwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
                    int64_t Hq, int64_t Hkv, int64_t Dh, bool causal, int64_t window, double scale,
-                   torch::Tensor status) {
+                   torch::Tensor status, c10::optional<torch::Tensor> kv, int64_t q_off) {
   const c10::cuda::CUDAGuard g(qkv.device());
   need(qkv, "qkv", torch::kBFloat16);
   need(o, "o", torch::kBFloat16);
   need_contig(lse, "lse", torch::kFloat32);
-  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(0) == B * S &&
-                  qkv.size(1) >= (Hq + 2 * Hkv) * Dh, "attention: bad qkv shape");
+  const int64_t qcols = kv.has_value() ? Hq * Dh : (Hq + 2 * Hkv) * Dh;
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(0) == B * S && qkv.size(1) >= qcols,
+              "attention: bad qkv shape");
   TORCH_CHECK(o.dim() == 2 && o.stride(1) == 1 && o.size(0) == B * S && o.size(1) >= Hq * Dh,
               "attention: bad o shape");
   TORCH_CHECK(lse.numel() >= B * Hq * S, "attention: lse too small");
@@ -305,6 +306,15 @@ void attention_fwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_
   d.window = (int)window;
   d.scale = (float)scale;
   d.status = status.data_ptr<int>();
+  if (kv.has_value()) {
+    need(*kv, "kv", torch::kBFloat16);
+    TORCH_CHECK(kv->dim() == 2 && kv->stride(1) == 1 && kv->size(0) % B == 0 && kv->size(1) >= 2 * Hkv * Dh,
+                "attention: kv must be [B*Skv, 2*Hkv*Dh]");
+    d.kv = kv->data_ptr();
+    d.ld_kv = kv->stride(0);
+    d.Skv = (int)(kv->size(0) / B);
+    d.q_off = (int)q_off;
+  }
   check(lk_attention_fwd(&d, stream()));
 }
 
@@ -392,6 +402,104 @@ void norm_exchange(torch::Tensor partial, torch::Tensor nbuf_ptrs, torch::Tensor
                          stream()));
 }
 
+// ---------------------------------------------------------------- serving
+void kv_append(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t Dh, torch::Tensor slots,
+               torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> k_scale,
+               c10::optional<torch::Tensor> v_scale, int64_t kv_dtype, torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(qkv.device());
+  need(qkv, "qkv", torch::kBFloat16);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "kv_append: qkv must be row-major 2-D");
+  need_contig(slots, "slots", torch::kInt32);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "kv_append: caches must be contiguous");
+  LkKvAppendDesc d{};
+  d.qkv = qkv.data_ptr(); d.ld = qkv.stride(0); d.T = (int)qkv.size(0);
+  d.Hq = (int)Hq; d.Hkv = (int)Hkv; d.Dh = (int)Dh;
+  d.slots = slots.data_ptr<int>();
+  d.k_cache = k_cache.data_ptr(); d.v_cache = v_cache.data_ptr();
+  d.k_scale = optp<float>(k_scale); d.v_scale = optp<float>(v_scale);
+  d.num_slots = (int)(k_cache.numel() / (Hkv * Dh));
+  d.kv_dtype = (int)kv_dtype;
+  d.status = status.data_ptr<int>();
+  TORCH_CHECK(kv_dtype == 0 || (d.k_scale && d.v_scale), "kv_append: quantized caches need scales");
+  check(lk_kv_append(&d, stream()));
+}
+
+void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                      c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale,
+                      torch::Tensor block_tables, torch::Tensor ctx_lens, int64_t block_size, int64_t Hq,
+                      int64_t Hkv, int64_t Dh, double scale, int64_t split_len, int64_t num_splits,
+                      c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml,
+                      torch::Tensor out, int64_t kv_dtype) {
+  const c10::cuda::CUDAGuard g(q.device());
+  need(q, "q", torch::kBFloat16);
+  need(out, "out", torch::kBFloat16);
+  need_contig(block_tables, "block_tables", torch::kInt32);
+  need_contig(ctx_lens, "ctx_lens", torch::kInt32);
+  LkDecodeDesc d{};
+  d.q = q.data_ptr(); d.ldq = q.stride(0);
+  d.k_cache = k_cache.data_ptr(); d.v_cache = v_cache.data_ptr();
+  d.k_scale = optp<float>(k_scale); d.v_scale = optp<float>(v_scale);
+  d.block_tables = block_tables.data_ptr<int>(); d.max_blocks = (int)block_tables.size(1);
+  d.ctx_lens = ctx_lens.data_ptr<int>();
+  d.block_size = (int)block_size; d.num_seqs = (int)q.size(0);
+  d.Hq = (int)Hq; d.Hkv = (int)Hkv; d.Dh = (int)Dh; d.scale = (float)scale;
+  d.split_len = (int)split_len; d.num_splits = (int)num_splits;
+  d.part_o = optp<float>(part_o); d.part_ml = optp<float>(part_ml);
+  d.out = out.data_ptr(); d.ldo = out.stride(0);
+  d.kv_dtype = (int)kv_dtype;
+  check(lk_decode_attention(&d, stream()));
+}
+
+void kv_gather(torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> k_scale,
+               c10::optional<torch::Tensor> v_scale, torch::Tensor slots, int64_t Hkv, int64_t Dh,
+               torch::Tensor out, int64_t kv_dtype) {
+  const c10::cuda::CUDAGuard g(out.device());
+  need_contig(slots, "slots", torch::kInt32);
+  need(out, "out", torch::kBFloat16);
+  TORCH_CHECK(out.stride(1) == 1 && out.size(0) >= slots.numel(), "kv_gather: out shape");
+  check(lk_kv_gather(k_cache.data_ptr(), v_cache.data_ptr(), optp<float>(k_scale), optp<float>(v_scale),
+                     slots.data_ptr<int>(), (int)slots.numel(), (int)Hkv, (int)Dh, out.data_ptr(), out.stride(0),
+                     (int)kv_dtype, stream()));
+}
+
+void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, int64_t seed, torch::Tensor out_tok,
+            c10::optional<torch::Tensor> out_val) {
+  const c10::cuda::CUDAGuard g(logits.device());
+  need(logits, "logits", torch::kBFloat16);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits must be row-major 2-D");
+  need_contig(out_tok, "out_tok", torch::kInt64);
+  check(lk_sample(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                  optp<float>(temperature), (uint64_t)seed, out_tok.data_ptr<int64_t>(), optp<float>(out_val),
+                  stream()));
+}
+
+void quantize(int64_t fmt, torch::Tensor w, int64_t group, torch::Tensor q, torch::Tensor scale,
+              c10::optional<torch::Tensor> zero) {
+  const c10::cuda::CUDAGuard g(w.device());
+  need_contig(w, "w", torch::kBFloat16);
+  need_contig(scale, "scale", torch::kFloat32);
+  check(lk_quantize((int)fmt, w.data_ptr(), (int)w.size(0), (int)w.size(1), (int)group, q.data_ptr(),
+                    scale.data_ptr<float>(), optp<float>(zero), stream()));
+}
+
+void dequant_gemv(int64_t fmt, torch::Tensor x, torch::Tensor q, torch::Tensor scale,
+                  c10::optional<torch::Tensor> zero, int64_t N, int64_t K, int64_t group, torch::Tensor y) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need(x, "x", torch::kBFloat16);
+  need(y, "y", torch::kBFloat16);
+  TORCH_CHECK(x.stride(1) == 1 && y.stride(1) == 1, "dequant_gemv: row-major x, y");
+  check(lk_dequant_gemv((int)fmt, x.data_ptr(), x.stride(0), (int)x.size(0), q.data_ptr(), scale.data_ptr<float>(),
+                        optp<float>(zero), (int)N, (int)K, (int)group, y.data_ptr(), y.stride(0), stream()));
+}
+
+void dequantize(int64_t fmt, torch::Tensor q, torch::Tensor scale, c10::optional<torch::Tensor> zero, int64_t N,
+                int64_t K, int64_t group, torch::Tensor w) {
+  const c10::cuda::CUDAGuard g(q.device());
+  need_contig(w, "w", torch::kBFloat16);
+  check(lk_dequantize((int)fmt, q.data_ptr(), scale.data_ptr<float>(), optp<float>(zero), (int)N, (int)K,
+                      (int)group, w.data_ptr(), stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -412,6 +520,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optimizer_finalize", &optimizer_finalize);
   m.def("attention_fwd", &attention_fwd);
   m.def("signal_barrier", &signal_barrier);
+  m.def("kv_append", &kv_append);
+  m.def("decode_attention", &decode_attention);
+  m.def("sample", &sample);
+  m.def("kv_gather", &kv_gather);
+  m.def("quantize", &quantize);
+  m.def("dequant_gemv", &dequant_gemv);
+  m.def("dequantize", &dequantize);
   m.def("allgather_copy", &allgather_copy);
   m.def("reduce_scatter_sum", &reduce_scatter_sum);
   m.def("allreduce_sum", &allreduce_sum);

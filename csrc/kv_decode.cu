@@ -1,0 +1,431 @@
+// Serving kernels: K15 paged KV-cache append (bf16 / fp8-e4m3 / int8 with a
+// scale per (token, kv head)), K13 paged decode attention (split-KV with a
+// combine pass, GQA query heads packed per CTA) and K19 sampling (greedy
+// argmax, Gumbel-max temperature sampling).
+//
+// Cache layout per layer: K and V pages [num_blocks, block_size, Hkv, Dh] of
+// the cache dtype, scales [num_blocks, block_size, Hkv] fp32 (quantized
+// caches only).  A token's slot is block_id * block_size + offset; per
+// sequence a block table maps logical block i to a physical block id, so
+// sequences sharing a prefix can point at the same physical blocks.
+//
+// Replaces the reference's KVCache / PagedKVCache (include/nn/kv_cache.hpp:
+// 12-219, a single global page table of fp32 copies), its KVCacheQuantizer
+// (include/nn/quantization_production.hpp:293-316, truncating fake-quant) and
+// the unreachable decode path of TransformerBlock::forward
+// (src/nn/transformer_blocks.cpp:425-483, whose running softmax is wrong).
+#include "common.cuh"
+#include "host_util.h"
+#include "lk_api.h"
+
+namespace lk {
+
+template <int KV>  // 0 bf16, 1 fp8 e4m3, 2 int8
+struct KvT;
+template <>
+struct KvT<0> {
+  using T = __nv_bfloat16;
+  static constexpr float QMAX = 1.f;
+};
+template <>
+struct KvT<1> {
+  using T = __nv_fp8_e4m3;
+  static constexpr float QMAX = 448.f;
+};
+template <>
+struct KvT<2> {
+  using T = int8_t;
+  static constexpr float QMAX = 127.f;
+};
+
+template <int KV>
+__device__ __forceinline__ typename KvT<KV>::T kv_encode(float x, float inv_scale) {
+  if constexpr (KV == 0) {
+    return __float2bfloat16(x);
+  } else if constexpr (KV == 1) {
+    return __nv_fp8_e4m3(x * inv_scale);  // saturating round-to-nearest-even
+  } else {
+    float q = rintf(x * inv_scale);
+    q = fminf(fmaxf(q, -127.f), 127.f);
+    return (int8_t)q;
+  }
+}
+
+template <int KV>
+__device__ __forceinline__ float kv_decode(typename KvT<KV>::T v) {
+  if constexpr (KV == 0) return __bfloat162float(v);
+  else if constexpr (KV == 1) return float(v);
+  else return (float)v;
+}
+
+// One warp per (token, kv head, K|V): amax over Dh, scale, encode, store.
+template <int KV>
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld, int T, int Hq,
+                                 int Hkv, int Dh, const int* __restrict__ slots,
+                                 typename KvT<KV>::T* __restrict__ kc, typename KvT<KV>::T* __restrict__ vc,
+                                 float* __restrict__ ks, float* __restrict__ vs, int num_slots,
+                                 int* status) {
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)T * Hkv * 2) return;
+  const int which = (int)(w & 1);  // 0 = K, 1 = V
+  const int h = (int)((w >> 1) % Hkv);
+  const int t = (int)((w >> 1) / Hkv);
+  const int slot = slots[t];
+  if (slot < 0) return;
+  if (slot >= num_slots) {
+    if (lane == 0 && status) atomicCAS(status, 0, LK_ERR_BAD_INDEX);
+    return;
+  }
+  const __nv_bfloat16* src = qkv + (int64_t)t * ld + (Hq + which * Hkv + h) * Dh;
+  float x[4];
+  float amax = 0.f;
+  const int per = Dh / 32;  // 2 or 4
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[i] = i < per ? __bfloat162float(src[lane * per + i]) : 0.f;
+    amax = fmaxf(amax, fabsf(x[i]));
+  }
+  amax = warp_max(amax);
+  const float scale = (KV == 0 || amax == 0.f) ? 1.f : amax / KvT<KV>::QMAX;
+  const float inv = 1.f / scale;
+  typename KvT<KV>::T* dst = (which ? vc : kc) + ((int64_t)slot * Hkv + h) * Dh;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (i < per) dst[lane * per + i] = kv_encode<KV>(x[i], inv);
+  if (KV != 0 && lane == 0) (which ? vs : ks)[(int64_t)slot * Hkv + h] = scale;
+}
+
+// Decode attention, split-KV.  grid (num_splits, Hkv, num_seqs), 128 threads.
+// Phase 1: each thread scores whole tokens against all G query heads of the
+// kv head (q in shared memory); phase 2: softmax statistics; phase 3: thread d
+// accumulates sum_t p[g][t] * v[t][d].  Writes unnormalised partial outputs
+// plus (max, sum) per (split, head) when num_splits > 1, else the final output.
+template <int KV, int DH, int G>
+__global__ void __launch_bounds__(128) decode_attn_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq, const typename KvT<KV>::T* __restrict__ kc,
+    const typename KvT<KV>::T* __restrict__ vc, const float* __restrict__ ks, const float* __restrict__ vs,
+    const int* __restrict__ block_tables, int max_blocks, const int* __restrict__ ctx_lens,
+    int block_size, int Hkv, float sl2, int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo,
+    float* __restrict__ part_o, float* __restrict__ part_ml, int num_splits) {
+  extern __shared__ float sm[];
+  float* sq = sm;                 // [G][DH]
+  float* sp = sm + G * DH;        // [G][split_len] scores -> probabilities
+  __shared__ float red[G][4];
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int ctx = ctx_lens[seq];
+  const int t0 = split * split_len;
+  const int t1 = min(ctx, t0 + split_len);
+  const int n = max(0, t1 - t0);
+  const int tid = threadIdx.x;
+  for (int i = tid; i < G * DH; i += 128) {
+    const int g = i / DH, d = i % DH;
+    sq[i] = __bfloat162float(q[(int64_t)seq * ldq + (kvh * G + g) * DH + d]);
+  }
+  __syncthreads();
+  const int* bt = block_tables + (int64_t)seq * max_blocks;
+  // phase 1: scores (log2 domain)
+  for (int tt = tid; tt < n; tt += 128) {
+    const int t = t0 + tt;
+    const int blk = bt[t / block_size];
+    const int64_t slot = (int64_t)blk * block_size + (t % block_size);
+    const typename KvT<KV>::T* kp = kc + (slot * Hkv + kvh) * DH;
+    const float kscale = KV == 0 ? 1.f : ks[slot * Hkv + kvh];
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < DH; ++d) {
+      const float kv = kv_decode<KV>(kp[d]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] += sq[g * DH + d] * kv;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sp[g * split_len + tt] = acc[g] * kscale * sl2;
+  }
+  __syncthreads();
+  // phase 2: max and sum per head
+  const int warp = tid >> 5, lane = tid & 31;
+  float mx[G], sum[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float m = -INFINITY;
+    for (int tt = tid; tt < n; tt += 128) m = fmaxf(m, sp[g * split_len + tt]);
+    m = warp_max(m);
+    if (lane == 0) red[g][warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) mx[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float s = 0.f;
+    for (int tt = tid; tt < n; tt += 128) {
+      const float p = mx[g] == -INFINITY ? 0.f : fast_exp2(sp[g * split_len + tt] - mx[g]);
+      sp[g * split_len + tt] = p;
+      s += p;
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[g][warp] = s;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) sum[g] = red[g][0] + red[g][1] + red[g][2] + red[g][3];
+  // phase 3: P V, thread d owns output column d (DH <= 128)
+  for (int d = tid; d < DH; d += 128) {
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    for (int tt = 0; tt < n; ++tt) {
+      const int t = t0 + tt;
+      const int blk = bt[t / block_size];
+      const int64_t slot = (int64_t)blk * block_size + (t % block_size);
+      const float vscale = KV == 0 ? 1.f : vs[slot * Hkv + kvh];
+      const float vv = kv_decode<KV>(vc[(slot * Hkv + kvh) * DH + d]) * vscale;
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] += sp[g * split_len + tt] * vv;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int h = kvh * G + g;
+      if (num_splits == 1) {
+        const float inv = sum[g] > 0.f ? 1.f / sum[g] : 0.f;
+        out[(int64_t)seq * ldo + h * DH + d] = __float2bfloat16(acc[g] * inv);
+      } else {
+        part_o[(((int64_t)seq * (Hkv * G) + h) * num_splits + split) * DH + d] = acc[g];
+      }
+    }
+  }
+  if (num_splits > 1 && tid < G) {
+    const int h = kvh * G + tid;
+    float* ml = part_ml + (((int64_t)seq * (Hkv * G) + h) * num_splits + split) * 2;
+    ml[0] = mx[tid];
+    ml[1] = sum[tid];
+  }
+}
+
+// Combine split partials: one warp per (seq, head).
+template <int DH>
+__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                      int num_seqs, int Hq, int num_splits, const int* __restrict__ ctx_lens,
+                                      int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)num_seqs * Hq) return;
+  const int seq = (int)(w / Hq), h = (int)(w % Hq);
+  const int used = min(num_splits, (ctx_lens[seq] + split_len - 1) / split_len);
+  const float* ml = part_ml + w * num_splits * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < used; ++s) M = fmaxf(M, ml[2 * s]);
+  float L = 0.f;
+  float acc[DH / 32];
+#pragma unroll
+  for (int i = 0; i < DH / 32; ++i) acc[i] = 0.f;
+  for (int s = 0; s < used; ++s) {
+    const float m = ml[2 * s];
+    const float f = m == -INFINITY ? 0.f : fast_exp2(m - M);
+    L += ml[2 * s + 1] * f;
+    const float* po = part_o + (w * num_splits + s) * DH;
+#pragma unroll
+    for (int i = 0; i < DH / 32; ++i) acc[i] += po[lane + 32 * i] * f;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int i = 0; i < DH / 32; ++i)
+    out[(int64_t)seq * ldo + h * DH + lane + 32 * i] = __float2bfloat16(acc[i] * inv);
+}
+
+// Gather a sequence's cached K/V (token t at slot slots[t]) into contiguous
+// bf16 rows [n, 2*Hkv*Dh]: keys in columns [0, Hkv*Dh), values after.
+template <int KV>
+__global__ void kv_gather_kernel(const typename KvT<KV>::T* __restrict__ kc, const typename KvT<KV>::T* __restrict__ vc,
+                                 const float* __restrict__ ks, const float* __restrict__ vs,
+                                 const int* __restrict__ slots, int n, int Hkv, int Dh,
+                                 __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t total = (int64_t)n * 2 * Hkv * Dh;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % Dh);
+    const int64_t r = idx / Dh;
+    const int h = (int)(r % Hkv);
+    const int which = (int)((r / Hkv) & 1);
+    const int t = (int)(r / (2 * Hkv));
+    const int64_t slot = slots[t];
+    const int64_t src = (slot * Hkv + h) * Dh + d;
+    float v = kv_decode<KV>((which ? vc : kc)[src]);
+    if (KV != 0) v *= (which ? vs : ks)[slot * Hkv + h];
+    out[(int64_t)t * ldo + (which * Hkv + h) * Dh + d] = __float2bfloat16(v);
+  }
+}
+
+// ---------------------------------------------------------------- sampling
+// Greedy: argmax per row (ties -> lowest index).  Temperature > 0: Gumbel-max
+// with a counter-based hash of (seed, row, column), i.e. an exact sample from
+// softmax(logits / temperature).
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  // 32-bit finaliser of a multiply-xorshift hash (public-domain "lowbias32")
+  x ^= x >> 16;
+  x *= 0x7feb352dU;
+  x ^= x >> 15;
+  x *= 0x846ca68bU;
+  x ^= x >> 16;
+  return x;
+}
+
+__global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V,
+                              const float* __restrict__ temperature, uint64_t seed,
+                              int64_t* __restrict__ out_tok, float* __restrict__ out_val) {
+  const int row = blockIdx.x;
+  const float temp = temperature ? temperature[row] : 0.f;
+  const __nv_bfloat16* z = logits + (int64_t)row * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    float v = __bfloat162float(z[j]);
+    if (temp > 0.f) {
+      const uint32_t h = mix32((uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U) ^
+                               mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
+      const float u = ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+      v = v / temp - logf(-logf(u));
+    }
+    if (v > best || (v == best && j < bi)) {
+      best = v;
+      bi = j;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sb[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+      if (sb[k] > best || (sb[k] == best && si[k] < bi)) {
+        best = sb[k];
+        bi = si[k];
+      }
+    out_tok[row] = bi;
+    if (out_val) out_val[row] = best;
+  }
+}
+
+template <int KV, int DH>
+static int launch_decode_g(const LkDecodeDesc& d, int G, int nsplit, int smem, cudaStream_t s) {
+  dim3 grid(nsplit, d.Hkv, d.num_seqs);
+  const float sl2 = d.scale * 1.4426950408889634f;
+  using T = typename KvT<KV>::T;
+#define LK_DEC(GG)                                                                                   \
+  {                                                                                                  \
+    auto k = decode_attn_kernel<KV, DH, GG>;                                                         \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    k<<<grid, 128, smem, s>>>((const __nv_bfloat16*)d.q, d.ldq, (const T*)d.k_cache, (const T*)d.v_cache, \
+                              d.k_scale, d.v_scale, d.block_tables, d.max_blocks, d.ctx_lens,        \
+                              d.block_size, d.Hkv, sl2, d.split_len, (__nv_bfloat16*)d.out, d.ldo,   \
+                              d.part_o, d.part_ml, nsplit);                                          \
+    break;                                                                                           \
+  }
+  switch (G) {
+    case 1: LK_DEC(1)
+    case 2: LK_DEC(2)
+    case 4: LK_DEC(4)
+    case 8: LK_DEC(8)
+    default: return fail("decode_attention: GQA group must be 1, 2, 4 or 8");
+  }
+#undef LK_DEC
+  if (check_launch("decode_attn")) return -1;
+  if (nsplit > 1) {
+    const int64_t warps = (int64_t)d.num_seqs * d.Hkv * G;
+    decode_combine_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
+        d.part_o, d.part_ml, d.num_seqs, d.Hkv * G, nsplit, d.ctx_lens, d.split_len,
+        (__nv_bfloat16*)d.out, d.ldo);
+    return check_launch("decode_combine");
+  }
+  return 0;
+}
+
+}  // namespace lk
+
+using namespace lk;
+
+extern "C" int lk_kv_append(const LkKvAppendDesc* d, cudaStream_t s) {
+  LK_REQUIRE(d->Dh == 64 || d->Dh == 128, "kv_append: head_dim must be 64 or 128");
+  const int64_t warps = (int64_t)d->T * d->Hkv * 2;
+  if (warps == 0) return 0;
+  const int grid = cdiv(warps * 32, 256);
+  switch (d->kv_dtype) {
+    case 0:
+      kv_append_kernel<0><<<grid, 256, 0, s>>>((const __nv_bfloat16*)d->qkv, d->ld, d->T, d->Hq, d->Hkv, d->Dh,
+                                               d->slots, (__nv_bfloat16*)d->k_cache, (__nv_bfloat16*)d->v_cache,
+                                               nullptr, nullptr, d->num_slots, d->status);
+      break;
+    case 1:
+      kv_append_kernel<1><<<grid, 256, 0, s>>>((const __nv_bfloat16*)d->qkv, d->ld, d->T, d->Hq, d->Hkv, d->Dh,
+                                               d->slots, (__nv_fp8_e4m3*)d->k_cache, (__nv_fp8_e4m3*)d->v_cache,
+                                               d->k_scale, d->v_scale, d->num_slots, d->status);
+      break;
+    case 2:
+      kv_append_kernel<2><<<grid, 256, 0, s>>>((const __nv_bfloat16*)d->qkv, d->ld, d->T, d->Hq, d->Hkv, d->Dh,
+                                               d->slots, (int8_t*)d->k_cache, (int8_t*)d->v_cache, d->k_scale,
+                                               d->v_scale, d->num_slots, d->status);
+      break;
+    default:
+      return fail("kv_append: kv_dtype must be 0 (bf16), 1 (fp8) or 2 (int8)");
+  }
+  return check_launch("kv_append");
+}
+
+extern "C" int lk_decode_attention(const LkDecodeDesc* d, cudaStream_t s) {
+  LK_REQUIRE(d->Dh == 64 || d->Dh == 128, "decode_attention: head_dim must be 64 or 128");
+  LK_REQUIRE(d->Hq % d->Hkv == 0, "decode_attention: Hq % Hkv");
+  LK_REQUIRE(d->split_len > 0 && d->split_len <= 1024, "decode_attention: split_len in (0, 1024]");
+  if (d->num_seqs == 0) return 0;
+  const int G = d->Hq / d->Hkv;
+  const int nsplit = d->num_splits;
+  LK_REQUIRE(nsplit == 1 || (d->part_o && d->part_ml), "decode_attention: split partial buffers needed");
+  const int smem = (G * d->Dh + G * d->split_len) * (int)sizeof(float);
+  if (d->kv_dtype == 0)
+    return d->Dh == 64 ? launch_decode_g<0, 64>(*d, G, nsplit, smem, s) : launch_decode_g<0, 128>(*d, G, nsplit, smem, s);
+  if (d->kv_dtype == 1)
+    return d->Dh == 64 ? launch_decode_g<1, 64>(*d, G, nsplit, smem, s) : launch_decode_g<1, 128>(*d, G, nsplit, smem, s);
+  if (d->kv_dtype == 2)
+    return d->Dh == 64 ? launch_decode_g<2, 64>(*d, G, nsplit, smem, s) : launch_decode_g<2, 128>(*d, G, nsplit, smem, s);
+  return fail("decode_attention: bad kv_dtype");
+}
+
+extern "C" int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale,
+                            const float* v_scale, const int* slots, int n, int Hkv, int Dh, void* out,
+                            int64_t ldo, int kv_dtype, cudaStream_t s) {
+  const int64_t work = (int64_t)n * 2 * Hkv * Dh;
+  if (work == 0) return 0;
+  const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms() * 8);
+  if (kv_dtype == 0)
+    kv_gather_kernel<0><<<grid, 256, 0, s>>>((const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, k_scale,
+                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+  else if (kv_dtype == 1)
+    kv_gather_kernel<1><<<grid, 256, 0, s>>>((const __nv_fp8_e4m3*)k_cache, (const __nv_fp8_e4m3*)v_cache, k_scale,
+                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+  else
+    kv_gather_kernel<2><<<grid, 256, 0, s>>>((const int8_t*)k_cache, (const int8_t*)v_cache, k_scale, v_scale,
+                                             slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+  return check_launch("kv_gather");
+}
+
+extern "C" int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
+                         uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s) {
+  if (rows == 0) return 0;
+  sample_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, seed, out_tok, out_val);
+  return check_launch("sample");
+}

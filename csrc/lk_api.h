@@ -160,6 +160,12 @@ typedef struct LkAttnDesc {
   int causal, window;
   float scale;
   int* status;
+  // Optional separate key/value source (serving prefill over a cached prefix):
+  // when kv != NULL, qkv holds only the queries [B*S, Hq*Dh] and kv holds
+  // [B*Skv, 2*Hkv*Dh] (keys then values); query i sits at position q_off + i.
+  const void* kv;
+  int64_t ld_kv;
+  int Skv, q_off;
 } LkAttnDesc;
 int lk_attention_fwd(const LkAttnDesc* d, cudaStream_t s);
 
@@ -181,6 +187,57 @@ typedef struct LkAttnBwdDesc {
   int* status;
 } LkAttnBwdDesc;
 int lk_attention_bwd(const LkAttnBwdDesc* d, cudaStream_t s);
+
+// ------------------------------------------- K15 KV append / K13 decode / K19
+typedef struct LkKvAppendDesc {
+  const void* qkv;  // [T, (Hq+2Hkv)*Dh] bf16 (post-RoPE), row pitch ld
+  int64_t ld;
+  int T, Hq, Hkv, Dh;
+  const int* slots;  // [T] block_id * block_size + offset, < 0 = skip
+  void* k_cache;     // [num_slots, Hkv, Dh]
+  void* v_cache;
+  float* k_scale;    // [num_slots, Hkv] (quantized caches)
+  float* v_scale;
+  int num_slots;
+  int kv_dtype;      // 0 bf16, 1 fp8 e4m3, 2 int8
+  int* status;
+} LkKvAppendDesc;
+int lk_kv_append(const LkKvAppendDesc* d, cudaStream_t s);
+
+typedef struct LkDecodeDesc {
+  const void* q;  // [num_seqs, Hq*Dh] bf16, row pitch ldq
+  int64_t ldq;
+  const void* k_cache;
+  const void* v_cache;
+  const float* k_scale;
+  const float* v_scale;
+  const int* block_tables;  // [num_seqs, max_blocks]
+  int max_blocks;
+  const int* ctx_lens;      // [num_seqs]
+  int block_size, num_seqs, Hq, Hkv, Dh;
+  float scale;
+  int split_len, num_splits;
+  float* part_o;   // [num_seqs, Hq, num_splits, Dh] when num_splits > 1
+  float* part_ml;  // [num_seqs, Hq, num_splits, 2]
+  void* out;       // [num_seqs, Hq*Dh] bf16
+  int64_t ldo;
+  int kv_dtype;
+} LkDecodeDesc;
+int lk_decode_attention(const LkDecodeDesc* d, cudaStream_t s);
+int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale, const float* v_scale,
+                 const int* slots, int n, int Hkv, int Dh, void* out, int64_t ldo, int kv_dtype,
+                 cudaStream_t s);
+int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
+              uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s);
+
+// ------------------------------------------------------ K14 quantised weights
+enum LkQuantFmt { LK_Q_INT8 = 0, LK_Q_FP8 = 1, LK_Q_INT4 = 2 };
+int lk_quantize(int fmt, const void* w, int N, int K, int group, void* q, float* scale, float* zero,
+                cudaStream_t s);
+int lk_dequant_gemv(int fmt, const void* x, int64_t ldx, int M, const void* q, const float* scale,
+                    const float* zero, int N, int K, int group, void* y, int64_t ldy, cudaStream_t s);
+int lk_dequantize(int fmt, const void* q, const float* scale, const float* zero, int N, int K,
+                  int group, void* w, cudaStream_t s);
 
 // ---------------------------------------------- peer-memory collectives (comm.cu)
 // Pointer arguments named *_ptrs are DEVICE arrays of `world` peer pointers

@@ -26,7 +26,10 @@ def _buf(key, numel, device):
 
 def attention_fwd(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, Dh: int, *,
                   causal: bool = True, window: int = 0, scale: Optional[float] = None,
-                  out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
+                  out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                  kv: Optional[torch.Tensor] = None, q_off: int = 0):
+    """Self-attention over packed qkv, or (kv given) queries qkv [B*S, Hq*Dh] at
+    positions q_off.. against keys/values kv [B*Skv, 2*Hkv*Dh] at positions 0.."""
     require_device(qkv)
     scale = 1.0 / math.sqrt(Dh) if scale is None else scale
     if out is None:
@@ -34,7 +37,7 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, Dh: int,
     if lse is None:
         lse = torch.empty(B, Hq, S, dtype=torch.float32, device=qkv.device)
     C().attention_fwd(qkv, out, lse, B, S, Hq, Hkv, Dh, bool(causal), int(window), float(scale),
-                      status(qkv.device))
+                      status(qkv.device), kv, int(q_off))
     return out, lse
 
 

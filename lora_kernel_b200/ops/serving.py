@@ -1,0 +1,110 @@
+"""K13 paged decode attention, K15 KV append / gather, K19 sampling, K14
+quantised-weight kernels: Python wrappers."""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .._ext import C, require_device, status
+
+KV_DTYPES = {"bf16": 0, "fp8": 1, "int8": 2}
+KV_TORCH = {"bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn, "int8": torch.int8}
+QFMT = {"int8": 0, "fp8": 1, "int4": 2}
+
+
+def kv_append(qkv: torch.Tensor, Hq: int, Hkv: int, Dh: int, slots: torch.Tensor, k_cache, v_cache,
+              k_scale=None, v_scale=None, kv_dtype: str = "bf16") -> None:
+    require_device(qkv)
+    C().kv_append(qkv, Hq, Hkv, Dh, slots, k_cache, v_cache, k_scale, v_scale, KV_DTYPES[kv_dtype],
+                  status(qkv.device))
+
+
+def kv_gather(k_cache, v_cache, k_scale, v_scale, slots: torch.Tensor, Hkv: int, Dh: int,
+              kv_dtype: str = "bf16", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(slots.numel(), 2 * Hkv * Dh, dtype=torch.bfloat16, device=slots.device)
+    C().kv_gather(k_cache, v_cache, k_scale, v_scale, slots, Hkv, Dh, out, KV_DTYPES[kv_dtype])
+    return out
+
+
+_parts = {}
+
+
+def decode_attention(q: torch.Tensor, k_cache, v_cache, k_scale, v_scale, block_tables: torch.Tensor,
+                     ctx_lens: torch.Tensor, block_size: int, Hq: int, Hkv: int, Dh: int, *,
+                     kv_dtype: str = "bf16", max_ctx: int = 0, split_len: int = 512,
+                     out: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
+    """q [num_seqs, Hq*Dh] (post-RoPE) -> out [num_seqs, Hq*Dh]; ctx_lens include the new token."""
+    require_device(q)
+    n = q.shape[0]
+    scale = 1.0 / math.sqrt(Dh) if scale is None else scale
+    if out is None:
+        out = torch.empty(n, Hq * Dh, dtype=torch.bfloat16, device=q.device)
+    max_ctx = max_ctx or block_tables.shape[1] * block_size
+    nsplit = max(1, (max_ctx + split_len - 1) // split_len)
+    po = pm = None
+    if nsplit > 1:
+        key = (q.device, n, Hq, nsplit, Dh)
+        bufs = _parts.get(key)
+        if bufs is None:
+            bufs = (torch.empty(n * Hq * nsplit * Dh, device=q.device),
+                    torch.empty(n * Hq * nsplit * 2, device=q.device))
+            _parts[key] = bufs
+        po, pm = bufs
+    C().decode_attention(q, k_cache, v_cache, k_scale, v_scale, block_tables, ctx_lens, block_size, Hq,
+                         Hkv, Dh, float(scale), split_len, nsplit, po, pm, out, KV_DTYPES[kv_dtype])
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None, seed: int = 0) -> torch.Tensor:
+    """Greedy (temperature 0 / None) or exact temperature sampling (Gumbel-max)."""
+    require_device(logits)
+    tok = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    C().sample(logits, temperature, int(seed) & ((1 << 63) - 1), tok, None)
+    return tok
+
+
+class QuantizedWeight:
+    """A [N, K] weight quantised on the device: int8 / fp8 per row, int4 per group."""
+
+    def __init__(self, w: torch.Tensor, fmt: str = "int4", group: int = 128):
+        require_device(w)
+        w = w.to(torch.bfloat16).contiguous()
+        N, K = w.shape
+        self.fmt, self.group, self.N, self.K = fmt, group, N, K
+        dev = w.device
+        if fmt == "int4":
+            self.q = torch.empty(N, K // 2, dtype=torch.uint8, device=dev)
+            self.scale = torch.empty(N, K // group, dtype=torch.float32, device=dev)
+            self.zero = torch.empty(N, K // group, dtype=torch.float32, device=dev)
+        else:
+            self.q = torch.empty(N, K, dtype=torch.int8 if fmt == "int8" else torch.uint8, device=dev)
+            self.scale = torch.empty(N, dtype=torch.float32, device=dev)
+            self.zero = None
+        C().quantize(QFMT[fmt], w, group, self.q, self.scale, self.zero)
+
+    def dequantize(self, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.q.device)
+        C().dequantize(QFMT[self.fmt], self.q, self.scale, self.zero, self.N, self.K, self.group, out)
+        return out
+
+    def nbytes(self) -> int:
+        n = self.q.numel() * self.q.element_size() + self.scale.numel() * 4
+        return n + (self.zero.numel() * 4 if self.zero is not None else 0)
+
+    def matmul_t(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [M, K] @ W^T -> [M, N]: dequantising GEMV for M <= 16, otherwise a
+        dequantise-to-bf16 pass followed by the tcgen05 GEMM."""
+        M = x.shape[0]
+        if out is None:
+            out = torch.empty(M, self.N, dtype=torch.bfloat16, device=x.device)
+        if M <= 16:
+            C().dequant_gemv(QFMT[self.fmt], x, self.q, self.scale, self.zero, self.N, self.K, self.group, out)
+            return out
+        from .gemm import gemm
+        w = self.dequantize(scratch)
+        return gemm(x, w, out)

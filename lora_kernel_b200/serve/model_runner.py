@@ -1,0 +1,217 @@
+"""Inference forward passes over the paged KV cache.
+
+One `ModelRunner` per GPU holds the (optionally quantised) weights and the KV
+cache of every layer and runs two kinds of batches:
+
+  prefill   chunks of prompts (several sequences, token rows concatenated):
+            GEMMs over all rows at once; RoPE at each token's position; the
+            chunk's K/V appended to the cache (K15); attention per sequence
+            with the tcgen05 flash kernel against the sequence's cached
+            K/V gathered back to bf16 (so prefix-cached blocks are reused);
+  decode    one new token per running sequence: the same GEMMs with M = batch,
+            K15 append, then K13 paged decode attention straight over the
+            (fp8 / int8 / bf16) pages.
+
+The LM head runs only on each sequence's last row; K19 samples the next token.
+Weights can stay bf16 (tcgen05 GEMM, SwiGLU fused into the gate|up epilogue)
+or be int8 / fp8 per row or int4 group-128 (K14: dequantising GEMV for
+decode-sized batches, dequantise + tcgen05 GEMM for prefill-sized ones).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from ..config import TransformerConfig
+from ..models.params import FlatParams
+from ..ops import elementwise as E
+from ..ops import gemm as G
+from ..ops import norm as N
+from ..ops import serving as SV
+from ..ops.attention import attention_fwd
+
+
+@dataclass
+class PrefillItem:
+    seq_id: int
+    tokens: List[int]       # this chunk's token ids
+    start: int              # position of the chunk's first token
+    slots: List[int]        # KV slots of positions [0, start + len(tokens))
+    want_logits: bool       # chunk ends the prompt: sample its next token
+
+
+class ModelRunner:
+    def __init__(self, cfg: TransformerConfig, params: FlatParams, device="cuda", *,
+                 kv_dtype: str = "fp8", weights: str = "none", group_size: int = 128,
+                 num_blocks: int = 0, block_size: int = 16, max_model_len: int = 4096,
+                 mem_fraction: float = 0.85):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.kv_dtype = kv_dtype
+        self.wq = weights
+        self.block_size = block_size
+        self.max_model_len = max_model_len
+        self.params = params
+        self.W: Dict[str, object] = {}
+        self._scratch: Optional[torch.Tensor] = None
+        self._load_weights(params, weights, group_size)
+        H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        per_token = 2 * cfg.num_layers * KV * Dh * (2 if kv_dtype == "bf16" else 1)
+        per_token += 2 * cfg.num_layers * KV * 4 if kv_dtype != "bf16" else 0
+        if num_blocks <= 0:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            num_blocks = max(16, int(free * mem_fraction) // (per_token * block_size))
+        self.num_blocks = num_blocks
+        slots = num_blocks * block_size
+        dt = SV.KV_TORCH[kv_dtype]
+        self.k_cache = torch.zeros(cfg.num_layers, slots, KV, Dh, dtype=dt, device=self.device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        if kv_dtype != "bf16":
+            self.k_scale = torch.zeros(cfg.num_layers, slots, KV, dtype=torch.float32, device=self.device)
+            self.v_scale = torch.zeros_like(self.k_scale)
+        else:
+            self.k_scale = self.v_scale = None
+        self.rope = E.rope_table(max_model_len, Dh, cfg.rope_base, self.device)
+
+    # --------------------------------------------------------------- weights
+    def _load_weights(self, params: FlatParams, fmt: str, group: int) -> None:
+        cfg = self.cfg
+        quant_names = ("wqkv", "wo", "wgu", "wdown")
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}."
+            for n in ("attn_norm", "ffn_norm"):
+                self.W[p + n] = params[p + n]
+            for n in quant_names:
+                w = params[p + n]
+                self.W[p + n] = SV.QuantizedWeight(w, fmt, group) if fmt != "none" else w
+        self.W["embed"] = params["embed"]
+        self.W["final_norm"] = params["final_norm"]
+        self.W["lm_head"] = params["lm_head"]
+
+    def weight_bytes(self) -> int:
+        n = 0
+        for w in self.W.values():
+            n += w.nbytes() if isinstance(w, SV.QuantizedWeight) else w.numel() * w.element_size()
+        return n
+
+    def _linear(self, x: torch.Tensor, name: str, residual: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        w = self.W[name]
+        if isinstance(w, SV.QuantizedWeight):
+            if x.shape[0] > 16:
+                need = w.N * w.K
+                if self._scratch is None or self._scratch.numel() < need:
+                    self._scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
+                y = w.matmul_t(x, scratch=self._scratch[:need].view(w.N, w.K))
+            else:
+                y = w.matmul_t(x)
+            if residual is not None:
+                y += residual
+            return y
+        return G.linear(x, w, residual=residual, out=out)
+
+    def _ffn(self, x: torch.Tensor, p: str, residual: torch.Tensor) -> torch.Tensor:
+        w = self.W[p + "wgu"]
+        if isinstance(w, SV.QuantizedWeight):
+            gu = self._linear(x, p + "wgu")
+            a = E.swiglu_fwd(gu)
+        else:
+            _, a = G.linear_swiglu(x, w)
+        return self._linear(a, p + "wdown", residual=residual)
+
+    # --------------------------------------------------------------- layers
+    def _layer(self, i: int, h: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, attn) -> torch.Tensor:
+        cfg = self.cfg
+        p = f"layers.{i}."
+        xn, _, _ = N.rmsnorm_fwd(h, self.W[p + "attn_norm"], cfg.norm_eps)
+        qkv = self._linear(xn, p + "wqkv")
+        E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, positions=pos)
+        ks = self.k_scale[i] if self.k_scale is not None else None
+        vs = self.v_scale[i] if self.v_scale is not None else None
+        SV.kv_append(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, slots, self.k_cache[i],
+                     self.v_cache[i], ks, vs, self.kv_dtype)
+        o = attn(i, qkv)
+        h2 = self._linear(o, p + "wo", residual=h)
+        xn2, _, _ = N.rmsnorm_fwd(h2, self.W[p + "ffn_norm"], cfg.norm_eps)
+        return self._ffn(xn2, p, h2)
+
+    def _head(self, h_last: torch.Tensor) -> torch.Tensor:
+        xf, _, _ = N.rmsnorm_fwd(h_last, self.W["final_norm"], self.cfg.norm_eps)
+        return G.linear(xf, self.W["lm_head"])
+
+    # -------------------------------------------------------------- prefill
+    @torch.no_grad()
+    def prefill(self, items: List[PrefillItem]) -> Tuple[List[int], torch.Tensor]:
+        """Returns (seq ids that want a token, logits [n, vocab]) for items whose
+        chunk ends the prompt."""
+        cfg = self.cfg
+        dev = self.device
+        ids, pos, slots, bounds = [], [], [], []
+        r = 0
+        for it in items:
+            n = len(it.tokens)
+            ids += it.tokens
+            pos += list(range(it.start, it.start + n))
+            slots += it.slots[it.start:it.start + n]
+            bounds.append((r, r + n))
+            r += n
+        ids_t = torch.tensor(ids, dtype=torch.int64, device=dev)
+        pos_t = torch.tensor(pos, dtype=torch.int32, device=dev)
+        slots_t = torch.tensor(slots, dtype=torch.int32, device=dev)
+        all_slots = [torch.tensor(it.slots[:it.start + len(it.tokens)], dtype=torch.int32, device=dev)
+                     for it in items]
+        H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+
+        def attn(i, qkv):
+            o = torch.empty(qkv.shape[0], H * Dh, dtype=torch.bfloat16, device=dev)
+            ks = self.k_scale[i] if self.k_scale is not None else None
+            vs = self.v_scale[i] if self.v_scale is not None else None
+            for it, (a, b), sl in zip(items, bounds, all_slots):
+                kv = SV.kv_gather(self.k_cache[i], self.v_cache[i], ks, vs, sl, KV, Dh, self.kv_dtype)
+                attention_fwd(qkv[a:b, :H * Dh], 1, b - a, H, KV, Dh, causal=True, out=o[a:b],
+                              kv=kv, q_off=it.start)
+            return o
+
+        h = E.embedding_fwd(ids_t, self.W["embed"])
+        for i in range(cfg.num_layers):
+            h = self._layer(i, h, pos_t, slots_t, attn)
+        want = [k for k, it in enumerate(items) if it.want_logits]
+        if not want:
+            return [], torch.empty(0, cfg.vocab_size, device=dev)
+        rows = torch.tensor([bounds[k][1] - 1 for k in want], dtype=torch.int64, device=dev)
+        logits = self._head(h.index_select(0, rows).contiguous())
+        return [items[k].seq_id for k in want], logits
+
+    # --------------------------------------------------------------- decode
+    @torch.no_grad()
+    def decode(self, tokens: List[int], positions: List[int], slots: List[int],
+               block_tables: List[List[int]]) -> torch.Tensor:
+        """One token per sequence; returns logits [n, vocab]."""
+        cfg = self.cfg
+        dev = self.device
+        n = len(tokens)
+        ids_t = torch.tensor(tokens, dtype=torch.int64, device=dev)
+        pos_t = torch.tensor(positions, dtype=torch.int32, device=dev)
+        slots_t = torch.tensor(slots, dtype=torch.int32, device=dev)
+        mb = max(len(t) for t in block_tables)
+        bt = torch.zeros(n, mb, dtype=torch.int32)
+        for k, t in enumerate(block_tables):
+            bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        bt = bt.to(dev)
+        ctx = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=dev)
+        max_ctx = max(positions) + 1
+        H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+
+        def attn(i, qkv):
+            ks = self.k_scale[i] if self.k_scale is not None else None
+            vs = self.v_scale[i] if self.v_scale is not None else None
+            return SV.decode_attention(qkv[:, :H * Dh], self.k_cache[i], self.v_cache[i], ks, vs, bt, ctx,
+                                       self.block_size, H, KV, Dh, kv_dtype=self.kv_dtype, max_ctx=max_ctx)
+
+        h = E.embedding_fwd(ids_t, self.W["embed"])
+        for i in range(cfg.num_layers):
+            h = self._layer(i, h, pos_t, slots_t, attn)
+        return self._head(h)

@@ -1,0 +1,197 @@
+"""Serving kernels and engine on the GPU against fp32 references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _close(out, ref, rtol, atol, what=""):
+    err = (out.float() - ref.float()).abs()
+    bad = (err > atol + rtol * ref.float().abs()).sum().item()
+    assert bad == 0, f"{what}: {bad} mismatches, max err {err.max().item():.4g}"
+
+
+@pytest.mark.parametrize("kv", ["bf16", "fp8", "int8"])
+@pytest.mark.parametrize("Hq,Hkv,Dh", [(8, 2, 64), (4, 1, 128), (8, 8, 128)])
+def test_kv_append_gather_and_decode(kv, Hq, Hkv, Dh):
+    from lora_kernel_b200.ops import serving as SV
+    torch.manual_seed(0)
+    bs, nblk = 16, 64
+    slots_total = bs * nblk
+    kc = torch.zeros(slots_total, Hkv, Dh, dtype=SV.KV_TORCH[kv], device=dev)
+    vc = torch.zeros_like(kc)
+    ks = vs = None
+    if kv != "bf16":
+        ks = torch.zeros(slots_total, Hkv, device=dev)
+        vs = torch.zeros_like(ks)
+    ctxs = [5, 37, 700]
+    W = (Hq + 2 * Hkv) * Dh
+    tables, kref, vref = [], [], []
+    perm = torch.randperm(nblk).tolist()
+    for c in ctxs:
+        nb = (c + bs - 1) // bs
+        tables.append([perm.pop() for _ in range(nb)])
+    for si, c in enumerate(ctxs):
+        qkv = torch.randn(c, W, device=dev).to(torch.bfloat16)
+        slots = torch.tensor([tables[si][t // bs] * bs + t % bs for t in range(c)], dtype=torch.int32, device=dev)
+        SV.kv_append(qkv, Hq, Hkv, Dh, slots, kc, vc, ks, vs, kv)
+        kref.append(qkv[:, Hq * Dh:(Hq + Hkv) * Dh].float().view(c, Hkv, Dh))
+        vref.append(qkv[:, (Hq + Hkv) * Dh:].float().view(c, Hkv, Dh))
+        g = SV.kv_gather(kc, vc, ks, vs, slots, Hkv, Dh, kv)
+        tol = 1e-2 if kv == "bf16" else (7e-2 if kv == "fp8" else 1.5e-2)
+        _close(g[:, :Hkv * Dh], kref[-1].view(c, -1), tol, tol * 2, "gather K")
+        _close(g[:, Hkv * Dh:], vref[-1].view(c, -1), tol, tol * 2, "gather V")
+    n = len(ctxs)
+    q = torch.randn(n, Hq * Dh, device=dev).to(torch.bfloat16)
+    mb = max(len(t) for t in tables)
+    bt = torch.zeros(n, mb, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t)
+    ctx = torch.tensor(ctxs, dtype=torch.int32, device=dev)
+    for split in (64, 512):
+        out = SV.decode_attention(q, kc, vc, ks, vs, bt.to(dev), ctx, bs, Hq, Hkv, Dh, kv_dtype=kv,
+                                  max_ctx=max(ctxs), split_len=split)
+        for i, c in enumerate(ctxs):
+            qi = q[i].float().view(Hq, Dh)
+            k = kref[i].repeat_interleave(Hq // Hkv, dim=1)  # [c, Hq, Dh]
+            v = vref[i].repeat_interleave(Hq // Hkv, dim=1)
+            s = torch.einsum("hd,thd->ht", qi, k) / math.sqrt(Dh)
+            ref = torch.einsum("ht,thd->hd", torch.softmax(s, -1), v).reshape(-1)
+            tol = 2e-2 if kv == "bf16" else 8e-2
+            _close(out[i], ref, tol, tol, f"decode seq {i} split {split}")
+    from lora_kernel_b200._ext import check_status
+    check_status()
+
+
+@pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
+@pytest.mark.parametrize("M", [1, 5, 16, 40])
+def test_quantized_matmul(fmt, M):
+    from lora_kernel_b200.ops.serving import QuantizedWeight
+    torch.manual_seed(1)
+    N, K = 384, 1024
+    w = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
+    qw = QuantizedWeight(w, fmt, 128)
+    wd = qw.dequantize()
+    # quantisation error bound: int8 / int4 per step, fp8 relative
+    err = (wd.float() - w.float()).abs()
+    if fmt == "int8":
+        bound = qw.scale[:, None] * 0.5 + 1e-3
+    elif fmt == "int4":
+        bound = qw.scale.repeat_interleave(128, 1) * 0.51 + 1e-3
+    else:
+        bound = w.float().abs() * 0.07 + qw.scale[:, None] * 2 ** -9
+    assert torch.all(err <= bound + 1e-3)
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    y = qw.matmul_t(x)
+    ref = x.float() @ wd.float().t()
+    _close(y, ref, 3e-2, 3e-2 * math.sqrt(K) * 0.05, f"{fmt} M={M}")
+
+
+def test_sampling():
+    from lora_kernel_b200.ops.serving import sample
+    torch.manual_seed(2)
+    logits = torch.randn(64, 1000, device=dev).to(torch.bfloat16)
+    tok = sample(logits)
+    assert torch.equal(tok, logits.float().argmax(-1))
+    # Gumbel-max temperature sampling matches the softmax distribution
+    V = 8
+    z = torch.tensor([[0.0, 1.0, 2.0, -1.0, 0.5, 0.0, 3.0, -2.0]], device=dev).repeat(20000, 1).to(torch.bfloat16)
+    temp = torch.full((20000,), 1.0, device=dev)
+    t = sample(z, temp, seed=42)
+    freq = torch.bincount(t, minlength=V).float() / t.numel()
+    p = torch.softmax(z[0].float(), -1)
+    assert torch.allclose(freq, p, atol=0.015), (freq, p)
+
+
+def _tiny_engine(kv="bf16", weights="none", prefix=True):
+    from lora_kernel_b200.config import ServeConfig, TransformerConfig
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.serve.engine import LLMEngine
+    cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=512,
+                            vocab_size=512, num_layers=2, max_seq_len=1024)
+    params = FlatParams(cfg, dev)
+    params.init_(3, 0.08)
+    sc = ServeConfig(num_kv_blocks=256, block_size=16, max_num_batched_tokens=512,
+                     enable_prefix_caching=prefix, max_model_len=1024)
+    return cfg, params, LLMEngine(cfg, params, sc, kv_dtype=kv, weights=weights)
+
+
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_engine_logits_match_full_forward(kv):
+    from lora_kernel_b200.models.llama import LlamaModel
+    from lora_kernel_b200.serve.model_runner import PrefillItem
+    cfg, params, eng = _tiny_engine(kv)
+    model = LlamaModel(cfg, dev, params=params, with_grads=False)
+    torch.manual_seed(4)
+    seq = torch.randint(0, cfg.vocab_size, (300,)).tolist()
+    r = eng.runner
+    table, _ = eng.blocks.allocate(seq)
+    # prefill in two chunks (chunked prefill), then 3 decode steps
+    slots = eng.blocks.slots_for(table, 0, 200)
+    r.prefill([PrefillItem(0, seq[:120], 0, slots[:120], False)])
+    _, lg = r.prefill([PrefillItem(0, seq[120:200], 120, slots, True)])
+    full = model.forward(torch.tensor([seq], device=dev))[0].float()
+    tol = 0.05 if kv == "bf16" else 0.2  # fp8 KV: ~2^-4 relative per element
+    rel = (lg[0].float() - full[199]).norm() / full[199].norm()
+    assert rel < tol, rel
+    for p in range(200, 203):
+        slot = eng.blocks.append_slot(table, p)
+        lg = r.decode([seq[p]], [p], [slot], [table])
+        rel = (lg[0].float() - full[p]).norm() / full[p].norm()
+        assert rel < tol, (p, rel)
+
+
+def test_engine_prefix_cache_and_generate():
+    cfg, params, eng = _tiny_engine("bf16")
+    torch.manual_seed(5)
+    prefix = torch.randint(0, cfg.vocab_size, (96,)).tolist()
+    a = prefix + torch.randint(0, cfg.vocab_size, (40,)).tolist()
+    b = prefix + torch.randint(0, cfg.vocab_size, (23,)).tolist()
+    from lora_kernel_b200.serve.engine import SamplingParams
+    out_a = eng.generate([a], SamplingParams(max_tokens=8))[0]
+    hits0 = eng.blocks.stats.hits
+    out_b = eng.generate([b], SamplingParams(max_tokens=8))[0]
+    assert eng.blocks.stats.hits - hits0 == 6  # 96 / 16 shared blocks
+    # same tokens without the cache
+    _, _, eng2 = _tiny_engine("bf16", prefix=False)
+    assert eng2.generate([b], SamplingParams(max_tokens=8))[0] == out_b
+    # batch of many requests, continuous batching finishes them all
+    prompts = [torch.randint(0, cfg.vocab_size, (int(n),)).tolist() for n in torch.randint(5, 200, (20,))]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=5))
+    assert all(len(o) == 5 for o in outs)
+    assert eng.blocks.num_free() == eng.blocks.num_blocks
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
+def test_engine_quantized_weights_match_dequantized_bf16(fmt):
+    """The quantised-weight engine computes the same logits as a bf16 engine
+    running the dequantised weights (isolates the kernels from quantisation error)."""
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.serve.engine import LLMEngine
+    from lora_kernel_b200.serve.model_runner import PrefillItem
+    from lora_kernel_b200.config import ServeConfig
+    cfg, params, eng = _tiny_engine("bf16", weights=fmt)
+    deq = FlatParams(cfg, dev)
+    deq.flat.copy_(params.flat)
+    for name, w in eng.runner.W.items():
+        if hasattr(w, "dequantize"):
+            deq.views[name].copy_(w.dequantize())
+    sc = ServeConfig(num_kv_blocks=256, block_size=16, max_num_batched_tokens=512, max_model_len=1024)
+    eng_ref = LLMEngine(cfg, deq, sc, kv_dtype="bf16", weights="none")
+    torch.manual_seed(6)
+    seq = torch.randint(0, cfg.vocab_size, (64,)).tolist()
+    outs = []
+    for e in (eng, eng_ref):
+        t, _ = e.blocks.allocate(seq)
+        _, lg = e.runner.prefill([PrefillItem(0, seq, 0, e.blocks.slots_for(t, 0, 64), True)])
+        outs.append(lg[0].float())
+        # decode path (M = 1 -> dequantising GEMV)
+        slot = e.blocks.append_slot(t, 64)
+        outs.append(e.runner.decode([seq[-1]], [64], [slot], [t])[0].float())
+    for a_, b_ in ((outs[0], outs[2]), (outs[1], outs[3])):
+        rel = (a_ - b_).norm() / b_.norm()
+        assert rel < 0.05, rel
+    assert eng.runner.weight_bytes() < eng_ref.runner.weight_bytes()
