@@ -1,0 +1,128 @@
+"""Command line: `python -m lora_kernel_b200 {train,bench,serve,env}`.
+
+  train  --preset NAME | --config FILE [--steps N] [--set section.key=value ...]
+         (launch with torch.distributed.run for more than one GPU: ZeRO-3)
+  bench  [--gpus N --steps K --warmup W]   the headline training benchmark
+         [--kernels]                       kernel micro-benchmarks instead
+         [--serve ...]                     serving load generator
+  serve  --preset NAME [--port P] [--weights int4|int8|fp8|none] [--kv fp8|int8|bf16]
+  env    versions, GPU, NVLink, extension status
+
+Mirrors the reference's train / bench / serve verbs (README.md:107-115,
+main.cpp:18 always ran the train demo).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+
+
+def _overrides(items):
+    out = {}
+    for it in items or []:
+        k, _, v = it.partition("=")
+        try:
+            v = json.loads(v)
+        except json.JSONDecodeError:
+            pass
+        out[k] = v
+    return out
+
+
+def cmd_train(a):
+    from .config import load_config
+    from .parallel.comm import init_distributed
+    from .train.trainer import Trainer
+    rc = load_config(a.config, a.preset, _overrides(a.set))
+    if a.checkpoint_dir:
+        rc.train.checkpoint_dir = a.checkpoint_dir
+    init_distributed("nccl")
+    tr = Trainer(rc)
+    hist = tr.fit(a.steps)
+    if tr.rank == 0 and hist:
+        print(json.dumps(hist[-1]))
+
+
+def cmd_bench(a, rest):
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if a.kernels:
+        from .utils import kernel_bench
+        sys.argv = ["kernel_bench"] + rest
+        kernel_bench.main()
+        return
+    if a.serve:
+        from .serve import bench_serve
+        sys.argv = ["bench_serve"] + rest
+        bench_serve.main()
+        return
+    cmd = [sys.executable, os.path.join(here, "bench.py")] + rest
+    if a.gpus > 1:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={a.gpus}",
+               "--master-addr", "127.0.0.1", "--master-port", "29531", os.path.join(here, "bench.py"),
+               "--gpus", str(a.gpus)] + rest
+    raise SystemExit(subprocess.call(cmd))
+
+
+def cmd_serve(a):
+    from .config import load_config
+    from .models.params import FlatParams
+    from .serve.engine import LLMEngine
+    from .serve.server import serve
+    rc = load_config(a.config, a.preset, _overrides(a.set))
+    cfg = rc.model
+    params = FlatParams(cfg, "cuda")
+    if a.checkpoint:
+        from .train.checkpoint import load_model_safetensors
+        params.load_reference_state_dict({k: v.cuda() for k, v in load_model_safetensors(a.checkpoint).items()})
+    else:
+        params.init_(rc.train.seed, cfg.init_std)
+    eng = LLMEngine(cfg, params, rc.serve, kv_dtype=a.kv or rc.quant.kv_cache,
+                    weights=a.weights or rc.quant.weights, group_size=rc.quant.group_size)
+    serve(eng, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
+          api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps)
+
+
+def cmd_env(_):
+    from .utils.env import env_report
+    print(json.dumps(env_report(), indent=1))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="lora_kernel_b200")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    t = sub.add_parser("train")
+    t.add_argument("--preset", default="cpu-demo")
+    t.add_argument("--config")
+    t.add_argument("--steps", type=int)
+    t.add_argument("--checkpoint-dir")
+    t.add_argument("--set", nargs="*")
+    b = sub.add_parser("bench")
+    b.add_argument("--gpus", type=int, default=1)
+    b.add_argument("--kernels", action="store_true")
+    b.add_argument("--serve", action="store_true")
+    s = sub.add_parser("serve")
+    s.add_argument("--preset", default="llama-8b-serve-int4")
+    s.add_argument("--config")
+    s.add_argument("--host")
+    s.add_argument("--port", type=int)
+    s.add_argument("--weights")
+    s.add_argument("--kv")
+    s.add_argument("--checkpoint")
+    s.add_argument("--set", nargs="*")
+    sub.add_parser("env")
+    a, rest = ap.parse_known_args(argv)
+    if a.cmd == "train":
+        cmd_train(a)
+    elif a.cmd == "bench":
+        cmd_bench(a, rest)
+    elif a.cmd == "serve":
+        cmd_serve(a)
+    else:
+        cmd_env(a)
+
+
+if __name__ == "__main__":
+    main()

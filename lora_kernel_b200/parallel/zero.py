@@ -288,6 +288,8 @@ class Zero3Trainer:
 
     # -------------------------------------------------------------- stepping
     def _optimizer_step(self):
+        if getattr(self, "pre_optimizer", None) is not None:
+            self.pre_optimizer(self.shard_grads)
         o = self.opt
         s = o.scaler
         if self.mode == "p2p":
@@ -319,6 +321,9 @@ class Zero3Trainer:
 
     def current_step(self) -> int:
         return self._opt_steps
+
+    def set_learning_rate(self, lr: float) -> None:
+        self.opt.set_lr(lr)
 
     # --------------------------------------------------------------- utils
     def full_params(self) -> torch.Tensor:

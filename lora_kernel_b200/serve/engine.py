@@ -174,12 +174,12 @@ class LLMEngine:
         if r.first_token_time is None:
             r.first_token_time = now
         self.stats["generated_tokens"] += 1
-        if r.on_token:
-            r.on_token(r, tok)
         if tok in r.params.stop_token_ids:
             r.finished, r.finish_reason = True, "stop"
         elif len(r.output) >= r.params.max_tokens:
             r.finished, r.finish_reason = True, "length"
+        if r.on_token:
+            r.on_token(r, tok)
         if r.finished:
             self.blocks.free_seq(r.table)
             self.running.remove(r)

@@ -86,6 +86,7 @@ class TrainingPipeline:
         self.swa: Optional[SWA] = None
         self.loss_acc = torch.zeros(2, dtype=torch.float32, device=eng.device)
         self.last_loss = float("nan")
+        self.pre_optimizer = None  # optional callable(flat fp32 grads), e.g. fault injection
 
     # ----------------------------------------------------- reference setters
     def set_learning_rate(self, lr: float) -> None:
@@ -120,6 +121,8 @@ class TrainingPipeline:
                                      overwrite_grads=(self._micro % self.accum_steps == 0))
         self._micro += 1
         if self._micro % self.accum_steps == 0:
+            if self.pre_optimizer is not None:
+                self.pre_optimizer(self.engine.grads.flat)
             self.opt.norm_partials(self.engine.grads.flat)
             self.opt.finalize()
             self.opt.apply(self.engine.grads.flat, self.engine.params.flat, zero_grad=False)

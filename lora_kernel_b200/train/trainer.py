@@ -1,0 +1,198 @@
+"""`Trainer.fit()`: the training loop around the B200 engine.
+
+One process per GPU.  World size 1 runs the single-GPU TrainingPipeline; more
+ranks run ZeRO-3 (`parallel.zero.Zero3Trainer`) over peer memory.  The loop:
+learning-rate schedule -> micro-batches (device-resident gradient
+accumulation) -> device-side optimizer step; every `log_every` steps one host
+read of loss / grad-norm / loss scale; periodic and final checkpoints
+(resumable, reshardable); SIGTERM / SIGINT finish the current step, write a
+checkpoint and return; consecutive overflow steps beyond the limit abort;
+heartbeats detect dead ranks between steps; LORAK_FAULT injects host faults.
+
+Reference: ProductionTrainer::train (include/nn/production_trainer.hpp:153-187)
+and the main demo loop (main.cpp:60-72).
+"""
+from __future__ import annotations
+
+import json
+import os
+import signal
+import time
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..config import RunConfig, to_dict
+from ..models.params import FlatParams, build_layout
+from ..parallel.fault import FaultInjector, HeartbeatMonitor
+from ..utils.data import SyntheticTokens
+from ..utils.logging import get_logger, log_fields
+from .checkpoint import Checkpointer, latest
+from .schedules import lr_at
+
+log = get_logger("lora_kernel.train")
+
+
+def _layout_info(cfg, align: int) -> dict:
+    specs, groups, total = build_layout(cfg, align)
+    return {"total": total, "align": align,
+            "specs": {s.name: [s.offset, s.numel] for s in specs}}
+
+
+def remap_flat(src: torch.Tensor, src_layout: dict, dst_layout: dict) -> torch.Tensor:
+    """Move a flat vector between two layouts of the same model (parameter by name)."""
+    out = torch.zeros(dst_layout["total"], dtype=src.dtype)
+    for name, (o, n) in src_layout["specs"].items():
+        if name in dst_layout["specs"]:
+            o2, n2 = dst_layout["specs"][name]
+            assert n == n2, name
+            out[o2:o2 + n] = src[o:o + n]
+    return out
+
+
+class Trainer:
+    def __init__(self, rc: RunConfig, device: Optional[str] = None, data=None):
+        self.rc = rc
+        cfg, tc = rc.model, rc.train
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        if self.world == 1:
+            from .pipeline import Transformer, TrainingPipeline
+            self.model = Transformer(cfg, self.device, seed=tc.seed)
+            self.pipe = TrainingPipeline(self.model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
+            self.align = 64
+        else:
+            from ..parallel.zero import Zero3Trainer
+            self.pipe = Zero3Trainer(cfg, tc, device=self.device)
+            self.align = self.pipe.L.align
+        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed, self.rank)
+        self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
+                                  barrier=(dist.barrier if self.world > 1 else None))
+                     if tc.checkpoint_dir else None)
+        self.step = 0
+        self._stop = False
+        self.faults = FaultInjector(self.rank)
+        self.pipe.pre_optimizer = lambda g: self.faults.on_grads(self.step, g)
+        self.hb = None
+        if self.world > 1 and os.environ.get("LORAK_HEARTBEAT", "1") == "1":
+            store = dist.distributed_c10d._get_default_store()
+            self.hb = HeartbeatMonitor(store, self.rank, self.world,
+                                       timeout_s=float(os.environ.get("LORAK_HEARTBEAT_TIMEOUT", "60")))
+        self.history: List[dict] = []
+
+    # ------------------------------------------------------------ signals
+    def _install_signals(self):
+        def handler(signum, frame):
+            self._stop = True
+            log_fields(log, "signal received; stopping after this step", signal=signum)
+        try:
+            signal.signal(signal.SIGTERM, handler)
+            signal.signal(signal.SIGINT, handler)
+        except ValueError:  # not the main thread
+            pass
+
+    # ------------------------------------------------------- checkpointing
+    def _optim(self):
+        o = self.pipe.opt
+        t = {"p32": o.p32, "m": o.m, "v": o.v, "state": o.state}
+        if o.ema is not None:
+            t["ema"] = o.ema
+        return t
+
+    def _ranges(self) -> List[Tuple[int, int]]:
+        if self.world == 1:
+            return [(0, self.pipe.engine.params.numel)]
+        L = self.pipe.L
+        return [(L.owned(g)[0], L.owned(g)[0] + L.chunk[g]) for g in L.names]
+
+    def save_checkpoint(self, async_save: bool = False) -> Optional[str]:
+        if self.ckpt is None:
+            return None
+        cfg = self.rc.model
+        if self.world == 1:
+            model_state = self.pipe.engine.params.to_reference_state_dict()
+        else:
+            full = self.pipe.full_params()
+            fp = FlatParams(cfg, self.device, torch.bfloat16, buffer=full, group_align=self.align)
+            model_state = fp.to_reference_state_dict() if self.rank == 0 else None
+        state = {"step": self.step, "data": self.data.state(), "config": to_dict(self.rc),
+                 "world": self.world, "time": time.time()}
+        path = self.ckpt.save(self.step, model_state, self._ranges(), self._optim(),
+                              _layout_info(cfg, self.align), state, async_save=async_save)
+        return path
+
+    def load_checkpoint(self, path: str) -> None:
+        with open(os.path.join(path, "index.json")) as f:
+            index = json.load(f)
+        flat = Checkpointer.load_flat(path)
+        mine = _layout_info(self.rc.model, self.align)
+        o = self.pipe.opt
+        with torch.no_grad():
+            for name in ("p32", "m", "v", "ema"):
+                if name not in flat or (name == "ema" and o.ema is None):
+                    continue
+                full = remap_flat(flat[name], index["layout"], mine)
+                if self.world == 1:
+                    dst_full = full
+                else:
+                    dst_full = self.pipe.L.extract_shard(full)
+                getattr(o, name).copy_(dst_full.to(self.device))
+            o.state.copy_(flat["state"].to(self.device))
+            if self.world == 1:
+                self.pipe.engine.params.flat.copy_(o.p32.to(torch.bfloat16))
+            else:
+                self.pipe.shard_p16.copy_(o.p32.to(torch.bfloat16))
+        st = Checkpointer.trainer_state(path)
+        self.step = int(st["step"])
+        self.data.load_state(st.get("data", {}))
+        log_fields(log, "resumed", path=path, step=self.step)
+
+    # ---------------------------------------------------------------- loop
+    def fit(self, steps: Optional[int] = None, resume: bool = True) -> List[dict]:
+        tc = self.rc.train
+        total = steps if steps is not None else tc.total_steps
+        if resume and self.ckpt is not None:
+            p = latest(tc.checkpoint_dir)
+            if p:
+                self.load_checkpoint(p)
+        self._install_signals()
+        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * self.world
+        t_last, s_last = time.perf_counter(), self.step
+        while self.step < total:
+            if self.hb is not None:
+                self.hb.set_step(self.step)
+                self.hb.check()
+            self.faults.at_step(self.step)
+            self.pipe.set_learning_rate(lr_at(self.step, tc.lr, tc.schedule, tc.warmup_steps, total,
+                                              tc.min_lr_ratio))
+            self.pipe.loss_acc.zero_()
+            for _ in range(tc.grad_accum_steps):
+                x, y = self.data.next()
+                self.pipe.micro_step_async(x.to(self.device, non_blocking=True),
+                                           y.to(self.device, non_blocking=True))
+            self.step += 1
+            o = self.pipe.opt
+            if self.step % tc.log_every == 0 or self.step == total:
+                s, n = self.pipe.loss_acc.tolist()
+                now = time.perf_counter()
+                rec = {"step": self.step, "loss": s / max(n, 1.0), "grad_norm": o.grad_norm(),
+                       "loss_scale": o.scaler.get_scale(), "skipped": o.scaler.num_skipped(),
+                       "lr": o.lr, "tokens_per_s": tok_per_step * (self.step - s_last) / (now - t_last)}
+                t_last, s_last = now, self.step
+                self.history.append(rec)
+                if self.rank == 0:
+                    log_fields(log, "train", **rec)
+                if o.scaler.consecutive_skips() > tc.max_consecutive_skips:
+                    raise FloatingPointError(f"{o.scaler.consecutive_skips()} consecutive overflow steps")
+            if self.ckpt is not None and tc.checkpoint_every and self.step % tc.checkpoint_every == 0:
+                self.save_checkpoint(async_save=True)
+            if self._stop:
+                break
+        if self.ckpt is not None:
+            self.save_checkpoint()
+            self.ckpt.finish()
+        if self.hb is not None:
+            self.hb.stop()
+        return self.history

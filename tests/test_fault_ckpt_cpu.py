@@ -1,0 +1,114 @@
+"""Failure detection (gloo / TCPStore ranks on CPU) and checkpoint logic."""
+import json
+import os
+import random
+import time
+
+import pytest
+import torch
+
+from lora_kernel_b200.config import TransformerConfig
+from lora_kernel_b200.parallel.fault import FaultInjector, HeartbeatMonitor, RankFailure, parse_faults
+
+
+def test_parse_faults():
+    f = parse_faults("kill_rank:3@step:7, delay_rank:1@step:2:0.5,nan_grad@step:4")
+    assert [(x.kind, x.rank, x.step, x.arg) for x in f] == [
+        ("kill_rank", 3, 7, 0.0), ("delay_rank", 1, 2, 0.5), ("nan_grad", -1, 4, 0.0)]
+    fi = FaultInjector(0, "raise_rank:0@step:2,nan_grad@step:1")
+    fi.at_step(1)
+    g = torch.zeros(4)
+    fi.on_grads(1, g)
+    assert torch.isnan(g).all()
+    with pytest.raises(RuntimeError):
+        fi.at_step(2)
+
+
+def _hb_worker(rank, world, port, q):
+    from torch.distributed import TCPStore
+    store = TCPStore("127.0.0.1", port, world, is_master=(rank == 0), timeout=__import__("datetime").timedelta(seconds=30))
+    hb = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=1.0)
+    time.sleep(0.5)
+    if rank == 1:
+        os._exit(0)  # the rank dies without warning (store stays up on rank 0)
+    hb.check()  # everyone alive so far
+    deadline = time.time() + 10
+    found = None
+    while time.time() < deadline:
+        try:
+            hb.check()
+        except RankFailure as e:
+            found = e.ranks
+            break
+        time.sleep(0.1)
+    q.put(found)
+
+
+def test_heartbeat_detects_dead_rank():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = random.randint(20000, 40000)
+    ps = [ctx.Process(target=_hb_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    found = q.get(timeout=60)
+    for p in ps:
+        p.join(timeout=30)
+    assert found == [1]
+
+
+def test_checkpoint_roundtrip_and_reshard(tmp_path):
+    from lora_kernel_b200.parallel.zero import ShardLayout
+    from lora_kernel_b200.train.checkpoint import Checkpointer, latest
+    from lora_kernel_b200.train.trainer import _layout_info, remap_flat
+    cfg = TransformerConfig(hidden_dim=128, num_heads=2, head_dim=64, ff_dim=256, vocab_size=300, num_layers=2)
+    # a "2-rank" ZeRO checkpoint written rank by rank
+    world = 2
+    L0 = ShardLayout(cfg, world, 0)
+    lay = _layout_info(cfg, L0.align)
+    full = torch.randn(L0.total)
+    for r in range(world):
+        L = ShardLayout(cfg, world, r)
+        ck = Checkpointer(str(tmp_path), r, world)
+        shard = L.extract_shard(full)
+        ranges = [(L.owned(g)[0], L.owned(g)[0] + L.chunk[g]) for g in L.names]
+        if r == world - 1:
+            ck.save(5, None, ranges, {"p32": shard, "m": shard * 2, "v": shard * 3, "state": torch.arange(16.)},
+                    lay, {"step": 5})
+        else:  # the non-final rank only writes its file (rank 0 publishes)
+            import threading
+            os.makedirs(os.path.join(tmp_path, "step_5.tmp"), exist_ok=True)
+            from safetensors.torch import save_file
+            save_file({"p32": shard, "m": shard * 2, "v": shard * 3, "state": torch.arange(16.)},
+                      os.path.join(tmp_path, "step_5.tmp", f"optim-rank{r}-of-{world}.safetensors"),
+                      metadata={"ranges": json.dumps(ranges)})
+    # rank 1 (non-zero) does not publish; publish as rank 0 would
+    ck0 = Checkpointer(str(tmp_path), 0, world)
+    ck0._pending = (str(tmp_path / "step_5.tmp"), str(tmp_path / "step_5"), 5, lay, {"step": 5})
+    ck0.finish()
+    p = latest(str(tmp_path))
+    assert p.endswith("step_5") and Checkpointer.verify(p)
+    flat = Checkpointer.load_flat(p)
+    # padding between groups is not covered by any shard; parameters must match exactly
+    one = _layout_info(cfg, 64)
+    a = remap_flat(flat["p32"], lay, one)
+    b = remap_flat(full, lay, one)
+    assert torch.equal(a, b)
+    assert torch.equal(remap_flat(flat["m"], lay, one), 2 * b)
+    assert Checkpointer.trainer_state(p)["step"] == 5
+
+
+def test_model_safetensors_reference_names(tmp_path):
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.train.checkpoint import load_model_safetensors, save_model_safetensors
+    cfg = TransformerConfig(hidden_dim=128, num_heads=2, head_dim=64, ff_dim=200, vocab_size=300, num_layers=2)
+    p = FlatParams(cfg, "cpu", torch.float32)
+    p.init_(0, 0.02)
+    path = str(tmp_path / "model.safetensors")
+    save_model_safetensors(p.to_reference_state_dict(), path)
+    sd = load_model_safetensors(path)
+    assert "blocks.1.ffn.Wdown.weight" in sd and sd["token_embedding.weight"].shape == (300, 128)
+    q = FlatParams(cfg, "cpu", torch.float32)
+    q.load_reference_state_dict(sd)
+    assert torch.equal(q.flat, p.flat)

@@ -1,0 +1,140 @@
+"""HTTP contract of the OpenAI-compatible server (CPU, fake engine)."""
+import asyncio
+import json
+import time
+
+import pytest
+from aiohttp.test_utils import TestClient, TestServer
+
+from lora_kernel_b200.serve.kv_cache import CacheStats
+from lora_kernel_b200.serve.server import TokenBucket, create_app, jwt_decode, jwt_encode
+
+
+class _Cfg:
+    vocab_size = 256
+
+
+class _Blocks:
+    stats = CacheStats()
+
+    def usage(self):
+        return 0.0
+
+
+class FakeEngine:
+    """Echoes the prompt's bytes back one token per step."""
+
+    def __init__(self):
+        self.cfg = _Cfg()
+        self.blocks = _Blocks()
+        self.running, self.waiting = [], []
+        self.n = 0
+
+    def add_request(self, prompt, params, on_token=None):
+        class R:
+            pass
+        r = R()
+        r.prompt, r.params, r.on_token = list(prompt), params, on_token
+        r.output, r.finished, r.finish_reason = [], False, None
+        r.arrival, r.first_token_time, r.token_times = time.perf_counter(), None, []
+        self.waiting.append(r)
+        self.n += 1
+        return self.n
+
+    def has_work(self):
+        return bool(self.running or self.waiting)
+
+    def step(self):
+        self.running += self.waiting
+        self.waiting = []
+        done = []
+        for r in list(self.running):
+            t = r.prompt[len(r.output) % len(r.prompt)]
+            r.output.append(t)
+            now = time.perf_counter()
+            r.token_times.append(now)
+            r.first_token_time = r.first_token_time or now
+            if len(r.output) >= r.params.max_tokens:
+                r.finished, r.finish_reason = True, "length"
+            r.on_token(r, t)
+            if r.finished:
+                self.running.remove(r)
+                done.append(r)
+        return done
+
+
+def _run(coro_fn, **kw):
+    async def main():
+        app = create_app(FakeEngine(), **kw)
+        async with TestClient(TestServer(app)) as client:
+            return await coro_fn(client)
+    return asyncio.run(main())
+
+
+def test_completion_json_schema():
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": "hi!", "max_tokens": 5})
+        assert r.status == 200
+        d = await r.json()
+        assert d["object"] == "text_completion" and d["choices"][0]["text"] == "hi!hi"
+        assert d["choices"][0]["finish_reason"] == "length"
+        assert d["usage"] == {"prompt_tokens": 3, "completion_tokens": 5, "total_tokens": 8}
+        r = await c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "yo"}],
+                                                      "max_tokens": 3})
+        d = await r.json()
+        assert d["object"] == "chat.completion" and d["choices"][0]["message"]["role"] == "assistant"
+        r = await c.get("/v1/models")
+        assert (await r.json())["data"][0]["id"]
+        r = await c.get("/health")
+        assert (await r.json())["status"] == "healthy"
+        r = await c.post("/v1/completions", data="not json")
+        assert r.status == 400
+    _run(go)
+
+
+def test_sse_stream_framing():
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": [65, 66], "max_tokens": 4, "stream": True})
+        assert r.headers["Content-Type"].startswith("text/event-stream")
+        body = (await r.read()).decode()
+        events = [e for e in body.split("\n\n") if e]
+        assert all(e.startswith("data: ") for e in events)
+        assert events[-1] == "data: [DONE]"
+        chunks = [json.loads(e[6:]) for e in events[:-1]]
+        assert [ch["token"] for ch in chunks] == [65, 66, 65, 66]
+        assert [ch["index"] for ch in chunks] == [0, 1, 2, 3]
+        assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+        assert "".join(ch["choices"][0]["text"] for ch in chunks) == "ABAB"
+        m = await (await c.get("/metrics")).text()
+        assert "lora_kernel_generation_tokens_total" in m and '_bucket{le="+Inf"}' in m
+    _run(go)
+
+
+def test_auth_and_rate_limit():
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": "x", "max_tokens": 1})
+        assert r.status == 401
+        r = await c.post("/v1/completions", json={"prompt": "x", "max_tokens": 1},
+                         headers={"Authorization": "Bearer k1"})
+        assert r.status == 200
+        tok = jwt_encode({"sub": "u", "exp": time.time() + 60}, "s3cret")
+        r = await c.post("/v1/completions", json={"prompt": "x", "max_tokens": 1},
+                         headers={"Authorization": f"Bearer {tok}"})
+        assert r.status == 200
+        codes = []
+        for _ in range(6):
+            r = await c.post("/v1/completions", json={"prompt": "x", "max_tokens": 1},
+                             headers={"Authorization": "Bearer k1"})
+            codes.append(r.status)
+        assert 429 in codes
+    _run(go, api_keys=("k1",), jwt_secret="s3cret", rate_limit_rps=1.0)
+
+
+def test_jwt_and_bucket_units():
+    t = jwt_encode({"sub": "a", "exp": 100.0}, "k")
+    assert jwt_decode(t, "k", now=50.0)["sub"] == "a"
+    assert jwt_decode(t, "k", now=150.0) is None
+    assert jwt_decode(t, "wrong", now=50.0) is None
+    b = TokenBucket(rate=1.0, burst=2.0)
+    assert b.allow("c", 0.0) and b.allow("c", 0.0) and not b.allow("c", 0.0)
+    assert b.allow("c", 1.5)
