@@ -106,6 +106,7 @@ class TrainConfig:
     checkpoint_every: int = 0
     max_consecutive_skips: int = 20
     log_every: int = 10
+    fixed_batch: bool = False  # reuse one seeded batch every step (the CPU demo's data)
 
 
 @dataclass
@@ -165,7 +166,7 @@ PRESETS: Dict[str, RunConfig] = {
         model=TransformerConfig(hidden_dim=256, num_heads=4, head_dim=64, ff_dim=688,
                                 vocab_size=1024, num_layers=4, max_seq_len=128),
         train=TrainConfig(lr=3e-4, weight_decay=0.1, micro_batch=8, seq_len=128, total_steps=50,
-                          beta2=0.999, dynamic_loss_scale=False)),
+                          beta2=0.999, dynamic_loss_scale=False, fixed_batch=True)),
     "llama-1.1b-zero3": RunConfig(
         model=_llama_1b(),
         train=TrainConfig(micro_batch=4, seq_len=2048, total_steps=100),

@@ -67,7 +67,8 @@ class Trainer:
             from ..parallel.zero import Zero3Trainer
             self.pipe = Zero3Trainer(cfg, tc, device=self.device)
             self.align = self.pipe.L.align
-        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed, self.rank)
+        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed, self.rank,
+                                            fixed=tc.fixed_batch)
         self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
                                   barrier=(dist.barrier if self.world > 1 else None))
                      if tc.checkpoint_dir else None)

@@ -19,16 +19,19 @@ import torch
 
 
 class SyntheticTokens:
-    def __init__(self, vocab: int, batch: int, seq: int, seed: int = 0, rank: int = 0, pin: bool = True):
+    def __init__(self, vocab: int, batch: int, seq: int, seed: int = 0, rank: int = 0, pin: bool = True,
+                 fixed: bool = False):
         self.vocab, self.batch, self.seq = vocab, batch, seq
         self.seed, self.rank = seed, rank
+        self.fixed = fixed  # the same batch every call
         self.cursor = 0
         self.pin = pin and torch.cuda.is_available()
 
     def next(self) -> Tuple[torch.Tensor, torch.Tensor]:
         g = torch.Generator().manual_seed(self.seed * 1_000_003 + self.rank * 7919 + self.cursor)
         x = torch.randint(0, self.vocab, (self.batch, self.seq + 1), generator=g)
-        self.cursor += 1
+        if not self.fixed:
+            self.cursor += 1
         if self.pin:
             x = x.pin_memory()
         return x[:, :-1], x[:, 1:]
