@@ -54,7 +54,6 @@ class ModelRunner:
         self.wq = weights
         self.block_size = block_size
         self.max_model_len = max_model_len
-        self.params = params
         self.W: Dict[str, object] = {}
         self._scratch: Optional[torch.Tensor] = None
         self._load_weights(params, weights, group_size)
@@ -80,16 +79,19 @@ class ModelRunner:
     def _load_weights(self, params: FlatParams, fmt: str, group: int) -> None:
         cfg = self.cfg
         quant_names = ("wqkv", "wo", "wgu", "wdown")
+        # with quantised weights, copy the few bf16 tensors kept as-is out of the
+        # flat buffer so the caller can free the full-precision weights
+        keep = (lambda t: t.clone()) if fmt != "none" else (lambda t: t)
         for i in range(cfg.num_layers):
             p = f"layers.{i}."
             for n in ("attn_norm", "ffn_norm"):
-                self.W[p + n] = params[p + n]
+                self.W[p + n] = keep(params[p + n])
             for n in quant_names:
                 w = params[p + n]
                 self.W[p + n] = SV.QuantizedWeight(w, fmt, group) if fmt != "none" else w
-        self.W["embed"] = params["embed"]
-        self.W["final_norm"] = params["final_norm"]
-        self.W["lm_head"] = params["lm_head"]
+        self.W["embed"] = keep(params["embed"])
+        self.W["final_norm"] = keep(params["final_norm"])
+        self.W["lm_head"] = self.W["embed"] if cfg.tie_embeddings else keep(params["lm_head"])
 
     def weight_bytes(self) -> int:
         n = 0
