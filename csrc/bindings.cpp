@@ -60,7 +60,8 @@ Operand classify(const torch::Tensor& x, const char* name) {
 
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
           c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> h, double alpha,
-          torch::Tensor status, int64_t bn) {
+          torch::Tensor status, int64_t bn, c10::optional<torch::Tensor> a2,
+          c10::optional<torch::Tensor> b2) {
   const c10::cuda::CUDAGuard g(a.device());
   TORCH_CHECK(a.size(1) == b.size(1), "gemm: K mismatch ", a.sizes(), " vs ", b.sizes());
   Operand A = classify(a, "a"), B = classify(b, "b");
@@ -94,6 +95,15 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
   d.bn = (int)bn;
   need(status, "status", torch::kInt32);
   d.status = status.data_ptr<int>();
+  if (a2.has_value() && b2.has_value()) {
+    TORCH_CHECK(a2->size(0) == d.M && b2->size(0) == d.N && a2->size(1) == b2->size(1),
+                "gemm: second segment shapes");
+    Operand A2 = classify(*a2, "a2"), B2 = classify(*b2, "b2");
+    TORCH_CHECK(A2.mn == A.mn && B2.mn == B.mn, "gemm: segment operands must share majorness");
+    d.a2 = A2.base; d.a2_rows = A2.rows; d.a2_cols = A2.cols; d.a2_ld = A2.ld;
+    d.b2 = B2.base; d.b2_rows = B2.rows; d.b2_cols = B2.cols; d.b2_ld = B2.ld;
+    d.K2 = (int)a2->size(1);
+  }
   check(lk_gemm(&d, stream()));
 }
 

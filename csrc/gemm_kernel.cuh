@@ -51,6 +51,7 @@ struct GemmArgs {
   float alpha;
   int* status;
   int tiles_m, tiles_n;
+  int K2;  // > 0: a second contraction segment (A2 . B2^T) accumulated into the same tile
 };
 
 constexpr int GEMM_BM = 128;
@@ -86,6 +87,7 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const GemmArgs args) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -119,6 +121,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.K2 > 0) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
@@ -127,7 +133,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int T = args.tiles_m * args.tiles_n;
-  const int nk = (args.K + GEMM_BK - 1) / GEMM_BK;
+  const int nk1 = (args.K + GEMM_BK - 1) / GEMM_BK;
+  const int nk = nk1 + (args.K2 > 0 ? (args.K2 + GEMM_BK - 1) / GEMM_BK : 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -148,18 +155,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t sa = sbase + s * C::STAGE;
           const uint32_t sb = sa + C::A_BYTES;
           mbar_expect_tx(fb, C::STAGE);
+          // k-blocks [0, nk1) come from (A, B), the rest from the second segment (A2, B2)
+          const bool seg2 = kb >= nk1;
+          const CUtensorMap* ma = seg2 ? &tmA2 : &tmA;
+          const CUtensorMap* mb = seg2 ? &tmB2 : &tmB;
+          const int kc = (seg2 ? kb - nk1 : kb) * GEMM_BK;
           if (!A_MN) {
-            tma_load_2d(sa, &tmA, fb, kb * GEMM_BK, tm * GEMM_BM);
+            tma_load_2d(sa, ma, fb, kc, tm * GEMM_BM);
           } else {
-            tma_load_2d(sa, &tmA, fb, tm * GEMM_BM, kb * GEMM_BK);
-            tma_load_2d(sa + 8192, &tmA, fb, tm * GEMM_BM + 64, kb * GEMM_BK);
+            tma_load_2d(sa, ma, fb, tm * GEMM_BM, kc);
+            tma_load_2d(sa + 8192, ma, fb, tm * GEMM_BM + 64, kc);
           }
           if (!B_MN) {
-            tma_load_2d(sb, &tmB, fb, kb * GEMM_BK, tn * BN);
+            tma_load_2d(sb, mb, fb, kc, tn * BN);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + 8192 * j, &tmB, fb, tn * BN + 64 * j, kb * GEMM_BK);
+              tma_load_2d(sb + 8192 * j, mb, fb, tn * BN + 64 * j, kc);
           }
           pending |= 1u << s;
           parbits = (parbits & ~(1u << s)) | (ph << s);
@@ -366,10 +378,18 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   args.status = g.status;
   args.tiles_m = cdiv(g.M, GEMM_BM);
   args.tiles_n = cdiv(g.N, BN);
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ta2, tb2;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   if (!make_tmap_2d(&ta, g.a, bf, 2, g.a_rows, g.a_cols, g.a_ld, A_MN ? 64 : GEMM_BM, 64)) return -1;
   if (!make_tmap_2d(&tb, g.b, bf, 2, g.b_rows, g.b_cols, g.b_ld, B_MN ? 64 : BN, 64)) return -1;
+  args.K2 = g.K2;
+  if (g.K2 > 0) {
+    if (!make_tmap_2d(&ta2, g.a2, bf, 2, g.a2_rows, g.a2_cols, g.a2_ld, A_MN ? 64 : GEMM_BM, 64)) return -1;
+    if (!make_tmap_2d(&tb2, g.b2, bf, 2, g.b2_rows, g.b2_cols, g.b2_ld, B_MN ? 64 : BN, 64)) return -1;
+  } else {
+    ta2 = ta;
+    tb2 = tb;
+  }
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
@@ -380,7 +400,7 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   }
   const int tiles = args.tiles_m * args.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, args);
+  kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, ta2, tb2, args);
   return check_launch("gemm_tc_kernel");
 }
 

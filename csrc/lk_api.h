@@ -47,6 +47,14 @@ typedef struct LkGemmDesc {
   int epi;
   int bn;  // 0 = choose, 128 or 256
   int* status;
+  // Optional second contraction segment accumulated into the same output:
+  // D = alpha * (A.B^T + A2.B2^T); A2 [M, K2] and B2 [N, K2] share the majorness
+  // of A and B (used by the fused LoRA update: A2 = s*x*A_lora^T, B2 = B_lora).
+  const void* a2;
+  int64_t a2_rows, a2_cols, a2_ld;
+  const void* b2;
+  int64_t b2_rows, b2_cols, b2_ld;
+  int K2;
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);

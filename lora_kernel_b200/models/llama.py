@@ -91,6 +91,9 @@ class LlamaModel:
         self.hooks = None  # optional: pre_forward / pre_layer_fwd(i) / pre_layer_bwd(i) /
         #                    post_layer_bwd(i) / post_head_bwd / post_backward (ZeRO-3)
         self._overwrite = False
+        self.lora = None        # optional LoRAAdapters (models/lora.py)
+        self.train_base = True  # False: frozen base weights (no base weight gradients)
+        self._u: Dict[Tuple[int, str], torch.Tensor] = {}
 
     # -------------------------------------------------------------- helpers
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
@@ -118,7 +121,50 @@ class LlamaModel:
 
     def _wgrad(self, dy, x, name):
         """Weight gradient: stored on the first micro-step of a window, else accumulated."""
+        if not self.train_base and not name.endswith("norm") and name != "embed":
+            return
         G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
+
+    # ------------------------------------------------------ linear + LoRA
+    def _lora_u(self, i: int, t: str, x: torch.Tensor, save: bool):
+        """s * x A^T for an adapted linear (None without an adapter)."""
+        if self.lora is None or not self.lora.has(i, t):
+            return None
+        key = (i, t)
+        u = self._u.get(key) if save else None
+        if u is None or u.shape[0] != x.shape[0]:
+            u = torch.empty(x.shape[0], self.lora.lc.rank, dtype=torch.bfloat16, device=x.device)
+            if save:
+                self._u[key] = u
+        G.gemm(x, self.lora.A(i, t), u, alpha=self.lora.lc.scale)
+        return u
+
+    def _lin(self, i: int, t: str, x, out, residual=None, save: bool = True):
+        u = self._lora_u(i, t, x, save)
+        B = self.lora.B(i, t) if u is not None else None
+        G.gemm(x, self._p(f"layers.{i}.{t}"), out, epi="bf16_resid" if residual is not None else "bf16",
+               residual=residual, a2=u, b2=B)
+        return out
+
+    def _lin_swiglu(self, i: int, x, gu_out, h_out, save: bool = True):
+        u = self._lora_u(i, "wgu", x, save)
+        B = self.lora.B(i, "wgu") if u is not None else None
+        G.gemm(x, self._p(f"layers.{i}.wgu"), gu_out, epi="swiglu", h_out=h_out, a2=u, b2=B)
+
+    def _lin_bwd(self, i: int, t: str, dy, x, dx_out):
+        """dx = dy W (+ s (dy B) A); base and adapter weight gradients."""
+        name = f"layers.{i}.{t}"
+        if self.lora is not None and self.lora.has(i, t):
+            lc = self.lora.lc
+            v = torch.empty(dy.shape[0], lc.rank, dtype=torch.bfloat16, device=dy.device)
+            G.gemm(dy, self.lora.B(i, t).t(), v, alpha=lc.scale)           # s * dy B
+            G.gemm(dy, self._p(name).t(), dx_out, a2=v, b2=self.lora.A(i, t).t())
+            acc = "f32" if self._overwrite else "f32_acc"
+            G.gemm(v.t(), x.t(), self.lora.gA(i, t), epi=acc)               # dA = (s v)^T x
+            G.gemm(dy.t(), self._u[(i, t)].t(), self.lora.gB(i, t), epi=acc)  # dB = dy^T (s u)
+        else:
+            G.linear_dgrad(dy, self._p(name), out=dx_out)
+        self._wgrad(dy, x, name)
 
     # -------------------------------------------------------------- forward
     def _layer_fwd(self, i: int, ws: _Workspace, h_in: torch.Tensor, h_out: torch.Tensor, slot: int):
@@ -127,18 +173,19 @@ class LlamaModel:
         xn1, rstd1 = ws.xn1[slot], ws.rstd1[slot]
         N.rmsnorm_fwd(h_in, self._p(p + "attn_norm"), cfg.norm_eps, y=xn1, rstd=rstd1)
         qkv = ws.qkv[slot]
-        G.linear(xn1, self._p(p + "wqkv"), out=qkv)
+        self._lin(i, "wqkv", xn1, qkv, save=self._saving)
         E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
         A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                         causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
         hmid = ws.hmid[slot]
-        G.linear(ws.o[slot], self._p(p + "wo"), residual=h_in, out=hmid)
+        self._lin(i, "wo", ws.o[slot], hmid, residual=h_in, save=self._saving)
         N.rmsnorm_fwd(hmid, self._p(p + "ffn_norm"), cfg.norm_eps, y=ws.xn2[slot], rstd=ws.rstd2[slot])
-        G.linear_swiglu(ws.xn2[slot], self._p(p + "wgu"), gu_out=ws.gu[slot], h_out=ws.act[slot])
-        G.linear(ws.act[slot], self._p(p + "wdown"), residual=hmid, out=h_out)
+        self._lin_swiglu(i, ws.xn2[slot], ws.gu[slot], ws.act[slot], save=self._saving)
+        self._lin(i, "wdown", ws.act[slot], h_out, residual=hmid, save=self._saving)
 
     def _forward(self, ids: torch.Tensor, ws: _Workspace, save: bool) -> torch.Tensor:
         cfg = self.cfg
+        self._saving = save
         self._hook("pre_forward")
         E.embedding_fwd(ids.reshape(-1), self._p("embed"), out=ws.h[0])
         for i in range(cfg.num_layers):
@@ -194,9 +241,10 @@ class LlamaModel:
             self._hook("pre_layer_bwd", i)
             self._layer_bwd(i, ws)
             self._hook("post_layer_bwd", i)
-        if overwrite_grads and not cfg.tie_embeddings:
-            self._g("embed").zero_()
-        E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
+        if self.train_base:
+            if overwrite_grads and not cfg.tie_embeddings:
+                self._g("embed").zero_()
+            E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
         self._hook("post_backward")
         self._overwrite = False
         return acc
@@ -206,22 +254,18 @@ class LlamaModel:
         p = f"layers.{i}."
         dh = ws.dh
         # FFN
-        G.linear_dgrad(dh, self._p(p + "wdown"), out=ws.dact)
-        self._wgrad(dh, ws.act[i], p + "wdown")
+        self._lin_bwd(i, "wdown", dh, ws.act[i], ws.dact)
         E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
-        G.linear_dgrad(ws.dgu, self._p(p + "wgu"), out=ws.dx)
-        self._wgrad(ws.dgu, ws.xn2[i], p + "wgu")
+        self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[i], ws.dx)
         N.rmsnorm_bwd(ws.dx, ws.hmid[i], self._p(p + "ffn_norm"), ws.rstd2[i], self._g(p + "ffn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)
         # attention
-        G.linear_dgrad(dh, self._p(p + "wo"), out=ws.do)
-        self._wgrad(dh, ws.o[i], p + "wo")
+        self._lin_bwd(i, "wo", dh, ws.o[i], ws.do)
         A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, cfg.num_heads,
                         cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
                         dqkv=ws.dqkv)
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
                 inverse=True)
-        G.linear_dgrad(ws.dqkv, self._p(p + "wqkv"), out=ws.dx)
-        self._wgrad(ws.dqkv, ws.xn1[i], p + "wqkv")
+        self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[i], ws.dx)
         N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[i], self._g(p + "attn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)

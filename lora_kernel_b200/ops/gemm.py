@@ -19,15 +19,27 @@ from .._ext import C, require_device, status
 EPI = {"bf16": 0, "f32": 1, "f32_acc": 2, "bf16_resid": 3, "swiglu": 4}
 
 
+_cap = {}
+
+
+def _check_device(t: torch.Tensor) -> None:
+    idx = t.device.index
+    if idx not in _cap:
+        require_device(t)
+        _cap[idx] = True
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *,
          epi: str = "bf16", residual: Optional[torch.Tensor] = None,
-         h_out: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0) -> torch.Tensor:
-    require_device(a)
+         h_out: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0,
+         a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = alpha * (a @ b.T [+ a2 @ b2.T]) with the requested epilogue."""
+    _check_device(a)
     M, N = a.shape[0], b.shape[0]
     if out is None:
         dt = torch.float32 if epi in ("f32", "f32_acc") else torch.bfloat16
         out = (torch.zeros if epi == "f32_acc" else torch.empty)(M, N, dtype=dt, device=a.device)
-    C().gemm(a, b, out, EPI[epi], residual, h_out, float(alpha), status(a.device), int(bn))
+    C().gemm(a, b, out, EPI[epi], residual, h_out, float(alpha), status(a.device), int(bn), a2, b2)
     return out
 
 

@@ -145,3 +145,50 @@ class TrainingPipeline:
 
     def ema_weights(self) -> Optional[torch.Tensor]:
         return self.opt.ema
+
+
+class LoRATrainingPipeline(TrainingPipeline):
+    """Fine-tune LoRA adapters on a frozen base model (same stepping API)."""
+
+    def __init__(self, model: Transformer, lora_cfg=None, lr: float = 1e-4, weight_decay: float = 0.0,
+                 max_grad_norm: float = 1.0, train_cfg: Optional[TrainConfig] = None):
+        from ..models.lora import LoRAAdapters, LoRAConfig
+        tc = train_cfg or TrainConfig(lr=lr, weight_decay=weight_decay, max_grad_norm=max_grad_norm)
+        tc.lr, tc.weight_decay, tc.max_grad_norm = lr, weight_decay, max_grad_norm
+        self.tc = tc
+        self.model = model
+        eng = self.engine = model.engine
+        self.lora = LoRAAdapters(model.cfg, lora_cfg or LoRAConfig(), eng.device)
+        eng.lora = self.lora
+        eng.train_base = False
+        self.opt = FusedAdamW(self.lora.flat.float(), self.lora.segments(), lr=lr,
+                              betas=(tc.beta1, tc.beta2), eps=tc.eps, weight_decay=weight_decay,
+                              max_grad_norm=max_grad_norm, dynamic_loss_scale=tc.dynamic_loss_scale,
+                              init_loss_scale=tc.init_loss_scale,
+                              growth_interval=tc.loss_scale_growth_interval, ema_decay=tc.ema_decay)
+        self.accum_steps = max(1, tc.grad_accum_steps)
+        self._micro = 0
+        self._opt_steps = 0
+        self.swa = None
+        self.loss_acc = torch.zeros(2, dtype=torch.float32, device=eng.device)
+        self.last_loss = float("nan")
+        self.pre_optimizer = None
+
+    def micro_step_async(self, ids: torch.Tensor, targets: torch.Tensor) -> None:
+        first = self._micro % self.accum_steps == 0
+        self.engine.forward_backward(ids, targets, loss_scale=self.opt.scaler.scale_tensor(),
+                                     grad_scale=1.0 / (ids.numel() * self.accum_steps),
+                                     loss_acc=self.loss_acc, overwrite_grads=first)
+        self._micro += 1
+        if self._micro % self.accum_steps == 0:
+            if self.pre_optimizer is not None:
+                self.pre_optimizer(self.lora.grads)
+            self.opt.norm_partials(self.lora.grads)
+            self.opt.finalize()
+            self.opt.apply(self.lora.grads, self.lora.flat, zero_grad=False)
+            self._opt_steps += 1
+
+    def merge(self) -> None:
+        """Fold the adapters into the base weights (W += s B A) and detach them."""
+        self.lora.merge_into(self.engine.params)
+        self.engine.lora = None
