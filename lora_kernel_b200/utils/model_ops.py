@@ -1,0 +1,71 @@
+"""Offline model utilities: merging and pruning of state dicts.
+
+Merging: linear interpolation, task arithmetic (base + lambda * sum of task
+vectors) and TIES (trim each task vector to its top-k% magnitudes, elect a
+per-parameter sign by total mass, average the values that agree with it).
+Pruning: unstructured magnitude pruning and structured row (output-channel)
+pruning by L2 norm.  Gradient noise for regularisation.
+Reference: ModelMerging (include/nn/model_merging.hpp:7-35, TIES reduced to a
+mean there), ModelPruning (include/nn/model_pruning.hpp:8-37), GradientNoise
+(include/nn/training_enhancements.hpp:147-162).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Sequence
+
+import torch
+
+SD = Dict[str, torch.Tensor]
+
+
+def linear_merge(models: Sequence[SD], weights: Sequence[float]) -> SD:
+    tot = float(sum(weights))
+    return {k: sum(w * m[k].float() for m, w in zip(models, weights)) / tot for k in models[0]}
+
+
+def task_arithmetic(base: SD, finetuned: Sequence[SD], lam: float = 1.0) -> SD:
+    return {k: base[k].float() + lam * sum(f[k].float() - base[k].float() for f in finetuned) for k in base}
+
+
+def ties_merge(base: SD, finetuned: Sequence[SD], density: float = 0.2, lam: float = 1.0) -> SD:
+    out = {}
+    for k in base:
+        b = base[k].float()
+        taus = []
+        for f in finetuned:
+            t = f[k].float() - b
+            n = t.numel()
+            keep = max(1, int(round(density * n)))
+            thr = t.abs().flatten().kthvalue(n - keep + 1).values if keep < n else t.abs().min() - 1
+            taus.append(torch.where(t.abs() >= thr, t, torch.zeros_like(t)))
+        T = torch.stack(taus)
+        sign = torch.sign(T.sum(0))
+        agree = (torch.sign(T) == sign) & (T != 0)
+        cnt = agree.sum(0).clamp(min=1)
+        out[k] = b + lam * (T * agree).sum(0) / cnt
+    return out
+
+
+def prune_magnitude(w: torch.Tensor, sparsity: float) -> torch.Tensor:
+    n = w.numel()
+    k = int(sparsity * n)
+    if k <= 0:
+        return w.clone()
+    thr = w.abs().flatten().kthvalue(k).values
+    return torch.where(w.abs() > thr, w, torch.zeros_like(w))
+
+
+def prune_structured_rows(w: torch.Tensor, fraction: float) -> torch.Tensor:
+    norms = w.float().norm(dim=1)
+    k = int(fraction * w.shape[0])
+    out = w.clone()
+    if k > 0:
+        out[norms.argsort()[:k]] = 0
+    return out
+
+
+def gradient_noise_(grads: torch.Tensor, step: int, eta: float = 0.01, gamma: float = 0.55,
+                    generator=None) -> torch.Tensor:
+    """g += N(0, eta / (1 + step)^gamma)."""
+    std = (eta / (1.0 + step) ** gamma) ** 0.5
+    return grads.add_(torch.randn(grads.shape, generator=generator, device=grads.device) * std)

@@ -1,0 +1,133 @@
+"""Quantisation algorithms, losses, model utilities, attention variants (CPU)."""
+import math
+
+import pytest
+import torch
+
+from lora_kernel_b200.quant import algorithms as Q
+
+
+def test_int8_fp8_int4_roundtrips():
+    torch.manual_seed(0)
+    w = torch.randn(64, 256)
+    q, s = Q.quantize_int8(w)
+    assert (Q.dequantize_int8(q, s) - w).abs().max() <= s.max() * 0.5 + 1e-6
+    for fmt in ("e4m3", "e5m2"):
+        qf, sf = Q.quantize_fp8(w, fmt, per_row=True)
+        rel = ((Q.dequantize_fp8(qf, sf) - w).abs() / (w.abs() + 1e-3)).median()
+        assert rel < (0.04 if fmt == "e4m3" else 0.08)
+    qb, sb = Q.quantize_fp8(w, "e4m3", block=128)
+    assert sb.shape == (64, 2)
+    assert (Q.dequantize_fp8(qb, sb, block=128) - w).abs().max() < 0.3
+    c, sc, z = Q.quantize_int4_groupwise(w, 128)
+    assert c.max() <= 15 and torch.equal(Q.unpack_int4(Q.pack_int4(c)), c)
+    err = (Q.dequantize_int4_groupwise(c, sc, z, 128) - w).abs()
+    assert torch.all(err <= sc.repeat_interleave(128, 1) * 0.5 + 1e-5)
+
+
+def test_static_quantizer_and_kv_reference():
+    sq = Q.StaticQuantizer()
+    for _ in range(3):
+        sq.observe(torch.randn(100) * 2)
+    x = torch.randn(100)
+    assert (sq.dequantize(sq.quantize(x)) - x).abs().max() <= sq.scale
+    kv = torch.randn(10, 2, 64)
+    codes, scale = Q.kv_quantize_reference(kv, "int8")
+    assert codes.dtype == torch.int8 and scale.shape == (10, 2)
+
+
+def test_smoothquant_preserves_output():
+    torch.manual_seed(1)
+    x = torch.randn(32, 128)
+    x[:, 3] *= 50  # an outlier channel
+    w = torch.randn(64, 128)
+    s = Q.smoothquant_scales(x.abs().amax(0), w, 0.5)
+    y = (x / s) @ Q.apply_smoothquant(w, s).t()
+    assert torch.allclose(y, x @ w.t(), rtol=1e-4, atol=1e-3)
+    assert (x / s).abs().amax(0)[3] < x.abs().amax(0)[3]
+
+
+def _rtn_err(w, x, group=128):
+    c, s, z = Q.quantize_int4_groupwise(w, group)
+    return float((x @ Q.dequantize_int4_groupwise(c, s, z, group).t() - x @ w.t()).pow(2).mean())
+
+
+def test_gptq_and_awq_beat_round_to_nearest():
+    torch.manual_seed(2)
+    K, N = 256, 64
+    x = torch.randn(512, K) @ torch.randn(K, K) * 0.1  # correlated activations
+    x[:, :8] *= 10
+    w = torch.randn(N, K) * 0.05
+    base = _rtn_err(w, x)
+    c, s, z = Q.gptq_quantize(w, x, bits=4, group=128, block=128)
+    err_g = float((x @ Q.dequantize_int4_groupwise(c.long(), s, z, 128).t() - x @ w.t()).pow(2).mean())
+    assert err_g < base
+    scales, a = Q.awq_search(w, x, group=128)
+    c2, s2, z2 = Q.quantize_int4_groupwise(w * scales[None], 128)
+    wq = Q.dequantize_int4_groupwise(c2, s2, z2, 128) / scales[None]
+    err_a = float((x @ wq.t() - x @ w.t()).pow(2).mean())
+    assert err_a <= base + 1e-12
+
+
+def test_qat_straight_through():
+    lin = Q.QATLinear(16, 8, w_bits=4, a_bits=8)
+    x = torch.randn(4, 16, requires_grad=True)
+    lin(x).sum().backward()
+    assert x.grad is not None and lin.linear.weight.grad is not None
+    assert torch.count_nonzero(lin.linear.weight.grad) > 0
+
+
+def test_losses():
+    from lora_kernel_b200.train import losses as L
+    torch.manual_seed(3)
+    s = torch.randn(4, 10, requires_grad=True)
+    t = torch.randn(4, 10)
+    kd = L.distillation_loss(s, s.detach(), temperature=2.0)
+    assert abs(float(kd)) < 1e-6
+    L.distillation_loss(s, t, torch.randint(0, 10, (4,)), 2.0, 0.5).backward()
+    assert s.grad is not None
+    lp_old = torch.randn(8)
+    lp_new = (lp_old + 0.5).requires_grad_(True)
+    adv = torch.ones(8)
+    loss = L.ppo_loss(lp_new, lp_old, adv, clip_eps=0.2)
+    assert abs(float(loss) + 1.2) < 1e-5  # ratio clipped at 1 + eps
+    r = torch.tensor([1.0, 2.0, 3.0, 0.0, 0.0, 6.0])
+    a = L.grpo_advantages(r, 3)
+    assert torch.allclose(a.view(2, 3).mean(1), torch.zeros(2), atol=1e-6)
+    g = L.grpo_loss(torch.zeros(6, requires_grad=True), torch.zeros(6), torch.zeros(6), r, 3)
+    assert g.requires_grad
+
+
+def test_merging_pruning():
+    from lora_kernel_b200.utils import model_ops as M
+    base = {"w": torch.zeros(100)}
+    f1 = {"w": torch.linspace(-1, 1, 100)}
+    f2 = {"w": torch.linspace(-1, 1, 100) * 2}
+    assert torch.allclose(M.linear_merge([f1, f2], [1, 1])["w"], 1.5 * f1["w"])
+    assert torch.allclose(M.task_arithmetic(base, [f1, f2], 0.5)["w"], 1.5 * f1["w"])
+    t = M.ties_merge(base, [f1, f2], density=0.2)["w"]
+    assert torch.count_nonzero(t) <= 40 and t[-1] > 0
+    w = torch.randn(10, 10)
+    p = M.prune_magnitude(w, 0.5)
+    assert torch.count_nonzero(p) == 50
+    r = M.prune_structured_rows(w, 0.3)
+    assert int((r.abs().sum(1) == 0).sum()) == 3
+
+
+def test_attention_variants():
+    from lora_kernel_b200.oracle import attention_variants as A
+    torch.manual_seed(4)
+    q = torch.randn(1, 4, 16, 8)
+    k = torch.randn(1, 2, 16, 8)
+    v = torch.randn(1, 2, 16, 8)
+    o = A.attention(q, k, v, mask=A.causal_mask(16, 16))
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k.repeat_interleave(2, 1), v.repeat_interleave(2, 1),
+                                                           is_causal=True)
+    assert torch.allclose(o, ref, atol=1e-5)
+    assert A.sliding_window_mask(8, 2)[5].tolist() == [True] * 4 + [False, False] + [True] * 2
+    assert A.dilated_mask(8, 2)[6, 4] == False and A.dilated_mask(8, 2)[6, 5] == True
+    b = A.alibi_bias(4, 8)
+    assert b.shape == (4, 8, 8) and float(b[0, 3, 3]) == 0.0
+    assert A.RelativePositionBias(4)(8).shape == (4, 8, 8)
+    lo = A.linear_attention(q, k, v, causal=True)
+    assert lo.shape == (1, 4, 16, 8) and torch.isfinite(lo).all()
