@@ -107,6 +107,153 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
   check(lk_gemm(&d, stream()));
 }
 
+// K18: GEMM whose bf16 output rows are stored into their owner rank's receive
+// buffer (peer pointers `rptrs`, int64 device tensor) at slot rs_rank.
+void gemm_rs(torch::Tensor a, torch::Tensor b, torch::Tensor rptrs, int64_t rs_rows, int64_t rs_rank,
+             int64_t ldd, int64_t m_rot, torch::Tensor status, int64_t bn) {
+  const c10::cuda::CUDAGuard g(a.device());
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm_rs: K mismatch");
+  Operand A = classify(a, "a"), B = classify(b, "b");
+  TORCH_CHECK(rptrs.is_cuda() && rptrs.scalar_type() == torch::kInt64, "gemm_rs: rptrs int64 cuda");
+  LkGemmDesc d{};
+  d.a = A.base; d.a_rows = A.rows; d.a_cols = A.cols; d.a_ld = A.ld; d.a_mn = A.mn;
+  d.b = B.base; d.b_rows = B.rows; d.b_cols = B.cols; d.b_ld = B.ld; d.b_mn = B.mn;
+  d.M = (int)a.size(0);
+  d.N = (int)b.size(0);
+  d.K = (int)a.size(1);
+  TORCH_CHECK(d.M % rs_rows == 0 && d.M / rs_rows == rptrs.numel(), "gemm_rs: M must be world * rs_rows");
+  TORCH_CHECK(ldd >= d.N && ldd % 8 == 0, "gemm_rs: ldd");
+  d.ldd = ldd;
+  d.alpha = 1.f;
+  d.epi = LK_EPI_REMOTE;
+  d.bn = (int)bn;
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  d.comm_mode = 1;
+  d.m_rot = (int)m_rot;
+  d.rptrs = reinterpret_cast<void* const*>(rptrs.data_ptr());
+  d.rs_rows = (int)rs_rows;
+  d.rs_rank = (int)rs_rank;
+  check(lk_gemm(&d, stream()));
+}
+
+// K16: all-gather of A's rows from every rank's staging buffer (pointers in
+// `src_ptrs`, int64 device tensor) into `a` on first use, fused with the GEMM.
+void gemm_ag(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
+             c10::optional<torch::Tensor> h, torch::Tensor src_ptrs, int64_t src_ld, int64_t rows,
+             int64_t rank, torch::Tensor count, int64_t m_rot, torch::Tensor status, int64_t bn) {
+  const c10::cuda::CUDAGuard g(a.device());
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm_ag: K mismatch");
+  Operand A = classify(a, "a"), B = classify(b, "b");
+  TORCH_CHECK(!A.mn && a.stride(0) == A.ld, "gemm_ag: a must be row-major");
+  TORCH_CHECK(src_ptrs.is_cuda() && src_ptrs.scalar_type() == torch::kInt64, "gemm_ag: src_ptrs");
+  LkGemmDesc d{};
+  d.a = A.base; d.a_rows = A.rows; d.a_cols = A.cols; d.a_ld = A.ld; d.a_mn = A.mn;
+  d.b = B.base; d.b_rows = B.rows; d.b_cols = B.cols; d.b_ld = B.ld; d.b_mn = B.mn;
+  d.M = (int)a.size(0);
+  d.N = (int)b.size(0);
+  d.K = (int)a.size(1);
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.size(0) == d.M &&
+                  out.size(1) == d.N && out.stride(1) == 1,
+              "gemm_ag: out must be bf16 [M, N]");
+  d.d = out.data_ptr();
+  d.ldd = out.stride(0);
+  if (h.has_value()) {
+    need(*h, "h", torch::kBFloat16);
+    TORCH_CHECK(h->size(0) == d.M && h->size(1) == d.N / 2 && h->stride(1) == 1, "gemm_ag: h shape");
+    d.h = h->data_ptr();
+    d.ldh = h->stride(0);
+  }
+  d.alpha = 1.f;
+  d.epi = (int)epi;
+  d.bn = (int)bn;
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  need(count, "count", torch::kInt32);
+  TORCH_CHECK(count.numel() >= d.M / 128, "gemm_ag: count too small");
+  d.comm_mode = 2;
+  d.m_rot = (int)m_rot;
+  d.ag_src = reinterpret_cast<const void* const*>(src_ptrs.data_ptr());
+  d.ag_ld_src = src_ld * 2;
+  d.ag_rows = (int)rows;
+  d.ag_rank = (int)rank;
+  d.ag_world = (int)src_ptrs.numel();
+  d.ag_count = count.data_ptr<int>();
+  check(lk_gemm(&d, stream()));
+}
+
+// K18 owner side: sum of the received slots (+ residual, + RMSNorm).
+void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
+            c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> y,
+            c10::optional<torch::Tensor> rstd, double eps) {
+  const c10::cuda::CUDAGuard g(recv.device());
+  need(recv, "recv", torch::kBFloat16);
+  need(out, "out", torch::kBFloat16);
+  TORCH_CHECK(recv.dim() == 2 && recv.stride(1) == 1 && out.stride(1) == 1, "rs_sum: row-major");
+  LkRsSumDesc d{};
+  d.recv = recv.data_ptr();
+  d.ld_recv = recv.stride(0);
+  d.world = (int)world;
+  d.rows = (int)out.size(0);
+  d.cols = (int)out.size(1);
+  TORCH_CHECK(recv.size(0) >= world * d.rows && recv.size(1) >= d.cols, "rs_sum: recv shape");
+  d.out = out.data_ptr();
+  d.ld_out = out.stride(0);
+  if (resid.has_value()) {
+    need(*resid, "resid", torch::kBFloat16);
+    TORCH_CHECK(resid->size(0) == d.rows && resid->size(1) == d.cols && resid->stride(1) == 1, "rs_sum: resid");
+    d.resid = resid->data_ptr();
+    d.ld_resid = resid->stride(0);
+  }
+  if (gamma.has_value()) {
+    TORCH_CHECK(y.has_value(), "rs_sum: y needed with gamma");
+    need_contig(*gamma, "gamma", torch::kBFloat16);
+    need(*y, "y", torch::kBFloat16);
+    TORCH_CHECK(y->size(0) == d.rows && y->size(1) == d.cols && y->stride(1) == 1, "rs_sum: y shape");
+    d.gamma = gamma->data_ptr();
+    d.y = y->data_ptr();
+    d.ld_y = y->stride(0);
+    d.rstd = optp<float>(rstd);
+    d.eps = (float)eps;
+  }
+  check(lk_rs_sum(&d, stream()));
+}
+
+// Vocabulary-parallel cross-entropy (phase 1: statistics, phase 2: finish).
+void cross_entropy_vp(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss_acc,
+                      c10::optional<torch::Tensor> scale, double scale_mul, double smoothing,
+                      double zloss, int64_t ignore_index, bool write_grad, int64_t v0,
+                      int64_t v_total, torch::Tensor stats, torch::Tensor peer_stats, int64_t phase) {
+  const c10::cuda::CUDAGuard g(logits.device());
+  need(logits, "logits", torch::kBFloat16);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "cross_entropy_vp: logits row-major");
+  need_contig(targets, "targets", torch::kInt64);
+  LkCeVpDesc d{};
+  d.ce.logits = logits.data_ptr();
+  d.ce.ld = logits.stride(0);
+  d.ce.targets = targets.data_ptr<int64_t>();
+  d.ce.T = (int)logits.size(0);
+  d.ce.V = (int)logits.size(1);
+  TORCH_CHECK(targets.numel() == d.ce.T, "cross_entropy_vp: targets");
+  d.ce.loss_acc = loss_acc.data_ptr<float>();
+  d.ce.scale_ptr = optp<const float>(scale);
+  d.ce.scale_mul = (float)scale_mul;
+  d.ce.smoothing = (float)smoothing;
+  d.ce.zloss = (float)zloss;
+  d.ce.ignore_index = ignore_index;
+  d.ce.write_grad = write_grad ? 1 : 0;
+  d.v0 = v0;
+  d.V_total = v_total;
+  need(stats, "stats", torch::kFloat32);
+  TORCH_CHECK(stats.numel() >= 4 * d.ce.T, "cross_entropy_vp: stats [T, 4]");
+  d.stats = stats.data_ptr<float>();
+  TORCH_CHECK(peer_stats.is_cuda() && peer_stats.scalar_type() == torch::kInt64, "peer_stats int64");
+  d.peer_stats = reinterpret_cast<const float* const*>(peer_stats.data_ptr());
+  d.world = (int)peer_stats.numel();
+  d.phase = (int)phase;
+  check(lk_cross_entropy_vp(&d, stream()));
+}
+
 // ------------------------------------------------------------- RMSNorm
 void rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res, torch::Tensor gamma,
                  torch::Tensor y, c10::optional<torch::Tensor> h_out,
@@ -246,7 +393,7 @@ void cross_entropy(torch::Tensor logits, torch::Tensor targets, torch::Tensor lo
 void adamw(torch::Tensor p32, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
            c10::optional<torch::Tensor> p16, c10::optional<torch::Tensor> ema,
            torch::Tensor chunks, torch::Tensor state, double beta1, double beta2, double eps,
-           double wd, double ema_decay, bool zero_grad) {
+           double wd, double ema_decay, bool zero_grad, c10::optional<torch::Tensor> p16_peers) {
   const c10::cuda::CUDAGuard g(p32.device());
   need_contig(p32, "p32", torch::kFloat32);
   need_contig(grad, "grad", torch::kFloat32);
@@ -270,6 +417,11 @@ void adamw(torch::Tensor p32, torch::Tensor grad, torch::Tensor m, torch::Tensor
   d.wd = (float)wd;
   d.ema_decay = (float)ema_decay;
   d.zero_grad = zero_grad ? 1 : 0;
+  if (p16_peers.has_value()) {
+    TORCH_CHECK(p16_peers->is_cuda() && p16_peers->scalar_type() == torch::kInt64, "adamw: p16_peers");
+    d.p16_peers = reinterpret_cast<void* const*>(p16_peers->data_ptr());
+    d.world = (int)p16_peers->numel();
+  }
   check(lk_adamw(&d, stream()));
 }
 
@@ -515,6 +667,10 @@ void dequantize(int64_t fmt, torch::Tensor q, torch::Tensor scale, c10::optional
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lora_kernel_b200 sm_100a kernels";
   m.def("gemm", &gemm);
+  m.def("gemm_rs", &gemm_rs);
+  m.def("gemm_ag", &gemm_ag);
+  m.def("rs_sum", &rs_sum);
+  m.def("cross_entropy_vp", &cross_entropy_vp);
   m.def("launch_count", []() { return (int64_t)lk_launch_count(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

@@ -60,6 +60,7 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int epoch, int* statu
 __global__ void signal_barrier_kernel(int* const* __restrict__ sig_ptrs, int rank, int world,
                                       int slot, int epoch, int* status) {
   const int p = threadIdx.x;
+  __threadfence_system();  // earlier kernels' peer stores are visible before the flag
   if (p < world) st_release_sys(sig_ptrs[p] + slot * world + rank, epoch);
   __syncthreads();
   if (p < world) wait_flag(sig_ptrs[rank] + slot * world + p, epoch, status);

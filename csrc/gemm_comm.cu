@@ -1,0 +1,39 @@
+// K1 GEMM instantiations with fused collectives:
+//   K18  GEMM -> reduce-scatter: the epilogue stores each output tile into the
+//        owner rank's receive slot in peer memory (the owner sums the slots);
+//   K16  all-gather -> GEMM: a copy warp per CTA pulls peers' rows of A into
+//        local memory on first use; the TMA producer waits (bounded) on per-chunk
+//        counters before loading a remote row block.  Cooperative launch.
+// Both rotate the M-tile order by rank so peers do not all hit the same owner.
+#include "gemm_kernel.cuh"
+
+namespace lk {
+int choose_bn(const LkGemmDesc& g);
+
+int gemm_dispatch_comm(const LkGemmDesc& g, cudaStream_t s) {
+  LK_REQUIRE(!g.a_mn, "fused-collective GEMM: A must be K-major");
+  const int bn = choose_bn(g);
+  if (g.comm_mode == 1) {
+    LK_REQUIRE(g.epi == LK_EPI_REMOTE && g.rptrs && g.rs_rows > 0, "gemm_rs: needs rptrs / rs_rows");
+    if (!g.b_mn) return bn == 128 ? launch_gemm<128, false, false, EPI_REMOTE>(g, s)
+                                  : launch_gemm<256, false, false, EPI_REMOTE>(g, s);
+    return bn == 128 ? launch_gemm<128, false, true, EPI_REMOTE>(g, s)
+                     : launch_gemm<256, false, true, EPI_REMOTE>(g, s);
+  }
+  if (g.comm_mode == 2) {
+    LK_REQUIRE(g.ag_src && g.ag_count && g.ag_rows % 128 == 0 && g.ag_world >= 1 &&
+                   (int64_t)g.ag_rows * g.ag_world == g.M && (g.a_cols * 2) % 16 == 0,
+               "gemm_ag: M must be world * ag_rows with ag_rows % 128 == 0");
+    if (g.epi == LK_EPI_SWIGLU) {
+      LK_REQUIRE(!g.b_mn && g.N % 256 == 0 && g.h, "gemm_ag swiglu: K-major B, N % 256");
+      return launch_gemm<256, false, false, EPI_SWIGLU, true>(g, s);
+    }
+    LK_REQUIRE(g.epi == LK_EPI_BF16, "gemm_ag: bf16 or swiglu epilogue");
+    if (!g.b_mn) return bn == 128 ? launch_gemm<128, false, false, EPI_BF16, true>(g, s)
+                                  : launch_gemm<256, false, false, EPI_BF16, true>(g, s);
+    return bn == 128 ? launch_gemm<128, false, true, EPI_BF16, true>(g, s)
+                     : launch_gemm<256, false, true, EPI_BF16, true>(g, s);
+  }
+  return fail("gemm: unknown comm_mode");
+}
+}  // namespace lk

@@ -14,6 +14,7 @@ extern "C" int lk_gemm(const LkGemmDesc* g, cudaStream_t stream) {
   LK_REQUIRE(g->N % 8 == 0, "lk_gemm: N must be a multiple of 8");
   LK_REQUIRE(g->a_ld % 8 == 0 && g->b_ld % 8 == 0, "lk_gemm: operand pitch must be a multiple of 8");
   LK_REQUIRE(g->ldd % 4 == 0, "lk_gemm: output pitch must be 16-byte aligned");
+  if (g->comm_mode != 0) return gemm_dispatch_comm(*g, stream);
   switch (g->epi) {
     case LK_EPI_BF16:
       return gemm_dispatch_bf16(*g, stream);

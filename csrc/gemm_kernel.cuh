@@ -38,6 +38,7 @@ enum GemmEpi : int {
   EPI_F32_ACC = 2,     // D(f32) += alpha*acc          (gradient accumulation)
   EPI_BF16_RESID = 3,  // D(bf16) = alpha*acc + R(bf16) (residual add; D may alias R)
   EPI_SWIGLU = 4,      // D(bf16) = acc (gate|up), H(bf16) = silu(gate) * up
+  EPI_REMOTE = 5,      // K18: bf16 tile stored into the owner rank's receive slot (peer memory)
 };
 
 struct GemmArgs {
@@ -52,7 +53,24 @@ struct GemmArgs {
   int* status;
   int tiles_m, tiles_n;
   int K2;  // > 0: a second contraction segment (A2 . B2^T) accumulated into the same tile
+  int m_rot;  // M-tile rotation: rank r starts at M-tile m_rot (staggers peers' traffic)
+  // K18 remote-store epilogue: row m belongs to owner m / rs_rows and lands in
+  // rptrs[owner] at row (rs_rank * rs_rows + m % rs_rows), pitch ldd
+  void* const* rptrs;
+  int rs_rows, rs_rank;
+  // K16 all-gather of A on first use: rank p's rows [0, ag_rows) live at
+  // ag_src[p] (pitch ag_ld_src bytes; p == ag_rank is this GPU's own staging
+  // rows) and are copied into rows [p*ag_rows, (p+1)*ag_rows) of the local A
+  // buffer ag_dst (pitch ag_ld_dst bytes) by the copy warps; ag_count[c]
+  // counts copied 16-row pieces of the 128-row chunk c (8 = ready).
+  const uint8_t* const* ag_src;
+  int64_t ag_ld_src, ag_ld_dst;
+  uint8_t* ag_dst;
+  int ag_rows, ag_rank, ag_world, ag_row_bytes;
+  int* ag_count;
 };
+
+constexpr int AG_SUB = 16;  // rows per copy piece
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
@@ -84,8 +102,78 @@ __device__ __forceinline__ void gemm_tile_coords(int t, int tiles_m, int tiles_n
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// K16 copy warp: pull this CTA's share of the peers' rows into the local A buffer.
+static __device__ __noinline__ void ag_copy_warp(const GemmArgs& a, int lane) {
+  const int R = a.ag_rows, W = a.ag_world, me = a.ag_rank;
+  const int per_rank = R / AG_SUB;
+  const int total = per_rank * W;
+  const int units = AG_SUB * a.ag_row_bytes / 16;
+  for (int s = blockIdx.x; s < total; s += gridDim.x) {
+    const int p = (me + s / per_rank) % W;  // own rows first, then the next ranks (tile order matches)
+    const int r0 = (s % per_rank) * AG_SUB;
+    const uint8_t* src = a.ag_src[p] + (int64_t)r0 * a.ag_ld_src;
+    uint8_t* dst = a.ag_dst + (int64_t)(p * R + r0) * a.ag_ld_dst;
+    const int upr = a.ag_row_bytes / 16;  // 16-byte units per row
+    for (int u0 = lane; u0 < units; u0 += 32 * 16) {
+      uint4 v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int u = u0 + 32 * k;
+        if (u < units) v[k] = *reinterpret_cast<const uint4*>(src + (int64_t)(u / upr) * a.ag_ld_src + (u % upr) * 16);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int u = u0 + 32 * k;
+        if (u < units) *reinterpret_cast<uint4*>(dst + (int64_t)(u / upr) * a.ag_ld_dst + (u % upr) * 16) = v[k];
+      }
+    }
+    __threadfence();
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence();
+      atomicAdd(a.ag_count + (p * R + r0) / 128, 1);
+    }
+  }
+}
+
+// Producer side of K16: wait (bounded) until the 128-row chunk of M-tile tm is in place.
+__device__ __forceinline__ bool ag_wait_chunk(const GemmArgs& a, int tm, volatile int* abort_flag) {
+  const int* cnt = a.ag_count + tm;
+  if (ld_acquire_gpu(cnt) >= 128 / AG_SUB) {
+    fence_proxy_async_global();
+    return true;
+  }
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i) {
+      if (ld_acquire_gpu(cnt) >= 128 / AG_SUB) {
+        fence_proxy_async_global();
+        return true;
+      }
+      __nanosleep(100);
+    }
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > LK_WAIT_TIMEOUT_NS) {
+      atomicCAS(a.status, 0, LK_ERR_TIMEOUT_PEER);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool AG = false>
+__global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const GemmArgs args) {
@@ -145,6 +233,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
         int tm, tn;
         gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        tm = (tm + args.m_rot) % args.tiles_m;
+        if constexpr (AG) {
+          if (!ag_wait_chunk(args, tm, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
         for (int kb = 0; kb < nk; ++kb) {
           if (!bounded_wait(empty0 + 8 * s, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY,
                             abort_flag)) {
@@ -235,6 +330,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_commit(drain_bar);
       bounded_wait(drain_bar, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
+  } else if (AG && warp == 6) {
+    // ------------------------------------------------------- K16 copy warp
+    ag_copy_warp(args, lane);
   } else {
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -243,6 +341,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int t = blockIdx.x; t < T; t += gridDim.x, ++local) {
       int tm, tn;
       gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      tm = (tm + args.m_rot) % args.tiles_m;
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
       bool ok = bounded_wait(tfull0 + 8 * buf, use & 1, args.status, LK_ERR_TIMEOUT_ACCUM,
@@ -302,8 +401,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_wait_ld();
           if (!row_ok) continue;
           const int col0 = tn * BN + c * 32;
-          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
-            __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID || EPI == EPI_REMOTE) {
+            __nv_bfloat16* drow;
+            if constexpr (EPI == EPI_REMOTE) {
+              const int owner = row / args.rs_rows;
+              drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
+                     (int64_t)(args.rs_rank * args.rs_rows + row - owner * args.rs_rows) * args.ldd;
+            } else {
+              drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+            }
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int col = col0 + v * 8;
@@ -361,7 +467,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool AG = false>
 int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   GemmArgs args{};
@@ -390,7 +496,20 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
     ta2 = ta;
     tb2 = tb;
   }
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  args.m_rot = g.m_rot;
+  args.rptrs = reinterpret_cast<void* const*>(g.rptrs);
+  args.rs_rows = g.rs_rows;
+  args.rs_rank = g.rs_rank;
+  args.ag_src = reinterpret_cast<const uint8_t* const*>(g.ag_src);
+  args.ag_ld_src = g.ag_ld_src;
+  args.ag_ld_dst = g.a_ld * 2;
+  args.ag_dst = reinterpret_cast<uint8_t*>(const_cast<void*>(g.a));
+  args.ag_rows = g.ag_rows;
+  args.ag_rank = g.ag_rank;
+  args.ag_world = g.ag_world;
+  args.ag_row_bytes = (int)(g.a_cols * 2);
+  args.ag_count = g.ag_count;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, AG>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -400,13 +519,28 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   }
   const int tiles = args.tiles_m * args.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, ta2, tb2, args);
-  return check_launch("gemm_tc_kernel");
+  if constexpr (AG) {
+    // CTAs wait on rows copied by other CTAs: they must all be resident
+    if (cudaMemsetAsync(g.ag_count, 0, sizeof(int) * args.tiles_m, stream) != cudaSuccess)
+      return fail("gemm_ag: memset failed");
+    void* params[] = {&ta, &tb, &ta2, &tb2, &args};
+    cudaError_t e = cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(GEMM_THREADS + 32), params,
+                                                C::SMEM, stream);
+    if (e != cudaSuccess) {
+      last_error() = std::string("gemm_ag cooperative launch: ") + cudaGetErrorString(e);
+      return -1;
+    }
+    return check_launch("gemm_tc_kernel_ag");
+  } else {
+    kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, ta2, tb2, args);
+    return check_launch("gemm_tc_kernel");
+  }
 }
 
 // Per-epilogue dispatchers (each defined in its own translation unit).
 int gemm_dispatch_bf16(const LkGemmDesc& g, cudaStream_t s);
 int gemm_dispatch_f32(const LkGemmDesc& g, cudaStream_t s);
 int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s);
+int gemm_dispatch_comm(const LkGemmDesc& g, cudaStream_t s);
 
 }  // namespace lk

@@ -27,6 +27,7 @@ enum LkGemmEpi {
   LK_EPI_F32_ACC = 2,
   LK_EPI_BF16_RESID = 3,
   LK_EPI_SWIGLU = 4,
+  LK_EPI_REMOTE = 5,
 };
 
 typedef struct LkGemmDesc {
@@ -55,6 +56,22 @@ typedef struct LkGemmDesc {
   const void* b2;
   int64_t b2_rows, b2_cols, b2_ld;
   int K2;
+  // Fused collectives (comm_mode): 0 none; 1 = K18 GEMM -> reduce-scatter: the
+  // bf16 output row m goes to rank m / rs_rows at row (rs_rank * rs_rows + m %
+  // rs_rows) of its receive buffer rptrs[owner] (pitch ldd; rptrs is a DEVICE
+  // array of peer pointers); 2 = K16 all-gather -> GEMM: A (K-major, [M, K],
+  // any local buffer) is filled on first use from ag_src[p] (DEVICE array of
+  // pointers to each rank's ag_rows x K staging rows in symmetric memory,
+  // pitch ag_ld_src bytes, this rank's own entry included); ag_count is int
+  // scratch [M/128] zeroed by the launcher.  m_rot rotates the M-tile order.
+  int comm_mode;
+  int m_rot;
+  void* const* rptrs;
+  int rs_rows, rs_rank;
+  const void* const* ag_src;
+  int64_t ag_ld_src;
+  int ag_rows, ag_rank, ag_world;
+  int* ag_count;
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
@@ -109,6 +126,23 @@ int lk_embedding_fwd(const int64_t* ids, const void* W, void* out, int T, int D,
 int lk_embedding_bwd(const int64_t* ids, const void* dy, float* dW, int T, int D, int V,
                      cudaStream_t s);
 
+// --------------------------------------------- K18 owner-side slot reduction
+typedef struct LkRsSumDesc {
+  const void* recv;   // [world * rows, ld_recv] bf16: slot s = rank s's partial
+  int64_t ld_recv;
+  int world, rows, cols;
+  const void* resid;  // optional [rows, ld_resid] bf16 added to the sum
+  int64_t ld_resid;
+  void* out;          // [rows, ld_out] bf16 sum (may alias resid)
+  int64_t ld_out;
+  const void* gamma;  // optional: RMSNorm of the sum -> y, rstd
+  void* y;
+  int64_t ld_y;
+  float* rstd;
+  float eps;
+} LkRsSumDesc;
+int lk_rs_sum(const LkRsSumDesc* d, cudaStream_t s);
+
 // ------------------------------------------------------------ K9 cross-entropy
 typedef struct LkCeDesc {
   void* logits;  // [T, V] bf16, overwritten with the gradient when write_grad
@@ -124,6 +158,21 @@ typedef struct LkCeDesc {
   int write_grad;
 } LkCeDesc;
 int lk_cross_entropy(const LkCeDesc* d, cudaStream_t s);
+
+// Vocabulary-parallel cross-entropy: each rank holds logits [T, V_local] for
+// vocabulary columns [v0, v0 + V_local).  Phase 1 writes per-row partial
+// statistics {max, sum exp, sum z, z[target] if owned} to stats (float4 [T],
+// symmetric memory); after a device barrier phase 2 combines every rank's
+// statistics (peer pointers `peer_stats`, a DEVICE array of `world` float4*)
+// into the loss (identical on every rank) and writes the local dlogits slice.
+typedef struct LkCeVpDesc {
+  LkCeDesc ce;         // logits / ld / targets / T / V (= V_local) / loss / scale fields
+  int64_t v0, V_total;
+  float* stats;        // this rank's float4 [T]
+  const float* const* peer_stats;
+  int world, phase;
+} LkCeVpDesc;
+int lk_cross_entropy_vp(const LkCeVpDesc* d, cudaStream_t s);
 
 // ------------------------------------------------------- K11 AdamW + K12 (1 GPU)
 // Device-resident optimizer state vector (fp32) indices.
@@ -150,6 +199,12 @@ typedef struct LkAdamWDesc {
   const float* state;
   float beta1, beta2, eps, wd, ema_decay;
   int zero_grad;
+  // Optional fused parameter all-gather (ZeRO-1/2): the new bf16 value of
+  // master element o is also stored into every rank's full parameter buffer
+  // (p16_peers, a DEVICE array of `world` bf16 pointers) at element
+  // o + 64 * chunks[c].w, the chunk's shard-to-flat offset in 64-element units.
+  void* const* p16_peers;
+  int world;
 } LkAdamWDesc;
 int lk_adamw(const LkAdamWDesc* d, cudaStream_t s);
 int lk_grad_norm_partials(const float* g, int64_t n, float* partial, int nparts, cudaStream_t s);

@@ -27,7 +27,9 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p32, flo
                                                     const int4* __restrict__ chunks,
                                                     const float* __restrict__ state, float beta1,
                                                     float beta2, float eps, float wd,
-                                                    float ema_decay, int zero_grad) {
+                                                    float ema_decay, int zero_grad,
+                                                    __nv_bfloat16* const* __restrict__ p16_peers,
+                                                    int world) {
   if (state[LK_ST_SKIP] != 0.f) {
     // overflow step: only clear the gradient
     if (zero_grad) {
@@ -68,8 +70,12 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p32, flo
     *reinterpret_cast<float4*>(m + o) = Mm;
     *reinterpret_cast<float4*>(v + o) = Vv;
     if (zero_grad) *reinterpret_cast<float4*>(g + o) = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p16)
-      *reinterpret_cast<uint2*>(p16 + o) = make_uint2(pack_bf16x2(P.x, P.y), pack_bf16x2(P.z, P.w));
+    const uint2 pb = make_uint2(pack_bf16x2(P.x, P.y), pack_bf16x2(P.z, P.w));
+    if (p16) *reinterpret_cast<uint2*>(p16 + o) = pb;
+    if (p16_peers) {
+      const int64_t fo = o + 64 * (int64_t)ck.w;
+      for (int q = 0; q < world; ++q) *reinterpret_cast<uint2*>(p16_peers[q] + fo) = pb;
+    }
     if (ema) {
       float4 E = *reinterpret_cast<float4*>(ema + o);
       E.x = ema_decay * E.x + (1.f - ema_decay) * P.x;
@@ -88,6 +94,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p32, flo
     p32[o] = p32[o] - lr * (wdl * p32[o] + (m[o] / bc1) / (sqrtf(v[o] / bc2) + eps));
     if (zero_grad) g[o] = 0.f;
     if (p16) p16[o] = __float2bfloat16(p32[o]);
+    if (p16_peers)
+      for (int q = 0; q < world; ++q) p16_peers[q][o + 64 * (int64_t)ck.w] = __float2bfloat16(p32[o]);
     if (ema) ema[o] = ema_decay * ema[o] + (1.f - ema_decay) * p32[o];
   }
 }
@@ -182,6 +190,7 @@ extern "C" int lk_adamw(const LkAdamWDesc* d, cudaStream_t s) {
   if (d->nchunks == 0) return 0;
   adamw_kernel<<<d->nchunks, 256, 0, s>>>(d->p32, d->g, d->m, d->v, (__nv_bfloat16*)d->p16, d->ema,
                                           (const int4*)d->chunks, d->state, d->beta1, d->beta2,
-                                          d->eps, d->wd, d->ema_decay, d->zero_grad);
+                                          d->eps, d->wd, d->ema_decay, d->zero_grad,
+                                          (__nv_bfloat16* const*)d->p16_peers, d->world);
   return check_launch("adamw");
 }

@@ -23,11 +23,16 @@ def new_state(device, loss_scale: float = 1.0, lr: float = 0.0) -> torch.Tensor:
 
 
 def make_chunks(segments, chunk: int = 16384, device=None) -> torch.Tensor:
-    """segments: iterable of (start, length, weight_decay_on) -> int32 [n, 4]."""
+    """segments: iterable of (start, length, weight_decay_on[, flat_delta]) ->
+    int32 [n, 4].  flat_delta (a multiple of 64) maps a master element to its
+    position in the full flat layout for the fused parameter all-gather."""
     rows = []
-    for start, length, wd in segments:
+    for seg in segments:
+        start, length, wd = seg[:3]
+        delta = seg[3] if len(seg) > 3 else 0
+        assert delta % 64 == 0
         for off in range(0, length, chunk):
-            rows.append((start + off, min(chunk, length - off), 1 if wd else 0, 0))
+            rows.append((start + off, min(chunk, length - off), 1 if wd else 0, delta // 64))
     t = torch.tensor(rows if rows else [(0, 0, 0, 0)], dtype=torch.int32)
     if not rows:
         t = t[:0]
@@ -50,7 +55,9 @@ def adamw_(p32: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torch.Tens
            chunks: torch.Tensor, state: torch.Tensor, *, p16: Optional[torch.Tensor] = None,
            ema: Optional[torch.Tensor] = None, beta1: float = 0.9, beta2: float = 0.95,
            eps: float = 1e-8, wd: float = 0.0, ema_decay: float = 0.0,
-           zero_grad: bool = True) -> None:
+           zero_grad: bool = True, p16_peers: Optional[torch.Tensor] = None) -> None:
+    """p16_peers: device int64 array of every rank's full bf16 parameter buffer;
+    the updated values are stored into all of them (fused all-gather)."""
     require_device(p32)
     C().adamw(p32, grad, m, v, p16, ema, chunks, state, float(beta1), float(beta2), float(eps),
-              float(wd), float(ema_decay), bool(zero_grad))
+              float(wd), float(ema_decay), bool(zero_grad), p16_peers)

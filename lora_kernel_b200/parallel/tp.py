@@ -1,0 +1,603 @@
+"""Tensor parallelism (Megatron column/row-parallel linears with sequence
+parallelism) on the fused collective GEMMs.
+
+Layout (tp ranks, rank r):
+  * the residual stream, norms and the embedding lookup are sequence-sharded:
+    rank r owns token rows [r*R, (r+1)*R) of the flattened batch (R = T / tp);
+  * column-parallel linears (Wqkv by heads, Wgate|up by FFN blocks, the LM head
+    by vocabulary rows) consume the all-gathered normalised activations
+    through K16 - the all-gather runs inside the GEMM: a copy warp per CTA pulls
+    peers' rows over NVLink into the local A buffer, and the TMA producer starts
+    on a 128-row block as soon as its counter says it has landed;
+  * row-parallel linears (Wo, Wdown, and every dgrad of a column-parallel
+    linear) run K18 - the GEMM epilogue stores each output row block straight
+    into its owner's receive slot in peer memory; the owner then sums the slots
+    in fixed rank order fused with the residual add and the next RMSNorm,
+    writing the normalised rows into the symmetric staging buffer the next K16
+    reads (csrc/tp.cu);
+  * the LM head is vocabulary-parallel and the cross-entropy combines per-row
+    statistics from every rank through peer memory (no logits all-gather);
+  * replicated parameters (embedding, norms) get their gradients summed by the
+    one-shot peer-memory all-reduce (K12) at the end of the accumulation window.
+
+`comm="nccl"` runs the same schedule on NCCL all-gather / reduce-scatter with
+plain GEMMs: the baseline the fused kernels are measured against.
+
+Hazards: every buffer a peer reads (staging rows, receive slots, CE
+statistics) is rewritten only after a device barrier that follows the peers'
+last read of it; the schedule alternates two staging and two receive buffers
+so that one barrier per hand-off suffices.
+
+Reference: ColumnParallelLinear / RowParallelLinear / TensorParallelTransformer
+(include/distributed/tensor_parallel.hpp:14-104) - a forward-only column/row
+split with an all-gather / all-reduce around a plain matmul.
+"""
+from __future__ import annotations
+
+import copy
+from collections import OrderedDict
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .._ext import C, check_status, status
+from ..config import TransformerConfig
+from ..models.params import ALIGN, ParamSpec, build_layout
+from ..ops import attention as A
+from ..ops import elementwise as E
+from ..ops import gemm as G
+from ..ops import norm as N
+from ..ops.gemm import EPI
+from . import comm as CM
+
+SLOT_TP = 5
+
+
+def _round(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+def check_tp_config(cfg: TransformerConfig, tp: int) -> None:
+    if cfg.num_heads % tp or cfg.num_kv_heads % tp:
+        raise ValueError(f"tp={tp} must divide the query and KV head counts")
+    if cfg.ff_dim_padded % (128 * tp):
+        raise ValueError(f"tp={tp}: padded FFN width {cfg.ff_dim_padded} must split into 128-row blocks")
+    if cfg.vocab_size % (8 * tp):
+        raise ValueError(f"tp={tp}: vocabulary {cfg.vocab_size} must split into multiples of 8")
+
+
+# --------------------------------------------------------------------- layout
+def build_tp_layout(cfg: TransformerConfig, tp: int) -> Tuple[List[ParamSpec], int, int]:
+    """Local parameter layout of one TP rank.  Replicated tensors first (so
+    their gradients are one contiguous range for the all-reduce), then the
+    sharded ones.  Returns (specs, replicated numel, total numel)."""
+    check_tp_config(cfg, tp)
+    D, V = cfg.hidden_dim, cfg.vocab_size
+    Fl = cfg.ff_dim_padded // tp
+    ql, kvl = cfg.q_dim // tp, cfg.kv_dim // tp
+    specs: List[ParamSpec] = []
+    off = 0
+
+    def add(name, shape, group, decay, init):
+        nonlocal off
+        s = ParamSpec(name, tuple(shape), off, group, decay, init)
+        specs.append(s)
+        off += _round(s.numel)
+
+    add("embed", (V, D), "replicated", True, "normal")
+    for i in range(cfg.num_layers):
+        add(f"layers.{i}.attn_norm", (D,), "replicated", False, "ones")
+        add(f"layers.{i}.ffn_norm", (D,), "replicated", False, "ones")
+    add("final_norm", (D,), "replicated", False, "ones")
+    n_rep = off
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        add(p + "wqkv", (ql + 2 * kvl, D), f"layers.{i}", True, "normal")
+        add(p + "wo", (D, ql), f"layers.{i}", True, "normal")
+        add(p + "wgu", (2 * Fl, D), f"layers.{i}", True, "normal")
+        add(p + "wdown", (D, Fl), f"layers.{i}", True, "normal")
+    if not cfg.tie_embeddings:
+        add("lm_head", (V // tp, D), "head", True, "normal")
+    return specs, n_rep, off
+
+
+def shard_tensor(cfg: TransformerConfig, name: str, full: torch.Tensor, r: int, tp: int) -> torch.Tensor:
+    """Rank r's piece of a full (engine-layout) tensor."""
+    q, kv = cfg.q_dim, cfg.kv_dim
+    ql, kvl = q // tp, kv // tp
+    Fl = cfg.ff_dim_padded // tp
+    if name.endswith("wqkv"):
+        return torch.cat([full[r * ql:(r + 1) * ql], full[q + r * kvl:q + (r + 1) * kvl],
+                          full[q + kv + r * kvl:q + kv + (r + 1) * kvl]])
+    if name.endswith(".wo"):
+        return full[:, r * ql:(r + 1) * ql]
+    if name.endswith("wgu"):  # blocked gate|up layout: rank r owns a contiguous run of blocks
+        return full[r * 2 * Fl:(r + 1) * 2 * Fl]
+    if name.endswith("wdown"):
+        return full[:, r * Fl:(r + 1) * Fl]
+    if name == "lm_head":
+        Vl = cfg.vocab_size // tp
+        return full[r * Vl:(r + 1) * Vl]
+    return full
+
+
+def unshard_tensor(cfg: TransformerConfig, name: str, pieces: List[torch.Tensor]) -> torch.Tensor:
+    """Inverse of shard_tensor over all ranks' pieces (rank order)."""
+    tp = len(pieces)
+    if name.endswith("wqkv"):
+        ql, kvl = cfg.q_dim // tp, cfg.kv_dim // tp
+        qs = [p[:ql] for p in pieces]
+        ks = [p[ql:ql + kvl] for p in pieces]
+        vs = [p[ql + kvl:] for p in pieces]
+        return torch.cat(qs + ks + vs)
+    if name.endswith(".wo") or name.endswith("wdown"):
+        return torch.cat(pieces, dim=1)
+    if name.endswith("wgu") or name == "lm_head":
+        return torch.cat(pieces, dim=0)
+    return pieces[0]
+
+
+class TPParams:
+    """Flat local parameter buffer of one TP rank with named views."""
+
+    def __init__(self, cfg: TransformerConfig, tp: int, rank: int, device, dtype=torch.bfloat16,
+                 buffer: Optional[torch.Tensor] = None):
+        self.cfg, self.tp, self.rank = cfg, tp, rank
+        self.specs, self.n_rep, self.numel = build_tp_layout(cfg, tp)
+        self.by_name = {s.name: s for s in self.specs}
+        self.flat = torch.zeros(self.numel, dtype=dtype, device=device) if buffer is None else buffer
+        assert self.flat.numel() == self.numel
+        self.views: Dict[str, torch.Tensor] = {
+            s.name: self.flat[s.offset:s.offset + s.numel].view(s.shape) for s in self.specs}
+        Vl = cfg.vocab_size // tp
+        if cfg.tie_embeddings:  # the vocabulary-parallel head is this rank's rows of the embedding
+            self.views["lm_head"] = self.views["embed"][rank * Vl:(rank + 1) * Vl]
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        return self.views[name]
+
+    def like(self, dtype=torch.float32, buffer: Optional[torch.Tensor] = None) -> "TPParams":
+        return TPParams(self.cfg, self.tp, self.rank, self.flat.device, dtype,
+                        buffer if buffer is not None else torch.zeros(self.numel, dtype=dtype,
+                                                                      device=self.flat.device))
+
+    def segments(self, lo: int = 0, hi: Optional[int] = None):
+        hi = self.numel if hi is None else hi
+        out = []
+        for s in self.specs:
+            a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
+            if a < b:
+                out.append((a - lo, b - a, s.decay))
+        return out
+
+    @torch.no_grad()
+    def load_full(self, full) -> None:
+        """Copy this rank's shards out of a full FlatParams (same cfg)."""
+        for s in self.specs:
+            self.views[s.name].copy_(shard_tensor(self.cfg, s.name, full[s.name], self.rank, self.tp))
+
+    @torch.no_grad()
+    def init_(self, seed: int, std: float) -> None:
+        """The shards of exactly the weights FlatParams(cfg).init_(seed, std)
+        produces (same per-tensor generators), one full tensor at a time."""
+        from ..models.params import FlatParams
+        full_specs, _, _ = build_layout(self.cfg)
+        idx = {s.name: k for k, s in enumerate(full_specs)}
+        cfg = self.cfg
+        F, Fp = cfg.ff_dim, cfg.ff_dim_padded
+        dev = self.flat.device
+        for s in self.specs:
+            fs = full_specs[idx[s.name]]
+            if fs.init == "ones":
+                self.views[s.name].fill_(1.0)
+                continue
+            g = torch.Generator(device=dev).manual_seed(seed * 1000003 + idx[s.name])
+            t = torch.empty(fs.shape, dtype=torch.float32, device=dev)
+            t.normal_(0.0, std, generator=g)
+            if s.name.endswith("wgu") and Fp != F:
+                blk = t.view(Fp // 128, 2, 128, -1)
+                mask = (torch.arange(Fp, device=dev) >= F).view(Fp // 128, 128)
+                blk[:, 0][mask] = 0.0
+                blk[:, 1][mask] = 0.0
+            if s.name.endswith("wdown") and Fp != F:
+                t[:, F:] = 0.0
+            self.views[s.name].copy_(shard_tensor(cfg, s.name, t, self.rank, self.tp).to(self.flat.dtype))
+            del t
+
+
+# ------------------------------------------------------------ communication
+class TPComm:
+    """Symmetric buffers and the fused-collective launch helpers of one TP group."""
+
+    def __init__(self, cfg: TransformerConfig, max_tokens: int, device, group=None, comm: str = "p2p"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group or dist.group.WORLD
+        self.tp = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.comm = comm
+        if max_tokens % (128 * self.tp):
+            raise ValueError(f"tokens per micro-batch ({max_tokens}) must be a multiple of 128 x tp")
+        self.max_tokens = max_tokens
+        D = cfg.hidden_dim
+        R = max_tokens // self.tp
+        self.pc = CM.PeerComm(self.device, self.group)
+        self.stage = [CM.SymBuffer(R * D, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.recv = [CM.SymBuffer(max_tokens * D, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.stats = CM.SymBuffer(max_tokens * 4, torch.float32, self.device, self.group)
+        self.count = torch.zeros(max_tokens // 128, dtype=torch.int32, device=self.device)
+        self._nccl_tmp: Dict[Tuple[int, int], torch.Tensor] = {}
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+
+    # ------------------------------------------------------------- views
+    def stage_view(self, k: int, rows: int, cols: int) -> torch.Tensor:
+        return self.stage[k].local[:rows * cols].view(rows, cols)
+
+    def recv_view(self, k: int, rows: int, cols: int) -> torch.Tensor:
+        return self.recv[k].local[:self.tp * rows * cols].view(self.tp * rows, cols)
+
+    def barrier(self) -> None:
+        if self.comm == "nccl":
+            return  # NCCL collectives synchronise by themselves
+        self.pc.barrier(SLOT_TP)
+
+    # --------------------------------------------------- K16 AG -> GEMM
+    def ag_gemm(self, k: int, dst: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
+                epi: str = "bf16", h_out: Optional[torch.Tensor] = None) -> None:
+        """dst <- all-gather of every rank's staging rows k; out = dst @ w^T.
+        The caller has written its own rows into stage k and called barrier()."""
+        T, K = dst.shape
+        R = T // self.tp
+        if self.comm == "nccl":
+            dist.all_gather_into_tensor(dst, self.stage_view(k, R, K), group=self.group)
+            G.gemm(dst, w, out, epi=epi, h_out=h_out)
+            return
+        C().gemm_ag(dst, w, out, EPI[epi], h_out, self.stage[k].ptrs, K, R, self.rank, self.count,
+                    (self.rank * R) // 128, status(self.device), 0)
+
+    # --------------------------------------------------- K18 GEMM -> RS
+    def gemm_rs(self, k: int, a: torch.Tensor, w: torch.Tensor) -> None:
+        """Partial a @ w^T; rows go to their owner's receive buffer k, slot = rank."""
+        T, Nc = a.shape[0], w.shape[0]
+        R = T // self.tp
+        if self.comm == "nccl":
+            full = self._tmp((T, Nc))
+            G.gemm(a, w, full)
+            dist.reduce_scatter_tensor(self.recv_view(k, R, Nc)[:R], full, group=self.group)
+            return
+        C().gemm_rs(a, w, self.recv[k].ptrs, R, self.rank, Nc, ((self.rank + 1) % self.tp) * R // 128,
+                    status(self.device), 0)
+
+    def rs_sum(self, k: int, out: torch.Tensor, resid: Optional[torch.Tensor] = None,
+               gamma: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None,
+               rstd: Optional[torch.Tensor] = None, eps: float = 1e-5) -> None:
+        """After gemm_rs(k): out = sum of the slots (+ resid); y = rmsnorm(out)."""
+        R, Nc = out.shape
+        self.barrier()
+        world = 1 if self.comm == "nccl" else self.tp
+        C().rs_sum(self.recv_view(k, R, Nc), world, out, resid, gamma, y, rstd, float(eps))
+
+    def _tmp(self, shape) -> torch.Tensor:
+        t = self._nccl_tmp.get(shape)
+        if t is None:
+            t = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+            self._nccl_tmp[shape] = t
+        return t
+
+    # ------------------------------------------------ vocab-parallel CE
+    def cross_entropy(self, logits: torch.Tensor, targets: torch.Tensor, loss_acc: torch.Tensor, *,
+                      scale: Optional[torch.Tensor], scale_mul: float, smoothing: float = 0.0,
+                      z_loss: float = 0.0, ignore_index: int = -100) -> None:
+        T, Vl = logits.shape
+        v0 = self.rank * Vl
+        st = self.stats.local[:T * 4]
+        args = (targets, loss_acc, scale, float(scale_mul), float(smoothing), float(z_loss),
+                int(ignore_index), True, v0, Vl * self.tp)
+        if self.comm == "nccl":
+            C().cross_entropy_vp(logits, *args, st, self._self_ptr(), 1)
+            allst = self._tmp_f32((self.tp * T * 4,))
+            dist.all_gather_into_tensor(allst, st, group=self.group)
+            ptrs = self._ptrs_of(allst, T * 4)
+            C().cross_entropy_vp(logits, *args, st, ptrs, 2)
+            return
+        C().cross_entropy_vp(logits, *args, st, self.stats.ptrs, 1)
+        self.barrier()
+        C().cross_entropy_vp(logits, *args, st, self.stats.ptrs, 2)
+
+    def _self_ptr(self) -> torch.Tensor:
+        if not hasattr(self, "_selfp"):
+            self._selfp = torch.tensor([self.stats.local.data_ptr()], dtype=torch.int64, device=self.device)
+        return self._selfp
+
+    def _tmp_f32(self, shape) -> torch.Tensor:
+        key = ("f32",) + tuple(shape)
+        t = self._nccl_tmp.get(key)
+        if t is None:
+            t = torch.empty(shape, dtype=torch.float32, device=self.device)
+            self._nccl_tmp[key] = t
+        return t
+
+    def _ptrs_of(self, buf: torch.Tensor, stride: int) -> torch.Tensor:
+        key = ("ptrs", buf.data_ptr(), stride)
+        t = self._nccl_tmp.get(key)
+        if t is None:
+            base = buf.data_ptr()
+            t = torch.tensor([base + 4 * stride * p for p in range(self.tp)], dtype=torch.int64,
+                             device=self.device)
+            self._nccl_tmp[key] = t
+        return t
+
+
+# ------------------------------------------------------------------- model
+class _TPWorkspace:
+    def __init__(self, cfg: TransformerConfig, tp: int, B: int, S: int, device):
+        T = B * S
+        R = T // tp
+        D = cfg.hidden_dim
+        L = cfg.num_layers
+        ql, kvl = cfg.q_dim // tp, cfg.kv_dim // tp
+        Fl = cfg.ff_dim_padded // tp
+        Vl = cfg.vocab_size // tp
+        bf = dict(dtype=torch.bfloat16, device=device)
+        f32 = dict(dtype=torch.float32, device=device)
+        self.B, self.S, self.T, self.R = B, S, T, R
+        self.h = [torch.empty(R, D, **bf) for _ in range(L + 1)]      # residual stream (local rows)
+        self.hmid = [torch.empty(R, D, **bf) for _ in range(L)]
+        self.rstd1 = [torch.empty(R, **f32) for _ in range(L)]
+        self.rstd2 = [torch.empty(R, **f32) for _ in range(L)]
+        self.rstdf = torch.empty(R, **f32)
+        self.xn1 = [torch.empty(T, D, **bf) for _ in range(L)]        # gathered normalised inputs
+        self.xn2 = [torch.empty(T, D, **bf) for _ in range(L)]
+        self.xf = torch.empty(T, D, **bf)
+        self.qkv = [torch.empty(T, ql + 2 * kvl, **bf) for _ in range(L)]
+        self.o = [torch.empty(T, ql, **bf) for _ in range(L)]
+        self.lse = [torch.empty(B, cfg.num_heads // tp, S, **f32) for _ in range(L)]
+        self.gu = [torch.empty(T, 2 * Fl, **bf) for _ in range(L)]
+        self.act = [torch.empty(T, Fl, **bf) for _ in range(L)]
+        self.logits = torch.empty(T, Vl, **bf)
+        self.loss_acc = torch.zeros(2, **f32)
+        self.dfull = torch.empty(T, D, **bf)       # gathered residual gradient
+        self.dx = torch.empty(R, D, **bf)
+        self.dact = torch.empty(T, Fl, **bf)
+        self.dgu = torch.empty(T, 2 * Fl, **bf)
+        self.do = torch.empty(T, ql, **bf)
+        self.dqkv = torch.empty(T, ql + 2 * kvl, **bf)
+
+
+class TPLlamaModel:
+    """Llama decoder sharded over a TP group (one process per GPU).
+
+    forward_backward(ids, targets) takes the FULL micro-batch [B, S] on every
+    rank (every rank reads its own token rows of it) and returns the loss
+    accumulator [sum of token losses, count] - identical on every rank."""
+
+    def __init__(self, cfg: TransformerConfig, comm: TPComm, params: Optional[TPParams] = None,
+                 seed: int = 1234, grads: Optional[TPParams] = None):
+        self.cfg = cfg
+        self.comm = comm
+        self.tp, self.rank = comm.tp, comm.rank
+        self.device = comm.device
+        check_tp_config(cfg, self.tp)
+        if params is None:
+            params = TPParams(cfg, self.tp, self.rank, self.device)
+            params.init_(seed, cfg.init_std)
+        self.params = params
+        self.grads = grads if grads is not None else params.like(torch.float32)
+        self.rope = E.rope_table(max(cfg.max_seq_len, 1), cfg.head_dim, cfg.rope_base, self.device)
+        self._ws: Dict[Tuple[int, int], _TPWorkspace] = {}
+        self._overwrite = False
+
+    def workspace(self, B: int, S: int) -> _TPWorkspace:
+        ws = self._ws.get((B, S))
+        if ws is None:
+            if B * S > self.comm.max_tokens:
+                raise ValueError(f"micro-batch of {B * S} tokens exceeds the TP buffers ({self.comm.max_tokens})")
+            if S > self.rope.shape[0]:
+                self.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
+            ws = _TPWorkspace(self.cfg, self.tp, B, S, self.device)
+            self._ws[(B, S)] = ws
+        return ws
+
+    def _p(self, n):
+        return self.params[n]
+
+    def _g(self, n):
+        return self.grads[n]
+
+    def _wgrad(self, dy, x, name):
+        G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
+
+    # -------------------------------------------------------------- forward
+    def _forward(self, ids: torch.Tensor, ws: _TPWorkspace) -> None:
+        cfg, c = self.cfg, self.comm
+        R, D, eps = ws.R, cfg.hidden_dim, cfg.norm_eps
+        Hl, Hkvl = cfg.num_heads // self.tp, cfg.num_kv_heads // self.tp
+        ids_local = ids.reshape(-1)[self.rank * R:(self.rank + 1) * R]
+        E.embedding_fwd(ids_local, self._p("embed"), out=ws.h[0])
+        N.rmsnorm_fwd(ws.h[0], self._p("layers.0.attn_norm"), eps, y=c.stage_view(0, R, D), rstd=ws.rstd1[0])
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}."
+            c.barrier()
+            c.ag_gemm(0, ws.xn1[i], self._p(p + "wqkv"), ws.qkv[i])
+            E.rope_(ws.qkv[i], 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S)
+            A.attention_fwd(ws.qkv[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim, causal=True,
+                            out=ws.o[i], lse=ws.lse[i])
+            c.gemm_rs(0, ws.o[i], self._p(p + "wo"))
+            c.rs_sum(0, ws.hmid[i], resid=ws.h[i], gamma=self._p(p + "ffn_norm"),
+                     y=c.stage_view(1, R, D), rstd=ws.rstd2[i], eps=eps)
+            c.barrier()
+            c.ag_gemm(1, ws.xn2[i], self._p(p + "wgu"), ws.gu[i], epi="swiglu", h_out=ws.act[i])
+            c.gemm_rs(1, ws.act[i], self._p(p + "wdown"))
+            last = i == cfg.num_layers - 1
+            nxt = "final_norm" if last else f"layers.{i + 1}.attn_norm"
+            c.rs_sum(1, ws.h[i + 1], resid=ws.hmid[i], gamma=self._p(nxt), y=c.stage_view(0, R, D),
+                     rstd=ws.rstdf if last else ws.rstd1[i + 1], eps=eps)
+        c.barrier()
+        c.ag_gemm(0, ws.xf, self._p("lm_head"), ws.logits)
+
+    # ----------------------------------------------------- forward+backward
+    @torch.no_grad()
+    def forward_backward(self, ids: torch.Tensor, targets: torch.Tensor, *,
+                         loss_scale: Optional[torch.Tensor] = None, grad_scale: float = 1.0,
+                         label_smoothing: float = 0.0, z_loss: float = 0.0,
+                         loss_acc: Optional[torch.Tensor] = None,
+                         overwrite_grads: bool = False) -> torch.Tensor:
+        cfg, c = self.cfg, self.comm
+        self._overwrite = overwrite_grads
+        B, S = ids.shape
+        ws = self.workspace(B, S)
+        R, D, L = ws.R, cfg.hidden_dim, cfg.num_layers
+        Hl, Hkvl = cfg.num_heads // self.tp, cfg.num_kv_heads // self.tp
+        acc = ws.loss_acc if loss_acc is None else loss_acc
+        if loss_acc is None:
+            acc.zero_()
+        self._forward(ids, ws)
+        c.cross_entropy(ws.logits, targets.reshape(-1), acc, scale=loss_scale, scale_mul=grad_scale,
+                        smoothing=label_smoothing, z_loss=z_loss)
+        dlog = ws.logits
+        # LM head: dW (local vocab rows), dx partial -> owners
+        self._wgrad(dlog, ws.xf, "lm_head")
+        c.gemm_rs(1, dlog, self._p("lm_head").t())
+        c.rs_sum(1, ws.dx)
+        dh = c.stage_view(0, R, D)
+        N.rmsnorm_bwd(ws.dx, ws.h[L], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=dh,
+                      accumulate=not overwrite_grads)
+        k = 0
+        for i in reversed(range(L)):
+            p = f"layers.{i}."
+            # ---- FFN: dact = dh_full Wdown (all-gather fused), dgu, dxn2 -> owners
+            c.barrier()
+            c.ag_gemm(k, ws.dfull, self._p(p + "wdown").t(), ws.dact)
+            self._wgrad(ws.dfull, ws.act[i], p + "wdown")
+            E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
+            self._wgrad(ws.dgu, ws.xn2[i], p + "wgu")
+            c.gemm_rs(0, ws.dgu, self._p(p + "wgu").t())
+            c.rs_sum(0, ws.dx)
+            dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
+            N.rmsnorm_bwd(ws.dx, ws.hmid[i], self._p(p + "ffn_norm"), ws.rstd2[i], self._g(p + "ffn_norm"),
+                          dres=dh_in, dx=dh_out, accumulate=not overwrite_grads)
+            k = 1 - k
+            # ---- attention
+            c.barrier()
+            c.ag_gemm(k, ws.dfull, self._p(p + "wo").t(), ws.do)
+            self._wgrad(ws.dfull, ws.o[i], p + "wo")
+            A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim,
+                            causal=True, dqkv=ws.dqkv)
+            E.rope_(ws.dqkv, 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S, inverse=True)
+            self._wgrad(ws.dqkv, ws.xn1[i], p + "wqkv")
+            c.gemm_rs(1, ws.dqkv, self._p(p + "wqkv").t())
+            c.rs_sum(1, ws.dx)
+            dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
+            N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[i], self._g(p + "attn_norm"),
+                          dres=dh_in, dx=dh_out, accumulate=not overwrite_grads)
+            k = 1 - k
+        if overwrite_grads and not cfg.tie_embeddings:
+            self._g("embed").zero_()
+        ids_local = ids.reshape(-1)[self.rank * R:(self.rank + 1) * R]
+        E.embedding_bwd(ids_local, c.stage_view(k, R, D), self._g("embed"))
+        self._overwrite = False
+        return acc
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        """Local vocabulary slice of the logits, [B*S, V/tp] (bf16)."""
+        B, S = ids.shape
+        ws = self.workspace(B, S)
+        self._forward(ids, ws)
+        return ws.logits
+
+
+# ----------------------------------------------------------------- trainer
+class TPTrainer:
+    """AdamW training of a TPLlamaModel: gradient accumulation, replicated-grad
+    all-reduce (K12, peer memory), the global-norm exchange and finaliser on the
+    device, then AdamW over this rank's local parameters."""
+
+    def __init__(self, cfg: TransformerConfig, tc, *, micro_batch: int, seq_len: int, device=None,
+                 group=None, comm: str = "p2p", seed: int = 1234):
+        from ..ops import optim as O
+        from ..train.optimizer import FusedAdamW
+        self.cfg, self.tc = cfg, tc
+        self.device = torch.device(device or torch.cuda.current_device())
+        self.comm = TPComm(cfg, micro_batch * seq_len, self.device, group, comm)
+        self.tp, self.rank = self.comm.tp, self.comm.rank
+        params = TPParams(cfg, self.tp, self.rank, self.device)
+        params.init_(seed, cfg.init_std)
+        # fp32 gradients in symmetric memory: the replicated prefix is summed in place over peers
+        self.gbuf = CM.SymBuffer(params.numel, torch.float32, self.device, self.comm.group)
+        grads = params.like(torch.float32, buffer=self.gbuf.local)
+        self.model = TPLlamaModel(cfg, self.comm, params, grads=grads)
+        self.params, self.grads = params, grads
+        self.master = params.flat.float()
+        self.opt = FusedAdamW(self.master, params.segments(), lr=tc.lr, betas=(tc.beta1, tc.beta2),
+                              eps=tc.eps, weight_decay=tc.weight_decay, max_grad_norm=tc.max_grad_norm,
+                              dynamic_loss_scale=tc.dynamic_loss_scale,
+                              init_loss_scale=tc.init_loss_scale, ema_decay=tc.ema_decay)
+        self.n_rep = params.n_rep
+        self.partial = torch.zeros(256, dtype=torch.float32, device=self.device)
+        self._O = O
+        self.micro = 0
+
+    def set_learning_rate(self, lr: float) -> None:
+        self.opt.set_lr(lr)
+
+    def micro_step(self, ids: torch.Tensor, targets: torch.Tensor, grad_scale: float,
+                   loss_acc: torch.Tensor) -> None:
+        self.model.forward_backward(ids, targets, loss_scale=self.opt.scaler.scale_tensor(),
+                                    grad_scale=grad_scale, loss_acc=loss_acc,
+                                    label_smoothing=self.tc.label_smoothing, z_loss=self.tc.z_loss,
+                                    overwrite_grads=self.micro == 0)
+        self.micro += 1
+
+    def optimizer_step(self) -> None:
+        c = self.comm
+        P = self.partial
+        if self.tp > 1:
+            # replicated grads: one-shot peer all-reduce + their sum-of-squares partials
+            if c.comm == "nccl":
+                dist.all_reduce(self.gbuf.local[:self.n_rep], group=c.group)
+                P[128:].zero_()
+                C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[128:])
+                P[128:].div_(self.tp)  # every rank holds the same replicated grads
+            else:
+                c.pc.allreduce_sum_(self.gbuf, self.n_rep, P[128:])
+        else:
+            C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[128:])
+        C().grad_norm_partials(self.gbuf.local[self.n_rep:], P[:128])
+        o = self.opt
+        s = o.scaler
+        if self.tp > 1 and c.comm != "nccl":
+            c.pc.norm_exchange(P, o.state, o.max_grad_norm, s.enabled, s.growth, s.backoff,
+                               s.growth_interval, s.min_scale)
+        elif self.tp > 1:
+            dist.all_reduce(P, group=c.group)
+            o.finalize(P)
+        else:
+            o.finalize(P)
+        o.apply(self.gbuf.local, self.params.flat)
+        self.micro = 0
+
+    def train_step(self, batches) -> torch.Tensor:
+        """batches: list of (ids, targets) [B, S] micro-batches (full batch on
+        every rank).  Returns the loss accumulator [sum, count]."""
+        acc = torch.zeros(2, dtype=torch.float32, device=self.device)
+        n_tok = sum(int(t.numel()) for _, t in batches)
+        for ids, tg in batches:
+            self.micro_step(ids, tg, 1.0 / n_tok, acc)
+        self.optimizer_step()
+        return acc
+
+    def check(self) -> None:
+        check_status(self.device)
+
+    def full_state_dict(self) -> "OrderedDict[str, torch.Tensor]":
+        """Engine-layout full tensors (gathered over the TP group with NCCL)."""
+        out: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+        for s in self.params.specs:
+            v = self.params[s.name].contiguous()
+            pieces = [torch.empty_like(v) for _ in range(self.tp)]
+            dist.all_gather(pieces, v, group=self.comm.group)
+            out[s.name] = unshard_tensor(self.cfg, s.name, pieces)
+        return out

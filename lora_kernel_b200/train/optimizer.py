@@ -81,10 +81,11 @@ class FusedAdamW:
         O.finalize(self.partial if partial is None else partial, self.state, self.max_grad_norm,
                    s.enabled, s.growth, s.backoff, s.growth_interval, s.min_scale)
 
-    def apply(self, grad: torch.Tensor, p16: Optional[torch.Tensor], zero_grad: bool = True) -> None:
+    def apply(self, grad: torch.Tensor, p16: Optional[torch.Tensor], zero_grad: bool = True,
+              p16_peers: Optional[torch.Tensor] = None) -> None:
         O.adamw_(self.p32, grad, self.m, self.v, self.chunks, self.state, p16=p16, ema=self.ema,
                  beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, wd=self.wd,
-                 ema_decay=self.ema_decay, zero_grad=zero_grad)
+                 ema_decay=self.ema_decay, zero_grad=zero_grad, p16_peers=p16_peers)
 
     def step(self, grad: torch.Tensor, p16: Optional[torch.Tensor]) -> None:
         """grad-norm partials -> finalize (clip/skip/scale) -> AdamW (+EMA),

@@ -80,3 +80,31 @@ def test_layout_collectives_gloo():
     for p in ps:
         p.join(timeout=60)
     assert all(ok_g and ok_r for _, ok_g, ok_r in res), res
+
+
+def test_tp_layout_shard_roundtrip():
+    """Every rank's TP shard of the seeded weights reassembles the full tensors."""
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.parallel import tp as TP
+    cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=512,
+                            vocab_size=1024, num_layers=2, max_seq_len=256)
+    full = FlatParams(cfg, "cpu", torch.float32)
+    full.init_(5, 0.02)
+    for tp in (1, 2):
+        shards = [TP.TPParams(cfg, tp, r, "cpu", torch.float32) for r in range(tp)]
+        for s in shards:
+            s.init_(5, 0.02)
+        for sp in shards[0].specs:
+            rec = TP.unshard_tensor(cfg, sp.name, [s[sp.name] for s in shards])
+            assert torch.equal(rec, full[sp.name]), sp.name
+        # replicated tensors come first and are contiguous
+        assert all(s.group == "replicated" for s in shards[0].specs if s.offset < shards[0].n_rep)
+
+
+def test_tp_config_checks():
+    from lora_kernel_b200.parallel import tp as TP
+    cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=512,
+                            vocab_size=1024, num_layers=2)
+    TP.check_tp_config(cfg, 2)
+    with pytest.raises(ValueError):
+        TP.check_tp_config(cfg, 4)  # 2 KV heads cannot split 4 ways
