@@ -550,6 +550,23 @@ void allreduce_sum(torch::Tensor buf_ptrs, int64_t n, int64_t rank, int64_t worl
                          partial.has_value() ? (int)partial->numel() : 0, stream()));
 }
 
+void allreduce_sum_nvls(int64_t mc_ptr, int64_t n, int64_t rank, int64_t world,
+                        c10::optional<torch::Tensor> partial, torch::Tensor like) {
+  const c10::cuda::CUDAGuard g(like.device());
+  check(lk_allreduce_sum_nvls(reinterpret_cast<float*>(mc_ptr), n, (int)rank, (int)world, optp<float>(partial),
+                              partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
+void reduce_scatter_sum_nvls(int64_t mc_ptr, int64_t n, torch::Tensor dst, bool accumulate,
+                             c10::optional<torch::Tensor> partial) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  need_contig(dst, "dst", torch::kFloat32);
+  TORCH_CHECK(dst.numel() >= n, "reduce_scatter_nvls: dst too small");
+  check(lk_reduce_scatter_sum_nvls(reinterpret_cast<const float*>(mc_ptr), n, dst.data_ptr<float>(),
+                                   accumulate ? 1 : 0, optp<float>(partial),
+                                   partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
 void norm_exchange(torch::Tensor partial, torch::Tensor nbuf_ptrs, torch::Tensor sig_ptrs, int64_t rank,
                    int64_t world, int64_t slot, int64_t epoch, torch::Tensor state, double max_norm,
                    bool dynamic, double growth, double backoff, int64_t growth_interval, double min_scale,
@@ -670,6 +687,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &gemm_rs);
   m.def("gemm_ag", &gemm_ag);
   m.def("rs_sum", &rs_sum);
+  m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
+  m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);
   m.def("launch_count", []() { return (int64_t)lk_launch_count(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -230,6 +230,76 @@ __global__ void norm_exchange_kernel(const float* __restrict__ partial, int npar
   }
 }
 
+// ------------------------------------------------------------------ NVLS
+// The same two reductions through the NVSwitch: a multicast address maps
+// every rank's copy of the buffer; multimem.ld_reduce returns the sum over all
+// ranks (reduced inside the switch) and multimem.st writes one value into
+// every rank's copy.  Each rank moves 1/world of the data once in each
+// direction instead of pulling every peer's copy.
+__device__ __forceinline__ float4 mm_ld_reduce_add(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void mm_st(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void block_partial(float ss, float* partial) {
+  __shared__ float red[8];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < 8; ++k) t += red[k];
+    partial[blockIdx.x] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256) allreduce_nvls_kernel(float* __restrict__ mc, int64_t n, int rank,
+                                                             int world, float* __restrict__ partial) {
+  const int64_t n4 = n / 4;
+  const int64_t per = (n4 + world - 1) / world;
+  const int64_t lo = rank * per, hi = min(n4, lo + per);
+  float ss = 0.f;
+  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = mm_ld_reduce_add(mc + 4 * i);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    mm_st(mc + 4 * i, v);
+  }
+  if (partial) block_partial(ss, partial);
+}
+
+__global__ void __launch_bounds__(256) reduce_scatter_nvls_kernel(const float* __restrict__ mc, int64_t n,
+                                                                  float* __restrict__ dst, int accumulate,
+                                                                  float* __restrict__ partial) {
+  float ss = 0.f;
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = mm_ld_reduce_add(mc + 4 * i);
+    float4* d = reinterpret_cast<float4*>(dst) + i;
+    if (accumulate) {
+      const float4 o = *d;
+      acc.x += o.x;
+      acc.y += o.y;
+      acc.z += o.z;
+      acc.w += o.w;
+    }
+    *d = acc;
+    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+  }
+  if (partial) block_partial(ss, partial);
+}
+
 static int copy_grid(int64_t work) {
   int64_t g = (work + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 4;
@@ -290,4 +360,24 @@ extern "C" int lk_norm_exchange(const float* partial, int nparts, double* const*
                                          epoch, state, max_norm, dynamic, growth, backoff,
                                          growth_interval, min_scale, status);
   return check_launch("norm_exchange");
+}
+
+extern "C" int lk_allreduce_sum_nvls(float* mc, int64_t n, int rank, int world, float* partial, int nparts,
+                                     cudaStream_t s) {
+  LK_REQUIRE(mc && n % 4 == 0 && ((uintptr_t)mc & 15) == 0, "allreduce_nvls: aligned multicast buffer, n % 4");
+  int grid = copy_grid((n / 4 + world - 1) / world);
+  if (partial) grid = nparts < grid ? nparts : grid;
+  allreduce_nvls_kernel<<<grid, 256, 0, s>>>(mc, n, rank, world, partial);
+  if (partial && nparts > grid) cudaMemsetAsync(partial + grid, 0, sizeof(float) * (nparts - grid), s);
+  return check_launch("allreduce_nvls");
+}
+
+extern "C" int lk_reduce_scatter_sum_nvls(const float* mc, int64_t n, float* dst, int accumulate, float* partial,
+                                          int nparts, cudaStream_t s) {
+  LK_REQUIRE(mc && n % 4 == 0 && ((uintptr_t)mc & 15) == 0, "reduce_scatter_nvls: aligned multicast buffer");
+  int grid = copy_grid(n / 4);
+  if (partial) grid = nparts < grid ? nparts : grid;
+  reduce_scatter_nvls_kernel<<<grid, 256, 0, s>>>(mc, n, dst, accumulate, partial);
+  if (partial && nparts > grid) cudaMemsetAsync(partial + grid, 0, sizeof(float) * (nparts - grid), s);
+  return check_launch("reduce_scatter_nvls");
 }

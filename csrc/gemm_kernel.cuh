@@ -112,38 +112,42 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
-// K16 copy warp: pull this CTA's share of the peers' rows into the local A buffer.
-static __device__ __noinline__ void ag_copy_warp(const GemmArgs& a, int lane) {
+// K16 copy warps (AG_WARPS per CTA): pull the gathered rows of A into the
+// local buffer, one 16-row piece at a time.  Pieces are numbered own rows
+// first, then rank+1, rank+2, ... (the M-tile order of the GEMM), and dealt
+// round-robin over every copy warp of the grid so the first pieces land on
+// all SMs at once.  Each lane keeps 16 x 16-byte loads in flight per row.
+constexpr int AG_WARPS = 2;
+
+__device__ __forceinline__ void ag_copy_warp(const GemmArgs& a, int cw, int ncw, int lane) {
   const int R = a.ag_rows, W = a.ag_world, me = a.ag_rank;
   const int per_rank = R / AG_SUB;
   const int total = per_rank * W;
-  const int units = AG_SUB * a.ag_row_bytes / 16;
-  for (int s = blockIdx.x; s < total; s += gridDim.x) {
-    const int p = (me + s / per_rank) % W;  // own rows first, then the next ranks (tile order matches)
+  const int upr = a.ag_row_bytes / 16;  // 16-byte units per row
+  for (int s = cw; s < total; s += ncw) {
+    const int p = (me + s / per_rank) % W;
     const int r0 = (s % per_rank) * AG_SUB;
     const uint8_t* src = a.ag_src[p] + (int64_t)r0 * a.ag_ld_src;
     uint8_t* dst = a.ag_dst + (int64_t)(p * R + r0) * a.ag_ld_dst;
-    const int upr = a.ag_row_bytes / 16;  // 16-byte units per row
-    for (int u0 = lane; u0 < units; u0 += 32 * 16) {
-      uint4 v[16];
+#pragma unroll 1
+    for (int r = 0; r < AG_SUB; ++r) {
+      const uint4* sr = reinterpret_cast<const uint4*>(src + (int64_t)r * a.ag_ld_src);
+      uint4* dr = reinterpret_cast<uint4*>(dst + (int64_t)r * a.ag_ld_dst);
+#pragma unroll 1
+      for (int c0 = lane; c0 < upr; c0 += 32 * 16) {
+        uint4 v[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int u = u0 + 32 * k;
-        if (u < units) v[k] = *reinterpret_cast<const uint4*>(src + (int64_t)(u / upr) * a.ag_ld_src + (u % upr) * 16);
-      }
+        for (int k = 0; k < 16; ++k)
+          if (c0 + 32 * k < upr) v[k] = sr[c0 + 32 * k];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int u = u0 + 32 * k;
-        if (u < units) *reinterpret_cast<uint4*>(dst + (int64_t)(u / upr) * a.ag_ld_dst + (u % upr) * 16) = v[k];
+        for (int k = 0; k < 16; ++k)
+          if (c0 + 32 * k < upr) dr[c0 + 32 * k] = v[k];
       }
     }
+    fence_proxy_async_global();  // the rows are read next by TMA (async proxy)
     __threadfence();
-    fence_proxy_async_global();
     __syncwarp();
-    if (lane == 0) {
-      __threadfence();
-      atomicAdd(a.ag_count + (p * R + r0) / 128, 1);
-    }
+    if (lane == 0) atomicAdd(a.ag_count + (p * R + r0) / 128, 1);
   }
 }
 
@@ -173,7 +177,7 @@ __device__ __forceinline__ bool ag_wait_chunk(const GemmArgs& a, int tm, volatil
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool AG = false>
-__global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 : GEMM_THREADS, 1)
+__global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const GemmArgs args) {
@@ -330,9 +334,9 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 : GEMM_THREADS, 1)
       tc_commit(drain_bar);
       bounded_wait(drain_bar, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
-  } else if (AG && warp == 6) {
-    // ------------------------------------------------------- K16 copy warp
-    ag_copy_warp(args, lane);
+  } else if (AG && warp >= 6) {
+    // ------------------------------------------------------ K16 copy warps
+    ag_copy_warp(args, (warp - 6) * gridDim.x + blockIdx.x, AG_WARPS * gridDim.x, lane);
   } else {
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -393,6 +397,44 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 : GEMM_THREADS, 1)
             }
           }
         }
+      } else if constexpr (EPI == EPI_REMOTE) {
+        // K18: stage 32 rows x 64 columns (bf16) per warp in shared memory,
+        // then store whole 128-byte row segments into the owner's receive
+        // slot over NVLink (4 rows per warp instruction).
+        uint8_t* stg = smem + C::STAGES * C::STAGE + C::BAR_BYTES + q * 4096;
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(taddr + c * 64, r0);
+          tmem_ld32(taddr + c * 64 + 32, r1);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* rr = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(rr[0]) * alpha, __uint_as_float(rr[1]) * alpha);
+            pk.y = pack_bf16x2(__uint_as_float(rr[2]) * alpha, __uint_as_float(rr[3]) * alpha);
+            pk.z = pack_bf16x2(__uint_as_float(rr[4]) * alpha, __uint_as_float(rr[5]) * alpha);
+            pk.w = pack_bf16x2(__uint_as_float(rr[6]) * alpha, __uint_as_float(rr[7]) * alpha);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) = pk;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rl = it * 4 + (lane >> 3);
+            const int j = lane & 7;
+            const uint4 pk = *reinterpret_cast<const uint4*>(stg + rl * 128 + ((j ^ (rl & 7)) * 16));
+            const int grow = tm * GEMM_BM + q * 32 + rl;
+            const int col = tn * BN + c * 64 + j * 8;
+            if (grow < args.M && col < args.N) {
+              const int owner = grow / args.rs_rows;
+              __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
+                                    (int64_t)(args.rs_rank * args.rs_rows + grow - owner * args.rs_rows) * args.ldd;
+              *reinterpret_cast<uint4*>(drow + col) = pk;
+            }
+          }
+          __syncwarp();
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -401,15 +443,8 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 : GEMM_THREADS, 1)
           tc_wait_ld();
           if (!row_ok) continue;
           const int col0 = tn * BN + c * 32;
-          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID || EPI == EPI_REMOTE) {
-            __nv_bfloat16* drow;
-            if constexpr (EPI == EPI_REMOTE) {
-              const int owner = row / args.rs_rows;
-              drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
-                     (int64_t)(args.rs_rank * args.rs_rows + row - owner * args.rs_rows) * args.ldd;
-            } else {
-              drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
-            }
+          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
+            __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int col = col0 + v * 8;
@@ -513,8 +548,9 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
+  constexpr int SMEM = C::SMEM + (EPI == EPI_REMOTE ? 4 * 4096 : 0);  // + K18 staging
   if (!(attr_set & (1ull << dev))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     attr_set |= 1ull << dev;
   }
   const int tiles = args.tiles_m * args.tiles_n;
@@ -524,15 +560,15 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
     if (cudaMemsetAsync(g.ag_count, 0, sizeof(int) * args.tiles_m, stream) != cudaSuccess)
       return fail("gemm_ag: memset failed");
     void* params[] = {&ta, &tb, &ta2, &tb2, &args};
-    cudaError_t e = cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(GEMM_THREADS + 32), params,
-                                                C::SMEM, stream);
+    cudaError_t e = cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(GEMM_THREADS + 32 * AG_WARPS), params,
+                                                SMEM, stream);
     if (e != cudaSuccess) {
       last_error() = std::string("gemm_ag cooperative launch: ") + cudaGetErrorString(e);
       return -1;
     }
     return check_launch("gemm_tc_kernel_ag");
   } else {
-    kern<<<grid, GEMM_THREADS, C::SMEM, stream>>>(ta, tb, ta2, tb2, args);
+    kern<<<grid, GEMM_THREADS, SMEM, stream>>>(ta, tb, ta2, tb2, args);
     return check_launch("gemm_tc_kernel");
   }
 }

@@ -313,6 +313,12 @@ int lk_allgather_copy(const void* const* src_ptrs, int64_t src_off_bytes, int64_
                       void* dst, int world, cudaStream_t s);
 int lk_reduce_scatter_sum(const float* const* src_ptrs, int64_t src_off, int64_t n, float* dst,
                           int world, int accumulate, float* partial, int nparts, cudaStream_t s);
+// NVLS variants: `mc` is the multicast address of the symmetric buffer (+ the
+// element offset); reductions happen inside the NVSwitch (multimem.*).
+int lk_allreduce_sum_nvls(float* mc, int64_t n, int rank, int world, float* partial, int nparts,
+                          cudaStream_t s);
+int lk_reduce_scatter_sum_nvls(const float* mc, int64_t n, float* dst, int accumulate, float* partial,
+                               int nparts, cudaStream_t s);
 int lk_allreduce_sum(float* const* buf_ptrs, int64_t n, int rank, int world, float* partial,
                      int nparts, cudaStream_t s);
 int lk_norm_exchange(const float* partial, int nparts, double* const* nbuf_ptrs, int* const* sig_ptrs,

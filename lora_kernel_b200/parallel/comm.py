@@ -71,6 +71,22 @@ class SymBuffer:
         self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self.dtype = dtype
         self.numel = numel
+        # NVLS multicast address of the buffer (0 when the switch/driver offers none)
+        try:
+            self.mc_ptr = int(self.handle.multicast_ptr) if self.world > 1 else 0
+        except Exception:  # noqa: BLE001 - older builds expose no multicast
+            self.mc_ptr = 0
+        self._offset_tables: Dict[int, torch.Tensor] = {}
+
+    def ptrs_at(self, off_elems: int) -> torch.Tensor:
+        """Device table of every rank's address of element `off_elems`."""
+        t = self._offset_tables.get(off_elems)
+        if t is None:
+            es = self.element_size()
+            t = torch.tensor([p + es * off_elems for p in self.ptrs_host], dtype=torch.int64,
+                             device=self.ptrs.device)
+            self._offset_tables[off_elems] = t
+        return t
 
     def element_size(self) -> int:
         return torch.empty((), dtype=self.dtype).element_size()
@@ -88,6 +104,8 @@ class PeerComm:
         self.sig = SymBuffer(nslots * self.world, torch.int32, self.device, self.group)
         self.nbuf = SymBuffer(max(2, self.world) * 2, torch.float64, self.device, self.group)
         self.epochs: Dict[int, int] = {}
+        # in-switch reductions (multimem) when NVLS is available; LK_NVLS=0 turns them off
+        self.nvls = os.environ.get("LK_NVLS", "1") != "0" and self.sig.mc_ptr != 0
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)
 
@@ -108,12 +126,21 @@ class PeerComm:
 
     def reduce_scatter_sum(self, src: SymBuffer, src_off: int, n: int, dst: torch.Tensor,
                            accumulate: bool = False, partial: Optional[torch.Tensor] = None) -> None:
-        C().reduce_scatter_sum(src.ptrs, src_off, n, dst, self.world, accumulate, partial)
+        """dst[:n] (+)= sum over ranks of src[src_off:src_off+n] (fp32).  The
+        caller has made every rank's src ready (device barrier)."""
+        if self.nvls and src.mc_ptr:
+            C().reduce_scatter_sum_nvls(src.mc_ptr + 4 * src_off, n, dst, accumulate, partial)
+        else:
+            C().reduce_scatter_sum(src.ptrs, src_off, n, dst, self.world, accumulate, partial)
 
-    def allreduce_sum_(self, buf: SymBuffer, n: int, partial: Optional[torch.Tensor] = None) -> None:
-        """In-place sum over ranks of buf[:n] (fp32), bracketed by barriers."""
+    def allreduce_sum_(self, buf: SymBuffer, n: int, partial: Optional[torch.Tensor] = None,
+                       off: int = 0) -> None:
+        """In-place sum over ranks of buf[off:off+n] (fp32), bracketed by barriers."""
         self.barrier(SLOT_AR_IN)
-        C().allreduce_sum(buf.ptrs, n, self.rank, self.world, partial)
+        if self.nvls and buf.mc_ptr:
+            C().allreduce_sum_nvls(buf.mc_ptr + 4 * off, n, self.rank, self.world, partial, buf.local)
+        else:
+            C().allreduce_sum(buf.ptrs_at(off), n, self.rank, self.world, partial)
         self.barrier(SLOT_AR_OUT)
 
     def norm_exchange(self, partial: torch.Tensor, state: torch.Tensor, max_norm: float,

@@ -85,12 +85,6 @@ class DataParallelTrainer:
             self.opt = FusedAdamW(master, segs, **okw)
             self.shard_grads = torch.zeros(L.shard_numel, dtype=f32, device=self.device)
         self.partial = torch.zeros(len(L.names) * NP, dtype=f32, device=self.device)
-        # per-group peer pointer tables (the all-reduce works on [0, n) of each table)
-        self._gptrs: Dict[str, torch.Tensor] = {}
-        if comm == "p2p":
-            for g, (s, e) in L.groups.items():
-                self._gptrs[g] = torch.tensor([p + 4 * s for p in self.g_sym.ptrs_host], dtype=torch.int64,
-                                              device=self.device)
         self.comm_stream = torch.cuda.Stream(self.device)
         self.accum_steps = max(1, tc.grad_accum_steps)
         self._micro = 0
@@ -114,9 +108,7 @@ class DataParallelTrainer:
         s, e = self.L.groups[g]
         if self.stage == 0:
             if self.mode == "p2p":
-                self.pc.barrier(CM.SLOT_AR_IN)
-                C().allreduce_sum(self._gptrs[g], e - s, self.rank, self.world, part)
-                self.pc.barrier(CM.SLOT_AR_OUT)
+                self.pc.allreduce_sum_(self.g_sym, e - s, part, off=s)
             else:
                 dist.all_reduce(self.grads.flat[s:e], group=self.group)
                 part.zero_()

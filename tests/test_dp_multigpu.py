@@ -16,13 +16,17 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("stage,mode", [(0, "p2p"), (1, "p2p"), (2, "p2p"), (2, "nccl"), (0, "nccl")])
+@pytest.mark.parametrize("stage,mode", [(0, "p2p"), (1, "p2p"), (2, "p2p"), (2, "nccl"), (0, "nccl"),
+                                        (0, "p2p-nonvls"), (2, "p2p-nonvls")])
 def test_dp_matches_single_gpu(stage, mode, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
     out = str(tmp_path / "dp.pt")
     env = dict(os.environ, LK_OUT=out, NCCL_NVLS_ENABLE="0")
+    if mode.endswith("-nonvls"):  # the one-shot P2P kernels instead of multimem
+        env["LK_NVLS"] = "0"
+        mode = mode.split("-")[0]
     port = random.randint(20000, 40000)
     cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(port),
