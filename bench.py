@@ -125,14 +125,14 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def build_trainer(impl: str, cfg, tc, rank: int, world: int):
+def build_trainer(impl: str, cfg, tc, rank: int, world: int, fuse_gather: bool = False):
     if impl == "lk":
         if world == 1:
             from lora_kernel_b200.train.pipeline import Transformer, TrainingPipeline
             model = Transformer(cfg, "cuda", seed=tc.seed)
             return TrainingPipeline(model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
         from lora_kernel_b200.parallel.zero import Zero3Trainer
-        return Zero3Trainer(cfg, tc, device="cuda")
+        return Zero3Trainer(cfg, tc, device="cuda", fuse_gather=fuse_gather)
     if impl == "torch":
         from lora_kernel_b200.models.torch_llama import TorchBaselineTrainer
         return TorchBaselineTrainer(cfg, tc, device="cuda", world=world)
@@ -156,6 +156,8 @@ def main():
     ap.add_argument("--micro-batch", type=int, default=4)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0, help="override (testing only; invalid for the headline)")
+    ap.add_argument("--fuse-gather", action="store_true",
+                    help="ZeRO-3: gather each layer inside its first GEMM instead of prefetching it")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -178,7 +180,7 @@ def main():
 
     rank, world, local = dist_setup(args.gpus)
     torch.manual_seed(tc.seed + rank)
-    trainer = build_trainer(args.impl, cfg, tc, rank, world)
+    trainer = build_trainer(args.impl, cfg, tc, rank, world, fuse_gather=args.fuse_gather)
     B, S, V = tc.micro_batch, tc.seq_len, cfg.vocab_size
 
     # synthetic data: uniform token ids from a seeded generator, next-token targets

@@ -182,6 +182,53 @@ void gemm_ag(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
   check(lk_gemm(&d, stream()));
 }
 
+// K17: ZeRO-3 group gather fused into the first GEMM that consumes it.  `b`
+// is a view of `dst` (the local group buffer) at element `boff`.
+void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
+                 c10::optional<torch::Tensor> h, torch::Tensor src_ptrs, int64_t chunk, torch::Tensor dst,
+                 int64_t boff, int64_t rank, torch::Tensor count, torch::Tensor status, int64_t bn) {
+  const c10::cuda::CUDAGuard g(a.device());
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm_gather: K mismatch");
+  Operand A = classify(a, "a"), B = classify(b, "b");
+  TORCH_CHECK(!A.mn, "gemm_gather: A must be K-major");
+  need_contig(dst, "dst", torch::kBFloat16);
+  TORCH_CHECK(src_ptrs.is_cuda() && src_ptrs.scalar_type() == torch::kInt64, "gemm_gather: src_ptrs");
+  LkGemmDesc d{};
+  d.a = A.base; d.a_rows = A.rows; d.a_cols = A.cols; d.a_ld = A.ld; d.a_mn = A.mn;
+  d.b = B.base; d.b_rows = B.rows; d.b_cols = B.cols; d.b_ld = B.ld; d.b_mn = B.mn;
+  d.M = (int)a.size(0);
+  d.N = (int)b.size(0);
+  d.K = (int)a.size(1);
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.size(0) == d.M &&
+                  out.size(1) == d.N && out.stride(1) == 1,
+              "gemm_gather: out must be bf16 [M, N]");
+  d.d = out.data_ptr();
+  d.ldd = out.stride(0);
+  if (h.has_value()) {
+    need(*h, "h", torch::kBFloat16);
+    TORCH_CHECK(h->size(0) == d.M && h->size(1) == d.N / 2 && h->stride(1) == 1, "gemm_gather: h shape");
+    d.h = h->data_ptr();
+    d.ldh = h->stride(0);
+  }
+  d.alpha = 1.f;
+  d.epi = (int)epi;
+  d.bn = (int)bn;
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  need(count, "count", torch::kInt32);
+  TORCH_CHECK(count.numel() >= (d.N + 127) / 128, "gemm_gather: count too small");
+  d.comm_mode = 3;
+  d.ag_rank = (int)rank;
+  d.ag_world = (int)src_ptrs.numel();
+  d.gb_src = reinterpret_cast<const void* const*>(src_ptrs.data_ptr());
+  d.gb_chunk = chunk;
+  d.gb_len = dst.numel();
+  d.gb_boff = boff;
+  d.gb_dst = dst.data_ptr();
+  d.gb_count = count.data_ptr<int>();
+  check(lk_gemm(&d, stream()));
+}
+
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
 void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
             c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> y,
@@ -687,6 +734,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &gemm_rs);
   m.def("gemm_ag", &gemm_ag);
   m.def("rs_sum", &rs_sum);
+  m.def("gemm_gather", &gemm_gather);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);

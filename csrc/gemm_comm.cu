@@ -26,13 +26,28 @@ int gemm_dispatch_comm(const LkGemmDesc& g, cudaStream_t s) {
                "gemm_ag: M must be world * ag_rows with ag_rows % 128 == 0");
     if (g.epi == LK_EPI_SWIGLU) {
       LK_REQUIRE(!g.b_mn && g.N % 256 == 0 && g.h, "gemm_ag swiglu: K-major B, N % 256");
-      return launch_gemm<256, false, false, EPI_SWIGLU, true>(g, s);
+      return launch_gemm<256, false, false, EPI_SWIGLU, 1>(g, s);
     }
     LK_REQUIRE(g.epi == LK_EPI_BF16, "gemm_ag: bf16 or swiglu epilogue");
-    if (!g.b_mn) return bn == 128 ? launch_gemm<128, false, false, EPI_BF16, true>(g, s)
-                                  : launch_gemm<256, false, false, EPI_BF16, true>(g, s);
-    return bn == 128 ? launch_gemm<128, false, true, EPI_BF16, true>(g, s)
-                     : launch_gemm<256, false, true, EPI_BF16, true>(g, s);
+    if (!g.b_mn) return bn == 128 ? launch_gemm<128, false, false, EPI_BF16, 1>(g, s)
+                                  : launch_gemm<256, false, false, EPI_BF16, 1>(g, s);
+    return bn == 128 ? launch_gemm<128, false, true, EPI_BF16, 1>(g, s)
+                     : launch_gemm<256, false, true, EPI_BF16, 1>(g, s);
+  }
+  if (g.comm_mode == 3) {
+    LK_REQUIRE(g.gb_src && g.gb_count && g.gb_dst && g.gb_chunk > 0 && g.ag_world >= 1 &&
+                   g.gb_chunk * g.ag_world == g.gb_len && g.gb_chunk % 8 == 0,
+               "gemm_gather: group must be world equal chunks of 8-element multiples");
+    LK_REQUIRE(g.b == (const void*)((const uint8_t*)g.gb_dst + 2 * g.gb_boff), "gemm_gather: B must lie in gb_dst");
+    LK_REQUIRE(g.epi == LK_EPI_BF16 || g.epi == LK_EPI_SWIGLU, "gemm_gather: bf16 or swiglu epilogue");
+    if (g.epi == LK_EPI_SWIGLU) {
+      LK_REQUIRE(!g.b_mn && g.N % 256 == 0 && g.h, "gemm_gather swiglu: K-major B, N % 256");
+      return launch_gemm<256, false, false, EPI_SWIGLU, 2>(g, s);
+    }
+    if (!g.b_mn) return bn == 128 ? launch_gemm<128, false, false, EPI_BF16, 2>(g, s)
+                                  : launch_gemm<256, false, false, EPI_BF16, 2>(g, s);
+    return bn == 128 ? launch_gemm<128, false, true, EPI_BF16, 2>(g, s)
+                     : launch_gemm<256, false, true, EPI_BF16, 2>(g, s);
   }
   return fail("gemm: unknown comm_mode");
 }

@@ -68,7 +68,18 @@ struct GemmArgs {
   uint8_t* ag_dst;
   int ag_rows, ag_rank, ag_world, ag_row_bytes;
   int* ag_count;
+  // K17 gather of a flat parameter group on first use (ZeRO-3): rank p owns
+  // group elements [p*gb_chunk, (p+1)*gb_chunk) at gb_src[p] (bf16); the copy
+  // warps assemble the whole group (gb_len elements) at gb_dst, B being the
+  // [N, K] tensor at element gb_boff of it.  gb_count[tn] counts the copied
+  // GB_PIECE-element pieces that overlap N-tile tn's part of B.
+  const uint8_t* const* gb_src;
+  int64_t gb_chunk, gb_len, gb_boff;
+  uint8_t* gb_dst;
+  int* gb_count;
 };
+
+constexpr int64_t GB_PIECE = 8192;  // elements per K17 copy piece (16 KB)
 
 constexpr int AG_SUB = 16;  // rows per copy piece
 
@@ -151,17 +162,18 @@ __device__ __forceinline__ void ag_copy_warp(const GemmArgs& a, int cw, int ncw,
   }
 }
 
-// Producer side of K16: wait (bounded) until the 128-row chunk of M-tile tm is in place.
-__device__ __forceinline__ bool ag_wait_chunk(const GemmArgs& a, int tm, volatile int* abort_flag) {
-  const int* cnt = a.ag_count + tm;
-  if (ld_acquire_gpu(cnt) >= 128 / AG_SUB) {
+// Producer side of K16/K17: wait (bounded) until *cnt reaches target, then
+// order the async-proxy (TMA) reads after the copies it counts.
+__device__ __forceinline__ bool wait_count(const GemmArgs& a, const int* cnt, int target,
+                                           volatile int* abort_flag) {
+  if (ld_acquire_gpu(cnt) >= target) {
     fence_proxy_async_global();
     return true;
   }
   const uint64_t t0 = globaltimer();
   while (true) {
     for (int i = 0; i < 64; ++i) {
-      if (ld_acquire_gpu(cnt) >= 128 / AG_SUB) {
+      if (ld_acquire_gpu(cnt) >= target) {
         fence_proxy_async_global();
         return true;
       }
@@ -176,7 +188,83 @@ __device__ __forceinline__ bool ag_wait_chunk(const GemmArgs& a, int tm, volatil
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool AG = false>
+// K17: the part of the group that N-tile tn of B reads: [lo, hi) elements.
+// K-major B reads rows [tn*BN, (tn+1)*BN); MN-major B reads every row.
+template <int BN, bool B_MN>
+__device__ __forceinline__ void gb_tile_range(const GemmArgs& a, int tn, int64_t& lo, int64_t& hi) {
+  const int64_t nk = (int64_t)a.N * a.K;
+  if (B_MN) {
+    lo = a.gb_boff;
+    hi = a.gb_boff + nk;
+  } else {
+    lo = a.gb_boff + (int64_t)tn * BN * a.K;
+    hi = a.gb_boff + min((int64_t)(tn + 1) * BN * a.K, nk);
+  }
+}
+
+// K17 copy warps: pieces of the group in order - B's pieces first (each rank
+// starting at a different one so the owners' links share the load), then the
+// rest.  A piece may straddle two owners' chunks.
+template <int BN, bool B_MN>
+__device__ __forceinline__ void gb_copy_warp(const GemmArgs& a, int cw, int ncw, int lane, int rank,
+                                             int world) {
+  const int64_t npieces = (a.gb_len + GB_PIECE - 1) / GB_PIECE;
+  const int64_t pb0 = a.gb_boff / GB_PIECE;
+  const int64_t pb1 = (a.gb_boff + (int64_t)a.N * a.K - 1) / GB_PIECE;
+  const int64_t nb = pb1 - pb0 + 1;
+  const int64_t rot = nb * rank / world;
+  for (int64_t s = cw; s < npieces; s += ncw) {
+    int64_t piece;
+    if (s < nb) {
+      piece = pb0 + (s + rot) % nb;
+    } else {
+      const int64_t k = s - nb;
+      piece = k < pb0 ? k : k + nb;
+    }
+    const int64_t a0 = piece * GB_PIECE;
+    const int64_t a1 = min(a0 + GB_PIECE, a.gb_len);
+    int64_t e = a0;
+    while (e < a1) {
+      const int64_t p = e / a.gb_chunk;
+      const int64_t seg_end = min(a1, (p + 1) * a.gb_chunk);
+      const uint4* src = reinterpret_cast<const uint4*>(a.gb_src[p] + (e - p * a.gb_chunk) * 2);
+      uint4* dst = reinterpret_cast<uint4*>(a.gb_dst + e * 2);
+      const int units = (int)((seg_end - e) / 8);
+#pragma unroll 1
+      for (int c0 = lane; c0 < units; c0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (c0 + 32 * k < units) v[k] = src[c0 + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (c0 + 32 * k < units) dst[c0 + 32 * k] = v[k];
+      }
+      e = seg_end;
+    }
+    fence_proxy_async_global();
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+      // count this piece for every N-tile whose part of B it overlaps
+      const int tiles_n = (a.N + BN - 1) / BN;
+      for (int tn = 0; tn < tiles_n; ++tn) {
+        int64_t lo, hi;
+        gb_tile_range<BN, B_MN>(a, tn, lo, hi);
+        if (a0 < hi && a1 > lo) atomicAdd(a.gb_count + tn, 1);
+      }
+    }
+  }
+}
+
+template <int BN, bool B_MN>
+__device__ __forceinline__ int gb_expected(const GemmArgs& a, int tn) {
+  int64_t lo, hi;
+  gb_tile_range<BN, B_MN>(a, tn, lo, hi);
+  return (int)((hi - 1) / GB_PIECE - lo / GB_PIECE + 1);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0>
 __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -238,8 +326,13 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
         int tm, tn;
         gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
         tm = (tm + args.m_rot) % args.tiles_m;
-        if constexpr (AG) {
-          if (!ag_wait_chunk(args, tm, abort_flag)) {
+        if constexpr (AG == 1) {
+          if (!wait_count(args, args.ag_count + tm, 128 / AG_SUB, abort_flag)) {
+            ok = false;
+            break;
+          }
+        } else if constexpr (AG == 2) {
+          if (!wait_count(args, args.gb_count + tn, gb_expected<BN, B_MN>(args, tn), abort_flag)) {
             ok = false;
             break;
           }
@@ -336,7 +429,11 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
     }
   } else if (AG && warp >= 6) {
     // ------------------------------------------------------ K16 copy warps
-    ag_copy_warp(args, (warp - 6) * gridDim.x + blockIdx.x, AG_WARPS * gridDim.x, lane);
+    if constexpr (AG == 1)
+      ag_copy_warp(args, (warp - 6) * gridDim.x + blockIdx.x, AG_WARPS * gridDim.x, lane);
+    else
+      gb_copy_warp<BN, B_MN>(args, (warp - 6) * gridDim.x + blockIdx.x, AG_WARPS * gridDim.x, lane,
+                             args.ag_rank, args.ag_world);
   } else {
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -502,7 +599,7 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool AG = false>
+template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0>
 int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   GemmArgs args{};
@@ -544,6 +641,12 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   args.ag_world = g.ag_world;
   args.ag_row_bytes = (int)(g.a_cols * 2);
   args.ag_count = g.ag_count;
+  args.gb_src = reinterpret_cast<const uint8_t* const*>(g.gb_src);
+  args.gb_chunk = g.gb_chunk;
+  args.gb_len = g.gb_len;
+  args.gb_boff = g.gb_boff;
+  args.gb_dst = reinterpret_cast<uint8_t*>(g.gb_dst);
+  args.gb_count = g.gb_count;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, AG>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
@@ -555,10 +658,11 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   }
   const int tiles = args.tiles_m * args.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  if constexpr (AG) {
-    // CTAs wait on rows copied by other CTAs: they must all be resident
-    if (cudaMemsetAsync(g.ag_count, 0, sizeof(int) * args.tiles_m, stream) != cudaSuccess)
-      return fail("gemm_ag: memset failed");
+  if constexpr (AG != 0) {
+    // CTAs wait on data copied by other CTAs: they must all be resident
+    int* cnt = AG == 1 ? g.ag_count : g.gb_count;
+    const int ncnt = AG == 1 ? args.tiles_m : args.tiles_n;
+    if (cudaMemsetAsync(cnt, 0, sizeof(int) * ncnt, stream) != cudaSuccess) return fail("gemm_ag: memset failed");
     void* params[] = {&ta, &tb, &ta2, &tb2, &args};
     cudaError_t e = cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(GEMM_THREADS + 32 * AG_WARPS), params,
                                                 SMEM, stream);

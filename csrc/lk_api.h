@@ -72,6 +72,16 @@ typedef struct LkGemmDesc {
   int64_t ag_ld_src;
   int ag_rows, ag_rank, ag_world;
   int* ag_count;
+  // 3 = K17 ZeRO-3 group gather -> GEMM: the flat parameter group (gb_len
+  // elements, bf16) is assembled at gb_dst from the owners' chunks gb_src[p]
+  // (DEVICE array of `ag_world` pointers, gb_chunk elements each) by the GEMM's
+  // copy warps; B must be the [N, K] view at element gb_boff of gb_dst.
+  // gb_count: int scratch [ceil(N / 128)] zeroed by the launcher.  ag_rank
+  // rotates the copy order.
+  const void* const* gb_src;
+  int64_t gb_chunk, gb_len, gb_boff;
+  void* gb_dst;
+  int* gb_count;
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);

@@ -91,6 +91,9 @@ class LlamaModel:
         self.hooks = None  # optional: pre_forward / pre_layer_fwd(i) / pre_layer_bwd(i) /
         #                    post_layer_bwd(i) / post_head_bwd / post_backward (ZeRO-3)
         self._overwrite = False
+        # optional (layer, target, fn): the next _lin / _lin_bwd of that linear runs
+        # fn(a, b, out) instead of the plain GEMM (ZeRO-3 gather fused into it, K17)
+        self.fused_gather = None
         self.lora = None        # optional LoRAAdapters (models/lora.py)
         self.train_base = True  # False: frozen base weights (no base weight gradients)
         self._u: Dict[Tuple[int, str], torch.Tensor] = {}
@@ -139,7 +142,18 @@ class LlamaModel:
         G.gemm(x, self.lora.A(i, t), u, alpha=self.lora.lc.scale)
         return u
 
+    def _take_fused(self, i: int, t: str):
+        fg = self.fused_gather
+        if fg is not None and fg[0] == i and fg[1] == t:
+            self.fused_gather = None
+            return fg[2]
+        return None
+
     def _lin(self, i: int, t: str, x, out, residual=None, save: bool = True):
+        fn = self._take_fused(i, t) if residual is None else None
+        if fn is not None:
+            fn(x, self._p(f"layers.{i}.{t}"), out)
+            return out
         u = self._lora_u(i, t, x, save)
         B = self.lora.B(i, t) if u is not None else None
         G.gemm(x, self._p(f"layers.{i}.{t}"), out, epi="bf16_resid" if residual is not None else "bf16",
@@ -163,7 +177,11 @@ class LlamaModel:
             G.gemm(v.t(), x.t(), self.lora.gA(i, t), epi=acc)               # dA = (s v)^T x
             G.gemm(dy.t(), self._u[(i, t)].t(), self.lora.gB(i, t), epi=acc)  # dB = dy^T (s u)
         else:
-            G.linear_dgrad(dy, self._p(name), out=dx_out)
+            fn = self._take_fused(i, t)
+            if fn is not None:
+                fn(dy, self._p(name).t(), dx_out)
+            else:
+                G.linear_dgrad(dy, self._p(name), out=dx_out)
         self._wgrad(dy, x, name)
 
     # -------------------------------------------------------------- forward

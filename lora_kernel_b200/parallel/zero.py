@@ -40,7 +40,9 @@ from typing import Dict, List, Optional, Tuple
 import torch
 import torch.distributed as dist
 
+from .._ext import C, status
 from ..config import TrainConfig, TransformerConfig
+from ..ops.gemm import EPI
 from ..models.llama import LlamaModel
 from ..models.params import FlatParams, build_layout
 from ..train.optimizer import FusedAdamW
@@ -110,6 +112,7 @@ class _SlotParams:
         self.by_name = {s.name: s for s in layout.specs}
         self.cur: Dict[str, torch.Tensor] = {}
         self._views: Dict[Tuple[int, str], torch.Tensor] = {}
+        self.override: Dict[str, torch.Tensor] = {}  # name -> tensor read elsewhere (peer memory)
 
     def bind(self, group: str, buf: torch.Tensor) -> None:
         self.cur[group] = buf
@@ -117,6 +120,9 @@ class _SlotParams:
     def __getitem__(self, name: str) -> torch.Tensor:
         if name == "lm_head" and self.L.cfg.tie_embeddings:
             name = "embed"
+        ov = self.override.get(name) if self.override else None
+        if ov is not None:
+            return ov
         sp = self.by_name[name]
         buf = self.cur[sp.group]
         key = (buf.data_ptr(), name)
@@ -129,14 +135,21 @@ class _SlotParams:
 
 
 class Zero3Trainer:
+    """fuse_gather (p2p only): instead of prefetching layer i+1's group on a
+    side stream, gather each layer's group inside the first GEMM that needs
+    it (K17: the QKV projection in the forward, the Wdown dgrad in the
+    backward); the layer's first RMSNorm reads its weight straight from the
+    owner's shard in peer memory."""
+
     def __init__(self, cfg: TransformerConfig, tc: TrainConfig, device="cuda", group=None,
-                 comm: str = "p2p"):
+                 comm: str = "p2p", fuse_gather: bool = False):
         self.cfg, self.tc = cfg, tc
         self.device = torch.device(device)
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self.mode = comm
+        self.fuse_gather = fuse_gather and comm == "p2p"
         L = self.L = ShardLayout(cfg, self.world, self.rank)
         bf, f32 = torch.bfloat16, torch.float32
 
@@ -180,6 +193,8 @@ class Zero3Trainer:
         self.params.bind("embed", self.buf["embed"])
         self.params.bind("head", self.buf["head"])
 
+        self.gb_count = torch.zeros((max(cfg.qkv_dim, cfg.hidden_dim, cfg.ff_dim_padded) + 127) // 128,
+                                    dtype=torch.int32, device=self.device)
         self.engine = LlamaModel(cfg, self.device, params=self.params, with_grads=False)
         self.engine.grads = FlatParams(cfg, self.device, f32, buffer=grads_flat, group_align=L.align)
         self.engine.hooks = self
@@ -256,11 +271,54 @@ class Zero3Trainer:
             self._gather("embed", self.buf["embed"])
             self._gather("head", self.buf["head"])
         ev = self._on_comm(initial)
-        for i in range(min(len(self.slots), self.cfg.num_layers)):
-            self._prefetch_layer(i)
+        if not self.fuse_gather:
+            for i in range(min(len(self.slots), self.cfg.num_layers)):
+                self._prefetch_layer(i)
         torch.cuda.current_stream().wait_event(ev)
 
+    # ------------------------------------------------ K17 fused gather
+    def _peer_view(self, name: str) -> Optional[torch.Tensor]:
+        """The owner's copy of a small tensor that lies inside one rank's chunk."""
+        sp = self.params.by_name[name]
+        g = sp.group
+        gs, _ = self.L.groups[g]
+        ch = self.L.chunk[g]
+        o = sp.offset - gs
+        owner = o // ch
+        if (o + sp.numel - 1) // ch != owner:
+            return None
+        off = self.L.shard_off[g] + o - owner * ch
+        return self.shard_sym.handle.get_buffer(owner, (sp.numel,), torch.bfloat16, off).view(sp.shape)
+
+    def _arm_fused(self, i: int, target: str, transpose: bool) -> None:
+        g = f"layers.{i}"
+        s = i % len(self.slots)
+        gs, ge = self.L.groups[g]
+        slot = self.slots[s][:ge - gs]
+        self.slot_layer[s] = i
+        self.params.bind(g, self.slots[s])
+        sp = self.params.by_name[f"{g}.{target}"]
+        src = self.shard_sym.ptrs_at(self.L.shard_off[g])
+        boff = sp.offset - gs
+        chunk, rank = self.L.chunk[g], self.rank
+        st = status(self.device)
+
+        def fn(a, b, out):
+            C().gemm_gather(a, b, out, EPI["bf16"], None, src, chunk, slot, boff, rank, self.gb_count, st, 0)
+        self.engine.fused_gather = (i, target, fn)
+
     def pre_layer_fwd(self, i):
+        if self.fuse_gather:
+            name = f"layers.{i}.attn_norm"
+            pv = self._peer_view(name)
+            if pv is not None:
+                self.params.override = {name: pv}
+                self._arm_fused(i, "wqkv", False)
+                return
+            self.params.override = {}
+            self._prefetch_layer(i)
+            self._use_layer(i)
+            return
         self._use_layer(i)
         self._prefetch_layer(i + 1)
 
@@ -269,6 +327,13 @@ class Zero3Trainer:
             self._on_comm(self._reduce_scatter, "head", self.L.names.index("head"))
 
     def pre_layer_bwd(self, i):
+        if self.fuse_gather:
+            self.params.override = {}
+            if self.slot_layer[i % len(self.slots)] == i:
+                self.params.bind(f"layers.{i}", self.slots[i % len(self.slots)])
+            else:
+                self._arm_fused(i, "wdown", True)
+            return
         if self.slot_layer[i % len(self.slots)] != i:
             self._prefetch_layer(i)
         self._use_layer(i)

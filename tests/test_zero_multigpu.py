@@ -38,7 +38,7 @@ def _single_gpu_reference(world):
     return out, losses, L, ref
 
 
-@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+@pytest.mark.parametrize("mode", ["p2p", "nccl", "p2p-fused"])
 def test_zero3_matches_single_gpu(mode, tmp_path):
     n = torch.cuda.device_count()
     if n < 2:
