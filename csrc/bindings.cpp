@@ -232,7 +232,8 @@ void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t ep
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
 void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
             c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> y,
-            c10::optional<torch::Tensor> rstd, double eps) {
+            c10::optional<torch::Tensor> rstd, double eps, int64_t src_mode,
+            c10::optional<torch::Tensor> peers, int64_t mc) {
   const c10::cuda::CUDAGuard g(recv.device());
   need(recv, "recv", torch::kBFloat16);
   need(out, "out", torch::kBFloat16);
@@ -243,7 +244,16 @@ void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<
   d.world = (int)world;
   d.rows = (int)out.size(0);
   d.cols = (int)out.size(1);
-  TORCH_CHECK(recv.size(0) >= world * d.rows && recv.size(1) >= d.cols, "rs_sum: recv shape");
+  TORCH_CHECK(recv.size(0) >= (src_mode == 0 ? world : 1) * d.rows && recv.size(1) >= d.cols, "rs_sum: recv shape");
+  d.src_mode = (int)src_mode;
+  if (src_mode == 1) {
+    TORCH_CHECK(peers.has_value() && peers->is_cuda() && peers->scalar_type() == torch::kInt64 &&
+                    peers->numel() == world, "rs_sum: peers must be an int64 device array of world pointers");
+    d.peers = reinterpret_cast<const void* const*>(peers->data_ptr());
+  } else if (src_mode == 2) {
+    TORCH_CHECK(mc != 0, "rs_sum: multicast address needed");
+    d.mc = reinterpret_cast<const void*>(mc);
+  }
   d.out = out.data_ptr();
   d.ld_out = out.stride(0);
   if (resid.has_value()) {
@@ -689,14 +699,14 @@ void kv_gather(torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch
 }
 
 void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, int64_t seed, torch::Tensor out_tok,
-            c10::optional<torch::Tensor> out_val) {
+            c10::optional<torch::Tensor> out_val, int64_t v0) {
   const c10::cuda::CUDAGuard g(logits.device());
   need(logits, "logits", torch::kBFloat16);
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits must be row-major 2-D");
   need_contig(out_tok, "out_tok", torch::kInt64);
-  check(lk_sample(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
-                  optp<float>(temperature), (uint64_t)seed, out_tok.data_ptr<int64_t>(), optp<float>(out_val),
-                  stream()));
+  check(lk_sample_vp(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1), v0,
+                     optp<float>(temperature), (uint64_t)seed, out_tok.data_ptr<int64_t>(), optp<float>(out_val),
+                     stream()));
 }
 
 void quantize(int64_t fmt, torch::Tensor w, int64_t group, torch::Tensor q, torch::Tensor scale,

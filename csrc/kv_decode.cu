@@ -275,7 +275,7 @@ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
 
 __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V,
                               const float* __restrict__ temperature, uint64_t seed,
-                              int64_t* __restrict__ out_tok, float* __restrict__ out_val) {
+                              int64_t* __restrict__ out_tok, float* __restrict__ out_val, int64_t v0) {
   const int row = blockIdx.x;
   const float temp = temperature ? temperature[row] : 0.f;
   const __nv_bfloat16* z = logits + (int64_t)row * ld;
@@ -285,7 +285,7 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
     float v = __bfloat162float(z[j]);
     if (temp > 0.f) {
       const uint32_t h = mix32((uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U) ^
-                               mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
+                               mix32((uint32_t)(j + v0) * 0x85ebca6bU + 0x1234567U));
       const float u = ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
       v = v / temp - logf(-logf(u));
     }
@@ -317,7 +317,7 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
         best = sb[k];
         bi = si[k];
       }
-    out_tok[row] = bi;
+    out_tok[row] = bi + v0;
     if (out_val) out_val[row] = best;
   }
 }
@@ -425,7 +425,18 @@ extern "C" int lk_kv_gather(const void* k_cache, const void* v_cache, const floa
 
 extern "C" int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
                          uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s) {
+  return lk_sample_vp(logits, ld, rows, V, 0, temperature, seed, out_tok, out_val, s);
+}
+
+// Vocabulary-parallel form: the logits hold columns [v0, v0 + V) of the
+// vocabulary; tokens come back as global ids and the Gumbel noise is drawn for
+// the global id, so the best (value, id) over every rank's slice is exactly
+// the single-GPU sample.
+extern "C" int lk_sample_vp(const void* logits, int64_t ld, int rows, int V, int64_t v0,
+                            const float* temperature, uint64_t seed, int64_t* out_tok, float* out_val,
+                            cudaStream_t s) {
   if (rows == 0) return 0;
-  sample_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, seed, out_tok, out_val);
+  sample_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, seed, out_tok, out_val,
+                                     v0);
   return check_launch("sample");
 }

@@ -150,6 +150,13 @@ typedef struct LkRsSumDesc {
   int64_t ld_y;
   float* rstd;
   float eps;
+  // Source of the partial sums (the RMSNorm form only): 0 = `world` slots of
+  // recv (K18 owner side); 1 = all-reduce: row r of every rank's own partial
+  // buffer peers[s] (DEVICE array of `world` pointers, pitch ld_recv); 2 =
+  // all-reduce through the buffer's NVLS multicast address `mc`.
+  int src_mode;
+  const void* const* peers;
+  const void* mc;
 } LkRsSumDesc;
 int lk_rs_sum(const LkRsSumDesc* d, cudaStream_t s);
 
@@ -302,6 +309,8 @@ int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale,
                  cudaStream_t s);
 int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
               uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s);
+int lk_sample_vp(const void* logits, int64_t ld, int rows, int V, int64_t v0, const float* temperature,
+                 uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s);
 
 // ------------------------------------------------------ K14 quantised weights
 enum LkQuantFmt { LK_Q_INT8 = 0, LK_Q_FP8 = 1, LK_Q_INT4 = 2 };

@@ -20,7 +20,30 @@
 
 namespace lk {
 
-template <int VPT, bool NORM>
+// Sum of 8 bf16 over every rank, reduced inside the NVSwitch (fp32 accumulation).
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void acc_bf16x8(float* v, uint4 a) {
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = unpack_bf16x2(aw[e]);
+    v[2 * e] += f.x;
+    v[2 * e + 1] += f.y;
+  }
+}
+
+// SRC 0: the owner's receive slots (K18); 1: every rank's own partial, read
+// from peer memory in fixed rank order (all-reduce, every rank sums every
+// row); 2: the same through the multicast address (NVLS ld_reduce).
+template <int VPT, bool NORM, int SRC>
 __global__ void __launch_bounds__(256) rs_sum_norm_kernel(LkRsSumDesc d) {
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -31,18 +54,18 @@ __global__ void __launch_bounds__(256) rs_sum_norm_kernel(LkRsSumDesc d) {
     for (int i = 0; i < VPT; ++i)
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
-    for (int s = 0; s < d.world; ++s) {
-      const uint4* src = reinterpret_cast<const uint4*>(recv + ((int64_t)s * d.rows + row) * d.ld_recv);
+    if constexpr (SRC == 2) {
+      const __nv_bfloat16* mc = reinterpret_cast<const __nv_bfloat16*>(d.mc) + (int64_t)row * d.ld_recv;
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const uint4 a = src[i * 32 + lane];
-        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      for (int i = 0; i < VPT; ++i) acc_bf16x8(v[i], mm_ld_reduce_bf16x8(mc + 8 * (i * 32 + lane)));
+    } else {
+      for (int s = 0; s < d.world; ++s) {
+        const __nv_bfloat16* base =
+            SRC == 1 ? reinterpret_cast<const __nv_bfloat16*>(d.peers[s]) + (int64_t)row * d.ld_recv
+                     : recv + ((int64_t)s * d.rows + row) * d.ld_recv;
+        const uint4* src = reinterpret_cast<const uint4*>(base);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16x2(aw[e]);
-          v[i][2 * e] += f.x;
-          v[i][2 * e + 1] += f.y;
-        }
+        for (int i = 0; i < VPT; ++i) acc_bf16x8(v[i], src[i * 32 + lane]);
       }
     }
     float ss = 0.f;
@@ -147,11 +170,15 @@ extern "C" int lk_rs_sum(const LkRsSumDesc* d, cudaStream_t s) {
     return check_launch("rs_sum");
   }
   LK_REQUIRE(d->y && d->cols % 256 == 0 && d->ld_y % 8 == 0, "rs_sum+norm: cols % 256 and y needed");
+  LK_REQUIRE(d->src_mode == 0 || (d->src_mode == 1 && d->peers) || (d->src_mode == 2 && d->mc),
+             "rs_sum+norm: source pointers missing");
   const int grid = (int)std::min<int64_t>((d->rows + 7) / 8, 4 * num_sms());
   switch (d->cols / 256) {
-#define LK_RS_CASE(V)                                      \
-  case V:                                                  \
-    rs_sum_norm_kernel<V, true><<<grid, 256, 0, s>>>(*d); \
+#define LK_RS_CASE(V)                                                                    \
+  case V:                                                                                \
+    if (d->src_mode == 0) rs_sum_norm_kernel<V, true, 0><<<grid, 256, 0, s>>>(*d);       \
+    else if (d->src_mode == 1) rs_sum_norm_kernel<V, true, 1><<<grid, 256, 0, s>>>(*d);  \
+    else rs_sum_norm_kernel<V, true, 2><<<grid, 256, 0, s>>>(*d);                        \
     break;
     LK_RS_CASE(1)
     LK_RS_CASE(2)

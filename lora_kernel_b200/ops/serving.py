@@ -58,11 +58,14 @@ def decode_attention(q: torch.Tensor, k_cache, v_cache, k_scale, v_scale, block_
     return out
 
 
-def sample(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None, seed: int = 0) -> torch.Tensor:
-    """Greedy (temperature 0 / None) or exact temperature sampling (Gumbel-max)."""
+def sample(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None, seed: int = 0, *,
+           v0: int = 0, out_val: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy (temperature 0 / None) or exact temperature sampling (Gumbel-max).
+    v0: vocabulary id of column 0 (a vocabulary-parallel slice); out_val
+    receives each row's winning (noised) score for the cross-rank pick."""
     require_device(logits)
     tok = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
-    C().sample(logits, temperature, int(seed) & ((1 << 63) - 1), tok, None)
+    C().sample(logits, temperature, int(seed) & ((1 << 63) - 1), tok, out_val, int(v0))
     return tok
 
 

@@ -277,7 +277,7 @@ class TPComm:
         R, Nc = out.shape
         self.barrier()
         world = 1 if self.comm == "nccl" else self.tp
-        C().rs_sum(self.recv_view(k, R, Nc), world, out, resid, gamma, y, rstd, float(eps))
+        C().rs_sum(self.recv_view(k, R, Nc), world, out, resid, gamma, y, rstd, float(eps), 0, None, 0)
 
     def _tmp(self, shape) -> torch.Tensor:
         t = self._nccl_tmp.get(shape)

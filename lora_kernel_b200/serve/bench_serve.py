@@ -8,9 +8,10 @@ token ids.
 
     python -m lora_kernel_b200.serve.bench_serve [--num-requests 200 --rate 20 ...]
 
-The engine runs in-process on one GPU (tensor parallelism is not used by this
-driver); requests are injected at their arrival times and the engine steps
-continuously.  Reported: output tok/s = generated tokens / (last completion -
+Launched plainly it runs on one GPU.  Under torchrun with N processes it
+serves with tensor parallelism N (serve.tp_runner): rank 0 runs the engine
+and the clock, every rank runs its weight / KV-head shard.  Requests are
+injected at their arrival times and the engine steps continuously.  Reported: output tok/s = generated tokens / (last completion -
 first arrival), TTFT percentiles (arrival -> first token), inter-token latency,
 request throughput and the prefix-cache hit rate.  One JSON line.
 """
@@ -42,6 +43,8 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
 
+    import os
+
     from ..config import get_preset
     from ..models.params import FlatParams
     from .engine import LLMEngine, SamplingParams
@@ -55,10 +58,30 @@ def main(argv=None):
     sc.max_model_len = max(sc.max_model_len, a.prompt_max + a.output_len + 16)
     weights = a.weights or rc.quant.weights
     kv = a.kv or rc.quant.kv_cache
-    params = FlatParams(cfg, "cuda")
-    params.init_(a.seed, cfg.init_std)
-    eng = LLMEngine(cfg, params, sc, kv_dtype=kv, weights=weights, group_size=rc.quant.group_size)
-    del params
+    tp = int(os.environ.get("WORLD_SIZE", "1"))
+    proxy = None
+    if tp > 1:
+        from ..parallel.comm import init_distributed
+        from .tp_runner import RunnerProxy, build_tp_runner, worker_loop
+        rank, _, _ = init_distributed("nccl", timeout_s=600)
+        runner, ctrl = build_tp_runner(cfg, a.seed, weights=weights, kv_dtype=kv,
+                                       group_size=rc.quant.group_size, block_size=sc.block_size,
+                                       max_model_len=sc.max_model_len,
+                                       max_rows=max(sc.max_num_batched_tokens, sc.max_num_seqs))
+        torch.cuda.synchronize()
+        if rank != 0:
+            worker_loop(runner, ctrl)
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+            return None
+        proxy = RunnerProxy(runner, ctrl)
+        eng = LLMEngine(cfg, None, sc, kv_dtype=kv, weights=weights, runner=proxy)
+    else:
+        params = FlatParams(cfg, "cuda")
+        params.init_(a.seed, cfg.init_std)
+        eng = LLMEngine(cfg, params, sc, kv_dtype=kv, weights=weights, group_size=rc.quant.group_size)
+        del params
     torch.cuda.synchronize()
 
     rng = np.random.default_rng(a.seed)
@@ -111,15 +134,20 @@ def main(argv=None):
         "num_requests": a.num_requests, "rate": a.rate, "output_len": a.output_len,
         "prefix_cache_hit_rate": round(eng.blocks.stats.hit_rate, 3),
         "preemptions": eng.stats["preemptions"],
-        "n_gpus": 1,
+        "n_gpus": tp,
         "config": {"model": f"Llama-style 8B ({cfg.num_layers} layers)", "weights": weights, "kv_cache": kv,
                    "max_num_seqs": sc.max_num_seqs, "prompts": f"uniform [{a.prompt_min},{a.prompt_max}]",
-                   "shared_prefix": f"{a.shared_frac:.0%} x {a.shared_len}", "parallelism": "tp1"},
+                   "shared_prefix": f"{a.shared_frac:.0%} x {a.shared_len}", "parallelism": f"tp{tp}"},
         "data": "synthetic (random token ids, random-init weights)",
         "wall_s": round(t_end - t0, 2),
         "kv_blocks": eng.runner.num_blocks, "weight_gb": round(eng.runner.weight_bytes() / 1e9, 2),
     }
     print(json.dumps(res), flush=True)
+    if proxy is not None:
+        proxy.stop()
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
     return res
 
 

@@ -73,12 +73,15 @@ class Request:
 class LLMEngine:
     def __init__(self, cfg: TransformerConfig, params: FlatParams, serve: Optional[ServeConfig] = None, *,
                  device="cuda", kv_dtype: str = "fp8", weights: str = "none", group_size: int = 128,
-                 clock: Callable[[], float] = time.perf_counter):
+                 clock: Callable[[], float] = time.perf_counter, runner=None):
+        """runner: an already built runner (e.g. the tensor-parallel
+        serve.tp_runner.RunnerProxy on rank 0); params is then unused."""
         self.cfg = cfg
         self.sc = serve or ServeConfig()
-        self.runner = ModelRunner(cfg, params, device, kv_dtype=kv_dtype, weights=weights,
-                                  group_size=group_size, num_blocks=self.sc.num_kv_blocks,
-                                  block_size=self.sc.block_size, max_model_len=self.sc.max_model_len)
+        self.runner = runner if runner is not None else ModelRunner(
+            cfg, params, device, kv_dtype=kv_dtype, weights=weights, group_size=group_size,
+            num_blocks=self.sc.num_kv_blocks, block_size=self.sc.block_size,
+            max_model_len=self.sc.max_model_len)
         self.blocks = BlockManager(self.runner.num_blocks, self.sc.block_size,
                                    self.sc.enable_prefix_caching)
         self.waiting: deque = deque()
@@ -188,11 +191,10 @@ class LLMEngine:
     def _sample(self, reqs: List[Request], logits: torch.Tensor) -> List[int]:
         temps = [r.params.temperature for r in reqs]
         if all(t <= 0 for t in temps):
-            tok = SV.sample(logits)
+            tok = self.runner.sample(logits, None, 0)
         else:
-            t = torch.tensor(temps, dtype=torch.float32, device=logits.device)
             self._seed += 1
-            tok = SV.sample(logits, t, self._seed)
+            tok = self.runner.sample(logits, temps, self._seed)
         return tok.tolist()
 
     def step(self) -> List[Request]:

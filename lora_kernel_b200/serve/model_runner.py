@@ -144,6 +144,11 @@ class ModelRunner:
         xf, _, _ = N.rmsnorm_fwd(h_last, self.W["final_norm"], self.cfg.norm_eps)
         return G.linear(xf, self.W["lm_head"])
 
+    def sample(self, logits: torch.Tensor, temps: Optional[List[float]], seed: int) -> torch.Tensor:
+        """Next token per row (K19): greedy when temps is None, else Gumbel-max."""
+        t = None if temps is None else torch.tensor(temps, dtype=torch.float32, device=logits.device)
+        return SV.sample(logits, t, seed)
+
     # -------------------------------------------------------------- prefill
     @torch.no_grad()
     def prefill(self, items: List[PrefillItem]) -> Tuple[List[int], torch.Tensor]:

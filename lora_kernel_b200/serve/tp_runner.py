@@ -1,0 +1,219 @@
+"""Tensor-parallel serving: one process per GPU, Megatron column/row split.
+
+Every rank holds its shard of the weights (query/KV heads, FFN blocks and
+vocabulary rows, optionally int4/int8/fp8 quantised) and the KV cache of its
+own KV heads.  Activations between the linears are replicated: after each
+row-parallel linear (Wo, Wdown) every rank has a partial [rows, D]; one kernel
+then sums the partials of all ranks - through the NVLS multicast address
+(multimem.ld_reduce, reduced inside the NVSwitch) or by peer loads in fixed
+rank order - and fuses the residual add and the next RMSNorm (csrc/tp.cu).
+The LM head is vocabulary-parallel: each rank samples over its slice with the
+Gumbel noise of the global token id (K19) and the best (score, id) across
+ranks is the exact single-GPU sample.
+
+Scheduling runs on rank 0 only (the LLMEngine with a `RunnerProxy`); each
+runner call is broadcast over a CPU (gloo) group to the other ranks, whose
+`worker_loop` executes the same call on their shard, so every rank launches
+the same kernels in the same order.
+
+Reference: the reference serves from one process without tensor parallelism
+(include/serving/*, SURVEY call stack 3.4); its TP layers
+(include/distributed/tensor_parallel.hpp:14-104) are forward-only matmul
+splits with an all-reduce.
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .._ext import C
+from ..config import TransformerConfig
+from ..ops import elementwise as E
+from ..ops import norm as N
+from ..ops import serving as SV
+from ..parallel import comm as CM
+from .model_runner import ModelRunner, PrefillItem
+
+SLOT_SERVE = 6
+
+
+class TPServeComm:
+    """Two alternating symmetric partial buffers + the fused all-reduce/norm."""
+
+    def __init__(self, hidden: int, max_rows: int, device, group=None):
+        self.group = group or dist.group.WORLD
+        self.tp = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.device = torch.device(device)
+        self.D, self.max_rows = hidden, max_rows
+        self.pc = CM.PeerComm(self.device, self.group)
+        self.part = [CM.SymBuffer(max_rows * hidden, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.k = 0
+
+    def partial(self, rows: int) -> torch.Tensor:
+        if rows > self.max_rows:
+            raise ValueError(f"{rows} rows exceed the TP partial buffers ({self.max_rows})")
+        return self.part[self.k].local[:rows * self.D].view(rows, self.D)
+
+    def allreduce_norm(self, rows: int, out: torch.Tensor, resid: torch.Tensor, gamma: torch.Tensor,
+                       y: torch.Tensor, eps: float) -> None:
+        """out = resid + sum over ranks of partial(rows); y = rmsnorm(out).  Flips
+        to the other partial buffer (a buffer is rewritten only after the next
+        barrier, by which time every rank has finished reading it)."""
+        buf = self.part[self.k]
+        self.pc.barrier(SLOT_SERVE)
+        view = buf.local[:rows * self.D].view(rows, self.D)
+        if self.pc.nvls and buf.mc_ptr:
+            C().rs_sum(view, self.tp, out, resid, gamma, y, None, float(eps), 2, None, buf.mc_ptr)
+        else:
+            C().rs_sum(view, self.tp, out, resid, gamma, y, None, float(eps), 1, buf.ptrs, 0)
+        self.k ^= 1
+
+
+class TPModelRunner(ModelRunner):
+    """ModelRunner over this rank's shard (`params`: parallel.tp.TPParams)."""
+
+    def __init__(self, cfg: TransformerConfig, params, comm: TPServeComm, device="cuda", **kw):
+        tp = comm.tp
+        if cfg.num_heads % tp or cfg.num_kv_heads % tp:
+            raise ValueError(f"tp={tp} must divide the head counts")
+        self.full_cfg = cfg
+        self.comm = comm
+        self.tp, self.rank = tp, comm.rank
+        local = dataclasses.replace(cfg, num_heads=cfg.num_heads // tp, num_kv_heads=cfg.num_kv_heads // tp)
+        super().__init__(local, params, device, **kw)
+        # every rank must index the same KV blocks: agree on the smallest pool
+        nb = torch.tensor([self.num_blocks], dtype=torch.int64, device=self.device)
+        dist.all_reduce(nb, op=dist.ReduceOp.MIN, group=comm.group)
+        self.num_blocks = int(nb.item())
+        self.vocab_local = self.W["lm_head"].shape[0]
+        self._xn: Optional[torch.Tensor] = None
+
+    def _layer(self, i, h, pos, slots, attn):
+        cfg, c = self.cfg, self.comm
+        p = f"layers.{i}."
+        xn = self._xn if self._xn is not None else N.rmsnorm_fwd(h, self.W[p + "attn_norm"], cfg.norm_eps)[0]
+        qkv = self._linear(xn, p + "wqkv")
+        E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, positions=pos)
+        ks = self.k_scale[i] if self.k_scale is not None else None
+        vs = self.v_scale[i] if self.v_scale is not None else None
+        SV.kv_append(qkv, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, slots, self.k_cache[i],
+                     self.v_cache[i], ks, vs, self.kv_dtype)
+        o = attn(i, qkv)
+        M = h.shape[0]
+        self._row_parallel(o, p + "wo", c.partial(M))
+        h2, xn2 = torch.empty_like(h), torch.empty_like(h)
+        c.allreduce_norm(M, h2, h, self.W[p + "ffn_norm"], xn2, cfg.norm_eps)
+        w = self.W[p + "wgu"]
+        if isinstance(w, SV.QuantizedWeight):
+            a = E.swiglu_fwd(self._linear(xn2, p + "wgu"))
+        else:
+            from ..ops import gemm as G
+            _, a = G.linear_swiglu(xn2, w)
+        self._row_parallel(a, p + "wdown", c.partial(M))
+        last = i == cfg.num_layers - 1
+        g = self.W["final_norm"] if last else self.W[f"layers.{i + 1}.attn_norm"]
+        h3, xn3 = torch.empty_like(h), torch.empty_like(h)
+        c.allreduce_norm(M, h3, h2, g, xn3, cfg.norm_eps)
+        self._xn = None if last else xn3
+        return h3
+
+    def _row_parallel(self, x: torch.Tensor, name: str, part: torch.Tensor) -> None:
+        y = self._linear(x, name, out=part)
+        if y.data_ptr() != part.data_ptr():
+            part.copy_(y)
+
+    def prefill(self, items: List[PrefillItem]):
+        self._xn = None
+        return super().prefill(items)
+
+    def decode(self, tokens, positions, slots, block_tables):
+        self._xn = None
+        return super().decode(tokens, positions, slots, block_tables)
+
+    def sample(self, logits: torch.Tensor, temps: Optional[List[float]], seed: int) -> torch.Tensor:
+        n = logits.shape[0]
+        t = None if temps is None else torch.tensor(temps, dtype=torch.float32, device=logits.device)
+        val = torch.empty(n, dtype=torch.float32, device=logits.device)
+        tok = SV.sample(logits, t, seed, v0=self.rank * self.vocab_local, out_val=val)
+        mine = torch.stack([val.double(), tok.double()], 1)
+        allp = torch.empty(self.tp, n, 2, dtype=torch.float64, device=logits.device)
+        dist.all_gather_into_tensor(allp, mine, group=self.comm.group)
+        best = allp[:, :, 0].argmax(0)  # first maximum = lowest rank = lowest id on ties
+        return allp[best, torch.arange(n, device=logits.device), 1].long()
+
+
+class RunnerProxy:
+    """Rank 0's stand-in for the runner: broadcasts every call to the workers
+    (CPU group) and runs it on its own shard."""
+
+    def __init__(self, runner: TPModelRunner, ctrl_group):
+        self.runner = runner
+        self.ctrl = ctrl_group
+        self.num_blocks = runner.num_blocks
+        self.block_size = runner.block_size
+        self._logits = None
+
+    def _bcast(self, msg) -> None:
+        obj = [msg]
+        dist.broadcast_object_list(obj, src=0, group=self.ctrl)
+
+    def prefill(self, items):
+        self._bcast(("prefill", items))
+        seq_ids, self._logits = self.runner.prefill(items)
+        return seq_ids, self._logits
+
+    def decode(self, tokens, positions, slots, block_tables):
+        self._bcast(("decode", (tokens, positions, slots, block_tables)))
+        self._logits = self.runner.decode(tokens, positions, slots, block_tables)
+        return self._logits
+
+    def sample(self, logits, temps, seed):
+        self._bcast(("sample", (temps, seed)))
+        return self.runner.sample(logits, temps, seed)
+
+    def weight_bytes(self) -> int:
+        return self.runner.weight_bytes()
+
+    def stop(self) -> None:
+        self._bcast(("stop", None))
+
+
+def worker_loop(runner: TPModelRunner, ctrl_group) -> None:
+    """Ranks > 0: execute rank 0's runner calls until it says stop."""
+    logits = None
+    while True:
+        obj = [None]
+        dist.broadcast_object_list(obj, src=0, group=ctrl_group)
+        op, arg = obj[0]
+        if op == "stop":
+            return
+        if op == "prefill":
+            _, logits = runner.prefill(arg)
+        elif op == "decode":
+            logits = runner.decode(*arg)
+        elif op == "sample":
+            runner.sample(logits, *arg)
+        else:
+            raise RuntimeError(f"unknown runner call {op!r}")
+
+
+def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none", kv_dtype: str = "fp8",
+                    group_size: int = 128, block_size: int = 16, max_model_len: int = 4096,
+                    max_rows: int = 8192, num_blocks: int = 0, device=None, params=None):
+    """This rank's TPModelRunner (weights initialised as FlatParams(cfg).init_(seed)
+    would, then sharded) plus the CPU control group."""
+    from ..parallel.tp import TPParams
+    dev = torch.device(device or torch.cuda.current_device())
+    tp, rank = dist.get_world_size(), dist.get_rank()
+    comm = TPServeComm(cfg.hidden_dim, max_rows, dev)
+    if params is None:
+        params = TPParams(cfg, tp, rank, dev)
+        params.init_(seed, cfg.init_std)
+    runner = TPModelRunner(cfg, params, comm, dev, kv_dtype=kv_dtype, weights=weights, group_size=group_size,
+                           num_blocks=num_blocks, block_size=block_size, max_model_len=max_model_len)
+    ctrl = dist.new_group(backend="gloo")
+    return runner, ctrl

@@ -108,7 +108,7 @@ def bench_diag(cfg, B, S, iters, rank0):
     res["gemm_wo_local"] = _time(lambda: G.gemm(o, wo, full_o), iters, 3, flush)
     res["gemm_rs_wo"] = _time(lambda: c.gemm_rs(0, o, wo), iters, 3, flush)
     hout = torch.empty(R, D, **bf)
-    res["rs_sum_plain"] = _time(lambda: C().rs_sum(c.recv_view(0, R, D), W, hout, None, None, None, None, 1e-5),
+    res["rs_sum_plain"] = _time(lambda: C().rs_sum(c.recv_view(0, R, D), W, hout, None, None, None, None, 1e-5, 0, None, 0),
                                 iters, 3, flush)
     res["nccl_reduce_scatter"] = _time(
         lambda: dist.reduce_scatter_tensor(hout, full_o), iters, 3, flush)
