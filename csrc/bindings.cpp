@@ -229,6 +229,71 @@ void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t ep
   check(lk_gemm(&d, stream()));
 }
 
+// K2: block-scaled fp8 GEMM and its quantisers.
+void gemm_fp8(torch::Tensor a8, torch::Tensor sa, int64_t a_fmt, torch::Tensor b8, torch::Tensor sb,
+              torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(a8.device());
+  TORCH_CHECK(a8.is_cuda() && a8.scalar_type() == torch::kUInt8 && a8.dim() == 2 && a8.stride(1) == 1,
+              "gemm_fp8: a8 must be a row-major uint8 (fp8 bits) matrix");
+  TORCH_CHECK(b8.is_cuda() && b8.scalar_type() == torch::kUInt8 && b8.dim() == 2 && b8.stride(1) == 1,
+              "gemm_fp8: b8 must be a row-major uint8 (fp8 bits) matrix");
+  TORCH_CHECK(a8.size(1) == b8.size(1), "gemm_fp8: K mismatch");
+  need_contig(sa, "sa", torch::kFloat32);
+  need_contig(sb, "sb", torch::kFloat32);
+  need(out, "out", torch::kBFloat16);
+  LkGemmFp8Desc d{};
+  d.a = a8.data_ptr();
+  d.a_ld = a8.stride(0);
+  d.b = b8.data_ptr();
+  d.b_ld = b8.stride(0);
+  d.M = (int)a8.size(0);
+  d.N = (int)b8.size(0);
+  d.K = (int)a8.size(1);
+  d.a_fmt = (int)a_fmt;
+  TORCH_CHECK(sa.numel() >= (int64_t)(d.K / 128) * d.M, "gemm_fp8: sa [K/128, M]");
+  TORCH_CHECK(sb.numel() >= (int64_t)((d.N + 127) / 128) * (d.K / 128), "gemm_fp8: sb [N/128, K/128]");
+  d.sa = sa.data_ptr<float>();
+  d.sb = sb.data_ptr<float>();
+  TORCH_CHECK(out.size(0) == d.M && out.size(1) == d.N && out.stride(1) == 1, "gemm_fp8: out [M, N]");
+  d.d = out.data_ptr();
+  d.ldd = out.stride(0);
+  if (resid.has_value()) {
+    need(*resid, "resid", torch::kBFloat16);
+    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == d.N && resid->stride(1) == 1, "gemm_fp8: resid");
+    d.r = resid->data_ptr();
+    d.ldr = resid->stride(0);
+  }
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  check(lk_gemm_fp8(&d, stream()));
+}
+
+void quant_1x128(torch::Tensor x, int64_t fmt, torch::Tensor q, torch::Tensor scale) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need(x, "x", torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "quant_1x128: x row-major");
+  TORCH_CHECK(q.scalar_type() == torch::kUInt8 && q.stride(1) == 1 && q.size(0) == x.size(0) &&
+                  q.size(1) == x.size(1), "quant_1x128: q");
+  need_contig(scale, "scale", torch::kFloat32);
+  TORCH_CHECK(scale.numel() >= x.size(0) * (x.size(1) / 128), "quant_1x128: scale");
+  check(lk_quant_1x128(x.data_ptr(), x.stride(0), (int)x.size(0), (int)x.size(1), (int)fmt, q.data_ptr(),
+                       q.stride(0), scale.data_ptr<float>(), stream()));
+}
+
+void quant_128x128(torch::Tensor w, torch::Tensor q, c10::optional<torch::Tensor> qt, torch::Tensor scale) {
+  const c10::cuda::CUDAGuard g(w.device());
+  need(w, "w", torch::kBFloat16);
+  TORCH_CHECK(w.dim() == 2 && w.stride(1) == 1, "quant_128x128: w row-major");
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == torch::kUInt8 && q.numel() == w.numel(), "quant_128x128: q");
+  if (qt.has_value())
+    TORCH_CHECK(qt->is_contiguous() && qt->scalar_type() == torch::kUInt8 && qt->numel() == w.numel(),
+                "quant_128x128: qt");
+  need_contig(scale, "scale", torch::kFloat32);
+  TORCH_CHECK(scale.numel() >= ((w.size(0) + 127) / 128) * (w.size(1) / 128), "quant_128x128: scale");
+  check(lk_quant_128x128(w.data_ptr(), w.stride(0), (int)w.size(0), (int)w.size(1), q.data_ptr(),
+                         qt.has_value() ? qt->data_ptr() : nullptr, scale.data_ptr<float>(), stream()));
+}
+
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
 void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
             c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> y,
@@ -745,6 +810,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ag", &gemm_ag);
   m.def("rs_sum", &rs_sum);
   m.def("gemm_gather", &gemm_gather);
+  m.def("gemm_fp8", &gemm_fp8);
+  m.def("quant_1x128", &quant_1x128);
+  m.def("quant_128x128", &quant_128x128);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);

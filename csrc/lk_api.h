@@ -136,6 +136,32 @@ int lk_embedding_fwd(const int64_t* ids, const void* W, void* out, int T, int D,
 int lk_embedding_bwd(const int64_t* ids, const void* dy, float* dW, int T, int D, int V,
                      cudaStream_t s);
 
+// ------------------------------------------------- K2 block-scaled fp8 GEMM
+// D[M, N] (bf16) = (A8 . B8^T with per-block scales) [+ R].  A8 [M, K] fp8
+// (a_fmt 0 = e4m3, 1 = e5m2), scale sa[K/128][M] (one per row and 128-wide K
+// block); B8 [N, K] e4m3, scale sb[ceil(N/128)][K/128] (one per 128 x 128
+// block).  K % 128 == 0; pitches in elements (= bytes) multiples of 16.
+typedef struct LkGemmFp8Desc {
+  const void* a;
+  int64_t a_ld;
+  const void* b;
+  int64_t b_ld;
+  int M, N, K, a_fmt;
+  const float* sa;
+  const float* sb;
+  void* d;
+  int64_t ldd;
+  const void* r;  // optional residual (bf16, pitch ldr)
+  int64_t ldr;
+  int* status;
+} LkGemmFp8Desc;
+int lk_gemm_fp8(const LkGemmFp8Desc* desc, cudaStream_t stream);
+// x bf16 [M, K] -> q fp8 [M, K] (fmt 0 e4m3 / 1 e5m2) + scale [K/128][M]
+int lk_quant_1x128(const void* x, int64_t ldx, int M, int K, int fmt, void* q, int64_t ldq, float* scale,
+                   cudaStream_t s);
+// w bf16 [N, K] -> q e4m3 [N, K], optional qt = q^T [K, N], scale [ceil(N/128)][K/128]
+int lk_quant_128x128(const void* w, int64_t ldw, int N, int K, void* q, void* qt, float* scale, cudaStream_t s);
+
 // --------------------------------------------- K18 owner-side slot reduction
 typedef struct LkRsSumDesc {
   const void* recv;   // [world * rows, ld_recv] bf16: slot s = rank s's partial
