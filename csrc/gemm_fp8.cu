@@ -9,8 +9,8 @@
 // epilogue warps read the partial back (tcgen05.ld), scale it by
 // sa[m] * sb and add it to the row's fp32 accumulator in registers, so the
 // block scales are applied exactly (DeepSeek-V3 style promotion, with TMEM
-// instead of a register accumulator).  Two TMEM partials alternate so the
-// MMAs of block kb+1 overlap the promotion of block kb.
+// instead of a register accumulator).  Four TMEM partials rotate so the MMAs
+// run up to four K blocks ahead of the promotion.
 //
 // Tile 128 x 128 (one CTA per SM, persistent), K step 128 fp8 = one 128-byte
 // swizzle row, 6-stage TMA ring.  Warp 0: TMA producer; warp 1: MMA issuer;
@@ -28,8 +28,22 @@ namespace {
 constexpr int F8_BM = 128, F8_BN = 128, F8_BK = 128;  // BK in elements (= bytes)
 constexpr int F8_STAGES = 6;
 constexpr int F8_STAGE = (F8_BM + F8_BN) * F8_BK;     // 32 KB
-constexpr int F8_THREADS = 192;
-constexpr int F8_SMEM = F8_STAGES * F8_STAGE + 256 + 1024;
+constexpr int F8_EW = 4;                     // promotion warps (4: one per TMEM lane quarter)
+constexpr int F8_THREADS = 64 + 32 * F8_EW;  // + producer and MMA-issuer warps
+constexpr int F8_EPI = 32 * F8_EW;           // promotion threads
+constexpr int F8_NPB = 4;                    // TMEM partials in flight (4 x 128 columns)
+constexpr int F8_SC_DIST = 6, F8_SC_RING = 8;  // scale prefetch distance / ring depth (K blocks)
+constexpr int F8_SMEM = F8_STAGES * F8_STAGE + 256 + F8_SC_RING * F8_EPI * 8 + 1024;
+
+// 4-byte asynchronous copy global -> shared (zero-filled when src_bytes == 0).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 struct F8Args {
   int M, N, K;
@@ -63,10 +77,10 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F8_STAGES * F8_STAGE);
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + 8 * F8_STAGES;
-  const uint32_t pfull0 = empty0 + 8 * F8_STAGES;  // [2] a TMEM partial is ready
-  const uint32_t pempty0 = pfull0 + 16;            // [2] the epilogue has read it
-  const uint32_t drain_bar = pempty0 + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * F8_STAGES + 5);
+  const uint32_t pfull0 = empty0 + 8 * F8_STAGES;  // [NPB] a TMEM partial is ready
+  const uint32_t pempty0 = pfull0 + 8 * F8_NPB;    // [NPB] the epilogue has read it
+  const uint32_t drain_bar = pempty0 + 8 * F8_NPB;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * F8_STAGES + 2 * F8_NPB + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -75,9 +89,9 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < F8_NPB; ++b) {
       mbar_init(pfull0 + 8 * b, 1);
-      mbar_init(pempty0 + 8 * b, 4);
+      mbar_init(pempty0 + 8 * b, F8_EW);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -85,7 +99,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 256);
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), F8_NPB * F8_BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -133,7 +147,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       uint32_t g = 0;  // K blocks issued by this CTA (selects the TMEM partial)
       for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
         for (int kb = 0; kb < nk; ++kb, ++g) {
-          const uint32_t pb = g & 1, use = g >> 1;
+          const uint32_t pb = g % F8_NPB, use = g / F8_NPB;
           if (!bounded_wait(pempty0 + 8 * pb, (use & 1) ^ 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
               !bounded_wait(full0 + 8 * s, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
             ok = false;
@@ -159,36 +173,63 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
     }
   } else {
     // ------------------------------------------- promotion + epilogue (row per thread)
-    const int q = warp & 3;
+    const int q = warp & 3;                 // TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;       // which slice of the tile's columns (8 warps)
+    const int et = (warp - 2) * 32 + lane;  // promotion thread id (scale ring slot)
     const int row_in_tile = q * 32 + lane;
+    constexpr int HN = F8_BN * 4 / F8_EW;   // columns per thread
     const int nkb_b = nk;  // sb row length
+    // per-thread ring of (sa, sb) scale pairs, filled F8_SC_DIST K blocks ahead with cp.async
+    const uint32_t sring = sbase + F8_STAGES * F8_STAGE + 256;
     uint32_t g = 0;
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
       int tm, tn;
       f8_tile(t, args.tiles_m, args.tiles_n, tm, tn);
       const int row = tm * F8_BM + row_in_tile;
       const bool row_ok = row < args.M;
-      float acc[F8_BN];
+      float acc[HN];
 #pragma unroll
-      for (int j = 0; j < F8_BN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < HN; ++j) acc[j] = 0.f;
       bool ok = true;
+      auto issue_scales = [&](int k) {
+        const uint32_t slot = sring + ((k % F8_SC_RING) * F8_EPI + et) * 8;
+        cp_async4(slot, args.sa + (int64_t)k * args.M + (row_ok ? row : 0), row_ok ? 4 : 0);
+        cp_async4(slot + 4, args.sb + (int64_t)tn * nkb_b + k, 4);
+      };
+#pragma unroll 1
+      for (int k = 0; k < F8_SC_DIST; ++k) {
+        if (k < nk) issue_scales(k);
+        cp_async_commit();
+      }
       for (int kb = 0; kb < nk; ++kb, ++g) {
-        const uint32_t pb = g & 1, use = g >> 1;
+        if (kb + F8_SC_DIST < nk) issue_scales(kb + F8_SC_DIST);
+        cp_async_commit();
+        const uint32_t pb = g % F8_NPB, use = g / F8_NPB;
         ok = bounded_wait(pfull0 + 8 * pb, use & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float s = (row_ok ? args.sa[(int64_t)kb * args.M + row] : 0.f) * args.sb[(int64_t)tn * nkb_b + kb];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + pb * F8_BN;
+        cp_async_wait<F8_SC_DIST>();  // this thread's scales of block kb have landed
+        float sa_v, sb_v;
+        {
+          const uint32_t slot = sring + ((kb % F8_SC_RING) * F8_EPI + et) * 8;
+          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(sa_v), "=f"(sb_v) : "r"(slot));
+        }
+        const float s = sa_v * sb_v;
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + pb * F8_BN + half * HN;
 #pragma unroll
-        for (int c = 0; c < F8_BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
+        for (int c = 0; c < HN / 64; ++c) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(taddr + c * 64, r0);
+          tmem_ld32(taddr + c * 64 + 32, r1);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(r[j]), s, acc[c * 32 + j]);
+          for (int j = 0; j < 32; ++j) {
+            acc[c * 64 + j] = fmaf(__uint_as_float(r0[j]), s, acc[c * 64 + j]);
+            acc[c * 64 + 32 + j] = fmaf(__uint_as_float(r1[j]), s, acc[c * 64 + 32 + j]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -198,8 +239,8 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       if (row_ok) {
         __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
 #pragma unroll
-        for (int v = 0; v < F8_BN / 8; ++v) {
-          const int col = tn * F8_BN + v * 8;
+        for (int v = 0; v < HN / 8; ++v) {
+          const int col = tn * F8_BN + half * HN + v * 8;
           if (col >= args.N) break;
           float f[8];
 #pragma unroll
@@ -226,7 +267,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, F8_NPB * F8_BN);
   }
 }
 

@@ -81,6 +81,32 @@ def bench_gemm(shapes, iters):
                           "peak_src": pk["src"]}), flush=True)
 
 
+def bench_fp8(shapes, iters):
+    """K2 block-scaled fp8 GEMM (quantised operands prepared outside the timed
+    region) against the bf16 tcgen05 GEMM and cuBLAS bf16 on the same shape."""
+    from lora_kernel_b200.ops import fp8 as F
+    from lora_kernel_b200.ops.gemm import gemm
+    pk = peaks()
+    for (M, N, K) in shapes:
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        w8 = F.Fp8Weight(w, transpose=False)
+        q, s = F.quantize_1x128(x)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        t8 = time_fn(lambda: F.gemm_fp8(q, s, w8.q, w8.scale, out=out), iters)
+        tq = time_fn(lambda: F.quantize_1x128(x), iters)
+        tb = time_fn(lambda: gemm(x, w, out), iters)
+        tc = time_fn(lambda: torch.matmul(x, w.t(), out=out), iters)
+        fl = 2.0 * M * N * K
+        print(json.dumps({"kernel": "gemm_fp8_blockscaled", "M": M, "N": N, "K": K,
+                          "ms": round(t8, 4), "tflops": round(fl / t8 / 1e9, 1),
+                          "act_quant_ms": round(tq, 4),
+                          "bf16_tc_ms": round(tb, 4), "cublas_bf16_ms": round(tc, 4),
+                          "speedup_vs_bf16_tc": round(tb / t8, 3),
+                          "frac_of_bf16_peak": round(fl / t8 / 1e9 / pk["bf16_tflops"], 3),
+                          "peak_src": pk["src"]}), flush=True)
+
+
 def bench_norm(iters):
     from lora_kernel_b200.ops.norm import rmsnorm_fwd
     pk = peaks()
@@ -134,6 +160,9 @@ def main():
                       (8192, 2048, 5632, "tn"), (8192, 32000, 2048, "tn"),
                       (8192, 2048, 11264, "dgrad"), (11264, 2048, 8192, "wgrad")]
         bench_gemm(shapes, args.iters)
+    if "fp8" in which:
+        bench_fp8([(8192, 8192, 8192), (8192, 3584, 4096), (8192, 4096, 1792), (8192, 768, 4096)]
+                  if not args.small else [(8192, 8192, 8192)], args.iters)
     if "norm" in which:
         bench_norm(args.iters)
     if "attn" in which:
