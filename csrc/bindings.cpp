@@ -640,6 +640,14 @@ T ptrs(const torch::Tensor& t) {
   return reinterpret_cast<T>(t.data_ptr());
 }
 
+void signal_barrier_dev(torch::Tensor sig_ptrs, int64_t rank, int64_t world, int64_t slot, torch::Tensor epoch_ctr,
+                        torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(sig_ptrs.device());
+  need(epoch_ctr, "epoch_ctr", torch::kInt32);
+  check(lk_signal_barrier_dev(ptrs<int* const*>(sig_ptrs), (int)rank, (int)world, (int)slot,
+                              epoch_ctr.data_ptr<int>(), status.data_ptr<int>(), stream()));
+}
+
 void signal_barrier(torch::Tensor sig_ptrs, int64_t rank, int64_t world, int64_t slot, int64_t epoch,
                     torch::Tensor status) {
   const c10::cuda::CUDAGuard g(sig_ptrs.device());
@@ -831,6 +839,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optimizer_finalize", &optimizer_finalize);
   m.def("attention_fwd", &attention_fwd);
   m.def("signal_barrier", &signal_barrier);
+  m.def("signal_barrier_dev", &signal_barrier_dev);
   m.def("kv_append", &kv_append);
   m.def("decode_attention", &decode_attention);
   m.def("sample", &sample);

@@ -67,6 +67,25 @@ __global__ void signal_barrier_kernel(int* const* __restrict__ sig_ptrs, int ran
   __syncthreads();
 }
 
+// The same barrier with the epoch kept on the device: the kernel advances
+// *epoch_ctr itself, so a captured CUDA graph can replay it (every rank runs the
+// same sequence of barriers on the slot, so the counters stay equal).
+__global__ void signal_barrier_dev_kernel(int* const* __restrict__ sig_ptrs, int rank, int world, int slot,
+                                          int* __restrict__ epoch_ctr, int* status) {
+  __shared__ int e;
+  if (threadIdx.x == 0) {
+    e = *epoch_ctr + 1;
+    *epoch_ctr = e;
+  }
+  __syncthreads();
+  const int p = threadIdx.x;
+  __threadfence_system();
+  if (p < world) st_release_sys(sig_ptrs[p] + slot * world + rank, e);
+  __syncthreads();
+  if (p < world) wait_flag(sig_ptrs[rank] + slot * world + p, e, status);
+  __syncthreads();
+}
+
 __global__ void allgather_copy_kernel(const uint8_t* const* __restrict__ src_ptrs, int64_t src_off,
                                       int64_t chunk_bytes, uint8_t* __restrict__ dst, int world) {
   const int64_t n16 = chunk_bytes / 16;
@@ -315,6 +334,14 @@ extern "C" int lk_signal_barrier(int* const* sig_ptrs, int rank, int world, int 
   LK_REQUIRE(world >= 1 && world <= 32 && slot >= 0 && slot < LK_SIG_SLOTS, "signal_barrier: bad args");
   signal_barrier_kernel<<<1, 32, 0, s>>>(sig_ptrs, rank, world, slot, epoch, status);
   return check_launch("signal_barrier");
+}
+
+extern "C" int lk_signal_barrier_dev(int* const* sig_ptrs, int rank, int world, int slot, int* epoch_ctr,
+                                     int* status, cudaStream_t s) {
+  LK_REQUIRE(world >= 1 && world <= 32 && slot >= 0 && slot < LK_SIG_SLOTS && epoch_ctr,
+             "signal_barrier_dev: bad args");
+  signal_barrier_dev_kernel<<<1, 32, 0, s>>>(sig_ptrs, rank, world, slot, epoch_ctr, status);
+  return check_launch("signal_barrier_dev");
 }
 
 extern "C" int lk_allgather_copy(const void* const* src_ptrs, int64_t src_off_bytes,

@@ -352,6 +352,9 @@ int lk_dequantize(int fmt, const void* q, const float* scale, const float* zero,
 // (rank order) into symmetric (peer-mapped) buffers.  Flag arrays hold
 // LK_SIG_SLOTS * world int32 per rank, zero-initialised; epochs increase.
 #define LK_SIG_SLOTS 16
+// Device-epoch form (graph-replayable): *epoch_ctr (device int) is advanced by the kernel.
+int lk_signal_barrier_dev(int* const* sig_ptrs, int rank, int world, int slot, int* epoch_ctr, int* status,
+                          cudaStream_t s);
 int lk_signal_barrier(int* const* sig_ptrs, int rank, int world, int slot, int epoch, int* status,
                       cudaStream_t s);
 int lk_allgather_copy(const void* const* src_ptrs, int64_t src_off_bytes, int64_t chunk_bytes,

@@ -136,6 +136,7 @@ class ServeConfig:
     num_kv_blocks: int = 0  # 0 = size from free memory
     enable_prefix_caching: bool = True
     max_model_len: int = 4096
+    cuda_graphs: bool = True  # decode steps replayed from CUDA graphs (per batch-size bucket)
     api_keys: tuple = ()
     rate_limit_rps: float = 0.0
 

@@ -114,6 +114,14 @@ class PeerComm:
         self.epochs[slot] = e
         return e
 
+    def barrier_dev(self, slot: int) -> None:
+        """Device barrier whose epoch lives on the device (replayable inside a
+        CUDA graph).  A slot is used either with this or with barrier(), never both."""
+        if not hasattr(self, "_dev_epochs"):
+            self._dev_epochs = torch.zeros(C().SIG_SLOTS, dtype=torch.int32, device=self.device)
+        C().signal_barrier_dev(self.sig.ptrs, self.rank, self.world, slot, self._dev_epochs[slot:slot + 1],
+                               status(self.device))
+
     def barrier(self, slot: int) -> None:
         """Device barrier on the current stream (bounded wait per peer)."""
         C().signal_barrier(self.sig.ptrs, self.rank, self.world, slot, self.next_epoch(slot),

@@ -64,7 +64,9 @@ class ModelRunner:
             free, _ = torch.cuda.mem_get_info(self.device)
             num_blocks = max(16, int(free * mem_fraction) // (per_token * block_size))
         self.num_blocks = num_blocks
-        slots = num_blocks * block_size
+        # one extra block at the end: the KV sink of padding rows in graph-captured decode
+        slots = (num_blocks + 1) * block_size
+        self.dummy_block = num_blocks
         dt = SV.KV_TORCH[kv_dtype]
         self.k_cache = torch.zeros(cfg.num_layers, slots, KV, Dh, dtype=dt, device=self.device)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -74,6 +76,9 @@ class ModelRunner:
         else:
             self.k_scale = self.v_scale = None
         self.rope = E.rope_table(max_model_len, Dh, cfg.rope_base, self.device)
+        self.use_graphs = False
+        self._graphs: Dict[int, Tuple] = {}
+        self._pool = None
 
     # --------------------------------------------------------------- weights
     def _load_weights(self, params: FlatParams, fmt: str, group: int) -> None:
@@ -107,9 +112,9 @@ class ModelRunner:
                 need = w.N * w.K
                 if self._scratch is None or self._scratch.numel() < need:
                     self._scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
-                y = w.matmul_t(x, scratch=self._scratch[:need].view(w.N, w.K))
+                y = w.matmul_t(x, out=out, scratch=self._scratch[:need].view(w.N, w.K))
             else:
-                y = w.matmul_t(x)
+                y = w.matmul_t(x, out=out)
             if residual is not None:
                 y += residual
             return y
@@ -193,23 +198,27 @@ class ModelRunner:
         return [items[k].seq_id for k in want], logits
 
     # --------------------------------------------------------------- decode
-    @torch.no_grad()
-    def decode(self, tokens: List[int], positions: List[int], slots: List[int],
-               block_tables: List[List[int]]) -> torch.Tensor:
-        """One token per sequence; returns logits [n, vocab]."""
+    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
+
+    def enable_graphs(self) -> None:
+        """Replay decode steps from CUDA graphs captured per batch-size bucket
+        (inputs padded to the bucket; padding rows write their K/V into a
+        reserved block).  The launch sequence of a whole decode step - every
+        layer's GEMMs, norms, RoPE, KV append and paged attention - becomes one
+        graph launch, which is what bounds small-batch decode otherwise."""
+        if self.use_graphs:
+            return
+        need = 0
+        for w in self.W.values():
+            if isinstance(w, SV.QuantizedWeight):
+                need = max(need, w.N * w.K)
+        if need and (self._scratch is None or self._scratch.numel() < need):
+            self._scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
+        self._pool = torch.cuda.graph_pool_handle()
+        self.use_graphs = True
+
+    def _decode_body(self, ids_t, pos_t, slots_t, bt, ctx, max_ctx: int) -> torch.Tensor:
         cfg = self.cfg
-        dev = self.device
-        n = len(tokens)
-        ids_t = torch.tensor(tokens, dtype=torch.int64, device=dev)
-        pos_t = torch.tensor(positions, dtype=torch.int32, device=dev)
-        slots_t = torch.tensor(slots, dtype=torch.int32, device=dev)
-        mb = max(len(t) for t in block_tables)
-        bt = torch.zeros(n, mb, dtype=torch.int32)
-        for k, t in enumerate(block_tables):
-            bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
-        bt = bt.to(dev)
-        ctx = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=dev)
-        max_ctx = max(positions) + 1
         H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
 
         def attn(i, qkv):
@@ -222,3 +231,81 @@ class ModelRunner:
         for i in range(cfg.num_layers):
             h = self._layer(i, h, pos_t, slots_t, attn)
         return self._head(h)
+
+    @torch.no_grad()
+    def decode(self, tokens: List[int], positions: List[int], slots: List[int],
+               block_tables: List[List[int]]) -> torch.Tensor:
+        """One token per sequence; returns logits [n, vocab]."""
+        n = len(tokens)
+        if self.use_graphs and n <= self.GRAPH_BUCKETS[-1]:
+            return self._decode_graph(tokens, positions, slots, block_tables)
+        dev = self.device
+        ids_t = torch.tensor(tokens, dtype=torch.int64, device=dev)
+        pos_t = torch.tensor(positions, dtype=torch.int32, device=dev)
+        slots_t = torch.tensor(slots, dtype=torch.int32, device=dev)
+        mb = max(len(t) for t in block_tables)
+        bt = torch.zeros(n, mb, dtype=torch.int32)
+        for k, t in enumerate(block_tables):
+            bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        bt = bt.to(dev)
+        ctx = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=dev)
+        return self._decode_body(ids_t, pos_t, slots_t, bt, ctx, max(positions) + 1)
+
+    def _decode_graph(self, tokens, positions, slots, block_tables) -> torch.Tensor:
+        n = len(tokens)
+        b = next(x for x in self.GRAPH_BUCKETS if x >= n)
+        mb = (self.max_model_len + self.block_size - 1) // self.block_size
+        st = self._graphs.get(b)
+        if st is None:
+            st = self._capture(b, mb)
+            self._graphs[b] = st
+        graph, host, dev_in, out = st
+        # host staging (pinned): ids | pos | slots | ctx | block table, padding rows -> reserved block
+        hi = host.numpy()
+        hi[:] = 0
+        hi[0:n] = tokens
+        hi[b:b + n] = positions
+        hi[2 * b:2 * b + n] = slots
+        hi[2 * b + n:3 * b] = self.dummy_block * self.block_size
+        hi[3 * b:3 * b + n] = [p + 1 for p in positions]
+        hi[3 * b + n:4 * b] = 1
+        btab = hi[4 * b:].reshape(b, mb)
+        for k, t in enumerate(block_tables):
+            btab[k, :len(t)] = t
+        btab[n:, 0] = self.dummy_block
+        dev_in.copy_(host, non_blocking=True)
+        graph.replay()
+        return out[:n]
+
+    def _capture(self, b: int, mb: int):
+        dev = self.device
+        host = torch.zeros(4 * b + b * mb, dtype=torch.int32, pin_memory=True)
+        dev_in = torch.zeros_like(host, device=dev)
+        ids_t = dev_in[0:b]
+        pos_t = dev_in[b:2 * b]
+        slots_t = dev_in[2 * b:3 * b]
+        ctx = dev_in[3 * b:4 * b]
+        bt = dev_in[4 * b:].view(b, mb)
+        # a valid dummy batch for warm-up and capture: every row is padding
+        host[2 * b:3 * b] = self.dummy_block * self.block_size
+        host[3 * b:4 * b] = 1
+        host[4 * b:].view(b, mb)[:, 0] = self.dummy_block
+        dev_in.copy_(host)
+        ids64 = torch.empty(b, dtype=torch.int64, device=dev)
+
+        def body():
+            ids64.copy_(ids_t)
+            return self._decode_body(ids64, pos_t, slots_t, bt, ctx, self.max_model_len)
+
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=self._pool):
+            out = body()
+        torch.cuda.synchronize(dev)
+        return graph, host, dev_in, out

@@ -52,6 +52,8 @@ class TPServeComm:
         self.pc = CM.PeerComm(self.device, self.group)
         self.part = [CM.SymBuffer(max_rows * hidden, torch.bfloat16, self.device, self.group) for _ in range(2)]
         self.k = 0
+        self.pc.barrier_dev(SLOT_SERVE)  # create the device epoch counter before any graph capture
+        torch.cuda.synchronize(self.device)
 
     def partial(self, rows: int) -> torch.Tensor:
         if rows > self.max_rows:
@@ -64,7 +66,7 @@ class TPServeComm:
         to the other partial buffer (a buffer is rewritten only after the next
         barrier, by which time every rank has finished reading it)."""
         buf = self.part[self.k]
-        self.pc.barrier(SLOT_SERVE)
+        self.pc.barrier_dev(SLOT_SERVE)
         view = buf.local[:rows * self.D].view(rows, self.D)
         if self.pc.nvls and buf.mc_ptr:
             C().rs_sum(view, self.tp, out, resid, gamma, y, None, float(eps), 2, None, buf.mc_ptr)
@@ -203,7 +205,8 @@ def worker_loop(runner: TPModelRunner, ctrl_group) -> None:
 
 def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none", kv_dtype: str = "fp8",
                     group_size: int = 128, block_size: int = 16, max_model_len: int = 4096,
-                    max_rows: int = 8192, num_blocks: int = 0, device=None, params=None):
+                    max_rows: int = 8192, num_blocks: int = 0, device=None, params=None,
+                    cuda_graphs: bool = True):
     """This rank's TPModelRunner (weights initialised as FlatParams(cfg).init_(seed)
     would, then sharded) plus the CPU control group."""
     from ..parallel.tp import TPParams
@@ -215,5 +218,7 @@ def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none",
         params.init_(seed, cfg.init_std)
     runner = TPModelRunner(cfg, params, comm, dev, kv_dtype=kv_dtype, weights=weights, group_size=group_size,
                            num_blocks=num_blocks, block_size=block_size, max_model_len=max_model_len)
+    if cuda_graphs:
+        runner.enable_graphs()  # every rank captures the same buckets in the same order
     ctrl = dist.new_group(backend="gloo")
     return runner, ctrl
