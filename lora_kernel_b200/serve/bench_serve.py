@@ -67,7 +67,8 @@ def main(argv=None):
         runner, ctrl = build_tp_runner(cfg, a.seed, weights=weights, kv_dtype=kv,
                                        group_size=rc.quant.group_size, block_size=sc.block_size,
                                        max_model_len=sc.max_model_len,
-                                       max_rows=max(sc.max_num_batched_tokens, sc.max_num_seqs))
+                                       max_rows=max(sc.max_num_batched_tokens, sc.max_num_seqs),
+                                       max_batch=sc.max_num_seqs)
         torch.cuda.synchronize()
         if rank != 0:
             worker_loop(runner, ctrl)

@@ -83,7 +83,7 @@ class LLMEngine:
             num_blocks=self.sc.num_kv_blocks, block_size=self.sc.block_size,
             max_model_len=self.sc.max_model_len)
         if self.sc.cuda_graphs and hasattr(self.runner, "enable_graphs"):
-            self.runner.enable_graphs()
+            self.runner.enable_graphs(self.sc.max_num_seqs)
         self.blocks = BlockManager(self.runner.num_blocks, self.sc.block_size,
                                    self.sc.enable_prefix_caching)
         self.waiting: deque = deque()

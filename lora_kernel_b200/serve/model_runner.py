@@ -200,7 +200,7 @@ class ModelRunner:
     # --------------------------------------------------------------- decode
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
 
-    def enable_graphs(self) -> None:
+    def enable_graphs(self, max_batch: int = 256, capture: bool = True) -> None:
         """Replay decode steps from CUDA graphs captured per batch-size bucket
         (inputs padded to the bucket; padding rows write their K/V into a
         reserved block).  The launch sequence of a whole decode step - every
@@ -216,6 +216,12 @@ class ModelRunner:
             self._scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
         self._pool = torch.cuda.graph_pool_handle()
         self.use_graphs = True
+        self.graph_max_batch = max_batch
+        if capture:
+            # capture every bucket now (largest first) so no request waits on a capture later
+            mb = (self.max_model_len + self.block_size - 1) // self.block_size
+            for b in sorted((x for x in self.GRAPH_BUCKETS if x <= max_batch), reverse=True):
+                self._graphs[b] = self._capture(b, mb)
 
     def _decode_body(self, ids_t, pos_t, slots_t, bt, ctx, max_ctx: int) -> torch.Tensor:
         cfg = self.cfg
@@ -237,7 +243,7 @@ class ModelRunner:
                block_tables: List[List[int]]) -> torch.Tensor:
         """One token per sequence; returns logits [n, vocab]."""
         n = len(tokens)
-        if self.use_graphs and n <= self.GRAPH_BUCKETS[-1]:
+        if self.use_graphs and n <= getattr(self, "graph_max_batch", self.GRAPH_BUCKETS[-1]):
             return self._decode_graph(tokens, positions, slots, block_tables)
         dev = self.device
         ids_t = torch.tensor(tokens, dtype=torch.int64, device=dev)
@@ -259,7 +265,7 @@ class ModelRunner:
         if st is None:
             st = self._capture(b, mb)
             self._graphs[b] = st
-        graph, host, dev_in, out = st
+        graph, host, dev_in, out, _ = st
         # host staging (pinned): ids | pos | slots | ctx | block table, padding rows -> reserved block
         hi = host.numpy()
         hi[:] = 0
@@ -308,4 +314,6 @@ class ModelRunner:
         with torch.cuda.graph(graph, pool=self._pool):
             out = body()
         torch.cuda.synchronize(dev)
-        return graph, host, dev_in, out
+        # every tensor the graph reads or writes outside its private pool must
+        # stay alive as long as the graph: the input buffers and ids64
+        return graph, host, dev_in, out, ids64

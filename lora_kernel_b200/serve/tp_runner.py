@@ -206,7 +206,7 @@ def worker_loop(runner: TPModelRunner, ctrl_group) -> None:
 def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none", kv_dtype: str = "fp8",
                     group_size: int = 128, block_size: int = 16, max_model_len: int = 4096,
                     max_rows: int = 8192, num_blocks: int = 0, device=None, params=None,
-                    cuda_graphs: bool = True):
+                    cuda_graphs: bool = True, max_batch: int = 256):
     """This rank's TPModelRunner (weights initialised as FlatParams(cfg).init_(seed)
     would, then sharded) plus the CPU control group."""
     from ..parallel.tp import TPParams
@@ -219,6 +219,6 @@ def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none",
     runner = TPModelRunner(cfg, params, comm, dev, kv_dtype=kv_dtype, weights=weights, group_size=group_size,
                            num_blocks=num_blocks, block_size=block_size, max_model_len=max_model_len)
     if cuda_graphs:
-        runner.enable_graphs()  # every rank captures the same buckets in the same order
+        runner.enable_graphs(max_batch)  # every rank captures the same buckets in the same order
     ctrl = dist.new_group(backend="gloo")
     return runner, ctrl

@@ -28,7 +28,7 @@ def main():
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (17, 40, 64, 5)]
     sp = SamplingParams(max_tokens=12, temperature=0.0)
     runner, ctrl = build_tp_runner(cfg, 7, weights=weights, kv_dtype="bf16", num_blocks=128,
-                                   max_model_len=512, max_rows=512)
+                                   max_model_len=512, max_rows=512, max_batch=sc.max_num_seqs)
     if rank != 0:
         worker_loop(runner, ctrl)
     else:

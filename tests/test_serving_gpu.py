@@ -191,9 +191,9 @@ def test_engine_quantized_weights_match_dequantized_bf16(fmt):
         # decode path (M = 1 -> dequantising GEMV)
         slot = e.blocks.append_slot(t, 64)
         outs.append(e.runner.decode([seq[-1]], [64], [slot], [t])[0].float())
-    for a_, b_ in ((outs[0], outs[2]), (outs[1], outs[3])):
+    for which, (a_, b_) in (("prefill", (outs[0], outs[2])), ("decode", (outs[1], outs[3]))):
         rel = (a_ - b_).norm() / b_.norm()
-        assert rel < 0.05, rel
+        assert rel < 0.05, (which, rel)
     assert eng.runner.weight_bytes() < eng_ref.runner.weight_bytes()
 
 
@@ -218,7 +218,7 @@ def test_decode_cuda_graph_matches_eager(weights):
     use = r.use_graphs
     r.use_graphs = False
     eager = r.decode(toks, pos, sl, tables).float().clone()
-    r.enable_graphs()
+    r.enable_graphs(capture=False)
     r.use_graphs = True
     for _ in range(2):  # first call captures, second replays
         g = r.decode(toks, pos, sl, tables).float()
