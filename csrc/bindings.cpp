@@ -109,8 +109,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
 
 // K18: GEMM whose bf16 output rows are stored into their owner rank's receive
 // buffer (peer pointers `rptrs`, int64 device tensor) at slot rs_rank.
+// Device copy of the K18 store tensor maps of every rank's receive buffer.
+torch::Tensor make_remote_maps(std::vector<int64_t> ptrs, int64_t rows, int64_t cols, int64_t ld,
+                               torch::Device device) {
+  std::vector<void*> p(ptrs.size());
+  for (size_t i = 0; i < ptrs.size(); ++i) p[i] = reinterpret_cast<void*>(ptrs[i]);
+  auto host = torch::empty({(int64_t)ptrs.size() * 128}, torch::dtype(torch::kUInt8));
+  check(lk_make_remote_maps(p.data(), (int)p.size(), rows, cols, ld, host.data_ptr()));
+  return host.to(device);
+}
+
 void gemm_rs(torch::Tensor a, torch::Tensor b, torch::Tensor rptrs, int64_t rs_rows, int64_t rs_rank,
-             int64_t ldd, int64_t m_rot, torch::Tensor status, int64_t bn) {
+             int64_t ldd, int64_t m_rot, torch::Tensor status, int64_t bn, c10::optional<torch::Tensor> rmaps) {
   const c10::cuda::CUDAGuard g(a.device());
   TORCH_CHECK(a.size(1) == b.size(1), "gemm_rs: K mismatch");
   Operand A = classify(a, "a"), B = classify(b, "b");
@@ -134,6 +144,12 @@ void gemm_rs(torch::Tensor a, torch::Tensor b, torch::Tensor rptrs, int64_t rs_r
   d.rptrs = reinterpret_cast<void* const*>(rptrs.data_ptr());
   d.rs_rows = (int)rs_rows;
   d.rs_rank = (int)rs_rank;
+  if (rmaps.has_value()) {
+    TORCH_CHECK(rmaps->is_cuda() && rmaps->numel() == rptrs.numel() * 128 &&
+                    reinterpret_cast<uintptr_t>(rmaps->data_ptr()) % 64 == 0,
+                "gemm_rs: rmaps must be world x 128-byte tensor maps on the device");
+    d.rmaps = rmaps->data_ptr();
+  }
   check(lk_gemm(&d, stream()));
 }
 
@@ -815,6 +831,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lora_kernel_b200 sm_100a kernels";
   m.def("gemm", &gemm);
   m.def("gemm_rs", &gemm_rs);
+  m.def("make_remote_maps", &make_remote_maps);
   m.def("gemm_ag", &gemm_ag);
   m.def("rs_sum", &rs_sum);
   m.def("gemm_gather", &gemm_gather);

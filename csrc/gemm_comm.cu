@@ -52,3 +52,12 @@ int gemm_dispatch_comm(const LkGemmDesc& g, cudaStream_t s) {
   return fail("gemm: unknown comm_mode");
 }
 }  // namespace lk
+
+extern "C" int lk_make_remote_maps(void* const* host_ptrs, int world, int64_t rows, int64_t cols, int64_t ld,
+                                   void* out) {
+  CUtensorMap* m = reinterpret_cast<CUtensorMap*>(out);
+  for (int p = 0; p < world; ++p)
+    if (!lk::make_tmap_2d(m + p, host_ptrs[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, ld, 32, 64))
+      return -1;
+  return 0;
+}

@@ -57,6 +57,7 @@ struct GemmArgs {
   // K18 remote-store epilogue: row m belongs to owner m / rs_rows and lands in
   // rptrs[owner] at row (rs_rank * rs_rows + m % rs_rows), pitch ldd
   void* const* rptrs;
+  const CUtensorMap* rmaps;  // optional: per-owner tensor maps of the receive buffers (TMA stores)
   int rs_rows, rs_rank;
   // K16 all-gather of A on first use: rank p's rows [0, ag_rows) live at
   // ag_src[p] (pitch ag_ld_src bytes; p == ag_rank is this GPU's own staging
@@ -495,10 +496,44 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
           }
         }
       } else if constexpr (EPI == EPI_REMOTE) {
-        // K18: stage 32 rows x 64 columns (bf16) per warp in shared memory,
-        // then store whole 128-byte row segments into the owner's receive
-        // slot over NVLink (4 rows per warp instruction).
-        uint8_t* stg = smem + C::STAGES * C::STAGE + C::BAR_BYTES + q * 4096;
+        // K18: stage 32 rows x 64 columns (bf16) per warp in shared memory
+        // (128-byte swizzle), then move it into the owner's receive slot over
+        // NVLink: one TMA tile store per 32 x 64 block when the owners' tensor
+        // maps are given (double-buffered staging), else whole 128-byte row
+        // segments with generic stores (4 rows per warp instruction).
+        if (args.rmaps != nullptr) {
+          const int grow0 = tm * GEMM_BM + q * 32;
+          const int owner = grow0 / args.rs_rows;
+          const int ydst = args.rs_rank * args.rs_rows + grow0 - owner * args.rs_rows;
+          const CUtensorMap* map = args.rmaps + owner;
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            uint8_t* stg = smem + C::STAGES * C::STAGE + 1024 + (q * 2 + (c & 1)) * 4096;
+            uint32_t r0[32], r1[32];
+            tmem_ld32(taddr + c * 64, r0);
+            tmem_ld32(taddr + c * 64 + 32, r1);
+            tc_wait_ld();
+            if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t* rr = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(rr[0]) * alpha, __uint_as_float(rr[1]) * alpha);
+              pk.y = pack_bf16x2(__uint_as_float(rr[2]) * alpha, __uint_as_float(rr[3]) * alpha);
+              pk.z = pack_bf16x2(__uint_as_float(rr[4]) * alpha, __uint_as_float(rr[5]) * alpha);
+              pk.w = pack_bf16x2(__uint_as_float(rr[6]) * alpha, __uint_as_float(rr[7]) * alpha);
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) = pk;
+            }
+            fence_proxy_async_smem();  // generic smem writes -> visible to the TMA unit
+            __syncwarp();
+            if (lane == 0 && tn * BN + c * 64 < args.N) {
+              tma_store_2d(map, smem_u32(stg), tn * BN + c * 64, ydst);
+              bulk_commit();
+            }
+          }
+        } else {
+        uint8_t* stg = smem + C::STAGES * C::STAGE + 1024 + q * 4096;
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t r0[32], r1[32];
@@ -531,6 +566,7 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
             }
           }
           __syncwarp();
+        }
         }
       } else {
 #pragma unroll 1
@@ -589,6 +625,10 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
     }
+    if constexpr (EPI == EPI_REMOTE) {
+      if (lane == 0) bulk_wait<0>();  // every TMA store of this warp has landed in peer memory
+      __syncwarp();
+    }
   }
 
   tc_fence_before();
@@ -630,6 +670,7 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   }
   args.m_rot = g.m_rot;
   args.rptrs = reinterpret_cast<void* const*>(g.rptrs);
+  args.rmaps = reinterpret_cast<const CUtensorMap*>(g.rmaps);
   args.rs_rows = g.rs_rows;
   args.rs_rank = g.rs_rank;
   args.ag_src = reinterpret_cast<const uint8_t* const*>(g.ag_src);
@@ -651,7 +692,8 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
-  constexpr int SMEM = C::SMEM + (EPI == EPI_REMOTE ? 4 * 4096 : 0);  // + K18 staging
+  // K18 staging: 1024-aligned after the barriers, 2 x 4 KB per epilogue warp
+  constexpr int SMEM = C::SMEM + (EPI == EPI_REMOTE ? 1024 - C::BAR_BYTES + 8 * 4096 : 0);
   if (!(attr_set & (1ull << dev))) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     attr_set |= 1ull << dev;

@@ -67,6 +67,7 @@ typedef struct LkGemmDesc {
   int comm_mode;
   int m_rot;
   void* const* rptrs;
+  const void* rmaps;  // optional K18 TMA stores: DEVICE array of per-owner tensor maps (lk_make_remote_maps)
   int rs_rows, rs_rank;
   const void* const* ag_src;
   int64_t ag_ld_src;
@@ -85,6 +86,10 @@ typedef struct LkGemmDesc {
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
+// Encode the K18 store tensor maps of `world` receive buffers (bf16 [rows, cols],
+// pitch ld elements; 32 x 64 boxes, 128-byte swizzle) into host memory out
+// (world * 128 bytes, to be copied to the device by the caller).
+int lk_make_remote_maps(void* const* host_ptrs, int world, int64_t rows, int64_t cols, int64_t ld, void* out);
 
 // --------------------------------------------------------------- K5 RMSNorm
 typedef struct LkNormFwdDesc {

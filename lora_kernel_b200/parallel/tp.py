@@ -35,6 +35,7 @@ split with an all-gather / all-reduce around a plain matmul.
 from __future__ import annotations
 
 import copy
+import os
 from collections import OrderedDict
 from typing import Dict, List, Optional, Tuple
 
@@ -228,6 +229,7 @@ class TPComm:
         self.stats = CM.SymBuffer(max_tokens * 4, torch.float32, self.device, self.group)
         self.count = torch.zeros(max_tokens // 128, dtype=torch.int32, device=self.device)
         self._nccl_tmp: Dict[Tuple[int, int], torch.Tensor] = {}
+        self._tmaps: Dict[Tuple[int, int, int], torch.Tensor] = {}
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)
 
@@ -268,7 +270,19 @@ class TPComm:
             dist.reduce_scatter_tensor(self.recv_view(k, R, Nc)[:R], full, group=self.group)
             return
         C().gemm_rs(a, w, self.recv[k].ptrs, R, self.rank, Nc, ((self.rank + 1) % self.tp) * R // 128,
-                    status(self.device), 0)
+                    status(self.device), 0, self._maps(k, R, Nc))
+
+    def _maps(self, k: int, R: int, Nc: int):
+        """Per-owner TMA store maps of receive buffer k viewed as [tp*R, Nc]
+        (LK_TMA_STORE=0 selects the generic-store epilogue)."""
+        if os.environ.get("LK_TMA_STORE", "1") == "0":
+            return None
+        key = (k, R, Nc)
+        m = self._tmaps.get(key)
+        if m is None:
+            m = C().make_remote_maps(self.recv[k].ptrs_host, self.tp * R, Nc, Nc, self.device)
+            self._tmaps[key] = m
+        return m
 
     def rs_sum(self, k: int, out: torch.Tensor, resid: Optional[torch.Tensor] = None,
                gamma: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None,
