@@ -25,13 +25,18 @@
 
 namespace lk {
 
+// element offset of the LSE * log2(e) half of the dvec scratch (16-byte aligned)
+static inline int64_t lk_attn_dvec_half(int B, int Hq, int S) {
+  return ((int64_t)B * Hq * S + 63) / 64 * 64;
+}
+
 struct AttnBwdArgs {
   int B, S, Hq, Hkv;
   int causal, window;
   float sl2;    // scale * log2(e)
   float scale;  // softmax scale
-  const float* lse;   // [B, Hq, S] natural log
-  const float* Dvec;  // [B, Hq, S]
+  const float* lse;   // [B, Hq, S] LSE * log2(e)
+  const float* Dvec;  // [B, Hq, S] scale * rowsum(dO * O)
   float* dq_acc;      // [B*S, Hq*Dh] fp32
   __nv_bfloat16* dqkv;
   int64_t ld_dqkv;
@@ -52,7 +57,7 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 template <int DH>
 struct BwdCfg {
   static constexpr int QB = 128 * DH * 2;
-  static constexpr int STAGES = DH == 64 ? 2 : 1;
+  static constexpr int STAGES = DH == 64 ? 3 : 1;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = QB;
   static constexpr int OFF_Q = 2 * QB;
@@ -83,6 +88,10 @@ __global__ void __launch_bounds__(320, 1)
   using C = BwdCfg<DH>;
   // head_dim 64: dQ has its own TMEM columns; head_dim 128 reuses S^T's.
   constexpr bool DQ_ALIAS = DH == 128;
+  // head_dim 64 runs the skewed schedule: S^T/dP^T of iteration it+1 are issued
+  // before the dV/dK/dQ MMAs of iteration it, so the tensor cores work while
+  // the softmax warps turn S^T(it) into P/dS (needs dQ in its own columns).
+  constexpr bool SKEW = !DQ_ALIAS;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023) {
@@ -90,9 +99,9 @@ __global__ void __launch_bounds__(320, 1)
     return;
   }
   const uint32_t bar = sbase + C::OFF_BAR;
-  const uint32_t kv_full = bar, qd_full = bar + 8, qd_empty = bar + 24, sdp_full = bar + 40,
-                 sdp_free = bar + 48, ds_ready = bar + 56, dq_full = bar + 64, dq_free = bar + 72,
-                 drain = bar + 80;
+  const uint32_t kv_full = bar, qd_full = bar + 8, qd_empty = bar + 32, sdp_full = bar + 56,
+                 sdp_free = bar + 64, ds_ready = bar + 72, dq_full = bar + 80, dq_free = bar + 88,
+                 drain = bar + 96, pds_free = bar + 104;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 132);
 
@@ -113,10 +122,11 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(qd_full + 8 * s, 1);
       mbar_init(qd_empty + 8 * s, 1);
     }
+    mbar_init(pds_free, 1);
     mbar_init(sdp_full, 1);
     mbar_init(sdp_free, 8);
     mbar_init(ds_ready, 8);
@@ -188,7 +198,60 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
       const uint32_t sp = sbase + C::OFF_P, sds = sbase + C::OFF_DS;
       bool ok = bounded_wait(kv_full, 0, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
+      if constexpr (SKEW) {
+        // gradient MMAs of iteration m: dV += P^T dO, dK += dS^T Q, dQ = dS K
+        auto grad = [&](int m) -> bool {
+          const int stm = m % C::STAGES;
+          if (!bounded_wait(ds_ready, m & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
+              (m > 0 && !bounded_wait(dq_free, (m - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)))
+            return false;
+          tc_fence_after();
+          const uint32_t sq = sbase + C::OFF_Q + stm * C::QB, sdo = sbase + C::OFF_DO + stm * C::QB;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+            tc_mma_f16(tdV, make_desc_sw128(sp + aoff, 16, 1024), make_desc_sw128(sdo + kk * 2048, 16384, 1024),
+                       id_kv, (m > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16(tdK, make_desc_sw128(sds + aoff, 16, 1024), make_desc_sw128(sq + kk * 2048, 16384, 1024),
+                       id_kv, (m > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            tc_mma_f16(tdQ, make_desc_sw128(sds + kk * 2048, 16384, 1024),
+                       make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
+          tc_commit(dq_full);
+          tc_commit(qd_empty + 8 * stm);
+          tc_commit(pds_free);
+          return true;
+        };
+        for (int it = 0; it < n_it && ok; ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
+          if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
+              (it > 0 && !bounded_wait(sdp_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sq = sbase + C::OFF_Q + st * C::QB, sdo = sbase + C::OFF_DO + st * C::QB;
+#pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            tc_mma_f16(tS, make_desc_sw128(sk + off, 16, 1024), make_desc_sw128(sq + off, 16, 1024), id_s,
+                       kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            tc_mma_f16(tdP, make_desc_sw128(sv + off, 16, 1024), make_desc_sw128(sdo + off, 16, 1024), id_s,
+                       kk > 0 ? 1u : 0u);
+          }
+          tc_commit(sdp_full);
+          if (it > 0 && !grad(it - 1)) ok = false;
+        }
+        if (ok && n_it > 0) grad(n_it - 1);
+      }
+      for (int it = 0; it < n_it && ok && !SKEW; ++it) {
         const int st = it % C::STAGES;
         const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
         const uint32_t prev = (uint32_t)(it - 1) & 1;
@@ -251,6 +314,136 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t* sDS = smem + C::OFF_DS;
     const int ldq = args.Hq * DH;
     bool ok = true;
+    if constexpr (SKEW) {
+      // P/dS of iteration it are built in registers while the tensor cores run
+      // the gradient MMAs of it-1; dQ(it-1) is drained and P/dS(it) stored once
+      // those MMAs have finished with the shared P/dS tile.
+      auto drain_dq = [&](int m) {
+        const int hm = g * group + m / nq;
+        const int im = i0 + m % nq;
+        const int q = im * 128 + kr;
+        float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + hm * DH;
+#pragma unroll 1
+        for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
+          uint32_t v[32];
+          tmem_ld32(tdQ + lane_off + c * 32, v);
+          tc_wait_ld();
+          if (q < S) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              red_add_v4(dqrow + c * 32 + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                         __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+      };
+      for (int it = 0; it < n_it; ++it) {
+        const int h = g * group + it / nq;
+        const int i = i0 + it % nq;
+        bool w_ok = bounded_wait(sdp_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[2][32], dv[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32(tS + lane_off + (wg * 2 + c) * 32, sv[c]);
+          tmem_ld32(tdP + lane_off + (wg * 2 + c) * 32, dv[c]);
+        }
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sdp_free);  // S^T / dP^T may be overwritten now
+        const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
+        const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
+        const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
+                               args.window > 0;
+        const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
+        const int st = it % C::STAGES;
+        const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
+        uint32_t pp[2][16], pd[2][16];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int cc = wg * 2 + c;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const int qi = cc * 32 + e;
+            float Ls[4], Ds[4];
+            if (bulk_ld) {
+              const float4 L = *reinterpret_cast<const float4*>(sL + qi);
+              const float4 Dd = *reinterpret_cast<const float4*>(sL + 128 + qi);
+              Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
+              Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
+            } else if (vec_ok) {
+              const float4 L = *reinterpret_cast<const float4*>(lse_row + qi);
+              const float4 Dd = *reinterpret_cast<const float4*>(d_row + qi);
+              Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
+              Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
+            } else {
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const bool in = i * 128 + qi + t < S;
+                Ls[t] = in ? lse_row[qi + t] : 0.f;
+                Ds[t] = in ? d_row[qi + t] : 0.f;
+              }
+            }
+            float p[4], ds[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int q = i * 128 + qi + t;
+              p[t] = fast_exp2(fmaf(__uint_as_float(sv[c][e + t]), args.sl2, -Ls[t]));
+              if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
+                                (args.window > 0 && key <= q - args.window)))
+                p[t] = 0.f;
+              ds[t] = p[t] * fmaf(__uint_as_float(dv[c][e + t]), args.scale, -Ds[t]);
+            }
+            pp[c][e / 2] = pack_bf16x2(p[0], p[1]);
+            pp[c][e / 2 + 1] = pack_bf16x2(p[2], p[3]);
+            pd[c][e / 2] = pack_bf16x2(ds[0], ds[1]);
+            pd[c][e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+          }
+        }
+        if (it > 0) {
+          // the gradient MMAs of it-1 are done: the P/dS tile is free and dQ(it-1) is ready
+          w_ok = bounded_wait(dq_full, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) &&
+                 bounded_wait(pds_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+          if (!__all_sync(0xffffffffu, w_ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          drain_dq(it - 1);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int cc = wg * 2 + c;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t off = sw128_off_b(kr, cc * 4 + u);
+            *reinterpret_cast<uint4*>(sP + off) =
+                make_uint4(pp[c][4 * u], pp[c][4 * u + 1], pp[c][4 * u + 2], pp[c][4 * u + 3]);
+            *reinterpret_cast<uint4*>(sDS + off) =
+                make_uint4(pd[c][4 * u], pd[c][4 * u + 1], pd[c][4 * u + 2], pd[c][4 * u + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_ready);
+      }
+      if (ok && n_it > 0) {
+        const bool w_ok = bounded_wait(dq_full, (n_it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (__all_sync(0xffffffffu, w_ok)) {
+          tc_fence_after();
+          drain_dq(n_it - 1);
+        } else {
+          ok = false;
+        }
+      }
+    } else
     for (int it = 0; it < n_it; ++it) {
       const int h = g * group + it / nq;
       const int i = i0 + it % nq;
@@ -307,11 +500,11 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const int q = i * 128 + qi + t;
-            p[t] = fast_exp2(__uint_as_float(sv[c][e + t]) * args.sl2 - Ls[t] * 1.4426950408889634f);
+            p[t] = fast_exp2(fmaf(__uint_as_float(sv[c][e + t]), args.sl2, -Ls[t]));
             if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
                               (args.window > 0 && key <= q - args.window)))
               p[t] = 0.f;
-            ds[t] = p[t] * (__uint_as_float(dv[c][e + t]) - Ds[t]) * args.scale;
+            ds[t] = p[t] * fmaf(__uint_as_float(dv[c][e + t]), args.scale, -Ds[t]);
           }
           pp[e / 2] = pack_bf16x2(p[0], p[1]);
           pp[e / 2 + 1] = pack_bf16x2(p[2], p[3]);
@@ -399,11 +592,14 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-// D[b, h, q] = sum_d dO[q, h, d] * O[q, h, d]   (one warp per (row, head))
+// D[b, h, q] = scale * sum_d dO[q, h, d] * O[q, h, d]  and  L2 = LSE * log2(e)
+// (one warp per (row, head)): both pre-scaled so the softmax backward spends
+// one FFMA per element on each instead of a multiply and a subtract.
 template <int DH>
 __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                     const __nv_bfloat16* __restrict__ dout, int64_t lddo,
-                                    float* __restrict__ Dvec, int B, int S, int Hq) {
+                                    float* __restrict__ Dvec, const float* __restrict__ lse,
+                                    float* __restrict__ l2, float scale, int B, int S, int Hq) {
   const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)B * S * Hq;
@@ -421,7 +617,9 @@ __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t
   s = warp_sum(s);
   if (lane == 0) {
     const int bb = (int)(row / S), q = (int)(row % S);
-    Dvec[((int64_t)bb * Hq + h) * S + q] = s;
+    const int64_t idx = ((int64_t)bb * Hq + h) * S + q;
+    Dvec[idx] = s * scale;
+    l2[idx] = lse[idx] * 1.4426950408889634f;
   }
 }
 
@@ -443,11 +641,14 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   using C = BwdCfg<DH>;
   const int64_t T = (int64_t)d.B * d.S;
   const int ncols = (d.Hq + 2 * d.Hkv) * DH;
+  // dvec holds scale * D in its first half and LSE * log2(e) in the second
+  float* l2 = d.dvec + lk_attn_dvec_half(d.B, d.Hq, d.S);
   // D = rowsum(dO * O)
   {
     const int64_t warps = T * d.Hq;
     attn_bwd_dot_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
-        (const __nv_bfloat16*)d.o, d.ld_o, (const __nv_bfloat16*)d.dout, d.ld_do, d.dvec, d.B, d.S, d.Hq);
+        (const __nv_bfloat16*)d.o, d.ld_o, (const __nv_bfloat16*)d.dout, d.ld_do, d.dvec, d.lse, l2, d.scale,
+        d.B, d.S, d.Hq);
     if (check_launch("attn_bwd_dot")) return -1;
   }
   if (cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * T * d.Hq * DH, s) != cudaSuccess)
@@ -465,7 +666,7 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   a.window = d.window;
   a.scale = d.scale;
   a.sl2 = d.scale * 1.4426950408889634f;
-  a.lse = d.lse;
+  a.lse = l2;
   a.Dvec = d.dvec;
   a.dq_acc = d.dq_acc;
   a.dqkv = (__nv_bfloat16*)d.dqkv;

@@ -630,7 +630,7 @@ void attention_bwd(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch
   need_contig(lse, "lse", torch::kFloat32);
   need_contig(dq_acc, "dq_acc", torch::kFloat32);
   need_contig(dvec, "dvec", torch::kFloat32);
-  TORCH_CHECK(dq_acc.numel() >= B * S * Hq * Dh && dvec.numel() >= B * Hq * S, "attention_bwd: scratch too small");
+  TORCH_CHECK(dq_acc.numel() >= B * S * Hq * Dh && dvec.numel() >= 2 * ((B * Hq * S + 63) / 64 * 64), "attention_bwd: scratch too small");
   for (auto* t : {&qkv, &o, &dout, &dqkv})
     TORCH_CHECK(t->dim() == 2 && t->stride(1) == 1 && t->size(0) == B * S, "attention_bwd: bad 2-D operand");
   LkAttnBwdDesc d{};

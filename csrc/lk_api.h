@@ -291,7 +291,7 @@ typedef struct LkAttnBwdDesc {
   void* dqkv;        // [B*S, (Hq+2Hkv)*Dh] bf16 output
   int64_t ld_dqkv;
   float* dq_acc;     // scratch [B*S, Hq*Dh] fp32
-  float* dvec;       // scratch [B, Hq, S] fp32
+  float* dvec;       // scratch fp32: 2 x round_up(B*Hq*S, 64) (scaled D, LSE * log2(e))
   int B, S, Hq, Hkv, Dh;
   int causal, window;
   float scale;

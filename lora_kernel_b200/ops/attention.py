@@ -50,7 +50,7 @@ def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, dout: torch.Tensor, lse: t
     if dqkv is None:
         dqkv = torch.empty(B * S, (Hq + 2 * Hkv) * Dh, dtype=torch.bfloat16, device=qkv.device)
     dq_acc = _buf("dq", B * S * Hq * Dh, qkv.device)
-    dvec = _buf("dvec", B * Hq * S + 128, qkv.device)
+    dvec = _buf("dvec", 2 * ((B * Hq * S + 63) // 64 * 64), qkv.device)
     C().attention_bwd(qkv, o, dout, lse, dqkv, dq_acc, dvec, B, S, Hq, Hkv, Dh, bool(causal),
                       int(window), float(scale), status(qkv.device))
     return dqkv

@@ -136,10 +136,15 @@ def bench_attention(iters, B=4, S=2048, Hq=32, Hkv=4, Dh=64):
     v = qkv[:, (Hq + Hkv) * Dh:].view(B, S, Hkv, Dh).transpose(1, 2)
     sdpa = torch.nn.functional.scaled_dot_product_attention
     t_ref = time_fn(lambda: sdpa(q, k, v, is_causal=True, enable_gqa=True), iters)
+    qg, kg, vg = (x.detach().clone().requires_grad_(True) for x in (q, k, v))
+    og = sdpa(qg, kg, vg, is_causal=True, enable_gqa=True)
+    gref = torch.randn_like(og)
+    t_refb = time_fn(lambda: torch.autograd.grad(og, (qg, kg, vg), gref, retain_graph=True), iters)
     print(json.dumps({"kernel": "attention", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "Dh": Dh,
                       "fwd_ms": round(t_f, 4), "fwd_tflops": round(fl / t_f / 1e9, 1),
                       "bwd_ms": round(t_b, 4), "bwd_tflops": round(2.5 * fl / t_b / 1e9, 1),
-                      "sdpa_fwd_ms": round(t_ref, 4), "sdpa_fwd_tflops": round(fl / t_ref / 1e9, 1)}),
+                      "sdpa_fwd_ms": round(t_ref, 4), "sdpa_fwd_tflops": round(fl / t_ref / 1e9, 1),
+                      "sdpa_bwd_ms": round(t_refb, 4), "sdpa_bwd_tflops": round(2.5 * fl / t_refb / 1e9, 1)}),
           flush=True)
 
 
