@@ -81,8 +81,13 @@ __device__ __forceinline__ void q_range(const AttnBwdArgs& a, int j, int& i0, in
   }
 }
 
+// softmax warps: 16 for head_dim 64 (four per TMEM lane quarter, one 32-query
+// chunk each), 8 for head_dim 128
 template <int DH>
-__global__ void __launch_bounds__(320, 1)
+constexpr int bwd_softmax_warps() { return DH == 64 ? 16 : 8; }
+
+template <int DH>
+__global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const AttnBwdArgs args) {
   using C = BwdCfg<DH>;
@@ -92,6 +97,9 @@ __global__ void __launch_bounds__(320, 1)
   // before the dV/dK/dQ MMAs of iteration it, so the tensor cores work while
   // the softmax warps turn S^T(it) into P/dS (needs dQ in its own columns).
   constexpr bool SKEW = !DQ_ALIAS;
+  constexpr int NSW = bwd_softmax_warps<DH>();  // softmax warps
+  constexpr int NG = NSW / 4;                  // warps per TMEM lane quarter
+  constexpr int CPW = 4 / NG;                  // 32-query chunks per warp
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023) {
@@ -128,10 +136,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(pds_free, 1);
     mbar_init(sdp_full, 1);
-    mbar_init(sdp_free, 8);
-    mbar_init(ds_ready, 8);
+    mbar_init(sdp_free, NSW);
+    mbar_init(ds_ready, NSW);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 8);
+    mbar_init(dq_free, NSW);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -324,7 +332,7 @@ __global__ void __launch_bounds__(320, 1)
         const int q = im * 128 + kr;
         float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + hm * DH;
 #pragma unroll 1
-        for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
+        for (int c = wg; c < DH / 32; c += NG) {
           uint32_t v[32];
           tmem_ld32(tdQ + lane_off + c * 32, v);
           tc_wait_ld();
@@ -348,11 +356,11 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        uint32_t sv[2][32], dv[2][32];
+        uint32_t sv[CPW][32], dv[CPW][32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tS + lane_off + (wg * 2 + c) * 32, sv[c]);
-          tmem_ld32(tdP + lane_off + (wg * 2 + c) * 32, dv[c]);
+        for (int c = 0; c < CPW; ++c) {
+          tmem_ld32(tS + lane_off + (wg * CPW + c) * 32, sv[c]);
+          tmem_ld32(tdP + lane_off + (wg * CPW + c) * 32, dv[c]);
         }
         tc_wait_ld();
         tc_fence_before();
@@ -365,10 +373,10 @@ __global__ void __launch_bounds__(320, 1)
         const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
         const int st = it % C::STAGES;
         const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
-        uint32_t pp[2][16], pd[2][16];
+        uint32_t pp[CPW][16], pd[CPW][16];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int cc = wg * 2 + c;
+        for (int c = 0; c < CPW; ++c) {
+          const int cc = wg * CPW + c;
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             const int qi = cc * 32 + e;
@@ -419,8 +427,8 @@ __global__ void __launch_bounds__(320, 1)
           drain_dq(it - 1);
         }
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int cc = wg * 2 + c;
+        for (int c = 0; c < CPW; ++c) {
+          const int cc = wg * CPW + c;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const uint32_t off = sw128_off_b(kr, cc * 4 + u);
@@ -553,7 +561,7 @@ __global__ void __launch_bounds__(320, 1)
       __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
       __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
 #pragma unroll 1
-      for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
+      for (int c = wg; c < DH / 32; c += NG) {
         uint32_t a[32], bb[32];
         tmem_ld32(tdK + lane_off + c * 32, a);
         tmem_ld32(tdV + lane_off + c * 32, bb);
@@ -577,7 +585,7 @@ __global__ void __launch_bounds__(320, 1)
       // no query sees this key tile: its gradients are zero
       __nv_bfloat16* dk = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + g) * DH;
       __nv_bfloat16* dvp = args.dqkv + (int64_t)(row0 + key) * args.ld_dqkv + (args.Hq + args.Hkv + g) * DH;
-      for (int e = wg * (DH / 2); e < (wg + 1) * (DH / 2); e += 8) {
+      for (int e = wg * 8; e < DH; e += 8 * NG) {
         *reinterpret_cast<uint4*>(dk + e) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(dvp + e) = make_uint4(0, 0, 0, 0);
       }
@@ -675,7 +683,7 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   a.n_tiles = cdiv(d.S, 128);
   auto k = attn_bwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  k<<<a.n_tiles * d.Hkv * d.B, 320, C::SMEM, s>>>(tq, tdo, a);
+  k<<<a.n_tiles * d.Hkv * d.B, 64 + 32 * bwd_softmax_warps<DH>(), C::SMEM, s>>>(tq, tdo, a);
   if (check_launch("attn_bwd")) return -1;
   const int64_t n4 = T * d.Hq * DH / 4;
   int grid_c = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms() * 16);
