@@ -107,6 +107,7 @@ class TrainConfig:
     max_consecutive_skips: int = 20
     log_every: int = 10
     fixed_batch: bool = False  # reuse one seeded batch every step (the CPU demo's data)
+    recompute_activations: bool = False  # activation checkpointing: re-run each layer's forward in the backward
 
 
 @dataclass

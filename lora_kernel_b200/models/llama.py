@@ -40,10 +40,11 @@ from .params import FlatParams
 
 
 class _Workspace:
-    def __init__(self, cfg: TransformerConfig, B: int, S: int, device, save: bool):
+    def __init__(self, cfg: TransformerConfig, B: int, S: int, device, save: bool, recompute: bool = False):
         T = B * S
         D, F, V = cfg.hidden_dim, cfg.ff_dim_padded, cfg.vocab_size
-        nl = cfg.num_layers if save else 1
+        # recompute: keep every layer's input h, one slot of per-layer intermediates
+        nl = cfg.num_layers if (save and not recompute) else 1
         bf = dict(dtype=torch.bfloat16, device=device)
         f32 = dict(dtype=torch.float32, device=device)
         self.B, self.S, self.T = B, S, T
@@ -94,18 +95,22 @@ class LlamaModel:
         # optional (layer, target, fn): the next _lin / _lin_bwd of that linear runs
         # fn(a, b, out) instead of the plain GEMM (ZeRO-3 gather fused into it, K17)
         self.fused_gather = None
+        # activation checkpointing: the forward keeps only each layer's input; the
+        # backward re-runs a layer's forward (same kernels, same values) right
+        # before its backward
+        self.recompute = False
         self.lora = None        # optional LoRAAdapters (models/lora.py)
         self.train_base = True  # False: frozen base weights (no base weight gradients)
         self._u: Dict[Tuple[int, str], torch.Tensor] = {}
 
     # -------------------------------------------------------------- helpers
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
-        key = (B, S, save)
+        key = (B, S, save, self.recompute and save)
         ws = self._ws.get(key)
         if ws is None:
             if S > self.rope.shape[0]:
                 self.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
-            ws = _Workspace(self.cfg, B, S, self.device, save)
+            ws = _Workspace(self.cfg, B, S, self.device, save, recompute=self.recompute and save)
             self._ws[key] = ws
         return ws
 
@@ -209,7 +214,7 @@ class LlamaModel:
         for i in range(cfg.num_layers):
             self._hook("pre_layer_fwd", i)
             if save:
-                self._layer_fwd(i, ws, ws.h[i], ws.h[i + 1], i)
+                self._layer_fwd(i, ws, ws.h[i], ws.h[i + 1], 0 if self.recompute else i)
             else:
                 self._layer_fwd(i, ws, ws.h[i % 2], ws.h[(i + 1) % 2], 0)
         h_last = ws.h[cfg.num_layers] if save else ws.h[cfg.num_layers % 2]
@@ -257,6 +262,11 @@ class LlamaModel:
         self._hook("post_head_bwd")
         for i in reversed(range(L_)):
             self._hook("pre_layer_bwd", i)
+            if self.recompute:
+                # regenerate slot 0 (h[i+1] is rewritten with identical values; layer
+                # i+1's backward, its only other reader, has already run)
+                self._saving = True
+                self._layer_fwd(i, ws, ws.h[i], ws.h[i + 1], 0)
             self._layer_bwd(i, ws)
             self._hook("post_layer_bwd", i)
         if self.train_base:
@@ -270,20 +280,21 @@ class LlamaModel:
     def _layer_bwd(self, i: int, ws: _Workspace):
         cfg = self.cfg
         p = f"layers.{i}."
+        s = 0 if self.recompute else i  # workspace slot of layer i's intermediates
         dh = ws.dh
         # FFN
-        self._lin_bwd(i, "wdown", dh, ws.act[i], ws.dact)
-        E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
-        self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[i], ws.dx)
-        N.rmsnorm_bwd(ws.dx, ws.hmid[i], self._p(p + "ffn_norm"), ws.rstd2[i], self._g(p + "ffn_norm"),
+        self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
+        E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
+        self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[s], ws.dx)
+        N.rmsnorm_bwd(ws.dx, ws.hmid[s], self._p(p + "ffn_norm"), ws.rstd2[s], self._g(p + "ffn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)
         # attention
-        self._lin_bwd(i, "wo", dh, ws.o[i], ws.do)
-        A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, cfg.num_heads,
+        self._lin_bwd(i, "wo", dh, ws.o[s], ws.do)
+        A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
                         cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
                         dqkv=ws.dqkv)
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
                 inverse=True)
-        self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[i], ws.dx)
-        N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[i], self._g(p + "attn_norm"),
+        self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[s], ws.dx)
+        N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)

@@ -88,6 +88,15 @@ class QuantizedWeight:
             self.zero = None
         C().quantize(QFMT[fmt], w, group, self.q, self.scale, self.zero)
 
+    @classmethod
+    def from_parts(cls, fmt: str, group: int, N: int, K: int, q: torch.Tensor, scale: torch.Tensor,
+                   zero: Optional[torch.Tensor] = None) -> "QuantizedWeight":
+        """A weight quantised earlier (e.g. loaded from a checkpoint)."""
+        self = cls.__new__(cls)
+        self.fmt, self.group, self.N, self.K = fmt, group, N, K
+        self.q, self.scale, self.zero = q, scale, zero
+        return self
+
     def dequantize(self, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if out is None:
             out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.q.device)

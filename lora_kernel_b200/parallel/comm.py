@@ -42,6 +42,9 @@ def init_distributed(backend: str = "nccl", timeout_s: int = 300) -> tuple:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if backend == "nccl":
         torch.cuda.set_device(local)
+        if os.environ.get("LK_PIN_NUMA") == "1":  # CPU affinity = the GPU's NUMA node
+            from ..utils.env import pin_to_gpu_numa
+            pin_to_gpu_numa(local)
     if world > 1 and not dist.is_initialized():
         kw = dict(timeout=datetime.timedelta(seconds=timeout_s))
         if backend == "nccl":

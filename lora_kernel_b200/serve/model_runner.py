@@ -93,7 +93,10 @@ class ModelRunner:
                 self.W[p + n] = keep(params[p + n])
             for n in quant_names:
                 w = params[p + n]
-                self.W[p + n] = SV.QuantizedWeight(w, fmt, group) if fmt != "none" else w
+                if isinstance(w, SV.QuantizedWeight):  # already quantised (loaded checkpoint)
+                    self.W[p + n] = w
+                else:
+                    self.W[p + n] = SV.QuantizedWeight(w, fmt, group) if fmt != "none" else w
         self.W["embed"] = keep(params["embed"])
         self.W["final_norm"] = keep(params["final_norm"])
         self.W["lm_head"] = self.W["embed"] if cfg.tie_embeddings else keep(params["lm_head"])

@@ -73,6 +73,7 @@ class TrainingPipeline:
         self.model = model
         eng = model.engine
         self.engine = eng
+        eng.recompute = tc.recompute_activations
         master = eng.params.flat.float()
         self.opt = FusedAdamW(master, eng.params.segments(decay_norms=tc.decay_norms), lr=lr,
                               betas=(tc.beta1, tc.beta2), eps=tc.eps, weight_decay=weight_decay,

@@ -112,3 +112,18 @@ def test_bench_reference_arm_reports_unavailable():
                          text=True, check=True)
     d = json.loads(out.stdout.strip().splitlines()[-1])
     assert d["impl"] == "reference" and "unavailable" in d
+
+
+def test_numa_cpulist_from_fake_sysfs(tmp_path):
+    """The GPU's NUMA node CPUs are read from sysfs (a fake tree here)."""
+    from lora_kernel_b200.utils.env import gpu_numa_cpus, parse_cpulist
+    assert parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    (dev / "numa_node").write_text("1\n")
+    node = tmp_path / "devices" / "system" / "node" / "node1"
+    node.mkdir(parents=True)
+    (node / "cpulist").write_text("32-35,96\n")
+    assert gpu_numa_cpus("00000000:1B:00.0", str(tmp_path)) == {32, 33, 34, 35, 96}
+    (dev / "numa_node").write_text("-1\n")
+    assert gpu_numa_cpus("0000:1b:00.0", str(tmp_path)) == set()

@@ -131,3 +131,22 @@ def test_attention_variants():
     assert A.RelativePositionBias(4)(8).shape == (4, 8, 8)
     lo = A.linear_attention(q, k, v, causal=True)
     assert lo.shape == (1, 4, 16, 8) and torch.isfinite(lo).all()
+
+
+def test_quantized_checkpoint_roundtrip(tmp_path):
+    """qweight / scales / zeros + bf16 tensors survive a safetensors round trip."""
+    from lora_kernel_b200.ops.serving import QuantizedWeight
+    from lora_kernel_b200.quant.io import load_quantized, save_quantized
+    g = torch.Generator().manual_seed(0)
+    w4 = QuantizedWeight.from_parts("int4", 128, 64, 256, torch.randint(0, 255, (64, 128), dtype=torch.uint8, generator=g),
+                                    torch.rand(64, 2, generator=g), torch.rand(64, 2, generator=g))
+    w8 = QuantizedWeight.from_parts("int8", 128, 32, 256, torch.randint(-127, 127, (32, 256), dtype=torch.int8, generator=g),
+                                    torch.rand(32, generator=g))
+    emb = torch.randn(10, 4, generator=g).bfloat16()
+    path = str(tmp_path / "q.safetensors")
+    save_quantized({"layers.0.wqkv": w4, "layers.0.wo": w8, "embed": emb, "lm_head": emb}, path)
+    back = load_quantized(path, device="cpu")
+    assert back["layers.0.wqkv"].fmt == "int4" and back["layers.0.wqkv"].N == 64 and back["layers.0.wqkv"].K == 256
+    assert torch.equal(back["layers.0.wqkv"].q, w4.q) and torch.equal(back["layers.0.wqkv"].zero, w4.zero)
+    assert back["layers.0.wo"].zero is None and torch.equal(back["layers.0.wo"].scale, w8.scale)
+    assert torch.equal(back["embed"], emb) and back["lm_head"] is back["embed"]
