@@ -284,6 +284,65 @@ void gemm_fp8(torch::Tensor a8, torch::Tensor sa, int64_t a_fmt, torch::Tensor b
   check(lk_gemm_fp8(&d, stream()));
 }
 
+// K2 with a fused collective: mode "ag" (all-gather of A's fp8 rows + scales into
+// a8 / sa) or "rs" (reduce-scatter epilogue into the owners' receive buffers).
+void gemm_fp8_comm(torch::Tensor a8, torch::Tensor sa, int64_t a_fmt, torch::Tensor b8, torch::Tensor sb,
+                   c10::optional<torch::Tensor> out, torch::Tensor status, int64_t rank, int64_t world,
+                   c10::optional<torch::Tensor> ag_rows, c10::optional<torch::Tensor> ag_scales,
+                   int64_t rows_per_rank, c10::optional<torch::Tensor> count, c10::optional<torch::Tensor> rptrs,
+                   int64_t rs_rows, int64_t ldd) {
+  const c10::cuda::CUDAGuard g(a8.device());
+  TORCH_CHECK(a8.is_cuda() && a8.scalar_type() == torch::kUInt8 && a8.dim() == 2 && a8.stride(1) == 1, "a8");
+  TORCH_CHECK(b8.is_cuda() && b8.scalar_type() == torch::kUInt8 && b8.dim() == 2 && b8.stride(1) == 1, "b8");
+  TORCH_CHECK(a8.size(1) == b8.size(1), "gemm_fp8_comm: K mismatch");
+  need_contig(sa, "sa", torch::kFloat32);
+  need_contig(sb, "sb", torch::kFloat32);
+  LkGemmFp8Desc d{};
+  d.a = a8.data_ptr();
+  d.a_ld = a8.stride(0);
+  d.b = b8.data_ptr();
+  d.b_ld = b8.stride(0);
+  d.M = (int)a8.size(0);
+  d.N = (int)b8.size(0);
+  d.K = (int)a8.size(1);
+  d.a_fmt = (int)a_fmt;
+  d.sa = sa.data_ptr<float>();
+  d.sb = sb.data_ptr<float>();
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  d.rank = (int)rank;
+  d.world = (int)world;
+  if (ag_rows.has_value()) {
+    TORCH_CHECK(ag_scales.has_value() && count.has_value() && out.has_value(), "gemm_fp8_comm ag: missing args");
+    d.ag_rows = reinterpret_cast<const void* const*>(ag_rows->data_ptr());
+    d.ag_scales = reinterpret_cast<const float* const*>(ag_scales->data_ptr());
+    d.ag_rows_per_rank = (int)rows_per_rank;
+    d.ag_count = count->data_ptr<int>();
+  }
+  if (out.has_value()) {
+    need(*out, "out", torch::kBFloat16);
+    TORCH_CHECK(out->size(0) == d.M && out->size(1) == d.N && out->stride(1) == 1, "gemm_fp8_comm: out");
+    d.d = out->data_ptr();
+    d.ldd = out->stride(0);
+  }
+  if (rptrs.has_value()) {
+    d.rptrs = reinterpret_cast<void* const*>(rptrs->data_ptr());
+    d.rs_rows = (int)rs_rows;
+    d.ldd = ldd;
+  }
+  check(lk_gemm_fp8(&d, stream()));
+}
+
+void dequant_1x128(torch::Tensor q, int64_t fmt, torch::Tensor scale, torch::Tensor x) {
+  const c10::cuda::CUDAGuard g(q.device());
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == torch::kUInt8 && q.dim() == 2, "dequant_1x128: q");
+  need_contig(scale, "scale", torch::kFloat32);
+  need(x, "x", torch::kBFloat16);
+  TORCH_CHECK(x.size(0) == q.size(0) && x.size(1) == q.size(1) && x.stride(1) == 1, "dequant_1x128: x");
+  check(lk_dequant_1x128(q.data_ptr(), (int)q.size(0), (int)q.size(1), (int)fmt, scale.data_ptr<float>(),
+                         x.data_ptr(), x.stride(0), stream()));
+}
+
 void quant_1x128(torch::Tensor x, int64_t fmt, torch::Tensor q, torch::Tensor scale) {
   const c10::cuda::CUDAGuard g(x.device());
   need(x, "x", torch::kBFloat16);
@@ -837,6 +896,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_gather", &gemm_gather);
   m.def("gemm_fp8", &gemm_fp8);
   m.def("quant_1x128", &quant_1x128);
+  m.def("gemm_fp8_comm", &gemm_fp8_comm);
+  m.def("dequant_1x128", &dequant_1x128);
   m.def("quant_128x128", &quant_128x128);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);

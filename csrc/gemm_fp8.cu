@@ -55,7 +55,80 @@ struct F8Args {
   int64_t ldr;
   int* status;
   int tiles_m, tiles_n;
+  // fused all-gather of A (fp8 rows + their 1x128 scales) on first use
+  const uint8_t* const* ag_rows;  // per rank: ag_r rows x K fp8 (pitch K)
+  const float* const* ag_scales;  // per rank: [K/128, ag_r] scales
+  uint8_t* a_dst;                 // local A [M, K] (pitch K)
+  float* sa_dst;                  // local sa [K/128, M] (= sa)
+  int ag_r, ag_rank, ag_world;
+  int* ag_count;                  // [M/128] pieces copied per 128-row chunk
+  // remote-store epilogue (reduce-scatter): row m -> rptrs[m / rs_rows] at row rs_rank*rs_rows + m % rs_rows
+  void* const* rptrs;
+  int rs_rows, rs_rank;
 };
+
+__device__ __forceinline__ void f8_fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ int f8_ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// bounded wait for a 128-row chunk of gathered rows (8 pieces of 16 rows)
+__device__ __forceinline__ bool f8_wait_chunk(const F8Args& a, int tm, volatile int* abort_flag) {
+  const int* cnt = a.ag_count + tm;
+  const uint64_t t0 = globaltimer();
+  while (f8_ld_acquire(cnt) < 8) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > LK_WAIT_TIMEOUT_NS) {
+      atomicCAS(a.status, 0, LK_ERR_TIMEOUT_PEER);
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(100);
+  }
+  f8_fence_proxy_async_global();
+  return true;
+}
+
+// copy warps: 16-row pieces (own rows first, then rank+1, ...) of fp8 rows and their scales
+__device__ __forceinline__ void f8_ag_copy(const F8Args& a, int cw, int ncw, int lane) {
+  const int R = a.ag_r, W = a.ag_world, me = a.ag_rank, K = a.K, KB = a.K / 128;
+  const int per_rank = R / 16;
+  const int upr = K / 16;  // 16-byte units per fp8 row
+  for (int s = cw; s < per_rank * W; s += ncw) {
+    const int p = (me + s / per_rank) % W;
+    const int r0 = (s % per_rank) * 16;
+#pragma unroll 1
+    for (int r = 0; r < 16; ++r) {
+      const uint4* sr = reinterpret_cast<const uint4*>(a.ag_rows[p] + (int64_t)(r0 + r) * K);
+      uint4* dr = reinterpret_cast<uint4*>(a.a_dst + (int64_t)(p * R + r0 + r) * K);
+#pragma unroll 1
+      for (int c0 = lane; c0 < upr; c0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (c0 + 32 * k < upr) v[k] = sr[c0 + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (c0 + 32 * k < upr) dr[c0 + 32 * k] = v[k];
+      }
+    }
+    // scales of those 16 rows: KB rows of 16 floats
+    for (int u = lane; u < KB * 4; u += 32) {
+      const int kb = u >> 2, q4 = u & 3;
+      const float4 v = *reinterpret_cast<const float4*>(a.ag_scales[p] + (int64_t)kb * R + r0 + q4 * 4);
+      *reinterpret_cast<float4*>(a.sa_dst + (int64_t)kb * a.M + p * R + r0 + q4 * 4) = v;
+    }
+    f8_fence_proxy_async_global();
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(a.ag_count + (p * R + r0) / 128, 1);
+  }
+}
 
 __device__ __forceinline__ void f8_tile(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
   constexpr int G = 16;
@@ -67,8 +140,8 @@ __device__ __forceinline__ void f8_tile(int t, int tiles_m, int tiles_n, int& tm
   tn = r / gsz;
 }
 
-template <int AFMT>
-__global__ void __launch_bounds__(F8_THREADS, 1)
+template <int AFMT, bool AG = false, bool REMOTE = false>
+__global__ void __launch_bounds__(F8_THREADS + (AG ? 64 : 0), 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const F8Args args) {
   extern __shared__ uint8_t smem_raw[];
@@ -115,6 +188,13 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
         int tm, tn;
         f8_tile(t, args.tiles_m, args.tiles_n, tm, tn);
+        if constexpr (AG) {
+          tm = (tm + args.ag_rank * (args.ag_r / F8_BM)) % args.tiles_m;  // own rows first
+          if (!f8_wait_chunk(args, tm, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
         for (int kb = 0; kb < nk; ++kb) {
           if (!bounded_wait(empty0 + 8 * s, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
             ok = false;
@@ -171,6 +251,9 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       tc_commit(drain_bar);
       bounded_wait(drain_bar, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
+  } else if (AG && warp >= 2 + F8_EW) {
+    // ---------------------------------------------------------- copy warps
+    f8_ag_copy(args, (warp - 2 - F8_EW) * gridDim.x + blockIdx.x, 2 * gridDim.x, lane);
   } else {
     // ------------------------------------------- promotion + epilogue (row per thread)
     const int q = warp & 3;                 // TMEM lane quarter this warp may read
@@ -185,6 +268,11 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
       int tm, tn;
       f8_tile(t, args.tiles_m, args.tiles_n, tm, tn);
+      if constexpr (AG) {
+        tm = (tm + args.ag_rank * (args.ag_r / F8_BM)) % args.tiles_m;
+        // the tile's row scales come with the gathered rows: acquire them too
+        if (!__all_sync(0xffffffffu, f8_wait_chunk(args, tm, abort_flag))) break;
+      }
       const int row = tm * F8_BM + row_in_tile;
       const bool row_ok = row < args.M;
       float acc[HN];
@@ -237,7 +325,14 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       }
       if (!ok) break;
       if (row_ok) {
-        __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+        __nv_bfloat16* drow;
+        if constexpr (REMOTE) {
+          const int owner = row / args.rs_rows;
+          drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
+                 (int64_t)(args.rs_rank * args.rs_rows + row - owner * args.rs_rows) * args.ldd;
+        } else {
+          drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+        }
 #pragma unroll
         for (int v = 0; v < HN / 8; ++v) {
           const int col = tn * F8_BN + half * HN + v * 8;
@@ -345,6 +440,31 @@ __global__ void __launch_bounds__(256) quant_128x128_kernel(const __nv_bfloat16*
   }
 }
 
+// x = q * scale (1 x 128 blocks, scale layout [K/128, M]) -> bf16
+__global__ void __launch_bounds__(256) dequant_1x128_kernel(const uint8_t* __restrict__ q, int M, int K, int fmt,
+                                                            const float* __restrict__ scale,
+                                                            __nv_bfloat16* __restrict__ x, int64_t ldx) {
+  const int64_t n8 = (int64_t)M * K / 8;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < n8; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = u * 8;
+    const int row = (int)(e / K), col = (int)(e % K);
+    const float sc = scale[(int64_t)(col / 128) * M + row];
+    const uint2 v = *reinterpret_cast<const uint2*>(q + e);
+    const uint32_t w[2] = {v.x, v.y};
+    float f[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const __nv_fp8_storage_t bits = (__nv_fp8_storage_t)((w[h] >> (8 * b)) & 0xff);
+        const __half_raw hr = __nv_cvt_fp8_to_halfraw(bits, fmt == 0 ? __NV_E4M3 : __NV_E5M2);
+        f[h * 4 + b] = __half2float(__half(hr)) * sc;
+      }
+    *reinterpret_cast<uint4*>(x + (int64_t)row * ldx + col) =
+        make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+}
+
 }  // namespace
 }  // namespace lk
 
@@ -373,22 +493,56 @@ extern "C" int lk_gemm_fp8(const LkGemmFp8Desc* g, cudaStream_t stream) {
   const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   if (!make_tmap_2d(&ta, g->a, u8, 1, g->M, g->K, g->a_ld, F8_BM, F8_BK)) return -1;
   if (!make_tmap_2d(&tb, g->b, u8, 1, g->N, g->K, g->b_ld, F8_BN, F8_BK)) return -1;
-  static uint64_t attr_set[2] = {0, 0};
+  a.ag_rows = reinterpret_cast<const uint8_t* const*>(g->ag_rows);
+  a.ag_scales = reinterpret_cast<const float* const*>(g->ag_scales);
+  a.a_dst = reinterpret_cast<uint8_t*>(const_cast<void*>(g->a));
+  a.sa_dst = const_cast<float*>(g->sa);
+  a.ag_r = g->ag_rows_per_rank;
+  a.ag_rank = g->rank;
+  a.ag_world = g->world;
+  a.ag_count = g->ag_count;
+  a.rptrs = reinterpret_cast<void* const*>(g->rptrs);
+  a.rs_rows = g->rs_rows;
+  a.rs_rank = g->rank;
+  const int grid = std::min(a.tiles_m * a.tiles_n, num_sms());
+  const bool ag = g->ag_rows != nullptr, remote = g->rptrs != nullptr;
+  if (ag) {
+    LK_REQUIRE(g->ag_count && g->ag_scales && g->ag_rows_per_rank % 128 == 0 &&
+                   (int64_t)g->ag_rows_per_rank * g->world == g->M && g->a_ld == g->K,
+               "gemm_fp8 all-gather: M = world x rows (rows % 128 == 0), dense A");
+    if (cudaMemsetAsync(g->ag_count, 0, sizeof(int) * a.tiles_m, stream) != cudaSuccess)
+      return fail("gemm_fp8: memset failed");
+  }
+  if (remote) LK_REQUIRE(g->rs_rows > 0 && g->M % g->rs_rows == 0, "gemm_fp8 reduce-scatter: M = world x rs_rows");
+  void* kern = nullptr;
+#define LK_F8_PICK(F, AGV, RV) \
+  if (g->a_fmt == F && ag == AGV && remote == RV) kern = (void*)gemm_fp8_kernel<F, AGV, RV>;
+  LK_F8_PICK(0, false, false) LK_F8_PICK(1, false, false) LK_F8_PICK(0, true, false)
+  LK_F8_PICK(0, false, true) LK_F8_PICK(1, true, false) LK_F8_PICK(1, false, true)
+#undef LK_F8_PICK
+  LK_REQUIRE(kern != nullptr, "gemm_fp8: all-gather and reduce-scatter modes are exclusive");
+  static uint64_t attr_set[8] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int grid = std::min(a.tiles_m * a.tiles_n, num_sms());
-  if (g->a_fmt == 0) {
-    if (!(attr_set[0] & (1ull << dev))) {
-      cudaFuncSetAttribute(gemm_fp8_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM);
-      attr_set[0] |= 1ull << dev;
+  const int variant = g->a_fmt * 4 + (ag ? 2 : 0) + (remote ? 1 : 0);
+  if (!(attr_set[variant] & (1ull << dev))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM);
+    attr_set[variant] |= 1ull << dev;
+  }
+  void* params[] = {&ta, &tb, &a};
+  if (ag) {
+    // CTAs wait on rows copied by other CTAs: all of them must be resident
+    cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3(grid), dim3(F8_THREADS + 64), params, F8_SMEM, stream);
+    if (e != cudaSuccess) {
+      last_error() = std::string("gemm_fp8 cooperative launch: ") + cudaGetErrorString(e);
+      return -1;
     }
-    gemm_fp8_kernel<0><<<grid, F8_THREADS, F8_SMEM, stream>>>(ta, tb, a);
   } else {
-    if (!(attr_set[1] & (1ull << dev))) {
-      cudaFuncSetAttribute(gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM);
-      attr_set[1] |= 1ull << dev;
+    cudaError_t e = cudaLaunchKernel(kern, dim3(grid), dim3(F8_THREADS), params, F8_SMEM, stream);
+    if (e != cudaSuccess) {
+      last_error() = std::string("gemm_fp8 launch: ") + cudaGetErrorString(e);
+      return -1;
     }
-    gemm_fp8_kernel<1><<<grid, F8_THREADS, F8_SMEM, stream>>>(ta, tb, a);
   }
   return check_launch("gemm_fp8");
 }
@@ -410,4 +564,14 @@ extern "C" int lk_quant_128x128(const void* w, int64_t ldw, int N, int K, void* 
   dim3 grid(K / 128, (N + 127) / 128);
   quant_128x128_kernel<<<grid, 256, 0, s>>>((const __nv_bfloat16*)w, ldw, N, K, (uint8_t*)q, (uint8_t*)qt, scale);
   return check_launch("quant_128x128");
+}
+
+extern "C" int lk_dequant_1x128(const void* q, int M, int K, int fmt, const float* scale, void* x, int64_t ldx,
+                                cudaStream_t s) {
+  LK_REQUIRE(K % 128 == 0 && ldx % 8 == 0, "dequant_1x128: K % 128, ldx % 8");
+  const int64_t n8 = (int64_t)M * K / 8;
+  if (n8 == 0) return 0;
+  const int grid = (int)std::min<int64_t>((n8 + 255) / 256, 8 * num_sms());
+  dequant_1x128_kernel<<<grid, 256, 0, s>>>((const uint8_t*)q, M, K, fmt, scale, (__nv_bfloat16*)x, ldx);
+  return check_launch("dequant_1x128");
 }

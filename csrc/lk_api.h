@@ -159,11 +159,26 @@ typedef struct LkGemmFp8Desc {
   const void* r;  // optional residual (bf16, pitch ldr)
   int64_t ldr;
   int* status;
+  // Fused collectives (at most one): all-gather of A on first use - every
+  // rank's ag_rows_per_rank fp8 rows (ag_rows[p], pitch K) and scales
+  // (ag_scales[p], [K/128][ag_rows_per_rank]) are copied into a / sa (DEVICE
+  // pointer arrays of `world` entries; ag_count int scratch [M/128]); or
+  // reduce-scatter epilogue - bf16 row m goes to rptrs[m / rs_rows] at row
+  // rank * rs_rows + m % rs_rows (pitch ldd).
+  const void* const* ag_rows;
+  const float* const* ag_scales;
+  int ag_rows_per_rank;
+  int* ag_count;
+  void* const* rptrs;
+  int rs_rows;
+  int rank, world;
 } LkGemmFp8Desc;
 int lk_gemm_fp8(const LkGemmFp8Desc* desc, cudaStream_t stream);
 // x bf16 [M, K] -> q fp8 [M, K] (fmt 0 e4m3 / 1 e5m2) + scale [K/128][M]
 int lk_quant_1x128(const void* x, int64_t ldx, int M, int K, int fmt, void* q, int64_t ldq, float* scale,
                    cudaStream_t s);
+// q fp8 [M, K] with scale [K/128][M] -> x bf16 [M, ldx]
+int lk_dequant_1x128(const void* q, int M, int K, int fmt, const float* scale, void* x, int64_t ldx, cudaStream_t s);
 // w bf16 [N, K] -> q e4m3 [N, K], optional qt = q^T [K, N], scale [ceil(N/128)][K/128]
 int lk_quant_128x128(const void* w, int64_t ldw, int N, int K, void* q, void* qt, float* scale, cudaStream_t s);
 

@@ -227,6 +227,9 @@ class TPComm:
         self.stage = [CM.SymBuffer(R * D, torch.bfloat16, self.device, self.group) for _ in range(2)]
         self.recv = [CM.SymBuffer(max_tokens * D, torch.bfloat16, self.device, self.group) for _ in range(2)]
         self.stats = CM.SymBuffer(max_tokens * 4, torch.float32, self.device, self.group)
+        # fp8 staging (created on first use): e4m3 rows [R, D] and their 1x128 scales [D/128, R]
+        self.stage8: List = []
+        self.sscale: List = []
         self.count = torch.zeros(max_tokens // 128, dtype=torch.int32, device=self.device)
         self._nccl_tmp: Dict[Tuple[int, int], torch.Tensor] = {}
         self._tmaps: Dict[Tuple[int, int, int], torch.Tensor] = {}
@@ -244,6 +247,41 @@ class TPComm:
         if self.comm == "nccl":
             return  # NCCL collectives synchronise by themselves
         self.pc.barrier(SLOT_TP)
+
+    # ------------------------------------------------ fp8 (K2) variants
+    def _fp8_bufs(self) -> None:
+        if not self.stage8:
+            R, D = self.max_tokens // self.tp, self.cfg.hidden_dim
+            self.stage8 = [CM.SymBuffer(R * D, torch.uint8, self.device, self.group) for _ in range(2)]
+            self.sscale = [CM.SymBuffer((D // 128) * R, torch.float32, self.device, self.group) for _ in range(2)]
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)
+
+    def publish_fp8(self, k: int, rows: torch.Tensor) -> None:
+        """Quantise this rank's staging rows (bf16 [R, D]) into fp8 staging k."""
+        self._fp8_bufs()
+        R, D = rows.shape
+        q = self.stage8[k].local[:R * D].view(R, D)
+        sc = self.sscale[k].local[:(D // 128) * R].view(D // 128, R)
+        C().quant_1x128(rows, 0, q, sc)
+
+    def ag_gemm_fp8(self, k: int, dst8: torch.Tensor, dsts: torch.Tensor, w8, out: torch.Tensor) -> None:
+        """dst8 / dsts <- all-gather of every rank's fp8 staging rows / scales; out = dst . W^T
+        (block-scaled fp8), the gather fused into the GEMM."""
+        T, K = dst8.shape
+        R = T // self.tp
+        C().gemm_fp8_comm(dst8, dsts, 0, w8.q, w8.scale, out, status(self.device), self.rank, self.tp,
+                          self.stage8[k].ptrs, self.sscale[k].ptrs, R, self.count, None, 0, 0)
+
+    def gemm_rs_fp8(self, k: int, a: torch.Tensor, w8) -> None:
+        """a (bf16, quantised here to e4m3 1x128) . W^T as block-scaled fp8, the bf16 rows
+        stored straight into their owner's receive buffer k (reduce-scatter epilogue)."""
+        from ..ops.fp8 import quantize_1x128
+        T = a.shape[0]
+        R, Nc = T // self.tp, w8.N
+        q, sc = quantize_1x128(a)
+        C().gemm_fp8_comm(q, sc, 0, w8.q, w8.scale, None, status(self.device), self.rank, self.tp,
+                          None, None, 0, None, self.recv[k].ptrs, R, Nc)
 
     # --------------------------------------------------- K16 AG -> GEMM
     def ag_gemm(self, k: int, dst: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
@@ -346,7 +384,7 @@ class TPComm:
 
 # ------------------------------------------------------------------- model
 class _TPWorkspace:
-    def __init__(self, cfg: TransformerConfig, tp: int, B: int, S: int, device):
+    def __init__(self, cfg: TransformerConfig, tp: int, B: int, S: int, device, fp8: bool = False):
         T = B * S
         R = T // tp
         D = cfg.hidden_dim
@@ -362,8 +400,19 @@ class _TPWorkspace:
         self.rstd1 = [torch.empty(R, **f32) for _ in range(L)]
         self.rstd2 = [torch.empty(R, **f32) for _ in range(L)]
         self.rstdf = torch.empty(R, **f32)
-        self.xn1 = [torch.empty(T, D, **bf) for _ in range(L)]        # gathered normalised inputs
-        self.xn2 = [torch.empty(T, D, **bf) for _ in range(L)]
+        if fp8:
+            # gathered normalised inputs as e4m3 + 1x128 scales; bf16 copies are
+            # rebuilt (dequantised) right before each weight-gradient GEMM
+            u8 = dict(dtype=torch.uint8, device=device)
+            self.xn1_8 = [torch.empty(T, D, **u8) for _ in range(L)]
+            self.xn2_8 = [torch.empty(T, D, **u8) for _ in range(L)]
+            self.xn1_s = [torch.empty(D // 128, T, **f32) for _ in range(L)]
+            self.xn2_s = [torch.empty(D // 128, T, **f32) for _ in range(L)]
+            self.xn_deq = torch.empty(T, D, **bf)
+            self.xn1 = self.xn2 = None
+        else:
+            self.xn1 = [torch.empty(T, D, **bf) for _ in range(L)]    # gathered normalised inputs
+            self.xn2 = [torch.empty(T, D, **bf) for _ in range(L)]
         self.xf = torch.empty(T, D, **bf)
         self.qkv = [torch.empty(T, ql + 2 * kvl, **bf) for _ in range(L)]
         self.o = [torch.empty(T, ql, **bf) for _ in range(L)]
@@ -388,8 +437,16 @@ class TPLlamaModel:
     accumulator [sum of token losses, count] - identical on every rank."""
 
     def __init__(self, cfg: TransformerConfig, comm: TPComm, params: Optional[TPParams] = None,
-                 seed: int = 1234, grads: Optional[TPParams] = None):
+                 seed: int = 1234, grads: Optional[TPParams] = None, fp8: bool = False):
+        """fp8: the four projections of every layer run as block-scaled fp8 GEMMs
+        (e4m3 activations in 1x128 blocks, e4m3 weights in 128x128 blocks) with the
+        all-gather / reduce-scatter fused in (the gather moves fp8 rows + scales,
+        half the bf16 bytes); backward data-gradient GEMMs and weight gradients stay
+        bf16, the latter on the dequantised forward inputs."""
         self.cfg = cfg
+        self.fp8 = fp8
+        if fp8 and comm.comm != "p2p":
+            raise ValueError("the fp8 tensor-parallel path runs on the peer-memory kernels (comm='p2p')")
         self.comm = comm
         self.tp, self.rank = comm.tp, comm.rank
         self.device = comm.device
@@ -410,7 +467,7 @@ class TPLlamaModel:
                 raise ValueError(f"micro-batch of {B * S} tokens exceeds the TP buffers ({self.comm.max_tokens})")
             if S > self.rope.shape[0]:
                 self.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
-            ws = _TPWorkspace(self.cfg, self.tp, B, S, self.device)
+            ws = _TPWorkspace(self.cfg, self.tp, B, S, self.device, fp8=self.fp8)
             self._ws[(B, S)] = ws
         return ws
 
@@ -431,8 +488,15 @@ class TPLlamaModel:
         ids_local = ids.reshape(-1)[self.rank * R:(self.rank + 1) * R]
         E.embedding_fwd(ids_local, self._p("embed"), out=ws.h[0])
         N.rmsnorm_fwd(ws.h[0], self._p("layers.0.attn_norm"), eps, y=c.stage_view(0, R, D), rstd=ws.rstd1[0])
+        if self.fp8:
+            from ..ops.fp8 import Fp8Weight
+            self._w8 = {f"layers.{i}.{t}": Fp8Weight(self._p(f"layers.{i}.{t}"), transpose=False)
+                        for i in range(cfg.num_layers) for t in ("wqkv", "wo", "wgu", "wdown")}
         for i in range(cfg.num_layers):
             p = f"layers.{i}."
+            if self.fp8:
+                self._layer_fwd_fp8(i, ws)
+                continue
             c.barrier()
             c.ag_gemm(0, ws.xn1[i], self._p(p + "wqkv"), ws.qkv[i])
             E.rope_(ws.qkv[i], 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S)
@@ -450,6 +514,37 @@ class TPLlamaModel:
                      rstd=ws.rstdf if last else ws.rstd1[i + 1], eps=eps)
         c.barrier()
         c.ag_gemm(0, ws.xf, self._p("lm_head"), ws.logits)
+
+    def _layer_fwd_fp8(self, i: int, ws: _TPWorkspace) -> None:
+        cfg, c = self.cfg, self.comm
+        R, D, eps = ws.R, cfg.hidden_dim, cfg.norm_eps
+        Hl, Hkvl = cfg.num_heads // self.tp, cfg.num_kv_heads // self.tp
+        p = f"layers.{i}."
+        c.publish_fp8(0, c.stage_view(0, R, D))
+        c.barrier()
+        c.ag_gemm_fp8(0, ws.xn1_8[i], ws.xn1_s[i], self._w8[p + "wqkv"], ws.qkv[i])
+        E.rope_(ws.qkv[i], 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S)
+        A.attention_fwd(ws.qkv[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim, causal=True, out=ws.o[i], lse=ws.lse[i])
+        c.gemm_rs_fp8(0, ws.o[i], self._w8[p + "wo"])
+        c.rs_sum(0, ws.hmid[i], resid=ws.h[i], gamma=self._p(p + "ffn_norm"), y=c.stage_view(1, R, D),
+                 rstd=ws.rstd2[i], eps=eps)
+        c.publish_fp8(1, c.stage_view(1, R, D))
+        c.barrier()
+        c.ag_gemm_fp8(1, ws.xn2_8[i], ws.xn2_s[i], self._w8[p + "wgu"], ws.gu[i])
+        E.swiglu_fwd(ws.gu[i], ws.act[i])
+        c.gemm_rs_fp8(1, ws.act[i], self._w8[p + "wdown"])
+        last = i == cfg.num_layers - 1
+        nxt = "final_norm" if last else f"layers.{i + 1}.attn_norm"
+        c.rs_sum(1, ws.h[i + 1], resid=ws.hmid[i], gamma=self._p(nxt), y=c.stage_view(0, R, D),
+                 rstd=ws.rstdf if last else ws.rstd1[i + 1], eps=eps)
+
+    def _xn_bf16(self, ws: _TPWorkspace, which: int, i: int) -> torch.Tensor:
+        """The gathered normalised input of layer i (1: attention, 2: FFN) as bf16."""
+        if not self.fp8:
+            return ws.xn1[i] if which == 1 else ws.xn2[i]
+        q, sc = (ws.xn1_8[i], ws.xn1_s[i]) if which == 1 else (ws.xn2_8[i], ws.xn2_s[i])
+        C().dequant_1x128(q, 0, sc, ws.xn_deq)
+        return ws.xn_deq
 
     # ----------------------------------------------------- forward+backward
     @torch.no_grad()
@@ -486,7 +581,7 @@ class TPLlamaModel:
             c.ag_gemm(k, ws.dfull, self._p(p + "wdown").t(), ws.dact)
             self._wgrad(ws.dfull, ws.act[i], p + "wdown")
             E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
-            self._wgrad(ws.dgu, ws.xn2[i], p + "wgu")
+            self._wgrad(ws.dgu, self._xn_bf16(ws, 2, i), p + "wgu")
             c.gemm_rs(0, ws.dgu, self._p(p + "wgu").t())
             c.rs_sum(0, ws.dx)
             dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
@@ -500,7 +595,7 @@ class TPLlamaModel:
             A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim,
                             causal=True, dqkv=ws.dqkv)
             E.rope_(ws.dqkv, 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S, inverse=True)
-            self._wgrad(ws.dqkv, ws.xn1[i], p + "wqkv")
+            self._wgrad(ws.dqkv, self._xn_bf16(ws, 1, i), p + "wqkv")
             c.gemm_rs(1, ws.dqkv, self._p(p + "wqkv").t())
             c.rs_sum(1, ws.dx)
             dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
@@ -530,7 +625,7 @@ class TPTrainer:
     device, then AdamW over this rank's local parameters."""
 
     def __init__(self, cfg: TransformerConfig, tc, *, micro_batch: int, seq_len: int, device=None,
-                 group=None, comm: str = "p2p", seed: int = 1234):
+                 group=None, comm: str = "p2p", seed: int = 1234, fp8: bool = False):
         from ..ops import optim as O
         from ..train.optimizer import FusedAdamW
         self.cfg, self.tc = cfg, tc
@@ -542,7 +637,7 @@ class TPTrainer:
         # fp32 gradients in symmetric memory: the replicated prefix is summed in place over peers
         self.gbuf = CM.SymBuffer(params.numel, torch.float32, self.device, self.comm.group)
         grads = params.like(torch.float32, buffer=self.gbuf.local)
-        self.model = TPLlamaModel(cfg, self.comm, params, grads=grads)
+        self.model = TPLlamaModel(cfg, self.comm, params, grads=grads, fp8=fp8)
         self.params, self.grads = params, grads
         self.master = params.flat.float()
         self.opt = FusedAdamW(self.master, params.segments(), lr=tc.lr, betas=(tc.beta1, tc.beta2),

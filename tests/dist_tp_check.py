@@ -119,6 +119,65 @@ def check_ops(rank, world, res):
     check_status()
 
 
+def check_fp8(rank, world, res):
+    """fp8 (K2) with the collectives fused: gather of e4m3 rows + scales, and the
+    reduce-scatter epilogue, against unfused fp8 GEMMs + NCCL; then the TP model
+    with fp8 projections against the bf16 TP model."""
+    from lora_kernel_b200.ops import fp8 as F
+    cfg = TransformerConfig(**CFG)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    T = 256 * world
+    R, D = T // world, cfg.hidden_dim
+    comm = TP.TPComm(cfg, T, dev)
+    g = torch.Generator(device=dev).manual_seed(200 + rank)
+    mine = torch.randn(R, D, device=dev, generator=g).bfloat16()
+    gw = torch.Generator(device=dev).manual_seed(9)
+    w8 = F.Fp8Weight((torch.randn(384, D, device=dev, generator=gw) * 0.05).bfloat16(), transpose=False)
+    comm.publish_fp8(0, mine)
+    comm.barrier()
+    dst8 = torch.empty(T, D, dtype=torch.uint8, device=dev)
+    dsts = torch.empty(D // 128, T, dtype=torch.float32, device=dev)
+    out = torch.empty(T, 384, dtype=torch.bfloat16, device=dev)
+    comm.ag_gemm_fp8(0, dst8, dsts, w8, out)
+    torch.cuda.synchronize()
+    q, sc = F.quantize_1x128(mine)
+    allq = [torch.empty_like(q) for _ in range(world)]
+    alls = [torch.empty_like(sc) for _ in range(world)]
+    dist.all_gather(allq, q)
+    dist.all_gather(alls, sc)
+    fq, fs = torch.cat(allq), torch.cat(alls, dim=1).contiguous()
+    res["fp8_ag_rows_exact"] = bool(torch.equal(dst8, fq)) and bool(torch.equal(dsts, fs))
+    ref = F.gemm_fp8(fq, fs, w8.q, w8.scale)
+    res["fp8_ag_gemm_err"] = rel(out, ref)
+    # reduce-scatter epilogue
+    a = (torch.randn(T, 256, device=dev, generator=g)).bfloat16()
+    wo8 = F.Fp8Weight((torch.randn(D, 256, device=dev, generator=gw) * 0.05).bfloat16(), transpose=False)
+    comm.gemm_rs_fp8(0, a, wo8)
+    hout = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    comm.rs_sum(0, hout)
+    part = F.linear_fp8(a, wo8).float()
+    dist.all_reduce(part)
+    torch.cuda.synchronize()
+    res["fp8_rs_err"] = rel(hout, part[rank * R:(rank + 1) * R])
+    # model: fp8 projections vs bf16
+    B, S = 2, 128
+    gt = torch.Generator().manual_seed(11)
+    tok = torch.randint(0, cfg.vocab_size, (B, S + 1), generator=gt).cuda()
+    ids, tg = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+    outs = []
+    for fp8 in (False, True):
+        c2 = TP.TPComm(cfg, B * S, dev)
+        params = TP.TPParams(cfg, world, rank, dev)
+        params.init_(5, cfg.init_std)
+        m = TP.TPLlamaModel(cfg, c2, params, fp8=fp8)
+        acc = m.forward_backward(ids, tg, grad_scale=1.0 / tg.numel(), overwrite_grads=True)
+        torch.cuda.synchronize()
+        outs.append((acc.clone(), m.grads.flat.clone()))
+    check_status()
+    res["fp8_model_loss_rel"] = abs(outs[1][0][0].item() - outs[0][0][0].item()) / outs[0][0][0].item()
+    res["fp8_model_grad_rel"] = rel(outs[1][1], outs[0][1])
+
+
 def _single_gpu(cfg, ids, tg, seed):
     from lora_kernel_b200.models.llama import LlamaModel
     m = LlamaModel(cfg, "cuda", seed=seed)
@@ -186,6 +245,8 @@ def main():
     elif what == "model":
         check_model(rank, world, res, "p2p")
         check_model(rank, world, res, "nccl")
+    elif what == "fp8":
+        check_fp8(rank, world, res)
     elif what == "train":
         check_train(rank, world, res, "p2p")
         check_train(rank, world, res, "nccl")

@@ -59,3 +59,12 @@ def test_tp_trainer(tmp_path):
     # every rank computes the same loss (row-loss atomics may add in a different order)
     a0, a1 = res[0]["train.p2p.losses"], res[1]["train.p2p.losses"]
     assert max(abs(x - y) for x, y in zip(a0, a1)) < 1e-4 * a0[0], (a0, a1)
+
+
+def test_tp_fp8_fused_paths(tmp_path):
+    for res in _run("fp8", tmp_path):
+        assert res["fp8_ag_rows_exact"], res
+        assert res["fp8_ag_gemm_err"] < 1e-3, res
+        assert res["fp8_rs_err"] < 1e-2, res
+        assert res["fp8_model_loss_rel"] < 3e-2, res
+        assert res["fp8_model_grad_rel"] < 0.25, res
