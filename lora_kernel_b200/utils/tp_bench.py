@@ -183,9 +183,9 @@ def bench_ops(cfg, B, S, iters, warmup, rank0):
     return results
 
 
-def bench_step(cfg, tc, B, S, accum, steps, warmup, comm, rank0):
+def bench_step(cfg, tc, B, S, accum, steps, warmup, comm, rank0, fp8=False):
     from ..parallel.tp import TPTrainer
-    tr = TPTrainer(cfg, tc, micro_batch=B, seq_len=S, comm=comm, seed=tc.seed)
+    tr = TPTrainer(cfg, tc, micro_batch=B, seq_len=S, comm=comm, seed=tc.seed, fp8=fp8)
     g = torch.Generator().manual_seed(0)
     tok = torch.randint(0, cfg.vocab_size, (accum, B, S + 1), generator=g).cuda()
     batches = [(tok[i, :, :-1].contiguous(), tok[i, :, 1:].contiguous()) for i in range(accum)]
@@ -205,10 +205,12 @@ def bench_step(cfg, tc, B, S, accum, steps, warmup, comm, rank0):
     loss = (acc[0] / acc[1]).item()
     tokens = accum * B * S  # the TP group shares one batch
     res = {"metric": "train tokens/sec", "value": round(tokens / ms * 1e3, 1), "unit": "tokens/s",
-           "ms_per_step": round(ms, 2), "comm": comm, "n_gpus": dist.get_world_size(),
+           "ms_per_step": round(ms, 2), "comm": comm + ("+fp8" if fp8 else ""), "n_gpus": dist.get_world_size(),
            "config": {"model": f"Llama-style {cfg.num_layers} layers d{cfg.hidden_dim}",
                       "global_batch": accum * B, "seq_len": S, "parallelism": f"tp{dist.get_world_size()}",
-                      "micro_batch": B, "accum": accum}, "dtype": "bf16", "loss": round(loss, 4)}
+                      "micro_batch": B, "accum": accum},
+           "dtype": "fp8 e4m3 projections (1x128 / 128x128 scales), bf16 rest" if fp8 else "bf16",
+           "loss": round(loss, 4), "nvls": bool(tr.comm.pc.nvls)}
     if rank0:
         print(json.dumps(res), flush=True)
     del tr
@@ -229,6 +231,7 @@ def main(argv=None):
     ap.add_argument("--step", action="store_true")
     ap.add_argument("--comm", default="p2p,nccl")
     ap.add_argument("--diag", action="store_true")
+    ap.add_argument("--fp8", action="store_true", help="also run the block-scaled fp8 TP step (p2p)")
     a = ap.parse_args(argv)
     from ..config import get_preset
     from ..parallel.comm import init_distributed
@@ -246,6 +249,8 @@ def main(argv=None):
     if a.step:
         for comm in a.comm.split(","):
             bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, comm, rank == 0)
+        if a.fp8:
+            bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, "p2p", rank == 0, fp8=True)
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
