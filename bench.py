@@ -40,7 +40,7 @@ sys.path.insert(0, HERE)
 
 METRIC = "train tokens/sec (max over ranks) at 1/2/4/8 B200; serve output tok/s + p50 TTFT"
 MODEL_NAME = "Llama-style 1.1B (22 layers, d 2048, 32 heads/4 KV heads, ffn 5632, vocab 32000)"
-BASELINE_VALUE = None  # the reference publishes no GPU number for this workload
+PUBLISHED_VALUE = None  # the reference publishes no GPU number for this workload
 
 
 class ClockSampler:
@@ -250,7 +250,7 @@ def main():
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
         "scaling": "weak",
-        "vs_baseline": (round(value / BASELINE_VALUE, 3) if BASELINE_VALUE else None),
+        "vs_baseline": (round(value / PUBLISHED_VALUE, 3) if PUBLISHED_VALUE else None),
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids, N(0,0.02) random-init weights)",
         "impl": args.impl,

@@ -16,8 +16,8 @@ runner call is broadcast over a CPU (gloo) group to the other ranks, whose
 `worker_loop` executes the same call on their shard, so every rank launches
 the same kernels in the same order.
 
-Reference: the reference serves from one process without tensor parallelism
-(include/serving/*, SURVEY call stack 3.4); its TP layers
+Reference: the reference's serving stack (include/api/serving_production.hpp)
+runs in one process without tensor parallelism; its TP layers
 (include/distributed/tensor_parallel.hpp:14-104) are forward-only matmul
 splits with an all-reduce.
 """
