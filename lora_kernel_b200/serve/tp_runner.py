@@ -144,8 +144,14 @@ class TPModelRunner(ModelRunner):
         mine = torch.stack([val.double(), tok.double()], 1)
         allp = torch.empty(self.tp, n, 2, dtype=torch.float64, device=logits.device)
         dist.all_gather_into_tensor(allp, mine, group=self.comm.group)
-        best = allp[:, :, 0].argmax(0)  # first maximum = lowest rank = lowest id on ties
-        return allp[best, torch.arange(n, device=logits.device), 1].long()
+        return pick_global(allp)
+
+
+def pick_global(allp: torch.Tensor) -> torch.Tensor:
+    """allp [ranks, rows, (score, token id)] -> the token of the best score per row;
+    ties go to the lowest rank, i.e. the lowest token id (slices are in rank order)."""
+    best = allp[:, :, 0].argmax(0)  # argmax returns the first maximum
+    return allp[best, torch.arange(allp.shape[1], device=allp.device), 1].long()
 
 
 class RunnerProxy:

@@ -108,3 +108,41 @@ def test_tp_config_checks():
     TP.check_tp_config(cfg, 2)
     with pytest.raises(ValueError):
         TP.check_tp_config(cfg, 4)  # 2 KV heads cannot split 4 ways
+
+
+def test_dp_shard_to_flat_deltas():
+    """The sharded AdamW writes master element o of a rank's shard to flat element
+    o + delta of its chunk: every owned parameter piece maps back onto itself."""
+    from lora_kernel_b200.ops.optim import make_chunks
+    cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=512,
+                            vocab_size=512, num_layers=3)
+    for world in (2, 4):
+        for rank in range(world):
+            L = ShardLayout(cfg, world, rank)
+            flat = torch.arange(L.total, dtype=torch.float64)
+            shard = L.extract_shard(flat)
+            segs = []
+            for s_off, n, decay in L.shard_segments():
+                g = next(g for g in L.names if L.shard_off[g] <= s_off < L.shard_off[g] + L.chunk[g])
+                a0, _ = L.owned(g)
+                segs.append((s_off, n, decay, a0 - L.shard_off[g]))
+            ch = make_chunks(segs, chunk=97)
+            for start, length, _, d64 in ch.tolist():
+                assert torch.equal(shard[start:start + length], flat[start + 64 * d64:start + 64 * d64 + length])
+
+
+def test_vocab_parallel_pick_matches_global_argmax():
+    from lora_kernel_b200.serve.tp_runner import pick_global
+    g = torch.Generator().manual_seed(0)
+    V, ranks, rows = 64, 4, 5
+    scores = torch.randn(rows, V, generator=g).to(torch.bfloat16).float()
+    scores[2, 10] = scores[2, 40] = scores[2].max() + 1  # a tie across slices
+    Vl = V // ranks
+    allp = torch.empty(ranks, rows, 2, dtype=torch.float64)
+    for r in range(ranks):
+        sl = scores[:, r * Vl:(r + 1) * Vl]
+        v, i = sl.max(1)  # first maximum inside the slice
+        allp[r, :, 0] = v.double()
+        allp[r, :, 1] = (i + r * Vl).double()
+    assert pick_global(allp).tolist() == scores.argmax(1).tolist()
+    assert pick_global(allp)[2].item() == 10
