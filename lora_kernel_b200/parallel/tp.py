@@ -645,7 +645,7 @@ class TPTrainer:
                               dynamic_loss_scale=tc.dynamic_loss_scale,
                               init_loss_scale=tc.init_loss_scale, ema_decay=tc.ema_decay)
         self.n_rep = params.n_rep
-        self.partial = torch.zeros(256, dtype=torch.float32, device=self.device)
+        self.partial = torch.zeros(2048, dtype=torch.float32, device=self.device)
         self._O = O
         self.micro = 0
 
@@ -667,14 +667,14 @@ class TPTrainer:
             # replicated grads: one-shot peer all-reduce + their sum-of-squares partials
             if c.comm == "nccl":
                 dist.all_reduce(self.gbuf.local[:self.n_rep], group=c.group)
-                P[128:].zero_()
-                C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[128:])
-                P[128:].div_(self.tp)  # every rank holds the same replicated grads
+                P[1024:].zero_()
+                C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[1024:])
+                P[1024:].div_(self.tp)  # every rank holds the same replicated grads
             else:
-                c.pc.allreduce_sum_(self.gbuf, self.n_rep, P[128:])
+                c.pc.allreduce_sum_(self.gbuf, self.n_rep, P[1024:])
         else:
-            C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[128:])
-        C().grad_norm_partials(self.gbuf.local[self.n_rep:], P[:128])
+            C().grad_norm_partials(self.gbuf.local[:self.n_rep], P[1024:])
+        C().grad_norm_partials(self.gbuf.local[self.n_rep:], P[:1024])
         o = self.opt
         s = o.scaler
         if self.tp > 1 and c.comm != "nccl":

@@ -48,7 +48,7 @@ from ..models.params import FlatParams, build_layout
 from ..train.optimizer import FusedAdamW
 from . import comm as CM
 
-NP = 128  # sum-of-squares partial slots per group
+NP = 1024  # sum-of-squares partial slots per group (one per reduction CTA: the grid is not capped below the SM count)
 
 
 class ShardLayout:

@@ -31,7 +31,7 @@ def main(argv=None):
     dev = torch.device("cuda", local)
     pc = CM.PeerComm(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    part = torch.zeros(128, device=dev)
+    part = torch.zeros(1024, device=dev)
     for mb in (int(x) for x in a.sizes_mb.split(",")):
         n = (mb << 20) // 4
         buf = CM.SymBuffer(n, torch.float32, dev)

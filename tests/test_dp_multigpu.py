@@ -27,6 +27,8 @@ def test_dp_matches_single_gpu(stage, mode, tmp_path):
     if mode.endswith("-nonvls"):  # the one-shot P2P kernels instead of multimem
         env["LK_NVLS"] = "0"
         mode = mode.split("-")[0]
+    elif mode == "p2p":  # exercise the multimem kernels even on 2 ranks
+        env["LK_NVLS"] = "1"
     port = random.randint(20000, 40000)
     cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(port),
