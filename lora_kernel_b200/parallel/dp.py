@@ -169,6 +169,8 @@ class DataParallelTrainer:
 
     # -------------------------------------------------------------- stepping
     def _optimizer_step(self):
+        if getattr(self, "pre_optimizer", None) is not None:
+            self.pre_optimizer(self.grads.flat if self.stage == 0 else self.shard_grads)
         o = self.opt
         s = o.scaler
         if self.mode == "p2p":

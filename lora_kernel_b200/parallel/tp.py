@@ -648,6 +648,21 @@ class TPTrainer:
         self.partial = torch.zeros(2048, dtype=torch.float32, device=self.device)
         self._O = O
         self.micro = 0
+        # the train.trainer.Trainer interface (same as the data-parallel trainers)
+        self.loss_acc = torch.zeros(2, dtype=torch.float32, device=self.device)
+        self.accum_steps = max(1, tc.grad_accum_steps)
+        self.pre_optimizer = None
+        self._opt_steps = 0
+
+    def micro_step_async(self, ids: torch.Tensor, targets: torch.Tensor) -> None:
+        """One micro-batch (the same [B, S] batch on every rank); the optimizer
+        steps after grad_accum_steps of them.  Loss sums go to self.loss_acc."""
+        self.micro_step(ids, targets, 1.0 / (ids.numel() * self.accum_steps), self.loss_acc)
+        if self.micro == self.accum_steps:
+            self.optimizer_step()
+
+    def current_step(self) -> int:
+        return self._opt_steps
 
     def set_learning_rate(self, lr: float) -> None:
         self.opt.set_lr(lr)
@@ -663,6 +678,8 @@ class TPTrainer:
     def optimizer_step(self) -> None:
         c = self.comm
         P = self.partial
+        if self.pre_optimizer is not None:
+            self.pre_optimizer(self.gbuf.local)
         if self.tp > 1:
             # replicated grads: one-shot peer all-reduce + their sum-of-squares partials
             if c.comm == "nccl":
@@ -687,6 +704,7 @@ class TPTrainer:
             o.finalize(P)
         o.apply(self.gbuf.local, self.params.flat)
         self.micro = 0
+        self._opt_steps += 1
 
     def train_step(self, batches) -> torch.Tensor:
         """batches: list of (ids, targets) [B, S] micro-batches (full batch on

@@ -63,12 +63,31 @@ class Trainer:
             self.model = Transformer(cfg, self.device, seed=tc.seed)
             self.pipe = TrainingPipeline(self.model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
             self.align = 64
+        par = rc.parallel
+        self.tp = self.world > 1 and par.tp > 1
+        if self.world == 1:
+            pass
+        elif self.tp:
+            # tensor (+ sequence) parallelism over every rank: they share one batch
+            if par.tp != self.world:
+                raise ValueError(f"tensor parallelism spans the whole job: tp={par.tp} but {self.world} ranks")
+            if tc.checkpoint_dir:
+                raise NotImplementedError("checkpoints of the tensor-parallel trainer are not supported; "
+                                          "use TPTrainer.full_state_dict() to export the weights")
+            from ..parallel.tp import TPTrainer
+            self.pipe = TPTrainer(cfg, tc, micro_batch=tc.micro_batch, seq_len=tc.seq_len, device=self.device,
+                                  fp8=par.fp8, seed=tc.seed)
+            self.align = 64
+        elif par.zero_stage in (0, 1, 2):
+            from ..parallel.dp import DataParallelTrainer
+            self.pipe = DataParallelTrainer(cfg, tc, zero_stage=par.zero_stage, device=self.device)
+            self.align = self.pipe.L.align
         else:
             from ..parallel.zero import Zero3Trainer
             self.pipe = Zero3Trainer(cfg, tc, device=self.device)
             self.align = self.pipe.L.align
-        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed, self.rank,
-                                            fixed=tc.fixed_batch)
+        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed,
+                                            0 if self.tp else self.rank, fixed=tc.fixed_batch)
         self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
                                   barrier=(dist.barrier if self.world > 1 else None))
                      if tc.checkpoint_dir else None)
@@ -102,8 +121,12 @@ class Trainer:
             t["ema"] = o.ema
         return t
 
+    def _dp_full_optimizer(self) -> bool:
+        """Data parallelism with ZeRO stage 0: every rank holds the whole optimizer state."""
+        return getattr(self.pipe, "stage", 3) == 0
+
     def _ranges(self) -> List[Tuple[int, int]]:
-        if self.world == 1:
+        if self.world == 1 or self._dp_full_optimizer():
             return [(0, self.pipe.engine.params.numel)]
         L = self.pipe.L
         return [(L.owned(g)[0], L.owned(g)[0] + L.chunk[g]) for g in L.names]
@@ -135,7 +158,9 @@ class Trainer:
                 if name not in flat or (name == "ema" and o.ema is None):
                     continue
                 full = remap_flat(flat[name], index["layout"], mine)
-                if self.world == 1:
+                if name == "p32":
+                    full_p32 = full
+                if self.world == 1 or self._dp_full_optimizer():
                     dst_full = full
                 else:
                     dst_full = self.pipe.L.extract_shard(full)
@@ -143,8 +168,10 @@ class Trainer:
             o.state.copy_(flat["state"].to(self.device))
             if self.world == 1:
                 self.pipe.engine.params.flat.copy_(o.p32.to(torch.bfloat16))
-            else:
+            elif hasattr(self.pipe, "shard_p16"):
                 self.pipe.shard_p16.copy_(o.p32.to(torch.bfloat16))
+            else:  # data parallel: every rank holds the full bf16 parameters
+                self.pipe.params.flat.copy_(full_p32.to(self.device, torch.bfloat16))
         st = Checkpointer.trainer_state(path)
         self.step = int(st["step"])
         self.data.load_state(st.get("data", {}))
@@ -159,7 +186,7 @@ class Trainer:
             if p:
                 self.load_checkpoint(p)
         self._install_signals()
-        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * self.world
+        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if self.tp else self.world)
         t_last, s_last = time.perf_counter(), self.step
         while self.step < total:
             if self.hb is not None:
