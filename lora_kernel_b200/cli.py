@@ -73,14 +73,43 @@ def cmd_serve(a):
     from .serve.server import serve
     rc = load_config(a.config, a.preset, _overrides(a.set))
     cfg = rc.model
+    kv, weights = a.kv or rc.quant.kv_cache, a.weights or rc.quant.weights
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # tensor-parallel serving under torchrun: rank 0 runs the HTTP server and
+        # the scheduler, every rank its weight / KV-head shard
+        import torch.distributed as dist
+        from .parallel.comm import init_distributed
+        from .serve.tp_runner import RunnerProxy, build_tp_runner, worker_loop
+        if a.checkpoint:
+            raise NotImplementedError("tensor-parallel serving starts from seeded weights; "
+                                      "load a checkpoint on one GPU")
+        rank, _, _ = init_distributed("nccl", timeout_s=3600)
+        sc = rc.serve
+        runner, ctrl = build_tp_runner(cfg, rc.train.seed, weights=weights, kv_dtype=kv,
+                                       group_size=rc.quant.group_size, block_size=sc.block_size,
+                                       max_model_len=sc.max_model_len,
+                                       max_rows=max(sc.max_num_batched_tokens, sc.max_num_seqs),
+                                       cuda_graphs=sc.cuda_graphs, max_batch=sc.max_num_seqs)
+        if rank != 0:
+            worker_loop(runner, ctrl)
+            dist.destroy_process_group()
+            return
+        proxy = RunnerProxy(runner, ctrl)
+        eng = LLMEngine(cfg, None, sc, kv_dtype=kv, weights=weights, runner=proxy)
+        try:
+            serve(eng, host=a.host or sc.host, port=a.port or sc.port,
+                  api_keys=tuple(sc.api_keys), rate_limit_rps=sc.rate_limit_rps)
+        finally:
+            proxy.stop()
+            dist.destroy_process_group()
+        return
     params = FlatParams(cfg, "cuda")
     if a.checkpoint:
         from .train.checkpoint import load_model_safetensors
         params.load_reference_state_dict({k: v.cuda() for k, v in load_model_safetensors(a.checkpoint).items()})
     else:
         params.init_(rc.train.seed, cfg.init_std)
-    eng = LLMEngine(cfg, params, rc.serve, kv_dtype=a.kv or rc.quant.kv_cache,
-                    weights=a.weights or rc.quant.weights, group_size=rc.quant.group_size)
+    eng = LLMEngine(cfg, params, rc.serve, kv_dtype=kv, weights=weights, group_size=rc.quant.group_size)
     serve(eng, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
           api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps)
 
