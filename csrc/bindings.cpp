@@ -451,6 +451,54 @@ void cross_entropy_vp(torch::Tensor logits, torch::Tensor targets, torch::Tensor
   check(lk_cross_entropy_vp(&d, stream()));
 }
 
+// ------------------------------------------------------ GELU, LayerNorm
+void gelu_fwd(torch::Tensor x, torch::Tensor y) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(y, "y", torch::kBFloat16);
+  TORCH_CHECK(x.numel() == y.numel(), "gelu: sizes");
+  check(lk_gelu_fwd(x.data_ptr(), y.data_ptr(), x.numel(), stream()));
+}
+
+void gelu_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor dx) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(dy, "dy", torch::kBFloat16);
+  need_contig(dx, "dx", torch::kBFloat16);
+  TORCH_CHECK(x.numel() == dy.numel() && x.numel() == dx.numel(), "gelu: sizes");
+  check(lk_gelu_bwd(x.data_ptr(), dy.data_ptr(), dx.data_ptr(), x.numel(), stream()));
+}
+
+void layernorm_fwd(torch::Tensor x, torch::Tensor gamma, torch::Tensor beta, torch::Tensor y, torch::Tensor mean,
+                   torch::Tensor rstd, double eps) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(gamma, "gamma", torch::kBFloat16);
+  need_contig(beta, "beta", torch::kBFloat16);
+  need_contig(y, "y", torch::kBFloat16);
+  need_contig(mean, "mean", torch::kFloat32);
+  need_contig(rstd, "rstd", torch::kFloat32);
+  const int D = (int)x.size(-1), M = (int)(x.numel() / D);
+  TORCH_CHECK(gamma.numel() == D && beta.numel() == D && mean.numel() >= M && rstd.numel() >= M, "layernorm: shapes");
+  check(lk_layernorm_fwd(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), y.data_ptr(), mean.data_ptr<float>(),
+                         rstd.data_ptr<float>(), M, D, (float)eps, stream()));
+}
+
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::Tensor mean, torch::Tensor rstd,
+                   torch::Tensor dx, torch::Tensor dgamma, torch::Tensor dbeta) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(dy, "dy", torch::kBFloat16);
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(gamma, "gamma", torch::kBFloat16);
+  need_contig(dx, "dx", torch::kBFloat16);
+  need_contig(dgamma, "dgamma", torch::kFloat32);
+  need_contig(dbeta, "dbeta", torch::kFloat32);
+  const int D = (int)x.size(-1), M = (int)(x.numel() / D);
+  check(lk_layernorm_bwd(dy.data_ptr(), x.data_ptr(), gamma.data_ptr(), mean.data_ptr<float>(),
+                         rstd.data_ptr<float>(), dx.data_ptr(), dgamma.data_ptr<float>(), dbeta.data_ptr<float>(),
+                         M, D, stream()));
+}
+
 // ------------------------------------------------------------- RMSNorm
 void rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res, torch::Tensor gamma,
                  torch::Tensor y, c10::optional<torch::Tensor> h_out,
@@ -904,6 +952,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_vp", &cross_entropy_vp);
   m.def("launch_count", []() { return (int64_t)lk_launch_count(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("gelu_fwd", &gelu_fwd);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rmsnorm_bwd_partial_rows", &rmsnorm_bwd_partial_rows);
   m.def("rope", &rope);

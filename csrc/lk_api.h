@@ -206,6 +206,16 @@ typedef struct LkRsSumDesc {
 } LkRsSumDesc;
 int lk_rs_sum(const LkRsSumDesc* d, cudaStream_t s);
 
+// ------------------------------------------- GELU (tanh form) and LayerNorm
+int lk_gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t s);
+int lk_gelu_bwd(const void* x, const void* dy, void* dx, int64_t n, cudaStream_t s);
+// y = (x - mean) * rstd * gamma + beta (bf16 [M, D], D = 256 x {1,2,4,8,16}); mean / rstd fp32 [M]
+int lk_layernorm_fwd(const void* x, const void* gamma, const void* beta, void* y, float* mean, float* rstd,
+                     int M, int D, float eps, cudaStream_t s);
+// dx (bf16); dgamma / dbeta (fp32 [D]) are ADDED to
+int lk_layernorm_bwd(const void* dy, const void* x, const void* gamma, const float* mean, const float* rstd,
+                     void* dx, float* dgamma, float* dbeta, int M, int D, cudaStream_t s);
+
 // ------------------------------------------------------------ K9 cross-entropy
 typedef struct LkCeDesc {
   void* logits;  // [T, V] bf16, overwritten with the gradient when write_grad

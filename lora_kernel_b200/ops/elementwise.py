@@ -64,3 +64,18 @@ def embedding_bwd(ids: torch.Tensor, dy: torch.Tensor, dW: torch.Tensor) -> torc
     require_device(dW)
     C().embedding_bwd(ids.reshape(-1), dy, dW)
     return dW
+
+
+def gelu_fwd(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """GELU, tanh form (bf16)."""
+    require_device(x)
+    out = torch.empty_like(x) if out is None else out
+    C().gelu_fwd(x, out)
+    return out
+
+
+def gelu_bwd(x: torch.Tensor, dy: torch.Tensor, dx: Optional[torch.Tensor] = None) -> torch.Tensor:
+    require_device(x)
+    dx = torch.empty_like(x) if dx is None else dx
+    C().gelu_bwd(x, dy, dx)
+    return dx

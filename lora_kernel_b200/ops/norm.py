@@ -47,3 +47,24 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor, rstd: to
     C().rmsnorm_bwd(dy, x, gamma, rstd, dres, dx, dgamma, _partial(x.numel() // D, D, x.device),
                     bool(accumulate))
     return dx
+
+
+def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5):
+    """LayerNorm with affine gamma / beta (bf16).  Returns (y, mean, rstd)."""
+    require_device(x)
+    D = x.shape[-1]
+    M = x.numel() // D
+    y = torch.empty_like(x)
+    mean = torch.empty(M, dtype=torch.float32, device=x.device)
+    rstd = torch.empty(M, dtype=torch.float32, device=x.device)
+    C().layernorm_fwd(x, gamma, beta, y, mean, rstd, float(eps))
+    return y, mean, rstd
+
+
+def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor, mean: torch.Tensor,
+                  rstd: torch.Tensor, dgamma: torch.Tensor, dbeta: torch.Tensor) -> torch.Tensor:
+    """dx; the parameter gradients are added into dgamma / dbeta (fp32)."""
+    require_device(x)
+    dx = torch.empty_like(x)
+    C().layernorm_bwd(dy, x, gamma, mean, rstd, dx, dgamma, dbeta)
+    return dx

@@ -238,3 +238,41 @@ def test_adamw_and_finalize():
     optim.adamw_(p, gs2, m, v, chunks, st, p16=p16)
     assert torch.equal(p, before)
     assert st[optim.ST_SKIP].item() == 1 and st[optim.ST_LOSS_SCALE].item() == scale / 2
+
+
+def test_gelu_fwd_bwd_vs_fp32():
+    from lora_kernel_b200.ops import elementwise as E
+    torch.manual_seed(0)
+    x = (torch.randn(300, 1024, device="cuda") * 3).bfloat16()
+    dy = torch.randn_like(x)
+    xf = x.float().requires_grad_(True)
+    ref = torch.nn.functional.gelu(xf, approximate="tanh")
+    ref.backward(dy.float())
+    y = E.gelu_fwd(x)
+    dx = E.gelu_bwd(x, dy)
+    torch.cuda.synchronize()
+    assert ((y.float() - ref).abs() <= 1e-2 * ref.abs() + 1e-2).all()
+    assert ((dx.float() - xf.grad).norm() / xf.grad.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("D", [256, 1024, 4096])
+def test_layernorm_fwd_bwd_vs_fp32(D):
+    from lora_kernel_b200.ops import norm as N
+    torch.manual_seed(1)
+    M = 333
+    x = (torch.randn(M, D, device="cuda") * 2 + 0.5).bfloat16()
+    g = (1 + 0.2 * torch.randn(D, device="cuda")).bfloat16()
+    b = (0.1 * torch.randn(D, device="cuda")).bfloat16()
+    dy = torch.randn(M, D, device="cuda").bfloat16()
+    xf, gf, bf = (t.float().requires_grad_(True) for t in (x, g, b))
+    ref = torch.nn.functional.layer_norm(xf, (D,), gf, bf, 1e-5)
+    ref.backward(dy.float())
+    y, mean, rstd = N.layernorm_fwd(x, g, b, 1e-5)
+    dgamma = torch.zeros(D, device="cuda")
+    dbeta = torch.zeros(D, device="cuda")
+    dx = N.layernorm_bwd(dy, x, g, mean, rstd, dgamma, dbeta)
+    torch.cuda.synchronize()
+    rel = lambda a, r: ((a.float() - r).norm() / r.norm()).item()  # noqa: E731
+    assert rel(y, ref.detach()) < 1e-2
+    assert rel(dx, xf.grad) < 2e-2
+    assert rel(dgamma, gf.grad) < 1e-3 and rel(dbeta, bf.grad) < 1e-3
