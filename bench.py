@@ -19,8 +19,9 @@ stream; the reported time is the max over ranks.  Every step streams several
 GB of weights and activations (far larger than the 126 MB L2), so no explicit
 L2 flush is added.  SM clocks and throttle reasons are sampled with nvidia-smi
 during the timed region.  A second, end-to-end pass times K more steps through
-the public API with the step's token ids copied from pinned host memory and
-the loss read back to the host every step.
+the public API: the native token loader fills page-locked host slots on its
+worker threads, each step copies its ids and targets to the device in one
+transfer, and the loss is read back to the host every step.
 """
 from __future__ import annotations
 
@@ -219,19 +220,22 @@ def main():
     tokens_per_step = B * S * world
     value = tokens_per_step / (ms / 1e3)
 
-    # ---- end-to-end through the public API: H2D of inputs, D2H of the loss
+    # ---- end-to-end through the public API: the native loader fills page-locked
+    # slots on host threads, one H2D copy per step moves ids|targets, the loss
+    # is read back to the host every step
+    from lora_kernel_b200.utils.data import NativeTokens
+    loader = NativeTokens(V, B, S, seed=tc.seed, rank=rank, world=world, depth=6)
     h2d = 0
     d2h = 0
-    staging = torch.empty(B, S + 1, dtype=torch.int64, device="cuda")
     losses = []
+    loader.next_device("cuda")  # first fill outside the timed loop
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
-        hb = host_ids[i % n_batches]
-        staging.copy_(hb, non_blocking=True)
-        h2d += hb.numel() * hb.element_size()
-        loss = trainer.train_step(staging[:, :-1], staging[:, 1:])
+        x, y = loader.next_device("cuda")
+        h2d += loader.bytes_per_batch()
+        loss = trainer.train_step(x, y)
         d2h += 8
         losses.append(loss)
     torch.cuda.synchronize()
@@ -252,7 +256,7 @@ def main():
         "scaling": "weak",
         "vs_baseline": (round(value / PUBLISHED_VALUE, 3) if PUBLISHED_VALUE else None),
         "dtype": "bf16",
-        "data": "synthetic (uniform random token ids, N(0,0.02) random-init weights)",
+        "data": "synthetic (uniform random token ids from the native loader, N(0,0.02) random-init weights)",
         "impl": args.impl,
         "config": {"model": MODEL_NAME, "global_batch": B * world, "micro_batch_per_gpu": B,
                    "seq_len": S, "parallelism": f"zero3-dp{world}",

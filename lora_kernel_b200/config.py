@@ -107,6 +107,9 @@ class TrainConfig:
     max_consecutive_skips: int = 20
     log_every: int = 10
     fixed_batch: bool = False  # reuse one seeded batch every step (the CPU demo's data)
+    data_path: str = ""  # flat uint16/uint32 token file; empty = synthetic uniform ids
+    data_dtype: str = "uint16"
+    loader_threads: int = 4  # native loader fill workers
     recompute_activations: bool = False  # activation checkpointing: re-run each layer's forward in the backward
 
 

@@ -28,7 +28,6 @@ import json
 import os
 import shutil
 import threading
-import zlib
 from typing import Dict, List, Optional, Tuple
 
 import torch
@@ -36,13 +35,18 @@ from safetensors.torch import load_file, save_file
 
 
 def _crc(path: str) -> int:
+    """CRC-32 of a file (zlib's polynomial), chunks checksummed in parallel by
+    the native runtime."""
+    from .. import _rt
     c = 0
+    buf = bytearray(1 << 28)
+    mv = memoryview(buf)
     with open(path, "rb") as f:
         while True:
-            b = f.read(1 << 24)
-            if not b:
+            n = f.readinto(buf)
+            if not n:
                 return c
-            c = zlib.crc32(b, c)
+            c = _rt.crc32(mv[:n], c)
 
 
 def latest(root: str) -> Optional[str]:

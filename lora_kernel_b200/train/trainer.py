@@ -26,7 +26,7 @@ import torch.distributed as dist
 from ..config import RunConfig, to_dict
 from ..models.params import FlatParams, build_layout
 from ..parallel.fault import FaultInjector, HeartbeatMonitor
-from ..utils.data import SyntheticTokens
+from ..utils.data import NativeTokens
 from ..utils.logging import get_logger, log_fields
 from .checkpoint import Checkpointer, latest
 from .schedules import lr_at
@@ -86,8 +86,11 @@ class Trainer:
             from ..parallel.zero import Zero3Trainer
             self.pipe = Zero3Trainer(cfg, tc, device=self.device)
             self.align = self.pipe.L.align
-        self.data = data or SyntheticTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed,
-                                            0 if self.tp else self.rank, fixed=tc.fixed_batch)
+        # tensor parallelism: every rank reads the same batch
+        self.data = data or NativeTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed,
+                                         0 if self.tp else self.rank, 1 if self.tp else self.world,
+                                         path=tc.data_path or None, dtype=tc.data_dtype,
+                                         threads=tc.loader_threads, fixed=tc.fixed_batch)
         self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
                                   barrier=(dist.barrier if self.world > 1 else None))
                      if tc.checkpoint_dir else None)
@@ -197,9 +200,13 @@ class Trainer:
                                               tc.min_lr_ratio))
             self.pipe.loss_acc.zero_()
             for _ in range(tc.grad_accum_steps):
-                x, y = self.data.next()
-                self.pipe.micro_step_async(x.to(self.device, non_blocking=True),
-                                           y.to(self.device, non_blocking=True))
+                if hasattr(self.data, "next_device"):
+                    x, y = self.data.next_device(self.device)
+                else:
+                    x, y = self.data.next()
+                    x = x.to(self.device, non_blocking=True)
+                    y = y.to(self.device, non_blocking=True)
+                self.pipe.micro_step_async(x, y)
             self.step += 1
             o = self.pipe.opt
             if self.step % tc.log_every == 0 or self.step == total:

@@ -1,7 +1,10 @@
 """Token data sources.
 
-SyntheticTokens: uniform random ids in [0, vocab) from a seeded generator per
-rank (the benchmarks' data), with next-token targets.  MemmapTokens: a flat
+NativeTokens: the C++ loader (csrc/runtime/token_loader.cpp): worker threads
+fill a ring of page-locked host slots ahead of the step, synthetic or from a
+memmap'd token file, each slot one contiguous ids|targets pair that a single
+host-to-device copy moves.  SyntheticTokens: uniform random ids in [0, vocab)
+from a seeded torch generator per rank, with next-token targets.  MemmapTokens: a flat
 uint16 / uint32 token file read through numpy.memmap, sharded across data-
 parallel ranks by contiguous windows.  CurriculumScheduler: sequence-length
 warm-up.  Each source keeps a cursor so a checkpoint can resume the stream.
@@ -12,10 +15,121 @@ random tokens regardless of the file), StreamDataset and CurriculumScheduler
 """
 from __future__ import annotations
 
-from typing import Tuple
+import collections
+from typing import Optional, Tuple
 
 import numpy as np
 import torch
+
+
+class NativeTokens:
+    """Prefetching token loader backed by the native runtime.
+
+    next() returns host (ids, targets) [B, S] int64 tensors that stay valid
+    for the next depth-2 calls; next_device(device) returns device tensors
+    after one asynchronous copy on the current stream (the slot goes back to
+    the producers once that copy has completed).  path=None: synthetic ids
+    uniform in [0, vocab); otherwise a flat uint16 / uint32 token file cut
+    into windows of seq+1 tokens, shuffled per epoch, sharded by rank.
+    state()/load_state() carry the batch cursor for checkpoint resume."""
+
+    def __init__(self, vocab: int, batch: int, seq: int, seed: int = 0, rank: int = 0, world: int = 1, *,
+                 path: Optional[str] = None, dtype: str = "uint16", depth: int = 6, threads: int = 4,
+                 shuffle: bool = True, fixed: bool = False, pin: bool = True):
+        from .. import _rt
+        if depth < 3:
+            raise ValueError("NativeTokens: depth must be >= 3")
+        tb = {"uint16": 2, "uint32": 4}[dtype]
+        self.vocab, self.batch, self.seq, self.depth = vocab, batch, seq, depth
+        self._l = _rt.TokenLoader(path or "", tb, vocab, batch, seq, rank, world, seed, depth, threads,
+                                  shuffle, fixed)
+        self._views = [self._l.slot_tensor(s, batch, seq) for s in range(depth)]
+        self._held = collections.deque()  # [slot, event or None]
+        self._pinned = False
+        if pin and torch.cuda.is_available():
+            err = torch.cuda.cudart().cudaHostRegister(self._l.arena_ptr, self._l.arena_bytes, 0)
+            self._pinned = int(err) == 0
+        self._stage = {}
+
+    @property
+    def pinned(self) -> bool:
+        return self._pinned
+
+    @property
+    def num_windows(self) -> int:
+        return self._l.num_windows
+
+    def _recycle(self, keep: int) -> None:
+        while len(self._held) > keep:
+            slot, ev = self._held.popleft()
+            if ev is not None:
+                ev.synchronize()
+            self._l.release(slot)
+
+    def _acquire(self, timeout_ms: int = 600_000) -> int:
+        slot = self._l.acquire(timeout_ms)
+        if slot < 0:
+            raise TimeoutError(f"NativeTokens: no batch within {timeout_ms} ms")
+        return slot
+
+    def next(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        # copies the caller issued from the previous slot are ordered before this event
+        if self._held and self._held[-1][1] is None and torch.cuda.is_available() and self._pinned:
+            ev = torch.cuda.Event()
+            ev.record()
+            self._held[-1][1] = ev
+        self._recycle(self.depth - 2)
+        slot = self._acquire()
+        self._held.append([slot, None])
+        v = self._views[slot]
+        return v[0], v[1]
+
+    def next_device(self, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        device = torch.device(device)
+        ring = self._stage.get(device)
+        if ring is None:
+            ring = self._stage[device] = [[torch.empty(2, self.batch, self.seq, dtype=torch.int64, device=device)
+                                           for _ in range(2)], 0]
+        self._recycle(self.depth - 2)
+        slot = self._acquire()
+        buf = ring[0][ring[1]]
+        ring[1] ^= 1
+        # same stream as the step that reads buf, so reuse two steps later is ordered
+        buf.copy_(self._views[slot], non_blocking=self._pinned)
+        ev = None
+        if device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+        self._held.append([slot, ev])
+        return buf[0], buf[1]
+
+    def bytes_per_batch(self) -> int:
+        return 2 * self.batch * self.seq * 8
+
+    def state(self) -> dict:
+        return {"cursor": self._l.cursor()}
+
+    def load_state(self, s: dict) -> None:
+        self._recycle(0)
+        self._l.seek(int(s.get("cursor", 0)))
+
+    def close(self) -> None:
+        if getattr(self, "_l", None) is None:
+            return
+        if torch.cuda.is_available() and self._held:
+            torch.cuda.synchronize()
+        self._recycle(0)
+        if self._pinned:
+            torch.cuda.cudart().cudaHostUnregister(self._l.arena_ptr)
+            self._pinned = False
+        self._views = []
+        self._l = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class SyntheticTokens:

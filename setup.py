@@ -10,7 +10,7 @@ import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -24,6 +24,7 @@ NVCC_FLAGS = [
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
 sources = [os.path.relpath(s, HERE) for s in sources]
+rt_sources = sorted(os.path.relpath(s, HERE) for s in glob.glob(os.path.join(CSRC, "runtime", "*.cpp")))
 
 setup(
     name="lora_kernel_b200",
@@ -35,7 +36,16 @@ setup(
             sources=sources,
             include_dirs=[CSRC],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        # host runtime (no device code): work-stealing pool, host arena, token
+        # loader, parallel CRC-32
+        CppExtension(
+            name="lora_kernel_b200._rt",
+            sources=rt_sources,
+            include_dirs=[os.path.join(CSRC, "runtime")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-pthread", "-fvisibility=hidden"]},
+            extra_link_args=["-pthread"],
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
