@@ -117,6 +117,7 @@ class TrainConfig:
 class ParallelConfig:
     dp: int = 1
     tp: int = 1
+    pp: int = 1  # pipeline stages (1F1B); spans every rank of the job
     zero_stage: int = 0  # 0, 1, 2, 3 (3 == FSDP)
     sequence_parallel: bool = False
     fused_collectives: bool = True

@@ -40,7 +40,8 @@ from .params import FlatParams
 
 
 class _Workspace:
-    def __init__(self, cfg: TransformerConfig, B: int, S: int, device, save: bool, recompute: bool = False):
+    def __init__(self, cfg: TransformerConfig, B: int, S: int, device, save: bool, recompute: bool = False,
+                 logits: bool = True):
         T = B * S
         D, F, V = cfg.hidden_dim, cfg.ff_dim_padded, cfg.vocab_size
         # recompute: keep every layer's input h, one slot of per-layer intermediates
@@ -62,7 +63,7 @@ class _Workspace:
         self.act = [torch.empty(T, F, **bf) for _ in range(nl)]
         self.xf = torch.empty(T, D, **bf)
         self.rstdf = torch.empty(T, **f32)
-        self.logits = torch.empty(T, V, **bf)
+        self.logits = torch.empty(T, V, **bf) if logits else None
         self.loss_acc = torch.zeros(2, **f32)
         if save:
             self.dh = torch.empty(T, D, **bf)
@@ -277,10 +278,14 @@ class LlamaModel:
         self._overwrite = False
         return acc
 
-    def _layer_bwd(self, i: int, ws: _Workspace):
+    def _layer_bwd(self, i: int, ws: _Workspace, slot: Optional[int] = None, hidx: Optional[int] = None):
+        """Backward of layer i with the running residual gradient in ws.dh.
+        slot: workspace slot of its intermediates; hidx: index of its input in
+        ws.h (both default to the whole-model positions)."""
         cfg = self.cfg
         p = f"layers.{i}."
-        s = 0 if self.recompute else i  # workspace slot of layer i's intermediates
+        s = slot if slot is not None else (0 if self.recompute else i)
+        h_in = ws.h[i if hidx is None else hidx]
         dh = ws.dh
         # FFN
         self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
@@ -296,5 +301,5 @@ class LlamaModel:
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
                 inverse=True)
         self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[s], ws.dx)
-        N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
+        N.rmsnorm_bwd(ws.dx, h_in, self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)

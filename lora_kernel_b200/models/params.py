@@ -38,6 +38,7 @@ class ParamSpec:
     group: str
     decay: bool
     init: str  # "normal" | "ones" | "zeros"
+    gidx: int = -1  # index of this tensor in the full model's layout (seeds its init)
 
     @property
     def numel(self) -> int:
@@ -51,33 +52,44 @@ def _round(n: int) -> int:
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
 
-def build_layout(cfg: TransformerConfig, group_align: int = ALIGN
+LAYER_TENSORS = 6  # attn_norm, wqkv, wo, ffn_norm, wgu, wdown
+
+
+def build_layout(cfg: TransformerConfig, group_align: int = ALIGN, layers: Optional[range] = None,
+                 embed: bool = True, head: bool = True
                  ) -> Tuple[List[ParamSpec], Dict[str, Tuple[int, int]], int]:
     """Returns (specs, group ranges {group: (start, end)}, total numel).  Every
     group is padded to a multiple of `group_align` elements (64 x world size for
-    ZeRO sharding, so each rank owns an equal, aligned chunk of every group)."""
+    ZeRO sharding, so each rank owns an equal, aligned chunk of every group).
+
+    layers / embed / head select a subset of the model (a pipeline stage):
+    layer tensors keep their global names ("layers.{i}.*") and every spec
+    records its index in the full layout, so a stage initialises exactly the
+    weights the whole model would."""
     assert group_align % ALIGN == 0
     D, V, F = cfg.hidden_dim, cfg.vocab_size, cfg.ff_dim_padded
+    layers = range(cfg.num_layers) if layers is None else layers
     specs: List[ParamSpec] = []
     groups: Dict[str, Tuple[int, int]] = OrderedDict()
     off = 0
 
-    def add(name, shape, group, decay, init):
+    def add(name, shape, group, decay, init, gidx):
         nonlocal off
-        s = ParamSpec(name, tuple(shape), off, group, decay, init)
+        s = ParamSpec(name, tuple(shape), off, group, decay, init, gidx)
         specs.append(s)
         off += _round(s.numel)
 
-    def group(name, items):
+    def group(name, items, g0):
         nonlocal off
         start = off
-        for it in items:
-            add(*it[:2], name, *it[2:])
+        for k, it in enumerate(items):
+            add(*it[:2], name, *it[2:], g0 + k)
         off = (off + group_align - 1) // group_align * group_align
         groups[name] = (start, off)
 
-    group("embed", [("embed", (V, D), True, "normal")])
-    for i in range(cfg.num_layers):
+    if embed:
+        group("embed", [("embed", (V, D), True, "normal")], 0)
+    for i in layers:
         p = f"layers.{i}."
         group(f"layers.{i}", [
             (p + "attn_norm", (D,), False, "ones"),
@@ -86,11 +98,12 @@ def build_layout(cfg: TransformerConfig, group_align: int = ALIGN
             (p + "ffn_norm", (D,), False, "ones"),
             (p + "wgu", (2 * F, D), True, "normal"),
             (p + "wdown", (D, F), True, "normal"),
-        ])
-    head = [("final_norm", (D,), False, "ones")]
-    if not cfg.tie_embeddings:
-        head.append(("lm_head", (V, D), True, "normal"))
-    group("head", head)
+        ], 1 + LAYER_TENSORS * i)
+    if head:
+        items = [("final_norm", (D,), False, "ones")]
+        if not cfg.tie_embeddings:
+            items.append(("lm_head", (V, D), True, "normal"))
+        group("head", items, 1 + LAYER_TENSORS * cfg.num_layers)
     return specs, groups, off
 
 
@@ -98,10 +111,13 @@ class FlatParams:
     """A flat buffer plus named views following `build_layout(cfg)`."""
 
     def __init__(self, cfg: TransformerConfig, device, dtype=torch.bfloat16,
-                 buffer: Optional[torch.Tensor] = None, group_align: int = ALIGN):
+                 buffer: Optional[torch.Tensor] = None, group_align: int = ALIGN,
+                 layers: Optional[range] = None, embed: bool = True, head: bool = True):
         self.cfg = cfg
         self.group_align = group_align
-        self.specs, self.groups, self.numel = build_layout(cfg, group_align)
+        self.layer_ids = range(cfg.num_layers) if layers is None else layers
+        self.has_embed, self.has_head = embed, head
+        self.specs, self.groups, self.numel = build_layout(cfg, group_align, self.layer_ids, embed, head)
         self.by_name = {s.name: s for s in self.specs}
         if buffer is None:
             buffer = torch.zeros(self.numel, dtype=dtype, device=device)
@@ -118,7 +134,7 @@ class FlatParams:
     def like(self, dtype=torch.float32, device=None) -> "FlatParams":
         return FlatParams(self.cfg, device or self.flat.device, dtype,
                           torch.zeros(self.numel, dtype=dtype, device=device or self.flat.device),
-                          self.group_align)
+                          self.group_align, self.layer_ids, self.has_embed, self.has_head)
 
     def group_of(self, name: str) -> str:
         return self.by_name[name].group
@@ -140,7 +156,8 @@ class FlatParams:
         cfg = self.cfg
         F, Fp = cfg.ff_dim, cfg.ff_dim_padded
         dev = self.flat.device
-        for idx, s in enumerate(self.specs):
+        for s in self.specs:
+            idx = s.gidx
             v = self.views[s.name]
             if s.init == "ones":
                 v.fill_(1.0)
@@ -167,8 +184,9 @@ class FlatParams:
         cfg = self.cfg
         q, kv, F = cfg.q_dim, cfg.kv_dim, cfg.ff_dim
         out: "OrderedDict[str, torch.Tensor]" = OrderedDict()
-        out["token_embedding.weight"] = self.views["embed"]
-        for i in range(cfg.num_layers):
+        if self.has_embed:
+            out["token_embedding.weight"] = self.views["embed"]
+        for i in self.layer_ids:
             p, r = f"layers.{i}.", f"blocks.{i}."
             wqkv = self.views[p + "wqkv"]
             out[r + "attn.Wq.weight"] = wqkv[:q].t()
@@ -183,17 +201,19 @@ class FlatParams:
             out[r + "ffn.Wdown.weight"] = self.views[p + "wdown"][:, :F].t()
             out[r + "rms_norm_attn.weight"] = self.views[p + "attn_norm"]
             out[r + "rms_norm_ffn.weight"] = self.views[p + "ffn_norm"]
-        out["final_norm.weight"] = self.views["final_norm"]
-        if not cfg.tie_embeddings:
-            out["lm_head.weight"] = self.views["lm_head"].t()
+        if self.has_head:
+            out["final_norm.weight"] = self.views["final_norm"]
+            if not cfg.tie_embeddings:
+                out["lm_head.weight"] = self.views["lm_head"].t()
         return out
 
     def load_reference_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
         cfg = self.cfg
         q, kv, F = cfg.q_dim, cfg.kv_dim, cfg.ff_dim
         with torch.no_grad():
-            self.views["embed"].copy_(sd["token_embedding.weight"])
-            for i in range(cfg.num_layers):
+            if self.has_embed:
+                self.views["embed"].copy_(sd["token_embedding.weight"])
+            for i in self.layer_ids:
                 p, r = f"layers.{i}.", f"blocks.{i}."
                 wqkv = self.views[p + "wqkv"]
                 wqkv[:q].copy_(sd[r + "attn.Wq.weight"].t())
@@ -214,6 +234,7 @@ class FlatParams:
                 wd[:, :F].copy_(sd[r + "ffn.Wdown.weight"].t())
                 self.views[p + "attn_norm"].copy_(sd[r + "rms_norm_attn.weight"])
                 self.views[p + "ffn_norm"].copy_(sd[r + "rms_norm_ffn.weight"])
-            self.views["final_norm"].copy_(sd["final_norm.weight"])
-            if not cfg.tie_embeddings:
-                self.views["lm_head"].copy_(sd["lm_head.weight"].t())
+            if self.has_head:
+                self.views["final_norm"].copy_(sd["final_norm.weight"])
+                if not cfg.tie_embeddings:
+                    self.views["lm_head"].copy_(sd["lm_head.weight"].t())

@@ -65,8 +65,19 @@ class Trainer:
             self.align = 64
         par = rc.parallel
         self.tp = self.world > 1 and par.tp > 1
+        self.pp = self.world > 1 and par.pp > 1
         if self.world == 1:
             pass
+        elif self.pp:
+            # pipeline stages over every rank; all ranks read the same micro-batches
+            if par.pp != self.world:
+                raise ValueError(f"pipeline parallelism spans the whole job: pp={par.pp} but {self.world} ranks")
+            if tc.checkpoint_dir:
+                raise NotImplementedError("checkpoints of the pipeline trainer are not supported; "
+                                          "use PipelineTrainer.full_state_dict() to export the weights")
+            from ..parallel.pp import PipelineTrainer
+            self.pipe = PipelineTrainer(cfg, tc, device=self.device)
+            self.align = 64
         elif self.tp:
             # tensor (+ sequence) parallelism over every rank: they share one batch
             if par.tp != self.world:
@@ -86,9 +97,10 @@ class Trainer:
             from ..parallel.zero import Zero3Trainer
             self.pipe = Zero3Trainer(cfg, tc, device=self.device)
             self.align = self.pipe.L.align
-        # tensor parallelism: every rank reads the same batch
+        # tensor and pipeline parallelism: every rank reads the same batch
+        shared = self.tp or self.pp
         self.data = data or NativeTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed,
-                                         0 if self.tp else self.rank, 1 if self.tp else self.world,
+                                         0 if shared else self.rank, 1 if shared else self.world,
                                          path=tc.data_path or None, dtype=tc.data_dtype,
                                          threads=tc.loader_threads, fixed=tc.fixed_batch)
         self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
@@ -189,7 +201,7 @@ class Trainer:
             if p:
                 self.load_checkpoint(p)
         self._install_signals()
-        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if self.tp else self.world)
+        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if (self.tp or self.pp) else self.world)
         t_last, s_last = time.perf_counter(), self.step
         while self.step < total:
             if self.hb is not None:
