@@ -107,7 +107,9 @@ def _pp_worker(rank, world, port, q):
         st = _AutogradStage([full[i] for i in parts[rank]], rank == 0, rank == world - 1, _inputs())
         run_schedule(schedule_1f1b(world, rank, M), st, rank - 1 if rank else None,
                      rank + 1 if rank < world - 1 else None)
-        grads = {i: w.grad for i, w in zip(parts[rank], st.ws)}
+        # plain lists: a tensor put on an mp queue lives in the child's shared
+        # memory, which disappears when the child exits
+        grads = {i: w.grad.tolist() for i, w in zip(parts[rank], st.ws)}
         out = [None] * world
         dist.all_gather_object(out, (grads, st.loss))
         if rank == 0:
@@ -143,7 +145,7 @@ def test_pipeline_executor_matches_unpipelined_on_gloo_ranks():
         got.update(grads)
     assert sorted(got) == list(range(L_TOTAL))
     for i in range(L_TOTAL):
-        torch.testing.assert_close(got[i], ws[i].grad, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(torch.tensor(got[i]), ws[i].grad, rtol=1e-5, atol=1e-6)
     assert abs(out[-1][1] - tot) < 1e-4 * abs(tot)
 
 
