@@ -41,6 +41,7 @@ class PrefillItem:
     start: int              # position of the chunk's first token
     slots: List[int]        # KV slots of positions [0, start + len(tokens))
     want_logits: bool       # chunk ends the prompt: sample its next token
+    all_logits: bool = False  # logits of every row of the chunk (speculative verification)
 
 
 class ModelRunner:
@@ -161,7 +162,8 @@ class ModelRunner:
     @torch.no_grad()
     def prefill(self, items: List[PrefillItem]) -> Tuple[List[int], torch.Tensor]:
         """Returns (seq ids that want a token, logits [n, vocab]) for items whose
-        chunk ends the prompt."""
+        chunk ends the prompt: one row per such item (its last token), or one
+        per chunk token for items with all_logits."""
         cfg = self.cfg
         dev = self.device
         ids, pos, slots, bounds = [], [], [], []
@@ -196,9 +198,15 @@ class ModelRunner:
         want = [k for k, it in enumerate(items) if it.want_logits]
         if not want:
             return [], torch.empty(0, cfg.vocab_size, device=dev)
-        rows = torch.tensor([bounds[k][1] - 1 for k in want], dtype=torch.int64, device=dev)
-        logits = self._head(h.index_select(0, rows).contiguous())
-        return [items[k].seq_id for k in want], logits
+        rows, ids_out = [], []
+        for k in want:
+            a, b = bounds[k]
+            r0 = a if items[k].all_logits else b - 1
+            rows += range(r0, b)
+            ids_out += [items[k].seq_id] * (b - r0)
+        rows_t = torch.tensor(rows, dtype=torch.int64, device=dev)
+        logits = self._head(h.index_select(0, rows_t).contiguous())
+        return ids_out, logits
 
     # --------------------------------------------------------------- decode
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
