@@ -4,18 +4,22 @@ Routes
   POST /v1/completions        {prompt (str | [ids]), max_tokens, temperature, top_p, stream, stop}
   POST /v1/chat/completions   {messages: [{role, content}], ...}
   GET  /v1/models, /health, /metrics (Prometheus text)
+  GET  /v1/ws                 WebSocket: JSON requests in, one JSON message per token out
 Streaming responses are server-sent events: one `data: {json}\\n\\n` per token
 (OpenAI `choices[0].text` / `choices[0].delta.content`, plus the reference
 README's `token` and `index` fields) and a final `data: [DONE]\\n\\n`.
 
-Middleware (optional): Bearer API keys or HS256 JWTs (stdlib hmac), a
-token-bucket rate limit per client, and a JSON audit log line per request.
+Middleware (optional): Bearer API keys or HS256 JWTs (stdlib hmac), role-based
+path access, HMAC request signatures, a token-bucket rate limit per client, PII
+masking of generated text and an audit log (serve/security.py); requests are
+validated before they reach the engine.
 
 The engine runs in one background thread; HTTP handlers only enqueue requests
 and await tokens pushed back through asyncio queues.
 
 Reference: RestApiServer (include/api/rest_api.hpp:24-212, canned responses),
-SSEStreamer (include/api/serving_production.hpp:111-131), JWTAuth /
+SSEStreamer (include/api/serving_production.hpp:111-131), WebSocketStreamer
+(include/api/websocket_streaming.hpp:9-33, a local queue with no socket), JWTAuth /
 TokenBucketLimiter (include/monitoring/production_monitoring.hpp:272-406).
 """
 from __future__ import annotations
@@ -28,13 +32,14 @@ import json
 import threading
 import time
 import uuid
-from typing import Dict, Optional
+from typing import Dict, List, Optional
 
-from aiohttp import web
+from aiohttp import WSMsgType, web
 
 from ..utils.logging import get_logger, log_fields
 from ..utils.metrics import REGISTRY
 from .engine import LLMEngine, SamplingParams
+from .security import AuditLog, InputValidator, PIIMasker, RequestSigner, RoleAccess
 from .tokenizer import ByteTokenizer
 
 log = get_logger("lora_kernel.serve")
@@ -137,31 +142,69 @@ class EngineWorker:
 
 
 # ------------------------------------------------------------------- the app
+WORKER_KEY = web.AppKey("worker", EngineWorker)
+
+
 def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys=(),
                jwt_secret: str = "", rate_limit_rps: float = 0.0,
-               tokenizer: Optional[ByteTokenizer] = None) -> web.Application:
+               tokenizer: Optional[ByteTokenizer] = None, *,
+               validator: Optional[InputValidator] = None, pii_filter: bool = False,
+               roles: Optional[RoleAccess] = None, signing_secret: str = "",
+               audit: Optional[AuditLog] = None) -> web.Application:
+    """OpenAI-compatible app.  Optional policies: API keys / HS256 JWT bearer
+    auth, token-bucket rate limit per client, role-based path access (JWT
+    `role` claim or the key's role), HMAC request signatures, PII masking of
+    generated text, an audit log; every request is validated (prompt length,
+    token ids, sampling parameters) before it reaches the engine."""
     tok = tokenizer or ByteTokenizer(engine.cfg.vocab_size)
     worker = EngineWorker(engine)
     bucket = TokenBucket(rate_limit_rps, max(1.0, rate_limit_rps * 2)) if rate_limit_rps > 0 else None
     keys = set(api_keys)
+    validator = validator or InputValidator(engine.cfg.vocab_size)
+    masker = PIIMasker() if pii_filter else None
+    signer = RequestSigner(signing_secret) if signing_secret else None
+
+    def _err(msg, typ, status):
+        return web.json_response({"error": {"message": msg, "type": typ}}, status=status)
+
+    async def _admit(request: web.Request, who: dict):
+        """None when the request may proceed, else the rejection response."""
+        api = request.path.startswith("/v1/")
+        if api and (keys or jwt_secret):
+            auth = request.headers.get("Authorization", "")
+            cred = auth[7:] if auth.startswith("Bearer ") else ""
+            claims = jwt_decode(cred, jwt_secret) if (jwt_secret and cred not in keys) else None
+            if not (cred in keys or claims is not None):
+                return _err("unauthorized", "auth", 401)
+            who["client"] = cred[:16]
+            if roles is not None:
+                who["role"] = roles.role_for(cred if cred in keys else None, claims)
+        elif roles is not None:
+            who["role"] = roles.default_role
+        if roles is not None and not roles.allowed(who["role"], request.path):
+            return _err(f"role {who['role']!r} may not access {request.path}", "forbidden", 403)
+        if signer is not None and api and request.method == "POST":
+            body = await request.read()  # cached: handlers read it again
+            if not signer.verify(body, request.headers.get("X-Timestamp", ""),
+                                 request.headers.get("X-Signature", "")):
+                return _err("bad or stale request signature", "auth", 401)
+        if bucket is not None and api and not bucket.allow(who["client"]):
+            return _err("rate limit exceeded", "rate_limit", 429)
+        return None
 
     @web.middleware
     async def guard(request: web.Request, handler):
-        client = request.remote or "?"
-        if request.path.startswith("/v1/") and (keys or jwt_secret):
-            auth = request.headers.get("Authorization", "")
-            cred = auth[7:] if auth.startswith("Bearer ") else ""
-            ok = cred in keys or (jwt_secret and jwt_decode(cred, jwt_secret) is not None)
-            if not ok:
-                return web.json_response({"error": {"message": "unauthorized", "type": "auth"}}, status=401)
-            client = cred[:16]
-        if bucket is not None and request.path.startswith("/v1/") and not bucket.allow(client):
-            return web.json_response({"error": {"message": "rate limit exceeded", "type": "rate_limit"}},
-                                     status=429)
+        who = {"client": request.remote or "?", "role": None}
         t0 = time.perf_counter()
-        resp = await handler(request)
-        log_fields(log, "request", path=request.path, status=resp.status, client=client,
-                   ms=round((time.perf_counter() - t0) * 1e3, 2))
+        resp = await _admit(request, who)
+        if resp is None:
+            resp = await handler(request)
+        client, role = who["client"], who["role"]
+        ms = round((time.perf_counter() - t0) * 1e3, 2)
+        log_fields(log, "request", path=request.path, status=resp.status, client=client, ms=ms)
+        if audit is not None:
+            audit.record(client=client, role=role, path=request.path, method=request.method,
+                         status=resp.status, ms=ms)
         return resp
 
     app = web.Application(middlewares=[guard])
@@ -187,9 +230,20 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
             await resp.prepare(request)
             idx = 0
+            toks: List[int] = []
+            sent = 0
             while True:
                 t, done, reason = await q.get()
-                text = tok.decode([t])
+                if masker is None:
+                    text = tok.decode([t])
+                else:
+                    # mask the whole text so far; release all but the last 64
+                    # characters (a pattern shorter than that is final once it
+                    # is out of the window)
+                    toks.append(t)
+                    full = masker.mask(tok.decode(toks))
+                    upto = len(full) if done else max(sent, len(full) - 64)
+                    text, sent = full[sent:upto], upto
                 choice = {"index": 0, "finish_reason": reason if done else None}
                 if chat:
                     choice["delta"] = {"content": text}
@@ -211,6 +265,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             if done:
                 break
         text = tok.decode(out)
+        if masker is not None:
+            text = masker.mask(text)
         choice = {"index": 0, "finish_reason": reason}
         if chat:
             choice["message"] = {"role": "assistant", "content": text}
@@ -229,12 +285,11 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             return web.json_response({"error": {"message": "invalid JSON", "type": "invalid_request"}}, status=400)
         prompt = body.get("prompt", "")
         ids = prompt if isinstance(prompt, list) else tok.encode(str(prompt))
-        if not ids:
-            return web.json_response({"error": {"message": "empty prompt", "type": "invalid_request"}}, status=400)
         try:
+            validator.check(ids, body)
             return await _run(ids, _params(body), bool(body.get("stream")), request, chat=False)
         except ValueError as e:
-            return web.json_response({"error": {"message": str(e), "type": "invalid_request"}}, status=400)
+            return _err(str(e), "invalid_request", 400)
 
     async def chat(request: web.Request):
         try:
@@ -243,9 +298,10 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             return web.json_response({"error": {"message": "invalid JSON", "type": "invalid_request"}}, status=400)
         ids = tok.apply_chat_template(body.get("messages", []))
         try:
+            validator.check(ids, body)
             return await _run(ids, _params(body), bool(body.get("stream")), request, chat=True)
         except ValueError as e:
-            return web.json_response({"error": {"message": str(e), "type": "invalid_request"}}, status=400)
+            return _err(str(e), "invalid_request", 400)
 
     async def models(_):
         return web.json_response({"object": "list", "data": [{"id": model_name, "object": "model",
@@ -258,7 +314,49 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
     async def metrics(_):
         return web.Response(text=REGISTRY.exposition(), content_type="text/plain")
 
+    async def websocket(request: web.Request):
+        """Token streaming over one WebSocket: each text message is a request
+        ({"prompt": str | [ids], "max_tokens", "temperature", "top_p"}); the
+        server answers {"id", "token", "index", "text"} per token, then
+        {"id", "done": true, "finish_reason", "usage"}.  Requests on one
+        socket run one after another."""
+        ws = web.WebSocketResponse(heartbeat=30.0)
+        await ws.prepare(request)
+        loop = asyncio.get_running_loop()
+        async for msg in ws:
+            if msg.type != WSMsgType.TEXT:
+                continue
+            try:
+                body = json.loads(msg.data)
+                prompt = body.get("prompt", "")
+                ids = prompt if isinstance(prompt, list) else tok.encode(str(prompt))
+                validator.check(ids, body)
+                params = _params(body)
+            except (ValueError, AttributeError) as e:
+                await ws.send_json({"error": {"message": str(e), "type": "invalid_request"}})
+                continue
+            q: asyncio.Queue = asyncio.Queue()
+            worker.submit(ids, params, lambda r, t: loop.call_soon_threadsafe(
+                q.put_nowait, (t, r.finished, r.finish_reason)))
+            cid = f"ws-{uuid.uuid4().hex[:16]}"
+            out: List[int] = []
+            while True:
+                t, done, reason = await q.get()
+                out.append(t)
+                text = tok.decode([t]) if masker is None else ""
+                await ws.send_json({"id": cid, "token": t, "index": len(out) - 1, "text": text})
+                if done:
+                    break
+            final = {"id": cid, "done": True, "finish_reason": reason,
+                     "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                               "total_tokens": len(ids) + len(out)}}
+            if masker is not None:
+                final["text"] = masker.mask(tok.decode(out))
+            await ws.send_json(final)
+        return ws
+
     app.router.add_post("/v1/completions", completions)
+    app.router.add_get("/v1/ws", websocket)
     app.router.add_post("/v1/chat/completions", chat)
     app.router.add_get("/v1/models", models)
     app.router.add_get("/health", health)
@@ -268,7 +366,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         worker.stop = True
         worker.wake.set()
     app.on_shutdown.append(on_shutdown)
-    app["worker"] = worker
+    app[WORKER_KEY] = worker
     return app
 
 

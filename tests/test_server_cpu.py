@@ -138,3 +138,87 @@ def test_jwt_and_bucket_units():
     b = TokenBucket(rate=1.0, burst=2.0)
     assert b.allow("c", 0.0) and b.allow("c", 0.0) and not b.allow("c", 0.0)
     assert b.allow("c", 1.5)
+
+
+# ------------------------------------------------------- policies and WebSocket
+from lora_kernel_b200.serve.security import (AuditLog, InputValidator, PIIMasker,  # noqa: E402
+                                             RequestSigner, RoleAccess, ValidationError)
+
+
+def test_websocket_streaming():
+    async def go(c):
+        ws = await c.ws_connect("/v1/ws")
+        await ws.send_json({"prompt": [72, 73], "max_tokens": 3})
+        msgs = []
+        while True:
+            m = await ws.receive_json()
+            msgs.append(m)
+            if m.get("done"):
+                break
+        assert [m["token"] for m in msgs[:-1]] == [72, 73, 72]
+        assert [m["index"] for m in msgs[:-1]] == [0, 1, 2]
+        assert "".join(m["text"] for m in msgs[:-1]) == "HIH"
+        assert msgs[-1]["finish_reason"] == "length" and msgs[-1]["usage"]["completion_tokens"] == 3
+        # a bad request on the same socket gets an error message, the socket stays usable
+        await ws.send_json({"prompt": [999], "max_tokens": 1})
+        assert "error" in await ws.receive_json()
+        await ws.send_json({"prompt": "ok", "max_tokens": 1})
+        assert (await ws.receive_json())["token"] == ord("o")
+        await ws.close()
+    _run(go)
+
+
+def test_input_validation_rejects_bad_requests():
+    async def go(c):
+        for body in ({"prompt": [1, 2, 300], "max_tokens": 2}, {"prompt": "x", "max_tokens": 0},
+                     {"prompt": "x", "temperature": -1}, {"prompt": "x", "top_p": 1.5},
+                     {"prompt": ""}, {"prompt": "x" * 50}):
+            r = await c.post("/v1/completions", json=body)
+            assert r.status == 400, body
+    _run(go, validator=InputValidator(256, max_prompt_tokens=40))
+
+
+def test_pii_masking_in_responses():
+    m = PIIMasker()
+    assert m.mask("mail bob.smith@example.com now") == "mail [EMAIL] now"
+    assert m.mask("ssn 123-45-6789.") == "ssn [SSN]."
+    assert m.mask("card 4111 1111 1111 1111 ok") == "card [CARD] ok"
+    assert m.mask("num 4111 1111 1111 1112 ok") != "num [CARD] ok"  # fails the Luhn check
+    assert m.mask("call (555) 123-4567") == "call [PHONE]"
+    secret = "reach me at a@b.io please"
+
+    async def go(c):
+        ids = [ord(ch) for ch in secret]
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": len(ids)})
+        assert (await r.json())["choices"][0]["text"] == "reach me at [EMAIL] please"
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": len(ids), "stream": True})
+        events = [e for e in (await r.read()).decode().split("\n\n") if e and e != "data: [DONE]"]
+        text = "".join(json.loads(e[6:])["choices"][0]["text"] for e in events)
+        assert text == "reach me at [EMAIL] please"
+    _run(go, pii_filter=True)
+
+
+def test_roles_signatures_and_audit(tmp_path):
+    roles = RoleAccess({"admin": ["*"], "user": ["/v1/completions", "/v1/chat", "/v1/ws"]},
+                       key_roles={"k-admin": "admin", "k-user": "user"})
+    signer = RequestSigner("sig")
+    audit = AuditLog(str(tmp_path / "audit.jsonl"))
+
+    async def go(c):
+        body = json.dumps({"prompt": "x", "max_tokens": 1}).encode()
+        h = {"Authorization": "Bearer k-user", "Content-Type": "application/json", **signer.sign(body)}
+        assert (await c.post("/v1/completions", data=body, headers=h)).status == 200
+        bad = dict(h, **{"X-Signature": "0" * 64})
+        assert (await c.post("/v1/completions", data=body, headers=bad)).status == 401
+        stale = dict(h, **signer.sign(body, ts=time.time() - 3600))
+        assert (await c.post("/v1/completions", data=body, headers=stale)).status == 401
+        assert (await c.get("/v1/models", headers={"Authorization": "Bearer k-user"})).status == 403
+        assert (await c.get("/v1/models", headers={"Authorization": "Bearer k-admin"})).status == 200
+        tok = jwt_encode({"sub": "u", "role": "admin", "exp": time.time() + 60}, "j")
+        assert (await c.get("/v1/models", headers={"Authorization": f"Bearer {tok}"})).status == 200
+    _run(go, api_keys=("k-admin", "k-user"), jwt_secret="j", roles=roles, signing_secret="sig", audit=audit)
+    lines = [json.loads(x) for x in open(tmp_path / "audit.jsonl")]
+    assert [x["status"] for x in lines] == [200, 401, 401, 403, 200, 200]
+    assert [x["role"] for x in lines] == ["user"] * 4 + ["admin"] * 2
+    with pytest.raises(ValidationError):
+        InputValidator(10).check([11], {})
