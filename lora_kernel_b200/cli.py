@@ -103,15 +103,25 @@ def cmd_serve(a):
             proxy.stop()
             dist.destroy_process_group()
         return
-    params = FlatParams(cfg, "cuda")
-    if a.checkpoint:
-        from .train.checkpoint import load_model_safetensors
-        params.load_reference_state_dict({k: v.cuda() for k, v in load_model_safetensors(a.checkpoint).items()})
-    else:
-        params.init_(rc.train.seed, cfg.init_std)
-    eng = LLMEngine(cfg, params, rc.serve, kv_dtype=kv, weights=weights, group_size=rc.quant.group_size)
-    serve(eng, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
-          api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps)
+    import torch
+    engines = []
+    n_rep = max(1, a.replicas)
+    if n_rep > torch.cuda.device_count():
+        raise SystemExit(f"--replicas {n_rep} but {torch.cuda.device_count()} GPUs")
+    for g in range(n_rep):  # one independent engine per GPU
+        dev = f"cuda:{g}"
+        torch.cuda.set_device(g)
+        params = FlatParams(cfg, dev)
+        if a.checkpoint:
+            from .train.checkpoint import load_model_safetensors
+            params.load_reference_state_dict({k: v.to(dev) for k, v in load_model_safetensors(a.checkpoint).items()})
+        else:
+            params.init_(rc.train.seed, cfg.init_std)
+        engines.append(LLMEngine(cfg, params, rc.serve, device=dev, kv_dtype=kv, weights=weights,
+                                 group_size=rc.quant.group_size))
+    serve(engines[0] if n_rep == 1 else engines, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
+          api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps,
+          replica_policy=a.replica_policy)
 
 
 def cmd_env(_):
@@ -138,6 +148,9 @@ def main(argv=None):
     s.add_argument("--host")
     s.add_argument("--port", type=int)
     s.add_argument("--weights")
+    s.add_argument("--replicas", type=int, default=1, help="independent engines, one per GPU")
+    s.add_argument("--replica-policy", default="prefix_affinity",
+                   choices=["round_robin", "least_loaded", "prefix_affinity"])
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
     s.add_argument("--set", nargs="*")

@@ -34,6 +34,7 @@ import time
 import uuid
 from typing import Dict, List, Optional
 
+import torch
 from aiohttp import WSMsgType, web
 
 from ..utils.logging import get_logger, log_fields
@@ -111,6 +112,16 @@ class EngineWorker:
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
+    def running(self) -> int:
+        return len(self.engine.running)
+
+    def waiting(self) -> int:
+        return len(self.engine.waiting)
+
+    def shutdown(self) -> None:
+        self.stop = True
+        self.wake.set()
+
     def submit(self, prompt, params, on_token) -> int:
         with self.lock:
             rid = self.engine.add_request(prompt, params, on_token=on_token)
@@ -119,6 +130,10 @@ class EngineWorker:
         return rid
 
     def _loop(self):
+        # kernels launch on the current device's stream: make it the engine's
+        dev = getattr(getattr(self.engine, "runner", None), "device", None)
+        if isinstance(dev, torch.device) and dev.type == "cuda":
+            torch.cuda.set_device(dev)
         while not self.stop:
             if not self.engine.has_work():
                 self.wake.wait(0.05)
@@ -142,7 +157,7 @@ class EngineWorker:
 
 
 # ------------------------------------------------------------------- the app
-WORKER_KEY = web.AppKey("worker", EngineWorker)
+WORKER_KEY = web.AppKey("worker", object)
 
 
 def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys=(),
@@ -150,14 +165,22 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                tokenizer: Optional[ByteTokenizer] = None, *,
                validator: Optional[InputValidator] = None, pii_filter: bool = False,
                roles: Optional[RoleAccess] = None, signing_secret: str = "",
-               audit: Optional[AuditLog] = None) -> web.Application:
+               audit: Optional[AuditLog] = None, replica_policy: str = "least_loaded") -> web.Application:
     """OpenAI-compatible app.  Optional policies: API keys / HS256 JWT bearer
     auth, token-bucket rate limit per client, role-based path access (JWT
     `role` claim or the key's role), HMAC request signatures, PII masking of
     generated text, an audit log; every request is validated (prompt length,
-    token ids, sampling parameters) before it reaches the engine."""
+    token ids, sampling parameters) before it reaches the engine.  `engine`
+    may be a list of engines: requests are then routed over the replicas by
+    `replica_policy`."""
+    if isinstance(engine, (list, tuple)):
+        # several replicas behind one server (serve/replicas.py)
+        from .replicas import ReplicaPool
+        worker = ReplicaPool(engine, policy=replica_policy)
+        engine = engine[0]
+    else:
+        worker = EngineWorker(engine)
     tok = tokenizer or ByteTokenizer(engine.cfg.vocab_size)
-    worker = EngineWorker(engine)
     bucket = TokenBucket(rate_limit_rps, max(1.0, rate_limit_rps * 2)) if rate_limit_rps > 0 else None
     keys = set(api_keys)
     validator = validator or InputValidator(engine.cfg.vocab_size)
@@ -308,8 +331,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                                                                "owned_by": "lora_kernel_b200"}]})
 
     async def health(_):
-        return web.json_response({"status": "healthy", "running": len(engine.running),
-                                  "waiting": len(engine.waiting)})
+        return web.json_response({"status": "healthy", "running": worker.running(),
+                                  "waiting": worker.waiting()})
 
     async def metrics(_):
         return web.Response(text=REGISTRY.exposition(), content_type="text/plain")
@@ -363,8 +386,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
     app.router.add_get("/metrics", metrics)
 
     async def on_shutdown(_):
-        worker.stop = True
-        worker.wake.set()
+        worker.shutdown()
     app.on_shutdown.append(on_shutdown)
     app[WORKER_KEY] = worker
     return app

@@ -222,3 +222,42 @@ def test_roles_signatures_and_audit(tmp_path):
     assert [x["role"] for x in lines] == ["user"] * 4 + ["admin"] * 2
     with pytest.raises(ValidationError):
         InputValidator(10).check([11], {})
+
+
+def test_replica_pool_policies():
+    from lora_kernel_b200.serve.engine import SamplingParams
+    from lora_kernel_b200.serve.replicas import ReplicaPool
+    done = []
+    rr = ReplicaPool([FakeEngine() for _ in range(3)], policy="round_robin")
+    for k in range(9):
+        rr.submit([65 + k], SamplingParams(max_tokens=2), lambda r, t: done.append(r) if r.finished else None)
+    assert rr.routed == [3, 3, 3]
+    aff = ReplicaPool([FakeEngine() for _ in range(4)], policy="prefix_affinity", affinity_tokens=4, slack=100)
+    picks = {aff.pick([1, 2, 3, 4, k]) for k in range(10)}
+    assert len(picks) == 1  # shared 4-token prefix -> one replica
+    ll = ReplicaPool([FakeEngine() for _ in range(2)], policy="least_loaded")
+    ll.outstanding = [5, 1]
+    assert ll.pick([1]) == 1
+    deadline = time.time() + 10
+    while len(done) < 9 and time.time() < deadline:
+        time.sleep(0.01)
+    assert len(done) == 9 and rr.outstanding == [0, 0, 0]
+    for p in (rr, aff, ll):
+        p.shutdown()
+
+
+def test_server_over_replicas():
+    engines = [FakeEngine(), FakeEngine()]
+
+    async def go(c):
+        for k in range(4):
+            r = await c.post("/v1/completions", json={"prompt": [70 + k], "max_tokens": 2})
+            assert r.status == 200
+        assert (await (await c.get("/health")).json())["status"] == "healthy"
+
+    async def main():
+        app = create_app(engines, replica_policy="round_robin")
+        async with TestClient(TestServer(app)) as client:
+            await go(client)
+    asyncio.run(main())
+    assert engines[0].n == 2 and engines[1].n == 2
