@@ -114,7 +114,9 @@ def cmd_serve(a):
         params = FlatParams(cfg, dev)
         if a.checkpoint:
             from .train.checkpoint import load_model_safetensors
-            params.load_reference_state_dict({k: v.to(dev) for k, v in load_model_safetensors(a.checkpoint).items()})
+            from .train.crypto import key_from_env
+            sd = load_model_safetensors(a.checkpoint, key=key_from_env())
+            params.load_reference_state_dict({k: v.to(dev) for k, v in sd.items()})
         else:
             params.init_(rc.train.seed, cfg.init_std)
         engines.append(LLMEngine(cfg, params, rc.serve, device=dev, kv_dtype=kv, weights=weights,

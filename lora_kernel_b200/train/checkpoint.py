@@ -68,14 +68,37 @@ def save_model_safetensors(state: Dict[str, torch.Tensor], path: str, dtype=None
     save_file(out, path, metadata={"format": "lora_kernel_b200"})
 
 
-def load_model_safetensors(path: str) -> Dict[str, torch.Tensor]:
+def _read_safetensors(path: str, key: Optional[bytes] = None) -> Tuple[Dict[str, torch.Tensor], dict]:
+    """(tensors, metadata) of a safetensors file, decrypting it first when it
+    is an encrypted checkpoint file (train/crypto.py)."""
+    from safetensors.torch import load as load_bytes
+    from .crypto import decrypt_bytes, is_encrypted
+    if is_encrypted(path):
+        if key is None:
+            raise ValueError(f"{path} is encrypted; set LORAK_CKPT_KEY or pass the key")
+        data = decrypt_bytes(path, key)
+    else:
+        with open(path, "rb") as f:
+            data = f.read()
+    hlen = int.from_bytes(data[:8], "little")
+    meta = json.loads(data[8:8 + hlen]).get("__metadata__", {}) or {}
+    return load_bytes(data), meta
+
+
+def load_model_safetensors(path: str, key: Optional[bytes] = None) -> Dict[str, torch.Tensor]:
+    from .crypto import is_encrypted
+    if is_encrypted(path):
+        return _read_safetensors(path, key)[0]
     return load_file(path)
 
 
 class Checkpointer:
-    def __init__(self, root: str, rank: int = 0, world: int = 1, barrier=None):
+    def __init__(self, root: str, rank: int = 0, world: int = 1, barrier=None, key: Optional[bytes] = None):
+        """key: 32-byte AES-256-GCM key; every file of the checkpoint is then
+        encrypted and authenticated (train/crypto.py)."""
         self.root = root
         self.rank, self.world = rank, world
+        self.key = key
         self.barrier = barrier or (lambda: None)
         self._thread: Optional[threading.Thread] = None
         self._pending = None
@@ -104,9 +127,15 @@ class Checkpointer:
 
         def write():
             name = f"optim-rank{self.rank}-of-{self.world}.safetensors"
-            save_file(snap, os.path.join(tmp, name), metadata={"ranges": json.dumps(optim_ranges)})
+            paths = [os.path.join(tmp, name)]
+            save_file(snap, paths[0], metadata={"ranges": json.dumps(optim_ranges)})
             if msnap is not None:
-                save_file(msnap, os.path.join(tmp, "model.safetensors"), metadata={"format": "lora_kernel_b200"})
+                paths.append(os.path.join(tmp, "model.safetensors"))
+                save_file(msnap, paths[1], metadata={"format": "lora_kernel_b200"})
+            if self.key is not None:
+                from .crypto import encrypt_file
+                for p in paths:
+                    encrypt_file(p, p, self.key)
 
         self._pending = (tmp, final, step, layout, trainer_state)
         if async_save:
@@ -127,7 +156,7 @@ class Checkpointer:
         tmp, final, step, layout, trainer_state = pending
         if self.rank == 0:
             files = sorted(f for f in os.listdir(tmp) if f.endswith(".safetensors"))
-            index = {"world": self.world, "step": step, "layout": layout,
+            index = {"world": self.world, "step": step, "layout": layout, "encrypted": self.key is not None,
                      "files": {f: {"crc32": _crc(os.path.join(tmp, f))} for f in files}}
             with open(os.path.join(tmp, "trainer.json"), "w") as f:
                 json.dump(trainer_state, f, indent=1, default=str)
@@ -152,7 +181,8 @@ class Checkpointer:
         return all(_crc(os.path.join(path, n)) == m["crc32"] for n, m in index["files"].items())
 
     @staticmethod
-    def load_flat(path: str, names=("p32", "m", "v"), total: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    def load_flat(path: str, names=("p32", "m", "v"), total: Optional[int] = None,
+                  key: Optional[bytes] = None) -> Dict[str, torch.Tensor]:
         """Full flat optimizer vectors reassembled from every rank's file."""
         with open(os.path.join(path, "index.json")) as f:
             index = json.load(f)
@@ -161,19 +191,17 @@ class Checkpointer:
         for fname in sorted(index["files"]):
             if not fname.startswith("optim-rank"):
                 continue
-            from safetensors import safe_open
-            with safe_open(os.path.join(path, fname), "pt") as f:
-                ranges = json.loads(f.metadata()["ranges"])
-                for n in f.keys():
-                    if n == "state":
-                        out.setdefault("state", f.get_tensor(n))
-                        continue
-                    t = f.get_tensor(n)
-                    full = out.setdefault(n, torch.zeros(total, dtype=t.dtype))
-                    o = 0
-                    for s, e in ranges:
-                        full[s:e] = t[o:o + e - s]
-                        o += e - s
+            tensors, meta = _read_safetensors(os.path.join(path, fname), key)
+            ranges = json.loads(meta["ranges"])
+            for n, t in tensors.items():
+                if n == "state":
+                    out.setdefault("state", t)
+                    continue
+                full = out.setdefault(n, torch.zeros(total, dtype=t.dtype))
+                o = 0
+                for s, e in ranges:
+                    full[s:e] = t[o:o + e - s]
+                    o += e - s
         return out
 
     @staticmethod

@@ -103,8 +103,10 @@ class Trainer:
                                          0 if shared else self.rank, 1 if shared else self.world,
                                          path=tc.data_path or None, dtype=tc.data_dtype,
                                          threads=tc.loader_threads, fixed=tc.fixed_batch)
+        from .crypto import key_from_env
+        self.ckpt_key = key_from_env()  # LORAK_CKPT_KEY: encrypt checkpoints (AES-256-GCM)
         self.ckpt = (Checkpointer(tc.checkpoint_dir, self.rank, self.world,
-                                  barrier=(dist.barrier if self.world > 1 else None))
+                                  barrier=(dist.barrier if self.world > 1 else None), key=self.ckpt_key)
                      if tc.checkpoint_dir else None)
         self.step = 0
         self._stop = False
@@ -165,7 +167,7 @@ class Trainer:
     def load_checkpoint(self, path: str) -> None:
         with open(os.path.join(path, "index.json")) as f:
             index = json.load(f)
-        flat = Checkpointer.load_flat(path)
+        flat = Checkpointer.load_flat(path, key=self.ckpt_key)
         mine = _layout_info(self.rc.model, self.align)
         o = self.pipe.opt
         with torch.no_grad():
