@@ -1,4 +1,4 @@
-"""Command line: `python -m lora_kernel_b200 {train,bench,serve,env}`.
+"""Command line: `python -m lora_kernel_b200 {train,bench,serve,export,env}`.
 
   train  --preset NAME | --config FILE [--steps N] [--set section.key=value ...]
          (launch with torch.distributed.run for more than one GPU: ZeRO-3)
@@ -6,6 +6,8 @@
          [--kernels]                       kernel micro-benchmarks instead
          [--serve ...]                     serving load generator
   serve  --preset NAME [--port P] [--weights int4|int8|fp8|none] [--kv fp8|int8|bf16]
+         [--replicas N --replica-policy prefix_affinity|least_loaded|round_robin]
+  export --out PATH [--format gguf|hf] [--dtype bf16|f16|f32] [--checkpoint model.safetensors]
   env    versions, GPU, NVLink, extension status
 
 Mirrors the reference's train / bench / serve verbs (README.md:107-115,
@@ -126,6 +128,31 @@ def cmd_serve(a):
           replica_policy=a.replica_policy)
 
 
+def cmd_export(a):
+    """Write a model as GGUF or Hugging Face safetensors from a checkpoint
+    (model.safetensors, reference names) or from the preset's seeded weights."""
+    import torch
+    from .config import load_config
+    from .models.params import FlatParams
+    from .utils.export import export_gguf, export_hf
+    rc = load_config(a.config, a.preset, _overrides(a.set))
+    cfg = rc.model
+    if a.checkpoint:
+        from .train.checkpoint import load_model_safetensors
+        from .train.crypto import key_from_env
+        sd = load_model_safetensors(a.checkpoint, key=key_from_env())
+    else:
+        p = FlatParams(cfg, "cpu", torch.float32)
+        p.init_(rc.train.seed, cfg.init_std)
+        sd = p.to_reference_state_dict()
+    if a.format == "gguf":
+        export_gguf(sd, cfg, a.out, dtype=a.dtype)
+    else:
+        export_hf(sd, cfg, a.out, dtype={"f32": torch.float32, "f16": torch.float16,
+                                         "bf16": torch.bfloat16}[a.dtype])
+    print(json.dumps({"exported": a.out, "format": a.format, "dtype": a.dtype}))
+
+
 def cmd_env(_):
     from .utils.env import env_report
     print(json.dumps(env_report(), indent=1))
@@ -156,6 +183,14 @@ def main(argv=None):
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
     s.add_argument("--set", nargs="*")
+    x = sub.add_parser("export")
+    x.add_argument("--preset", default="cpu-demo")
+    x.add_argument("--config")
+    x.add_argument("--checkpoint", help="model.safetensors of a checkpoint (default: seeded weights)")
+    x.add_argument("--format", choices=["gguf", "hf"], default="gguf")
+    x.add_argument("--dtype", choices=["f32", "f16", "bf16"], default="bf16")
+    x.add_argument("--out", required=True)
+    x.add_argument("--set", nargs="*")
     sub.add_parser("env")
     a, rest = ap.parse_known_args(argv)
     if a.cmd == "train":
@@ -164,6 +199,8 @@ def main(argv=None):
         cmd_bench(a, rest)
     elif a.cmd == "serve":
         cmd_serve(a)
+    elif a.cmd == "export":
+        cmd_export(a)
     else:
         cmd_env(a)
 
