@@ -111,6 +111,7 @@ class TrainConfig:
     data_dtype: str = "uint16"
     loader_threads: int = 4  # native loader fill workers
     recompute_activations: bool = False  # activation checkpointing: re-run each layer's forward in the backward
+    offload_optimizer: bool = False  # fp32 master + AdamW moments in pinned host memory (train/offload.py)
 
 
 @dataclass

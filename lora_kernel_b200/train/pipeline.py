@@ -74,13 +74,24 @@ class TrainingPipeline:
         eng = model.engine
         self.engine = eng
         eng.recompute = tc.recompute_activations
-        master = eng.params.flat.float()
-        self.opt = FusedAdamW(master, eng.params.segments(decay_norms=tc.decay_norms), lr=lr,
-                              betas=(tc.beta1, tc.beta2), eps=tc.eps, weight_decay=weight_decay,
-                              max_grad_norm=max_grad_norm, dynamic_loss_scale=tc.dynamic_loss_scale,
-                              init_loss_scale=tc.init_loss_scale,
-                              growth_interval=tc.loss_scale_growth_interval,
-                              ema_decay=tc.ema_decay)
+        if tc.offload_optimizer:
+            from .offload import OffloadedAdamW
+            if tc.ema_decay > 0:
+                raise NotImplementedError("EMA with the offloaded optimizer")
+            self.opt = OffloadedAdamW(eng.params.flat.float().cpu(), eng.params.segments(decay_norms=tc.decay_norms),
+                                      eng.device, lr=lr, betas=(tc.beta1, tc.beta2), eps=tc.eps,
+                                      weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                                      dynamic_loss_scale=tc.dynamic_loss_scale,
+                                      init_loss_scale=tc.init_loss_scale,
+                                      growth_interval=tc.loss_scale_growth_interval)
+        else:
+            master = eng.params.flat.float()
+            self.opt = FusedAdamW(master, eng.params.segments(decay_norms=tc.decay_norms), lr=lr,
+                                  betas=(tc.beta1, tc.beta2), eps=tc.eps, weight_decay=weight_decay,
+                                  max_grad_norm=max_grad_norm, dynamic_loss_scale=tc.dynamic_loss_scale,
+                                  init_loss_scale=tc.init_loss_scale,
+                                  growth_interval=tc.loss_scale_growth_interval,
+                                  ema_decay=tc.ema_decay)
         self.accum_steps = max(1, tc.grad_accum_steps)
         self._micro = 0
         self._opt_steps = 0
