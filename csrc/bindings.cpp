@@ -469,6 +469,14 @@ void gelu_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor dx) {
   check(lk_gelu_bwd(x.data_ptr(), dy.data_ptr(), dx.data_ptr(), x.numel(), stream()));
 }
 
+void dropout(torch::Tensor x, torch::Tensor y, double p, int64_t seed) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kBFloat16);
+  need_contig(y, "y", torch::kBFloat16);
+  TORCH_CHECK(x.numel() == y.numel(), "dropout: sizes");
+  check(lk_dropout(x.data_ptr(), y.data_ptr(), x.numel(), (float)p, (uint64_t)seed, stream()));
+}
+
 void layernorm_fwd(torch::Tensor x, torch::Tensor gamma, torch::Tensor beta, torch::Tensor y, torch::Tensor mean,
                    torch::Tensor rstd, double eps) {
   const c10::cuda::CUDAGuard g(x.device());
@@ -953,6 +961,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", []() { return (int64_t)lk_launch_count(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("gelu_fwd", &gelu_fwd);
+  m.def("dropout", &dropout);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("layernorm_bwd", &layernorm_bwd);

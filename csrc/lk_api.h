@@ -209,6 +209,7 @@ int lk_rs_sum(const LkRsSumDesc* d, cudaStream_t s);
 // ------------------------------------------- GELU (tanh form) and LayerNorm
 int lk_gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t s);
 int lk_gelu_bwd(const void* x, const void* dy, void* dx, int64_t n, cudaStream_t s);
+int lk_dropout(const void* x, void* y, int64_t n, float p, uint64_t seed, cudaStream_t s);
 // y = (x - mean) * rstd * gamma + beta (bf16 [M, D], D = 256 x {1,2,4,8,16}); mean / rstd fp32 [M]
 int lk_layernorm_fwd(const void* x, const void* gamma, const void* beta, void* y, float* mean, float* rstd,
                      int M, int D, float eps, cudaStream_t s);

@@ -41,7 +41,7 @@ from .params import FlatParams
 
 class _Workspace:
     def __init__(self, cfg: TransformerConfig, B: int, S: int, device, save: bool, recompute: bool = False,
-                 logits: bool = True):
+                 logits: bool = True, dropout: bool = False):
         T = B * S
         D, F, V = cfg.hidden_dim, cfg.ff_dim_padded, cfg.vocab_size
         # recompute: keep every layer's input h, one slot of per-layer intermediates
@@ -55,6 +55,8 @@ class _Workspace:
         self.rstd1 = [torch.empty(T, **f32) for _ in range(nl)]
         self.qkv = [torch.empty(T, cfg.qkv_dim, **bf) for _ in range(nl)]
         self.o = [torch.empty(T, cfg.q_dim, **bf) for _ in range(nl)]
+        # dropped attention context (the attention backward needs the undropped o)
+        self.od = [torch.empty(T, cfg.q_dim, **bf) for _ in range(nl)] if dropout else None
         self.lse = [torch.empty(B, cfg.num_heads, S, **f32) for _ in range(nl)]
         self.hmid = [torch.empty(T, D, **bf) for _ in range(nl)]
         self.xn2 = [torch.empty(T, D, **bf) for _ in range(nl)]
@@ -103,6 +105,10 @@ class LlamaModel:
         self.lora = None        # optional LoRAAdapters (models/lora.py)
         self.train_base = True  # False: frozen base weights (no base weight gradients)
         self._u: Dict[Tuple[int, str], torch.Tensor] = {}
+        # dropout (training only): counter-hash masks seeded by (seed, micro-step,
+        # layer, site); the backward regenerates the same masks
+        self.dropout_seed = seed
+        self._drop_step = 0
 
     # -------------------------------------------------------------- helpers
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
@@ -111,7 +117,8 @@ class LlamaModel:
         if ws is None:
             if S > self.rope.shape[0]:
                 self.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
-            ws = _Workspace(self.cfg, B, S, self.device, save, recompute=self.recompute and save)
+            ws = _Workspace(self.cfg, B, S, self.device, save, recompute=self.recompute and save,
+                            dropout=save and self.cfg.dropout > 0)
             self._ws[key] = ws
         return ws
 
@@ -190,10 +197,18 @@ class LlamaModel:
                 G.linear_dgrad(dy, self._p(name), out=dx_out)
         self._wgrad(dy, x, name)
 
+    # -------------------------------------------------------------- dropout
+    def _drop_seed(self, i: int, site: int) -> int:
+        return ((self.dropout_seed * 1000003 + self._drop_step) * 4099 + i * 2 + site) & 0x7FFFFFFFFFFFFFFF
+
+    def _dropping(self, ws: _Workspace) -> bool:
+        return self.cfg.dropout > 0 and ws.od is not None
+
     # -------------------------------------------------------------- forward
     def _layer_fwd(self, i: int, ws: _Workspace, h_in: torch.Tensor, h_out: torch.Tensor, slot: int):
         cfg = self.cfg
         p = f"layers.{i}."
+        drop = self._dropping(ws)
         xn1, rstd1 = ws.xn1[slot], ws.rstd1[slot]
         N.rmsnorm_fwd(h_in, self._p(p + "attn_norm"), cfg.norm_eps, y=xn1, rstd=rstd1)
         qkv = ws.qkv[slot]
@@ -201,10 +216,15 @@ class LlamaModel:
         E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
         A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                         causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
+        o_in = ws.o[slot]
+        if drop:  # attention-context dropout into its own buffer
+            o_in = E.dropout(o_in, cfg.dropout, self._drop_seed(i, 0), out=ws.od[slot])
         hmid = ws.hmid[slot]
-        self._lin(i, "wo", ws.o[slot], hmid, residual=h_in, save=self._saving)
+        self._lin(i, "wo", o_in, hmid, residual=h_in, save=self._saving)
         N.rmsnorm_fwd(hmid, self._p(p + "ffn_norm"), cfg.norm_eps, y=ws.xn2[slot], rstd=ws.rstd2[slot])
         self._lin_swiglu(i, ws.xn2[slot], ws.gu[slot], ws.act[slot], save=self._saving)
+        if drop:  # FFN-hidden dropout in place (its backward reads gu, not act)
+            E.dropout(ws.act[slot], cfg.dropout, self._drop_seed(i, 1), out=ws.act[slot])
         self._lin(i, "wdown", ws.act[slot], h_out, residual=hmid, save=self._saving)
 
     def _forward(self, ids: torch.Tensor, ws: _Workspace, save: bool) -> torch.Tensor:
@@ -276,6 +296,7 @@ class LlamaModel:
             E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
         self._hook("post_backward")
         self._overwrite = False
+        self._drop_step += 1
         return acc
 
     def _layer_bwd(self, i: int, ws: _Workspace, slot: Optional[int] = None, hidx: Optional[int] = None):
@@ -287,14 +308,19 @@ class LlamaModel:
         s = slot if slot is not None else (0 if self.recompute else i)
         h_in = ws.h[i if hidx is None else hidx]
         dh = ws.dh
+        drop = self._dropping(ws)
         # FFN
         self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
+        if drop:
+            E.dropout(ws.dact, cfg.dropout, self._drop_seed(i, 1), out=ws.dact)
         E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
         self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[s], ws.dx)
         N.rmsnorm_bwd(ws.dx, ws.hmid[s], self._p(p + "ffn_norm"), ws.rstd2[s], self._g(p + "ffn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)
         # attention
-        self._lin_bwd(i, "wo", dh, ws.o[s], ws.do)
+        self._lin_bwd(i, "wo", dh, ws.od[s] if drop else ws.o[s], ws.do)
+        if drop:
+            E.dropout(ws.do, cfg.dropout, self._drop_seed(i, 0), out=ws.do)
         A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
                         cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
                         dqkv=ws.dqkv)

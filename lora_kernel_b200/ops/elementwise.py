@@ -79,3 +79,29 @@ def gelu_bwd(x: torch.Tensor, dy: torch.Tensor, dx: Optional[torch.Tensor] = Non
     dx = torch.empty_like(x) if dx is None else dx
     C().gelu_bwd(x, dy, dx)
     return dx
+
+
+def dropout(x: torch.Tensor, p: float, seed: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Inverted dropout with the counter-hash mask of csrc/dropout.cu (out may
+    be x: in place).  The same (seed, p) applied to a gradient is the exact
+    backward."""
+    require_device(x)
+    out = torch.empty_like(x) if out is None else out
+    C().dropout(x, out, float(p), int(seed) & 0x7FFFFFFFFFFFFFFF)
+    return out
+
+
+def dropout_mask_reference(n: int, p: float, seed: int) -> torch.Tensor:
+    """The kernel's keep mask recomputed on the host (uint64 arithmetic)."""
+    import numpy as np
+    M = np.uint64(0xFFFFFFFFFFFFFFFF)
+    with np.errstate(over="ignore"):
+        i = np.arange(n, dtype=np.uint64)
+        z = np.uint64(seed & 0x7FFFFFFFFFFFFFFF) ^ (i * np.uint64(0x9E3779B97F4A7C15))
+        z = (z + np.uint64(0x9E3779B97F4A7C15)) & M
+        z = ((z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)) & M
+        z = ((z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)) & M
+        z ^= z >> np.uint64(31)
+        h = (z >> np.uint64(32)).astype(np.uint64)
+    thresh = min(4294967295, int(float(np.float32(p)) * 4294967296.0))  # the kernel gets p as float
+    return torch.from_numpy(h >= np.uint64(thresh))

@@ -64,8 +64,10 @@ def attention(q, k, v, causal=True, window=0):
 
 
 def forward(params: Dict[str, torch.Tensor], cfg: TransformerConfig, ids: torch.Tensor,
-            window: int = 0) -> torch.Tensor:
-    """Logits [B, S, V] from fp32 parameters keyed by FlatParams names."""
+            window: int = 0, drop=None) -> torch.Tensor:
+    """Logits [B, S, V] from fp32 parameters keyed by FlatParams names.
+    drop(layer, site, x) -> x: optional dropout applied to the attention
+    context (site 0, [B, S, q_dim]) and the SwiGLU hidden (site 1, [B, S, F])."""
     B, S = ids.shape
     H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
     h = params["embed"][ids]
@@ -78,18 +80,22 @@ def forward(params: Dict[str, torch.Tensor], cfg: TransformerConfig, ids: torch.
         v = qkv[..., (H + KV) * Dh:].reshape(B, S, KV, Dh)
         q, k = rope(q, cfg.rope_base), rope(k, cfg.rope_base)
         o = attention(q, k, v, True, window).reshape(B, S, H * Dh)
+        if drop is not None:
+            o = drop(i, 0, o)
         h = h + o @ params[p + "wo"].t()
         x = rmsnorm(h, params[p + "ffn_norm"], cfg.norm_eps)
         wg, wu = split_gate_up(params[p + "wgu"])
         a = torch.nn.functional.silu(x @ wg.t()) * (x @ wu.t())
+        if drop is not None:
+            a = drop(i, 1, a)
         h = h + a @ params[p + "wdown"].t()
     x = rmsnorm(h, params["final_norm"], cfg.norm_eps)
     head = params["embed"] if cfg.tie_embeddings else params["lm_head"]
     return x @ head.t()
 
 
-def loss_fn(params, cfg, ids, targets, label_smoothing: float = 0.0) -> torch.Tensor:
-    logits = forward(params, cfg, ids)
+def loss_fn(params, cfg, ids, targets, label_smoothing: float = 0.0, drop=None) -> torch.Tensor:
+    logits = forward(params, cfg, ids, drop=drop)
     if logits.dtype not in (torch.float32, torch.float64):
         logits = logits.float()
     return torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]),
@@ -97,10 +103,10 @@ def loss_fn(params, cfg, ids, targets, label_smoothing: float = 0.0) -> torch.Te
                                              label_smoothing=label_smoothing)
 
 
-def loss_and_grads(params: Dict[str, torch.Tensor], cfg, ids, targets, dtype=torch.float32):
+def loss_and_grads(params: Dict[str, torch.Tensor], cfg, ids, targets, dtype=torch.float32, drop=None):
     """(loss, {name: grad}) with autograd on copies of `params` in `dtype`."""
     leaf = {k: v.detach().to(dtype).clone().requires_grad_(True) for k, v in params.items()}
-    loss = loss_fn(leaf, cfg, ids, targets)
+    loss = loss_fn(leaf, cfg, ids, targets, drop=drop)
     loss.backward()
     return loss.detach(), {k: v.grad for k, v in leaf.items()}
 

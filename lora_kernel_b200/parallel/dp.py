@@ -67,6 +67,7 @@ class DataParallelTrainer:
         self.params.init_(tc.seed, cfg.init_std)
         self.grads = FlatParams(cfg, self.device, f32, buffer=gbuf, group_align=L.align)
         self.engine = LlamaModel(cfg, self.device, params=self.params, with_grads=False)
+        self.engine.dropout_seed = tc.seed + 7919 * self.rank  # ranks see different data: decorrelate masks
         self.engine.recompute = tc.recompute_activations
         self.engine.grads = self.grads
         self.engine.hooks = self

@@ -268,7 +268,8 @@ class PipelineStageEngine:
             if S > m.rope.shape[0]:
                 from ..ops import elementwise as E
                 m.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
-            wss = [_Workspace(self.local_cfg, B, S, self.device, save=True, logits=(self.last and k == 0))
+            wss = [_Workspace(self.local_cfg, B, S, self.device, save=True, logits=(self.last and k == 0),
+                              dropout=self.cfg.dropout > 0)
                    for k in range(n)]
             for w in wss[1:]:
                 w.logits = wss[0].logits  # the last stage runs F and B of one micro-batch back to back
@@ -315,21 +316,25 @@ class PipelineStageEngine:
 
 
 class _EngineCompute(StageCompute):
-    def __init__(self, eng: PipelineStageEngine, wss, batches, loss_scale, grad_scale, acc, tc):
+    def __init__(self, eng: PipelineStageEngine, wss, batches, loss_scale, grad_scale, acc, tc, micro_base: int):
         self.eng, self.wss, self.batches = eng, wss, batches
         self.loss_scale, self.grad_scale, self.acc, self.tc = loss_scale, grad_scale, acc, tc
         self.n = len(eng.layers)
+        self.micro_base = micro_base  # global micro-batch index of mb 0 (dropout seeds)
 
     def _ws(self, mb):
         return self.wss[mb % len(self.wss)]
 
     def forward(self, mb):
         ws = self._ws(mb)
+        # the same dropout masks as the single-GPU engine's micro-step counter
+        self.eng.model._drop_step = self.micro_base + mb
         self.eng.forward(ws, self.batches[mb][0] if self.eng.first else None)
         if self.eng.last:
             self.eng.head(ws, self.batches[mb][1], self.loss_scale, self.grad_scale, self.acc, mb == 0, self.tc)
 
     def backward(self, mb):
+        self.eng.model._drop_step = self.micro_base + mb
         self.eng.backward(self._ws(mb), self.batches[mb][0] if self.eng.first else None, mb == 0)
 
     def act_out(self, mb):
@@ -378,6 +383,7 @@ class PipelineTrainer:
         self.accum_steps = max(1, tc.grad_accum_steps)
         self._pending: List[Tuple[torch.Tensor, torch.Tensor]] = []
         self._opt_steps = 0
+        self._micro_done = 0
         self.pre_optimizer: Optional[Callable] = None
 
     @property
@@ -400,7 +406,8 @@ class PipelineTrainer:
         eng = self.engine
         wss = eng.workspaces(B, S, max(1, min(self.world - self.rank, M)))
         comp = _EngineCompute(eng, wss, batches, self.opt.scaler.scale_tensor(), 1.0 / (B * S * M),
-                              self.loss_acc, self.tc)
+                              self.loss_acc, self.tc, self._micro_done)
+        self._micro_done += M
         run_schedule(schedule_1f1b(self.world, self.rank, M), comp, self.prev_rank, self.next_rank, self.group)
         g = eng.grads.flat
         if self.pre_optimizer is not None:

@@ -626,6 +626,8 @@ class TPTrainer:
 
     def __init__(self, cfg: TransformerConfig, tc, *, micro_batch: int, seq_len: int, device=None,
                  group=None, comm: str = "p2p", seed: int = 1234, fp8: bool = False):
+        if cfg.dropout > 0:
+            raise NotImplementedError("dropout in the tensor-parallel model (use data / pipeline parallelism)")
         from ..ops import optim as O
         from ..train.optimizer import FusedAdamW
         self.cfg, self.tc = cfg, tc

@@ -196,6 +196,7 @@ class Zero3Trainer:
         self.gb_count = torch.zeros((max(cfg.qkv_dim, cfg.hidden_dim, cfg.ff_dim_padded) + 127) // 128,
                                     dtype=torch.int32, device=self.device)
         self.engine = LlamaModel(cfg, self.device, params=self.params, with_grads=False)
+        self.engine.dropout_seed = tc.seed + 7919 * self.rank  # ranks see different data: decorrelate masks
         self.engine.recompute = tc.recompute_activations
         self.engine.grads = FlatParams(cfg, self.device, f32, buffer=grads_flat, group_align=L.align)
         self.engine.hooks = self
