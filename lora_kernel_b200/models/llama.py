@@ -109,14 +109,18 @@ class LlamaModel:
         # layer, site); the backward regenerates the same masks
         self.dropout_seed = seed
         self._drop_step = 0
+        # optional context-parallel attention (parallel/cp.py): ids are this rank's
+        # chunk of every sequence; RoPE uses global positions
+        self.ctx = None
 
     # -------------------------------------------------------------- helpers
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
         key = (B, S, save, self.recompute and save)
         ws = self._ws.get(key)
         if ws is None:
-            if S > self.rope.shape[0]:
-                self.rope = E.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, self.device)
+            full = S * (self.ctx.world if self.ctx is not None else 1)
+            if full > self.rope.shape[0]:
+                self.rope = E.rope_table(full, self.cfg.head_dim, self.cfg.rope_base, self.device)
             ws = _Workspace(self.cfg, B, S, self.device, save, recompute=self.recompute and save,
                             dropout=save and self.cfg.dropout > 0)
             self._ws[key] = ws
@@ -213,9 +217,14 @@ class LlamaModel:
         N.rmsnorm_fwd(h_in, self._p(p + "attn_norm"), cfg.norm_eps, y=xn1, rstd=rstd1)
         qkv = ws.qkv[slot]
         self._lin(i, "wqkv", xn1, qkv, save=self._saving)
-        E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
-        A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
-                        causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
+        if self.ctx is None:
+            E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
+            A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                            causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
+        else:
+            E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
+                    pos_offset=self.ctx.pos_offset(ws.S))
+            self.ctx.forward(qkv, ws.B, ws.S, ws.o[slot], key=(id(ws), slot), window=self.attn_window)
         o_in = ws.o[slot]
         if drop:  # attention-context dropout into its own buffer
             o_in = E.dropout(o_in, cfg.dropout, self._drop_seed(i, 0), out=ws.od[slot])
@@ -321,11 +330,16 @@ class LlamaModel:
         self._lin_bwd(i, "wo", dh, ws.od[s] if drop else ws.o[s], ws.do)
         if drop:
             E.dropout(ws.do, cfg.dropout, self._drop_seed(i, 0), out=ws.do)
-        A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
-                        cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
-                        dqkv=ws.dqkv)
+        if self.ctx is None:
+            A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
+                            cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
+                            dqkv=ws.dqkv)
+            off = 0
+        else:
+            self.ctx.backward(ws.do, ws.B, ws.S, ws.dqkv, key=(id(ws), s), window=self.attn_window)
+            off = self.ctx.pos_offset(ws.S)
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
-                inverse=True)
+                pos_offset=off, inverse=True)
         self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[s], ws.dx)
         N.rmsnorm_bwd(ws.dx, h_in, self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)

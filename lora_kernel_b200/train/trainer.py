@@ -66,8 +66,18 @@ class Trainer:
         par = rc.parallel
         self.tp = self.world > 1 and par.tp > 1
         self.pp = self.world > 1 and par.pp > 1
+        self.cp = self.world > 1 and par.cp > 1
         if self.world == 1:
             pass
+        elif self.cp:
+            # every rank takes its chunk of each sequence of the same micro-batch
+            if par.cp != self.world:
+                raise ValueError(f"context parallelism spans the whole job: cp={par.cp} but {self.world} ranks")
+            if tc.checkpoint_dir:
+                raise NotImplementedError("checkpoints of the context-parallel trainer are not supported")
+            from ..parallel.cp import ContextParallelTrainer
+            self.pipe = ContextParallelTrainer(cfg, tc, zero_stage=min(par.zero_stage, 2), device=self.device)
+            self.align = self.pipe.dp.L.align
         elif self.pp:
             # pipeline stages over every rank; all ranks read the same micro-batches
             if par.pp != self.world:
@@ -98,7 +108,7 @@ class Trainer:
             self.pipe = Zero3Trainer(cfg, tc, device=self.device)
             self.align = self.pipe.L.align
         # tensor and pipeline parallelism: every rank reads the same batch
-        shared = self.tp or self.pp
+        shared = self.tp or self.pp or self.cp
         self.data = data or NativeTokens(cfg.vocab_size, tc.micro_batch, tc.seq_len, tc.seed,
                                          0 if shared else self.rank, 1 if shared else self.world,
                                          path=tc.data_path or None, dtype=tc.data_dtype,
@@ -203,7 +213,8 @@ class Trainer:
             if p:
                 self.load_checkpoint(p)
         self._install_signals()
-        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if (self.tp or self.pp) else self.world)
+        tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if (self.tp or self.pp or self.cp)
+                                                                             else self.world)
         t_last, s_last = time.perf_counter(), self.step
         while self.step < total:
             if self.hb is not None:
