@@ -147,21 +147,30 @@ class ContextParallelTrainer:
         self.dp = DataParallelTrainer(cfg, tc, zero_stage=zero_stage, device=device, group=group, comm=comm)
         self.rank, self.world = self.dp.rank, self.dp.world
         self.dp.engine.ctx = UlyssesAttention(cfg, self.dp.group)
-        self.opt, self.loss_acc = self.dp.opt, self.dp.loss_acc
+        self.opt = self.dp.opt
+        # [loss sum, token count] over the whole micro-batches (all ranks' chunks)
+        self.loss_acc = torch.zeros(2, dtype=torch.float32, device=self.dp.device)
 
     def micro_step_async(self, ids: torch.Tensor, targets: torch.Tensor) -> None:
         """ids / targets: the FULL micro-batch [B, S] (the same on every rank)."""
+        self.dp.loss_acc.zero_()
         self.dp.micro_step_async(shard_sequence(ids, self.rank, self.world),
                                  shard_sequence(targets, self.rank, self.world))
+        dist.all_reduce(self.dp.loss_acc, group=self.dp.group)
+        self.loss_acc += self.dp.loss_acc
 
     def train_step(self, ids, targets) -> float:
         """Mean token loss of the full micro-batch (every rank returns it)."""
         self.loss_acc.zero_()
         self.micro_step_async(ids, targets)
-        tot = self.loss_acc.clone()
-        dist.all_reduce(tot, group=self.dp.group)
-        s, n = tot.tolist()
+        s, n = self.loss_acc.tolist()
         return s / max(n, 1.0)
+
+    def __getattr__(self, name):
+        # everything else (optimizer, layout, parameters, checkpoint hooks) is the data-parallel trainer's
+        if name == "dp":
+            raise AttributeError(name)
+        return getattr(self.dp, name)
 
     @property
     def pre_optimizer(self):

@@ -194,6 +194,30 @@ def simulate(stages: int, micro: int) -> Dict[str, object]:
     return {"peak_inflight": peak, "ticks": ticks}
 
 
+def stage_global_ranges(local, global_layout: dict) -> List[Tuple[int, int, int]]:
+    """(local offset, global offset, numel) of every tensor of a stage's flat
+    parameters (FlatParams) in the full model's layout ({"specs": {name:
+    [offset, numel]}}), in local order."""
+    out = []
+    for sp in local.specs:
+        g_off, n = global_layout["specs"][sp.name]
+        assert n == sp.numel, sp.name
+        out.append((sp.offset, g_off, n))
+    return out
+
+
+def gather_stage(flat_local: torch.Tensor, ranges) -> torch.Tensor:
+    """The stage's values concatenated in the order of `ranges` (padding dropped)."""
+    return torch.cat([flat_local[lo:lo + n] for lo, _, n in ranges])
+
+
+def scatter_stage(flat_global: torch.Tensor, ranges, flat_local: torch.Tensor) -> torch.Tensor:
+    """Copy the stage's tensors out of a full-layout vector into its local flat."""
+    for lo, go, n in ranges:
+        flat_local[lo:lo + n].copy_(flat_global[go:go + n])
+    return flat_local
+
+
 # --------------------------------------------------------------------------
 # executor
 # --------------------------------------------------------------------------
@@ -433,6 +457,38 @@ class PipelineTrainer:
         self.micro_step_async(ids, targets)
         s, n = self.loss_acc.tolist()
         return s / max(n, 1.0)
+
+    # ------------------------------------------------------------ checkpoints
+    def global_layout(self) -> dict:
+        from ..models.params import build_layout
+        specs, _, total = build_layout(self.cfg, 64)
+        return {"total": total, "align": 64, "specs": {s.name: [s.offset, s.numel] for s in specs}}
+
+    def checkpoint_parts(self):
+        """(full-model layout, this stage's ranges in it, optimizer tensors
+        concatenated in range order) for Checkpointer.save."""
+        lay = self.global_layout()
+        rr = stage_global_ranges(self.engine.params, lay)
+        o = self.opt
+        tensors = {n: gather_stage(getattr(o, n), rr) for n in ("p32", "m", "v")}
+        tensors["state"] = o.state
+        return lay, [(g, g + n) for _, g, n in rr], tensors
+
+    def load_checkpoint_flat(self, flat: Dict[str, torch.Tensor], saved_layout: dict) -> None:
+        """Restore this stage from full-model optimizer vectors (any alignment)."""
+        from ..train.trainer import remap_flat
+        lay = self.global_layout()
+        rr = stage_global_ranges(self.engine.params, lay)
+        o = self.opt
+        with torch.no_grad():
+            for n in ("p32", "m", "v"):
+                full = remap_flat(flat[n], saved_layout, lay)
+                scatter_stage(full.to(self.device), rr, getattr(o, n))
+            o.state.copy_(flat["state"].to(self.device))
+            self.engine.params.flat.copy_(o.p32.to(torch.bfloat16))
+
+    def reference_state_dict(self) -> Dict[str, torch.Tensor]:
+        return self.full_state_dict()
 
     def full_state_dict(self) -> Dict[str, torch.Tensor]:
         """Every stage's tensors, reference names, gathered on all ranks (CPU)."""

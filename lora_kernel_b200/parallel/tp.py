@@ -721,6 +721,35 @@ class TPTrainer:
     def check(self) -> None:
         check_status(self.device)
 
+    # ------------------------------------------------------------ checkpoints
+    def checkpoint_parts(self):
+        """Per-rank local shards laid end to end ({"kind": "tp"} layout): a
+        checkpoint restores onto the same tensor-parallel degree."""
+        n = self.master.numel()
+        lay = {"kind": "tp", "tp": self.tp, "total": self.tp * n, "align": 0, "specs": {}}
+        o = self.opt
+        t = {"p32": o.p32, "m": o.m, "v": o.v, "state": o.state}
+        return lay, [(self.rank * n, (self.rank + 1) * n)], t
+
+    def load_checkpoint_flat(self, flat, saved_layout: dict) -> None:
+        n = self.master.numel()
+        if saved_layout.get("kind") != "tp" or saved_layout.get("tp") != self.tp or saved_layout["total"] != self.tp * n:
+            raise ValueError("tensor-parallel checkpoints restore onto the same tensor-parallel degree and model")
+        o = self.opt
+        with torch.no_grad():
+            for name in ("p32", "m", "v"):
+                getattr(o, name).copy_(flat[name][self.rank * n:(self.rank + 1) * n].to(self.device))
+            o.state.copy_(flat["state"].to(self.device))
+            self.params.flat.copy_(o.p32.to(torch.bfloat16))
+
+    def reference_state_dict(self) -> "OrderedDict[str, torch.Tensor]":
+        """Reference-named full tensors ([in, out]), gathered on every rank (CPU)."""
+        from ..models.params import FlatParams
+        full = FlatParams(self.cfg, "cpu", torch.bfloat16)
+        for name, t in self.full_state_dict().items():
+            full.views[name].copy_(t.cpu())
+        return full.to_reference_state_dict()
+
     def full_state_dict(self) -> "OrderedDict[str, torch.Tensor]":
         """Engine-layout full tensors (gathered over the TP group with NCCL)."""
         out: "OrderedDict[str, torch.Tensor]" = OrderedDict()

@@ -73,8 +73,6 @@ class Trainer:
             # every rank takes its chunk of each sequence of the same micro-batch
             if par.cp != self.world:
                 raise ValueError(f"context parallelism spans the whole job: cp={par.cp} but {self.world} ranks")
-            if tc.checkpoint_dir:
-                raise NotImplementedError("checkpoints of the context-parallel trainer are not supported")
             from ..parallel.cp import ContextParallelTrainer
             self.pipe = ContextParallelTrainer(cfg, tc, zero_stage=min(par.zero_stage, 2), device=self.device)
             self.align = self.pipe.dp.L.align
@@ -82,9 +80,6 @@ class Trainer:
             # pipeline stages over every rank; all ranks read the same micro-batches
             if par.pp != self.world:
                 raise ValueError(f"pipeline parallelism spans the whole job: pp={par.pp} but {self.world} ranks")
-            if tc.checkpoint_dir:
-                raise NotImplementedError("checkpoints of the pipeline trainer are not supported; "
-                                          "use PipelineTrainer.full_state_dict() to export the weights")
             from ..parallel.pp import PipelineTrainer
             self.pipe = PipelineTrainer(cfg, tc, device=self.device)
             self.align = 64
@@ -92,9 +87,6 @@ class Trainer:
             # tensor (+ sequence) parallelism over every rank: they share one batch
             if par.tp != self.world:
                 raise ValueError(f"tensor parallelism spans the whole job: tp={par.tp} but {self.world} ranks")
-            if tc.checkpoint_dir:
-                raise NotImplementedError("checkpoints of the tensor-parallel trainer are not supported; "
-                                          "use TPTrainer.full_state_dict() to export the weights")
             from ..parallel.tp import TPTrainer
             self.pipe = TPTrainer(cfg, tc, micro_batch=tc.micro_batch, seq_len=tc.seq_len, device=self.device,
                                   fp8=par.fp8, seed=tc.seed)
@@ -162,14 +154,19 @@ class Trainer:
         if self.ckpt is None:
             return None
         cfg = self.rc.model
+        state = {"step": self.step, "data": self.data.state(), "config": to_dict(self.rc),
+                 "world": self.world, "time": time.time()}
+        if hasattr(self.pipe, "checkpoint_parts"):  # pipeline / tensor parallel
+            layout, ranges, tensors = self.pipe.checkpoint_parts()
+            sd = self.pipe.reference_state_dict()  # collective: every rank takes part
+            return self.ckpt.save(self.step, sd if self.rank == 0 else None, ranges, tensors, layout, state,
+                                  async_save=async_save)
         if self.world == 1:
             model_state = self.pipe.engine.params.to_reference_state_dict()
         else:
             full = self.pipe.full_params()
             fp = FlatParams(cfg, self.device, torch.bfloat16, buffer=full, group_align=self.align)
             model_state = fp.to_reference_state_dict() if self.rank == 0 else None
-        state = {"step": self.step, "data": self.data.state(), "config": to_dict(self.rc),
-                 "world": self.world, "time": time.time()}
         path = self.ckpt.save(self.step, model_state, self._ranges(), self._optim(),
                               _layout_info(cfg, self.align), state, async_save=async_save)
         return path
@@ -178,6 +175,10 @@ class Trainer:
         with open(os.path.join(path, "index.json")) as f:
             index = json.load(f)
         flat = Checkpointer.load_flat(path, key=self.ckpt_key)
+        if hasattr(self.pipe, "load_checkpoint_flat"):  # pipeline / tensor parallel
+            self.pipe.load_checkpoint_flat(flat, index["layout"])
+            self._restore_trainer_state(path)
+            return
         mine = _layout_info(self.rc.model, self.align)
         o = self.pipe.opt
         with torch.no_grad():
@@ -199,6 +200,9 @@ class Trainer:
                 self.pipe.shard_p16.copy_(o.p32.to(torch.bfloat16))
             else:  # data parallel: every rank holds the full bf16 parameters
                 self.pipe.params.flat.copy_(full_p32.to(self.device, torch.bfloat16))
+        self._restore_trainer_state(path)
+
+    def _restore_trainer_state(self, path: str) -> None:
         st = Checkpointer.trainer_state(path)
         self.step = int(st["step"])
         self.data.load_state(st.get("data", {}))

@@ -166,3 +166,29 @@ def test_stage_params_reproduce_full_model_init():
     assert sorted(seen) == sorted(ref)
     for k in ref:
         assert torch.equal(seen[k], ref[k]), k
+
+
+def test_stage_checkpoint_mapping_roundtrip():
+    from lora_kernel_b200.models.params import FlatParams, build_layout
+    from lora_kernel_b200.parallel.pp import gather_stage, scatter_stage, stage_global_ranges
+    cfg = TransformerConfig(hidden_dim=128, num_heads=2, head_dim=64, ff_dim=200, vocab_size=300, num_layers=5)
+    specs, _, total = build_layout(cfg, 64)
+    lay = {"total": total, "specs": {s.name: [s.offset, s.numel] for s in specs}}
+    full = FlatParams(cfg, "cpu", torch.float32)
+    full.flat.copy_(torch.randn(full.numel))
+    rebuilt = torch.zeros(total)
+    for s, r in enumerate(partition_layers(5, 3)):
+        st = FlatParams(cfg, "cpu", torch.float32, layers=r, embed=(s == 0), head=(s == 2))
+        rr = stage_global_ranges(st, lay)
+        scatter_stage(full.flat, rr, st.flat)
+        for sp in st.specs:
+            assert torch.equal(st.views[sp.name], full.views[sp.name])
+        packed = gather_stage(st.flat, rr)
+        o = 0
+        for _, g, n in rr:  # what Checkpointer.load_flat reassembles from the saved ranges
+            rebuilt[g:g + n] = packed[o:o + n]
+            o += n
+    mask = torch.zeros(total, dtype=torch.bool)
+    for o, n in lay["specs"].values():
+        mask[o:o + n] = True
+    assert torch.equal(rebuilt[mask], full.flat[mask])

@@ -61,3 +61,23 @@ def test_pipeline_matches_single_gpu(tmp_path):
         got = res["full"][k]
         err = ((got - want).norm() / (want.norm() + 1e-12)).item()
         assert err < 2e-2, (k, err)
+
+
+def test_trainer_resume_pp(tmp_path):
+    """Trainer.fit with parallel.pp=2: 2 steps + checkpoint + resume to 4
+    gives the losses of 4 uninterrupted steps."""
+    import json
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = str(tmp_path / "resume.json")
+    env = dict(os.environ, LK_OUT=out, NCCL_NVLS_ENABLE="0", LK_NVLS="0", LORAK_HEARTBEAT="0")
+    port = random.randint(20000, 40000)
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(HERE, "dist_trainer_resume_check.py"), "pp", str(tmp_path)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.load(open(out))
+    assert res["steps"] == [3, 4] and "step_2" in res["saved"] and "step_4" in res["saved"]
+    for a, b in zip(res["full"][2:], res["resumed"]):
+        assert abs(a - b) < 1e-3 * abs(a), res
