@@ -119,7 +119,8 @@ class ParallelConfig:
     dp: int = 1
     tp: int = 1
     pp: int = 1  # pipeline stages (1F1B); spans every rank of the job
-    cp: int = 1  # context parallelism (Ulysses): ranks share each sequence; spans the job
+    cp: int = 1  # context parallelism: ranks share each sequence; spans the job
+    cp_mode: str = "ulysses"  # ulysses (heads divisible by cp) | ring (zigzag chunks, any head count)
     zero_stage: int = 0  # 0, 1, 2, 3 (3 == FSDP)
     sequence_parallel: bool = False
     fused_collectives: bool = True

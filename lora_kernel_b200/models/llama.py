@@ -223,7 +223,7 @@ class LlamaModel:
                             causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
         else:
             E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
-                    pos_offset=self.ctx.pos_offset(ws.S))
+                    **self.ctx.rope_args(ws.B, ws.S, self.device))
             self.ctx.forward(qkv, ws.B, ws.S, ws.o[slot], key=(id(ws), slot), window=self.attn_window)
         o_in = ws.o[slot]
         if drop:  # attention-context dropout into its own buffer
@@ -334,12 +334,12 @@ class LlamaModel:
             A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
                             cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
                             dqkv=ws.dqkv)
-            off = 0
+            off = {}
         else:
             self.ctx.backward(ws.do, ws.B, ws.S, ws.dqkv, key=(id(ws), s), window=self.attn_window)
-            off = self.ctx.pos_offset(ws.S)
+            off = self.ctx.rope_args(ws.B, ws.S, self.device)
         E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
-                pos_offset=off, inverse=True)
+                inverse=True, **off)
         self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[s], ws.dx)
         N.rmsnorm_bwd(ws.dx, h_in, self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
                       dres=dh, dx=dh, accumulate=not self._overwrite)

@@ -74,7 +74,8 @@ class Trainer:
             if par.cp != self.world:
                 raise ValueError(f"context parallelism spans the whole job: cp={par.cp} but {self.world} ranks")
             from ..parallel.cp import ContextParallelTrainer
-            self.pipe = ContextParallelTrainer(cfg, tc, zero_stage=min(par.zero_stage, 2), device=self.device)
+            self.pipe = ContextParallelTrainer(cfg, tc, zero_stage=min(par.zero_stage, 2), device=self.device,
+                                               mode=par.cp_mode)
             self.align = self.pipe.dp.L.align
         elif self.pp:
             # pipeline stages over every rank; all ranks read the same micro-batches

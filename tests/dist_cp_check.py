@@ -1,6 +1,7 @@
 """Launched by tests/test_cp_multigpu.py under torchrun: context parallelism
 (Ulysses attention, sequence chunks per rank, data-parallel gradient sum)
-must match the single-GPU pipeline on the same full micro-batches."""
+must match the single-GPU pipeline on the same full micro-batches.
+LK_CP_MODE selects Ulysses (default) or ring attention."""
 import os
 import sys
 
@@ -18,7 +19,7 @@ from test_cp_multigpu import CFG, TC, batches  # noqa: E402
 
 def main():
     rank, world, local = init_distributed("nccl", timeout_s=120)
-    tr = ContextParallelTrainer(CFG, TC, zero_stage=0, device="cuda")
+    tr = ContextParallelTrainer(CFG, TC, zero_stage=0, device="cuda", mode=os.environ.get("LK_CP_MODE", "ulysses"))
     losses = [tr.train_step(b[:, :-1].cuda(), b[:, 1:].cuda()) for b in batches()]
     torch.cuda.synchronize()
     check_status()

@@ -1,4 +1,5 @@
-"""Context parallelism (Ulysses) on 2 GPUs against the single-GPU pipeline."""
+"""Context parallelism (Ulysses and ring attention) on 2 GPUs against the
+single-GPU pipeline."""
 import os
 import random
 import subprocess
@@ -23,13 +24,14 @@ def batches():
     return [torch.randint(0, CFG.vocab_size, (2, 257), generator=g) for _ in range(3)]
 
 
-def test_context_parallel_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("mode", ["ulysses", "ring"])
+def test_context_parallel_matches_single_gpu(tmp_path, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from lora_kernel_b200.parallel.zero import ShardLayout
     from lora_kernel_b200.train.pipeline import Transformer, TrainingPipeline
     out = str(tmp_path / "cp.pt")
-    env = dict(os.environ, LK_OUT=out, NCCL_NVLS_ENABLE="0", LK_NVLS="0", PYTHONPATH=HERE)
+    env = dict(os.environ, LK_OUT=out, NCCL_NVLS_ENABLE="0", LK_NVLS="0", PYTHONPATH=HERE, LK_CP_MODE=mode)
     port = random.randint(20000, 40000)
     cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
