@@ -21,6 +21,30 @@ EPI = {"bf16": 0, "f32": 1, "f32_acc": 2, "bf16_resid": 3, "swiglu": 4}
 
 _cap = {}
 
+# optional per-problem tile widths measured by utils/autotune.py (LK_GEMM_TUNING)
+_tuning = None
+_tuning_loaded = False
+
+
+def set_tuning(table) -> None:
+    """Use `table` (utils.autotune.GemmTable, or a path to its JSON; None:
+    the dispatcher's built-in rule) for every gemm call without an explicit bn."""
+    global _tuning, _tuning_loaded
+    if isinstance(table, str):
+        from ..utils.autotune import GemmTable
+        table = GemmTable.load(table)
+    _tuning, _tuning_loaded = table, True
+
+
+def tuned_bn(a: torch.Tensor, b: torch.Tensor, epi: str) -> int:
+    """Tile width from the tuning table (0 = let the dispatcher choose)."""
+    global _tuning_loaded
+    if not _tuning_loaded:
+        import os
+        path = os.environ.get("LK_GEMM_TUNING", "")
+        set_tuning(path or None)
+    return _tuning.lookup(a, b, epi) if _tuning is not None else 0
+
 
 def _check_device(t: torch.Tensor) -> None:
     idx = t.device.index
@@ -35,6 +59,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
          a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = alpha * (a @ b.T [+ a2 @ b2.T]) with the requested epilogue."""
     _check_device(a)
+    if bn == 0:
+        bn = tuned_bn(a, b, epi)
     M, N = a.shape[0], b.shape[0]
     if out is None:
         dt = torch.float32 if epi in ("f32", "f32_acc") else torch.bfloat16
