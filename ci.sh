@@ -5,3 +5,5 @@ set -euo pipefail
 cd "$(dirname "$0")"
 python -c "import __graft_entry__ as g; g.build()"
 python -m pytest tests/ -x -q -m "not gpu"
+# native host runtime under ASan+UBSan and TSan (also run by tests/test_runtime_sanitizers.py)
+csrc/runtime/test/sanitize.sh
