@@ -106,6 +106,7 @@ class TrainConfig:
     checkpoint_every: int = 0
     max_consecutive_skips: int = 20
     log_every: int = 10
+    metrics_file: str = ""  # rank 0 appends one JSON line per logged step (loss, grad norm, tokens/s, MFU, ...)
     fixed_batch: bool = False  # reuse one seeded batch every step (the CPU demo's data)
     data_path: str = ""  # flat uint16/uint32 token file; empty = synthetic uniform ids
     data_dtype: str = "uint16"

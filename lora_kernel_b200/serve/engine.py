@@ -56,6 +56,7 @@ class Request:
     prefill_len: int = 0        # tokens to prefill before decoding (all but a pending last token)
     cached_prefix: int = 0
     first_token_time: Optional[float] = None
+    scheduled_time: Optional[float] = None  # first admission to the running set (queue time ends)
     token_times: List[float] = field(default_factory=list)
     finished: bool = False
     finish_reason: Optional[str] = None
@@ -154,6 +155,8 @@ class LLMEngine:
             except MemoryError:
                 break
             self.waiting.popleft()
+            if r.scheduled_time is None:
+                r.scheduled_time = self.clock()
             r.prefill_len = len(seq)
             r.computed = cached
             r.cached_prefix = cached

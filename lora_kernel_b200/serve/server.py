@@ -102,6 +102,9 @@ class EngineWorker:
         self.m_ttft = REGISTRY.histogram("time_to_first_token_seconds", "TTFT")
         self.m_itl = REGISTRY.histogram("inter_token_latency_seconds", "inter-token latency")
         self.m_e2e = REGISTRY.histogram("e2e_request_latency_seconds", "request latency")
+        self.m_queue = REGISTRY.histogram("request_queue_time_seconds", "arrival to first scheduling")
+        self.m_pre = REGISTRY.counter("preemptions_total", "sequences preempted for KV blocks")
+        self._pre_seen = 0
         self.m_out = REGISTRY.counter("generation_tokens_total", "generated tokens")
         self.m_in = REGISTRY.counter("prompt_tokens_total", "prompt tokens")
         self.m_req = REGISTRY.counter("requests_total", "finished requests")
@@ -146,9 +149,15 @@ class EngineWorker:
             self.g_wait.set(len(e.waiting))
             self.g_kv.set(e.blocks.usage())
             self.g_hit.set(e.blocks.stats.hit_rate)
+            pre = getattr(e, "stats", {}).get("preemptions", 0)
+            if pre > self._pre_seen:
+                self.m_pre.inc(pre - self._pre_seen)
+                self._pre_seen = pre
             for r in finished:
                 self.m_req.inc()
                 self.m_out.inc(len(r.output))
+                if getattr(r, "scheduled_time", None) is not None:
+                    self.m_queue.observe(r.scheduled_time - r.arrival)
                 if r.first_token_time is not None:
                     self.m_ttft.observe(r.first_token_time - r.arrival)
                     self.m_e2e.observe(r.token_times[-1] - r.arrival)

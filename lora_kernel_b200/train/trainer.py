@@ -220,6 +220,9 @@ class Trainer:
         self._install_signals()
         tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if (self.tp or self.pp or self.cp)
                                                                              else self.world)
+        from ..utils.metrics import TrainMetrics, mfu, train_flops_per_token
+        flops_tok = train_flops_per_token(self.rc.model, tc.seq_len)
+        metrics = TrainMetrics(tc.metrics_file if self.rank == 0 else "")
         t_last, s_last = time.perf_counter(), self.step
         while self.step < total:
             if self.hb is not None:
@@ -242,19 +245,22 @@ class Trainer:
             if self.step % tc.log_every == 0 or self.step == total:
                 s, n = self.pipe.loss_acc.tolist()
                 now = time.perf_counter()
+                tps = tok_per_step * (self.step - s_last) / (now - t_last)
                 rec = {"step": self.step, "loss": s / max(n, 1.0), "grad_norm": o.grad_norm(),
                        "loss_scale": o.scaler.get_scale(), "skipped": o.scaler.num_skipped(),
-                       "lr": o.lr, "tokens_per_s": tok_per_step * (self.step - s_last) / (now - t_last)}
+                       "lr": o.lr, "tokens_per_s": tps, "mfu": mfu(tps, flops_tok, self.world)}
                 t_last, s_last = now, self.step
                 self.history.append(rec)
                 if self.rank == 0:
                     log_fields(log, "train", **rec)
+                    metrics.record(rec)
                 if o.scaler.consecutive_skips() > tc.max_consecutive_skips:
                     raise FloatingPointError(f"{o.scaler.consecutive_skips()} consecutive overflow steps")
             if self.ckpt is not None and tc.checkpoint_every and self.step % tc.checkpoint_every == 0:
                 self.save_checkpoint(async_save=True)
             if self._stop:
                 break
+        metrics.close()
         if self.ckpt is not None:
             self.save_checkpoint()
             self.ckpt.finish()

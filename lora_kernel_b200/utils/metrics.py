@@ -120,3 +120,57 @@ class Registry:
 
 
 REGISTRY = Registry()
+
+
+# ------------------------------------------------------------------ training
+B200_BF16_DENSE_TFLOPS = 2250.0  # nominal dense bf16 tensor peak per GPU (no sparsity)
+
+
+def train_flops_per_token(cfg, seq_len: int) -> float:
+    """Model FLOPs of one trained token (forward + backward = 3x forward):
+    6 x the GEMM parameters (the four linear layers of every block and the LM
+    head; the embedding gather does no math) plus causal attention, whose
+    QK^T and PV products average seq_len/2 keys per query:
+    3 x 2 x 2 x (seq_len/2) x heads x head_dim per layer."""
+    D, F, Dh = cfg.hidden_dim, cfg.ff_dim, cfg.head_dim
+    H, KV = cfg.num_heads, cfg.num_kv_heads
+    per_layer = D * (H + 2 * KV) * Dh + H * Dh * D + 3 * D * F
+    gemm = cfg.num_layers * per_layer + D * cfg.vocab_size
+    attn = cfg.num_layers * 6.0 * seq_len * H * Dh
+    return 6.0 * gemm + attn
+
+
+def mfu(tokens_per_s: float, flops_per_token: float, n_gpus: int,
+        peak_tflops: float = B200_BF16_DENSE_TFLOPS) -> float:
+    """Model FLOPs utilisation: achieved model FLOP/s over n_gpus x peak."""
+    return tokens_per_s * flops_per_token / (n_gpus * peak_tflops * 1e12)
+
+
+class TrainMetrics:
+    """Training step records -> Prometheus gauges in REGISTRY and, when a path
+    is given, one JSON line per record appended to that file."""
+
+    FIELDS = ("loss", "grad_norm", "loss_scale", "skipped", "lr", "tokens_per_s", "mfu")
+
+    def __init__(self, path: str = "", registry: Optional["Registry"] = None):
+        reg = registry or REGISTRY
+        self.path = path
+        self.g = {k: reg.gauge(f"train_{k}", f"training {k.replace('_', ' ')}") for k in self.FIELDS}
+        self.g_step = reg.gauge("train_step", "optimizer steps taken")
+        self.f = open(path, "a", buffering=1) if path else None
+
+    def record(self, rec: dict) -> None:
+        import json
+        for k, g in self.g.items():
+            if k in rec and rec[k] is not None:
+                g.set(rec[k])
+        if "step" in rec:
+            self.g_step.set(rec["step"])
+        if self.f is not None:
+            self.f.write(json.dumps(rec) + "\n")
+
+    def close(self) -> None:
+        if self.f is not None:
+            self.f.close()
+            self.f = None
+

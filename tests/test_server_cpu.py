@@ -45,6 +45,8 @@ class FakeEngine:
         return bool(self.running or self.waiting)
 
     def step(self):
+        for r in self.waiting:
+            r.scheduled_time = time.perf_counter()
         self.running += self.waiting
         self.waiting = []
         done = []
@@ -89,6 +91,11 @@ def test_completion_json_schema():
         assert (await r.json())["status"] == "healthy"
         r = await c.post("/v1/completions", data="not json")
         assert r.status == 400
+        r = await c.get("/metrics")
+        text = await r.text()
+        count = [ln for ln in text.splitlines() if ln.startswith("lora_kernel_request_queue_time_seconds_count")]
+        assert count and float(count[0].split()[-1]) >= 2, text
+        assert "lora_kernel_preemptions_total" in text
     _run(go)
 
 
@@ -261,3 +268,27 @@ def test_server_over_replicas():
             await go(client)
     asyncio.run(main())
     assert engines[0].n == 2 and engines[1].n == 2
+
+
+def test_training_flops_mfu_and_metrics_file(tmp_path):
+    """Model FLOPs per token against a hand count for the 1.1B shape, MFU
+    arithmetic, and the JSONL file / gauges of TrainMetrics."""
+    import json as _json
+    from lora_kernel_b200.config import get_preset
+    from lora_kernel_b200.utils.metrics import Registry, TrainMetrics, mfu, train_flops_per_token
+    cfg = get_preset("llama-1.1b-zero3").model
+    D, F, L, V = 2048, 5632, 22, 32000
+    gemm_params = L * (D * 2560 + 2048 * D + 3 * D * F) + D * V
+    want = 6 * gemm_params + L * 6 * 2048 * 32 * 64
+    assert train_flops_per_token(cfg, 2048) == want
+    assert abs(mfu(100_000.0, 1e10, 2, peak_tflops=1000.0) - 0.5) < 1e-12
+    reg = Registry("t_")
+    path = str(tmp_path / "m.jsonl")
+    m = TrainMetrics(path, reg)
+    m.record({"step": 1, "loss": 2.5, "tokens_per_s": 10.0, "mfu": 0.4})
+    m.record({"step": 2, "loss": 2.0, "tokens_per_s": 12.0, "mfu": 0.5, "grad_norm": 1.5})
+    m.close()
+    lines = [_json.loads(x) for x in open(path)]
+    assert [r["step"] for r in lines] == [1, 2] and lines[1]["grad_norm"] == 1.5
+    text = reg.exposition()
+    assert "t_train_loss 2.0" in text and "t_train_mfu 0.5" in text and "t_train_step 2.0" in text
