@@ -1,7 +1,9 @@
 """Command line: `python -m lora_kernel_b200 {train,bench,serve,export,env}`.
 
   train  --preset NAME | --config FILE [--steps N] [--set section.key=value ...]
-         (launch with torch.distributed.run for more than one GPU: ZeRO-3)
+         [--tp N --pp N --cp N --cp-mode ulysses|ring --zero 0-3 --fp8 --sp]
+         [--lr X --micro-batch B --seq-len S --grad-accum K --metrics-file F]
+         (launch with torch.distributed.run for more than one GPU)
   bench  [--gpus N --steps K --warmup W]   the headline training benchmark
          [--kernels]                       kernel micro-benchmarks instead
          [--serve ...]                     serving load generator
@@ -34,11 +36,30 @@ def _overrides(items):
     return out
 
 
+# train flags that are shorthands for dotted overrides (applied after --set)
+TRAIN_FLAGS = {
+    "tp": "parallel.tp", "pp": "parallel.pp", "cp": "parallel.cp", "cp_mode": "parallel.cp_mode",
+    "zero": "parallel.zero_stage", "fp8": "parallel.fp8", "sp": "parallel.sequence_parallel",
+    "lr": "train.lr", "micro_batch": "train.micro_batch", "seq_len": "train.seq_len",
+    "grad_accum": "train.grad_accum_steps", "metrics_file": "train.metrics_file",
+}
+
+
+def train_overrides(a) -> dict:
+    """--set items, then the shorthand flags that were given."""
+    out = _overrides(a.set)
+    for flag, key in TRAIN_FLAGS.items():
+        v = getattr(a, flag, None)
+        if v is not None and v is not False:
+            out[key] = v
+    return out
+
+
 def cmd_train(a):
     from .config import load_config
     from .parallel.comm import init_distributed
     from .train.trainer import Trainer
-    rc = load_config(a.config, a.preset, _overrides(a.set))
+    rc = load_config(a.config, a.preset, train_overrides(a))
     if a.checkpoint_dir:
         rc.train.checkpoint_dir = a.checkpoint_dir
     init_distributed("nccl")
@@ -167,6 +188,13 @@ def main(argv=None):
     t.add_argument("--steps", type=int)
     t.add_argument("--checkpoint-dir")
     t.add_argument("--set", nargs="*")
+    for n in ("tp", "pp", "cp", "zero", "micro-batch", "seq-len", "grad-accum"):
+        t.add_argument(f"--{n}", type=int)
+    t.add_argument("--cp-mode", choices=["ulysses", "ring"])
+    t.add_argument("--lr", type=float)
+    t.add_argument("--metrics-file")
+    t.add_argument("--fp8", action="store_true", help="block-scaled fp8 GEMMs (tensor parallel)")
+    t.add_argument("--sp", action="store_true", help="Megatron sequence parallelism (tensor parallel)")
     b = sub.add_parser("bench")
     b.add_argument("--gpus", type=int, default=1)
     b.add_argument("--kernels", action="store_true")

@@ -127,3 +127,26 @@ def test_numa_cpulist_from_fake_sysfs(tmp_path):
     assert gpu_numa_cpus("00000000:1B:00.0", str(tmp_path)) == {32, 33, 34, 35, 96}
     (dev / "numa_node").write_text("-1\n")
     assert gpu_numa_cpus("0000:1b:00.0", str(tmp_path)) == set()
+
+
+def test_train_cli_shorthand_flags():
+    """`train --tp 8 --zero 3 ...` become the dotted overrides of the run config."""
+    import argparse
+    from lora_kernel_b200 import cli
+    from lora_kernel_b200.config import load_config
+    seen = {}
+    orig = cli.cmd_train
+    cli.cmd_train = lambda a: seen.update(a=a)
+    try:
+        cli.main(["train", "--preset", "llama-1.1b-zero3", "--cp", "8", "--cp-mode", "ring", "--zero", "2",
+                  "--lr", "1e-4", "--seq-len", "4096", "--fp8", "--set", "train.seed=7"])
+    finally:
+        cli.cmd_train = orig
+    ov = cli.train_overrides(seen["a"])
+    assert ov == {"train.seed": 7, "parallel.cp": 8, "parallel.cp_mode": "ring", "parallel.zero_stage": 2,
+                  "train.lr": 1e-4, "train.seq_len": 4096, "parallel.fp8": True}
+    rc = load_config(None, "llama-1.1b-zero3", ov)
+    assert (rc.parallel.cp, rc.parallel.cp_mode, rc.parallel.zero_stage) == (8, "ring", 2)
+    assert rc.train.seq_len == 4096 and rc.train.seed == 7
+    ov2 = cli.train_overrides(argparse.Namespace(set=None, tp=None, zero=0, fp8=False))
+    assert ov2 == {"parallel.zero_stage": 0}
