@@ -276,3 +276,34 @@ def test_layernorm_fwd_bwd_vs_fp32(D):
     assert rel(y, ref.detach()) < 1e-2
     assert rel(dx, xf.grad) < 2e-2
     assert rel(dgamma, gf.grad) < 1e-3 and rel(dbeta, bf.grad) < 1e-3
+
+
+@pytest.mark.gpu
+def test_peer_wait_gives_up_with_a_status_and_the_context_survives():
+    """Failure detection on one GPU without a fault: a two-rank signal barrier
+    whose second "peer" flag array is a local buffer that nothing writes.  The
+    waiting thread gives up after the kernels' bound (2 s), records "timeout
+    waiting for a peer GPU" (4) in the status word and returns; the same
+    barrier with the flag set passes and the context keeps working."""
+    import time as _time
+    from lora_kernel_b200._ext import C, STATUS_NAMES
+    mine = torch.zeros(2, dtype=torch.int32, device="cuda")     # rank 0's slots: [from 0, from 1]
+    peer = torch.zeros(2, dtype=torch.int32, device="cuda")     # the absent rank 1's slots
+    table = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    t0 = _time.perf_counter()
+    C().signal_barrier(table, 0, 2, 0, 1, status)
+    torch.cuda.synchronize()
+    waited = _time.perf_counter() - t0
+    assert STATUS_NAMES[int(status.item())] == "timeout waiting for a peer GPU"
+    assert 1.5 < waited < 30.0, waited
+    assert int(peer[0].item()) == 1          # rank 0 still signalled the peer
+    # the peer "arrives": epoch 2 is already in rank 0's slot from rank 1
+    mine[1] = 2
+    status.zero_()
+    C().signal_barrier(table, 0, 2, 0, 2, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    x = torch.arange(1024, device="cuda", dtype=torch.float32)
+    assert float(x.sum().item()) == 1023 * 1024 / 2
