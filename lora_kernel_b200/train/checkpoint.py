@@ -27,11 +27,14 @@ from __future__ import annotations
 import json
 import os
 import shutil
+import logging
 import threading
 from typing import Dict, List, Optional, Tuple
 
 import torch
 from safetensors.torch import load_file, save_file
+
+log = logging.getLogger(__name__)
 
 
 def _crc(path: str) -> int:
@@ -49,9 +52,10 @@ def _crc(path: str) -> int:
             c = _rt.crc32(mv[:n], c)
 
 
-def latest(root: str) -> Optional[str]:
+def complete_steps(root: str) -> List[str]:
+    """Published checkpoints under root (index written, not `.tmp`), newest first."""
     if not os.path.isdir(root):
-        return None
+        return []
     steps = []
     for d in os.listdir(root):
         if d.startswith("step_") and not d.endswith(".tmp") and os.path.exists(os.path.join(root, d, "index.json")):
@@ -59,7 +63,23 @@ def latest(root: str) -> Optional[str]:
                 steps.append((int(d[5:]), d))
             except ValueError:
                 pass
-    return os.path.join(root, max(steps)[1]) if steps else None
+    return [os.path.join(root, d) for _, d in sorted(steps, reverse=True)]
+
+
+def latest(root: str, verify: bool = False) -> Optional[str]:
+    """Newest published checkpoint; with verify, the newest whose files all
+    match their crc32 in the index (a corrupted or truncated checkpoint is
+    passed over for the one before it)."""
+    for p in complete_steps(root):
+        if not verify:
+            return p
+        try:
+            if Checkpointer.verify(p):
+                return p
+        except (OSError, ValueError, KeyError):
+            pass
+        log.warning("checkpoint %s fails its crc32 check; trying the one before it", p)
+    return None
 
 
 def save_model_safetensors(state: Dict[str, torch.Tensor], path: str, dtype=None) -> None:

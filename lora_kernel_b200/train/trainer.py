@@ -214,7 +214,11 @@ class Trainer:
         tc = self.rc.train
         total = steps if steps is not None else tc.total_steps
         if resume and self.ckpt is not None:
-            p = latest(tc.checkpoint_dir)
+            p = latest(tc.checkpoint_dir, verify=self.rank == 0)
+            if self.world > 1:  # rank 0 checks the checksums; every rank resumes from its choice
+                box = [p]
+                dist.broadcast_object_list(box, src=0)
+                p = box[0]
             if p:
                 self.load_checkpoint(p)
         self._install_signals()

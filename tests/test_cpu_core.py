@@ -150,3 +150,18 @@ def test_train_cli_shorthand_flags():
     assert rc.train.seq_len == 4096 and rc.train.seed == 7
     ov2 = cli.train_overrides(argparse.Namespace(set=None, tp=None, zero=0, fp8=False))
     assert ov2 == {"parallel.zero_stage": 0}
+
+
+def test_swa_running_mean():
+    """SWA from start_step every `every` steps equals the plain mean of the
+    snapshots it took."""
+    import torch
+    from lora_kernel_b200.train.optimizer import SWA
+    g = torch.Generator().manual_seed(0)
+    snaps = [torch.randn(1000, generator=g, dtype=torch.float64) for _ in range(12)]
+    swa = SWA(torch.zeros(1000, dtype=torch.float64), start_step=3, every=2)
+    for step, w in enumerate(snaps):
+        swa.update(w, step)
+    took = [snaps[s] for s in range(3, 12, 2)]
+    assert swa.n == len(took) == 5
+    torch.testing.assert_close(swa.avg, torch.stack(took).mean(0), rtol=1e-12, atol=1e-12)

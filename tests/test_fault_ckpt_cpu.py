@@ -112,3 +112,34 @@ def test_model_safetensors_reference_names(tmp_path):
     q = FlatParams(cfg, "cpu", torch.float32)
     q.load_reference_state_dict(sd)
     assert torch.equal(q.flat, p.flat)
+
+
+def test_resume_passes_over_a_corrupted_checkpoint(tmp_path):
+    """A flipped byte or a truncated shard fails the crc32 index check;
+    latest(verify=True) then returns the newest checkpoint that passes."""
+    import shutil
+    from lora_kernel_b200.train.checkpoint import Checkpointer, complete_steps, latest
+    from lora_kernel_b200.train.trainer import _layout_info
+    cfg = TransformerConfig(hidden_dim=128, num_heads=2, head_dim=64, ff_dim=256, vocab_size=300, num_layers=1)
+    lay = _layout_info(cfg, 64)
+    ck = Checkpointer(str(tmp_path), 0, 1)
+    state = {"p32": torch.randn(lay["total"]), "m": torch.zeros(lay["total"]), "v": torch.zeros(lay["total"]),
+             "state": torch.arange(16.)}
+    ck.save(3, None, [(0, lay["total"])], state, lay, {"step": 3})
+    ck.finish()
+    for step in (5, 7):
+        shutil.copytree(tmp_path / "step_3", tmp_path / f"step_{step}")
+    assert [os.path.basename(p) for p in complete_steps(str(tmp_path))] == ["step_7", "step_5", "step_3"]
+    shard = next(f for f in os.listdir(tmp_path / "step_7") if f.startswith("optim"))
+    with open(tmp_path / "step_7" / shard, "r+b") as f:   # flip one byte in the middle
+        f.seek(os.path.getsize(tmp_path / "step_7" / shard) // 2)
+        b = f.read(1)
+        f.seek(-1, 1)
+        f.write(bytes([b[0] ^ 0x40]))
+    with open(tmp_path / "step_5" / shard, "r+b") as f:   # truncate
+        f.truncate(100)
+    assert latest(str(tmp_path)).endswith("step_7")
+    assert not Checkpointer.verify(str(tmp_path / "step_7"))
+    assert latest(str(tmp_path), verify=True).endswith("step_3")
+    os.remove(tmp_path / "step_3" / shard)                 # a missing file fails too
+    assert latest(str(tmp_path), verify=True) is None
