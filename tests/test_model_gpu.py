@@ -93,3 +93,28 @@ def test_steady_state_steps_do_not_grow_device_memory():
         torch.cuda.synchronize()
         live.append(torch.cuda.memory_allocated())
     assert live[2] == live[1] and live[3] == live[2], live
+
+
+def test_gradient_accumulation_equals_one_big_batch():
+    """Two accumulated micro-batches of 2 sequences give the gradient of one
+    batch of the same 4 sequences (mean over all tokens), read at the
+    optimizer hook before the update."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.config import TrainConfig
+    from lora_kernel_b200.train.pipeline import Transformer, TrainingPipeline
+    cfg = _tiny()
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size, (4, 129), generator=g)
+    grads = {}
+    for accum in (1, 2):
+        model = Transformer(cfg, "cuda", seed=5)
+        tc = TrainConfig(lr=1e-3, weight_decay=0.0, dynamic_loss_scale=False, grad_accum_steps=accum)
+        pipe = TrainingPipeline(model, 1e-3, 0.0, 1.0, train_cfg=tc)
+        pipe.pre_optimizer = lambda flat, a=accum: grads.__setitem__(a, flat.float().clone())
+        parts = [ids] if accum == 1 else [ids[:2], ids[2:]]
+        for p in parts:
+            pipe.train_step(p[:, :-1], p[:, 1:])
+        assert pipe.current_step() == 1
+    torch.cuda.synchronize()
+    check_status()
+    assert _rel(grads[2], grads[1]) < 1e-3
