@@ -117,14 +117,15 @@ class TrainConfig:
 
 @dataclass
 class ParallelConfig:
-    dp: int = 1
+    dp: int = 1  # data-parallel ranks: 1 (whatever the job has) or the job's world size
     tp: int = 1
     pp: int = 1  # pipeline stages (1F1B); spans every rank of the job
     cp: int = 1  # context parallelism: ranks share each sequence; spans the job
     cp_mode: str = "ulysses"  # ulysses (heads divisible by cp) | ring (zigzag chunks, any head count)
     zero_stage: int = 0  # 0, 1, 2, 3 (3 == FSDP)
     sequence_parallel: bool = False
-    fused_collectives: bool = True
+    fused_collectives: bool = True  # False: the same schedules on NCCL collectives (library baseline)
+    fuse_gather: bool = False  # ZeRO-3: parameter all-gather inside the first consuming GEMM (K17)
     fp8: bool = False
 
 

@@ -99,6 +99,8 @@ class TrainingPipeline:
         self.loss_acc = torch.zeros(2, dtype=torch.float32, device=eng.device)
         self.last_loss = float("nan")
         self.pre_optimizer = None  # optional callable(flat fp32 grads), e.g. fault injection
+        if tc.swa_start >= 0:
+            self.init_swa(tc.swa_start)
 
     # ----------------------------------------------------- reference setters
     def set_learning_rate(self, lr: float) -> None:

@@ -51,6 +51,36 @@ def remap_flat(src: torch.Tensor, src_layout: dict, dst_layout: dict) -> torch.T
     return out
 
 
+def parallel_plan(par, world: int) -> dict:
+    """Which trainer a run config selects on `world` ranks, after checking the
+    parallel section: tp / pp / cp each span the whole job and exclude one
+    another; dp (when set) is the number of data-parallel ranks, so it must be
+    1 under tp / pp / cp and 1 or `world` otherwise.  fused_collectives=False
+    runs the same schedules on NCCL collectives (the library baseline)."""
+    from ..parallel.cp import CP_MODES
+    modes = [k for k in ("tp", "pp", "cp") if getattr(par, k) > 1]
+    if len(modes) > 1:
+        raise ValueError(f"parallel: {' and '.join(modes)} cannot be combined (each spans the whole job)")
+    if par.cp_mode not in CP_MODES:
+        raise ValueError(f"parallel.cp_mode must be one of {CP_MODES}, got {par.cp_mode!r}")
+    if par.zero_stage not in (0, 1, 2, 3):
+        raise ValueError(f"parallel.zero_stage must be 0..3, got {par.zero_stage}")
+    comm = "p2p" if par.fused_collectives else "nccl"
+    if world == 1:
+        return {"trainer": "single", "comm": comm}
+    if modes:
+        k = modes[0]
+        if getattr(par, k) != world:
+            name = {"tp": "tensor", "pp": "pipeline", "cp": "context"}[k]
+            raise ValueError(f"{name} parallelism spans the whole job: {k}={getattr(par, k)} but {world} ranks")
+        if par.dp not in (1,):
+            raise ValueError(f"parallel.dp={par.dp} with {k}={world}: data parallelism is not combined with {k}")
+        return {"trainer": k, "comm": comm}
+    if par.dp not in (1, world):
+        raise ValueError(f"parallel.dp={par.dp} but the job has {world} ranks (data parallelism spans the job)")
+    return {"trainer": "zero3" if par.zero_stage == 3 else "dp", "comm": comm}
+
+
 class Trainer:
     def __init__(self, rc: RunConfig, device: Optional[str] = None, data=None):
         self.rc = rc
@@ -64,41 +94,39 @@ class Trainer:
             self.pipe = TrainingPipeline(self.model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
             self.align = 64
         par = rc.parallel
-        self.tp = self.world > 1 and par.tp > 1
-        self.pp = self.world > 1 and par.pp > 1
-        self.cp = self.world > 1 and par.cp > 1
+        plan = parallel_plan(par, self.world)
+        comm = plan["comm"]
+        self.tp = plan["trainer"] == "tp"
+        self.pp = plan["trainer"] == "pp"
+        self.cp = plan["trainer"] == "cp"
+        if tc.swa_start >= 0 and self.world > 1:
+            raise NotImplementedError("train.swa_start: SWA runs on one GPU (TrainingPipeline.init_swa)")
         if self.world == 1:
             pass
         elif self.cp:
-            # every rank takes its chunk of each sequence of the same micro-batch
-            if par.cp != self.world:
-                raise ValueError(f"context parallelism spans the whole job: cp={par.cp} but {self.world} ranks")
+            # every rank takes its part of each sequence of the same micro-batch
             from ..parallel.cp import ContextParallelTrainer
             self.pipe = ContextParallelTrainer(cfg, tc, zero_stage=min(par.zero_stage, 2), device=self.device,
-                                               mode=par.cp_mode)
+                                               comm=comm, mode=par.cp_mode)
             self.align = self.pipe.dp.L.align
         elif self.pp:
             # pipeline stages over every rank; all ranks read the same micro-batches
-            if par.pp != self.world:
-                raise ValueError(f"pipeline parallelism spans the whole job: pp={par.pp} but {self.world} ranks")
             from ..parallel.pp import PipelineTrainer
             self.pipe = PipelineTrainer(cfg, tc, device=self.device)
             self.align = 64
         elif self.tp:
             # tensor (+ sequence) parallelism over every rank: they share one batch
-            if par.tp != self.world:
-                raise ValueError(f"tensor parallelism spans the whole job: tp={par.tp} but {self.world} ranks")
             from ..parallel.tp import TPTrainer
             self.pipe = TPTrainer(cfg, tc, micro_batch=tc.micro_batch, seq_len=tc.seq_len, device=self.device,
-                                  fp8=par.fp8, seed=tc.seed)
+                                  comm=comm, fp8=par.fp8, seed=tc.seed)
             self.align = 64
-        elif par.zero_stage in (0, 1, 2):
+        elif plan["trainer"] == "dp":
             from ..parallel.dp import DataParallelTrainer
-            self.pipe = DataParallelTrainer(cfg, tc, zero_stage=par.zero_stage, device=self.device)
+            self.pipe = DataParallelTrainer(cfg, tc, zero_stage=par.zero_stage, device=self.device, comm=comm)
             self.align = self.pipe.L.align
         else:
             from ..parallel.zero import Zero3Trainer
-            self.pipe = Zero3Trainer(cfg, tc, device=self.device)
+            self.pipe = Zero3Trainer(cfg, tc, device=self.device, comm=comm, fuse_gather=par.fuse_gather)
             self.align = self.pipe.L.align
         # tensor and pipeline parallelism: every rank reads the same batch
         shared = self.tp or self.pp or self.cp

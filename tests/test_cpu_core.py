@@ -165,3 +165,19 @@ def test_swa_running_mean():
     took = [snaps[s] for s in range(3, 12, 2)]
     assert swa.n == len(took) == 5
     torch.testing.assert_close(swa.avg, torch.stack(took).mean(0), rtol=1e-12, atol=1e-12)
+
+
+def test_parallel_plan_validates_and_selects():
+    from lora_kernel_b200.config import ParallelConfig
+    from lora_kernel_b200.train.trainer import parallel_plan
+    P = ParallelConfig
+    assert parallel_plan(P(), 1) == {"trainer": "single", "comm": "p2p"}
+    assert parallel_plan(P(zero_stage=3, fused_collectives=False), 8) == {"trainer": "zero3", "comm": "nccl"}
+    assert parallel_plan(P(dp=8, zero_stage=2), 8)["trainer"] == "dp"
+    assert parallel_plan(P(tp=8, fp8=True), 8)["trainer"] == "tp"
+    assert parallel_plan(P(cp=4, cp_mode="ring"), 4)["trainer"] == "cp"
+    for bad, msg in [(P(tp=2, pp=2), "cannot be combined"), (P(tp=4), "spans the whole job"),
+                     (P(dp=4), "data parallelism spans"), (P(cp=8, dp=8), "not combined"),
+                     (P(cp=8, cp_mode="tree"), "cp_mode"), (P(zero_stage=4), "zero_stage")]:
+        with pytest.raises(ValueError, match=msg):
+            parallel_plan(bad, 8)
