@@ -127,17 +127,9 @@ B200_BF16_DENSE_TFLOPS = 2250.0  # nominal dense bf16 tensor peak per GPU (no sp
 
 
 def train_flops_per_token(cfg, seq_len: int) -> float:
-    """Model FLOPs of one trained token (forward + backward = 3x forward):
-    6 x the GEMM parameters (the four linear layers of every block and the LM
-    head; the embedding gather does no math) plus causal attention, whose
-    QK^T and PV products average seq_len/2 keys per query:
-    3 x 2 x 2 x (seq_len/2) x heads x head_dim per layer."""
-    D, F, Dh = cfg.hidden_dim, cfg.ff_dim, cfg.head_dim
-    H, KV = cfg.num_heads, cfg.num_kv_heads
-    per_layer = D * (H + 2 * KV) * Dh + H * Dh * D + 3 * D * F
-    gemm = cfg.num_layers * per_layer + D * cfg.vocab_size
-    attn = cfg.num_layers * 6.0 * seq_len * H * Dh
-    return 6.0 * gemm + attn
+    """Model FLOPs of one trained token: TransformerConfig.flops_per_token
+    (6 x GEMM parameters + causal attention, forward and backward)."""
+    return cfg.flops_per_token(seq_len)
 
 
 def mfu(tokens_per_s: float, flops_per_token: float, n_gpus: int,
