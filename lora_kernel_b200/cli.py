@@ -1,7 +1,7 @@
 """Command line: `python -m lora_kernel_b200 {train,bench,serve,export,env}`.
 
   train  --preset NAME | --config FILE [--steps N] [--set section.key=value ...]
-         [--tp N --pp N --cp N --cp-mode ulysses|ring --zero 0-3 --fp8 --sp]
+         [--tp N --pp N --cp N --cp-mode ulysses|ring --zero 0-3 --fp8]
          [--lr X --micro-batch B --seq-len S --grad-accum K --metrics-file F]
          (launch with torch.distributed.run for more than one GPU)
   bench  [--gpus N --steps K --warmup W]   the headline training benchmark
@@ -39,7 +39,7 @@ def _overrides(items):
 # train flags that are shorthands for dotted overrides (applied after --set)
 TRAIN_FLAGS = {
     "tp": "parallel.tp", "pp": "parallel.pp", "cp": "parallel.cp", "cp_mode": "parallel.cp_mode",
-    "zero": "parallel.zero_stage", "fp8": "parallel.fp8", "sp": "parallel.sequence_parallel",
+    "zero": "parallel.zero_stage", "fp8": "parallel.fp8",
     "lr": "train.lr", "micro_batch": "train.micro_batch", "seq_len": "train.seq_len",
     "grad_accum": "train.grad_accum_steps", "metrics_file": "train.metrics_file",
 }
@@ -194,7 +194,6 @@ def main(argv=None):
     t.add_argument("--lr", type=float)
     t.add_argument("--metrics-file")
     t.add_argument("--fp8", action="store_true", help="block-scaled fp8 GEMMs (tensor parallel)")
-    t.add_argument("--sp", action="store_true", help="Megatron sequence parallelism (tensor parallel)")
     b = sub.add_parser("bench")
     b.add_argument("--gpus", type=int, default=1)
     b.add_argument("--kernels", action="store_true")

@@ -123,7 +123,7 @@ class ParallelConfig:
     cp: int = 1  # context parallelism: ranks share each sequence; spans the job
     cp_mode: str = "ulysses"  # ulysses (heads divisible by cp) | ring (zigzag chunks, any head count)
     zero_stage: int = 0  # 0, 1, 2, 3 (3 == FSDP)
-    sequence_parallel: bool = False
+    sequence_parallel: bool = True  # the tensor-parallel model keeps activations sequence-sharded (always)
     fused_collectives: bool = True  # False: the same schedules on NCCL collectives (library baseline)
     fuse_gather: bool = False  # ZeRO-3: parameter all-gather inside the first consuming GEMM (K17)
     fp8: bool = False

@@ -65,6 +65,9 @@ def parallel_plan(par, world: int) -> dict:
         raise ValueError(f"parallel.cp_mode must be one of {CP_MODES}, got {par.cp_mode!r}")
     if par.zero_stage not in (0, 1, 2, 3):
         raise ValueError(f"parallel.zero_stage must be 0..3, got {par.zero_stage}")
+    if par.tp > 1 and not par.sequence_parallel:
+        raise ValueError("parallel.sequence_parallel=False: the tensor-parallel model always keeps activations "
+                         "sequence-sharded between its fused all-gather and reduce-scatter GEMMs")
     comm = "p2p" if par.fused_collectives else "nccl"
     if world == 1:
         return {"trainer": "single", "comm": comm}

@@ -178,6 +178,7 @@ def test_parallel_plan_validates_and_selects():
     assert parallel_plan(P(cp=4, cp_mode="ring"), 4)["trainer"] == "cp"
     for bad, msg in [(P(tp=2, pp=2), "cannot be combined"), (P(tp=4), "spans the whole job"),
                      (P(dp=4), "data parallelism spans"), (P(cp=8, dp=8), "not combined"),
-                     (P(cp=8, cp_mode="tree"), "cp_mode"), (P(zero_stage=4), "zero_stage")]:
+                     (P(cp=8, cp_mode="tree"), "cp_mode"), (P(zero_stage=4), "zero_stage"),
+                     (P(tp=8, sequence_parallel=False), "sequence-sharded")]:
         with pytest.raises(ValueError, match=msg):
             parallel_plan(bad, 8)
