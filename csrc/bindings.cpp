@@ -913,6 +913,22 @@ void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, int6
                      stream()));
 }
 
+void sample_topp(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, int64_t seed,
+                 torch::Tensor out_tok) {
+  const c10::cuda::CUDAGuard g(logits.device());
+  need(logits, "logits", torch::kBFloat16);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample_topp: logits must be row-major 2-D");
+  need_contig(temperature, "temperature", torch::kFloat32);
+  need_contig(top_p, "top_p", torch::kFloat32);
+  need_contig(out_tok, "out_tok", torch::kInt64);
+  const int64_t rows = logits.size(0);
+  TORCH_CHECK(temperature.numel() >= rows && top_p.numel() >= rows && out_tok.numel() >= rows,
+              "sample_topp: one temperature, top_p and output per row");
+  check(lk_sample_topp(logits.data_ptr(), logits.stride(0), (int)rows, (int)logits.size(1),
+                       temperature.data_ptr<float>(), top_p.data_ptr<float>(), (uint64_t)seed,
+                       out_tok.data_ptr<int64_t>(), stream()));
+}
+
 void quantize(int64_t fmt, torch::Tensor w, int64_t group, torch::Tensor q, torch::Tensor scale,
               c10::optional<torch::Tensor> zero) {
   const c10::cuda::CUDAGuard g(w.device());
@@ -982,6 +998,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append", &kv_append);
   m.def("decode_attention", &decode_attention);
   m.def("sample", &sample);
+  m.def("sample_topp", &sample_topp);
   m.def("kv_gather", &kv_gather);
   m.def("quantize", &quantize);
   m.def("dequant_gemv", &dequant_gemv);

@@ -322,6 +322,108 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
   }
 }
 
+// Nucleus (top-p) sampling, one block per row.  For rows with temperature T > 0
+// and top_p p < 1 the nucleus is the smallest set of highest-scoring tokens whose
+// softmax(z / T) mass reaches p: the block finds the threshold t with a
+// bisection on the logit value (mass(t) = sum over z >= t of exp((z - max) / T),
+// monotone in t) between max - 40 T (below which a token's weight is under
+// e^-40) and max, 32 halvings, keeping mass(lo) >= p * total.  Bisection ends
+// far inside one bf16 spacing, so the set {z >= t} is the exact nucleus.  The
+// token is then the Gumbel-max over the nucleus with the same noise as
+// sample_kernel, which is an exact draw from the renormalised nucleus
+// distribution.  Rows with T <= 0 are greedy; rows with p >= 1 sample from
+// the whole vocabulary, as sample_kernel does.
+__device__ __forceinline__ float block_reduce_topp(float v, bool is_max, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red[] may still be read by the previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = is_max ? -INFINITY : 0.f;
+  for (int k = 0; k < nw; ++k) r = is_max ? fmaxf(r, red[k]) : r + red[k];
+  return r;
+}
+
+__global__ void sample_topp_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V,
+                                   const float* __restrict__ temperature, const float* __restrict__ top_p,
+                                   uint64_t seed, int64_t* __restrict__ out_tok) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const float temp = temperature ? temperature[row] : 0.f;
+  const float p = top_p ? top_p[row] : 1.f;
+  const __nv_bfloat16* z = logits + (int64_t)row * ld;
+  float thr = -INFINITY;
+  if (temp > 0.f && p < 1.f) {
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) m = fmaxf(m, __bfloat162float(z[j]));
+    m = block_reduce_topp(m, true, red);
+    const float inv_t = 1.f / temp;
+    float tot = 0.f;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) tot += __expf((__bfloat162float(z[j]) - m) * inv_t);
+    tot = block_reduce_topp(tot, false, red);
+    const float target = p * tot;
+    float lo = m - 40.f * temp, hi = m;
+#pragma unroll 1
+    for (int it = 0; it < 32; ++it) {
+      const float mid = 0.5f * (lo + hi);
+      float mass = 0.f;
+      for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = __bfloat162float(z[j]);
+        if (v >= mid) mass += __expf((v - m) * inv_t);
+      }
+      mass = block_reduce_topp(mass, false, red);
+      if (mass >= target) lo = mid;  // every thread holds the same sums, so the same branch
+      else hi = mid;
+    }
+    thr = lo;
+  }
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    float v = __bfloat162float(z[j]);
+    if (v < thr) continue;
+    if (temp > 0.f) {
+      const uint32_t h = mix32((uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U) ^
+                               mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
+      const float u = ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+      v = v / temp - logf(-logf(u));
+    }
+    if (v > best || (v == best && j < bi)) {
+      best = v;
+      bi = j;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sb[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+      if (sb[k] > best || (sb[k] == best && si[k] < bi)) {
+        best = sb[k];
+        bi = si[k];
+      }
+    out_tok[row] = bi;
+  }
+}
+
 template <int KV, int DH>
 static int launch_decode_g(const LkDecodeDesc& d, int G, int nsplit, int smem, cudaStream_t s) {
   dim3 grid(nsplit, d.Hkv, d.num_seqs);
@@ -426,6 +528,14 @@ extern "C" int lk_kv_gather(const void* k_cache, const void* v_cache, const floa
 extern "C" int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
                          uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s) {
   return lk_sample_vp(logits, ld, rows, V, 0, temperature, seed, out_tok, out_val, s);
+}
+
+extern "C" int lk_sample_topp(const void* logits, int64_t ld, int rows, int V, const float* temperature,
+                              const float* top_p, uint64_t seed, int64_t* out_tok, cudaStream_t s) {
+  LK_REQUIRE(V > 0, "sample_topp: empty vocabulary");
+  if (rows == 0) return 0;
+  sample_topp_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, top_p, seed, out_tok);
+  return check_launch("sample_topp");
 }
 
 // Vocabulary-parallel form: the logits hold columns [v0, v0 + V) of the

@@ -103,6 +103,10 @@ class LLMEngine:
             raise ValueError("empty prompt")
         if len(prompt) + (params.max_tokens if params else 16) > self.sc.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
+        if params is not None and params.top_p < 1.0 and params.temperature > 0 \
+                and not getattr(self.runner, "supports_top_p", False):
+            raise ValueError("top_p < 1 is not supported by this runner (tensor-parallel serving samples "
+                             "from vocabulary slices); use top_p = 1")
         r = Request(next(self.ids), list(prompt), params or SamplingParams(), priority,
                     self.clock() if arrival is None else arrival, on_token=on_token)
         self.stats["prompt_tokens"] += len(prompt)
@@ -199,7 +203,11 @@ class LLMEngine:
             tok = self.runner.sample(logits, None, 0)
         else:
             self._seed += 1
-            tok = self.runner.sample(logits, temps, self._seed)
+            top_ps = [r.params.top_p for r in reqs]
+            if any(p < 1.0 for p, t in zip(top_ps, temps) if t > 0):
+                tok = self.runner.sample(logits, temps, self._seed, top_ps=top_ps)
+            else:
+                tok = self.runner.sample(logits, temps, self._seed)
         return tok.tolist()
 
     def step(self) -> List[Request]:

@@ -153,9 +153,19 @@ class ModelRunner:
         xf, _, _ = N.rmsnorm_fwd(h_last, self.W["final_norm"], self.cfg.norm_eps)
         return G.linear(xf, self.W["lm_head"])
 
-    def sample(self, logits: torch.Tensor, temps: Optional[List[float]], seed: int) -> torch.Tensor:
-        """Next token per row (K19): greedy when temps is None, else Gumbel-max."""
+    # nucleus (top-p) sampling is a single-GPU kernel (the threshold needs the whole vocabulary)
+    supports_top_p = True
+
+    def sample(self, logits: torch.Tensor, temps: Optional[List[float]], seed: int,
+               top_ps: Optional[List[float]] = None) -> torch.Tensor:
+        """Next token per row (K19): greedy when temps is None, else Gumbel-max;
+        with top_ps, Gumbel-max over each row's top-p nucleus."""
         t = None if temps is None else torch.tensor(temps, dtype=torch.float32, device=logits.device)
+        if top_ps is not None:
+            if t is None:
+                t = torch.zeros(logits.shape[0], dtype=torch.float32, device=logits.device)
+            p = torch.tensor(top_ps, dtype=torch.float32, device=logits.device)
+            return SV.sample_topp(logits, t, p, seed)
         return SV.sample(logits, t, seed)
 
     # -------------------------------------------------------------- prefill

@@ -78,6 +78,9 @@ class TPServeComm:
 class TPModelRunner(ModelRunner):
     """ModelRunner over this rank's shard (`params`: parallel.tp.TPParams)."""
 
+    # each rank holds a vocabulary slice; the top-p threshold would need the whole row
+    supports_top_p = False
+
     def __init__(self, cfg: TransformerConfig, params, comm: TPServeComm, device="cuda", **kw):
         tp = comm.tp
         if cfg.num_heads % tp or cfg.num_kv_heads % tp:
@@ -157,6 +160,8 @@ def pick_global(allp: torch.Tensor) -> torch.Tensor:
 class RunnerProxy:
     """Rank 0's stand-in for the runner: broadcasts every call to the workers
     (CPU group) and runs it on its own shard."""
+
+    supports_top_p = False
 
     def __init__(self, runner: TPModelRunner, ctrl_group):
         self.runner = runner

@@ -117,3 +117,31 @@ def test_stop_tokens_and_priority():
     b = eng2.add_request([3, 4], SamplingParams(max_tokens=1), priority=-1)
     eng2.step()
     assert b in eng2.finished and a not in eng2.finished
+
+
+def test_top_p_reaches_a_runner_that_supports_it_and_is_refused_otherwise():
+    """Rows with temperature > 0 and top_p < 1 go to the runner's nucleus
+    sampler; a runner without one (tensor-parallel serving) refuses the
+    request instead of ignoring top_p; top_p = 1 keeps the plain call."""
+    eng, runner = _engine(100)
+    with pytest.raises(ValueError, match="top_p"):
+        eng.add_request([1, 2], SamplingParams(max_tokens=2, temperature=0.8, top_p=0.9))
+    eng.add_request([1, 2], SamplingParams(max_tokens=2, temperature=0.0, top_p=0.9))   # greedy: no nucleus
+    calls = []
+
+    class TopP(KVRunner):
+        supports_top_p = True
+
+        def sample(self, logits, temps, seed, top_ps=None):
+            calls.append((temps, top_ps))
+            return torch.argmax(logits, dim=-1)
+
+    sc = ServeConfig(num_kv_blocks=100, block_size=4, cuda_graphs=False, max_model_len=512)
+    eng = LLMEngine(TransformerConfig(vocab_size=V), None, sc, runner=TopP(100, 4))
+    p = [9, 8, 7]
+    out = eng.generate([p, p], SamplingParams(max_tokens=3, temperature=0.7, top_p=0.5))
+    assert out == [reference(p, 3)] * 2
+    assert calls and all(tp == [0.5] * len(t) for t, tp in calls)
+    calls.clear()
+    eng.generate([p], SamplingParams(max_tokens=2, temperature=0.7, top_p=1.0))
+    assert calls and all(tp is None for _, tp in calls)

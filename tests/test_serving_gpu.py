@@ -106,6 +106,43 @@ def test_sampling():
     assert torch.allclose(freq, p, atol=0.015), (freq, p)
 
 
+def test_top_p_sampling():
+    """Nucleus sampling: top_p = 1 rows equal the plain sampler (same noise),
+    temperature-0 rows are greedy, a nucleus of one token is always that token,
+    a two-token nucleus is drawn with its renormalised probabilities, and on a
+    32000-token vocabulary every draw lies in the fp64 reference nucleus."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.ops.serving import sample, sample_topp
+    row = torch.tensor([0.0, 1.0, 2.0, -1.0, 0.5, 0.0, 3.0, -2.0], device=dev)
+    n = 20000
+    z = row.repeat(n, 1).to(torch.bfloat16)
+    ones = torch.ones(n, device=dev)
+    plain = sample(z, ones, seed=7)
+    assert torch.equal(sample_topp(z, ones, ones, seed=7), plain)
+    greedy = sample_topp(z, torch.zeros(n, device=dev), torch.full((n,), 0.3, device=dev), seed=7)
+    assert bool((greedy == 6).all())
+    assert bool((sample_topp(z, ones, torch.full((n,), 0.5, device=dev), seed=3) == 6).all())
+    t = sample_topp(z, ones, torch.full((n,), 0.7, device=dev), seed=11)
+    freq = torch.bincount(t, minlength=8).float() / n
+    p = torch.softmax(row.double(), -1)
+    want = torch.zeros(8, dtype=torch.float64, device=dev)
+    want[[6, 2]] = p[[6, 2]] / p[[6, 2]].sum()
+    assert torch.allclose(freq.double(), want, atol=0.015), (freq, want)
+    # a real vocabulary: every draw is inside the reference nucleus (fp64, +1e-3 slack on p)
+    torch.manual_seed(5)
+    V, rows, top_p, temp = 32000, 64, 0.9, 0.8
+    logits = (torch.randn(rows, V, device=dev) * 3).to(torch.bfloat16)
+    tok = sample_topp(logits, torch.full((rows,), temp, device=dev), torch.full((rows,), top_p, device=dev), seed=9)
+    torch.cuda.synchronize()
+    check_status()
+    pr = torch.softmax(logits.double() / temp, -1)
+    srt, idx = pr.sort(-1, descending=True)
+    keep = (srt.cumsum(-1) - srt) < top_p + 1e-3          # tokens needed to reach top_p
+    for r in range(rows):
+        allowed = set(idx[r][keep[r]].tolist())
+        assert int(tok[r]) in allowed, (r, int(tok[r]), len(allowed))
+
+
 def _tiny_engine(kv="bf16", weights="none", prefix=True):
     from lora_kernel_b200.config import ServeConfig, TransformerConfig
     from lora_kernel_b200.models.params import FlatParams
