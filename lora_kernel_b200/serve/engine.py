@@ -40,7 +40,18 @@ class SamplingParams:
     temperature: float = 0.0
     top_p: float = 1.0
     stop_token_ids: tuple = ()
+    # token sequences that end generation when the output ends with one (the
+    # server's OpenAI `stop` strings, tokenized); the server leaves them out of the text
+    stop_sequences: tuple = ()
     seed: Optional[int] = None
+
+
+def _ends_with_any(out: List[int], seqs) -> bool:
+    for sq in seqs:
+        n = len(sq)
+        if n and len(out) >= n and tuple(out[-n:]) == tuple(sq):
+            return True
+    return False
 
 
 @dataclass
@@ -186,7 +197,7 @@ class LLMEngine:
         if r.first_token_time is None:
             r.first_token_time = now
         self.stats["generated_tokens"] += 1
-        if tok in r.params.stop_token_ids:
+        if tok in r.params.stop_token_ids or _ends_with_any(r.output, r.params.stop_sequences):
             r.finished, r.finish_reason = True, "stop"
         elif len(r.output) >= r.params.max_tokens:
             r.finished, r.finish_reason = True, "length"

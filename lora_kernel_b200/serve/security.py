@@ -1,7 +1,7 @@
 """Request and response policies for the HTTP server.
 
 InputValidator   prompt length, token-id range, max_tokens / temperature /
-                 top_p bounds; rejects with a message instead of letting a bad
+                 top_p bounds, stop strings; rejects with a message instead of letting a bad
                  request reach the engine.
 PIIMasker        masks e-mail addresses, phone numbers, US social-security
                  and payment-card numbers (Luhn-checked) in generated text.
@@ -55,6 +55,12 @@ class InputValidator:
         top_p = body.get("top_p", 1.0) or 1.0
         if not isinstance(top_p, (int, float)) or not 0.0 < float(top_p) <= 1.0:
             raise ValidationError("top_p must be in (0, 1]")
+        stop = body.get("stop")
+        if stop is not None:
+            seqs = [stop] if isinstance(stop, str) else stop
+            if not isinstance(seqs, list) or len(seqs) > 4 or \
+                    not all(isinstance(x, str) and 0 < len(x) <= 256 for x in seqs):
+                raise ValidationError("stop must be a string or a list of at most 4 non-empty strings")
 
 
 def _luhn_ok(digits: str) -> bool:

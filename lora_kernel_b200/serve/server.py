@@ -165,6 +165,34 @@ class EngineWorker:
                     self.m_itl.observe(b - a)
 
 
+class StopTrimmer:
+    """Releases generated tokens so that a matched stop sequence never reaches
+    the client: while a request runs, the last (longest stop length - 1)
+    tokens are held back (they could be the start of a stop sequence); when it
+    finishes with reason "stop" and its output ends with a stop sequence, that
+    sequence is dropped and the rest released (OpenAI `stop` semantics)."""
+
+    def __init__(self, stop_sequences=()):
+        self.stops = [tuple(sq) for sq in stop_sequences if sq]
+        self.hold = max((len(sq) for sq in self.stops), default=1) - 1
+        self.pending: List[int] = []
+
+    def push(self, tok_id: int, done: bool, reason: Optional[str]) -> List[int]:
+        self.pending.append(tok_id)
+        if done:
+            if reason == "stop":
+                for sq in self.stops:
+                    n = len(sq)
+                    if len(self.pending) >= n and tuple(self.pending[-n:]) == sq:
+                        del self.pending[-n:]
+                        break
+            out, self.pending = self.pending, []
+            return out
+        n = max(0, len(self.pending) - self.hold)
+        out, self.pending = self.pending[:n], self.pending[n:]
+        return out
+
+
 # ------------------------------------------------------------------- the app
 WORKER_KEY = web.AppKey("worker", object)
 
@@ -244,9 +272,14 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
 
     def _params(body) -> SamplingParams:
         stop = body.get("stop_token_ids") or ()
+        strs = body.get("stop") or ()
+        if isinstance(strs, str):
+            strs = (strs,)
+        seqs = tuple(tuple(tok.encode(x)) for x in strs if x)
         return SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
                               temperature=float(body.get("temperature", 0.0) or 0.0),
-                              top_p=float(body.get("top_p", 1.0) or 1.0), stop_token_ids=tuple(stop))
+                              top_p=float(body.get("top_p", 1.0) or 1.0), stop_token_ids=tuple(stop),
+                              stop_sequences=seqs)
 
     async def _run(prompt, params, stream: bool, request: web.Request, chat: bool):
         loop = asyncio.get_running_loop()
@@ -264,19 +297,22 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             idx = 0
             toks: List[int] = []
             sent = 0
-            while True:
-                t, done, reason = await q.get()
+            trim = StopTrimmer(params.stop_sequences)
+
+            async def send(t, last, reason):
+                nonlocal idx, sent
                 if masker is None:
-                    text = tok.decode([t])
+                    text = tok.decode([t]) if t is not None else ""
                 else:
                     # mask the whole text so far; release all but the last 64
                     # characters (a pattern shorter than that is final once it
                     # is out of the window)
-                    toks.append(t)
+                    if t is not None:
+                        toks.append(t)
                     full = masker.mask(tok.decode(toks))
-                    upto = len(full) if done else max(sent, len(full) - 64)
+                    upto = len(full) if last else max(sent, len(full) - 64)
                     text, sent = full[sent:upto], upto
-                choice = {"index": 0, "finish_reason": reason if done else None}
+                choice = {"index": 0, "finish_reason": reason if last else None}
                 if chat:
                     choice["delta"] = {"content": text}
                 else:
@@ -285,18 +321,28 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                          "model": model_name, "choices": [choice], "token": t, "index": idx}
                 await resp.write(f"data: {json.dumps(chunk)}\n\n".encode())
                 idx += 1
+
+            while True:
+                t, done, reason = await q.get()
+                ready = trim.push(t, done, reason)
+                for k, rt in enumerate(ready):
+                    await send(rt, done and k == len(ready) - 1, reason)
                 if done:
+                    if not ready:  # the stop sequence was all that was left
+                        await send(None, True, reason)
                     break
             await resp.write(b"data: [DONE]\n\n")
             await resp.write_eof()
             return resp
-        out, reason = [], None
+        out, kept, reason = [], [], None
+        trim = StopTrimmer(params.stop_sequences)
         while True:
             t, done, reason = await q.get()
             out.append(t)
+            kept += trim.push(t, done, reason)
             if done:
                 break
-        text = tok.decode(out)
+        text = tok.decode(kept)
         if masker is not None:
             text = masker.mask(text)
         choice = {"index": 0, "finish_reason": reason}
@@ -308,7 +354,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             "id": cid, "object": obj, "created": created, "model": model_name, "choices": [choice],
             "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out),
                       "total_tokens": len(prompt) + len(out)},
-            "token_ids": out})
+            "token_ids": kept})
 
     async def completions(request: web.Request):
         try:
@@ -372,18 +418,22 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                 q.put_nowait, (t, r.finished, r.finish_reason)))
             cid = f"ws-{uuid.uuid4().hex[:16]}"
             out: List[int] = []
+            kept: List[int] = []
+            trim = StopTrimmer(params.stop_sequences)
             while True:
                 t, done, reason = await q.get()
                 out.append(t)
-                text = tok.decode([t]) if masker is None else ""
-                await ws.send_json({"id": cid, "token": t, "index": len(out) - 1, "text": text})
+                for rt in trim.push(t, done, reason):
+                    kept.append(rt)
+                    text = tok.decode([rt]) if masker is None else ""
+                    await ws.send_json({"id": cid, "token": rt, "index": len(kept) - 1, "text": text})
                 if done:
                     break
             final = {"id": cid, "done": True, "finish_reason": reason,
                      "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                                "total_tokens": len(ids) + len(out)}}
             if masker is not None:
-                final["text"] = masker.mask(tok.decode(out))
+                final["text"] = masker.mask(tok.decode(kept))
             await ws.send_json(final)
         return ws
 

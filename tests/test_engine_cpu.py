@@ -145,3 +145,19 @@ def test_top_p_reaches_a_runner_that_supports_it_and_is_refused_otherwise():
     calls.clear()
     eng.generate([p], SamplingParams(max_tokens=2, temperature=0.7, top_p=1.0))
     assert calls and all(tp is None for _, tp in calls)
+
+
+def test_stop_sequences_end_generation():
+    """A request stops as soon as its output ends with one of its stop
+    sequences (finish reason "stop"); the engine keeps the tokens (the server
+    trims them)."""
+    eng, _ = _engine(100)
+    p = [11, 12, 13]
+    want = reference(p, 12)
+    seq = tuple(want[4:6])
+    rid = eng.add_request(p, SamplingParams(max_tokens=12, stop_sequences=((99, 98, 97), seq)))
+    while eng.has_work():
+        eng.step()
+    r = eng.finished[rid]
+    first = next(i for i in range(1, 12) if tuple(want[i - 1:i + 1]) == seq)
+    assert r.output == want[:first + 1] and r.finish_reason == "stop"

@@ -58,6 +58,9 @@ class FakeEngine:
             r.first_token_time = r.first_token_time or now
             if len(r.output) >= r.params.max_tokens:
                 r.finished, r.finish_reason = True, "length"
+            for sq in getattr(r.params, "stop_sequences", ()):
+                if sq and tuple(r.output[-len(sq):]) == tuple(sq):
+                    r.finished, r.finish_reason = True, "stop"
             r.on_token(r, t)
             if r.finished:
                 self.running.remove(r)
@@ -292,3 +295,36 @@ def test_training_flops_mfu_and_metrics_file(tmp_path):
     assert [r["step"] for r in lines] == [1, 2] and lines[1]["grad_norm"] == 1.5
     text = reg.exposition()
     assert "t_train_loss 2.0" in text and "t_train_mfu 0.5" in text and "t_train_step 2.0" in text
+
+
+def test_stop_trimmer_holds_back_and_drops_the_stop_sequence():
+    from lora_kernel_b200.serve.server import StopTrimmer
+    tr = StopTrimmer([(7, 8, 9), (5,)])
+    got = []
+    for t in [1, 2, 7, 8]:
+        got += tr.push(t, False, None)
+    assert got == [1, 2]                      # 7, 8 might start the stop sequence
+    got += tr.push(9, True, "stop")
+    assert got == [1, 2]                      # ... and did
+    tr = StopTrimmer([(7, 8, 9)])
+    assert tr.push(7, False, None) + tr.push(8, False, None) + tr.push(3, True, "length") == [7, 8, 3]
+    assert StopTrimmer().push(4, False, None) == [4]
+
+
+def test_stop_strings_over_http():
+    """`stop` ends generation at the first occurrence and is left out of the
+    text, in plain and streamed responses; bad `stop` values are rejected."""
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": "abcXYdef", "max_tokens": 30, "stop": ["XY", "zz"]})
+        d = await r.json()
+        assert d["choices"][0]["text"] == "abc" and d["choices"][0]["finish_reason"] == "stop", d
+        assert d["usage"]["completion_tokens"] == 5
+        r = await c.post("/v1/completions", json={"prompt": "abcXYdef", "max_tokens": 30, "stop": "XY",
+                                                  "stream": True})
+        body = (await r.read()).decode()
+        chunks = [json.loads(x[6:]) for x in body.split("\n\n") if x.startswith("data: {")]
+        assert "".join(ch["choices"][0]["text"] for ch in chunks) == "abc"
+        assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+        r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 3, "stop": ["a", "b", "c", "d", "e"]})
+        assert r.status == 400
+    _run(go)
