@@ -914,7 +914,7 @@ void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, int6
 }
 
 void sample_topp(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, int64_t seed,
-                 torch::Tensor out_tok) {
+                 c10::optional<torch::Tensor> row_seeds, torch::Tensor out_tok) {
   const c10::cuda::CUDAGuard g(logits.device());
   need(logits, "logits", torch::kBFloat16);
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample_topp: logits must be row-major 2-D");
@@ -924,8 +924,14 @@ void sample_topp(torch::Tensor logits, torch::Tensor temperature, torch::Tensor 
   const int64_t rows = logits.size(0);
   TORCH_CHECK(temperature.numel() >= rows && top_p.numel() >= rows && out_tok.numel() >= rows,
               "sample_topp: one temperature, top_p and output per row");
+  const uint64_t* rs = nullptr;
+  if (row_seeds.has_value()) {
+    need_contig(*row_seeds, "row_seeds", torch::kInt64);
+    TORCH_CHECK(row_seeds->numel() >= rows, "sample_topp: one seed per row");
+    rs = reinterpret_cast<const uint64_t*>(row_seeds->data_ptr<int64_t>());
+  }
   check(lk_sample_topp(logits.data_ptr(), logits.stride(0), (int)rows, (int)logits.size(1),
-                       temperature.data_ptr<float>(), top_p.data_ptr<float>(), (uint64_t)seed,
+                       temperature.data_ptr<float>(), top_p.data_ptr<float>(), (uint64_t)seed, rs,
                        out_tok.data_ptr<int64_t>(), stream()));
 }
 

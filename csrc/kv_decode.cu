@@ -332,7 +332,9 @@ __global__ void sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t 
 // token is then the Gumbel-max over the nucleus with the same noise as
 // sample_kernel, which is an exact draw from the renormalised nucleus
 // distribution.  Rows with T <= 0 are greedy; rows with p >= 1 sample from
-// the whole vocabulary, as sample_kernel does.
+// the whole vocabulary, as sample_kernel does.  With row_seeds, row r's noise
+// comes from row_seeds[r] alone (a request's draws then do not depend on which
+// batch row it lands in).
 __device__ __forceinline__ float block_reduce_topp(float v, bool is_max, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -350,7 +352,8 @@ __device__ __forceinline__ float block_reduce_topp(float v, bool is_max, float* 
 
 __global__ void sample_topp_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V,
                                    const float* __restrict__ temperature, const float* __restrict__ top_p,
-                                   uint64_t seed, int64_t* __restrict__ out_tok) {
+                                   uint64_t seed, const uint64_t* __restrict__ row_seeds,
+                                   int64_t* __restrict__ out_tok) {
   __shared__ float red[32];
   const int row = blockIdx.x;
   const float temp = temperature ? temperature[row] : 0.f;
@@ -387,8 +390,12 @@ __global__ void sample_topp_kernel(const __nv_bfloat16* __restrict__ logits, int
     float v = __bfloat162float(z[j]);
     if (v < thr) continue;
     if (temp > 0.f) {
-      const uint32_t h = mix32((uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U) ^
-                               mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
+      // without per-row seeds the noise is sample_kernel's, keyed by (seed, row);
+      // a per-row seed (a request's own stream) replaces that key
+      const uint32_t base = row_seeds
+          ? (uint32_t)row_seeds[row] ^ mix32((uint32_t)(row_seeds[row] >> 32))
+          : (uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U);
+      const uint32_t h = mix32(base ^ mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
       const float u = ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
       v = v / temp - logf(-logf(u));
     }
@@ -531,10 +538,12 @@ extern "C" int lk_sample(const void* logits, int64_t ld, int rows, int V, const 
 }
 
 extern "C" int lk_sample_topp(const void* logits, int64_t ld, int rows, int V, const float* temperature,
-                              const float* top_p, uint64_t seed, int64_t* out_tok, cudaStream_t s) {
+                              const float* top_p, uint64_t seed, const uint64_t* row_seeds, int64_t* out_tok,
+                              cudaStream_t s) {
   LK_REQUIRE(V > 0, "sample_topp: empty vocabulary");
   if (rows == 0) return 0;
-  sample_topp_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, top_p, seed, out_tok);
+  sample_topp_kernel<<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, top_p, seed, row_seeds,
+                                          out_tok);
   return check_launch("sample_topp");
 }
 

@@ -369,9 +369,11 @@ int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temp
 int lk_sample_vp(const void* logits, int64_t ld, int rows, int V, int64_t v0, const float* temperature,
                  uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s);
 // Nucleus sampling (one GPU): per-row temperature and top_p (rows with top_p >= 1
-// or temperature <= 0 behave as lk_sample).
+// or temperature <= 0 behave as lk_sample); optional per-row seeds (nullptr:
+// the noise of lk_sample for `seed`).
 int lk_sample_topp(const void* logits, int64_t ld, int rows, int V, const float* temperature,
-                   const float* top_p, uint64_t seed, int64_t* out_tok, cudaStream_t s);
+                   const float* top_p, uint64_t seed, const uint64_t* row_seeds, int64_t* out_tok,
+                   cudaStream_t s);
 
 // ------------------------------------------------------ K14 quantised weights
 enum LkQuantFmt { LK_Q_INT8 = 0, LK_Q_FP8 = 1, LK_Q_INT4 = 2 };

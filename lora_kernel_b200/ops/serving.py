@@ -69,14 +69,17 @@ def sample(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None, see
     return tok
 
 
-def sample_topp(logits: torch.Tensor, temperature: torch.Tensor, top_p: torch.Tensor, seed: int = 0) -> torch.Tensor:
+def sample_topp(logits: torch.Tensor, temperature: torch.Tensor, top_p: torch.Tensor, seed: int = 0,
+                row_seeds: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Nucleus sampling on one GPU: each row draws from softmax(logits / T)
     restricted to its smallest top set of probability mass >= top_p (rows with
-    T <= 0 are greedy, rows with top_p >= 1 sample from the whole vocabulary)."""
+    T <= 0 are greedy, rows with top_p >= 1 sample from the whole vocabulary).
+    row_seeds (int64 per row): each row's noise from its own seed instead of
+    (seed, row), so a request's draws do not depend on its batch row."""
     require_device(logits)
     tok = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
     C().sample_topp(logits, temperature.float().contiguous(), top_p.float().contiguous(),
-                    int(seed) & ((1 << 63) - 1), tok)
+                    int(seed) & ((1 << 63) - 1), row_seeds, tok)
     return tok
 
 

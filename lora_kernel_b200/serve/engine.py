@@ -46,6 +46,14 @@ class SamplingParams:
     seed: Optional[int] = None
 
 
+def _mix64(a: int, b: int) -> int:
+    """splitmix64 finaliser of a + golden-ratio * (b + 1): a 64-bit seed per (stream, index)."""
+    z = (int(a) + 0x9E3779B97F4A7C15 * (int(b) + 1)) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & 0xFFFFFFFFFFFFFFFF
+    return z ^ (z >> 31)
+
+
 def _ends_with_any(out: List[int], seqs) -> bool:
     for sq in seqs:
         n = len(sq)
@@ -114,10 +122,12 @@ class LLMEngine:
             raise ValueError("empty prompt")
         if len(prompt) + (params.max_tokens if params else 16) > self.sc.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
-        if params is not None and params.top_p < 1.0 and params.temperature > 0 \
-                and not getattr(self.runner, "supports_top_p", False):
-            raise ValueError("top_p < 1 is not supported by this runner (tensor-parallel serving samples "
-                             "from vocabulary slices); use top_p = 1")
+        if params is not None and params.temperature > 0 and not getattr(self.runner, "supports_top_p", False):
+            if params.top_p < 1.0:
+                raise ValueError("top_p < 1 is not supported by this runner (tensor-parallel serving samples "
+                                 "from vocabulary slices); use top_p = 1")
+            if params.seed is not None:
+                raise ValueError("per-request seeds are not supported by this runner (tensor-parallel serving)")
         r = Request(next(self.ids), list(prompt), params or SamplingParams(), priority,
                     self.clock() if arrival is None else arrival, on_token=on_token)
         self.stats["prompt_tokens"] += len(prompt)
@@ -214,11 +224,15 @@ class LLMEngine:
             tok = self.runner.sample(logits, None, 0)
         else:
             self._seed += 1
+            kw = {}
             top_ps = [r.params.top_p for r in reqs]
             if any(p < 1.0 for p, t in zip(top_ps, temps) if t > 0):
-                tok = self.runner.sample(logits, temps, self._seed, top_ps=top_ps)
-            else:
-                tok = self.runner.sample(logits, temps, self._seed)
+                kw["top_ps"] = top_ps
+            if any(r.params.seed is not None for r, t in zip(reqs, temps) if t > 0):
+                # a seeded request's draw k uses (its seed, k), whatever its batch row
+                kw["row_seeds"] = [_mix64(r.params.seed, len(r.output)) if r.params.seed is not None
+                                   else _mix64(self._seed, i) for i, r in enumerate(reqs)]
+            tok = self.runner.sample(logits, temps, self._seed, **kw)
         return tok.tolist()
 
     def step(self) -> List[Request]:

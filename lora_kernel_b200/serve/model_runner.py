@@ -153,19 +153,25 @@ class ModelRunner:
         xf, _, _ = N.rmsnorm_fwd(h_last, self.W["final_norm"], self.cfg.norm_eps)
         return G.linear(xf, self.W["lm_head"])
 
-    # nucleus (top-p) sampling is a single-GPU kernel (the threshold needs the whole vocabulary)
+    # nucleus (top-p) sampling and per-request seeds run on a single-GPU kernel
+    # (the nucleus threshold needs the whole vocabulary row)
     supports_top_p = True
 
     def sample(self, logits: torch.Tensor, temps: Optional[List[float]], seed: int,
-               top_ps: Optional[List[float]] = None) -> torch.Tensor:
+               top_ps: Optional[List[float]] = None, row_seeds: Optional[List[int]] = None) -> torch.Tensor:
         """Next token per row (K19): greedy when temps is None, else Gumbel-max;
-        with top_ps, Gumbel-max over each row's top-p nucleus."""
-        t = None if temps is None else torch.tensor(temps, dtype=torch.float32, device=logits.device)
-        if top_ps is not None:
+        with top_ps, Gumbel-max over each row's top-p nucleus; with row_seeds,
+        each row's noise from its own seed."""
+        n, dev = logits.shape[0], logits.device
+        t = None if temps is None else torch.tensor(temps, dtype=torch.float32, device=dev)
+        if top_ps is not None or row_seeds is not None:
             if t is None:
-                t = torch.zeros(logits.shape[0], dtype=torch.float32, device=logits.device)
-            p = torch.tensor(top_ps, dtype=torch.float32, device=logits.device)
-            return SV.sample_topp(logits, t, p, seed)
+                t = torch.zeros(n, dtype=torch.float32, device=dev)
+            p = torch.ones(n, dtype=torch.float32, device=dev) if top_ps is None else \
+                torch.tensor(top_ps, dtype=torch.float32, device=dev)
+            rs = None if row_seeds is None else \
+                torch.tensor([x & ((1 << 63) - 1) for x in row_seeds], dtype=torch.int64, device=dev)
+            return SV.sample_topp(logits, t, p, seed, row_seeds=rs)
         return SV.sample(logits, t, seed)
 
     # -------------------------------------------------------------- prefill

@@ -1,7 +1,7 @@
 """Request and response policies for the HTTP server.
 
 InputValidator   prompt length, token-id range, max_tokens / temperature /
-                 top_p bounds, stop strings; rejects with a message instead of letting a bad
+                 top_p bounds, stop strings, seed; rejects with a message instead of letting a bad
                  request reach the engine.
 PIIMasker        masks e-mail addresses, phone numbers, US social-security
                  and payment-card numbers (Luhn-checked) in generated text.
@@ -55,6 +55,9 @@ class InputValidator:
         top_p = body.get("top_p", 1.0) or 1.0
         if not isinstance(top_p, (int, float)) or not 0.0 < float(top_p) <= 1.0:
             raise ValidationError("top_p must be in (0, 1]")
+        seed = body.get("seed")
+        if seed is not None and (not isinstance(seed, int) or isinstance(seed, bool) or not 0 <= seed < 2 ** 63):
+            raise ValidationError("seed must be an integer in [0, 2^63)")
         stop = body.get("stop")
         if stop is not None:
             seqs = [stop] if isinstance(stop, str) else stop

@@ -279,7 +279,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         return SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
                               temperature=float(body.get("temperature", 0.0) or 0.0),
                               top_p=float(body.get("top_p", 1.0) or 1.0), stop_token_ids=tuple(stop),
-                              stop_sequences=seqs)
+                              stop_sequences=seqs, seed=body.get("seed"))
 
     async def _run(prompt, params, stream: bool, request: web.Request, chat: bool):
         loop = asyncio.get_running_loop()

@@ -161,3 +161,33 @@ def test_stop_sequences_end_generation():
     r = eng.finished[rid]
     first = next(i for i in range(1, 12) if tuple(want[i - 1:i + 1]) == seq)
     assert r.output == want[:first + 1] and r.finish_reason == "stop"
+
+
+def test_request_seeds_give_row_independent_noise():
+    """Seeded requests send one seed per row derived from (request seed, draw
+    index), so equal seeds give equal seeds per draw whatever the batch row;
+    a runner without per-row seeds refuses seeded sampling."""
+    eng, _ = _engine(100)
+    with pytest.raises(ValueError, match="seed"):
+        eng.add_request([1, 2], SamplingParams(max_tokens=2, temperature=0.5, seed=3))
+    calls = []
+
+    class Seeded(KVRunner):
+        supports_top_p = True
+
+        def sample(self, logits, temps, seed, top_ps=None, row_seeds=None):
+            calls.append(row_seeds)
+            return torch.argmax(logits, dim=-1)
+
+    sc = ServeConfig(num_kv_blocks=100, block_size=4, cuda_graphs=False, max_model_len=512)
+    eng = LLMEngine(TransformerConfig(vocab_size=V), None, sc, runner=Seeded(100, 4))
+    a = eng.add_request([5, 6], SamplingParams(max_tokens=3, temperature=0.9, seed=42))
+    b = eng.add_request([7, 8, 9], SamplingParams(max_tokens=3, temperature=0.9))
+    c = eng.add_request([5, 6], SamplingParams(max_tokens=3, temperature=0.9, seed=42))
+    while eng.has_work():
+        eng.step()
+    assert calls and all(rs is not None and len(rs) == 3 for rs in calls)
+    for rs in calls:   # rows a and c (same seed, same draw index) share a seed; b differs
+        assert rs[0] == rs[2] != rs[1]
+    assert len({rs[0] for rs in calls}) == len(calls)     # a new seed per draw
+    assert eng.finished[a].output == eng.finished[c].output

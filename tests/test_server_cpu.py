@@ -328,3 +328,12 @@ def test_stop_strings_over_http():
         r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 3, "stop": ["a", "b", "c", "d", "e"]})
         assert r.status == 400
     _run(go)
+
+
+def test_seed_validation():
+    from lora_kernel_b200.serve.security import InputValidator, ValidationError
+    v = InputValidator(256)
+    v.check([1], {"seed": 5})
+    for bad in (-1, 2 ** 63, "7", True, 1.5):
+        with pytest.raises(ValidationError, match="seed"):
+            v.check([1], {"seed": bad})

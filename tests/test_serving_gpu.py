@@ -143,6 +143,28 @@ def test_top_p_sampling():
         assert int(tok[r]) in allowed, (r, int(tok[r]), len(allowed))
 
 
+def test_per_row_seeds():
+    """With per-row seeds a row's draw depends only on its seed and logits, not
+    on its position in the batch; different seeds still follow the softmax."""
+    from lora_kernel_b200.ops.serving import sample_topp
+    torch.manual_seed(4)
+    rows, V = 256, 1000
+    logits = torch.randn(rows, V, device=dev).to(torch.bfloat16)
+    temp, ones = torch.full((rows,), 1.0, device=dev), torch.ones(rows, device=dev)
+    seeds = torch.randint(0, 2 ** 62, (rows,), device=dev)
+    a = sample_topp(logits, temp, ones, seed=1, row_seeds=seeds)
+    perm = torch.randperm(rows, device=dev)
+    b = sample_topp(logits[perm].contiguous(), temp, ones, seed=99, row_seeds=seeds[perm].contiguous())
+    assert torch.equal(a[perm], b)
+    # one logits row, 20000 different seeds: the softmax distribution
+    row = torch.tensor([0.0, 1.0, 2.0, -1.0, 0.5, 0.0, 3.0, -2.0], device=dev)
+    n = 20000
+    t = sample_topp(row.repeat(n, 1).to(torch.bfloat16), torch.ones(n, device=dev), torch.ones(n, device=dev),
+                    row_seeds=torch.arange(n, device=dev) * 7919 + 13)
+    freq = torch.bincount(t, minlength=8).float() / n
+    assert torch.allclose(freq, torch.softmax(row, -1), atol=0.015), freq
+
+
 def _tiny_engine(kv="bf16", weights="none", prefix=True):
     from lora_kernel_b200.config import ServeConfig, TransformerConfig
     from lora_kernel_b200.models.params import FlatParams
