@@ -1,8 +1,10 @@
 """Request and response policies for the HTTP server.
 
 InputValidator   prompt length, token-id range, max_tokens / temperature /
-                 top_p bounds, stop strings, seed; rejects with a message instead of letting a bad
-                 request reach the engine.
+                 top_p bounds, stop strings, seed; refuses the OpenAI
+                 options it does not implement (n > 1, penalties,
+                 logprobs) with a message instead of letting a bad request
+                 reach the engine or silently ignoring it.
 PIIMasker        masks e-mail addresses, phone numbers, US social-security
                  and payment-card numbers (Luhn-checked) in generated text.
 RoleAccess       role -> allowed path prefixes; the role comes from the JWT
@@ -55,6 +57,14 @@ class InputValidator:
         top_p = body.get("top_p", 1.0) or 1.0
         if not isinstance(top_p, (int, float)) or not 0.0 < float(top_p) <= 1.0:
             raise ValidationError("top_p must be in (0, 1]")
+        n = body.get("n", 1)
+        if n != 1:
+            raise ValidationError("n must be 1 (one choice per request)")
+        for k in ("presence_penalty", "frequency_penalty"):
+            if body.get(k, 0) not in (0, 0.0, None):
+                raise ValidationError(f"{k} is not supported (use 0)")
+        if body.get("logprobs") not in (None, False, 0):
+            raise ValidationError("logprobs are not returned by this server")
         seed = body.get("seed")
         if seed is not None and (not isinstance(seed, int) or isinstance(seed, bool) or not 0 <= seed < 2 ** 63):
             raise ValidationError("seed must be an integer in [0, 2^63)")

@@ -337,3 +337,13 @@ def test_seed_validation():
     for bad in (-1, 2 ** 63, "7", True, 1.5):
         with pytest.raises(ValidationError, match="seed"):
             v.check([1], {"seed": bad})
+
+
+def test_unimplemented_openai_options_are_refused():
+    from lora_kernel_b200.serve.security import InputValidator, ValidationError
+    v = InputValidator(256)
+    v.check([1], {"n": 1, "presence_penalty": 0, "logprobs": None})
+    for body, msg in [({"n": 2}, "n must be 1"), ({"frequency_penalty": 0.5}, "frequency_penalty"),
+                      ({"logprobs": 5}, "logprobs")]:
+        with pytest.raises(ValidationError, match=msg):
+            v.check([1], body)
