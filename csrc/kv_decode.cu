@@ -393,7 +393,7 @@ __global__ void sample_topp_kernel(const __nv_bfloat16* __restrict__ logits, int
       // without per-row seeds the noise is sample_kernel's, keyed by (seed, row);
       // a per-row seed (a request's own stream) replaces that key
       const uint32_t base = row_seeds
-          ? (uint32_t)row_seeds[row] ^ mix32((uint32_t)(row_seeds[row] >> 32))
+          ? mix32((uint32_t)row_seeds[row] ^ mix32((uint32_t)(row_seeds[row] >> 32)))
           : (uint32_t)seed ^ mix32((uint32_t)(seed >> 32) + row * 0x9e3779b9U);
       const uint32_t h = mix32(base ^ mix32((uint32_t)j * 0x85ebca6bU + 0x1234567U));
       const float u = ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
