@@ -2,7 +2,7 @@
 
   train  --preset NAME | --config FILE [--steps N] [--set section.key=value ...]
          [--tp N --pp N --cp N --cp-mode ulysses|ring --zero 0-3 --fp8]
-         [--lr X --micro-batch B --seq-len S --grad-accum K --metrics-file F]
+         [--lr X --micro-batch B --seq-len S --grad-accum K --metrics-file F] [--device cpu]
          (launch with torch.distributed.run for more than one GPU)
   bench  [--gpus N --steps K --warmup W]   the headline training benchmark
          [--kernels]                       kernel micro-benchmarks instead
@@ -57,9 +57,19 @@ def train_overrides(a) -> dict:
 
 def cmd_train(a):
     from .config import load_config
+    rc = load_config(a.config, a.preset, train_overrides(a))
+    if a.device == "cpu":
+        # fp32 on the host CPU with the oracle model (no B200 kernels)
+        from .train.cpu_demo import run_cpu
+        every = max(1, rc.train.log_every)
+        hist = run_cpu(rc, a.steps, log=lambda r: print(json.dumps(r)) if r["step"] % every == 0 else None)
+        if hist:
+            tps = sorted(r["tokens_per_s"] for r in hist[1:] or hist)
+            print(json.dumps({"summary": "train-cpu", "steps": len(hist), "loss_first": hist[0]["loss"],
+                              "loss_last": hist[-1]["loss"], "tokens_per_s_median": tps[len(tps) // 2]}))
+        return
     from .parallel.comm import init_distributed
     from .train.trainer import Trainer
-    rc = load_config(a.config, a.preset, train_overrides(a))
     if a.checkpoint_dir:
         rc.train.checkpoint_dir = a.checkpoint_dir
     init_distributed("nccl")
@@ -193,6 +203,8 @@ def main(argv=None):
     t.add_argument("--cp-mode", choices=["ulysses", "ring"])
     t.add_argument("--lr", type=float)
     t.add_argument("--metrics-file")
+    t.add_argument("--device", choices=["cuda", "cpu"], default="cuda",
+                   help="cpu: fp32 training on the host with the oracle model (no GPU needed)")
     t.add_argument("--fp8", action="store_true", help="block-scaled fp8 GEMMs (tensor parallel)")
     b = sub.add_parser("bench")
     b.add_argument("--gpus", type=int, default=1)

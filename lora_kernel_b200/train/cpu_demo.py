@@ -1,0 +1,65 @@
+"""fp32 training on the host CPU, for machines without a B200.
+
+The reference's only command-line behaviour is a CPU training demo
+(main.cpp:60-72; the CPU workload of its configuration 1: Llama-style 4 layers,
+d 256, 4 heads x 64, ffn 688, vocab 1024, seq 128, batch 8, fp32, AdamW).  This
+module runs that workload on the CPU with the framework's fp32 oracle model
+(oracle/llama_ref.py: eager PyTorch, autograd) and torch's AdamW with global-norm
+clipping, so `train --device cpu` works where there is no GPU.  It is not the
+B200 path (that is train/pipeline.py and the sm_100a kernels) and it computes
+the same standard Llama decoder: pre-norm RMSNorm, RoPE per head, GQA attention
+with an output projection, SwiGLU with ff_dim, final norm.
+"""
+from __future__ import annotations
+
+import time
+from typing import Callable, List, Optional
+
+import torch
+
+from ..config import RunConfig
+
+
+def run_cpu(rc: RunConfig, steps: Optional[int] = None, log: Optional[Callable[[dict], None]] = None,
+            threads: int = 0) -> List[dict]:
+    """Train rc.model on the CPU in fp32 for `steps` (default
+    rc.train.total_steps) optimizer steps; returns one record per step
+    (step, loss, lr, tokens_per_s) and calls `log` with each."""
+    from ..models.params import FlatParams
+    from ..oracle.llama_ref import OracleTrainer, loss_fn
+    from .schedules import lr_at
+    if threads:
+        torch.set_num_threads(threads)
+    cfg, tc = rc.model, rc.train
+    total = steps if steps is not None else tc.total_steps
+    params = FlatParams(cfg, "cpu", torch.float32)
+    params.init_(tc.seed, cfg.init_std)
+    decay = {k: (v.dim() > 1) or tc.decay_norms for k, v in params.views.items()}
+    tr = OracleTrainer(dict(params.views), cfg, lr=tc.lr, wd=tc.weight_decay, betas=(tc.beta1, tc.beta2),
+                       eps=tc.eps, max_norm=tc.max_grad_norm, decay=decay)
+    g = torch.Generator().manual_seed(tc.seed)
+    B, S = tc.micro_batch, tc.seq_len
+    fixed = torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g) if tc.fixed_batch else None
+    out: List[dict] = []
+    for step in range(total):
+        lr = lr_at(step, tc.lr, tc.schedule, tc.warmup_steps, total, tc.min_lr_ratio)
+        for grp in tr.opt.param_groups:
+            grp["lr"] = lr
+        t0 = time.perf_counter()
+        loss = 0.0
+        tr.opt.zero_grad(set_to_none=True)
+        for _ in range(tc.grad_accum_steps):
+            ids = fixed if fixed is not None else torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g)
+            lv = loss_fn(tr.params, cfg, ids[:, :-1], ids[:, 1:]) / tc.grad_accum_steps
+            lv.backward()
+            loss += float(lv.detach())
+        if tr.max_norm > 0:
+            torch.nn.utils.clip_grad_norm_(list(tr.params.values()), tr.max_norm)
+        tr.opt.step()
+        dt = time.perf_counter() - t0
+        rec = {"step": step + 1, "loss": loss, "lr": lr,
+               "tokens_per_s": B * S * tc.grad_accum_steps / dt, "device": "cpu", "dtype": "float32"}
+        out.append(rec)
+        if log is not None:
+            log(rec)
+    return out

@@ -182,3 +182,17 @@ def test_parallel_plan_validates_and_selects():
                      (P(tp=8, sequence_parallel=False), "sequence-sharded")]:
         with pytest.raises(ValueError, match=msg):
             parallel_plan(bad, 8)
+
+
+def test_cpu_training_path_runs_and_learns():
+    """`train --device cpu`: fp32 oracle model + AdamW on the host, on a fixed batch."""
+    from lora_kernel_b200.config import get_preset
+    from lora_kernel_b200.train.cpu_demo import run_cpu
+    rc = get_preset("cpu-demo")
+    rc.model.num_layers, rc.train.micro_batch, rc.train.seq_len, rc.train.lr = 1, 2, 32, 3e-3
+    seen = []
+    hist = run_cpu(rc, steps=8, log=seen.append)
+    assert len(hist) == len(seen) == 8 and hist[-1]["step"] == 8
+    assert abs(hist[0]["loss"] - math.log(rc.model.vocab_size)) < 0.2
+    assert hist[-1]["loss"] < hist[0]["loss"] - 0.3
+    assert all(r["tokens_per_s"] > 0 and r["dtype"] == "float32" for r in hist)
