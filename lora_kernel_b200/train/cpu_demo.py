@@ -1,8 +1,9 @@
 """fp32 training on the host CPU, for machines without a B200.
 
 The reference's only command-line behaviour is a CPU training demo
-(main.cpp:60-72; the CPU workload of its configuration 1: Llama-style 4 layers,
-d 256, 4 heads x 64, ffn 688, vocab 1024, seq 128, batch 8, fp32, AdamW).  This
+(main.cpp:60-72); the `cpu-demo` preset is that kind of workload at a fixed
+size: Llama-style 4 layers, d 256, 4 heads x 64, ffn 688, vocab 1024, seq 128,
+batch 8, fp32, AdamW.  This
 module runs that workload on the CPU with the framework's fp32 oracle model
 (oracle/llama_ref.py: eager PyTorch, autograd) and torch's AdamW with global-norm
 clipping, so `train --device cpu` works where there is no GPU.  It is not the
