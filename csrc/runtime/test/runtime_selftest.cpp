@@ -6,8 +6,8 @@
 // the concurrent paths.  Exit code 0 and the line "runtime selftest ok" mean
 // every check passed and no sanitizer report was raised.
 //
-// Reference: none as a program; the survey asks for the host code to be
-// ASAN/UBSAN clean in a CI job (the reference has no sanitizer configuration).
+// Reference: none (the reference has no sanitizer configuration); this keeps
+// the native host code ASan / UBSan / TSan clean in CI.
 #include <unistd.h>
 
 #include <algorithm>

@@ -39,8 +39,8 @@ The backward recomputes each block with the merged LSE and output, so the
 block gradients are exact parts of the full gradient; dK/dV accumulators
 (fp32) travel with their K/V and return to the owner after P hops.
 
-Reference: none (the survey lists context parallelism / ring attention /
-Ulysses as absent from the reference).
+Reference: none (the reference has no context parallelism, ring attention
+or Ulysses).
 """
 from __future__ import annotations
 
