@@ -38,7 +38,7 @@ import torch
 from aiohttp import WSMsgType, web
 
 from ..utils.logging import get_logger, log_fields
-from ..utils.metrics import REGISTRY
+from ..utils.metrics import REGISTRY, DeviceMetrics
 from .engine import LLMEngine, SamplingParams
 from .security import AuditLog, InputValidator, PIIMasker, RequestSigner, RoleAccess
 from .tokenizer import ByteTokenizer
@@ -210,6 +210,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
     token ids, sampling parameters) before it reaches the engine.  `engine`
     may be a list of engines: requests are then routed over the replicas by
     `replica_policy`."""
+    engines = list(engine) if isinstance(engine, (list, tuple)) else [engine]
     if isinstance(engine, (list, tuple)):
         # several replicas behind one server (serve/replicas.py)
         from .replicas import ReplicaPool
@@ -217,6 +218,10 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         engine = engine[0]
     else:
         worker = EngineWorker(engine)
+    # per-GPU memory / utilisation gauges, refreshed at each /metrics scrape
+    gpus = sorted({d.index for d in (getattr(getattr(e, "runner", None), "device", None) for e in engines)
+                   if isinstance(d, torch.device) and d.type == "cuda" and d.index is not None})
+    dev_metrics = [DeviceMetrics(i) for i in gpus]
     tok = tokenizer or ByteTokenizer(engine.cfg.vocab_size)
     bucket = TokenBucket(rate_limit_rps, max(1.0, rate_limit_rps * 2)) if rate_limit_rps > 0 else None
     keys = set(api_keys)
@@ -390,6 +395,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                                   "waiting": worker.waiting()})
 
     async def metrics(_):
+        for dm in dev_metrics:
+            dm.update()
         return web.Response(text=REGISTRY.exposition(), content_type="text/plain")
 
     async def websocket(request: web.Request):

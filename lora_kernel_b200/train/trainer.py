@@ -258,6 +258,8 @@ class Trainer:
         from ..utils.metrics import TrainMetrics, mfu, train_flops_per_token
         flops_tok = train_flops_per_token(self.rc.model, tc.seq_len)
         metrics = TrainMetrics(tc.metrics_file if self.rank == 0 else "")
+        from ..utils.metrics import DeviceMetrics
+        dev_metrics = DeviceMetrics(self.device.index or 0) if self.device.type == "cuda" else None
         t_last, s_last = time.perf_counter(), self.step
         while self.step < total:
             if self.hb is not None:
@@ -286,6 +288,9 @@ class Trainer:
                        "lr": o.lr, "tokens_per_s": tps, "mfu": mfu(tps, flops_tok, self.world)}
                 t_last, s_last = now, self.step
                 self.history.append(rec)
+                if dev_metrics is not None:
+                    dm = dev_metrics.update()
+                    rec["gpu_memory_peak_gb"] = round(dm.get("gpu_memory_peak_bytes", 0) / 2 ** 30, 3)
                 if self.rank == 0:
                     log_fields(log, "train", **rec)
                     metrics.record(rec)

@@ -40,14 +40,18 @@ class Counter(_Metric):
 class Gauge(_Metric):
     kind = "gauge"
 
-    def __init__(self, name, help=""):
+    def __init__(self, name, help="", labels: Optional[Dict[str, str]] = None):
         super().__init__(name, help)
         self.v = 0.0
+        self.labels = dict(labels or {})
 
     def set(self, v: float):
         self.v = float(v)
 
     def lines(self):
+        if self.labels:
+            lab = ",".join(f'{k}="{v}"' for k, v in sorted(self.labels.items()))
+            return [f"{self.name}{{{lab}}} {self.v}"]
         return [f"{self.name} {self.v}"]
 
 
@@ -104,19 +108,96 @@ class Registry:
     def counter(self, name, help="") -> Counter:
         return self._get(Counter, name, help)
 
-    def gauge(self, name, help="") -> Gauge:
-        return self._get(Gauge, name, help)
+    def gauge(self, name, help="", labels: Optional[Dict[str, str]] = None) -> Gauge:
+        if not labels:
+            return self._get(Gauge, name, help)
+        key = self.prefix + name + "{" + ",".join(f"{k}={v}" for k, v in sorted(labels.items())) + "}"
+        m = self.metrics.get(key)
+        if m is None:
+            m = self.metrics[key] = Gauge(self.prefix + name, help, labels)
+        return m
 
     def histogram(self, name, help="", **kw) -> Histogram:
         return self._get(Histogram, name, help, **kw)
 
     def exposition(self) -> str:
-        lines = []
+        """Prometheus text format; series of one name (labelled gauges) share
+        one HELP / TYPE header."""
+        lines, seen = [], set()
+        order: Dict[str, List[_Metric]] = {}
         for m in self.metrics.values():
-            lines.append(f"# HELP {m.name} {m.help}")
-            lines.append(f"# TYPE {m.name} {m.kind}")
-            lines.extend(m.lines())
+            order.setdefault(m.name, []).append(m)
+        for name, ms in order.items():
+            if name not in seen:
+                seen.add(name)
+                lines.append(f"# HELP {name} {ms[0].help}")
+                lines.append(f"# TYPE {name} {ms[0].kind}")
+            for m in ms:
+                lines.extend(m.lines())
         return "\n".join(lines) + "\n"
+
+
+class DeviceMetrics:
+    """Per-GPU gauges labelled gpu="<index>", refreshed by update(): device
+    memory of this process from the CUDA caching allocator (allocated,
+    reserved, peak allocated) and, through NVML (read-only queries), GPU
+    utilisation, memory in use by all processes, SM clock, power and
+    temperature.  Missing sources (no CUDA, no NVML) leave their gauges at 0.
+
+    Reference: GPUUtilizationTracker (a constant 75 %), MemoryProfiler and
+    PCIeMonitor (a constant) in include/monitoring/production_monitoring.hpp:122-159."""
+
+    FIELDS = {
+        "gpu_memory_allocated_bytes": "device memory held by live tensors of this process",
+        "gpu_memory_reserved_bytes": "device memory reserved by this process's caching allocator",
+        "gpu_memory_peak_bytes": "peak device memory held by tensors of this process",
+        "gpu_utilization_percent": "percent of time a kernel ran in the last sample period (NVML)",
+        "gpu_memory_used_bytes": "device memory used by all processes (NVML)",
+        "gpu_sm_clock_mhz": "SM clock (NVML)",
+        "gpu_power_watts": "board power draw (NVML)",
+        "gpu_temperature_celsius": "GPU temperature (NVML)",
+    }
+
+    def __init__(self, device_index: int = 0, registry: Optional["Registry"] = None, nvml=None):
+        self.idx = int(device_index)
+        reg = registry or REGISTRY
+        self.g = {k: reg.gauge(k, h, labels={"gpu": str(self.idx)}) for k, h in self.FIELDS.items()}
+        self._nvml, self._h = nvml, None
+
+    def _handle(self):
+        if self._h is None:
+            try:
+                if self._nvml is None:
+                    import pynvml
+                    self._nvml = pynvml
+                self._nvml.nvmlInit()
+                self._h = self._nvml.nvmlDeviceGetHandleByIndex(self.idx)
+            except Exception:
+                self._h = False
+        return self._h or None
+
+    def update(self) -> Dict[str, float]:
+        import torch
+        out: Dict[str, float] = {}
+        if torch.cuda.is_available() and self.idx < torch.cuda.device_count():
+            st = torch.cuda.memory_stats(self.idx)
+            out["gpu_memory_allocated_bytes"] = st.get("allocated_bytes.all.current", 0)
+            out["gpu_memory_reserved_bytes"] = st.get("reserved_bytes.all.current", 0)
+            out["gpu_memory_peak_bytes"] = st.get("allocated_bytes.all.peak", 0)
+        h = self._handle()
+        if h is not None:
+            n = self._nvml
+            try:
+                out["gpu_utilization_percent"] = n.nvmlDeviceGetUtilizationRates(h).gpu
+                out["gpu_memory_used_bytes"] = n.nvmlDeviceGetMemoryInfo(h).used
+                out["gpu_sm_clock_mhz"] = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
+                out["gpu_power_watts"] = n.nvmlDeviceGetPowerUsage(h) / 1000.0
+                out["gpu_temperature_celsius"] = n.nvmlDeviceGetTemperature(h, n.NVML_TEMPERATURE_GPU)
+            except Exception:
+                pass
+        for k, v in out.items():
+            self.g[k].set(v)
+        return out
 
 
 REGISTRY = Registry()

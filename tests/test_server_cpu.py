@@ -347,3 +347,49 @@ def test_unimplemented_openai_options_are_refused():
                       ({"logprobs": 5}, "logprobs")]:
         with pytest.raises(ValidationError, match=msg):
             v.check([1], body)
+
+
+def test_device_metrics_from_a_fake_nvml():
+    """DeviceMetrics reads NVML (read-only queries) into gpu-labelled gauges;
+    without CUDA or NVML the gauges stay at 0 and nothing raises."""
+    from types import SimpleNamespace
+    from lora_kernel_b200.utils.metrics import DeviceMetrics, Registry
+
+    class FakeNVML:
+        NVML_CLOCK_SM, NVML_TEMPERATURE_GPU = 1, 0
+
+        def nvmlInit(self):
+            pass
+
+        def nvmlDeviceGetHandleByIndex(self, i):
+            return ("h", i)
+
+        def nvmlDeviceGetUtilizationRates(self, h):
+            return SimpleNamespace(gpu=87, memory=40)
+
+        def nvmlDeviceGetMemoryInfo(self, h):
+            return SimpleNamespace(used=123 * 2 ** 20, total=180 * 2 ** 30)
+
+        def nvmlDeviceGetClockInfo(self, h, kind):
+            return 1845
+
+        def nvmlDeviceGetPowerUsage(self, h):
+            return 987654   # milliwatts
+
+        def nvmlDeviceGetTemperature(self, h, kind):
+            return 61
+
+    reg = Registry("t_")
+    got = DeviceMetrics(3, reg, nvml=FakeNVML()).update()
+    assert got["gpu_utilization_percent"] == 87 and got["gpu_sm_clock_mhz"] == 1845
+    text = reg.exposition()
+    assert 't_gpu_power_watts{gpu="3"} 987.654' in text and 't_gpu_temperature_celsius{gpu="3"} 61.0' in text
+    assert text.count("# TYPE t_gpu_power_watts gauge") == 1
+    DeviceMetrics(1, reg).update()      # second GPU's series under the same names, one header each
+    text = reg.exposition()
+    assert text.count("# TYPE t_gpu_power_watts gauge") == 1 and 't_gpu_power_watts{gpu="1"}' in text
+
+    class Broken(FakeNVML):
+        def nvmlInit(self):
+            raise RuntimeError("no driver")
+    assert DeviceMetrics(0, Registry("u_"), nvml=Broken()).update() == {}
