@@ -107,6 +107,8 @@ class TrainConfig:
     max_consecutive_skips: int = 20
     log_every: int = 10
     metrics_file: str = ""  # rank 0 appends one JSON line per logged step (loss, grad norm, tokens/s, MFU, ...)
+    curriculum_start_len: int = 0  # > 0: sequence length grows from this to seq_len over curriculum_steps
+    curriculum_steps: int = 0
     fixed_batch: bool = False  # reuse one seeded batch every step (the CPU demo's data)
     data_path: str = ""  # flat uint16/uint32 token file; empty = synthetic uniform ids
     data_dtype: str = "uint16"

@@ -253,6 +253,14 @@ class Trainer:
             if p:
                 self.load_checkpoint(p)
         self._install_signals()
+        curriculum = None
+        if tc.curriculum_start_len > 0:
+            if self.tp or self.pp:
+                raise NotImplementedError("train.curriculum_start_len: the tensor / pipeline-parallel trainers "
+                                          "keep one sequence length")
+            from ..utils.data import CurriculumScheduler
+            curriculum = CurriculumScheduler(tc.curriculum_start_len, tc.seq_len, max(1, tc.curriculum_steps),
+                                             multiple=min(128, tc.curriculum_start_len))
         tok_per_step = tc.micro_batch * tc.seq_len * tc.grad_accum_steps * (1 if (self.tp or self.pp or self.cp)
                                                                              else self.world)
         from ..utils.metrics import TrainMetrics, mfu, train_flops_per_token
@@ -261,6 +269,7 @@ class Trainer:
         from ..utils.metrics import DeviceMetrics
         dev_metrics = DeviceMetrics(self.device.index or 0) if self.device.type == "cuda" else None
         t_last, s_last = time.perf_counter(), self.step
+        tokens_done = 0
         while self.step < total:
             if self.hb is not None:
                 self.hb.set_step(self.step)
@@ -276,13 +285,21 @@ class Trainer:
                     x, y = self.data.next()
                     x = x.to(self.device, non_blocking=True)
                     y = y.to(self.device, non_blocking=True)
+                if curriculum is not None:
+                    x, y = curriculum.slice(x, y, self.step)
+                    tokens_done += x.numel()
                 self.pipe.micro_step_async(x, y)
             self.step += 1
             o = self.pipe.opt
             if self.step % tc.log_every == 0 or self.step == total:
                 s, n = self.pipe.loss_acc.tolist()
                 now = time.perf_counter()
-                tps = tok_per_step * (self.step - s_last) / (now - t_last)
+                steps_done = self.step - s_last
+                if curriculum is not None:  # tokens actually trained (x numel is per rank)
+                    scale = tok_per_step / (tc.micro_batch * tc.seq_len * tc.grad_accum_steps)
+                    tps, tokens_done = tokens_done * scale / (now - t_last), 0
+                else:
+                    tps = tok_per_step * steps_done / (now - t_last)
                 rec = {"step": self.step, "loss": s / max(n, 1.0), "grad_norm": o.grad_norm(),
                        "loss_scale": o.scaler.get_scale(), "skipped": o.scaler.num_skipped(),
                        "lr": o.lr, "tokens_per_s": tps, "mfu": mfu(tps, flops_tok, self.world)}

@@ -184,7 +184,12 @@ class MemmapTokens:
 
 class CurriculumScheduler:
     """Sequence length grows linearly from `start` to `end` over `steps`,
-    rounded to a multiple of `multiple`."""
+    rounded down to a multiple of `multiple` (at least `multiple`, at most
+    `end`).  The trainer keeps the first seq_len(step) tokens of each batch
+    (the targets stay the next tokens), so the loader and its resume cursor
+    are unchanged.
+
+    Reference: CurriculumScheduler (include/data/dataloader.hpp:185-200)."""
 
     def __init__(self, start: int, end: int, steps: int, multiple: int = 128):
         self.start, self.end, self.steps, self.multiple = start, end, steps, multiple
@@ -192,4 +197,11 @@ class CurriculumScheduler:
     def seq_len(self, step: int) -> int:
         f = min(1.0, step / max(1, self.steps))
         s = self.start + f * (self.end - self.start)
-        return max(self.multiple, int(s) // self.multiple * self.multiple)
+        return min(self.end, max(self.multiple, int(s) // self.multiple * self.multiple))
+
+    def slice(self, ids, targets, step: int):
+        """The first seq_len(step) positions of a batch [B, S] (contiguous)."""
+        n = self.seq_len(step)
+        if n >= ids.shape[1]:
+            return ids, targets
+        return ids[:, :n].contiguous(), targets[:, :n].contiguous()

@@ -196,3 +196,17 @@ def test_cpu_training_path_runs_and_learns():
     assert abs(hist[0]["loss"] - math.log(rc.model.vocab_size)) < 0.2
     assert hist[-1]["loss"] < hist[0]["loss"] - 0.3
     assert all(r["tokens_per_s"] > 0 and r["dtype"] == "float32" for r in hist)
+
+
+def test_curriculum_sequence_length_and_slice():
+    import torch
+    from lora_kernel_b200.utils.data import CurriculumScheduler
+    c = CurriculumScheduler(256, 2048, 100, multiple=128)
+    lens = [c.seq_len(s) for s in (0, 25, 50, 99, 100, 500)]
+    assert lens == [256, 640, 1152, 1920, 2048, 2048]
+    assert all(x % 128 == 0 for x in lens) and lens == sorted(lens)
+    ids = torch.arange(2 * 2048).view(2, 2048)
+    x, y = c.slice(ids, ids + 1, 0)
+    assert x.shape == (2, 256) and x.is_contiguous() and torch.equal(y, x + 1)
+    x, y = c.slice(ids, ids + 1, 1000)
+    assert x.data_ptr() == ids.data_ptr()
