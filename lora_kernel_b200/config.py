@@ -98,6 +98,8 @@ class TrainConfig:
     loss_scale_growth_interval: int = 2000
     ema_decay: float = 0.0  # 0 = off
     swa_start: int = -1  # -1 = off
+    grad_noise_eta: float = 0.0  # > 0: gradient noise N(0, eta / (1 + step)^gamma) before the optimizer
+    grad_noise_gamma: float = 0.55
     label_smoothing: float = 0.0
     z_loss: float = 0.0
     decay_norms: bool = False

@@ -145,7 +145,8 @@ class Trainer:
         self.step = 0
         self._stop = False
         self.faults = FaultInjector(self.rank)
-        self.pipe.pre_optimizer = lambda g: self.faults.on_grads(self.step, g)
+        self._noise_rank = self._grad_noise_rank(plan["trainer"], par.zero_stage) if tc.grad_noise_eta > 0 else None
+        self.pipe.pre_optimizer = self._pre_optimizer
         self.hb = None
         if self.world > 1 and os.environ.get("LORAK_HEARTBEAT", "1") == "1":
             store = dist.distributed_c10d._get_default_store()
@@ -233,6 +234,28 @@ class Trainer:
             else:  # data parallel: every rank holds the full bf16 parameters
                 self.pipe.params.flat.copy_(full_p32.to(self.device, torch.bfloat16))
         self._restore_trainer_state(path)
+
+    def _grad_noise_rank(self, trainer: str, zero_stage: int) -> int:
+        """-1 when every rank's optimizer sees the same (replicated) gradients,
+        so they must draw the same noise; the rank when each holds a shard."""
+        if trainer == "tp":
+            raise NotImplementedError("train.grad_noise_eta with tensor parallelism (replicated and sharded "
+                                      "gradients share one buffer)")
+        if trainer == "single" or (trainer in ("dp", "cp") and zero_stage == 0):
+            return -1
+        return self.rank
+
+    def _pre_optimizer(self, grads: torch.Tensor) -> None:
+        """Runs on the gradients the optimizer is about to use: host fault
+        injection, then optional gradient noise (in the loss-scaled units the
+        buffer holds)."""
+        self.faults.on_grads(self.step, grads)
+        tc = self.rc.train
+        if self._noise_rank is not None:
+            from ..utils.model_ops import gradient_noise_, noise_seed
+            g = torch.Generator(device=grads.device).manual_seed(noise_seed(tc.seed, self.step, self._noise_rank))
+            gradient_noise_(grads, self.step, tc.grad_noise_eta, tc.grad_noise_gamma, generator=g,
+                            scale=self.pipe.opt.scaler.scale_tensor())
 
     def _restore_trainer_state(self, path: str) -> None:
         st = Checkpointer.trainer_state(path)

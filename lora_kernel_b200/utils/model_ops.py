@@ -65,7 +65,20 @@ def prune_structured_rows(w: torch.Tensor, fraction: float) -> torch.Tensor:
 
 
 def gradient_noise_(grads: torch.Tensor, step: int, eta: float = 0.01, gamma: float = 0.55,
-                    generator=None) -> torch.Tensor:
-    """g += N(0, eta / (1 + step)^gamma)."""
+                    generator=None, scale=None) -> torch.Tensor:
+    """g += N(0, eta / (1 + step)^gamma) (Neelakantan et al. 2015).  `scale`
+    (a number or a device tensor, e.g. the dynamic loss scale that the stored
+    gradients still carry) multiplies the noise so it lands in the same units."""
     std = (eta / (1.0 + step) ** gamma) ** 0.5
-    return grads.add_(torch.randn(grads.shape, generator=generator, device=grads.device) * std)
+    noise = torch.randn(grads.shape, generator=generator, device=grads.device, dtype=grads.dtype).mul_(std)
+    if scale is not None:
+        noise.mul_(scale)
+    return grads.add_(noise)
+
+
+def noise_seed(seed: int, step: int, rank: int = -1) -> int:
+    """Generator seed of the gradient noise of one step: the same on every rank
+    when the gradients are replicated (rank = -1), distinct per rank when each
+    rank holds a different shard."""
+    z = (seed * 0x9E3779B97F4A7C15 + step * 0xBF58476D1CE4E5B9 + (rank + 1) * 0x94D049BB133111EB)
+    return z & ((1 << 63) - 1)

@@ -210,3 +210,27 @@ def test_curriculum_sequence_length_and_slice():
     assert x.shape == (2, 256) and x.is_contiguous() and torch.equal(y, x + 1)
     x, y = c.slice(ids, ids + 1, 1000)
     assert x.data_ptr() == ids.data_ptr()
+
+
+def test_gradient_noise_units_and_seeding():
+    """Noise variance eta / (1 + t)^gamma, multiplied by the loss scale the
+    stored gradients carry; replicated gradients draw the same noise on every
+    rank, shards draw their own; tensor parallelism refuses."""
+    from types import SimpleNamespace
+    import torch
+    from lora_kernel_b200.train.trainer import Trainer
+    from lora_kernel_b200.utils.model_ops import gradient_noise_, noise_seed
+    g = torch.zeros(200_000)
+    gen = torch.Generator().manual_seed(noise_seed(1, 9))
+    gradient_noise_(g, 9, eta=0.3, gamma=0.55, generator=gen, scale=torch.tensor([1024.0]))
+    want = 1024.0 * (0.3 / 10 ** 0.55) ** 0.5
+    assert abs(g.std().item() / want - 1) < 0.02
+    assert noise_seed(1, 9) == noise_seed(1, 9) != noise_seed(1, 10)
+    assert noise_seed(1, 9, 0) != noise_seed(1, 9, 1) != noise_seed(1, 9)
+    fake = SimpleNamespace(rank=3)
+    assert Trainer._grad_noise_rank(fake, "single", 0) == -1
+    assert Trainer._grad_noise_rank(fake, "dp", 0) == -1 and Trainer._grad_noise_rank(fake, "cp", 0) == -1
+    assert Trainer._grad_noise_rank(fake, "dp", 2) == 3 and Trainer._grad_noise_rank(fake, "zero3", 3) == 3
+    assert Trainer._grad_noise_rank(fake, "pp", 0) == 3
+    with pytest.raises(NotImplementedError):
+        Trainer._grad_noise_rank(fake, "tp", 0)
