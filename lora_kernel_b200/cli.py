@@ -9,7 +9,7 @@
          [--serve ...]                     serving load generator
   serve  --preset NAME [--port P] [--weights int4|int8|fp8|none] [--kv fp8|int8|bf16]
          [--replicas N --replica-policy prefix_affinity|least_loaded|round_robin]
-  export --out PATH [--format gguf|hf] [--dtype bf16|f16|f32] [--checkpoint model.safetensors]
+  export --out PATH [--format gguf|hf|onnx] [--dtype bf16|f16|f32] [--checkpoint model.safetensors]
   env    versions, GPU, NVLink, extension status
 
 Mirrors the reference's train / bench / serve verbs (README.md:107-115,
@@ -176,6 +176,11 @@ def cmd_export(a):
         p = FlatParams(cfg, "cpu", torch.float32)
         p.init_(rc.train.seed, cfg.init_std)
         sd = p.to_reference_state_dict()
+    if a.format == "onnx":
+        from .utils.onnx_export import export_onnx
+        export_onnx(sd, cfg, a.out)
+        print(json.dumps({"exported": a.out, "format": "onnx", "dtype": "f32"}))
+        return
     if a.format == "gguf":
         export_gguf(sd, cfg, a.out, dtype=a.dtype)
     else:
@@ -226,7 +231,7 @@ def main(argv=None):
     x.add_argument("--preset", default="cpu-demo")
     x.add_argument("--config")
     x.add_argument("--checkpoint", help="model.safetensors of a checkpoint (default: seeded weights)")
-    x.add_argument("--format", choices=["gguf", "hf"], default="gguf")
+    x.add_argument("--format", choices=["gguf", "hf", "onnx"], default="gguf")
     x.add_argument("--dtype", choices=["f32", "f16", "bf16"], default="bf16")
     x.add_argument("--out", required=True)
     x.add_argument("--set", nargs="*")

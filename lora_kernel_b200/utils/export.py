@@ -15,8 +15,9 @@ Hugging Face: `model.safetensors` + `config.json` for LlamaForCausalLM.  HF
 rotates dimension i with i + Dh/2, so every head's q/k rows are reordered
 (even dimensions first, then odd) to keep the same function.
 
-ONNX / TensorRT / OpenVINO export is not provided: none of those toolchains
-is part of this framework's runtime.
+ONNX export is in utils/onnx_export.py.  TensorRT and OpenVINO engines are
+built from an ONNX file by those toolchains, which are not part of this
+framework's runtime.
 
 Reference: ExportSuite::export_gguf / export_onnx / export_trt / export_ov
 (include/io/export_suite.hpp:7-13, print-only stubs).

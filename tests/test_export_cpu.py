@@ -48,3 +48,29 @@ def test_hf_export_matches_oracle(tmp_path):
     with torch.no_grad():
         got = hf(ids).logits
     assert torch.allclose(got, want, atol=1e-4, rtol=1e-4), (got - want).abs().max()
+
+
+@pytest.mark.parametrize("tie", [False, True])
+def test_onnx_export_reproduces_the_oracle(tmp_path, tie):
+    """The ONNX file parses back (IR 8, opset 17, standard operators only) and,
+    evaluated by the operator definitions with numpy, gives the fp32 oracle's
+    logits for two sequence lengths (symbolic sequence axis)."""
+    import dataclasses
+    from lora_kernel_b200.utils.onnx_export import export_onnx, load_onnx, run_onnx
+    cfg = dataclasses.replace(CFG, tie_embeddings=tie)
+    p = FlatParams(cfg, "cpu", torch.float32)
+    p.init_(3, 0.05)
+    path = str(tmp_path / "m.onnx")
+    export_onnx(p.to_reference_state_dict(), cfg, path)
+    m = load_onnx(path)
+    assert m["opset"] == 17 and m["inputs"] == ["input_ids"] and m["outputs"] == ["logits"]
+    ops = {n[0] for n in m["nodes"]}
+    assert ops <= {"Gather", "Shape", "Slice", "Concat", "Unsqueeze", "Reshape", "Transpose", "MatMul", "Add",
+                   "Sub", "Mul", "Div", "Sqrt", "Sigmoid", "ReduceMean", "Softmax"}
+    for S in (17, 40):
+        ids = torch.randint(0, cfg.vocab_size, (2, S), generator=torch.Generator().manual_seed(S))
+        want = llama_ref.forward({k: v for k, v in p.views.items()}, cfg, ids)
+        got = run_onnx(m, {"input_ids": ids.numpy().astype("int64")})["logits"]
+        assert got.shape == (2, S, cfg.vocab_size)
+        assert torch.allclose(torch.from_numpy(got), want, atol=1e-4, rtol=1e-4), \
+            (torch.from_numpy(got) - want).abs().max()
