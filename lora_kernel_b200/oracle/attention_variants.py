@@ -4,10 +4,11 @@ The B200 kernels implement causal / full / sliding-window GQA attention (the
 variants the Llama configurations use).  The rest of the reference's catalogue
 is provided here as plain PyTorch for experimentation and as oracles:
 MQA / GQA (K/V heads shared), sliding window, dilated, cross attention, ALiBi
-and learned relative position biases, and kernelised linear attention (elu+1
-feature map).  Reference: include/nn/attention_variants.hpp:14-424 (whose
-MQA/GQA running softmax is wrong and whose block-sparse / hybrid classes are
-stubs).
+and learned relative position biases, kernelised linear attention (elu+1
+feature map), block-sparse attention (local band of blocks + strided "summary"
+blocks, causal) and hybrid attention (some heads local, the others global).
+Reference: include/nn/attention_variants.hpp:14-424 (whose MQA/GQA running
+softmax is wrong and whose block-sparse / hybrid classes are stubs).
 """
 from __future__ import annotations
 
@@ -93,3 +94,25 @@ def linear_attention(q, k, v, causal: bool = True, eps: float = 1e-6):
         num = fq @ kv
         den = (fq @ fk.sum(2, keepdim=True).transpose(-1, -2))
     return num / (den + eps)
+
+
+def block_sparse_mask(S, block: int, local_blocks: int = 1, stride: int = 0, device=None):
+    """Causal block-sparse pattern (True = disallowed): query block i sees key
+    blocks i - local_blocks + 1 .. i, plus every block j with (j + 1) % stride
+    == 0 (fixed "summary" columns; stride 0 = none)."""
+    qb = torch.arange(S, device=device)[:, None] // block
+    kb = torch.arange(S, device=device)[None, :] // block
+    allowed = (kb <= qb) & (kb > qb - local_blocks)
+    if stride > 0:
+        allowed |= (kb <= qb) & ((kb + 1) % stride == 0)
+    return ~allowed | causal_mask(S, S, device)
+
+
+def hybrid_attention(q, k, v, local_heads: int, window: int):
+    """The first `local_heads` query heads attend within a causal sliding
+    window, the rest causally over the whole sequence."""
+    S = q.shape[2]
+    m = torch.stack([sliding_window_mask(S, window, q.device)] * local_heads +
+                    [causal_mask(S, S, q.device)] * (q.shape[1] - local_heads))
+    return attention(q, k, v, mask=m[None])
+

@@ -131,6 +131,15 @@ def test_attention_variants():
     assert A.RelativePositionBias(4)(8).shape == (4, 8, 8)
     lo = A.linear_attention(q, k, v, causal=True)
     assert lo.shape == (1, 4, 16, 8) and torch.isfinite(lo).all()
+    # block-sparse: a band covering every block is plain causal attention
+    assert torch.equal(A.block_sparse_mask(16, 4, local_blocks=4), A.causal_mask(16, 16))
+    m = A.block_sparse_mask(16, 4, local_blocks=1, stride=2)
+    assert not m[13, 12] and m[13, 8] and not m[13, 5] and m[13, 14] and m[2, 3]   # band, strided summary, causal
+    # hybrid: local heads see the window, global heads everything before them
+    hy = A.hybrid_attention(q, k, v, local_heads=2, window=3)
+    loc = A.attention(q, k, v, mask=A.sliding_window_mask(16, 3))
+    assert torch.allclose(hy[:, :2], loc[:, :2], atol=1e-6) and torch.allclose(hy[:, 2:], o[:, 2:], atol=1e-6)
+    assert torch.allclose(A.hybrid_attention(q, k, v, 4, 16), o, atol=1e-6)
 
 
 def test_quantized_checkpoint_roundtrip(tmp_path):
