@@ -131,7 +131,8 @@ def cmd_serve(a):
         eng = LLMEngine(cfg, None, sc, kv_dtype=kv, weights=weights, runner=proxy)
         try:
             serve(eng, host=a.host or sc.host, port=a.port or sc.port,
-                  api_keys=tuple(sc.api_keys), rate_limit_rps=sc.rate_limit_rps)
+                  api_keys=tuple(sc.api_keys), rate_limit_rps=sc.rate_limit_rps,
+                  max_inflight_per_client=sc.max_inflight_per_client)
         finally:
             proxy.stop()
             dist.destroy_process_group()
@@ -156,7 +157,7 @@ def cmd_serve(a):
                                  group_size=rc.quant.group_size))
     serve(engines[0] if n_rep == 1 else engines, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
           api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps,
-          replica_policy=a.replica_policy)
+          replica_policy=a.replica_policy, max_inflight_per_client=rc.serve.max_inflight_per_client)
 
 
 def cmd_export(a):

@@ -153,6 +153,7 @@ class ServeConfig:
     cuda_graphs: bool = True  # decode steps replayed from CUDA graphs (per batch-size bucket)
     api_keys: tuple = ()
     rate_limit_rps: float = 0.0
+    max_inflight_per_client: int = 0  # > 0: 429 for a client with this many requests running
 
 
 @dataclass

@@ -89,6 +89,46 @@ def _luhn_ok(digits: str) -> bool:
     return s % 10 == 0
 
 
+def sanitize_text(text: str, max_chars: int = 100_000) -> str:
+    """Prompt text with C0 control characters other than tab / newline /
+    carriage return replaced by spaces, cut to max_chars (reference:
+    TextSanitizer::sanitize, include/data/text_sanitizer.hpp:10-24)."""
+    out = "".join(c if (c >= " " or c in "\t\n\r") and c != "\x7f" else " " for c in text)
+    return out[:max_chars]
+
+
+class ConnectionLimiter:
+    """At most `limit` requests in flight per client (0 = unlimited): a
+    client that opens more gets 429 until one finishes (reference:
+    DDoSProtection, include/monitoring/production_monitoring.hpp:500-509, which
+    counts connections but never releases them)."""
+
+    def __init__(self, limit: int = 0):
+        self.limit = int(limit)
+        self.inflight: Dict[str, int] = {}
+        self._lock = threading.Lock()
+
+    def acquire(self, client: str) -> bool:
+        if self.limit <= 0:
+            return True
+        with self._lock:
+            n = self.inflight.get(client, 0)
+            if n >= self.limit:
+                return False
+            self.inflight[client] = n + 1
+            return True
+
+    def release(self, client: str) -> None:
+        if self.limit <= 0:
+            return
+        with self._lock:
+            n = self.inflight.get(client, 0) - 1
+            if n > 0:
+                self.inflight[client] = n
+            else:
+                self.inflight.pop(client, None)
+
+
 class PIIMasker:
     EMAIL = re.compile(r"[A-Za-z0-9._%+-]+@[A-Za-z0-9.-]+\.[A-Za-z]{2,}")
     SSN = re.compile(r"\b\d{3}-\d{2}-\d{4}\b")

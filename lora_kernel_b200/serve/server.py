@@ -40,7 +40,8 @@ from aiohttp import WSMsgType, web
 from ..utils.logging import get_logger, log_fields
 from ..utils.metrics import REGISTRY, DeviceMetrics
 from .engine import LLMEngine, SamplingParams
-from .security import AuditLog, InputValidator, PIIMasker, RequestSigner, RoleAccess
+from .security import (AuditLog, ConnectionLimiter, InputValidator, PIIMasker, RequestSigner, RoleAccess,
+                       sanitize_text)
 from .tokenizer import ByteTokenizer
 
 log = get_logger("lora_kernel.serve")
@@ -202,12 +203,15 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                tokenizer: Optional[ByteTokenizer] = None, *,
                validator: Optional[InputValidator] = None, pii_filter: bool = False,
                roles: Optional[RoleAccess] = None, signing_secret: str = "",
-               audit: Optional[AuditLog] = None, replica_policy: str = "least_loaded") -> web.Application:
+               audit: Optional[AuditLog] = None, replica_policy: str = "least_loaded",
+               sanitize_input: bool = True, max_inflight_per_client: int = 0) -> web.Application:
     """OpenAI-compatible app.  Optional policies: API keys / HS256 JWT bearer
     auth, token-bucket rate limit per client, role-based path access (JWT
     `role` claim or the key's role), HMAC request signatures, PII masking of
-    generated text, an audit log; every request is validated (prompt length,
-    token ids, sampling parameters) before it reaches the engine.  `engine`
+    generated text, an audit log, a per-client limit on requests in flight
+    (429 beyond it); prompt text has its control characters replaced
+    (sanitize_input) and every request is validated (prompt length, token
+    ids, sampling parameters) before it reaches the engine.  `engine`
     may be a list of engines: requests are then routed over the replicas by
     `replica_policy`."""
     engines = list(engine) if isinstance(engine, (list, tuple)) else [engine]
@@ -263,7 +267,13 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         t0 = time.perf_counter()
         resp = await _admit(request, who)
         if resp is None:
-            resp = await handler(request)
+            if not limiter.acquire(who["client"]):
+                resp = _err("too many requests in flight for this client", "rate_limited", 429)
+            else:
+                try:
+                    resp = await handler(request)
+                finally:
+                    limiter.release(who["client"])
         client, role = who["client"], who["role"]
         ms = round((time.perf_counter() - t0) * 1e3, 2)
         log_fields(log, "request", path=request.path, status=resp.status, client=client, ms=ms)
@@ -272,6 +282,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                          status=resp.status, ms=ms)
         return resp
 
+    limiter = ConnectionLimiter(max_inflight_per_client)
+    clean = sanitize_text if sanitize_input else (lambda t: t)
     app = web.Application(middlewares=[guard])
     loop_holder = {}
 
@@ -367,7 +379,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         except Exception:
             return web.json_response({"error": {"message": "invalid JSON", "type": "invalid_request"}}, status=400)
         prompt = body.get("prompt", "")
-        ids = prompt if isinstance(prompt, list) else tok.encode(str(prompt))
+        ids = prompt if isinstance(prompt, list) else tok.encode(clean(str(prompt)))
         try:
             validator.check(ids, body)
             return await _run(ids, _params(body), bool(body.get("stream")), request, chat=False)
@@ -379,7 +391,10 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             body = await request.json()
         except Exception:
             return web.json_response({"error": {"message": "invalid JSON", "type": "invalid_request"}}, status=400)
-        ids = tok.apply_chat_template(body.get("messages", []))
+        msgs = body.get("messages", [])
+        if isinstance(msgs, list):
+            msgs = [dict(m, content=clean(str(m.get("content", "")))) if isinstance(m, dict) else m for m in msgs]
+        ids = tok.apply_chat_template(msgs)
         try:
             validator.check(ids, body)
             return await _run(ids, _params(body), bool(body.get("stream")), request, chat=True)
@@ -414,7 +429,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
             try:
                 body = json.loads(msg.data)
                 prompt = body.get("prompt", "")
-                ids = prompt if isinstance(prompt, list) else tok.encode(str(prompt))
+                ids = prompt if isinstance(prompt, list) else tok.encode(clean(str(prompt)))
                 validator.check(ids, body)
                 params = _params(body)
             except (ValueError, AttributeError) as e:

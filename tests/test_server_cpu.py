@@ -393,3 +393,23 @@ def test_device_metrics_from_a_fake_nvml():
         def nvmlInit(self):
             raise RuntimeError("no driver")
     assert DeviceMetrics(0, Registry("u_"), nvml=Broken()).update() == {}
+
+
+def test_text_sanitizer_and_inflight_limit():
+    from lora_kernel_b200.serve.security import ConnectionLimiter, sanitize_text
+    assert sanitize_text("a\x00b\x1bc\td\ne\x7f") == "a b c\td\ne "
+    assert len(sanitize_text("x" * 10, max_chars=4)) == 4
+    lim = ConnectionLimiter(2)
+    assert lim.acquire("a") and lim.acquire("a") and not lim.acquire("a") and lim.acquire("b")
+    lim.release("a")
+    assert lim.acquire("a")
+    assert all(ConnectionLimiter(0).acquire("z") for _ in range(100))
+
+    async def go(c):
+        # control characters become spaces before tokenization (the echo engine returns the prompt)
+        r = await c.post("/v1/completions", json={"prompt": "a\x01b", "max_tokens": 3})
+        assert (await r.json())["choices"][0]["text"] == "a b"
+        for _ in range(3):   # the limit is released after every request
+            r = await c.post("/v1/completions", json={"prompt": "ok", "max_tokens": 2})
+            assert r.status == 200
+    _run(go, max_inflight_per_client=1)
