@@ -145,13 +145,19 @@ def cmd_serve(a):
     for g in range(n_rep):  # one independent engine per GPU
         dev = f"cuda:{g}"
         torch.cuda.set_device(g)
-        params = FlatParams(cfg, dev)
-        if a.checkpoint:
+        if a.checkpoint and a.checkpoint_format in ("gptq", "awq"):
+            # a 4-bit GPTQ / AWQ checkpoint of a Hugging Face Llama model
+            from .quant.gptq_awq import load_gptq_awq
+            params = load_gptq_awq(a.checkpoint, cfg, a.checkpoint_format, device=dev)
+            weights = "int4"
+        else:
+            params = FlatParams(cfg, dev)
+        if a.checkpoint and a.checkpoint_format == "safetensors":
             from .train.checkpoint import load_model_safetensors
             from .train.crypto import key_from_env
             sd = load_model_safetensors(a.checkpoint, key=key_from_env())
             params.load_reference_state_dict({k: v.to(dev) for k, v in sd.items()})
-        else:
+        elif not a.checkpoint:
             params.init_(rc.train.seed, cfg.init_std)
         engines.append(LLMEngine(cfg, params, rc.serve, device=dev, kv_dtype=kv, weights=weights,
                                  group_size=rc.quant.group_size))
@@ -227,6 +233,8 @@ def main(argv=None):
                    choices=["round_robin", "least_loaded", "prefix_affinity"])
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
+    s.add_argument("--checkpoint-format", choices=["safetensors", "gptq", "awq"], default="safetensors",
+                   help="gptq / awq: a 4-bit checkpoint of a Hugging Face Llama model")
     s.add_argument("--set", nargs="*")
     x = sub.add_parser("export")
     x.add_argument("--preset", default="cpu-demo")

@@ -12,7 +12,7 @@ are, the rest are copied).
 
 Reference: QuantizedModelLoader::load_awq / load_gptq
 (include/api/serving_production.hpp:231-241), a stub there; this loader reads what our own
-quantiser writes.
+quantiser writes, and quant/gptq_awq.py imports GPTQ / AWQ checkpoints.
 """
 from __future__ import annotations
 

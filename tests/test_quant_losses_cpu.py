@@ -159,3 +159,73 @@ def test_quantized_checkpoint_roundtrip(tmp_path):
     assert torch.equal(back["layers.0.wqkv"].q, w4.q) and torch.equal(back["layers.0.wqkv"].zero, w4.zero)
     assert back["layers.0.wo"].zero is None and torch.equal(back["layers.0.wo"].scale, w8.scale)
     assert torch.equal(back["embed"], emb) and back["lm_head"] is back["embed"]
+
+
+def _pack_int32(nibbles):
+    """[..., 8] codes 0..15 -> int32 words, nibble i at bits 4i (wrapping as int32)."""
+    import numpy as np
+    w = np.zeros(nibbles.shape[:-1], dtype=np.uint64)
+    for i in range(8):
+        w |= nibbles[..., i].astype(np.uint64) << np.uint64(4 * i)
+    return torch.from_numpy(w.astype(np.uint32).view(np.int32))
+
+
+def test_gptq_and_awq_unpacking():
+    """Codes, zero points and scales packed the GPTQ way (codes along K,
+    zeros minus one along N) and the AWQ way (codes along N in the order
+    0,2,4,6,1,3,5,7) come back as [N, K] codes with per-group scales/zeros."""
+    import numpy as np
+    from lora_kernel_b200.quant.gptq_awq import AWQ_ORDER, pack_nibbles, unpack_awq, unpack_gptq
+    rng = np.random.default_rng(0)
+    K, N, G = 256, 64, 128
+    codes = rng.integers(0, 16, (K, N))
+    zeros = rng.integers(1, 16, (K // G, N))
+    scales = torch.from_numpy(rng.random((K // G, N)).astype(np.float16))
+    want = torch.from_numpy((codes - np.repeat(zeros, G, 0)).astype(np.float32)).t() * \
+        scales.float().repeat_interleave(G, 0).t()
+    # GPTQ
+    qweight = _pack_int32(codes.reshape(K // 8, 8, N).transpose(0, 2, 1))
+    qzeros = _pack_int32((zeros - 1).reshape(K // G, N // 8, 8))
+    p = unpack_gptq(qweight, qzeros, scales, torch.arange(K, dtype=torch.int32) // G)
+    assert torch.equal(p.q.long(), torch.from_numpy(codes).t()) and p.group == G
+    assert torch.allclose(p.dequantize(), want)
+    with pytest.raises(NotImplementedError):
+        unpack_gptq(qweight, qzeros, scales, torch.randperm(K) // G)
+    # AWQ
+    order = list(AWQ_ORDER)
+    qweight = _pack_int32(codes.reshape(K, N // 8, 8)[..., order])
+    qzeros = _pack_int32(zeros.reshape(K // G, N // 8, 8)[..., order])
+    a = unpack_awq(qweight, qzeros, scales)
+    assert torch.equal(a.q.long(), torch.from_numpy(codes).t()) and torch.allclose(a.dequantize(), want)
+    # two codes per byte, the even column in the low nibble (the int4 kernels' layout)
+    pk = pack_nibbles(p.q)
+    assert pk.shape == (N, K // 2) and int(pk[3, 5]) == int(p.q[3, 10]) | (int(p.q[3, 11]) << 4)
+
+
+def test_llama_gptq_parts_map_to_the_engine_layout():
+    from lora_kernel_b200.config import TransformerConfig
+    from lora_kernel_b200.ops.gemm import split_gate_up
+    from lora_kernel_b200.quant.gptq_awq import Int4Parts, llama_parts_to_engine
+    from lora_kernel_b200.utils.export import _interleaved_to_half
+    cfg = TransformerConfig(hidden_dim=128, num_heads=4, num_kv_heads=2, head_dim=32, ff_dim=256,
+                            vocab_size=64, num_layers=1)
+    g = torch.Generator().manual_seed(1)
+
+    def rand(n, k):
+        return Int4Parts(torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8),
+                         torch.rand(n, k // 128, generator=g), torch.randint(0, 16, (n, k // 128), generator=g).float(),
+                         128)
+    p = "model.layers.0."
+    parts = {p + "self_attn.q_proj": rand(128, 128), p + "self_attn.k_proj": rand(64, 128),
+             p + "self_attn.v_proj": rand(64, 128), p + "self_attn.o_proj": rand(128, 128),
+             p + "mlp.gate_proj": rand(256, 128), p + "mlp.up_proj": rand(256, 128),
+             p + "mlp.down_proj": rand(128, 256)}
+    e = llama_parts_to_engine(parts, cfg)
+    qkv = e["layers.0.wqkv"].dequantize()
+    assert torch.equal(_interleaved_to_half(qkv[:128], 4, 32), parts[p + "self_attn.q_proj"].dequantize())
+    assert torch.equal(_interleaved_to_half(qkv[128:192], 2, 32), parts[p + "self_attn.k_proj"].dequantize())
+    assert torch.equal(qkv[192:], parts[p + "self_attn.v_proj"].dequantize())
+    gate, up = split_gate_up(e["layers.0.wgu"].dequantize())
+    assert torch.equal(gate, parts[p + "mlp.gate_proj"].dequantize())
+    assert torch.equal(up, parts[p + "mlp.up_proj"].dequantize())
+    assert e["layers.0.wdown"] is parts[p + "mlp.down_proj"]
