@@ -3,7 +3,7 @@
 Routes
   POST /v1/completions        {prompt (str | [ids]), max_tokens, temperature, top_p, stream, stop}
   POST /v1/chat/completions   {messages: [{role, content}], ...}
-  GET  /v1/models, /health, /metrics (Prometheus text)
+  GET  /v1/models, /health, /metrics (Prometheus text), /alerts (firing alert rules)
   GET  /v1/ws                 WebSocket: JSON requests in, one JSON message per token out
 Streaming responses are server-sent events: one `data: {json}\\n\\n` per token
 (OpenAI `choices[0].text` / `choices[0].delta.content`, plus the reference
@@ -38,7 +38,7 @@ import torch
 from aiohttp import WSMsgType, web
 
 from ..utils.logging import get_logger, log_fields
-from ..utils.metrics import REGISTRY, DeviceMetrics
+from ..utils.metrics import REGISTRY, AlertManager, AlertRule, DeviceMetrics
 from .engine import LLMEngine, SamplingParams
 from .security import (AuditLog, ConnectionLimiter, InputValidator, PIIMasker, RequestSigner, RoleAccess,
                        sanitize_text)
@@ -194,6 +194,14 @@ class StopTrimmer:
         return out
 
 
+# alert rules the server evaluates at GET /alerts unless create_app is given its own
+DEFAULT_ALERTS = (
+    AlertRule("kv_cache_nearly_full", "kv_cache_usage", ">=", 0.95, for_s=30.0),
+    AlertRule("ttft_p90_over_2s", "time_to_first_token_seconds", ">", 2.0, quantile=0.9),
+    AlertRule("requests_queued", "num_requests_waiting", ">", 64, for_s=30.0),
+)
+
+
 # ------------------------------------------------------------------- the app
 WORKER_KEY = web.AppKey("worker", object)
 
@@ -204,7 +212,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                validator: Optional[InputValidator] = None, pii_filter: bool = False,
                roles: Optional[RoleAccess] = None, signing_secret: str = "",
                audit: Optional[AuditLog] = None, replica_policy: str = "least_loaded",
-               sanitize_input: bool = True, max_inflight_per_client: int = 0) -> web.Application:
+               sanitize_input: bool = True, max_inflight_per_client: int = 0,
+               alert_rules=None) -> web.Application:
     """OpenAI-compatible app.  Optional policies: API keys / HS256 JWT bearer
     auth, token-bucket rate limit per client, role-based path access (JWT
     `role` claim or the key's role), HMAC request signatures, PII masking of
@@ -409,6 +418,13 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         return web.json_response({"status": "healthy", "running": worker.running(),
                                   "waiting": worker.waiting()})
 
+    alerts = AlertManager(alert_rules if alert_rules is not None else DEFAULT_ALERTS, log=log)
+
+    async def alerts_view(_):
+        for dm in dev_metrics:
+            dm.update()
+        return web.json_response({"firing": alerts.check()})
+
     async def metrics(_):
         for dm in dev_metrics:
             dm.update()
@@ -465,6 +481,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
     app.router.add_get("/v1/models", models)
     app.router.add_get("/health", health)
     app.router.add_get("/metrics", metrics)
+    app.router.add_get("/alerts", alerts_view)
 
     async def on_shutdown(_):
         worker.shutdown()

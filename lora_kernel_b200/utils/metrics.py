@@ -247,3 +247,64 @@ class TrainMetrics:
             self.f.close()
             self.f = None
 
+
+# ------------------------------------------------------------------ alerting
+class AlertRule:
+    """Fires while `metric` (a gauge or counter name without the registry
+    prefix, a histogram's quantile with `quantile`) compares `op` to
+    `threshold` (op: ">", ">=", "<", "<=") for at least `for_s` seconds."""
+
+    OPS = {">": lambda a, b: a > b, ">=": lambda a, b: a >= b, "<": lambda a, b: a < b, "<=": lambda a, b: a <= b}
+
+    def __init__(self, name: str, metric: str, op: str, threshold: float, for_s: float = 0.0,
+                 quantile: Optional[float] = None, labels: Optional[Dict[str, str]] = None):
+        if op not in self.OPS:
+            raise ValueError(f"alert op must be one of {sorted(self.OPS)}")
+        self.name, self.metric, self.op, self.threshold = name, metric, op, float(threshold)
+        self.for_s, self.quantile, self.labels = float(for_s), quantile, dict(labels or {})
+        self.since: Optional[float] = None
+
+
+class AlertManager:
+    """Evaluates alert rules over a Registry; `check(now)` returns the firing
+    alerts (name, metric, value, threshold) and logs each newly firing one.
+
+    Reference: AlertManager (include/monitoring/production_monitoring.hpp:185-196),
+    whose check_all returns nothing."""
+
+    def __init__(self, rules: Iterable[AlertRule], registry: Optional["Registry"] = None, log=None):
+        import copy
+        self.rules = [copy.copy(r) for r in rules]  # a rule's "since" state is per manager
+        self.reg = registry or REGISTRY
+        self.log = log
+        self.firing: Dict[str, dict] = {}
+
+    def _value(self, r: AlertRule) -> Optional[float]:
+        for m in self.reg.metrics.values():
+            if m.name != self.reg.prefix + r.metric:
+                continue
+            if isinstance(m, Histogram):
+                return m.quantile(r.quantile if r.quantile is not None else 0.5) if m.n else None
+            if getattr(m, "labels", {}) == r.labels or not r.labels:
+                return m.v
+        return None
+
+    def check(self, now: Optional[float] = None) -> List[dict]:
+        import time
+        now = time.monotonic() if now is None else now
+        out = []
+        for r in self.rules:
+            v = self._value(r)
+            if v is None or v != v or not AlertRule.OPS[r.op](v, r.threshold):
+                r.since = None
+                self.firing.pop(r.name, None)
+                continue
+            r.since = now if r.since is None else r.since
+            if now - r.since >= r.for_s:
+                alert = {"name": r.name, "metric": r.metric, "value": v, "op": r.op, "threshold": r.threshold}
+                if r.name not in self.firing and self.log is not None:
+                    self.log.warning("alert %s: %s %s %s (value %s)", r.name, r.metric, r.op, r.threshold, v)
+                self.firing[r.name] = alert
+                out.append(alert)
+        return out
+

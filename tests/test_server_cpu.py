@@ -99,6 +99,8 @@ def test_completion_json_schema():
         count = [ln for ln in text.splitlines() if ln.startswith("lora_kernel_request_queue_time_seconds_count")]
         assert count and float(count[0].split()[-1]) >= 2, text
         assert "lora_kernel_preemptions_total" in text
+        r = await c.get("/alerts")
+        assert r.status == 200 and (await r.json())["firing"] == []
     _run(go)
 
 
@@ -413,3 +415,23 @@ def test_text_sanitizer_and_inflight_limit():
             r = await c.post("/v1/completions", json={"prompt": "ok", "max_tokens": 2})
             assert r.status == 200
     _run(go, max_inflight_per_client=1)
+
+
+def test_alert_rules():
+    from lora_kernel_b200.utils.metrics import AlertManager, AlertRule, Registry
+    reg = Registry("a_")
+    g = reg.gauge("kv_cache_usage")
+    h = reg.histogram("time_to_first_token_seconds")
+    am = AlertManager([AlertRule("kv_full", "kv_cache_usage", ">=", 0.95, for_s=5.0),
+                       AlertRule("slow_ttft", "time_to_first_token_seconds", ">", 0.5, quantile=0.9),
+                       AlertRule("nothing", "missing_metric", ">", 0)], reg)
+    g.set(0.97)
+    assert am.check(now=0.0) == []                      # must hold for 5 s
+    assert [a["name"] for a in am.check(now=6.0)] == ["kv_full"]
+    for v in [0.1] * 5 + [0.9] * 5:
+        h.observe(v)
+    assert {a["name"] for a in am.check(now=7.0)} == {"kv_full", "slow_ttft"}
+    g.set(0.5)
+    assert [a["name"] for a in am.check(now=8.0)] == ["slow_ttft"] and "kv_full" not in am.firing
+    with pytest.raises(ValueError):
+        AlertRule("x", "m", "!=", 1)
