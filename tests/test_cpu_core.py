@@ -234,3 +234,18 @@ def test_gradient_noise_units_and_seeding():
     assert Trainer._grad_noise_rank(fake, "pp", 0) == 3
     with pytest.raises(NotImplementedError):
         Trainer._grad_noise_rank(fake, "tp", 0)
+
+
+def test_perf_regression_check(tmp_path):
+    from lora_kernel_b200.utils.perf_check import compare, last_json, main
+    ref = last_json("profiles/bench_llama1b_2gpu.json")       # a log: JSON after torchrun banner lines
+    assert ref["n_gpus"] == 2 and ref["value"] > 0
+    new = dict(ref, value=ref["value"] * 0.97)
+    assert compare(new, ref)["status"] == "ok"
+    assert compare(dict(ref, value=ref["value"] * 0.9), ref)["status"] == "regression"
+    assert compare(dict(ref, n_gpus=4), ref)["status"] == "not_comparable"
+    hot = dict(ref, clocks={"reasons": ["sw_power_cap", "hw_thermal_slowdown"]})
+    assert compare(hot, ref)["status"] == "not_comparable"
+    p = tmp_path / "new.json"
+    p.write_text("noise\n" + json.dumps(dict(ref, value=ref["value"] * 0.5)) + "\n")
+    assert main([str(p), "profiles/bench_llama1b_2gpu.json"]) == 1
