@@ -110,15 +110,25 @@ def cmd_serve(a):
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         # tensor-parallel serving under torchrun: rank 0 runs the HTTP server and
         # the scheduler, every rank its weight / KV-head shard
+        import torch
         import torch.distributed as dist
         from .parallel.comm import init_distributed
         from .serve.tp_runner import RunnerProxy, build_tp_runner, worker_loop
-        if a.checkpoint:
-            raise NotImplementedError("tensor-parallel serving starts from seeded weights; "
-                                      "load a checkpoint on one GPU")
-        rank, _, _ = init_distributed("nccl", timeout_s=3600)
+        if a.checkpoint and a.checkpoint_format != "safetensors":
+            raise NotImplementedError("tensor-parallel serving loads model.safetensors checkpoints; "
+                                      "serve GPTQ / AWQ files on one GPU or as replicas")
+        rank, world, _ = init_distributed("nccl", timeout_s=3600)
         sc = rc.serve
-        runner, ctrl = build_tp_runner(cfg, rc.train.seed, weights=weights, kv_dtype=kv,
+        tp_params = None
+        if a.checkpoint:  # every rank reads the file and keeps its shard
+            from .serve.tp_runner import tp_params_from_state_dict
+            from .train.checkpoint import load_model_safetensors
+            from .train.crypto import key_from_env
+            sd = load_model_safetensors(a.checkpoint, key=key_from_env())
+            dev = torch.device("cuda", torch.cuda.current_device())
+            tp_params = tp_params_from_state_dict(cfg, sd, world, rank, dev)
+            del sd
+        runner, ctrl = build_tp_runner(cfg, rc.train.seed, params=tp_params, weights=weights, kv_dtype=kv,
                                        group_size=rc.quant.group_size, block_size=sc.block_size,
                                        max_model_len=sc.max_model_len,
                                        max_rows=max(sc.max_num_batched_tokens, sc.max_num_seqs),

@@ -24,7 +24,7 @@ splits with an all-reduce.
 from __future__ import annotations
 
 import dataclasses
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -212,6 +212,21 @@ def worker_loop(runner: TPModelRunner, ctrl_group) -> None:
             runner.sample(logits, *arg)
         else:
             raise RuntimeError(f"unknown runner call {op!r}")
+
+
+def tp_params_from_state_dict(cfg: TransformerConfig, sd: Dict[str, torch.Tensor], tp: int, rank: int,
+                              device) -> "TPParams":
+    """This rank's shard of a reference-named state dict (a checkpoint's
+    model.safetensors): the full weights are laid out once on `device`, the
+    rank's slices copied out, and the full copy dropped."""
+    from ..models.params import FlatParams
+    from ..parallel.tp import TPParams
+    full = FlatParams(cfg, device)
+    full.load_reference_state_dict({k: v.to(device) for k, v in sd.items()})
+    params = TPParams(cfg, tp, rank, device)
+    params.load_full(full)
+    del full
+    return params
 
 
 def build_tp_runner(cfg: TransformerConfig, seed: int, *, weights: str = "none", kv_dtype: str = "fp8",
