@@ -99,6 +99,13 @@ def cmd_bench(a, rest):
     raise SystemExit(subprocess.call(cmd))
 
 
+def _tokenizer(a):
+    if not getattr(a, "tokenizer", None):
+        return None
+    from .serve.tokenizer import HFTokenizer
+    return HFTokenizer(a.tokenizer)
+
+
 def cmd_serve(a):
     from .config import load_config
     from .models.params import FlatParams
@@ -142,7 +149,7 @@ def cmd_serve(a):
         try:
             serve(eng, host=a.host or sc.host, port=a.port or sc.port,
                   api_keys=tuple(sc.api_keys), rate_limit_rps=sc.rate_limit_rps,
-                  max_inflight_per_client=sc.max_inflight_per_client)
+                  max_inflight_per_client=sc.max_inflight_per_client, tokenizer=_tokenizer(a))
         finally:
             proxy.stop()
             dist.destroy_process_group()
@@ -173,7 +180,8 @@ def cmd_serve(a):
                                  group_size=rc.quant.group_size))
     serve(engines[0] if n_rep == 1 else engines, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
           api_keys=tuple(rc.serve.api_keys), rate_limit_rps=rc.serve.rate_limit_rps,
-          replica_policy=a.replica_policy, max_inflight_per_client=rc.serve.max_inflight_per_client)
+          replica_policy=a.replica_policy, max_inflight_per_client=rc.serve.max_inflight_per_client,
+          tokenizer=_tokenizer(a))
 
 
 def cmd_export(a):
@@ -243,6 +251,7 @@ def main(argv=None):
                    choices=["round_robin", "least_loaded", "prefix_affinity"])
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
+    s.add_argument("--tokenizer", help="a Hugging Face tokenizer.json (default: bytes as token ids)")
     s.add_argument("--checkpoint-format", choices=["safetensors", "gptq", "awq"], default="safetensors",
                    help="gptq / awq: a 4-bit checkpoint of a Hugging Face Llama model")
     s.add_argument("--set", nargs="*")

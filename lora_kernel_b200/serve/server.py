@@ -208,7 +208,7 @@ WORKER_KEY = web.AppKey("worker", object)
 
 def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys=(),
                jwt_secret: str = "", rate_limit_rps: float = 0.0,
-               tokenizer: Optional[ByteTokenizer] = None, *,
+               tokenizer=None, *,
                validator: Optional[InputValidator] = None, pii_filter: bool = False,
                roles: Optional[RoleAccess] = None, signing_secret: str = "",
                audit: Optional[AuditLog] = None, replica_policy: str = "least_loaded",
@@ -297,7 +297,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
     loop_holder = {}
 
     def _params(body) -> SamplingParams:
-        stop = body.get("stop_token_ids") or ()
+        stop = tuple(body.get("stop_token_ids") or ()) + tuple(getattr(tok, "stop_ids", ()))
         strs = body.get("stop") or ()
         if isinstance(strs, str):
             strs = (strs,)

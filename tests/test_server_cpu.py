@@ -435,3 +435,37 @@ def test_alert_rules():
     assert [a["name"] for a in am.check(now=8.0)] == ["slow_ttft"] and "kv_full" not in am.firing
     with pytest.raises(ValueError):
         AlertRule("x", "m", "!=", 1)
+
+
+def _word_tokenizer(tmp_path, template=True):
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import Whitespace
+    words = ["<unk>", "</s>", "hello", "world", "user", "assistant", ":", "hi", "there"]
+    t = Tokenizer(WordLevel({w: i for i, w in enumerate(words)}, unk_token="<unk>"))
+    t.pre_tokenizer = Whitespace()
+    path = tmp_path / "tokenizer.json"
+    t.save(str(path))
+    if template:
+        (tmp_path / "tokenizer_config.json").write_text(json.dumps({
+            "eos_token": "</s>",
+            "chat_template": "{% for m in messages %}{{ m['role'] }} : {{ m['content'] }} {% endfor %}"
+                             "{% if add_generation_prompt %}assistant :{% endif %}"}))
+    return str(path)
+
+
+def test_hf_tokenizer_file(tmp_path):
+    from lora_kernel_b200.serve.tokenizer import HFTokenizer
+    tok = HFTokenizer(_word_tokenizer(tmp_path))
+    assert tok.encode("hello world") == [2, 3] and tok.decode([2, 3]) == "hello world"
+    assert tok.eos_token_id == 1 and tok.stop_ids == (1,)
+    assert tok.apply_chat_template([{"role": "user", "content": "hi there"}]) == [4, 6, 7, 8, 5, 6]
+    plain = HFTokenizer(_word_tokenizer(tmp_path / "x" if (tmp_path / "x").mkdir() is None else tmp_path,
+                                        template=False))
+    assert plain.stop_ids == () and plain.apply_chat_template([{"role": "user", "content": "hi"}])[:3] == [4, 6, 7]
+
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 3})
+        d = await r.json()
+        assert d["choices"][0]["text"] == "hello world hello" and d["usage"]["prompt_tokens"] == 2
+    _run(go, tokenizer=tok)
