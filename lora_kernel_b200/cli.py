@@ -112,16 +112,28 @@ def cmd_serve(a):
     from .serve.engine import LLMEngine
     from .serve.server import serve
     rc = load_config(a.config, a.preset, _overrides(a.set))
+    if a.checkpoint and a.checkpoint_format == "hf":  # the model shape comes with the checkpoint
+        from .utils.export import config_from_hf
+        rc.model = config_from_hf(a.checkpoint)
     cfg = rc.model
     kv, weights = a.kv or rc.quant.kv_cache, a.weights or rc.quant.weights
+
+    def read_state_dict():
+        if a.checkpoint_format == "hf":
+            from .utils.export import import_hf
+            return import_hf(a.checkpoint, cfg, dtype=torch.bfloat16)
+        from .train.checkpoint import load_model_safetensors
+        from .train.crypto import key_from_env
+        return load_model_safetensors(a.checkpoint, key=key_from_env())
+
+    import torch
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         # tensor-parallel serving under torchrun: rank 0 runs the HTTP server and
         # the scheduler, every rank its weight / KV-head shard
-        import torch
         import torch.distributed as dist
         from .parallel.comm import init_distributed
         from .serve.tp_runner import RunnerProxy, build_tp_runner, worker_loop
-        if a.checkpoint and a.checkpoint_format != "safetensors":
+        if a.checkpoint and a.checkpoint_format not in ("safetensors", "hf"):
             raise NotImplementedError("tensor-parallel serving loads model.safetensors checkpoints; "
                                       "serve GPTQ / AWQ files on one GPU or as replicas")
         rank, world, _ = init_distributed("nccl", timeout_s=3600)
@@ -129,9 +141,7 @@ def cmd_serve(a):
         tp_params = None
         if a.checkpoint:  # every rank reads the file and keeps its shard
             from .serve.tp_runner import tp_params_from_state_dict
-            from .train.checkpoint import load_model_safetensors
-            from .train.crypto import key_from_env
-            sd = load_model_safetensors(a.checkpoint, key=key_from_env())
+            sd = read_state_dict()
             dev = torch.device("cuda", torch.cuda.current_device())
             tp_params = tp_params_from_state_dict(cfg, sd, world, rank, dev)
             del sd
@@ -154,7 +164,6 @@ def cmd_serve(a):
             proxy.stop()
             dist.destroy_process_group()
         return
-    import torch
     engines = []
     n_rep = max(1, a.replicas)
     if n_rep > torch.cuda.device_count():
@@ -169,10 +178,8 @@ def cmd_serve(a):
             weights = "int4"
         else:
             params = FlatParams(cfg, dev)
-        if a.checkpoint and a.checkpoint_format == "safetensors":
-            from .train.checkpoint import load_model_safetensors
-            from .train.crypto import key_from_env
-            sd = load_model_safetensors(a.checkpoint, key=key_from_env())
+        if a.checkpoint and a.checkpoint_format in ("safetensors", "hf"):
+            sd = read_state_dict()
             params.load_reference_state_dict({k: v.to(dev) for k, v in sd.items()})
         elif not a.checkpoint:
             params.init_(rc.train.seed, cfg.init_std)
@@ -252,8 +259,9 @@ def main(argv=None):
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
     s.add_argument("--tokenizer", help="a Hugging Face tokenizer.json (default: bytes as token ids)")
-    s.add_argument("--checkpoint-format", choices=["safetensors", "gptq", "awq"], default="safetensors",
-                   help="gptq / awq: a 4-bit checkpoint of a Hugging Face Llama model")
+    s.add_argument("--checkpoint-format", choices=["safetensors", "hf", "gptq", "awq"], default="safetensors",
+                   help="hf: a Hugging Face Llama directory (config.json + safetensors); "
+                        "gptq / awq: a 4-bit checkpoint of a Hugging Face Llama model")
     s.add_argument("--set", nargs="*")
     x = sub.add_parser("export")
     x.add_argument("--preset", default="cpu-demo")

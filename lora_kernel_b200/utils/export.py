@@ -296,3 +296,59 @@ def export_hf(sd: Dict[str, torch.Tensor], cfg: TransformerConfig, out_dir: str,
     }
     with open(os.path.join(out_dir, "config.json"), "w") as f:
         json.dump(conf, f, indent=1)
+
+
+def _half_to_interleaved_rows(w_out_in: torch.Tensor, heads: int, dh: int) -> torch.Tensor:
+    """Inverse of _interleaved_to_half: rotate-half rows back to adjacent pairs."""
+    w = w_out_in.reshape(heads, 2, dh // 2, -1)
+    return torch.stack([w[:, 0], w[:, 1]], dim=2).reshape(heads * dh, -1)
+
+
+def config_from_hf(path: str) -> TransformerConfig:
+    """TransformerConfig from a Hugging Face LlamaForCausalLM config.json (or its directory)."""
+    if os.path.isdir(path):
+        path = os.path.join(path, "config.json")
+    with open(path) as f:
+        c = json.load(f)
+    H = c["num_attention_heads"]
+    return TransformerConfig(hidden_dim=c["hidden_size"], num_heads=H,
+                             num_kv_heads=c.get("num_key_value_heads", H),
+                             head_dim=c.get("head_dim") or c["hidden_size"] // H, ff_dim=c["intermediate_size"],
+                             vocab_size=c["vocab_size"], num_layers=c["num_hidden_layers"],
+                             max_seq_len=c.get("max_position_embeddings", 4096),
+                             norm_eps=c.get("rms_norm_eps", 1e-5), rope_base=float(c.get("rope_theta", 10000.0)),
+                             tie_embeddings=bool(c.get("tie_word_embeddings", False)))
+
+
+def import_hf(path: str, cfg: TransformerConfig, dtype: torch.dtype = torch.float32) -> Dict[str, torch.Tensor]:
+    """Reference-named state dict ([in, out] matrices, adjacent-pair RoPE rows)
+    from a Hugging Face Llama checkpoint: a directory with model.safetensors or
+    sharded model-*.safetensors (with or without the index file), or one file."""
+    from safetensors import safe_open
+    files = [path]
+    if os.path.isdir(path):
+        files = sorted(os.path.join(path, f) for f in os.listdir(path) if f.endswith(".safetensors"))
+    t: Dict[str, torch.Tensor] = {}
+    for fn in files:
+        with safe_open(fn, framework="pt") as f:
+            for k in f.keys():
+                t[k] = f.get_tensor(k)
+    H, KV, Dh = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    cv = (lambda x: x.to(dtype).contiguous())
+    sd = {"token_embedding.weight": cv(t["model.embed_tokens.weight"])}
+    for i in range(cfg.num_layers):
+        r, p = f"blocks.{i}.", f"model.layers.{i}."
+        sd[r + "attn.Wq.weight"] = cv(_half_to_interleaved_rows(t[p + "self_attn.q_proj.weight"], H, Dh).t())
+        sd[r + "attn.Wk.weight"] = cv(_half_to_interleaved_rows(t[p + "self_attn.k_proj.weight"], KV, Dh).t())
+        sd[r + "attn.Wv.weight"] = cv(t[p + "self_attn.v_proj.weight"].t())
+        sd[r + "attn.Wo.weight"] = cv(t[p + "self_attn.o_proj.weight"].t())
+        sd[r + "ffn.Wgate.weight"] = cv(t[p + "mlp.gate_proj.weight"].t())
+        sd[r + "ffn.Wup.weight"] = cv(t[p + "mlp.up_proj.weight"].t())
+        sd[r + "ffn.Wdown.weight"] = cv(t[p + "mlp.down_proj.weight"].t())
+        sd[r + "rms_norm_attn.weight"] = cv(t[p + "input_layernorm.weight"])
+        sd[r + "rms_norm_ffn.weight"] = cv(t[p + "post_attention_layernorm.weight"])
+    sd["final_norm.weight"] = cv(t["model.norm.weight"])
+    if not cfg.tie_embeddings:
+        sd["lm_head.weight"] = cv(t["lm_head.weight"].t())
+    return sd
+

@@ -74,3 +74,18 @@ def test_onnx_export_reproduces_the_oracle(tmp_path, tie):
         assert got.shape == (2, S, cfg.vocab_size)
         assert torch.allclose(torch.from_numpy(got), want, atol=1e-4, rtol=1e-4), \
             (torch.from_numpy(got) - want).abs().max()
+
+
+def test_hf_import_inverts_export(tmp_path):
+    from lora_kernel_b200.utils.export import config_from_hf, import_hf
+    p = _params()
+    sd = p.to_reference_state_dict()
+    export_hf(sd, CFG, str(tmp_path), dtype=torch.float32)
+    cfg = config_from_hf(str(tmp_path))
+    for k in ("hidden_dim", "num_heads", "num_kv_heads", "head_dim", "ff_dim", "vocab_size", "num_layers",
+              "norm_eps", "rope_base", "tie_embeddings"):
+        assert getattr(cfg, k) == getattr(CFG, k), k
+    back = import_hf(str(tmp_path), cfg)
+    assert set(back) == set(sd)
+    for k, v in sd.items():
+        assert torch.equal(back[k], v.float()), k
