@@ -104,6 +104,8 @@ class TrainConfig:
     z_loss: float = 0.0
     decay_norms: bool = False
     seed: int = 1234
+    init_from: str = ""  # start from pretrained weights: model.safetensors (reference names) or a HF directory
+    init_format: str = "safetensors"  # safetensors | hf
     checkpoint_dir: str = ""
     checkpoint_every: int = 0
     max_consecutive_skips: int = 20

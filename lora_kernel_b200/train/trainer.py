@@ -144,6 +144,14 @@ class Trainer:
                      if tc.checkpoint_dir else None)
         self.step = 0
         self._stop = False
+        if tc.init_from:
+            if tc.init_format == "hf":
+                from ..utils.export import import_hf
+                self.init_weights(import_hf(tc.init_from, cfg))
+            else:
+                from .checkpoint import load_model_safetensors
+                from .crypto import key_from_env
+                self.init_weights(load_model_safetensors(tc.init_from, key=key_from_env()))
         self.faults = FaultInjector(self.rank)
         self._noise_rank = self._grad_noise_rank(plan["trainer"], par.zero_stage) if tc.grad_noise_eta > 0 else None
         self.pipe.pre_optimizer = self._pre_optimizer
@@ -203,6 +211,30 @@ class Trainer:
         path = self.ckpt.save(self.step, model_state, self._ranges(), self._optim(),
                               _layout_info(cfg, self.align), state, async_save=async_save)
         return path
+
+    def init_weights(self, sd: Dict[str, torch.Tensor]) -> None:
+        """Start from pretrained weights (a reference-named state dict): the
+        fp32 master, its bf16 copies and the EMA take them, the AdamW moments
+        stay zero.  Single GPU and the data-parallel / ZeRO / context-parallel
+        trainers; a later checkpoint resume overrides it."""
+        if self.tp or self.pp:
+            raise NotImplementedError("train.init_from with tensor / pipeline parallelism")
+        from ..models.params import FlatParams
+        cpu = FlatParams(self.rc.model, "cpu", torch.float32)
+        cpu.load_reference_state_dict({k: v.float() for k, v in sd.items()})
+        full = remap_flat(cpu.flat, _layout_info(self.rc.model, 64), _layout_info(self.rc.model, self.align))
+        o = self.pipe.opt
+        with torch.no_grad():
+            dst = full if (self.world == 1 or self._dp_full_optimizer()) else self.pipe.L.extract_shard(full)
+            o.p32.copy_(dst.to(self.device))
+            if o.ema is not None:
+                o.ema.copy_(o.p32)
+            if self.world == 1:
+                self.pipe.engine.params.flat.copy_(o.p32.to(torch.bfloat16))
+            elif hasattr(self.pipe, "shard_p16"):
+                self.pipe.shard_p16.copy_(o.p32.to(torch.bfloat16))
+            else:  # data parallel: every rank holds the full bf16 parameters
+                self.pipe.params.flat.copy_(full.to(self.device, torch.bfloat16))
 
     def load_checkpoint(self, path: str) -> None:
         with open(os.path.join(path, "index.json")) as f:
