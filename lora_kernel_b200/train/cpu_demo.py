@@ -35,6 +35,15 @@ def run_cpu(rc: RunConfig, steps: Optional[int] = None, log: Optional[Callable[[
     total = steps if steps is not None else tc.total_steps
     params = FlatParams(cfg, "cpu", torch.float32)
     params.init_(tc.seed, cfg.init_std)
+    if tc.init_from:  # fine-tune pretrained weights
+        if tc.init_format == "hf":
+            from ..utils.export import import_hf
+            sd = import_hf(tc.init_from, cfg)
+        else:
+            from .checkpoint import load_model_safetensors
+            from .crypto import key_from_env
+            sd = load_model_safetensors(tc.init_from, key=key_from_env())
+        params.load_reference_state_dict({k: v.float() for k, v in sd.items()})
     decay = {k: (v.dim() > 1) or tc.decay_norms for k, v in params.views.items()}
     tr = OracleTrainer(dict(params.views), cfg, lr=tc.lr, wd=tc.weight_decay, betas=(tc.beta1, tc.beta2),
                        eps=tc.eps, max_norm=tc.max_grad_norm, decay=decay)

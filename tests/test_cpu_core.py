@@ -249,3 +249,29 @@ def test_perf_regression_check(tmp_path):
     p = tmp_path / "new.json"
     p.write_text("noise\n" + json.dumps(dict(ref, value=ref["value"] * 0.5)) + "\n")
     assert main([str(p), "profiles/bench_llama1b_2gpu.json"]) == 1
+
+
+def test_cpu_training_starts_from_pretrained_weights(tmp_path):
+    """train.init_from (reference safetensors and a Hugging Face directory):
+    the first step's loss is the loss of the loaded weights, not of a fresh init."""
+    import torch
+    from lora_kernel_b200.config import get_preset
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.oracle.llama_ref import loss_fn
+    from lora_kernel_b200.train.checkpoint import save_model_safetensors
+    from lora_kernel_b200.train.cpu_demo import run_cpu
+    from lora_kernel_b200.utils.export import export_hf
+    rc = get_preset("cpu-demo")
+    rc.model.num_layers, rc.train.micro_batch, rc.train.seq_len = 1, 2, 32
+    cfg, tc = rc.model, rc.train
+    src = FlatParams(cfg, "cpu", torch.float32)
+    src.init_(99, 0.2)                                   # far from the default init
+    g = torch.Generator().manual_seed(tc.seed)
+    ids = torch.randint(0, cfg.vocab_size, (tc.micro_batch, tc.seq_len + 1), generator=g)
+    want = float(loss_fn(dict(src.views), cfg, ids[:, :-1], ids[:, 1:]))
+    save_model_safetensors(src.to_reference_state_dict(), str(tmp_path / "model.safetensors"))
+    export_hf(src.to_reference_state_dict(), cfg, str(tmp_path / "hf"), dtype=torch.float32)
+    for path, fmt in ((str(tmp_path / "model.safetensors"), "safetensors"), (str(tmp_path / "hf"), "hf")):
+        tc.init_from, tc.init_format = path, fmt
+        first = run_cpu(rc, steps=1)[0]["loss"]
+        assert abs(first - want) < 1e-4, (fmt, first, want)
