@@ -43,6 +43,7 @@ TRAIN_FLAGS = {
     "lr": "train.lr", "micro_batch": "train.micro_batch", "seq_len": "train.seq_len",
     "grad_accum": "train.grad_accum_steps", "metrics_file": "train.metrics_file",
     "init_from": "train.init_from", "init_format": "train.init_format",
+    "lora_rank": "train.lora_rank", "lora_alpha": "train.lora_alpha",
 }
 
 
@@ -243,6 +244,8 @@ def main(argv=None):
     t.add_argument("--metrics-file")
     t.add_argument("--init-from", help="pretrained weights: model.safetensors or a Hugging Face directory")
     t.add_argument("--init-format", choices=["safetensors", "hf"])
+    t.add_argument("--lora-rank", type=int, help="train LoRA adapters of this rank on the frozen base (one GPU)")
+    t.add_argument("--lora-alpha", type=float)
     t.add_argument("--device", choices=["cuda", "cpu"], default="cuda",
                    help="cpu: fp32 training on the host with the oracle model (no GPU needed)")
     t.add_argument("--fp8", action="store_true", help="block-scaled fp8 GEMMs (tensor parallel)")

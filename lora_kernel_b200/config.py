@@ -104,6 +104,9 @@ class TrainConfig:
     z_loss: float = 0.0
     decay_norms: bool = False
     seed: int = 1234
+    lora_rank: int = 0  # > 0: train LoRA adapters of this rank on the frozen base (one GPU)
+    lora_alpha: float = 16.0
+    lora_targets: str = "wqkv,wo,wgu,wdown"
     init_from: str = ""  # start from pretrained weights: model.safetensors (reference names) or a HF directory
     init_format: str = "safetensors"  # safetensors | hf
     checkpoint_dir: str = ""

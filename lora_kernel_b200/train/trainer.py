@@ -91,10 +91,20 @@ class Trainer:
         self.world = dist.get_world_size() if dist.is_initialized() else 1
         self.rank = dist.get_rank() if dist.is_initialized() else 0
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        self.lora = tc.lora_rank > 0
+        if self.lora and self.world > 1:
+            raise NotImplementedError("train.lora_rank: LoRA fine-tuning runs on one GPU")
         if self.world == 1:
-            from .pipeline import Transformer, TrainingPipeline
+            from .pipeline import LoRATrainingPipeline, Transformer, TrainingPipeline
             self.model = Transformer(cfg, self.device, seed=tc.seed)
-            self.pipe = TrainingPipeline(self.model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
+            if self.lora:  # adapters on the frozen base weights (models/lora.py, fused into the GEMMs)
+                from ..models.lora import LoRAConfig
+                lc = LoRAConfig(rank=tc.lora_rank, alpha=tc.lora_alpha,
+                                targets=tuple(t for t in tc.lora_targets.split(",") if t), init_seed=tc.seed)
+                self.pipe = LoRATrainingPipeline(self.model, lc, tc.lr, tc.weight_decay, tc.max_grad_norm,
+                                                 train_cfg=tc)
+            else:
+                self.pipe = TrainingPipeline(self.model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
             self.align = 64
         par = rc.parallel
         plan = parallel_plan(par, self.world)
@@ -147,11 +157,16 @@ class Trainer:
         if tc.init_from:
             if tc.init_format == "hf":
                 from ..utils.export import import_hf
-                self.init_weights(import_hf(tc.init_from, cfg))
+                sd = import_hf(tc.init_from, cfg)
             else:
                 from .checkpoint import load_model_safetensors
                 from .crypto import key_from_env
-                self.init_weights(load_model_safetensors(tc.init_from, key=key_from_env()))
+                sd = load_model_safetensors(tc.init_from, key=key_from_env())
+            if self.lora:  # the frozen base takes the pretrained weights
+                self.model.load_state_dict(sd)
+            else:
+                self.init_weights(sd)
+            del sd
         self.faults = FaultInjector(self.rank)
         self._noise_rank = self._grad_noise_rank(plan["trainer"], par.zero_stage) if tc.grad_noise_eta > 0 else None
         self.pipe.pre_optimizer = self._pre_optimizer
@@ -195,6 +210,15 @@ class Trainer:
         if self.ckpt is None:
             return None
         cfg = self.rc.model
+        if self.lora:  # the adapters alone: lora_step_<N>.safetensors (rank / alpha in the metadata)
+            from safetensors.torch import save_file
+            lc = self.pipe.lora.lc
+            os.makedirs(self.rc.train.checkpoint_dir, exist_ok=True)
+            path = os.path.join(self.rc.train.checkpoint_dir, f"lora_step_{self.step}.safetensors")
+            save_file({k: v.detach().float().contiguous().cpu() for k, v in self.pipe.lora.state_dict().items()},
+                      path, metadata={"rank": str(lc.rank), "alpha": str(lc.alpha), "targets": ",".join(lc.targets),
+                                      "step": str(self.step)})
+            return path
         state = {"step": self.step, "data": self.data.state(), "config": to_dict(self.rc),
                  "world": self.world, "time": time.time()}
         if hasattr(self.pipe, "checkpoint_parts"):  # pipeline / tensor parallel
