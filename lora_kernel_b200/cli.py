@@ -185,6 +185,11 @@ def cmd_serve(a):
             params.load_reference_state_dict({k: v.to(dev) for k, v in sd.items()})
         elif not a.checkpoint:
             params.init_(rc.train.seed, cfg.init_std)
+        if a.lora:  # fold trained LoRA adapters into the base weights before serving
+            if a.checkpoint_format in ("gptq", "awq"):
+                raise NotImplementedError("--lora with a 4-bit checkpoint (merge into bf16 weights instead)")
+            from .models.lora import load_lora_file
+            load_lora_file(a.lora, cfg, dev).merge_into(params)
         engines.append(LLMEngine(cfg, params, rc.serve, device=dev, kv_dtype=kv, weights=weights,
                                  group_size=rc.quant.group_size))
     serve(engines[0] if n_rep == 1 else engines, host=a.host or rc.serve.host, port=a.port or rc.serve.port,
@@ -265,6 +270,7 @@ def main(argv=None):
     s.add_argument("--kv")
     s.add_argument("--checkpoint")
     s.add_argument("--tokenizer", help="a Hugging Face tokenizer.json (default: bytes as token ids)")
+    s.add_argument("--lora", help="LoRA adapters (lora_step_N.safetensors from train --lora-rank) merged at load")
     s.add_argument("--checkpoint-format", choices=["safetensors", "hf", "gptq", "awq"], default="safetensors",
                    help="hf: a Hugging Face Llama directory (config.json + safetensors); "
                         "gptq / awq: a 4-bit checkpoint of a Hugging Face Llama model")

@@ -128,3 +128,27 @@ class LoRAAdapters:
 
     def unmerge_from(self, params) -> None:
         self.merge_into(params, sign=-1.0)
+
+
+def save_lora_file(adapters: "LoRAAdapters", path: str, step: int = 0) -> None:
+    """The adapter tensors (fp32) with rank / alpha / targets in the metadata."""
+    from safetensors.torch import save_file
+    lc = adapters.lc
+    save_file({k: v.detach().float().contiguous().cpu() for k, v in adapters.state_dict().items()}, path,
+              metadata={"rank": str(lc.rank), "alpha": str(lc.alpha), "targets": ",".join(lc.targets),
+                        "step": str(step)})
+
+
+def load_lora_file(path: str, cfg: TransformerConfig, device="cuda") -> "LoRAAdapters":
+    """Adapters saved by the trainer (lora_step_N.safetensors: the adapter
+    tensors with rank / alpha / targets in the metadata)."""
+    from safetensors import safe_open
+    with safe_open(path, framework="pt") as f:
+        meta = f.metadata() or {}
+        tensors = {k: f.get_tensor(k) for k in f.keys()}
+    lc = LoRAConfig(rank=int(meta["rank"]), alpha=float(meta["alpha"]),
+                    targets=tuple(t for t in meta.get("targets", "wqkv,wo,wgu,wdown").split(",") if t))
+    ad = LoRAAdapters(cfg, lc, device)
+    ad.load_state_dict({k: v.to(device) for k, v in tensors.items()})
+    return ad
+

@@ -211,13 +211,10 @@ class Trainer:
             return None
         cfg = self.rc.model
         if self.lora:  # the adapters alone: lora_step_<N>.safetensors (rank / alpha in the metadata)
-            from safetensors.torch import save_file
-            lc = self.pipe.lora.lc
+            from ..models.lora import save_lora_file
             os.makedirs(self.rc.train.checkpoint_dir, exist_ok=True)
             path = os.path.join(self.rc.train.checkpoint_dir, f"lora_step_{self.step}.safetensors")
-            save_file({k: v.detach().float().contiguous().cpu() for k, v in self.pipe.lora.state_dict().items()},
-                      path, metadata={"rank": str(lc.rank), "alpha": str(lc.alpha), "targets": ",".join(lc.targets),
-                                      "step": str(self.step)})
+            save_lora_file(self.pipe.lora, path, self.step)
             return path
         state = {"step": self.step, "data": self.data.state(), "config": to_dict(self.rc),
                  "world": self.world, "time": time.time()}

@@ -229,3 +229,21 @@ def test_llama_gptq_parts_map_to_the_engine_layout():
     assert torch.equal(gate, parts[p + "mlp.gate_proj"].dequantize())
     assert torch.equal(up, parts[p + "mlp.up_proj"].dequantize())
     assert e["layers.0.wdown"] is parts[p + "mlp.down_proj"]
+
+
+def test_lora_file_round_trip(tmp_path):
+    from lora_kernel_b200.config import TransformerConfig
+    from lora_kernel_b200.models.lora import LoRAAdapters, LoRAConfig, load_lora_file, save_lora_file
+    cfg = TransformerConfig(hidden_dim=128, num_heads=4, num_kv_heads=2, head_dim=32, ff_dim=256,
+                            vocab_size=64, num_layers=2)
+    ad = LoRAAdapters(cfg, LoRAConfig(rank=8, alpha=4.0, targets=("wqkv", "wdown"), init_seed=3), "cpu",
+                      torch.float32)
+    g = torch.Generator().manual_seed(0)
+    for v in ad.state_dict().values():
+        v.copy_(torch.randn(v.shape, generator=g))
+    path = str(tmp_path / "lora_step_7.safetensors")
+    save_lora_file(ad, path, 7)
+    back = load_lora_file(path, cfg, "cpu")
+    assert (back.lc.rank, back.lc.alpha, back.lc.targets) == (8, 4.0, ("wqkv", "wdown"))
+    for k, v in ad.state_dict().items():
+        torch.testing.assert_close(back.state_dict()[k].float(), v.float(), rtol=1e-2, atol=1e-2)
