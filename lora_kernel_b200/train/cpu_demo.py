@@ -47,6 +47,28 @@ def run_cpu(rc: RunConfig, steps: Optional[int] = None, log: Optional[Callable[[
     decay = {k: (v.dim() > 1) or tc.decay_norms for k, v in params.views.items()}
     tr = OracleTrainer(dict(params.views), cfg, lr=tc.lr, wd=tc.weight_decay, betas=(tc.beta1, tc.beta2),
                        eps=tc.eps, max_norm=tc.max_grad_norm, decay=decay)
+    lora = None
+    if tc.lora_rank > 0:
+        # LoRA: the base stays frozen, only the adapters (the same tensors and file format as the
+        # GPU path, models/lora.py) are trained; W_eff = W + (alpha / r) B A for every target
+        from ..models.lora import LoRAAdapters, LoRAConfig
+        lora = LoRAAdapters(cfg, LoRAConfig(rank=tc.lora_rank, alpha=tc.lora_alpha, init_seed=tc.seed,
+                                            targets=tuple(t for t in tc.lora_targets.split(",") if t)),
+                            "cpu", torch.float32)
+        lora.flat.requires_grad_(True)
+        # views taken after requires_grad so that gradients reach the flat buffer
+        lv_ = {nm: lora.flat[o:o + sh[0] * sh[1]].view(sh) for nm, sh, o in lora.specs}
+        for v in tr.params.values():
+            v.requires_grad_(False)
+        tr.opt = torch.optim.AdamW([lora.flat], lr=tc.lr, betas=(tc.beta1, tc.beta2), eps=tc.eps,
+                                   weight_decay=tc.weight_decay)
+
+    def weights():
+        if lora is None:
+            return tr.params
+        s = lora.lc.scale
+        return {k: (v + s * (lv_[k + ".B"] @ lv_[k + ".A"]) if k + ".A" in lv_ else v)
+                for k, v in tr.params.items()}
     g = torch.Generator().manual_seed(tc.seed)
     B, S = tc.micro_batch, tc.seq_len
     fixed = torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g) if tc.fixed_batch else None
@@ -60,11 +82,12 @@ def run_cpu(rc: RunConfig, steps: Optional[int] = None, log: Optional[Callable[[
         tr.opt.zero_grad(set_to_none=True)
         for _ in range(tc.grad_accum_steps):
             ids = fixed if fixed is not None else torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g)
-            lv = loss_fn(tr.params, cfg, ids[:, :-1], ids[:, 1:]) / tc.grad_accum_steps
+            lv = loss_fn(weights(), cfg, ids[:, :-1], ids[:, 1:]) / tc.grad_accum_steps
             lv.backward()
             loss += float(lv.detach())
         if tr.max_norm > 0:
-            torch.nn.utils.clip_grad_norm_(list(tr.params.values()), tr.max_norm)
+            trained = [lora.flat] if lora is not None else list(tr.params.values())
+            torch.nn.utils.clip_grad_norm_(trained, tr.max_norm)
         tr.opt.step()
         dt = time.perf_counter() - t0
         rec = {"step": step + 1, "loss": loss, "lr": lr,
@@ -72,4 +95,10 @@ def run_cpu(rc: RunConfig, steps: Optional[int] = None, log: Optional[Callable[[
         out.append(rec)
         if log is not None:
             log(rec)
+    if lora is not None and tc.checkpoint_dir:
+        import os
+
+        from ..models.lora import save_lora_file
+        os.makedirs(tc.checkpoint_dir, exist_ok=True)
+        save_lora_file(lora, os.path.join(tc.checkpoint_dir, f"lora_step_{total}.safetensors"), total)
     return out

@@ -275,3 +275,20 @@ def test_cpu_training_starts_from_pretrained_weights(tmp_path):
         tc.init_from, tc.init_format = path, fmt
         first = run_cpu(rc, steps=1)[0]["loss"]
         assert abs(first - want) < 1e-4, (fmt, first, want)
+
+
+def test_cpu_lora_trains_adapters_only(tmp_path):
+    """`train --device cpu --lora-rank 8`: the loss falls with the base frozen,
+    and the adapters are written in the GPU path's file format."""
+    from lora_kernel_b200.config import get_preset
+    from lora_kernel_b200.models.lora import load_lora_file
+    from lora_kernel_b200.train.cpu_demo import run_cpu
+    rc = get_preset("cpu-demo")
+    rc.model.num_layers, rc.train.micro_batch, rc.train.seq_len = 1, 2, 32
+    rc.train.lr, rc.train.lora_rank, rc.train.lora_alpha = 1e-2, 8, 16.0
+    rc.train.checkpoint_dir = str(tmp_path)
+    hist = run_cpu(rc, steps=12)
+    assert hist[-1]["loss"] < hist[0]["loss"] - 0.2
+    ad = load_lora_file(str(tmp_path / "lora_step_12.safetensors"), rc.model, "cpu")
+    b = ad.state_dict()["layers.0.wqkv.B"]
+    assert ad.lc.rank == 8 and float(b.abs().sum()) > 0      # B starts at zero and was trained
