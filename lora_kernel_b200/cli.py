@@ -215,6 +215,9 @@ def cmd_export(a):
         p = FlatParams(cfg, "cpu", torch.float32)
         p.init_(rc.train.seed, cfg.init_std)
         sd = p.to_reference_state_dict()
+    if a.lora:  # fold trained LoRA adapters into the exported weights
+        from .models.lora import load_lora_file, merge_lora_state_dict
+        sd = merge_lora_state_dict(sd, load_lora_file(a.lora, cfg, "cpu"))
     if a.format == "onnx":
         from .utils.onnx_export import export_onnx
         export_onnx(sd, cfg, a.out)
@@ -282,6 +285,7 @@ def main(argv=None):
     x.add_argument("--format", choices=["gguf", "hf", "onnx"], default="gguf")
     x.add_argument("--dtype", choices=["f32", "f16", "bf16"], default="bf16")
     x.add_argument("--out", required=True)
+    x.add_argument("--lora", help="LoRA adapters (lora_step_N.safetensors) merged into the exported weights")
     x.add_argument("--set", nargs="*")
     sub.add_parser("env")
     a, rest = ap.parse_known_args(argv)

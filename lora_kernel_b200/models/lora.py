@@ -152,3 +152,18 @@ def load_lora_file(path: str, cfg: TransformerConfig, device="cuda") -> "LoRAAda
     ad.load_state_dict({k: v.to(device) for k, v in tensors.items()})
     return ad
 
+
+@torch.no_grad()
+def merge_lora_state_dict(sd: Dict[str, torch.Tensor], adapters: "LoRAAdapters") -> Dict[str, torch.Tensor]:
+    """A reference-named state dict with the adapters folded in (W + (alpha/r) B A,
+    fp32 on the host): the weights the merged model serves or exports."""
+    from .params import FlatParams
+    p = FlatParams(adapters.cfg, "cpu", torch.float32)
+    p.load_reference_state_dict({k: v.float().cpu() for k, v in sd.items()})
+    s = adapters.lc.scale
+    for i in range(adapters.cfg.num_layers):
+        for t in adapters.lc.targets:
+            w = p.views[f"layers.{i}.{t}"]
+            w += s * (adapters.B(i, t).float().cpu() @ adapters.A(i, t).float().cpu())
+    return p.to_reference_state_dict()
+

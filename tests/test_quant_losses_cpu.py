@@ -247,3 +247,28 @@ def test_lora_file_round_trip(tmp_path):
     assert (back.lc.rank, back.lc.alpha, back.lc.targets) == (8, 4.0, ("wqkv", "wdown"))
     for k, v in ad.state_dict().items():
         torch.testing.assert_close(back.state_dict()[k].float(), v.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_lora_merge_into_state_dict_matches_the_adapted_forward():
+    """Folding the adapters into the weights gives the logits of the base model
+    run with W + (alpha/r) B A."""
+    from lora_kernel_b200.config import TransformerConfig
+    from lora_kernel_b200.models.lora import LoRAAdapters, LoRAConfig, merge_lora_state_dict
+    from lora_kernel_b200.models.params import FlatParams
+    from lora_kernel_b200.oracle import llama_ref
+    cfg = TransformerConfig(hidden_dim=128, num_heads=4, num_kv_heads=2, head_dim=32, ff_dim=256,
+                            vocab_size=64, num_layers=1)
+    base = FlatParams(cfg, "cpu", torch.float32)
+    base.init_(2, 0.05)
+    ad = LoRAAdapters(cfg, LoRAConfig(rank=8, alpha=16.0, targets=("wqkv", "wgu")), "cpu", torch.float32)
+    g = torch.Generator().manual_seed(1)
+    for v in ad.state_dict().values():
+        v.copy_(torch.randn(v.shape, generator=g) * 0.05)
+    merged = FlatParams(cfg, "cpu", torch.float32)
+    merged.load_reference_state_dict(merge_lora_state_dict(base.to_reference_state_dict(), ad))
+    want = {k: v.clone() for k, v in base.views.items()}
+    for t in ("wqkv", "wgu"):
+        want[f"layers.0.{t}"] += 2.0 * ad.B(0, t) @ ad.A(0, t)
+    ids = torch.randint(0, 64, (2, 9), generator=g)
+    torch.testing.assert_close(llama_ref.forward(dict(merged.views), cfg, ids), llama_ref.forward(want, cfg, ids),
+                               rtol=1e-5, atol=1e-5)
