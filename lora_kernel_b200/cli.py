@@ -141,9 +141,17 @@ def cmd_serve(a):
         rank, world, _ = init_distributed("nccl", timeout_s=3600)
         sc = rc.serve
         tp_params = None
-        if a.checkpoint:  # every rank reads the file and keeps its shard
+        if a.checkpoint or a.lora:  # every rank reads the weights and keeps its shard
             from .serve.tp_runner import tp_params_from_state_dict
-            sd = read_state_dict()
+            if a.checkpoint:
+                sd = read_state_dict()
+            else:
+                seeded = FlatParams(cfg, "cpu", torch.float32)
+                seeded.init_(rc.train.seed, cfg.init_std)
+                sd = seeded.to_reference_state_dict()
+            if a.lora:  # adapters folded in before sharding
+                from .models.lora import load_lora_file, merge_lora_state_dict
+                sd = merge_lora_state_dict(sd, load_lora_file(a.lora, cfg, "cpu"))
             dev = torch.device("cuda", torch.cuda.current_device())
             tp_params = tp_params_from_state_dict(cfg, sd, world, rank, dev)
             del sd
