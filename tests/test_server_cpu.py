@@ -469,3 +469,23 @@ def test_hf_tokenizer_file(tmp_path):
         d = await r.json()
         assert d["choices"][0]["text"] == "hello world hello" and d["usage"]["prompt_tokens"] == 2
     _run(go, tokenizer=tok)
+
+
+def test_dashboard_renders_the_exposition():
+    from lora_kernel_b200.utils.dashboard import histogram_quantile, parse_prometheus, render
+    from lora_kernel_b200.utils.metrics import Registry
+    reg = Registry("lora_kernel_")
+    reg.counter("requests_total").inc(3)
+    reg.counter("generation_tokens_total").inc(120)
+    reg.gauge("kv_cache_usage").set(0.25)
+    h = reg.histogram("time_to_first_token_seconds")
+    for v in (0.004, 0.02, 0.02, 0.3):
+        h.observe(v)
+    reg.gauge("gpu_utilization_percent", labels={"gpu": "0"}).set(91)
+    m = parse_prometheus(reg.exposition())
+    assert m[("lora_kernel_requests_total", ())] == 3.0
+    assert m[("lora_kernel_gpu_utilization_percent", (("gpu", "0"),))] == 91.0
+    assert histogram_quantile(m, "lora_kernel_time_to_first_token_seconds", 0.5) == 0.025
+    text = render(m, [{"name": "kv", "metric": "kv_cache_usage", "op": ">", "threshold": 0.2, "value": 0.25}])
+    assert "requests 3" in text and "KV cache 25.0%" in text and "TTFT" in text and "GPU 0: util 91%" in text
+    assert "ALERT kv" in text
