@@ -133,4 +133,4 @@ class OracleTrainer:
         if self.max_norm > 0:
             torch.nn.utils.clip_grad_norm_(list(self.params.values()), self.max_norm)
         self.opt.step()
-        return float(loss)
+        return float(loss.detach())
