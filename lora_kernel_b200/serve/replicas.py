@@ -65,7 +65,7 @@ class ReplicaPool:
             self.routed[i] += 1
             return i
 
-    def submit(self, prompt, params, on_token) -> int:
+    def submit(self, prompt, params, on_token, priority: int = 0) -> int:
         i = self.pick(prompt)
 
         def wrapped(r, t, _i=i):
@@ -73,7 +73,7 @@ class ReplicaPool:
                 with self._lock:
                     self.outstanding[_i] -= 1
             on_token(r, t)
-        return self.workers[i].submit(prompt, params, wrapped)
+        return self.workers[i].submit(prompt, params, wrapped, priority)
 
     def running(self) -> int:
         return sum(len(e.running) for e in self.engines)

@@ -65,6 +65,9 @@ class InputValidator:
                 raise ValidationError(f"{k} is not supported (use 0)")
         if body.get("logprobs") not in (None, False, 0):
             raise ValidationError("logprobs are not returned by this server")
+        pr = body.get("priority", 0)
+        if pr is not None and (not isinstance(pr, int) or isinstance(pr, bool) or not -1000 <= pr <= 1000):
+            raise ValidationError("priority must be an integer in [-1000, 1000] (lower runs sooner)")
         seed = body.get("seed")
         if seed is not None and (not isinstance(seed, int) or isinstance(seed, bool) or not 0 <= seed < 2 ** 63):
             raise ValidationError("seed must be an integer in [0, 2^63)")

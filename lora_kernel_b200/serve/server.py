@@ -126,9 +126,10 @@ class EngineWorker:
         self.stop = True
         self.wake.set()
 
-    def submit(self, prompt, params, on_token) -> int:
+    def submit(self, prompt, params, on_token, priority: int = 0) -> int:
         with self.lock:
-            rid = self.engine.add_request(prompt, params, on_token=on_token)
+            rid = (self.engine.add_request(prompt, params, on_token=on_token, priority=priority) if priority
+                   else self.engine.add_request(prompt, params, on_token=on_token))
         self.m_in.inc(len(prompt))
         self.wake.set()
         return rid
@@ -307,13 +308,13 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                               top_p=float(body.get("top_p", 1.0) or 1.0), stop_token_ids=tuple(stop),
                               stop_sequences=seqs, seed=body.get("seed"))
 
-    async def _run(prompt, params, stream: bool, request: web.Request, chat: bool):
+    async def _run(prompt, params, stream: bool, request: web.Request, chat: bool, priority: int = 0):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
 
         def on_token(r, t):
             loop.call_soon_threadsafe(q.put_nowait, (t, r.finished, r.finish_reason))
-        rid = worker.submit(prompt, params, on_token)
+        rid = worker.submit(prompt, params, on_token, priority)
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
@@ -391,7 +392,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         ids = prompt if isinstance(prompt, list) else tok.encode(clean(str(prompt)))
         try:
             validator.check(ids, body)
-            return await _run(ids, _params(body), bool(body.get("stream")), request, chat=False)
+            return await _run(ids, _params(body), bool(body.get("stream")), request, chat=False,
+                              priority=int(body.get("priority", 0) or 0))
         except ValueError as e:
             return _err(str(e), "invalid_request", 400)
 
@@ -406,7 +408,8 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         ids = tok.apply_chat_template(msgs)
         try:
             validator.check(ids, body)
-            return await _run(ids, _params(body), bool(body.get("stream")), request, chat=True)
+            return await _run(ids, _params(body), bool(body.get("stream")), request, chat=True,
+                              priority=int(body.get("priority", 0) or 0))
         except ValueError as e:
             return _err(str(e), "invalid_request", 400)
 

@@ -30,10 +30,11 @@ class FakeEngine:
         self.running, self.waiting = [], []
         self.n = 0
 
-    def add_request(self, prompt, params, on_token=None):
+    def add_request(self, prompt, params, on_token=None, priority=0):
         class R:
             pass
         r = R()
+        self.priorities = getattr(self, "priorities", []) + [priority]
         r.prompt, r.params, r.on_token = list(prompt), params, on_token
         r.output, r.finished, r.finish_reason = [], False, None
         r.arrival, r.first_token_time, r.token_times = time.perf_counter(), None, []
@@ -489,3 +490,22 @@ def test_dashboard_renders_the_exposition():
     text = render(m, [{"name": "kv", "metric": "kv_cache_usage", "op": ">", "threshold": 0.2, "value": 0.25}])
     assert "requests 3" in text and "KV cache 25.0%" in text and "TTFT" in text and "GPU 0: util 91%" in text
     assert "ALERT kv" in text
+
+
+def test_priority_reaches_the_engine():
+    from lora_kernel_b200.serve.security import InputValidator, ValidationError
+    eng = FakeEngine()
+
+    async def main():
+        app = create_app(eng)
+        async with TestClient(TestServer(app)) as c:
+            r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 2, "priority": -5})
+            assert r.status == 200
+            r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 2})
+            assert r.status == 200
+            r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 2, "priority": 5000})
+            assert r.status == 400
+    asyncio.run(main())
+    assert eng.priorities == [-5, 0]
+    with pytest.raises(ValidationError, match="priority"):
+        InputValidator(256).check([1], {"priority": "high"})
