@@ -130,3 +130,23 @@ def test_zigzag_positions_are_a_permutation(world):
     x = torch.arange(S)[None]
     got = torch.cat([shard_zigzag(x, r, world) for r in range(world)], 1)[0]
     assert sorted(got.tolist()) == list(range(S))
+
+
+_json = st.recursive(st.none() | st.booleans() | st.integers(-10 ** 6, 10 ** 6) | st.floats(allow_nan=True) |
+                     st.text(max_size=8), lambda c: st.lists(c, max_size=4) | st.dictionaries(st.text(max_size=6), c,
+                                                                                           max_size=4), max_leaves=8)
+
+
+@FAST
+@given(body=st.dictionaries(st.sampled_from(["max_tokens", "temperature", "top_p", "stop", "seed", "n", "priority",
+                                             "logprobs", "presence_penalty", "frequency_penalty"]), _json,
+                            max_size=6),
+       ids=st.lists(st.integers(-5, 300), min_size=0, max_size=6))
+def test_request_validator_never_crashes(body, ids):
+    """Arbitrary JSON values in the sampling fields are either accepted or
+    rejected with ValidationError (a 400), never another exception (a 500)."""
+    from lora_kernel_b200.serve.security import InputValidator, ValidationError
+    try:
+        InputValidator(256).check(ids, body)
+    except ValidationError:
+        pass
