@@ -71,6 +71,10 @@ class InputValidator:
         seed = body.get("seed")
         if seed is not None and (not isinstance(seed, int) or isinstance(seed, bool) or not 0 <= seed < 2 ** 63):
             raise ValidationError("seed must be an integer in [0, 2^63)")
+        sti = body.get("stop_token_ids")
+        if sti is not None and (not isinstance(sti, list) or len(sti) > 64 or not all(
+                isinstance(t, int) and not isinstance(t, bool) and 0 <= t < self.vocab_size for t in sti)):
+            raise ValidationError(f"stop_token_ids must be a list of at most 64 token ids in [0, {self.vocab_size})")
         stop = body.get("stop")
         if stop is not None:
             seqs = [stop] if isinstance(stop, str) else stop

@@ -139,7 +139,8 @@ _json = st.recursive(st.none() | st.booleans() | st.integers(-10 ** 6, 10 ** 6) 
 
 @FAST
 @given(body=st.dictionaries(st.sampled_from(["max_tokens", "temperature", "top_p", "stop", "seed", "n", "priority",
-                                             "logprobs", "presence_penalty", "frequency_penalty"]), _json,
+                                             "logprobs", "presence_penalty", "frequency_penalty",
+                                             "stop_token_ids"]), _json,
                             max_size=6),
        ids=st.lists(st.integers(-5, 300), min_size=0, max_size=6))
 def test_request_validator_never_crashes(body, ids):
@@ -149,4 +150,13 @@ def test_request_validator_never_crashes(body, ids):
     try:
         InputValidator(256).check(ids, body)
     except ValidationError:
-        pass
+        return
+    # what the validator accepts, the server turns into sampling parameters without error
+    from lora_kernel_b200.serve.engine import SamplingParams
+    stop = body.get("stop") or ()
+    SamplingParams(max_tokens=int(body.get("max_tokens", 16)), temperature=float(body.get("temperature", 0.0) or 0.0),
+                   top_p=float(body.get("top_p", 1.0) or 1.0),
+                   stop_token_ids=tuple(body.get("stop_token_ids") or ()),
+                   stop_sequences=tuple(tuple(x.encode()) for x in ((stop,) if isinstance(stop, str) else stop)),
+                   seed=body.get("seed"))
+    int(body.get("priority", 0) or 0)
