@@ -456,7 +456,7 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                 continue
             q: asyncio.Queue = asyncio.Queue()
             worker.submit(ids, params, lambda r, t: loop.call_soon_threadsafe(
-                q.put_nowait, (t, r.finished, r.finish_reason)))
+                q.put_nowait, (t, r.finished, r.finish_reason)), int(body.get("priority", 0) or 0))
             cid = f"ws-{uuid.uuid4().hex[:16]}"
             out: List[int] = []
             kept: List[int] = []
