@@ -27,7 +27,7 @@ import os
 import threading
 import time
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import Tuple, Dict, List, Optional
 
 
 class RankFailure(RuntimeError):
@@ -104,10 +104,32 @@ def parse_faults(spec: Optional[str] = None) -> List[Fault]:
     return out
 
 
+def kill_is_safe() -> Tuple[bool, str]:
+    """Whether ending a rank's process abruptly is allowed here.
+
+    A rank whose device memory is bound to an NVLink multicast (NVLS) object
+    must not die in the middle of a job: when that happened the other ranks'
+    GPUs raised NVLink faults.  Killing is therefore allowed only for CPU /
+    gloo jobs, or for NCCL jobs that run with multicast off in this library
+    (LK_NVLS=0) and in NCCL (NCCL_NVLS_ENABLE=0)."""
+    import torch.distributed as dist
+    backend = dist.get_backend() if dist.is_available() and dist.is_initialized() else None
+    if backend in (None, "gloo"):
+        return True, ""
+    if os.environ.get("LK_NVLS") == "0" and os.environ.get("NCCL_NVLS_ENABLE") == "0":
+        return True, ""
+    return False, (f"kill_rank refused on a '{backend}' job with NVLink multicast possible: set LK_NVLS=0 and "
+                   "NCCL_NVLS_ENABLE=0, or inject raise_rank / delay_rank instead")
+
+
 class FaultInjector:
     def __init__(self, rank: int, spec: Optional[str] = None):
         self.rank = rank
         self.faults = parse_faults(spec)
+        if any(f.kind == "kill_rank" for f in self.faults):
+            ok, why = kill_is_safe()
+            if not ok:
+                raise ValueError(why)
 
     def _mine(self, f: Fault, step: int) -> bool:
         return f.step == step and (f.rank < 0 or f.rank == self.rank)
@@ -118,6 +140,9 @@ class FaultInjector:
             if not self._mine(f, step):
                 continue
             if f.kind == "kill_rank":
+                ok, why = kill_is_safe()
+                if not ok:
+                    raise RuntimeError(why)
                 os._exit(17)
             elif f.kind == "delay_rank":
                 time.sleep(f.arg)

@@ -131,13 +131,33 @@ class LLMEngine:
         r = Request(next(self.ids), list(prompt), params or SamplingParams(), priority,
                     self.clock() if arrival is None else arrival, on_token=on_token)
         self.stats["prompt_tokens"] += len(prompt)
-        # priority first (lower value = sooner), FIFO within a priority
-        if priority != 0 and self.waiting:
-            idx = next((k for k, w in enumerate(self.waiting) if w.priority > priority), len(self.waiting))
-            self.waiting.insert(idx, r)
-        else:
-            self.waiting.append(r)
+        # priority first (lower value = sooner), FIFO within a priority: every
+        # request, priority 0 included, goes in front of the first waiting
+        # request with a larger priority value
+        idx = next((k for k, w in enumerate(self.waiting) if w.priority > priority), len(self.waiting))
+        self.waiting.insert(idx, r)
         return r.req_id
+
+    def abort_request(self, req_id: int) -> bool:
+        """Drop a request that has not finished (its client went away): its KV
+        blocks are freed and it leaves the waiting / running queues.  Returns
+        False when the request is unknown or already finished."""
+        for r in list(self.running):
+            if r.req_id == req_id:
+                self.blocks.free_seq(r.table)
+                self.running.remove(r)
+                r.finished, r.finish_reason = True, "abort"
+                self.finished[r.req_id] = r
+                return True
+        for r in list(self.waiting):
+            if r.req_id == req_id:
+                if r.table:
+                    self.blocks.free_seq(r.table)
+                self.waiting.remove(r)
+                r.finished, r.finish_reason = True, "abort"
+                self.finished[r.req_id] = r
+                return True
+        return False
 
     def has_work(self) -> bool:
         return bool(self.waiting or self.running)

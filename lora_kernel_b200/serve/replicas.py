@@ -66,6 +66,8 @@ class ReplicaPool:
             return i
 
     def submit(self, prompt, params, on_token, priority: int = 0) -> int:
+        """Route a request to a replica; returns a pool-wide request handle
+        (replica index in the low bits), which abort() takes."""
         i = self.pick(prompt)
 
         def wrapped(r, t, _i=i):
@@ -73,7 +75,25 @@ class ReplicaPool:
                 with self._lock:
                     self.outstanding[_i] -= 1
             on_token(r, t)
-        return self.workers[i].submit(prompt, params, wrapped, priority)
+        try:
+            rid = self.workers[i].submit(prompt, params, wrapped, priority)
+        except Exception:
+            with self._lock:
+                self.outstanding[i] -= 1
+            raise
+        return rid * len(self.workers) + i
+
+    def abort(self, handle: int, on_done=None) -> None:
+        n = len(self.workers)
+        i, rid = handle % n, handle // n
+
+        def done(ok, _i=i):
+            if ok:
+                with self._lock:
+                    self.outstanding[_i] -= 1
+            if on_done is not None:
+                on_done(ok)
+        self.workers[i].abort(rid, done)
 
     def running(self) -> int:
         return sum(len(e.running) for e in self.engines)

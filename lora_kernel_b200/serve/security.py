@@ -46,10 +46,10 @@ class InputValidator:
         if len(ids) > self.max_prompt_tokens:
             raise ValidationError(f"prompt has {len(ids)} tokens; the limit is {self.max_prompt_tokens}")
         for t in ids:
-            if not isinstance(t, int) or t < 0 or t >= self.vocab_size:
+            if not isinstance(t, int) or isinstance(t, bool) or t < 0 or t >= self.vocab_size:
                 raise ValidationError(f"token id {t!r} outside [0, {self.vocab_size})")
         mt = body.get("max_tokens", 16)
-        if not isinstance(mt, int) or mt < 1 or mt > self.max_new_tokens:
+        if not isinstance(mt, int) or isinstance(mt, bool) or mt < 1 or mt > self.max_new_tokens:
             raise ValidationError(f"max_tokens must be an integer in [1, {self.max_new_tokens}]")
         temp = body.get("temperature", 0.0) or 0.0
         if not isinstance(temp, (int, float)) or not 0.0 <= float(temp) <= 10.0:

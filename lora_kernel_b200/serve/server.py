@@ -32,6 +32,7 @@ import json
 import threading
 import time
 import uuid
+from collections import deque
 from typing import Dict, List, Optional
 
 import torch
@@ -113,6 +114,9 @@ class EngineWorker:
         self.g_wait = REGISTRY.gauge("num_requests_waiting", "waiting requests")
         self.g_kv = REGISTRY.gauge("kv_cache_usage", "fraction of KV blocks in use")
         self.g_hit = REGISTRY.gauge("prefix_cache_hit_rate", "prefix cache block hit rate")
+        self._aborts: deque = deque()
+        self._gate = threading.Lock()
+        self._callers = 0
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
@@ -127,12 +131,34 @@ class EngineWorker:
         self.wake.set()
 
     def submit(self, prompt, params, on_token, priority: int = 0) -> int:
-        with self.lock:
-            rid = (self.engine.add_request(prompt, params, on_token=on_token, priority=priority) if priority
-                   else self.engine.add_request(prompt, params, on_token=on_token))
+        # announce the caller so the worker lets go of the lock between steps
+        # (a plain lock is not fair: the worker would take it straight back)
+        with self._gate:
+            self._callers += 1
+        try:
+            with self.lock:
+                rid = (self.engine.add_request(prompt, params, on_token=on_token, priority=priority) if priority
+                       else self.engine.add_request(prompt, params, on_token=on_token))
+        finally:
+            with self._gate:
+                self._callers -= 1
         self.m_in.inc(len(prompt))
         self.wake.set()
         return rid
+
+    def abort(self, rid: int, on_done=None) -> None:
+        """Stop a request whose client is gone (frees its KV blocks).  Does not
+        block: the worker applies it before its next step and then calls
+        on_done(aborted) with whether the request was still unfinished."""
+        self._aborts.append((rid, on_done))
+        self.wake.set()
+
+    def _apply_aborts(self) -> None:
+        while self._aborts:
+            rid, cb = self._aborts.popleft()
+            ok = self.engine.abort_request(rid)
+            if cb is not None:
+                cb(ok)
 
     def _loop(self):
         # kernels launch on the current device's stream: make it the engine's
@@ -140,10 +166,15 @@ class EngineWorker:
         if isinstance(dev, torch.device) and dev.type == "cuda":
             torch.cuda.set_device(dev)
         while not self.stop:
+            if self._aborts:
+                with self.lock:
+                    self._apply_aborts()
             if not self.engine.has_work():
                 self.wake.wait(0.05)
                 self.wake.clear()
                 continue
+            while self._callers:  # a submit() is waiting for the lock
+                time.sleep(0.0002)
             with self.lock:
                 finished = self.engine.step()
             e = self.engine
@@ -315,6 +346,18 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         def on_token(r, t):
             loop.call_soon_threadsafe(q.put_nowait, (t, r.finished, r.finish_reason))
         rid = worker.submit(prompt, params, on_token, priority)
+        finished = False
+        try:
+            resp = await _respond(rid, q, prompt, params, stream, request, chat)
+            finished = True
+            return resp
+        finally:
+            # a client that disconnected (or a failed write) leaves the request
+            # unfinished: stop it so it neither decodes on nor holds KV blocks
+            if not finished:
+                worker.abort(rid)
+
+    async def _respond(rid, q, prompt, params, stream: bool, request: web.Request, chat: bool):
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
@@ -438,31 +481,68 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
         ({"prompt": str | [ids], "max_tokens", "temperature", "top_p"}); the
         server answers {"id", "token", "index", "text"} per token, then
         {"id", "done": true, "finish_reason", "usage"}.  Requests on one
-        socket run one after another."""
+        socket run one after another; a reader task keeps reading the socket
+        while a request streams, so a client that closes it mid-request stops
+        that request."""
         ws = web.WebSocketResponse(heartbeat=30.0)
         await ws.prepare(request)
         loop = asyncio.get_running_loop()
-        async for msg in ws:
-            if msg.type != WSMsgType.TEXT:
-                continue
+        inbox: asyncio.Queue = asyncio.Queue()
+        closed = asyncio.Event()
+
+        async def reader():
             try:
-                body = json.loads(msg.data)
-                prompt = body.get("prompt", "")
-                ids = prompt if isinstance(prompt, list) else tok.encode(clean(str(prompt)))
-                validator.check(ids, body)
-                params = _params(body)
-            except (ValueError, AttributeError) as e:
-                await ws.send_json({"error": {"message": str(e), "type": "invalid_request"}})
-                continue
-            q: asyncio.Queue = asyncio.Queue()
-            worker.submit(ids, params, lambda r, t: loop.call_soon_threadsafe(
-                q.put_nowait, (t, r.finished, r.finish_reason)), int(body.get("priority", 0) or 0))
-            cid = f"ws-{uuid.uuid4().hex[:16]}"
-            out: List[int] = []
-            kept: List[int] = []
-            trim = StopTrimmer(params.stop_sequences)
+                async for msg in ws:
+                    if msg.type == WSMsgType.TEXT:
+                        inbox.put_nowait(msg.data)
+            finally:
+                closed.set()
+                inbox.put_nowait(None)
+
+        rtask = asyncio.create_task(reader())
+        try:
             while True:
-                t, done, reason = await q.get()
+                data = await inbox.get()
+                if data is None or closed.is_set():
+                    break
+                if not await _ws_request(ws, data, loop, closed):
+                    break
+        finally:
+            rtask.cancel()
+        return ws
+
+    async def _ws_request(ws, data, loop, closed: asyncio.Event) -> bool:
+        """Serve one WebSocket request; False when the socket closed meanwhile."""
+        try:
+            body = json.loads(data)
+            prompt = body.get("prompt", "")
+            ids = prompt if isinstance(prompt, list) else tok.encode(clean(str(prompt)))
+            validator.check(ids, body)
+            params = _params(body)
+        except (ValueError, AttributeError) as e:
+            await ws.send_json({"error": {"message": str(e), "type": "invalid_request"}})
+            return True
+        q: asyncio.Queue = asyncio.Queue()
+        try:
+            rid = worker.submit(ids, params, lambda r, t: loop.call_soon_threadsafe(
+                q.put_nowait, (t, r.finished, r.finish_reason)), int(body.get("priority", 0) or 0))
+        except ValueError as e:  # e.g. prompt + max_tokens over max_model_len
+            await ws.send_json({"error": {"message": str(e), "type": "invalid_request"}})
+            return True
+        cid = f"ws-{uuid.uuid4().hex[:16]}"
+        out: List[int] = []
+        kept: List[int] = []
+        trim = StopTrimmer(params.stop_sequences)
+        done, reason = False, None
+        closing = asyncio.ensure_future(closed.wait())
+        try:
+            while True:
+                get = asyncio.ensure_future(q.get())
+                await asyncio.wait({get, closing}, return_when=asyncio.FIRST_COMPLETED)
+                if not get.done():
+                    get.cancel()
+                    return False  # the socket went away mid-request
+                t, done, reason = get.result()
                 out.append(t)
                 for rt in trim.push(t, done, reason):
                     kept.append(rt)
@@ -470,13 +550,17 @@ def create_app(engine: LLMEngine, model_name: str = "lora-kernel-b200", api_keys
                     await ws.send_json({"id": cid, "token": rt, "index": len(kept) - 1, "text": text})
                 if done:
                     break
-            final = {"id": cid, "done": True, "finish_reason": reason,
-                     "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
-                               "total_tokens": len(ids) + len(out)}}
-            if masker is not None:
-                final["text"] = masker.mask(tok.decode(kept))
-            await ws.send_json(final)
-        return ws
+        finally:
+            closing.cancel()
+            if not done:
+                worker.abort(rid)
+        final = {"id": cid, "done": True, "finish_reason": reason,
+                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                           "total_tokens": len(ids) + len(out)}}
+        if masker is not None:
+            final["text"] = masker.mask(tok.decode(kept))
+        await ws.send_json(final)
+        return True
 
     app.router.add_post("/v1/completions", completions)
     app.router.add_get("/v1/ws", websocket)

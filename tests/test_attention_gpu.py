@@ -13,6 +13,24 @@ def _close(out, ref, rtol, atol, what=""):
     assert bad == 0, f"{what}: {bad}/{err.numel()} mismatches, max err {err.max().item():.4g}"
 
 
+def _rel_per_head(out, ref, heads, dh, tol, what=""):
+    """Relative L2 error of every head's slice (and of every 64-row block of
+    it): an error confined to a few low-magnitude heads or rows would pass a
+    check scaled by the whole tensor's maximum, not this one."""
+    o = out.float().reshape(out.shape[0], heads, dh)
+    r = ref.float().reshape(ref.shape[0], heads, dh)
+    for h in range(heads):
+        num = (o[:, h] - r[:, h]).norm().item()
+        den = r[:, h].norm().item()
+        assert num <= tol * den + 1e-6, f"{what} head {h}: relative error {num / max(den, 1e-30):.3g}"
+        for b0 in range(0, o.shape[0], 64):
+            rb = r[b0:b0 + 64, h]
+            dn = rb.norm().item()
+            if dn > 1e-3 * den:
+                nb = (o[b0:b0 + 64, h] - rb).norm().item()
+                assert nb <= 3 * tol * dn, f"{what} head {h} rows {b0}+: relative error {nb / dn:.3g}"
+
+
 CASES = [
     # B, S, Hq, Hkv, Dh, causal, window
     (1, 128, 1, 1, 64, True, 0),
@@ -47,3 +65,7 @@ def test_attention_fwd_bwd(B, S, Hq, Hkv, Dh, causal, window):
     _close(dqkv[:, :Hq * Dh], g[:, :Hq * Dh], 5e-2, 2e-2 * scale_ref, "dq")
     _close(dqkv[:, Hq * Dh:(Hq + Hkv) * Dh], g[:, Hq * Dh:(Hq + Hkv) * Dh], 5e-2, 2e-2 * scale_ref, "dk")
     _close(dqkv[:, (Hq + Hkv) * Dh:], g[:, (Hq + Hkv) * Dh:], 5e-2, 2e-2 * scale_ref, "dv")
+    _rel_per_head(o, o_ref.detach(), Hq, Dh, 1e-2, "o")
+    _rel_per_head(dqkv[:, :Hq * Dh], g[:, :Hq * Dh], Hq, Dh, 3e-2, "dq")
+    _rel_per_head(dqkv[:, Hq * Dh:(Hq + Hkv) * Dh], g[:, Hq * Dh:(Hq + Hkv) * Dh], Hkv, Dh, 3e-2, "dk")
+    _rel_per_head(dqkv[:, (Hq + Hkv) * Dh:], g[:, (Hq + Hkv) * Dh:], Hkv, Dh, 3e-2, "dv")

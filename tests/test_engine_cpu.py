@@ -191,3 +191,29 @@ def test_request_seeds_give_row_independent_noise():
         assert rs[0] == rs[2] != rs[1]
     assert len({rs[0] for rs in calls}) == len(calls)     # a new seed per draw
     assert eng.finished[a].output == eng.finished[c].output
+
+
+def test_priority_zero_goes_before_waiting_lower_priorities():
+    """Lower value = sooner for every request, the default priority 0 included."""
+    eng, _ = _engine(100, max_num_seqs=1)
+    a = eng.add_request([1, 2], SamplingParams(max_tokens=1), priority=5)
+    b = eng.add_request([3, 4], SamplingParams(max_tokens=1))
+    c = eng.add_request([5, 6], SamplingParams(max_tokens=1))
+    assert [r.req_id for r in eng.waiting] == [b, c, a]  # FIFO within priority 0
+    eng.step()
+    assert b in eng.finished and a not in eng.finished
+
+
+def test_abort_request_frees_blocks_and_work():
+    eng, _ = _engine(64, block_size=4)
+    free0 = eng.blocks.num_free()
+    a = eng.add_request(list(range(1, 30)), SamplingParams(max_tokens=50))
+    b = eng.add_request([7, 8, 9], SamplingParams(max_tokens=50))
+    eng.step()
+    eng.step()
+    assert any(r.req_id == a for r in eng.running)
+    assert eng.abort_request(a) and eng.abort_request(b)
+    assert not eng.has_work()
+    assert eng.finished[a].finish_reason == "abort"
+    assert eng.blocks.num_free() == free0
+    assert not eng.abort_request(a)  # already gone

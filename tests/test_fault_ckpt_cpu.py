@@ -24,6 +24,30 @@ def test_parse_faults():
         fi.at_step(2)
 
 
+def test_kill_rank_is_refused_when_nvlink_multicast_is_possible(monkeypatch):
+    """Killing a rank is allowed on CPU / gloo jobs; on an NCCL job only with
+    multicast off in this library and in NCCL."""
+    import torch.distributed as dist
+    from lora_kernel_b200.parallel import fault
+    FaultInjector(0, "kill_rank:1@step:3")  # no process group: allowed
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(dist, "get_backend", lambda *a: "nccl")
+    monkeypatch.delenv("LK_NVLS", raising=False)
+    monkeypatch.delenv("NCCL_NVLS_ENABLE", raising=False)
+    with pytest.raises(ValueError, match="LK_NVLS=0"):
+        FaultInjector(0, "kill_rank:1@step:3")
+    FaultInjector(0, "raise_rank:1@step:3")  # other faults stay available
+    monkeypatch.setenv("LK_NVLS", "0")
+    with pytest.raises(ValueError):
+        FaultInjector(0, "kill_rank:1@step:3")
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
+    assert fault.kill_is_safe()[0]
+    FaultInjector(0, "kill_rank:1@step:3")
+    monkeypatch.setattr(dist, "get_backend", lambda *a: "gloo")
+    monkeypatch.delenv("LK_NVLS")
+    assert fault.kill_is_safe()[0]
+
+
 def _hb_worker(rank, world, port, q):
     from torch.distributed import TCPStore
     store = TCPStore("127.0.0.1", port, world, is_master=(rank == 0), timeout=__import__("datetime").timedelta(seconds=30))

@@ -509,3 +509,82 @@ def test_priority_reaches_the_engine():
     assert eng.priorities == [-5, 0]
     with pytest.raises(ValidationError, match="priority"):
         InputValidator(256).check([1], {"priority": "high"})
+
+
+class SlowEngine(FakeEngine):
+    """FakeEngine that takes 10 ms a step, refuses prompt + max_tokens over 64
+    (the engine's max_model_len check) and can abort requests."""
+
+    def add_request(self, prompt, params, on_token=None, priority=0):
+        if len(prompt) + params.max_tokens > 64:
+            raise ValueError("prompt + max_tokens exceeds max_model_len")
+        rid = super().add_request(prompt, params, on_token, priority)
+        self.waiting[-1].req_id = rid
+        return rid
+
+    def step(self):
+        time.sleep(0.01)
+        return super().step()
+
+    def abort_request(self, rid):
+        for lst in (self.running, self.waiting):
+            for r in list(lst):
+                if r.req_id == rid:
+                    lst.remove(r)
+                    self.aborted = getattr(self, "aborted", []) + [rid]
+                    return True
+        return False
+
+
+def test_client_disconnect_aborts_the_request():
+    """A streaming client that goes away mid-stream stops its request: the
+    engine has no work left and the request was aborted, not decoded on."""
+    eng = SlowEngine()
+
+    async def main():
+        app = create_app(eng)
+        async with TestClient(TestServer(app)) as c:
+            r = await c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 60, "stream": True})
+            assert r.status == 200
+            await r.content.readline()  # first chunk arrived
+            r.close()  # drop the connection
+            for _ in range(200):
+                await asyncio.sleep(0.02)
+                if not eng.has_work():
+                    break
+            assert not eng.has_work()
+            assert getattr(eng, "aborted", []) == [1]
+    asyncio.run(main())
+
+
+def test_websocket_disconnect_aborts_and_engine_errors_are_messages():
+    eng = SlowEngine()
+
+    async def main():
+        app = create_app(eng)
+        async with TestClient(TestServer(app)) as c:
+            ws = await c.ws_connect("/v1/ws")
+            # the engine refuses prompt + max_tokens over its limit: an error message, not a closed socket
+            await ws.send_json({"prompt": "ab", "max_tokens": 63})
+            assert "max_model_len" in (await ws.receive_json())["error"]["message"]
+            await ws.send_json({"prompt": "ab", "max_tokens": 2})
+            msgs = [await ws.receive_json() for _ in range(3)]
+            assert msgs[-1]["done"]
+            await ws.send_json({"prompt": "ab", "max_tokens": 60})
+            await ws.receive_json()
+            await ws.close()
+            for _ in range(200):
+                await asyncio.sleep(0.02)
+                if not eng.has_work():
+                    break
+            assert not eng.has_work() and len(getattr(eng, "aborted", [])) == 1
+    asyncio.run(main())
+
+
+def test_boolean_max_tokens_and_token_ids_are_rejected():
+    from lora_kernel_b200.serve.security import InputValidator, ValidationError
+    v = InputValidator(256)
+    with pytest.raises(ValidationError, match="max_tokens"):
+        v.check([1], {"max_tokens": True})
+    with pytest.raises(ValidationError, match="token id"):
+        v.check([True], {})

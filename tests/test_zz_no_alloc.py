@@ -68,7 +68,15 @@ def test_noalloc_matches_regular_entry_point(M, D):
 
 def test_noalloc_rejects_oversized_requests():
     lib = _lib()
-    M, D = 8192, 4096  # needs min(1024, 2 x SMs) x 4096 floats > the built-in 1 Mi floats
+    # the backward needs min(ceil(M / 8), 2 x SMs) x D scratch floats; pick the
+    # case from this GPU so that it exceeds the built-in 1 Mi floats
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    D = 4096  # the largest width the kernel supports
+    rows_needed = SCRATCH_FLOATS // D + 1
+    if rows_needed > 2 * sms:
+        pytest.skip(f"{sms} SMs: no supported problem exceeds the built-in scratch")
+    M = 8 * rows_needed
+    assert min(-(-M // 8), 2 * sms) * D > SCRATCH_FLOATS
     x = torch.zeros(M, D, dtype=torch.bfloat16, device="cuda")
     g = torch.ones(D, dtype=torch.bfloat16, device="cuda")
     rstd = torch.ones(M, device="cuda")
