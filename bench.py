@@ -8,6 +8,13 @@ uniform-random token ids, N(0, 0.02) random-init weights.  Weak scaling: the
 per-GPU work is fixed as the GPU count grows.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lk|reference|torch]
+                    [--comm p2p|nccl] [--torch-precision mixed|bf16] [--no-phases]
+
+Arms: `--impl lk` (default) is this framework: hand-written sm_100a kernels,
+ZeRO-3 over peer memory (`--comm p2p`) or the same ZeRO-3 schedule with NCCL
+collectives (`--comm nccl`); `--impl torch` is the same workload on library
+code (cuBLAS, SDPA, fused AdamW, FSDP2 over NCCL); `--impl reference` reports
+why the reference cannot run this workload.
 
 For N > 1 launch one process per GPU:
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N \\
@@ -21,7 +28,10 @@ L2 flush is added.  SM clocks and throttle reasons are sampled with nvidia-smi
 during the timed region.  A second, end-to-end pass times K more steps through
 the public API: the native token loader fills page-locked host slots on its
 worker threads, each step copies its ids and targets to the device in one
-transfer, and the loss is read back to the host every step.
+transfer, and the loss is read back to the host every step.  A third, short
+pass (not part of either number) records CUDA events around every phase of
+the step on each stream and reports the per-step device time of each phase,
+max over ranks (`phases_ms`).
 """
 from __future__ import annotations
 
@@ -126,18 +136,27 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def build_trainer(impl: str, cfg, tc, rank: int, world: int, fuse_gather: bool = False):
+def build_trainer(impl: str, cfg, tc, rank: int, world: int, fuse_gather: bool = False, comm: str = "p2p",
+                  torch_precision: str = "mixed"):
     if impl == "lk":
         if world == 1:
             from lora_kernel_b200.train.pipeline import Transformer, TrainingPipeline
             model = Transformer(cfg, "cuda", seed=tc.seed)
             return TrainingPipeline(model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
         from lora_kernel_b200.parallel.zero import Zero3Trainer
-        return Zero3Trainer(cfg, tc, device="cuda", fuse_gather=fuse_gather)
+        return Zero3Trainer(cfg, tc, device="cuda", comm=comm, fuse_gather=fuse_gather)
     if impl == "torch":
         from lora_kernel_b200.models.torch_llama import TorchBaselineTrainer
-        return TorchBaselineTrainer(cfg, tc, device="cuda", world=world)
+        return TorchBaselineTrainer(cfg, tc, device="cuda", world=world, precision=torch_precision)
     raise ValueError(impl)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
 
 
 def launches():
@@ -159,6 +178,12 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override (testing only; invalid for the headline)")
     ap.add_argument("--fuse-gather", action="store_true",
                     help="ZeRO-3: gather each layer inside its first GEMM instead of prefetching it")
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
+                    help="ZeRO-3 collectives: peer-memory kernels (p2p) or NCCL, same schedule")
+    ap.add_argument("--torch-precision", default="mixed", choices=["mixed", "bf16"],
+                    help="--impl torch: fp32 master weights + bf16 compute (mixed), or bf16 weights")
+    ap.add_argument("--no-phases", action="store_true", help="skip the per-phase timing pass")
+    ap.add_argument("--phase-steps", type=int, default=3)
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -181,7 +206,8 @@ def main():
 
     rank, world, local = dist_setup(args.gpus)
     torch.manual_seed(tc.seed + rank)
-    trainer = build_trainer(args.impl, cfg, tc, rank, world, fuse_gather=args.fuse_gather)
+    trainer = build_trainer(args.impl, cfg, tc, rank, world, fuse_gather=args.fuse_gather, comm=args.comm,
+                            torch_precision=args.torch_precision)
     B, S, V = tc.micro_batch, tc.seq_len, cfg.vocab_size
 
     # synthetic data: uniform token ids from a seeded generator, next-token targets
@@ -243,7 +269,26 @@ def main():
     e2e_s = max_over_ranks(e2e_s, world)
     e2e_value = tokens_per_step / e2e_s
 
+    # ---- per-phase device times (separate short pass; every rank takes part)
+    phases = None
+    if not args.no_phases:
+        from lora_kernel_b200.utils.profiler import PhaseTimer, collecting
+        timer = PhaseTimer()
+        P = max(1, args.phase_steps)
+        barrier(world)
+        with collecting(timer):
+            for i in range(P):
+                x, y = dev_batches[i % n_batches]
+                trainer.micro_step_async(x, y)
+        phases = timer.per_step_ms(P)
+
     n_launch = int(l1 - l0)
+    peaks = measured_peaks()
+    model_tflops = value / world * cfg.flops_per_token(S) / 1e12
+    if args.impl == "lk":
+        parallelism = f"zero3-dp{world}" + ("" if world == 1 else f" ({args.comm})")
+    else:
+        parallelism = f"fsdp2-dp{world}" if world > 1 else "dp1"
     out = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -259,7 +304,7 @@ def main():
         "data": "synthetic (uniform random token ids from the native loader, N(0,0.02) random-init weights)",
         "impl": args.impl,
         "config": {"model": MODEL_NAME, "global_batch": B * world, "micro_batch_per_gpu": B,
-                   "seq_len": S, "parallelism": f"zero3-dp{world}",
+                   "seq_len": S, "parallelism": parallelism,
                    "layers": cfg.num_layers,
                    "optimizer": "AdamW+dynamic loss scale+global-norm clip 1.0",
                    "l2": "inputs larger than L2 (each step streams GBs of weights/activations)"},
@@ -268,8 +313,18 @@ def main():
                 "d2h_bytes_per_step": d2h // K},
         "gpu_launches": n_launch,
         "loss_last": round(losses[-1], 4) if losses else None,
-        "mfu": round(value / world * cfg.flops_per_token(S) / 1e12 / 2250.0, 4),
+        "mfu": round(model_tflops / 2250.0, 4),
+        "model_tflops_per_gpu": round(model_tflops, 1),
     }
+    if peaks.get("bf16_tflops_sustained"):
+        out["frac_of_measured_sustained_bf16"] = round(model_tflops / peaks["bf16_tflops_sustained"], 4)
+    if args.impl == "torch":
+        out["torch_precision"] = args.torch_precision
+    if phases is not None:
+        out["phases_ms"] = phases
+        out["phases_note"] = ("separate pass of %d steps: CUDA events around each phase on the stream it runs "
+                              "on, per-step mean, max over ranks; comm.* run on a side stream and overlap "
+                              "compute, wait.* is the main stream waiting on them" % max(1, args.phase_steps))
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:

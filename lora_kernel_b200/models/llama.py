@@ -36,6 +36,7 @@ from ..ops import elementwise as E
 from ..ops import gemm as G
 from ..ops import loss as L
 from ..ops import norm as N
+from ..utils.profiler import ph
 from .params import FlatParams
 
 
@@ -143,7 +144,8 @@ class LlamaModel:
         """Weight gradient: stored on the first micro-step of a window, else accumulated."""
         if not self.train_base and not name.endswith("norm") and name != "embed":
             return
-        G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
+        with ph("bwd.gemm_wgrad"):
+            G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
 
     # ------------------------------------------------------ linear + LoRA
     def _lora_u(self, i: int, t: str, x: torch.Tensor, save: bool):
@@ -169,18 +171,21 @@ class LlamaModel:
     def _lin(self, i: int, t: str, x, out, residual=None, save: bool = True):
         fn = self._take_fused(i, t) if residual is None else None
         if fn is not None:
-            fn(x, self._p(f"layers.{i}.{t}"), out)
+            with ph(f"fwd.gemm_{t}+gather"):
+                fn(x, self._p(f"layers.{i}.{t}"), out)
             return out
         u = self._lora_u(i, t, x, save)
         B = self.lora.B(i, t) if u is not None else None
-        G.gemm(x, self._p(f"layers.{i}.{t}"), out, epi="bf16_resid" if residual is not None else "bf16",
-               residual=residual, a2=u, b2=B)
+        with ph(f"fwd.gemm_{t}"):
+            G.gemm(x, self._p(f"layers.{i}.{t}"), out, epi="bf16_resid" if residual is not None else "bf16",
+                   residual=residual, a2=u, b2=B)
         return out
 
     def _lin_swiglu(self, i: int, x, gu_out, h_out, save: bool = True):
         u = self._lora_u(i, "wgu", x, save)
         B = self.lora.B(i, "wgu") if u is not None else None
-        G.gemm(x, self._p(f"layers.{i}.wgu"), gu_out, epi="swiglu", h_out=h_out, a2=u, b2=B)
+        with ph("fwd.gemm_wgu+swiglu"):
+            G.gemm(x, self._p(f"layers.{i}.wgu"), gu_out, epi="swiglu", h_out=h_out, a2=u, b2=B)
 
     def _lin_bwd(self, i: int, t: str, dy, x, dx_out):
         """dx = dy W (+ s (dy B) A); base and adapter weight gradients."""
@@ -196,9 +201,11 @@ class LlamaModel:
         else:
             fn = self._take_fused(i, t)
             if fn is not None:
-                fn(dy, self._p(name).t(), dx_out)
+                with ph("bwd.gemm_dgrad+gather"):
+                    fn(dy, self._p(name).t(), dx_out)
             else:
-                G.linear_dgrad(dy, self._p(name), out=dx_out)
+                with ph("bwd.gemm_dgrad"):
+                    G.linear_dgrad(dy, self._p(name), out=dx_out)
         self._wgrad(dy, x, name)
 
     # -------------------------------------------------------------- dropout
@@ -214,13 +221,16 @@ class LlamaModel:
         p = f"layers.{i}."
         drop = self._dropping(ws)
         xn1, rstd1 = ws.xn1[slot], ws.rstd1[slot]
-        N.rmsnorm_fwd(h_in, self._p(p + "attn_norm"), cfg.norm_eps, y=xn1, rstd=rstd1)
+        with ph("fwd.rmsnorm"):
+            N.rmsnorm_fwd(h_in, self._p(p + "attn_norm"), cfg.norm_eps, y=xn1, rstd=rstd1)
         qkv = ws.qkv[slot]
         self._lin(i, "wqkv", xn1, qkv, save=self._saving)
         if self.ctx is None:
-            E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
-            A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
-                            causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
+            with ph("fwd.rope"):
+                E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S)
+            with ph("fwd.attention"):
+                A.attention_fwd(qkv, ws.B, ws.S, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                                causal=True, window=self.attn_window, out=ws.o[slot], lse=ws.lse[slot])
         else:
             E.rope_(qkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
                     **self.ctx.rope_args(ws.B, ws.S, self.device))
@@ -230,7 +240,8 @@ class LlamaModel:
             o_in = E.dropout(o_in, cfg.dropout, self._drop_seed(i, 0), out=ws.od[slot])
         hmid = ws.hmid[slot]
         self._lin(i, "wo", o_in, hmid, residual=h_in, save=self._saving)
-        N.rmsnorm_fwd(hmid, self._p(p + "ffn_norm"), cfg.norm_eps, y=ws.xn2[slot], rstd=ws.rstd2[slot])
+        with ph("fwd.rmsnorm"):
+            N.rmsnorm_fwd(hmid, self._p(p + "ffn_norm"), cfg.norm_eps, y=ws.xn2[slot], rstd=ws.rstd2[slot])
         self._lin_swiglu(i, ws.xn2[slot], ws.gu[slot], ws.act[slot], save=self._saving)
         if drop:  # FFN-hidden dropout in place (its backward reads gu, not act)
             E.dropout(ws.act[slot], cfg.dropout, self._drop_seed(i, 1), out=ws.act[slot])
@@ -240,7 +251,8 @@ class LlamaModel:
         cfg = self.cfg
         self._saving = save
         self._hook("pre_forward")
-        E.embedding_fwd(ids.reshape(-1), self._p("embed"), out=ws.h[0])
+        with ph("fwd.embedding"):
+            E.embedding_fwd(ids.reshape(-1), self._p("embed"), out=ws.h[0])
         for i in range(cfg.num_layers):
             self._hook("pre_layer_fwd", i)
             if save:
@@ -248,8 +260,10 @@ class LlamaModel:
             else:
                 self._layer_fwd(i, ws, ws.h[i % 2], ws.h[(i + 1) % 2], 0)
         h_last = ws.h[cfg.num_layers] if save else ws.h[cfg.num_layers % 2]
-        N.rmsnorm_fwd(h_last, self._p("final_norm"), cfg.norm_eps, y=ws.xf, rstd=ws.rstdf)
-        G.linear(ws.xf, self._p("lm_head"), out=ws.logits)
+        with ph("fwd.rmsnorm"):
+            N.rmsnorm_fwd(h_last, self._p("final_norm"), cfg.norm_eps, y=ws.xf, rstd=ws.rstdf)
+        with ph("fwd.gemm_lm_head"):
+            G.linear(ws.xf, self._p("lm_head"), out=ws.logits)
         return ws.logits
 
     @torch.no_grad()
@@ -280,15 +294,18 @@ class LlamaModel:
             acc.zero_()
         self._forward(ids, ws, save=True)
         # K9: loss + dlogits in place (scaled)
-        L.cross_entropy_(ws.logits, targets.reshape(-1), acc, scale=loss_scale, scale_mul=grad_scale,
-                         smoothing=label_smoothing, z_loss=z_loss)
+        with ph("fwd.cross_entropy"):
+            L.cross_entropy_(ws.logits, targets.reshape(-1), acc, scale=loss_scale, scale_mul=grad_scale,
+                             smoothing=label_smoothing, z_loss=z_loss)
         dlogits = ws.logits
         # LM head
-        G.linear_dgrad(dlogits, self._p("lm_head"), out=ws.dx)
+        with ph("bwd.gemm_dgrad"):
+            G.linear_dgrad(dlogits, self._p("lm_head"), out=ws.dx)
         self._wgrad(dlogits, ws.xf, "lm_head")
         L_ = cfg.num_layers
-        N.rmsnorm_bwd(ws.dx, ws.h[L_], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=ws.dh,
-                      accumulate=not overwrite_grads)
+        with ph("bwd.rmsnorm"):
+            N.rmsnorm_bwd(ws.dx, ws.h[L_], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=ws.dh,
+                          accumulate=not overwrite_grads)
         self._hook("post_head_bwd")
         for i in reversed(range(L_)):
             self._hook("pre_layer_bwd", i)
@@ -300,9 +317,10 @@ class LlamaModel:
             self._layer_bwd(i, ws)
             self._hook("post_layer_bwd", i)
         if self.train_base:
-            if overwrite_grads and not cfg.tie_embeddings:
-                self._g("embed").zero_()
-            E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
+            with ph("bwd.embedding"):
+                if overwrite_grads and not cfg.tie_embeddings:
+                    self._g("embed").zero_()
+                E.embedding_bwd(ids.reshape(-1), ws.dh, self._g("embed"))
         self._hook("post_backward")
         self._overwrite = False
         self._drop_step += 1
@@ -322,24 +340,29 @@ class LlamaModel:
         self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
         if drop:
             E.dropout(ws.dact, cfg.dropout, self._drop_seed(i, 1), out=ws.dact)
-        E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
+        with ph("bwd.swiglu"):
+            E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
         self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[s], ws.dx)
-        N.rmsnorm_bwd(ws.dx, ws.hmid[s], self._p(p + "ffn_norm"), ws.rstd2[s], self._g(p + "ffn_norm"),
-                      dres=dh, dx=dh, accumulate=not self._overwrite)
+        with ph("bwd.rmsnorm"):
+            N.rmsnorm_bwd(ws.dx, ws.hmid[s], self._p(p + "ffn_norm"), ws.rstd2[s], self._g(p + "ffn_norm"),
+                          dres=dh, dx=dh, accumulate=not self._overwrite)
         # attention
         self._lin_bwd(i, "wo", dh, ws.od[s] if drop else ws.o[s], ws.do)
         if drop:
             E.dropout(ws.do, cfg.dropout, self._drop_seed(i, 0), out=ws.do)
         if self.ctx is None:
-            A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
-                            cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
-                            dqkv=ws.dqkv)
+            with ph("bwd.attention"):
+                A.attention_bwd(ws.qkv[s], ws.o[s], ws.do, ws.lse[s], ws.B, ws.S, cfg.num_heads,
+                                cfg.num_kv_heads, cfg.head_dim, causal=True, window=self.attn_window,
+                                dqkv=ws.dqkv)
             off = {}
         else:
             self.ctx.backward(ws.do, ws.B, ws.S, ws.dqkv, key=(id(ws), s), window=self.attn_window)
             off = self.ctx.rope_args(ws.B, ws.S, self.device)
-        E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
-                inverse=True, **off)
+        with ph("bwd.rope"):
+            E.rope_(ws.dqkv, 0, cfg.num_heads + cfg.num_kv_heads, cfg.head_dim, self.rope, seq_len=ws.S,
+                    inverse=True, **off)
         self._lin_bwd(i, "wqkv", ws.dqkv, ws.xn1[s], ws.dx)
-        N.rmsnorm_bwd(ws.dx, h_in, self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
-                      dres=dh, dx=dh, accumulate=not self._overwrite)
+        with ph("bwd.rmsnorm"):
+            N.rmsnorm_bwd(ws.dx, h_in, self._p(p + "attn_norm"), ws.rstd1[s], self._g(p + "attn_norm"),
+                          dres=dh, dx=dh, accumulate=not self._overwrite)

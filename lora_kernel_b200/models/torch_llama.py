@@ -1,5 +1,5 @@
 """Plain-PyTorch Llama trainer: the library baseline the B200 kernels are
-measured against (cuBLAS via F.linear, SDPA attention, F.rms_norm, fused
+measured against (cuBLAS via F.linear, SDPA attention, nn.RMSNorm, fused
 torch.optim.AdamW, FSDP2 `fully_shard` + NCCL for more than one GPU).
 Same math as the engine (interleaved RoPE, GQA, SwiGLU, final norm)."""
 from __future__ import annotations
@@ -69,14 +69,30 @@ class TorchLlama(nn.Module):
 
 
 class TorchBaselineTrainer:
-    def __init__(self, cfg: TransformerConfig, tc: TrainConfig, device="cuda", world: int = 1):
+    """The same training step on library code.
+
+    precision "mixed" (default, the engine's numerics): fp32 master weights,
+    bf16 compute (torch.autocast on one GPU; FSDP2 MixedPrecisionPolicy with
+    bf16 parameters and fp32 gradient reduction on several), fused fp32 AdamW,
+    global-norm clip.  "bf16": bf16 weights, moments and AdamW (no master
+    copy), which does less optimizer work than the engine."""
+
+    def __init__(self, cfg: TransformerConfig, tc: TrainConfig, device="cuda", world: int = 1,
+                 precision: str = "mixed"):
+        if precision not in ("mixed", "bf16"):
+            raise ValueError(precision)
         torch.manual_seed(tc.seed)
-        m = TorchLlama(cfg).to(device=device, dtype=torch.bfloat16)
+        self.precision = precision
+        dtype = torch.float32 if precision == "mixed" else torch.bfloat16
+        m = TorchLlama(cfg).to(device=device, dtype=dtype)
+        self.autocast = precision == "mixed" and world == 1
         if world > 1:
-            from torch.distributed.fsdp import fully_shard
+            from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
+            mp = (MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+                  if precision == "mixed" else MixedPrecisionPolicy())
             for b in m.blocks:
-                fully_shard(b)
-            fully_shard(m)
+                fully_shard(b, mp_policy=mp)
+            fully_shard(m, mp_policy=mp)
         self.m = m
         self.opt = torch.optim.AdamW(m.parameters(), lr=tc.lr, betas=(tc.beta1, tc.beta2), eps=tc.eps,
                                      weight_decay=tc.weight_decay, fused=True)
@@ -84,12 +100,17 @@ class TorchBaselineTrainer:
         self.loss_acc = torch.zeros(2, device=device)
 
     def micro_step_async(self, ids, targets):
-        logits = self.m(ids)
-        loss = F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
-        loss.backward()
-        torch.nn.utils.clip_grad_norm_(self.m.parameters(), self.tc.max_grad_norm)
-        self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
+        from ..utils.profiler import ph
+        with ph("fwd"):
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.autocast):
+                logits = self.m(ids)
+            loss = F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+        with ph("bwd"):
+            loss.backward()
+        with ph("step.clip+adamw"):
+            torch.nn.utils.clip_grad_norm_(self.m.parameters(), self.tc.max_grad_norm)
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=True)
         self.loss_acc[0] += loss.detach() * ids.numel()
         self.loss_acc[1] += ids.numel()
 

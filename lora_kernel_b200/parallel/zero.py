@@ -46,6 +46,7 @@ from ..ops.gemm import EPI
 from ..models.llama import LlamaModel
 from ..models.params import FlatParams, build_layout
 from ..train.optimizer import FusedAdamW
+from ..utils.profiler import ph
 from . import comm as CM
 
 NP = 1024  # sum-of-squares partial slots per group (one per reduction CTA: the grid is not capped below the SM count)
@@ -214,11 +215,12 @@ class Zero3Trainer:
     def _gather(self, g: str, dst: torch.Tensor) -> None:
         """On the current stream: dst <- group g gathered from every rank."""
         n = self.L.chunk[g]
-        if self.mode == "p2p":
-            self.pc.allgather_copy(self.shard_sym, self.L.shard_off[g], n, dst)
-        else:
-            o = self.L.shard_off[g]
-            dist.all_gather_into_tensor(dst[:n * self.world], self.shard_p16[o:o + n], group=self.group)
+        with ph("comm.all_gather"):
+            if self.mode == "p2p":
+                self.pc.allgather_copy(self.shard_sym, self.L.shard_off[g], n, dst)
+            else:
+                o = self.L.shard_off[g]
+                dist.all_gather_into_tensor(dst[:n * self.world], self.shard_p16[o:o + n], group=self.group)
 
     def _reduce_scatter(self, g: str, gi: int) -> None:
         """On the current stream: my shard of group g <- sum over ranks."""
@@ -227,14 +229,17 @@ class Zero3Trainer:
         o = self.L.shard_off[g]
         part = self.partial[gi * NP:(gi + 1) * NP]
         if self.mode == "p2p":
-            self.pc.barrier(CM.SLOT_GRAD)
-            self.pc.reduce_scatter_sum(self.grads_sym, a0, n, self.shard_grads[o:o + n],
-                                       accumulate=False, partial=part)
+            with ph("comm.barrier"):
+                self.pc.barrier(CM.SLOT_GRAD)
+            with ph("comm.reduce_scatter"):
+                self.pc.reduce_scatter_sum(self.grads_sym, a0, n, self.shard_grads[o:o + n],
+                                           accumulate=False, partial=part)
         else:
             full = self.engine.grads.flat[s:e]
-            dist.reduce_scatter_tensor(self.shard_grads[o:o + n], full, group=self.group)
-            part.zero_()
-            part[0] = self.shard_grads[o:o + n].float().pow(2).sum()
+            with ph("comm.reduce_scatter"):
+                dist.reduce_scatter_tensor(self.shard_grads[o:o + n], full, group=self.group)
+                part.zero_()
+                part[0] = self.shard_grads[o:o + n].float().pow(2).sum()
 
     def _on_comm(self, fn, *a):
         ev = torch.cuda.Event()
@@ -260,13 +265,15 @@ class Zero3Trainer:
         assert self.slot_layer[s] == i
         ev = self.gathered.pop(i, None)
         if ev is not None:
-            torch.cuda.current_stream().wait_event(ev)
+            with ph("wait.all_gather"):
+                torch.cuda.current_stream().wait_event(ev)
         self.params.bind(f"layers.{i}", self.slots[s])
 
     # --------------------------------------------------------- engine hooks
     def pre_forward(self):
         if self.mode == "p2p":
-            self.pc.barrier(CM.SLOT_STEP)  # every rank's previous update is visible
+            with ph("comm.barrier"):
+                self.pc.barrier(CM.SLOT_STEP)  # every rank's previous update is visible
         self.slot_layer = [-1] * len(self.slots)
 
         def initial():
@@ -276,7 +283,8 @@ class Zero3Trainer:
         if not self.fuse_gather:
             for i in range(min(len(self.slots), self.cfg.num_layers)):
                 self._prefetch_layer(i)
-        torch.cuda.current_stream().wait_event(ev)
+        with ph("wait.all_gather"):
+            torch.cuda.current_stream().wait_event(ev)
 
     # ------------------------------------------------ K17 fused gather
     def _peer_view(self, name: str) -> Optional[torch.Tensor]:
@@ -351,7 +359,8 @@ class Zero3Trainer:
             self._on_comm(self._reduce_scatter, "embed", self.L.names.index("embed"))
         ev = torch.cuda.Event()
         ev.record(self.comm_stream)
-        torch.cuda.current_stream().wait_event(ev)
+        with ph("wait.reduce_scatter"):
+            torch.cuda.current_stream().wait_event(ev)
 
     # -------------------------------------------------------------- stepping
     def _optimizer_step(self):
@@ -359,14 +368,16 @@ class Zero3Trainer:
             self.pre_optimizer(self.shard_grads)
         o = self.opt
         s = o.scaler
-        if self.mode == "p2p":
-            self.pc.norm_exchange(self.partial, o.state, o.max_grad_norm, s.enabled, s.growth,
-                                  s.backoff, s.growth_interval, s.min_scale)
-        else:
-            tot = self.partial.sum().reshape(1)
-            dist.all_reduce(tot, group=self.group)
-            o.finalize(tot)
-        o.apply(self.shard_grads, self.shard_p16, zero_grad=False)
+        with ph("step.grad_norm+finalize"):
+            if self.mode == "p2p":
+                self.pc.norm_exchange(self.partial, o.state, o.max_grad_norm, s.enabled, s.growth,
+                                      s.backoff, s.growth_interval, s.min_scale)
+            else:
+                tot = self.partial.sum().reshape(1)
+                dist.all_reduce(tot, group=self.group)
+                o.finalize(tot)
+        with ph("step.adamw"):
+            o.apply(self.shard_grads, self.shard_p16, zero_grad=False)
         self._opt_steps += 1
 
     def micro_step_async(self, ids: torch.Tensor, targets: torch.Tensor) -> None:

@@ -22,6 +22,7 @@ import torch
 
 from ..config import TrainConfig, TransformerConfig
 from ..models.llama import LlamaModel
+from ..utils.profiler import ph
 from .optimizer import SWA, FusedAdamW
 
 
@@ -137,9 +138,11 @@ class TrainingPipeline:
         if self._micro % self.accum_steps == 0:
             if self.pre_optimizer is not None:
                 self.pre_optimizer(self.engine.grads.flat)
-            self.opt.norm_partials(self.engine.grads.flat)
-            self.opt.finalize()
-            self.opt.apply(self.engine.grads.flat, self.engine.params.flat, zero_grad=False)
+            with ph("step.grad_norm+finalize"):
+                self.opt.norm_partials(self.engine.grads.flat)
+                self.opt.finalize()
+            with ph("step.adamw"):
+                self.opt.apply(self.engine.grads.flat, self.engine.params.flat, zero_grad=False)
             self._opt_steps += 1
             if self.swa is not None:
                 self.swa.update(self.opt.p32, self._opt_steps)

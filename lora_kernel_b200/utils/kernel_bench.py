@@ -171,7 +171,9 @@ def main():
     if "norm" in which:
         bench_norm(args.iters)
     if "attn" in which:
-        bench_attention(args.iters)
+        bench_attention(args.iters)  # Llama 1.1B: B 4, S 2048, 32 / 4 heads, head_dim 64
+    if "attn8b" in which:
+        bench_attention(args.iters, B=2, S=4096, Hq=32, Hkv=8, Dh=128)  # Llama 8B shape
 
 
 if __name__ == "__main__":
