@@ -137,14 +137,14 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 def build_trainer(impl: str, cfg, tc, rank: int, world: int, fuse_gather: bool = False, comm: str = "p2p",
-                  torch_precision: str = "mixed"):
+                  torch_precision: str = "mixed", grad_wire: str = "bf16"):
     if impl == "lk":
         if world == 1:
             from lora_kernel_b200.train.pipeline import Transformer, TrainingPipeline
             model = Transformer(cfg, "cuda", seed=tc.seed)
             return TrainingPipeline(model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
         from lora_kernel_b200.parallel.zero import Zero3Trainer
-        return Zero3Trainer(cfg, tc, device="cuda", comm=comm, fuse_gather=fuse_gather)
+        return Zero3Trainer(cfg, tc, device="cuda", comm=comm, fuse_gather=fuse_gather, grad_wire=grad_wire)
     if impl == "torch":
         from lora_kernel_b200.models.torch_llama import TorchBaselineTrainer
         return TorchBaselineTrainer(cfg, tc, device="cuda", world=world, precision=torch_precision)
@@ -180,6 +180,9 @@ def main():
                     help="ZeRO-3: gather each layer inside its first GEMM instead of prefetching it")
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="ZeRO-3 collectives: peer-memory kernels (p2p) or NCCL, same schedule")
+    ap.add_argument("--grad-wire", default="bf16", choices=["bf16", "fp32"],
+                    help="ZeRO-3: gradients reduce-scattered as bf16 every micro-batch (sharded fp32 "
+                         "accumulation) or from a full fp32 buffer")
     ap.add_argument("--torch-precision", default="mixed", choices=["mixed", "bf16"],
                     help="--impl torch: fp32 master weights + bf16 compute (mixed), or bf16 weights")
     ap.add_argument("--no-phases", action="store_true", help="skip the per-phase timing pass")
@@ -207,7 +210,7 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     torch.manual_seed(tc.seed + rank)
     trainer = build_trainer(args.impl, cfg, tc, rank, world, fuse_gather=args.fuse_gather, comm=args.comm,
-                            torch_precision=args.torch_precision)
+                            torch_precision=args.torch_precision, grad_wire=args.grad_wire)
     B, S, V = tc.micro_batch, tc.seq_len, cfg.vocab_size
 
     # synthetic data: uniform token ids from a seeded generator, next-token targets
@@ -286,7 +289,7 @@ def main():
     peaks = measured_peaks()
     model_tflops = value / world * cfg.flops_per_token(S) / 1e12
     if args.impl == "lk":
-        parallelism = f"zero3-dp{world}" + ("" if world == 1 else f" ({args.comm})")
+        parallelism = f"zero3-dp{world}" + ("" if world == 1 else f" ({args.comm}, {args.grad_wire} grads)")
     else:
         parallelism = f"fsdp2-dp{world}" if world > 1 else "dp1"
     out = {
@@ -320,6 +323,9 @@ def main():
         out["frac_of_measured_sustained_bf16"] = round(model_tflops / peaks["bf16_tflops_sustained"], 4)
     if args.impl == "torch":
         out["torch_precision"] = args.torch_precision
+    if hasattr(trainer, "grad_memory_bytes"):
+        out["grad_wire"] = args.grad_wire
+        out["grad_bytes_per_rank"] = int(trainer.grad_memory_bytes())
     if phases is not None:
         out["phases_ms"] = phases
         out["phases_note"] = ("separate pass of %d steps: CUDA events around each phase on the stream it runs "

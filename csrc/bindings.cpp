@@ -536,9 +536,12 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::
   need_contig(x, "x", torch::kBFloat16);
   need_contig(dx, "dx", torch::kBFloat16);
   need_contig(rstd, "rstd", torch::kFloat32);
-  need_contig(dgamma, "dgamma", torch::kFloat32);
+  const bool g16 = dgamma.scalar_type() == torch::kBFloat16;
+  need_contig(dgamma, "dgamma", g16 ? torch::kBFloat16 : torch::kFloat32);
+  TORCH_CHECK(!g16 || !accumulate, "rmsnorm_bwd: a bf16 dgamma is stored, not accumulated");
   need_contig(partial, "partial", torch::kFloat32);
   LkNormBwdDesc d{};
+  d.dgamma_bf16 = g16 ? 1 : 0;
   d.D = (int)x.size(-1);
   d.M = (int)(x.numel() / d.D);
   d.dy = dy.data_ptr();
@@ -547,7 +550,7 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::
   d.rstd = rstd.data_ptr<float>();
   d.dres = optp(dres);
   d.dx = dx.data_ptr();
-  d.dgamma = dgamma.data_ptr<float>();
+  d.dgamma = reinterpret_cast<float*>(dgamma.data_ptr());
   d.partial = partial.data_ptr<float>();
   d.partial_rows = (int)(partial.numel() / d.D);
   d.accumulate = accumulate ? 1 : 0;
@@ -804,6 +807,26 @@ void reduce_scatter_sum(torch::Tensor src_ptrs, int64_t src_off, int64_t n, torc
                               partial.has_value() ? (int)partial->numel() : 0, stream()));
 }
 
+void reduce_scatter_bf16(torch::Tensor src_ptrs, int64_t src_off, int64_t n, torch::Tensor dst, int64_t world,
+                         bool accumulate, c10::optional<torch::Tensor> partial) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  need_contig(dst, "dst", torch::kFloat32);
+  TORCH_CHECK(dst.numel() >= n, "reduce_scatter_bf16: dst too small");
+  check(lk_reduce_scatter_bf16(ptrs<const void* const*>(src_ptrs), src_off, n, dst.data_ptr<float>(), (int)world,
+                               accumulate ? 1 : 0, optp<float>(partial),
+                               partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
+void reduce_scatter_bf16_nvls(int64_t mc_ptr, int64_t n, torch::Tensor dst, bool accumulate,
+                              c10::optional<torch::Tensor> partial) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  need_contig(dst, "dst", torch::kFloat32);
+  TORCH_CHECK(dst.numel() >= n, "reduce_scatter_bf16_nvls: dst too small");
+  check(lk_reduce_scatter_bf16_nvls(reinterpret_cast<const void*>(mc_ptr), n, dst.data_ptr<float>(),
+                                    accumulate ? 1 : 0, optp<float>(partial),
+                                    partial.has_value() ? (int)partial->numel() : 0, stream()));
+}
+
 void allreduce_sum(torch::Tensor buf_ptrs, int64_t n, int64_t rank, int64_t world,
                    c10::optional<torch::Tensor> partial) {
   const c10::cuda::CUDAGuard g(buf_ptrs.device());
@@ -1011,6 +1034,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequantize", &dequantize);
   m.def("allgather_copy", &allgather_copy);
   m.def("reduce_scatter_sum", &reduce_scatter_sum);
+  m.def("reduce_scatter_bf16", &reduce_scatter_bf16);
+  m.def("reduce_scatter_bf16_nvls", &reduce_scatter_bf16_nvls);
   m.def("allreduce_sum", &allreduce_sum);
   m.def("norm_exchange", &norm_exchange);
   m.attr("SIG_SLOTS") = (int)LK_SIG_SLOTS;

@@ -8,7 +8,9 @@
 //                        parameter gather into a local slot; plain 16-byte P2P loads)
 //   reduce-scatter sum   K10 front half: out[k] = sum_p peer_p.grad[off + k] (fp32,
 //                        fixed rank order so every rank's shard is deterministic)
-//                        fused with the sum-of-squares partials of the result
+//                        fused with the sum-of-squares partials of the result;
+//                        the bf16 form reads bf16 gradients (half the NVLink
+//                        bytes), sums in fp32 and accumulates into the fp32 shard
 //   all-reduce sum       K12: out = sum_p peer_p.buf (one-shot, each rank reduces
 //                        its 1/N slice and writes it into every peer = reduce-scatter
 //                        + all-gather in one kernel) fused with unscale-free Σg^2
@@ -319,6 +321,99 @@ __global__ void __launch_bounds__(256) reduce_scatter_nvls_kernel(const float* _
   if (partial) block_partial(ss, partial);
 }
 
+// ZeRO gradient reduce-scatter with bf16 on the wire (K10): every rank's
+// gradients of a layer group sit in a bf16 slot of symmetric memory; the owner
+// of a chunk loads the peers' bf16 values, sums them in fp32 in a fixed rank
+// order, adds the result into its fp32 gradient shard (or stores it on the
+// first micro-batch of an accumulation window) and emits the sum-of-squares
+// partials of the shard when asked (last micro-batch).  Half the bytes of the
+// fp32 exchange cross NVLink.
+template <int MAXW>
+__global__ void __launch_bounds__(256) reduce_scatter_bf16_kernel(
+    const __nv_bfloat16* const* __restrict__ src_ptrs, int64_t src_off, int64_t n, float* __restrict__ dst,
+    int world, int accumulate, float* __restrict__ partial) {
+  const __nv_bfloat16* src[MAXW];
+#pragma unroll
+  for (int p = 0; p < MAXW; ++p) src[p] = p < world ? src_ptrs[p] + src_off : nullptr;
+  float ss = 0.f;
+  const int64_t n8 = n / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < MAXW; ++p) {
+      if (p >= world) break;
+      const uint4 v = reinterpret_cast<const uint4*>(src[p])[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    float4* d = reinterpret_cast<float4*>(dst) + 2 * i;
+    float4 o0 = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    float4 o1 = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    if (accumulate) {
+      const float4 a = d[0], b = d[1];
+      o0.x += a.x; o0.y += a.y; o0.z += a.z; o0.w += a.w;
+      o1.x += b.x; o1.y += b.y; o1.z += b.z; o1.w += b.w;
+    }
+    d[0] = o0;
+    d[1] = o1;
+    ss += o0.x * o0.x + o0.y * o0.y + o0.z * o0.z + o0.w * o0.w + o1.x * o1.x + o1.y * o1.y + o1.z * o1.z +
+          o1.w * o1.w;
+  }
+  if (partial) {
+    __shared__ float red[8];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int k = 0; k < 8; ++k) t += red[k];
+      partial[blockIdx.x] = t;
+    }
+  }
+}
+
+// NVLS form: the switch adds the ranks' bf16 values with fp32 accumulation
+// (one rounding of the sum to bf16), then the owner accumulates in fp32.
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const __nv_bfloat16* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) reduce_scatter_bf16_nvls_kernel(const __nv_bfloat16* __restrict__ mc,
+                                                                       int64_t n, float* __restrict__ dst,
+                                                                       int accumulate, float* __restrict__ partial) {
+  float ss = 0.f;
+  const int64_t n8 = n / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = mm_ld_reduce_bf16x8(mc + 8 * i);
+    const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), e = unpack_bf16x2(v.w);
+    float4 o0 = make_float4(a.x, a.y, b.x, b.y);
+    float4 o1 = make_float4(c.x, c.y, e.x, e.y);
+    float4* d = reinterpret_cast<float4*>(dst) + 2 * i;
+    if (accumulate) {
+      const float4 p0 = d[0], p1 = d[1];
+      o0.x += p0.x; o0.y += p0.y; o0.z += p0.z; o0.w += p0.w;
+      o1.x += p1.x; o1.y += p1.y; o1.z += p1.z; o1.w += p1.w;
+    }
+    d[0] = o0;
+    d[1] = o1;
+    ss += o0.x * o0.x + o0.y * o0.y + o0.z * o0.z + o0.w * o0.w + o1.x * o1.x + o1.y * o1.y + o1.z * o1.z +
+          o1.w * o1.w;
+  }
+  if (partial) block_partial(ss, partial);
+}
+
 static int copy_grid(int64_t work) {
   int64_t g = (work + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 4;
@@ -407,4 +502,30 @@ extern "C" int lk_reduce_scatter_sum_nvls(const float* mc, int64_t n, float* dst
   reduce_scatter_nvls_kernel<<<grid, 256, 0, s>>>(mc, n, dst, accumulate, partial);
   if (partial && nparts > grid) cudaMemsetAsync(partial + grid, 0, sizeof(float) * (nparts - grid), s);
   return check_launch("reduce_scatter_nvls");
+}
+
+extern "C" int lk_reduce_scatter_bf16(const void* const* src_ptrs, int64_t src_off, int64_t n, float* dst,
+                                      int world, int accumulate, float* partial, int nparts, cudaStream_t s) {
+  LK_REQUIRE(world >= 1 && world <= 8, "reduce_scatter_bf16: world must be 1..8");
+  LK_REQUIRE(n % 8 == 0 && src_off % 8 == 0 && ((uintptr_t)dst & 15) == 0,
+             "reduce_scatter_bf16: n and offset must be multiples of 8, dst 16-byte aligned");
+  if (n == 0) return 0;
+  int grid = copy_grid(n / 8);
+  if (partial) grid = nparts < grid ? nparts : grid;
+  reduce_scatter_bf16_kernel<8><<<grid, 256, 0, s>>>((const __nv_bfloat16* const*)src_ptrs, src_off, n, dst,
+                                                     world, accumulate, partial);
+  if (partial && nparts > grid) cudaMemsetAsync(partial + grid, 0, sizeof(float) * (nparts - grid), s);
+  return check_launch("reduce_scatter_bf16");
+}
+
+extern "C" int lk_reduce_scatter_bf16_nvls(const void* mc, int64_t n, float* dst, int accumulate, float* partial,
+                                           int nparts, cudaStream_t s) {
+  LK_REQUIRE(mc && n % 8 == 0 && ((uintptr_t)mc & 15) == 0 && ((uintptr_t)dst & 15) == 0,
+             "reduce_scatter_bf16_nvls: 16-byte aligned buffers, n % 8");
+  if (n == 0) return 0;
+  int grid = copy_grid(n / 8);
+  if (partial) grid = nparts < grid ? nparts : grid;
+  reduce_scatter_bf16_nvls_kernel<<<grid, 256, 0, s>>>((const __nv_bfloat16*)mc, n, dst, accumulate, partial);
+  if (partial && nparts > grid) cudaMemsetAsync(partial + grid, 0, sizeof(float) * (nparts - grid), s);
+  return check_launch("reduce_scatter_bf16_nvls");
 }

@@ -115,6 +115,7 @@ typedef struct LkNormBwdDesc {
   int partial_rows;
   int M, D;
   int accumulate;     // dgamma += (1) or = (0)
+  int dgamma_bf16;    // 1: dgamma points to bf16 [D] and is stored (accumulate must be 0)
 } LkNormBwdDesc;
 
 int lk_rmsnorm_fwd(const LkNormFwdDesc* d, cudaStream_t s);
@@ -404,6 +405,11 @@ int lk_allreduce_sum_nvls(float* mc, int64_t n, int rank, int world, float* part
                           cudaStream_t s);
 int lk_reduce_scatter_sum_nvls(const float* mc, int64_t n, float* dst, int accumulate, float* partial,
                                int nparts, cudaStream_t s);
+// bf16 gradients in, fp32 shard out (+= when accumulate), Σg² partials of the shard
+int lk_reduce_scatter_bf16(const void* const* src_ptrs, int64_t src_off, int64_t n, float* dst, int world,
+                           int accumulate, float* partial, int nparts, cudaStream_t s);
+int lk_reduce_scatter_bf16_nvls(const void* mc, int64_t n, float* dst, int accumulate, float* partial,
+                                int nparts, cudaStream_t s);
 int lk_allreduce_sum(float* const* buf_ptrs, int64_t n, int rank, int world, float* partial,
                      int nparts, cudaStream_t s);
 int lk_norm_exchange(const float* partial, int nparts, double* const* nbuf_ptrs, int* const* sig_ptrs,

@@ -80,8 +80,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(
 
 // Backward: one warp per row, grid-stride over rows, two passes over the row
 // (the second hits L1/L2).  dgamma partials accumulate per warp in shared
-// memory; each block then writes one partial row to partial[blockIdx.x, :]
-// (fp32 scratch, gridDim.x x D), summed by colsum_kernel.
+// memory (float4 read-modify-write); each block then writes one partial row to
+// partial[blockIdx.x, :] (fp32 scratch, gridDim.x x D), summed by colsum_kernel.
 template <int VPT>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
@@ -118,26 +118,27 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     for (int i = 0; i < VPT; ++i) {
       const int c = i * 32 + lane;
       const uint4 a = xr[c], b = yr[c], g = gr[c];
+      const uint4 r = dres ? reinterpret_cast<const uint4*>(dres + (int64_t)row * D)[c] : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
       const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-      uint32_t rw[4] = {0u, 0u, 0u, 0u};
-      if (dres) {
-        const uint4 r = reinterpret_cast<const uint4*>(dres + (int64_t)row * D)[c];
-        rw[0] = r.x; rw[1] = r.y; rw[2] = r.z; rw[3] = r.w;
-      }
+      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+      float4* acc4 = reinterpret_cast<float4*>(my + c * 8);
+      const float4 a0 = acc4[0], a1 = acc4[1];
+      float accv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       uint32_t o[4];
-      float* acc = my + c * 8;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 xf = unpack_bf16x2(aw[e]), yf = unpack_bf16x2(bw[e]), gf = unpack_bf16x2(gw[e]);
         const float2 rf = unpack_bf16x2(rw[e]);
         const float xh0 = xf.x * rs, xh1 = xf.y * rs;
-        acc[2 * e] += yf.x * xh0;
-        acc[2 * e + 1] += yf.y * xh1;
+        accv[2 * e] += yf.x * xh0;
+        accv[2 * e + 1] += yf.y * xh1;
         o[e] = pack_bf16x2(rs * (yf.x * gf.x - xh0 * dot) + rf.x,
                            rs * (yf.y * gf.y - xh1 * dot) + rf.y);
       }
+      acc4[0] = make_float4(accv[0], accv[1], accv[2], accv[3]);
+      acc4[1] = make_float4(accv[4], accv[5], accv[6], accv[7]);
       reinterpret_cast<uint4*>(dx + (int64_t)row * D)[c] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
@@ -149,14 +150,36 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
   }
 }
 
-// dgamma[c] (+)= sum_b partial[b, c]
-__global__ void colsum_kernel(const float* __restrict__ partial, int nrows, int D,
-                              float* __restrict__ out, int accumulate) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= D) return;
-  float s = 0.f;
-  for (int r = 0; r < nrows; ++r) s += partial[(int64_t)r * D + col];
-  out[col] = accumulate ? out[col] + s : s;
+// dgamma[c] (+)= sum_b partial[b, c]; bf16_out: dgamma is bf16 and stored.
+// One block per 32 columns: the 8 warps split the partial rows (coalesced
+// 128-byte loads, independent adds in flight), then combine in shared memory.
+__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ partial, int nrows, int D,
+                                                     float* __restrict__ out, int accumulate, int bf16_out) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (col < D) {
+    int r = w;
+    for (; r + 24 < nrows; r += 32) {
+      s0 += partial[(int64_t)r * D + col];
+      s1 += partial[(int64_t)(r + 8) * D + col];
+      s2 += partial[(int64_t)(r + 16) * D + col];
+      s3 += partial[(int64_t)(r + 24) * D + col];
+    }
+    for (; r < nrows; r += 8) s0 += partial[(int64_t)r * D + col];
+  }
+  red[w][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (w == 0 && col < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k][lane];
+    if (bf16_out)
+      reinterpret_cast<__nv_bfloat16*>(out)[col] = __float2bfloat16_rn(s);
+    else
+      out[col] = accumulate ? out[col] + s : s;
+  }
 }
 
 template <int VPT>
@@ -221,6 +244,8 @@ extern "C" int lk_rmsnorm_bwd(const LkNormBwdDesc* d, cudaStream_t s) {
     default: return fail("rmsnorm_bwd: unsupported D");
   }
   if (check_launch("rmsnorm_bwd")) return -1;
-  colsum_kernel<<<cdiv(d->D, 256), 256, 0, s>>>(d->partial, grid, d->D, d->dgamma, d->accumulate);
+  LK_REQUIRE(!d->dgamma_bf16 || !d->accumulate, "rmsnorm_bwd: a bf16 dgamma is stored, not accumulated");
+  colsum_kernel<<<cdiv(d->D, 32), 256, 0, s>>>(d->partial, grid, d->D, d->dgamma, d->accumulate,
+                                               d->dgamma_bf16);
   return check_launch("rmsnorm_dgamma");
 }

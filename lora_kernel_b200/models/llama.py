@@ -144,8 +144,13 @@ class LlamaModel:
         """Weight gradient: stored on the first micro-step of a window, else accumulated."""
         if not self.train_base and not name.endswith("norm") and name != "embed":
             return
+        g = self._g(name)
+        # a bf16 gradient view (ZeRO-3 slot, reduce-scattered every micro-batch)
+        # is stored; an fp32 one is stored on the first micro-batch of a window
+        # and accumulated afterwards
+        epi = "bf16" if g.dtype == torch.bfloat16 else ("f32" if self._overwrite else "f32_acc")
         with ph("bwd.gemm_wgrad"):
-            G.gemm(dy.t(), x.t(), self._g(name), epi="f32" if self._overwrite else "f32_acc")
+            G.gemm(dy.t(), x.t(), g, epi=epi)
 
     # ------------------------------------------------------ linear + LoRA
     def _lora_u(self, i: int, t: str, x: torch.Tensor, save: bool):

@@ -40,10 +40,13 @@ def _partial(M: int, D: int, device) -> torch.Tensor:
 def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor, rstd: torch.Tensor,
                 dgamma: torch.Tensor, *, dres: Optional[torch.Tensor] = None,
                 dx: Optional[torch.Tensor] = None, accumulate: bool = True) -> torch.Tensor:
-    """dx = d rmsnorm / dx (+ dres); dgamma (fp32) += / = sum over rows."""
+    """dx = d rmsnorm / dx (+ dres); dgamma (fp32) += / = sum over rows, or,
+    for a bf16 dgamma, the sum stored (accumulate must then be False)."""
     require_device(x)
     D = x.shape[-1]
     dx = torch.empty_like(x) if dx is None else dx
+    if dgamma.dtype == torch.bfloat16:
+        accumulate = False
     C().rmsnorm_bwd(dy, x, gamma, rstd, dres, dx, dgamma, _partial(x.numel() // D, D, x.device),
                     bool(accumulate))
     return dx

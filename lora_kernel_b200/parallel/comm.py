@@ -31,6 +31,7 @@ SLOT_GRAD = 1       # a layer's gradients are complete on every rank
 SLOT_NORM = 2       # gradient-norm exchange
 SLOT_AR_IN = 3      # all-reduce inputs ready
 SLOT_AR_OUT = 4     # all-reduce outputs written
+SLOT_GRAD_DONE = 5  # every rank has read a gradient slot (it may be overwritten)
 SLOT_USER = 8
 
 
@@ -146,6 +147,15 @@ class PeerComm:
             C().reduce_scatter_sum_nvls(src.mc_ptr + 4 * src_off, n, dst, accumulate, partial)
         else:
             C().reduce_scatter_sum(src.ptrs, src_off, n, dst, self.world, accumulate, partial)
+
+    def reduce_scatter_bf16(self, src: SymBuffer, src_off: int, n: int, dst: torch.Tensor,
+                            accumulate: bool = False, partial: Optional[torch.Tensor] = None) -> None:
+        """dst[:n] (fp32) (+)= sum over ranks of src[src_off:src_off+n] (bf16
+        on the wire, fp32 sum).  The caller has made every rank's src ready."""
+        if self.nvls and src.mc_ptr:
+            C().reduce_scatter_bf16_nvls(src.mc_ptr + 2 * src_off, n, dst, accumulate, partial)
+        else:
+            C().reduce_scatter_bf16(src.ptrs, src_off, n, dst, self.world, accumulate, partial)
 
     def allreduce_sum_(self, buf: SymBuffer, n: int, partial: Optional[torch.Tensor] = None,
                        off: int = 0) -> None:

@@ -11,12 +11,19 @@ Per micro-batch (one process per GPU, all on NVLink / NVSwitch):
              local slot (P2P copy kernel on a side stream, one layer ahead;
              two slots, so layer i+1's gather overlaps layer i's compute);
   backward   layers are re-gathered in reverse (the last two are still
-             resident); weight gradients accumulate in a full-size fp32 buffer
-             (symmetric memory) and, on the last micro-batch of the window,
-             every finished group is reduce-scattered right away on the side
-             stream: a device barrier, then K10's first half - the owner sums
-             its chunk over all peers in a fixed rank order and emits the
-             sum-of-squares partials of the result;
+             resident).  grad_wire="bf16" (default): each layer's weight
+             gradients are written as bf16 into one of three rotating slots of
+             symmetric memory (the LM head into its own), and as soon as a
+             layer's backward is done its slot is reduce-scattered on the side
+             stream: a device barrier, K10 - the owner loads every peer's bf16
+             chunk, sums in fp32 in a fixed rank order and adds it into its
+             fp32 gradient shard (every micro-batch, so per-rank gradient
+             memory is the 1/N shard plus the slots), with the sum-of-squares
+             partials on the last micro-batch - then a second barrier after
+             which the slot may be overwritten.  The embedding gradient
+             (scatter-add) stays in a local fp32 buffer reduced once per
+             window.  grad_wire="fp32": weight gradients accumulate in a
+             full-size fp32 buffer reduce-scattered on the last micro-batch;
   step       the partials are exchanged through peer memory and the step
              finaliser runs on the device (global-norm clip, overflow skip,
              dynamic loss scale), then AdamW updates the owned shard and
@@ -49,7 +56,8 @@ from ..train.optimizer import FusedAdamW
 from ..utils.profiler import ph
 from . import comm as CM
 
-NP = 1024  # sum-of-squares partial slots per group (one per reduction CTA: the grid is not capped below the SM count)
+NP = 1024
+N_GRAD_SLOTS = 3  # rotating bf16 gradient slots: layer i+3 must be read by every rank before layer i writes  # sum-of-squares partial slots per group (one per reduction CTA: the grid is not capped below the SM count)
 
 
 class ShardLayout:
@@ -143,7 +151,7 @@ class Zero3Trainer:
     owner's shard in peer memory."""
 
     def __init__(self, cfg: TransformerConfig, tc: TrainConfig, device="cuda", group=None,
-                 comm: str = "p2p", fuse_gather: bool = False):
+                 comm: str = "p2p", fuse_gather: bool = False, grad_wire: str = "bf16"):
         self.cfg, self.tc = cfg, tc
         self.device = torch.device(device)
         self.group = group or dist.group.WORLD
@@ -151,24 +159,48 @@ class Zero3Trainer:
         self.rank = dist.get_rank(self.group)
         self.mode = comm
         self.fuse_gather = fuse_gather and comm == "p2p"
+        if grad_wire not in ("bf16", "fp32"):
+            raise ValueError(grad_wire)
+        self.grad_wire = grad_wire
         L = self.L = ShardLayout(cfg, self.world, self.rank)
         bf, f32 = torch.bfloat16, torch.float32
+
+        def glen(g):
+            s, e = L.groups[g]
+            return e - s
+        nl = cfg.num_layers
+        gmax = max(glen(f"layers.{i}") for i in range(nl))
 
         # deterministic full init on the device, keep only the owned chunks
         full = FlatParams(cfg, self.device, bf, group_align=L.align)
         full.init_(tc.seed, cfg.init_std)
         shard = L.extract_shard(full.flat)
         del full
+        bf16_wire = grad_wire == "bf16"
+        self.n_gslots = min(N_GRAD_SLOTS, nl)
+        self.gslot_len = gmax
         if comm == "p2p":
             self.pc = CM.PeerComm(self.device, self.group)
             self.shard_sym = CM.SymBuffer(L.shard_numel, bf, self.device, self.group)
             self.shard_p16 = self.shard_sym.local
-            self.grads_sym = CM.SymBuffer(L.total, f32, self.device, self.group)
-            grads_flat = self.grads_sym.local
+            if bf16_wire:
+                self.gslot_sym = CM.SymBuffer(self.n_gslots * gmax, bf, self.device, self.group)
+                self.ghead_sym = CM.SymBuffer(glen("head"), bf, self.device, self.group)
+                self.gembed_sym = CM.SymBuffer(glen("embed"), f32, self.device, self.group)
+                gslot_flat, ghead, gembed = self.gslot_sym.local, self.ghead_sym.local, self.gembed_sym.local
+            else:
+                self.grads_sym = CM.SymBuffer(L.total, f32, self.device, self.group)
+                grads_flat = self.grads_sym.local
         else:
             self.pc = None
             self.shard_p16 = torch.empty(L.shard_numel, dtype=bf, device=self.device)
-            grads_flat = torch.zeros(L.total, dtype=f32, device=self.device)
+            if bf16_wire:
+                gslot_flat = torch.zeros(self.n_gslots * gmax, dtype=bf, device=self.device)
+                ghead = torch.zeros(glen("head"), dtype=bf, device=self.device)
+                gembed = torch.zeros(glen("embed"), dtype=f32, device=self.device)
+                self.rs_tmp = torch.empty(max(L.chunk.values()), dtype=bf, device=self.device)
+            else:
+                grads_flat = torch.zeros(L.total, dtype=f32, device=self.device)
         self.shard_p16.copy_(shard)
         del shard
         self.opt = FusedAdamW(self.shard_p16.float(), L.shard_segments(tc.decay_norms), lr=tc.lr,
@@ -181,11 +213,6 @@ class Zero3Trainer:
         self.partial = torch.zeros(len(L.names) * NP, dtype=f32, device=self.device)
 
         # gathered-weight buffers: embed, head, and two rotating layer slots
-        def glen(g):
-            s, e = L.groups[g]
-            return e - s
-        nl = cfg.num_layers
-        gmax = max(glen(f"layers.{i}") for i in range(nl))
         self.buf = {"embed": torch.empty(glen("embed"), dtype=bf, device=self.device),
                     "head": torch.empty(glen("head"), dtype=bf, device=self.device)}
         self.slots = [torch.empty(gmax, dtype=bf, device=self.device) for _ in range(min(2, nl))]
@@ -199,12 +226,25 @@ class Zero3Trainer:
         self.engine = LlamaModel(cfg, self.device, params=self.params, with_grads=False)
         self.engine.dropout_seed = tc.seed + 7919 * self.rank  # ranks see different data: decorrelate masks
         self.engine.recompute = tc.recompute_activations
-        self.engine.grads = FlatParams(cfg, self.device, f32, buffer=grads_flat, group_align=L.align)
+        if bf16_wire:
+            # gradient views: layer groups in rotating bf16 slots, the head in its
+            # own bf16 buffer, the embedding in a local fp32 buffer (scatter-add)
+            self.gslots = [gslot_flat[k * gmax:(k + 1) * gmax] for k in range(self.n_gslots)]
+            self.ghead = ghead
+            self.gembed = gembed
+            self.grad_views = _SlotParams(L)
+            self.grad_views.bind("embed", self.gembed)
+            self.grad_views.bind("head", self.ghead)
+            self.engine.grads = self.grad_views
+            self.slot_free: List[Optional[torch.cuda.Event]] = [None] * self.n_gslots
+        else:
+            self.engine.grads = FlatParams(cfg, self.device, f32, buffer=grads_flat, group_align=L.align)
         self.engine.hooks = self
         self.comm_stream = torch.cuda.Stream(self.device)
         self.gathered: Dict[int, torch.cuda.Event] = {}
         self.accum_steps = max(1, tc.grad_accum_steps)
         self._micro = 0
+        self._first = True
         self._last = True
         self._opt_steps = 0
         self.loss_acc = torch.zeros(2, dtype=f32, device=self.device)
@@ -223,11 +263,25 @@ class Zero3Trainer:
                 dist.all_gather_into_tensor(dst[:n * self.world], self.shard_p16[o:o + n], group=self.group)
 
     def _reduce_scatter(self, g: str, gi: int) -> None:
-        """On the current stream: my shard of group g <- sum over ranks."""
+        """On the current stream: my shard of group g <- sum over ranks of the
+        fp32 gradients (the whole window's, reduced on its last micro-batch)."""
         s, e = self.L.groups[g]
         a0, n = self.L.owned(g)
         o = self.L.shard_off[g]
         part = self.partial[gi * NP:(gi + 1) * NP]
+        if self.grad_wire == "bf16":  # only the embedding group is fp32, in its own buffer
+            if self.mode == "p2p":
+                with ph("comm.barrier"):
+                    self.pc.barrier(CM.SLOT_GRAD)
+                with ph("comm.reduce_scatter"):
+                    self.pc.reduce_scatter_sum(self.gembed_sym, a0 - s, n, self.shard_grads[o:o + n],
+                                               accumulate=False, partial=part)
+            else:
+                with ph("comm.reduce_scatter"):
+                    dist.reduce_scatter_tensor(self.shard_grads[o:o + n], self.gembed, group=self.group)
+                    part.zero_()
+                    part[0] = self.shard_grads[o:o + n].float().pow(2).sum()
+            return
         if self.mode == "p2p":
             with ph("comm.barrier"):
                 self.pc.barrier(CM.SLOT_GRAD)
@@ -240,6 +294,36 @@ class Zero3Trainer:
                 dist.reduce_scatter_tensor(self.shard_grads[o:o + n], full, group=self.group)
                 part.zero_()
                 part[0] = self.shard_grads[o:o + n].float().pow(2).sum()
+
+    def _reduce_scatter_bf16(self, g: str, gi: int, buf: torch.Tensor, sym_off: int) -> None:
+        """On the current stream: my fp32 shard of group g (+)= sum over ranks of
+        the group's bf16 gradients in `buf` (every micro-batch; partials on the
+        last one)."""
+        s, _ = self.L.groups[g]
+        a0, n = self.L.owned(g)
+        o = self.L.shard_off[g]
+        part = self.partial[gi * NP:(gi + 1) * NP] if self._last else None
+        first = self._first
+        dst = self.shard_grads[o:o + n]
+        if self.mode == "p2p":
+            sym = self.ghead_sym if g == "head" else self.gslot_sym
+            with ph("comm.barrier"):
+                self.pc.barrier(CM.SLOT_GRAD)
+            with ph("comm.reduce_scatter"):
+                self.pc.reduce_scatter_bf16(sym, sym_off + (a0 - s), n, dst, accumulate=not first, partial=part)
+            with ph("comm.barrier"):
+                self.pc.barrier(CM.SLOT_GRAD_DONE)  # every rank has read this slot
+        else:
+            glen = self.L.groups[g][1] - s
+            with ph("comm.reduce_scatter"):
+                dist.reduce_scatter_tensor(self.rs_tmp[:n], buf[:glen], group=self.group)
+                if first:
+                    dst.copy_(self.rs_tmp[:n])
+                else:
+                    dst.add_(self.rs_tmp[:n])
+                if part is not None:
+                    part.zero_()
+                    part[0] = dst.pow(2).sum()
 
     def _on_comm(self, fn, *a):
         ev = torch.cuda.Event()
@@ -333,10 +417,25 @@ class Zero3Trainer:
         self._prefetch_layer(i + 1)
 
     def post_head_bwd(self):
-        if self._last:
+        if self.grad_wire == "bf16":
+            # the head buffer is reused next micro-batch, after post_backward has
+            # waited for every side-stream collective of this one
+            self._on_comm(self._reduce_scatter_bf16, "head", self.L.names.index("head"), self.ghead, 0)
+        elif self._last:
             self._on_comm(self._reduce_scatter, "head", self.L.names.index("head"))
 
+    def _bind_grad_slot(self, i):
+        k = i % self.n_gslots
+        ev = self.slot_free[k]
+        if ev is not None:  # every rank has finished reading the slot's previous layer
+            with ph("wait.reduce_scatter"):
+                torch.cuda.current_stream().wait_event(ev)
+            self.slot_free[k] = None
+        self.grad_views.bind(f"layers.{i}", self.gslots[k])
+
     def pre_layer_bwd(self, i):
+        if self.grad_wire == "bf16":
+            self._bind_grad_slot(i)
         if self.fuse_gather:
             self.params.override = {}
             if self.slot_layer[i % len(self.slots)] == i:
@@ -350,13 +449,19 @@ class Zero3Trainer:
         self._prefetch_layer(i - 1)
 
     def post_layer_bwd(self, i):
-        if self._last:
-            g = f"layers.{i}"
+        g = f"layers.{i}"
+        if self.grad_wire == "bf16":
+            k = i % self.n_gslots
+            self.slot_free[k] = self._on_comm(self._reduce_scatter_bf16, g, self.L.names.index(g), self.gslots[k],
+                                              k * self.gslot_len)
+        elif self._last:
             self._on_comm(self._reduce_scatter, g, self.L.names.index(g))
 
     def post_backward(self):
         if self._last:
             self._on_comm(self._reduce_scatter, "embed", self.L.names.index("embed"))
+        if self.grad_wire == "bf16":
+            self.slot_free = [None] * self.n_gslots  # the wait below covers them
         ev = torch.cuda.Event()
         ev.record(self.comm_stream)
         with ph("wait.reduce_scatter"):
@@ -382,6 +487,7 @@ class Zero3Trainer:
 
     def micro_step_async(self, ids: torch.Tensor, targets: torch.Tensor) -> None:
         first = self._micro % self.accum_steps == 0
+        self._first = first
         self._last = (self._micro + 1) % self.accum_steps == 0
         self.engine.forward_backward(ids, targets, loss_scale=self.opt.scaler.scale_tensor(),
                                      grad_scale=1.0 / (ids.numel() * self.accum_steps * self.world),
@@ -404,6 +510,22 @@ class Zero3Trainer:
         self.opt.set_lr(lr)
 
     # --------------------------------------------------------------- utils
+    @staticmethod
+    def grad_memory_plan(L: "ShardLayout", grad_wire: str = "bf16") -> Dict[str, int]:
+        """Bytes of gradient buffers one rank holds (no device needed)."""
+        def glen(g):
+            s, e = L.groups[g]
+            return e - s
+        if grad_wire == "fp32":
+            return {"full_fp32": 4 * L.total, "shard_fp32": 4 * L.shard_numel}
+        nl = L.cfg.num_layers
+        gmax = max(glen(f"layers.{i}") for i in range(nl))
+        return {"shard_fp32": 4 * L.shard_numel, "layer_slots_bf16": 2 * min(N_GRAD_SLOTS, nl) * gmax,
+                "head_bf16": 2 * glen("head"), "embed_fp32": 4 * glen("embed")}
+
+    def grad_memory_bytes(self) -> int:
+        return sum(self.grad_memory_plan(self.L, self.grad_wire).values())
+
     def full_params(self) -> torch.Tensor:
         """Gather the full bf16 flat parameters on every rank (checkpointing/tests)."""
         parts = [torch.empty_like(self.shard_p16) for _ in range(self.world)]

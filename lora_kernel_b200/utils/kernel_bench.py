@@ -108,7 +108,7 @@ def bench_fp8(shapes, iters):
 
 
 def bench_norm(iters):
-    from lora_kernel_b200.ops.norm import rmsnorm_fwd
+    from lora_kernel_b200.ops.norm import rmsnorm_bwd, rmsnorm_fwd
     pk = peaks()
     for (M, D) in [(8192, 2048), (16384, 4096)]:
         x = torch.randn(M, D, device="cuda").to(torch.bfloat16)
@@ -118,6 +118,16 @@ def bench_norm(iters):
         t = time_fn(lambda: rmsnorm_fwd(x, g, 1e-5, y=y, rstd=r), iters)
         by = 2 * M * D * 2
         print(json.dumps({"kernel": "rmsnorm_fwd", "M": M, "D": D, "ms": round(t, 4),
+                          "gbs": round(by / t / 1e6, 1),
+                          "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+        # backward with the residual gradient added in place (the engine's form):
+        # reads dy, x, dres, writes dx
+        dy = torch.randn_like(x)
+        dh = torch.randn_like(x)
+        dg = torch.zeros(D, device="cuda")
+        t = time_fn(lambda: rmsnorm_bwd(dy, x, g, r, dg, dres=dh, dx=dh, accumulate=True), iters)
+        by = 4 * M * D * 2
+        print(json.dumps({"kernel": "rmsnorm_bwd", "M": M, "D": D, "ms": round(t, 4),
                           "gbs": round(by / t / 1e6, 1),
                           "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
 

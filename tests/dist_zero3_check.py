@@ -22,10 +22,14 @@ def main():
                             vocab_size=512, num_layers=3, max_seq_len=256)
     tc = TrainConfig(lr=1e-3, weight_decay=0.1, dynamic_loss_scale=True, init_loss_scale=1024.0,
                      micro_batch=2, seq_len=128, seed=5)
-    fused = mode.endswith("-fused")  # K17: the group gather inside the first consuming GEMM
-    tr = Zero3Trainer(cfg, tc, device="cuda", comm=mode.split("-")[0], fuse_gather=fused)
+    parts = mode.split("-")
+    fused = "fused" in parts  # K17: the group gather inside the first consuming GEMM
+    wire = "fp32" if "fp32" in parts else "bf16"  # gradients on the wire
+    accum = 2 if "accum2" in parts else 1
+    tc.grad_accum_steps = accum
+    tr = Zero3Trainer(cfg, tc, device="cuda", comm=parts[0], fuse_gather=fused, grad_wire=wire)
     g = torch.Generator().manual_seed(0)
-    batches = [torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=g) for _ in range(3)]
+    batches = [torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=g) for _ in range(3 * accum)]
     losses = []
     for b in batches:
         mine = b[2 * rank:2 * rank + 2].cuda()

@@ -146,3 +146,18 @@ def test_vocab_parallel_pick_matches_global_argmax():
         allp[r, :, 1] = (i + r * Vl).double()
     assert pick_global(allp).tolist() == scores.argmax(1).tolist()
     assert pick_global(allp)[2].item() == 10
+
+
+@pytest.mark.parametrize("preset", ["llama-1.1b-zero3", "llama-8b-fsdp-dp8"])
+def test_zero3_gradient_memory_is_a_shard_plus_slots(preset):
+    """With bf16 gradients on the wire a rank holds its fp32 gradient shard,
+    three bf16 layer slots, the bf16 head and the fp32 embedding gradient -
+    a fraction of the full fp32 gradient buffer of the fp32 wire."""
+    from lora_kernel_b200.config import get_preset
+    from lora_kernel_b200.parallel.zero import ShardLayout, Zero3Trainer
+    cfg = get_preset(preset).model
+    L = ShardLayout(cfg, 8, 0)
+    full = sum(Zero3Trainer.grad_memory_plan(L, "fp32").values()) - 4 * L.shard_numel
+    plan = Zero3Trainer.grad_memory_plan(L, "bf16")
+    assert plan["shard_fp32"] == 4 * L.shard_numel
+    assert sum(plan.values()) < 0.35 * full, (plan, full)

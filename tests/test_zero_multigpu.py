@@ -12,7 +12,7 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _single_gpu_reference(world):
+def _single_gpu_reference(world, accum=1):
     from lora_kernel_b200.config import TrainConfig, TransformerConfig
     from lora_kernel_b200.models.params import FlatParams
     from lora_kernel_b200.parallel.zero import ShardLayout
@@ -20,7 +20,7 @@ def _single_gpu_reference(world):
     cfg = TransformerConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, ff_dim=512,
                             vocab_size=512, num_layers=3, max_seq_len=256)
     tc = TrainConfig(lr=1e-3, weight_decay=0.1, dynamic_loss_scale=True, init_loss_scale=1024.0,
-                     micro_batch=2, seq_len=128, seed=5)
+                     micro_batch=2, seq_len=128, seed=5, grad_accum_steps=accum)
     L = ShardLayout(cfg, world, 0)
     # same initial weights as the sharded run: FlatParams with the ZeRO group alignment
     model = Transformer(cfg, "cuda", seed=tc.seed)
@@ -30,7 +30,7 @@ def _single_gpu_reference(world):
         v.copy_(ref.views[n])
     pipe = TrainingPipeline(model, tc.lr, tc.weight_decay, tc.max_grad_norm, train_cfg=tc)
     g = torch.Generator().manual_seed(0)
-    batches = [torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=g) for _ in range(3)]
+    batches = [torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=g) for _ in range(3 * accum)]
     losses = [pipe.train_step(b[:, :-1], b[:, 1:]) for b in batches]
     out = {}
     for n, v in model.engine.params.views.items():
@@ -38,7 +38,7 @@ def _single_gpu_reference(world):
     return out, losses, L, ref
 
 
-@pytest.mark.parametrize("mode", ["p2p", "nccl", "p2p-fused"])
+@pytest.mark.parametrize("mode", ["p2p", "nccl", "p2p-fused", "p2p-fp32", "p2p-accum2", "nccl-accum2"])
 def test_zero3_matches_single_gpu(mode, tmp_path):
     n = torch.cuda.device_count()
     if n < 2:
@@ -53,7 +53,7 @@ def test_zero3_matches_single_gpu(mode, tmp_path):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = torch.load(out)
-    ref_params, ref_losses, L, ref = _single_gpu_reference(world)
+    ref_params, ref_losses, L, ref = _single_gpu_reference(world, 2 if "accum2" in mode else 1)
     for a, b in zip(res["losses"], ref_losses):
         assert abs(a - b) < 2e-2 * abs(b), (res["losses"], ref_losses)
     full = res["full"]
