@@ -10,11 +10,13 @@
 //   P^T  = exp(S^T * scale - LSE),  dS^T = P^T (dP^T - D) * scale   (registers)
 //   dV  += P^T dO_i,  dK += dS^T Q_i,  dQ_i = dS K_j                 (tcgen05)
 //
-// dQ_i partials are added into an fp32 accumulator with vector reductions
-// (red.global.add.v4.f32) and converted to bf16 by a final kernel.  The same
+// dQ_i partials go from TMEM through a shared-memory staging tile into the fp32
+// accumulator with bulk tensor reduce-adds (cp.reduce.async.bulk.tensor, whole
+// 128-byte lines, no multicast) and are converted to bf16 by a final kernel.  The same
 // 128B-swizzled shared-memory tiles serve as K-major operands (S^T, dP^T) and
 // as MN-major operands (dV, dK, dQ), so nothing is transposed in memory.
-// D = rowsum(dO * O) is computed by a small pre-pass.
+// D = rowsum(dO * O) is computed by a small pre-pass, which also zeroes the
+// fp32 dQ accumulator.
 //
 // Replaces the reference's MultiHeadAttention::backward
 // (src/nn/transformer_blocks.cpp:156-207) and softmax_backward_inplace
@@ -48,23 +50,26 @@ __device__ __forceinline__ uint32_t sw128_off_b(int r, int u) {
   return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
 }
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
-
+// head_dim 64: P^T lives in its own TMEM columns and is the A operand of the
+// dV MMA (no shared-memory round trip), and the skewed schedule runs S^T/dP^T of
+// iteration it+1 before the gradient MMAs of it.  head_dim 128 has no TMEM
+// left for either (dQ reuses S^T's columns): P goes through shared memory and
+// the schedule is serial.
 template <int DH>
 struct BwdCfg {
+  static constexpr bool P_TMEM = DH == 64;
   static constexpr int QB = 128 * DH * 2;
   static constexpr int STAGES = DH == 64 ? 3 : 1;
+  static constexpr int NSW = DH == 64 ? 16 : 8;  // softmax warps
+  static constexpr int NDRAIN = 8;  // warps that drain dQ (one 4 KB staging tile each)
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = QB;
   static constexpr int OFF_Q = 2 * QB;
   static constexpr int OFF_DO = OFF_Q + STAGES * QB;
-  static constexpr int OFF_P = OFF_DO + STAGES * QB;
-  static constexpr int OFF_DS = OFF_P + 32768;
-  static constexpr int OFF_LD = OFF_DS + 32768;        // [STAGES][2][128] fp32 LSE, D
+  static constexpr int OFF_DS = OFF_DO + STAGES * QB;
+  static constexpr int OFF_P = OFF_DS + 32768;                     // unused when P_TMEM
+  static constexpr int OFF_STG = OFF_P + (P_TMEM ? 0 : 32768);     // dQ staging, 1024-aligned
+  static constexpr int OFF_LD = OFF_STG + NDRAIN * 4096;           // [STAGES][2][128] fp32 LSE, D
   static constexpr int OFF_BAR = OFF_LD + STAGES * 1024;
   static constexpr int SMEM = OFF_BAR + 256;
   static constexpr int TMEM_COLS = 512;
@@ -81,25 +86,20 @@ __device__ __forceinline__ void q_range(const AttnBwdArgs& a, int j, int& i0, in
   }
 }
 
-// softmax warps: 16 for head_dim 64 (four per TMEM lane quarter, one 32-query
-// chunk each), 8 for head_dim 128
 template <int DH>
-constexpr int bwd_softmax_warps() { return DH == 64 ? 16 : 8; }
+constexpr int bwd_softmax_warps() { return BwdCfg<DH>::NSW; }
 
 template <int DH>
 __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    const AttnBwdArgs args) {
+                    const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs args) {
   using C = BwdCfg<DH>;
-  // head_dim 64: dQ has its own TMEM columns; head_dim 128 reuses S^T's.
-  constexpr bool DQ_ALIAS = DH == 128;
-  // head_dim 64 runs the skewed schedule: S^T/dP^T of iteration it+1 are issued
-  // before the dV/dK/dQ MMAs of iteration it, so the tensor cores work while
-  // the softmax warps turn S^T(it) into P/dS (needs dQ in its own columns).
-  constexpr bool SKEW = !DQ_ALIAS;
-  constexpr int NSW = bwd_softmax_warps<DH>();  // softmax warps
-  constexpr int NG = NSW / 4;                  // warps per TMEM lane quarter
-  constexpr int CPW = 4 / NG;                  // 32-query chunks per warp
+  constexpr bool P_TMEM = C::P_TMEM;
+  constexpr bool SKEW = P_TMEM;       // needs dQ in its own TMEM columns
+  constexpr bool DQ_ALIAS = !P_TMEM;  // head_dim 128: dQ reuses S^T's columns
+  constexpr int NSW = C::NSW;
+  constexpr int NG = NSW / 4;   // warps per TMEM lane quarter
+  constexpr int CPW = 4 / NG;   // 32-query chunks per warp
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023) {
@@ -130,9 +130,9 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(qd_full + 8 * s, 1);
-      mbar_init(qd_empty + 8 * s, 1);
+    for (int s2 = 0; s2 < C::STAGES; ++s2) {
+      mbar_init(qd_full + 8 * s2, 1);
+      mbar_init(qd_empty + 8 * s2, 1);
     }
     mbar_init(pds_free, 1);
     mbar_init(sdp_full, 1);
@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + DH;
   const uint32_t tdQ = DQ_ALIAS ? tS : tmem + 256 + 2 * DH;
+  const uint32_t tP = tmem + 256 + 3 * DH;  // P^T, bf16 pairs (head_dim 64 only)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -206,70 +208,8 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
       const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
       const uint32_t sp = sbase + C::OFF_P, sds = sbase + C::OFF_DS;
       bool ok = bounded_wait(kv_full, 0, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
-      if constexpr (SKEW) {
-        // gradient MMAs of iteration m: dV += P^T dO, dK += dS^T Q, dQ = dS K
-        auto grad = [&](int m) -> bool {
-          const int stm = m % C::STAGES;
-          if (!bounded_wait(ds_ready, m & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
-              (m > 0 && !bounded_wait(dq_free, (m - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)))
-            return false;
-          tc_fence_after();
-          const uint32_t sq = sbase + C::OFF_Q + stm * C::QB, sdo = sbase + C::OFF_DO + stm * C::QB;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            tc_mma_f16(tdV, make_desc_sw128(sp + aoff, 16, 1024), make_desc_sw128(sdo + kk * 2048, 16384, 1024),
-                       id_kv, (m > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_f16(tdK, make_desc_sw128(sds + aoff, 16, 1024), make_desc_sw128(sq + kk * 2048, 16384, 1024),
-                       id_kv, (m > 0 || kk > 0) ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc_mma_f16(tdQ, make_desc_sw128(sds + kk * 2048, 16384, 1024),
-                       make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
-          tc_commit(dq_full);
-          tc_commit(qd_empty + 8 * stm);
-          tc_commit(pds_free);
-          return true;
-        };
-        for (int it = 0; it < n_it && ok; ++it) {
-          const int st = it % C::STAGES;
-          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
-          if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
-              (it > 0 && !bounded_wait(sdp_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sq = sbase + C::OFF_Q + st * C::QB, sdo = sbase + C::OFF_DO + st * C::QB;
-#pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            tc_mma_f16(tS, make_desc_sw128(sk + off, 16, 1024), make_desc_sw128(sq + off, 16, 1024), id_s,
-                       kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            tc_mma_f16(tdP, make_desc_sw128(sv + off, 16, 1024), make_desc_sw128(sdo + off, 16, 1024), id_s,
-                       kk > 0 ? 1u : 0u);
-          }
-          tc_commit(sdp_full);
-          if (it > 0 && !grad(it - 1)) ok = false;
-        }
-        if (ok && n_it > 0) grad(n_it - 1);
-      }
-      for (int it = 0; it < n_it && ok && !SKEW; ++it) {
+      auto issue_sdp = [&](int it) {
         const int st = it % C::STAGES;
-        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
-        const uint32_t prev = (uint32_t)(it - 1) & 1;
-        if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
-            (it > 0 && !bounded_wait(sdp_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) ||
-            (DQ_ALIAS && it > 0 && !bounded_wait(dq_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const uint32_t sq = sbase + C::OFF_Q + st * C::QB, sdo = sbase + C::OFF_DO + st * C::QB;
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk) {
@@ -284,35 +224,70 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
                      kk > 0 ? 1u : 0u);
         }
         tc_commit(sdp_full);
-        if (!bounded_wait(ds_ready, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
-            (!DQ_ALIAS && it > 0 && !bounded_wait(dq_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+      };
+      // gradient MMAs of iteration m: dV += P^T dO, dK += dS^T Q, dQ = dS K
+      auto issue_grad = [&](int m) {
+        const int stm = m % C::STAGES;
+        const uint32_t sq = sbase + C::OFF_Q + stm * C::QB, sdo = sbase + C::OFF_DO + stm * C::QB;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 queries
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          if constexpr (P_TMEM)
+            tc_mma_f16_ta(tdV, tP + kk * 8, make_desc_sw128(sdo + kk * 2048, 16384, 1024), id_kv,
+                          (m > 0 || kk > 0) ? 1u : 0u);
+          else
+            tc_mma_f16(tdV, make_desc_sw128(sp + aoff, 16, 1024), make_desc_sw128(sdo + kk * 2048, 16384, 1024),
+                       id_kv, (m > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16(tdK, make_desc_sw128(sds + aoff, 16, 1024), make_desc_sw128(sq + kk * 2048, 16384, 1024),
+                     id_kv, (m > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // contraction over the 128 keys
+          tc_mma_f16(tdQ, make_desc_sw128(sds + kk * 2048, 16384, 1024),
+                     make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(qd_empty + 8 * stm);
+        tc_commit(pds_free);
+      };
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % C::STAGES;
+        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1;
+        const uint32_t prev = (uint32_t)(it - 1) & 1;
+        if (!bounded_wait(qd_full + 8 * st, ph, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) ||
+            (it > 0 && !bounded_wait(sdp_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) ||
+            (DQ_ALIAS && it > 0 && !bounded_wait(dq_free, prev, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 queries
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          tc_mma_f16(tdV, make_desc_sw128(sp + aoff, 16, 1024), make_desc_sw128(sdo + kk * 2048, 16384, 1024),
-                     id_kv, (it > 0 || kk > 0) ? 1u : 0u);
-          tc_mma_f16(tdK, make_desc_sw128(sds + aoff, 16, 1024), make_desc_sw128(sq + kk * 2048, 16384, 1024),
-                     id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+        issue_sdp(it);
+        // skewed: the gradient MMAs of it-1 follow S^T/dP^T of it; serial: those of it
+        const int m = SKEW ? it - 1 : it;
+        if (m >= 0) {
+          if (!bounded_wait(ds_ready, m & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
+              (!DQ_ALIAS && m > 0 && !bounded_wait(dq_free, (m - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_grad(m);
         }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // contraction over the 128 keys
-          tc_mma_f16(tdQ, make_desc_sw128(sds + kk * 2048, 16384, 1024),
-                     make_desc_sw128(sk + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
+      }
+      if (SKEW && ok && n_it > 0) {
+        const int m = n_it - 1;
+        if (bounded_wait(ds_ready, m & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) &&
+            (m == 0 || bounded_wait(dq_free, (m - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))) {
+          tc_fence_after();
+          issue_grad(m);
         }
-        tc_commit(dq_full);
-        tc_commit(qd_empty + 8 * st);
       }
       tc_commit(drain);
       bounded_wait(drain, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
   } else {
     // ------------------------------------------------- softmax backward
-    // 8 warps: warp w owns TMEM lanes 32*(w%4)..+31 (key rows for S^T/dP^T/dK/dV,
-    // query rows for dQ) and half wg = (w-2)/4 of the columns.
+    // warp w owns TMEM lanes 32*(w%4)..+31 (key rows of S^T/dP^T/dK/dV, query
+    // rows of dQ) and query chunks wg*CPW .. +CPW-1 (32 queries each).
     const int quarter = warp & 3;
     const int wg = (warp - 2) >> 2;
     const int kr = quarter * 32 + lane;
@@ -320,66 +295,76 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* sP = smem + C::OFF_P;
     uint8_t* sDS = smem + C::OFF_DS;
-    const int ldq = args.Hq * DH;
-    bool ok = true;
-    if constexpr (SKEW) {
-      // P/dS of iteration it are built in registers while the tensor cores run
-      // the gradient MMAs of it-1; dQ(it-1) is drained and P/dS(it) stored once
-      // those MMAs have finished with the shared P/dS tile.
-      auto drain_dq = [&](int m) {
-        const int hm = g * group + m / nq;
-        const int im = i0 + m % nq;
-        const int q = im * 128 + kr;
-        float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + hm * DH;
+    // dQ staging: 32 rows x 32 fp32 columns (128B-swizzled) per draining warp
+    // draining warps are those with wg < 2 (head_dim 64: chunks 0, 1; head_dim
+    // 128: every warp, chunks wg and wg + 2): one tile per (quarter, wg)
+    static_assert(C::NDRAIN == 8, "one staging tile per draining warp");
+    const int drain_slot = (quarter * 2 + wg) & 7;
+    const uint32_t stg = sbase + C::OFF_STG + drain_slot * 4096;
+    uint8_t* stg_p = smem + C::OFF_STG + drain_slot * 4096;
+    // dQ(m) from TMEM into the staging tile, then one bulk reduce-add into the
+    // fp32 accumulator per 32 x 32 block
+    auto drain_dq = [&](int m) {
+      const int hm = g * group + m / nq;
+      const int im = i0 + m % nq;
 #pragma unroll 1
-        for (int c = wg; c < DH / 32; c += NG) {
-          uint32_t v[32];
-          tmem_ld32(tdQ + lane_off + c * 32, v);
-          tc_wait_ld();
-          if (q < S) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              red_add_v4(dqrow + c * 32 + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                         __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_free);
-      };
-      for (int it = 0; it < n_it; ++it) {
-        const int h = g * group + it / nq;
-        const int i = i0 + it % nq;
-        bool w_ok = bounded_wait(sdp_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
-        if (!__all_sync(0xffffffffu, w_ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t sv[CPW][32], dv[CPW][32];
-#pragma unroll
-        for (int c = 0; c < CPW; ++c) {
-          tmem_ld32(tS + lane_off + (wg * CPW + c) * 32, sv[c]);
-          tmem_ld32(tdP + lane_off + (wg * CPW + c) * 32, dv[c]);
-        }
+      for (int c = wg; c < DH / 32; c += NG) {
+        uint32_t v[32];
+        tmem_ld32(tdQ + lane_off + c * 32, v);
         tc_wait_ld();
-        tc_fence_before();
+        if (lane == 0) bulk_wait_read<0>();  // the previous reduce has read the staging tile
         __syncwarp();
-        if (lane == 0) mbar_arrive(sdp_free);  // S^T / dP^T may be overwritten now
-        const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
-        const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
-        const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
-                               args.window > 0;
-        const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
-        const int st = it % C::STAGES;
-        const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
-        uint32_t pp[CPW][16], pd[CPW][16];
 #pragma unroll
-        for (int c = 0; c < CPW; ++c) {
-          const int cc = wg * CPW + c;
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_dq, stg, hm * DH + c * 32, row0 + im * 128 + quarter * 32);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    };
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = g * group + it / nq;
+      const int i = i0 + it % nq;
+      bool w_ok = bounded_wait(sdp_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
+      const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
+      const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
+                             args.window > 0;
+      const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
+      const int st = it % C::STAGES;
+      const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
+      // P / dS of this warp's queries as bf16 pairs, built 16 queries at a time
+      uint32_t pp[CPW][16], pd[CPW][16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const int qi = cc * 32 + e;
+      for (int c = 0; c < CPW; ++c) {
+        const int cc = wg * CPW + c;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t sv[16], dv[16];
+          tmem_ld16(tS + lane_off + cc * 32 + hf * 16, sv);
+          tmem_ld16(tdP + lane_off + cc * 32 + hf * 16, dv);
+          tc_wait_ld();
+          if (c == CPW - 1 && hf == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sdp_free);  // S^T / dP^T may be overwritten now
+          }
+#pragma unroll
+          for (int e = 0; e < 16; e += 4) {
+            const int qi = cc * 32 + hf * 16 + e;
             float Ls[4], Ds[4];
             if (bulk_ld) {
               const float4 L = *reinterpret_cast<const float4*>(sL + qi);
@@ -403,157 +388,82 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
               const int q = i * 128 + qi + t;
-              p[t] = fast_exp2(fmaf(__uint_as_float(sv[c][e + t]), args.sl2, -Ls[t]));
+              p[t] = fast_exp2(fmaf(__uint_as_float(sv[e + t]), args.sl2, -Ls[t]));
               if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
                                 (args.window > 0 && key <= q - args.window)))
                 p[t] = 0.f;
-              ds[t] = p[t] * fmaf(__uint_as_float(dv[c][e + t]), args.scale, -Ds[t]);
+              ds[t] = p[t] * fmaf(__uint_as_float(dv[e + t]), args.scale, -Ds[t]);
             }
-            pp[c][e / 2] = pack_bf16x2(p[0], p[1]);
-            pp[c][e / 2 + 1] = pack_bf16x2(p[2], p[3]);
-            pd[c][e / 2] = pack_bf16x2(ds[0], ds[1]);
-            pd[c][e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+            pp[c][hf * 8 + e / 2] = pack_bf16x2(p[0], p[1]);
+            pp[c][hf * 8 + e / 2 + 1] = pack_bf16x2(p[2], p[3]);
+            pd[c][hf * 8 + e / 2] = pack_bf16x2(ds[0], ds[1]);
+            pd[c][hf * 8 + e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
           }
         }
-        if (it > 0) {
-          // the gradient MMAs of it-1 are done: the P/dS tile is free and dQ(it-1) is ready
-          w_ok = bounded_wait(dq_full, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) &&
-                 bounded_wait(pds_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
-          if (!__all_sync(0xffffffffu, w_ok)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          drain_dq(it - 1);
-        }
-#pragma unroll
-        for (int c = 0; c < CPW; ++c) {
-          const int cc = wg * CPW + c;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t off = sw128_off_b(kr, cc * 4 + u);
-            *reinterpret_cast<uint4*>(sP + off) =
-                make_uint4(pp[c][4 * u], pp[c][4 * u + 1], pp[c][4 * u + 2], pp[c][4 * u + 3]);
-            *reinterpret_cast<uint4*>(sDS + off) =
-                make_uint4(pd[c][4 * u], pd[c][4 * u + 1], pd[c][4 * u + 2], pd[c][4 * u + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ds_ready);
       }
-      if (ok && n_it > 0) {
-        const bool w_ok = bounded_wait(dq_full, (n_it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
-        if (__all_sync(0xffffffffu, w_ok)) {
-          tc_fence_after();
-          drain_dq(n_it - 1);
-        } else {
+      if (SKEW && it > 0) {
+        // the gradient MMAs of it-1 are done: P^T / dS are free and dQ(it-1) is ready
+        w_ok = bounded_wait(dq_full, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) &&
+               bounded_wait(pds_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
           ok = false;
+          break;
         }
+        tc_fence_after();
+        drain_dq(it - 1);
       }
-    } else
-    for (int it = 0; it < n_it; ++it) {
-      const int h = g * group + it / nq;
-      const int i = i0 + it % nq;
-      bool w_ok = bounded_wait(sdp_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
-      if (!__all_sync(0xffffffffu, w_ok)) {
-        ok = false;
-        break;
+      if (!SKEW && it > 0) {
+        // serial schedule: the previous gradient MMAs finished before dQ(it-1) was drained
+        w_ok = bounded_wait(pds_free, (it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
-      tc_fence_after();
-      uint32_t sv[2][32], dv[2][32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        tmem_ld32(tS + lane_off + (wg * 2 + c) * 32, sv[c]);
-        tmem_ld32(tdP + lane_off + (wg * 2 + c) * 32, dv[c]);
-      }
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sdp_free);  // S^T / dP^T may be overwritten now
-      const float* lse_row = args.lse + ((int64_t)b * args.Hq + h) * S + i * 128;
-      const float* d_row = args.Dvec + ((int64_t)b * args.Hq + h) * S + i * 128;
-      const bool need_mask = (args.causal && i == j) || (i + 1) * 128 > S || (j + 1) * 128 > S ||
-                             args.window > 0;
-      const bool vec_ok = (i * 128 + 127 < S) && (S & 3) == 0;
-      const int st = it % C::STAGES;
-      const float* sL = reinterpret_cast<const float*>(smem + C::OFF_LD + st * 1024);
+      for (int c = 0; c < CPW; ++c) {
+        const int cc = wg * CPW + c;
+        if constexpr (P_TMEM) {
+          tmem_st16(tP + lane_off + cc * 16, pp[c]);
+        } else {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int cc = wg * 2 + c;  // 32-query chunk index within the tile
-        uint32_t pp[16], pd[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const int qi = cc * 32 + e;
-          float Ls[4], Ds[4];
-          if (bulk_ld) {
-            const float4 L = *reinterpret_cast<const float4*>(sL + qi);
-            const float4 Dd = *reinterpret_cast<const float4*>(sL + 128 + qi);
-            Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
-            Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
-          } else if (vec_ok) {
-            const float4 L = *reinterpret_cast<const float4*>(lse_row + qi);
-            const float4 Dd = *reinterpret_cast<const float4*>(d_row + qi);
-            Ls[0] = L.x; Ls[1] = L.y; Ls[2] = L.z; Ls[3] = L.w;
-            Ds[0] = Dd.x; Ds[1] = Dd.y; Ds[2] = Dd.z; Ds[3] = Dd.w;
-          } else {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const bool in = i * 128 + qi + t < S;
-              Ls[t] = in ? lse_row[qi + t] : 0.f;
-              Ds[t] = in ? d_row[qi + t] : 0.f;
-            }
-          }
-          float p[4], ds[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int q = i * 128 + qi + t;
-            p[t] = fast_exp2(fmaf(__uint_as_float(sv[c][e + t]), args.sl2, -Ls[t]));
-            if (need_mask && (q >= S || key >= S || (args.causal && key > q) ||
-                              (args.window > 0 && key <= q - args.window)))
-              p[t] = 0.f;
-            ds[t] = p[t] * fmaf(__uint_as_float(dv[c][e + t]), args.scale, -Ds[t]);
-          }
-          pp[e / 2] = pack_bf16x2(p[0], p[1]);
-          pp[e / 2 + 1] = pack_bf16x2(p[2], p[3]);
-          pd[e / 2] = pack_bf16x2(ds[0], ds[1]);
-          pd[e / 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(sP + sw128_off_b(kr, cc * 4 + u)) =
+                make_uint4(pp[c][4 * u], pp[c][4 * u + 1], pp[c][4 * u + 2], pp[c][4 * u + 3]);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t off = sw128_off_b(kr, cc * 4 + u);
-          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-          *reinterpret_cast<uint4*>(sDS + off) = make_uint4(pd[4 * u], pd[4 * u + 1], pd[4 * u + 2], pd[4 * u + 3]);
-        }
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(sDS + sw128_off_b(kr, cc * 4 + u)) =
+              make_uint4(pd[c][4 * u], pd[c][4 * u + 1], pd[c][4 * u + 2], pd[c][4 * u + 3]);
       }
+      if constexpr (P_TMEM) tc_wait_st();
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      // dQ tile (lane = query row), this warp group's half of the columns
-      w_ok = bounded_wait(dq_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
-      if (!__all_sync(0xffffffffu, w_ok)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int q = i * 128 + kr;
-      float* dqrow = args.dq_acc + (int64_t)(row0 + q) * ldq + h * DH;
-#pragma unroll 1
-      for (int c = wg * (DH / 64); c < (wg + 1) * (DH / 64); ++c) {
-        uint32_t v[32];
-        tmem_ld32(tdQ + lane_off + c * 32, v);
-        tc_wait_ld();
-        if (q < S) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            red_add_v4(dqrow + c * 32 + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                       __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+      if (!SKEW) {
+        w_ok = bounded_wait(dq_full, it & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        drain_dq(it);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
     }
+    if (SKEW && ok && n_it > 0) {
+      const bool w_ok = bounded_wait(dq_full, (n_it - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      if (__all_sync(0xffffffffu, w_ok)) {
+        tc_fence_after();
+        drain_dq(n_it - 1);
+      } else {
+        ok = false;
+      }
+    }
+    // every bulk reduce of this warp has finished (its staging tile may go away)
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
     // dK, dV (lane = key row) -> bf16 into dqkv.  tcgen05.ld is warp-collective:
     // every lane loads, only in-range keys store.
     if (__all_sync(0xffffffffu, ok) && n_it > 0) {
@@ -607,7 +517,8 @@ template <int DH>
 __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                     const __nv_bfloat16* __restrict__ dout, int64_t lddo,
                                     float* __restrict__ Dvec, const float* __restrict__ lse,
-                                    float* __restrict__ l2, float scale, int B, int S, int Hq) {
+                                    float* __restrict__ l2, float scale, int B, int S, int Hq,
+                                    float* __restrict__ dq_acc) {
   const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)B * S * Hq;
@@ -622,6 +533,9 @@ __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t
     const float2 c = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dp + d));
     s += a.x * c.x + a.y * c.y;
   }
+  // zero this (row, head)'s fp32 dQ accumulator (the main kernel reduce-adds into it)
+  float* dqr = dq_acc + row * (int64_t)Hq * DH + h * DH;
+  for (int d = lane * 4; d < DH; d += 128) *reinterpret_cast<float4*>(dqr + d) = make_float4(0.f, 0.f, 0.f, 0.f);
   s = warp_sum(s);
   if (lane == 0) {
     const int bb = (int)(row / S), q = (int)(row % S);
@@ -656,14 +570,16 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
     const int64_t warps = T * d.Hq;
     attn_bwd_dot_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
         (const __nv_bfloat16*)d.o, d.ld_o, (const __nv_bfloat16*)d.dout, d.ld_do, d.dvec, d.lse, l2, d.scale,
-        d.B, d.S, d.Hq);
+        d.B, d.S, d.Hq, d.dq_acc);
     if (check_launch("attn_bwd_dot")) return -1;
   }
-  if (cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * T * d.Hq * DH, s) != cudaSuccess)
-    return fail("attention_bwd: memset failed");
-  CUtensorMap tq, tdo;
+  CUtensorMap tq, tdo, tdq;
   if (!make_tmap_2d(&tq, d.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, ncols, d.ld_qkv, 128, 64)) return -1;
   if (!make_tmap_2d(&tdo, d.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (int64_t)d.Hq * DH, d.ld_do, 128, 64))
+    return -1;
+  // fp32 dQ accumulator [T, Hq*Dh]: 32 x 32 boxes (128-byte rows) for the bulk reduce-adds
+  if (!make_tmap_2d(&tdq, d.dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, T, (int64_t)d.Hq * DH, (int64_t)d.Hq * DH,
+                    32, 32))
     return -1;
   AttnBwdArgs a{};
   a.B = d.B;
@@ -683,7 +599,7 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   a.n_tiles = cdiv(d.S, 128);
   auto k = attn_bwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  k<<<a.n_tiles * d.Hkv * d.B, 64 + 32 * bwd_softmax_warps<DH>(), C::SMEM, s>>>(tq, tdo, a);
+  k<<<a.n_tiles * d.Hkv * d.B, 64 + 32 * bwd_softmax_warps<DH>(), C::SMEM, s>>>(tq, tdo, tdq, a);
   if (check_launch("attn_bwd")) return -1;
   const int64_t n4 = T * d.Hq * DH / 4;
   int grid_c = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms() * 16);

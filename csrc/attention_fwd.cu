@@ -5,18 +5,19 @@
 // value head g at (Hq+Hkv+g)*Dh; q head h reads kv head h / (Hq/Hkv).
 // Output O [B*S, Hq*Dh] bf16 and the natural-log LSE [B, Hq, S] fp32.
 //
-// One CTA per (128-query tile, q head, batch), 6 warps:
-//   warp 0      TMA: Q once, then K_j / V_j into 2-stage rings (no multicast);
-//   warp 1      one thread issues S = Q K_j^T (M=128, N=128) into TMEM and,
-//               once P_j is in shared memory, O_j = P_j V_j (N = Dh) into a
-//               second TMEM region;
-//   warps 2..5  softmax: thread t of warp w owns query row 32*(w%4)+t, i.e.
-//               TMEM lane; reads its S row, keeps the running max / sum in
-//               registers, writes P (bf16, 128B-swizzled K-major) to shared
-//               memory and accumulates O_j into a register accumulator with
-//               the deferred rescale (acc = acc*alpha + O_j).
-// The S of tile j+1 is computed while the softmax warps consume tile j.
-//
+// One CTA per (pair of 128-query tiles a/b, q head, batch), 10 warps:
+//   warp 0      TMA: both Q tiles once, then K_j / V_j into 2-3 stage rings
+//               shared by the two tiles (no multicast);
+//   warp 1      one thread issues S_t = Q_t K_j^T (M=128, N=128) into TMEM and,
+//               once P_t is back in TMEM, O_t += P_t V_j with P_t as the
+//               tensor-memory A operand; order PV_a(j), S_a(j+1), PV_b(j),
+//               S_b(j+1), so the tensor cores serve one softmax group while the
+//               other works (ping-pong);
+//   warps 2..9  two softmax groups of 4 warps (tile a, tile b): thread = query
+//               row = TMEM lane; it reads its 128 scores, keeps the running
+//               max / sum in registers, writes P as bf16 pairs over the first 64
+//               columns of its S and rescales its O row in TMEM only when the
+//               max grew by more than 2^8.
 // Replaces the reference's CPU attention: MultiHeadAttention::forward
 // (src/nn/transformer_blocks.cpp:50-97), FlashAttentionV2::forward
 // (include/nn/flash_attention.hpp:10-96, whose running-sum bug at :86 is not
@@ -39,33 +40,28 @@ struct AttnFwdArgs {
   int64_t ldo;
   float* lse;      // [B, Hq, S]
   int* status;
-  int n_qtiles;
+  int n_qtiles;  // CTAs per (head, batch): pairs of 128-query tiles
 };
-
-// 16-byte unit `u` (0..15, 8 bf16 each) of row `r` in a K-major 128B-swizzled
-// [128 rows x 128 cols] bf16 tile stored as two [128 x 64] chunks.
-__device__ __forceinline__ uint32_t sw128_off(int r, int u) {
-  return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
-}
 
 template <int DH>
 struct FwdCfg {
   static constexpr int QB = 128 * DH * 2;  // bytes of a [128 x DH] bf16 tile
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = QB;
-  static constexpr int OFF_V = 3 * QB;
-  static constexpr int OFF_P = 5 * QB;
-  static constexpr int OFF_BAR = OFF_P + 32768;
+  static constexpr int NS = DH == 64 ? 3 : 2;  // K / V stages
+  static constexpr int OFF_Q = 0;              // two query tiles
+  static constexpr int OFF_K = 2 * QB;
+  static constexpr int OFF_V = OFF_K + NS * QB;
+  static constexpr int OFF_BAR = OFF_V + NS * QB;
   static constexpr int SMEM = OFF_BAR + 256;
-  static constexpr int TMEM_COLS = 256;  // S: [0,128), O_j: [128, 128+DH)
-  static constexpr int MIN_BLOCKS = DH == 64 ? 2 : 1;
+  static constexpr int TMEM_COLS = 512;  // S_a, S_b (P in their first 64 columns), O_a, O_b
+  static constexpr int THREADS = 320;    // TMA warp, MMA warp, two groups of 4 softmax warps
 };
 
 template <int DH>
-__global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
+__global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_kv,
                     const AttnFwdArgs args) {
   using C = FwdCfg<DH>;
+  constexpr int NS = C::NS;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023) {  // 128B-swizzled tiles need 1024-byte alignment
@@ -73,38 +69,51 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
     return;
   }
   const uint32_t bar = sbase + C::OFF_BAR;
-  const uint32_t q_full = bar, k_full = bar + 8, k_empty = bar + 24, v_full = bar + 40,
-                 v_empty = bar + 56, s_full = bar + 72, s_free = bar + 80, p_full = bar + 88,
-                 o_full = bar + 96, drain = bar + 112;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 132);
+  // [0] q_full, [1..3] k_full, [4..6] k_empty, [7..9] v_full, [10..12] v_empty,
+  // [13,14] s_full[t], [15,16] p_full[t], [17,18] o_done[t], [19] drain
+  const uint32_t q_full = bar, k_full = bar + 8, k_empty = bar + 32, v_full = bar + 56, v_empty = bar + 80,
+                 s_full = bar + 104, p_full = bar + 120, o_done = bar + 136, drain = bar + 152;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 196);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-D grid, heaviest causal q tiles first across all (head, batch) pairs
+  // 1-D grid, heaviest causal query pairs first across all (head, batch) pairs
   const int hb = args.Hq * args.B;
-  const int qt = args.n_qtiles - 1 - (int)(blockIdx.x / hb);
+  const int qp = args.n_qtiles - 1 - (int)(blockIdx.x / hb);  // n_qtiles counts 256-query pairs here
   const int h = (int)(blockIdx.x % hb) % args.Hq, b = (int)(blockIdx.x % hb) / args.Hq;
   const int kvh = h / (args.Hq / args.Hkv);
   const int S = args.S, Skv = args.Skv, q_off = args.q_off;
   const int nkv_all = (Skv + 127) / 128;
-  const int qpos_max = q_off + qt * 128 + 127;  // largest query position in the tile
-  int j_end = args.causal ? min(qpos_max / 128 + 1, nkv_all) : nkv_all;
-  int j_begin = 0;
-  if (args.window > 0) j_begin = max(0, (q_off + qt * 128 - args.window + 1) / 128);
-  const int nkv = j_end - j_begin;
+  // key-tile range [jb[t], je[t]) of query tile t (qt = 2 qp + t); empty past the sequence
+  auto key_range = [&](int qt, int& lo, int& hi) {
+    lo = hi = 0;
+    if (qt * 128 >= S) return;
+    const int qpos_max = q_off + qt * 128 + 127;
+    hi = args.causal ? min(qpos_max / 128 + 1, nkv_all) : nkv_all;
+    lo = args.window > 0 ? max(0, (q_off + qt * 128 - args.window + 1) / 128) : 0;
+    if (hi < lo) hi = lo;
+  };
+  int jb0, je0, jb1, je1;
+  key_range(2 * qp, jb0, je0);
+  key_range(2 * qp + 1, jb1, je1);
+  const int j_lo = je0 > jb0 ? jb0 : jb1;
+  const int j_hi = max(je0, je1);
+  const int nkv = max(0, j_hi - j_lo);  // key tiles loaded (union of both ranges)
+  auto active = [&](int t, int j) { return t == 0 ? (j >= jb0 && j < je0) : (j >= jb1 && j < je1); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full + 8 * s, 1);
-      mbar_init(k_empty + 8 * s, 1);
-      mbar_init(v_full + 8 * s, 1);
-      mbar_init(v_empty + 8 * s, 1);
+    for (int s2 = 0; s2 < NS; ++s2) {
+      mbar_init(k_full + 8 * s2, 1);
+      mbar_init(k_empty + 8 * s2, 1);
+      mbar_init(v_full + 8 * s2, 1);
+      mbar_init(v_empty + 8 * s2, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + 8 * t, 1);
+      mbar_init(p_full + 8 * t, 4);
+      mbar_init(o_done + 8 * t, 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -116,24 +125,25 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
   const int row0 = b * S;      // query rows
   const int krow0 = b * Skv;   // key / value rows
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA
-      uint32_t pending = 0, parbits = 0;  // bit0..1: K stages, bit2..3: V stages
-      mbar_expect_tx(q_full, C::QB);
+      uint32_t pending = 0, parbits = 0;  // bits 0..NS-1: K stages, NS..2NS-1: V stages
+      mbar_expect_tx(q_full, 2 * C::QB);
 #pragma unroll
-      for (int c = 0; c < DH / 64; ++c)
-        tma_load_2d(sbase + C::OFF_Q + c * 16384, &tm_qkv, q_full, h * DH + c * 64,
-                    row0 + qt * 128);
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < DH / 64; ++c)
+          tma_load_2d(sbase + C::OFF_Q + t * C::QB + c * 16384, &tm_qkv, q_full, h * DH + c * 64,
+                      row0 + (2 * qp + t) * 128);
       bool ok = true;
-      for (int jj = 0; jj < nkv && ok; ++jj) {
-        const int j = j_begin + jj;
-        const int st = jj & 1;
-        const uint32_t ph = (jj >> 1) & 1;
+      for (int u = 0; u < nkv && ok; ++u) {
+        const int j = j_lo + u;
+        const int st = u % NS;
+        const uint32_t ph = (uint32_t)(u / NS) & 1;
         if (!bounded_wait(k_empty + 8 * st, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
           ok = false;
           break;
@@ -154,169 +164,218 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
         for (int c = 0; c < DH / 64; ++c)
           tma_load_2d(sbase + C::OFF_V + st * C::QB + c * 16384, &tm_kv, v_full + 8 * st,
                       args.vcol0 + kvh * DH + c * 64, krow0 + j * 128);
-        pending |= 4u << st;
-        parbits = (parbits & ~(4u << st)) | (ph << (st + 2));
+        pending |= 1u << (NS + st);
+        parbits = (parbits & ~(1u << (NS + st))) | (ph << (NS + st));
       }
       if (!ok) {
         bounded_wait(q_full, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NS; ++i) {
           if (pending & (1u << i))
             bounded_wait(k_full + 8 * i, (parbits >> i) & 1, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
-          if (pending & (4u << i))
-            bounded_wait(v_full + 8 * i, (parbits >> (i + 2)) & 1, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+          if (pending & (1u << (NS + i)))
+            bounded_wait(v_full + 8 * i, (parbits >> (NS + i)) & 1, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA
+      // Ping-pong: PV_a(j), S_a(j+1), PV_b(j), S_b(j+1): while one softmax group
+      // works on its tile the tensor cores serve the other.  MMAs of one thread
+      // run in issue order, so S_t(j+1) overwriting P_t(j) in TMEM follows PV_t(j).
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(128, DH, false, true);
-      const uint32_t sq = sbase + C::OFF_Q, sp = sbase + C::OFF_P;
       bool ok = bounded_wait(q_full, 0, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
-      auto issue_s = [&](int jj) -> bool {
-        const int st = jj & 1;
-        if (!bounded_wait(k_full + 8 * st, (jj >> 1) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag))
-          return false;
-        if (jj > 0 && !bounded_wait(s_free, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag))
-          return false;
-        tc_fence_after();
-        const uint32_t sk = sbase + C::OFF_K + st * C::QB;
+      int n_pv0 = 0, n_pv1 = 0;  // PV MMAs issued per tile (= their p_full phase counters)
+      auto issue_s = [&](int t, int u) {
+        const int st = u % NS;
+        const uint32_t sq = sbase + C::OFF_Q + t * C::QB, sk = sbase + C::OFF_K + st * C::QB;
+        const uint32_t tS = tmem + 128 * t;
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          tc_mma_f16(tS, make_desc_sw128(sq + off, 16, 1024), make_desc_sw128(sk + off, 16, 1024),
-                     idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tS, make_desc_sw128(sq + off, 16, 1024), make_desc_sw128(sk + off, 16, 1024), idesc_s,
+                     kk > 0 ? 1u : 0u);
         }
-        tc_commit(s_full);
-        tc_commit(k_empty + 8 * st);
+        tc_commit(s_full + 8 * t);
+      };
+      auto issue_pv = [&](int t, int u) -> bool {
+        int& npv = t == 0 ? n_pv0 : n_pv1;
+        if (!bounded_wait(p_full + 8 * t, npv & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag)) return false;
+        tc_fence_after();
+        const int st = u % NS;
+        const uint32_t sv = sbase + C::OFF_V + st * C::QB;
+        const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + DH * t;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P (bf16 pairs) from TMEM
+          tc_mma_f16_ta(tO, tS + kk * 8, make_desc_sw128(sv + kk * 2048, 16384, 1024), idesc_o,
+                        (npv > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(o_done + 8 * t);
+        ++npv;
         return true;
       };
-      if (ok && nkv > 0) ok = issue_s(0);
-      for (int jj = 0; jj < nkv && ok; ++jj) {
-        if (jj + 1 < nkv && !issue_s(jj + 1)) {
+      if (ok && nkv > 0) {
+        ok = bounded_wait(k_full, 0, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (active(t, j_lo)) issue_s(t, 0);
+          tc_commit(k_empty);
+        }
+      }
+      for (int u = 0; u < nkv && ok; ++u) {
+        const int j = j_lo + u;
+        const int st = u % NS;
+        const bool nxt = u + 1 < nkv;
+        const int st1 = (u + 1) % NS;
+        if (!bounded_wait(v_full + 8 * st, (u / NS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
           ok = false;
           break;
         }
-        const int st = jj & 1;
-        if (!bounded_wait(p_full, jj & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag) ||
-            !bounded_wait(v_full + 8 * st, (jj >> 1) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
+        if (nxt && !bounded_wait(k_full + 8 * st1, ((u + 1) / NS) & 1, args.status, LK_ERR_TIMEOUT_FULL,
+                                 abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sv = sbase + C::OFF_V + st * C::QB;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 128 keys, 16 per MMA
-          const uint64_t ad = make_desc_sw128(sp + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_desc_sw128(sv + kk * 2048, 16384, 1024);
-          tc_mma_f16(tO, ad, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+        if (active(0, j) && !issue_pv(0, u)) {
+          ok = false;
+          break;
         }
-        tc_commit(o_full);
+        if (nxt && active(0, j + 1)) issue_s(0, u + 1);
+        if (active(1, j) && !issue_pv(1, u)) {
+          ok = false;
+          break;
+        }
         tc_commit(v_empty + 8 * st);
+        if (nxt && active(1, j + 1)) issue_s(1, u + 1);
+        if (nxt) tc_commit(k_empty + 8 * st1);
       }
       tc_commit(drain);
       bounded_wait(drain, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
   } else {
     // ---------------------------------------------------------- softmax
+    // Group t (warps 2..5: tile a, 6..9: tile b); thread = query row (TMEM lane).
     // O accumulates in TMEM across key tiles.  Each row keeps the max m_used
     // its exponentials are taken against and rescales its O row (TMEM
     // read-modify-write) only when a tile's max exceeds m_used by more than 8
     // (a factor 256), so P stays <= 256 and most tiles need no O traffic.
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
+    const int qt = 2 * qp + t;
     const int ql = qt * 128 + r;        // query row within the sequence
     const int q = q_off + ql;           // query position (keys are 0..Skv-1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint8_t* sP = smem + C::OFF_P;
+    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + DH * t + lane_off;
+    const int jbt = t == 0 ? jb0 : jb1;
+    const int n_t = (t == 0 ? je0 : je1) - jbt;
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int jj = 0; jj < nkv; ++jj) {
-      const int j = j_begin + jj;
-      bool w_ok = bounded_wait(s_full, jj & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+    for (int jj = 0; jj < n_t; ++jj) {
+      const int j = jbt + jj;
+      bool w_ok = bounded_wait(s_full + 8 * t, jj & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
       if (!__all_sync(0xffffffffu, w_ok)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, sv[c]);
-      tc_wait_ld();
-      // S is in registers: release the TMEM buffer so S_{j+1} can start now
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
       const bool need_mask = (args.causal && j * 128 + 127 > q_off + qt * 128) || (j + 1) * 128 > Skv ||
                              (args.window > 0 && j * 128 <= q - args.window + 127);
-      float mraw = -INFINITY;  // max of the raw scores (scale > 0 commutes with max)
-      if (need_mask) {
+      // keys of this tile the row may see: [klo, khi] relative to the tile start
+      const int kbase = j * 128;
+      const int khi = min(Skv - 1, args.causal ? q : Skv - 1) - kbase;
+      const int klo = (args.window > 0 ? q - args.window + 1 : 0) - kbase;
+      auto mask_chunk = [&](uint32_t (&x)[32], int c) {
+        if (!need_mask) return;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int e = 0; e < 32; ++e)
+          if (c * 32 + e > khi || c * 32 + e < klo) x[e] = __float_as_uint(-INFINITY);
+      };
+      // pass 1: the row max over all 128 keys (four independent max chains, two
+      // TMEM round trips); chunks 2, 3 stay in registers, chunks 0, 1 are read
+      // again in pass 2 (168 registers hold 64 + 64 scores at once)
+      uint32_t s2[32], s3[32];
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      {
+        uint32_t x0[32], x1[32];
+        tmem_ld32(tS, x0);
+        tmem_ld32(tS + 32, x1);
+        tc_wait_ld();
+        mask_chunk(x0, 0);
+        mask_chunk(x1, 1);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = j * 128 + c * 32 + e;
-            if (key >= Skv || (args.causal && key > q) || (args.window > 0 && key <= q - args.window))
-              sv[c][e] = __float_as_uint(-INFINITY);
-          }
-        }
+        for (int e = 0; e < 32; ++e)
+          m4[e & 3] = fmaxf(m4[e & 3], fmaxf(__uint_as_float(x0[e]), __uint_as_float(x1[e])));
       }
+      tmem_ld32(tS + 64, s2);
+      tmem_ld32(tS + 96, s3);
+      tc_wait_ld();
+      mask_chunk(s2, 2);
+      mask_chunk(s3, 3);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[c][e]));
+      for (int e = 0; e < 32; ++e)
+        m4[e & 3] = fmaxf(m4[e & 3], fmaxf(__uint_as_float(s2[e]), __uint_as_float(s3[e])));
+      // max of the raw scores (scale > 0 commutes with max)
+      const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float mx = mraw * args.sl2;
       const float m_new = (mx > m_used + 8.f) ? mx : m_used;
       const float alpha = (m_new != m_used) ? fast_exp2(m_used - m_new) : 1.f;
       const float mb = (m_new == -INFINITY) ? 0.f : m_new;
-      // P packed to bf16 pairs in place: sv[c][0..15] hold chunk c's 32 probabilities
-      float rowsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      // pass 2: P as bf16 pairs, 32 keys -> 16 TMEM columns at a time, written
+      // over the first 64 columns of S (in key order, so no score is
+      // overwritten before it is read); four independent partial sums
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
+      auto emit = [&](const uint32_t (&x)[32], int c) {
+        uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][e]), args.sl2, -mb));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][e + 1]), args.sl2, -mb));
-          rowsum += p0 + p1;
-          sv[c][e >> 1] = pack_bf16x2(p0, p1);
+          const float p0 = fast_exp2(fmaf(__uint_as_float(x[e]), args.sl2, -mb));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(x[e + 1]), args.sl2, -mb));
+          r4[(e >> 1) & 3] += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
         }
+        tmem_st16(tS + c * 16, pk);
+      };
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t x[32];
+        tmem_ld32(tS + c * 32, x);
+        tc_wait_ld();
+        mask_chunk(x, c);
+        emit(x, c);
       }
-      // PV_{j-1} must be done before O is rescaled and before P is overwritten
-      if (jj > 0) {
-        w_ok = bounded_wait(o_full, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      emit(s2, 2);
+      emit(s3, 3);
+      const float rowsum = (r4[0] + r4[1]) + (r4[2] + r4[3]);
+      // rescale O (rare): PV(jj-1) must have finished accumulating
+      if (jj > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        w_ok = bounded_wait(o_done + 8 * t, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < DH / 32; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(tO + lane_off + c * 32, ov);
-            tc_wait_ld();
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(tO + c * 32, ov);
+          tc_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, ov);
-          }
-          tc_wait_st();
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(tO + c * 32, ov);
         }
       }
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const uint32_t* pk = &sv[u >> 2][(u & 3) * 4];
-        *reinterpret_cast<uint4*>(sP + sw128_off(r, u)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
+      tc_wait_st();
       tc_fence_before();
-      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full + 8 * t);
       l_run = l_run * alpha + rowsum;
       m_used = m_new;
     }
-    if (ok && nkv > 0) {
-      bool w_ok = bounded_wait(o_full, (nkv - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+    if (ok && n_t > 0) {
+      bool w_ok = bounded_wait(o_done + 8 * t, (n_t - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
       if (__all_sync(0xffffffffu, w_ok)) {
         tc_fence_after();
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -324,7 +383,7 @@ __global__ void __launch_bounds__(192, FwdCfg<DH>::MIN_BLOCKS)
 #pragma unroll 1
         for (int c = 0; c < DH / 32; ++c) {
           uint32_t v[32];
-          tmem_ld32(tO + lane_off + c * 32, v);
+          tmem_ld32(tO + c * 32, v);
           tc_wait_ld();
           if (ql < S) {
 #pragma unroll
@@ -384,10 +443,10 @@ static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
   a.ldo = d.ld_o;
   a.lse = d.lse;
   a.status = d.status;
-  a.n_qtiles = cdiv(d.S, 128);
+  a.n_qtiles = cdiv(d.S, 256);  // pairs of 128-query tiles, one per CTA
   auto k = attn_fwd_kernel<DH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  k<<<a.n_qtiles * d.Hq * d.B, 192, C::SMEM, s>>>(tm, tkv, a);
+  k<<<a.n_qtiles * d.Hq * d.B, C::THREADS, C::SMEM, s>>>(tm, tkv, a);
   return check_launch("attn_fwd");
 }
 

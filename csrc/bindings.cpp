@@ -452,6 +452,14 @@ void cross_entropy_vp(torch::Tensor logits, torch::Tensor targets, torch::Tensor
 }
 
 // ------------------------------------------------------ GELU, LayerNorm
+void cast_f32_bf16(torch::Tensor x, torch::Tensor y) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need_contig(x, "x", torch::kFloat32);
+  need_contig(y, "y", torch::kBFloat16);
+  TORCH_CHECK(x.numel() == y.numel(), "cast_f32_bf16: sizes");
+  check(lk_cast_f32_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream()));
+}
+
 void gelu_fwd(torch::Tensor x, torch::Tensor y) {
   const c10::cuda::CUDAGuard g(x.device());
   need_contig(x, "x", torch::kBFloat16);
@@ -1034,6 +1042,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequantize", &dequantize);
   m.def("allgather_copy", &allgather_copy);
   m.def("reduce_scatter_sum", &reduce_scatter_sum);
+  m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("gemm_set_pair", [](int64_t mode) { lk_gemm_set_pair((int)mode); });
+  m.def("gemm_pair_count", []() { return (int64_t)lk_gemm_pair_count(); });
   m.def("reduce_scatter_bf16", &reduce_scatter_bf16);
   m.def("reduce_scatter_bf16_nvls", &reduce_scatter_bf16_nvls);
   m.def("allreduce_sum", &allreduce_sum);

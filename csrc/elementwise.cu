@@ -15,6 +15,8 @@
 // (src/nn/transformer_blocks.cpp:670-718); here the backward scatter-adds into
 // the fp32 gradient with vector atomics.  Out-of-range token ids are recorded
 // in the status word and read as a zero row instead of faulting.
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "lk_api.h"
@@ -159,6 +161,27 @@ static int grid_for(int64_t work, int threads) {
 }  // namespace lk
 
 using namespace lk;
+
+// fp32 -> bf16, 8 elements per thread (the vocabulary-chunked LM head sums its
+// input gradient over chunks in fp32 and rounds once)
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(x)[2 * i + 1];
+    reinterpret_cast<uint4*>(y)[i] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w),
+                                                pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+  }
+}
+
+extern "C" int lk_cast_f32_bf16(const float* x, void* y, int64_t n, cudaStream_t s) {
+  LK_REQUIRE(n % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0,
+             "cast_f32_bf16: n % 8 == 0 and 16-byte aligned buffers");
+  if (n == 0) return 0;
+  const int64_t n8 = n / 8;
+  int grid = (int)std::min<int64_t>((n8 + 255) / 256, (int64_t)num_sms() * 8);
+  cast_f32_bf16_kernel<<<grid, 256, 0, s>>>(x, (__nv_bfloat16*)y, n8);
+  return check_launch("cast_f32_bf16");
+}
 
 extern "C" int lk_rope(const LkRopeDesc* d, cudaStream_t s) {
   LK_REQUIRE(d->Dh % 8 == 0 && d->col0 % 8 == 0 && d->ld % 8 == 0, "rope: head_dim/col0/ld must be multiples of 8");

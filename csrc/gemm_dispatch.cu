@@ -1,6 +1,9 @@
 // K1 GEMM entry point: picks the tile width and the operand-major variant.
 // Instantiations are spread over gemm_bf16.cu / gemm_f32.cu / gemm_fused.cu so
 // they compile in parallel.
+#include <atomic>
+#include <cstdlib>
+
 #include "gemm_kernel.cuh"
 
 extern "C" const char* lk_last_error(void) { return lk::last_error().c_str(); }
@@ -30,6 +33,38 @@ extern "C" int lk_gemm(const LkGemmDesc* g, cudaStream_t stream) {
 }
 
 namespace lk {
+std::atomic<unsigned long long>& gemm_pair_count();
+}
+
+extern "C" void lk_gemm_set_pair(int mode) { lk::gemm_pair_mode() = mode; }
+
+extern "C" unsigned long long lk_gemm_pair_count(void) { return lk::gemm_pair_count().load(); }
+
+namespace lk {
+int& gemm_pair_mode() {
+  static int mode = [] {
+    const char* e = getenv("LK_GEMM_PAIR");
+    return e ? atoi(e) : 0;
+  }();
+  return mode;
+}
+
+// CTA-pair (256-row) tiles for plain GEMMs with at least two 256-row tiles
+// per SM pair's worth of work; 128-row tiles otherwise.
+std::atomic<unsigned long long>& gemm_pair_count() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
+bool use_pair(const LkGemmDesc& g) {
+  if (gemm_pair_mode() == 0 || g.comm_mode != 0 || g.bn == 128) return false;
+  if (g.M < 256 || g.N < 256) return false;
+  const int64_t tiles = (int64_t)cdiv(g.M, 256) * cdiv(g.N, 256);
+  if (tiles < num_sms() / 2) return false;
+  ++gemm_pair_count();
+  return true;
+}
+
 int choose_bn(const LkGemmDesc& g) {
   if (g.bn == 128 || g.bn == 256) return g.bn;
   const int64_t tiles256 = (int64_t)cdiv(g.M, 128) * cdiv(g.N, 256);

@@ -9,9 +9,11 @@ int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s) {
   LK_REQUIRE(!g.a_mn && !g.b_mn, "lk_gemm: fused epilogues need K-major operands");
   if (g.epi == LK_EPI_SWIGLU) {
     LK_REQUIRE(g.N % 256 == 0 && g.h != nullptr, "lk_gemm: swiglu needs N % 256 == 0 and h");
+    if (use_pair(g)) return launch_gemm<256, false, false, EPI_SWIGLU, 0, 2>(g, s);
     return launch_gemm<256, false, false, EPI_SWIGLU>(g, s);
   }
   LK_REQUIRE(g.r != nullptr && g.ldr % 8 == 0, "lk_gemm: residual epilogue needs r");
+  if (use_pair(g)) return launch_gemm<256, false, false, EPI_BF16_RESID, 0, 2>(g, s);
   return choose_bn(g) == 128 ? launch_gemm<128, false, false, EPI_BF16_RESID>(g, s)
                              : launch_gemm<256, false, false, EPI_BF16_RESID>(g, s);
 }

@@ -88,12 +88,16 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
-template <int BN>
+// CG = 2: a CTA pair (cluster of 2) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2; each CTA loads its own 128 rows of A and its half
+// of B's BN rows (plain TMA, no multicast), so per CTA the operand bytes per
+// FLOP drop by a third against the single-CTA 128 x BN tile.
+template <int BN, int CG = 1>
 struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int B_BYTES = (BN / CG) * GEMM_BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = CG == 1 ? ((BN == 256) ? 4 : 6) : (196608 / STAGE > 8 ? 8 : 196608 / STAGE);
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
@@ -265,12 +269,16 @@ __device__ __forceinline__ int gb_expected(const GemmArgs& a, int tn) {
   return (int)((hi - 1) / GB_PIECE - lo / GB_PIECE + 1);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0>
+template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0, int CG = 1>
 __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const GemmArgs args) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
+  static_assert(CG == 1 || (AG == 0 && EPI != EPI_REMOTE), "CTA pairs: plain epilogues only");
+  constexpr int BM_T = GEMM_BM * CG;  // rows of one output tile
+  constexpr int BNH = BN / CG;         // rows of B this CTA loads
+  const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;  // 0: leader (issues the MMAs)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -295,7 +303,7 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 4);
+      mbar_init(tempty0 + 8 * b, 4 * CG);  // every epilogue warp of the pair arrives on the leader's
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -307,13 +315,24 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
       tma_prefetch_desc(&tmB2);
     }
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (CG == 2)
+      tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+    else
+      tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   const int T = args.tiles_m * args.tiles_n;
+  // persistent tile loop: a pair walks the tiles as one unit
+  const int t_first = CG == 2 ? (int)(blockIdx.x / 2) : (int)blockIdx.x;
+  const int t_step = CG == 2 ? (int)(gridDim.x / 2) : (int)gridDim.x;
   const int nk1 = (args.K + GEMM_BK - 1) / GEMM_BK;
   const int nk = nk1 + (args.K2 > 0 ? (args.K2 + GEMM_BK - 1) / GEMM_BK : 0);
 
@@ -323,10 +342,12 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
       int s = 0;
       uint32_t ph = 0, pending = 0, parbits = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+      for (int t = t_first; t < T && ok; t += t_step) {
         int tm, tn;
         gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
         tm = (tm + args.m_rot) % args.tiles_m;
+        const int arow = tm * BM_T + (int)crank * GEMM_BM;  // this CTA's rows of A
+        const int brow = tn * BN + (int)crank * BNH;        // this CTA's rows of B
         if constexpr (AG == 1) {
           if (!wait_count(args, args.ag_count + tm, 128 / AG_SUB, abort_flag)) {
             ok = false;
@@ -347,24 +368,44 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
           const uint32_t fb = full0 + 8 * s;
           const uint32_t sa = sbase + s * C::STAGE;
           const uint32_t sb = sa + C::A_BYTES;
-          mbar_expect_tx(fb, C::STAGE);
           // k-blocks [0, nk1) come from (A, B), the rest from the second segment (A2, B2)
           const bool seg2 = kb >= nk1;
           const CUtensorMap* ma = seg2 ? &tmA2 : &tmA;
           const CUtensorMap* mb = seg2 ? &tmB2 : &tmB;
           const int kc = (seg2 ? kb - nk1 : kb) * GEMM_BK;
-          if (!A_MN) {
-            tma_load_2d(sa, ma, fb, kc, tm * GEMM_BM);
-          } else {
-            tma_load_2d(sa, ma, fb, tm * GEMM_BM, kc);
-            tma_load_2d(sa + 8192, ma, fb, tm * GEMM_BM + 64, kc);
-          }
-          if (!B_MN) {
-            tma_load_2d(sb, mb, fb, kc, tn * BN);
-          } else {
+          if constexpr (CG == 1) {
+            mbar_expect_tx(fb, C::STAGE);
+            if (!A_MN) {
+              tma_load_2d(sa, ma, fb, kc, arow);
+            } else {
+              tma_load_2d(sa, ma, fb, arow, kc);
+              tma_load_2d(sa + 8192, ma, fb, arow + 64, kc);
+            }
+            if (!B_MN) {
+              tma_load_2d(sb, mb, fb, kc, brow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + 8192 * j, mb, fb, tn * BN + 64 * j, kc);
+              for (int j = 0; j < BNH / 64; ++j)
+                tma_load_2d(sb + 8192 * j, mb, fb, brow + 64 * j, kc);
+            }
+          } else {
+            // both CTAs' bytes complete on the leader's full barrier, which the
+            // leader's producer arms with the pair's total
+            const uint32_t fbl = mapa_shared(fb, 0);
+            if (crank == 0) mbar_expect_tx(fb, 2 * C::STAGE);
+            if (!A_MN) {
+              tma_load_2d_pair(sa, ma, fbl, kc, arow);
+            } else {
+              tma_load_2d_pair(sa, ma, fbl, arow, kc);
+              tma_load_2d_pair(sa + 8192, ma, fbl, arow + 64, kc);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(sb, mb, fbl, kc, brow);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BNH / 64; ++j)
+                tma_load_2d_pair(sb + 8192 * j, mb, fbl, brow + 64 * j, kc);
+            }
           }
           pending |= 1u << s;
           parbits = (parbits & ~(1u << s)) | (ph << s);
@@ -374,8 +415,10 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
           }
         }
       }
-      if (!ok) {
-        // Abort: let every copy this thread issued land before smem is released.
+      if (!ok && crank == 0) {
+        // Abort: let every copy issued land before smem is released (a pair's
+        // copies all complete on the leader's barriers; the peer is held by the
+        // cluster barrier at the end until then).
         for (int i = 0; i < C::STAGES; ++i)
           if (pending & (1u << i))
             bounded_wait(full0 + 8 * i, (parbits >> i) & 1, args.status, LK_ERR_TIMEOUT_DRAIN,
@@ -384,17 +427,20 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(GEMM_BM, BN, A_MN, B_MN);
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM_T, BN, A_MN, B_MN);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
       int local = 0;
-      for (int t = blockIdx.x; t < T && ok; t += gridDim.x, ++local) {
+      for (int t = t_first; t < T && ok; t += t_step, ++local) {
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
-        if (!bounded_wait(tempty0 + 8 * buf, (use & 1) ^ 1, args.status, LK_ERR_TIMEOUT_ACCUM,
-                          abort_flag)) {
+        const bool tok = CG == 2 ? bounded_wait_cluster(tempty0 + 8 * buf, (use & 1) ^ 1, args.status,
+                                                        LK_ERR_TIMEOUT_ACCUM, abort_flag)
+                                 : bounded_wait(tempty0 + 8 * buf, (use & 1) ^ 1, args.status,
+                                                LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!tok) {
           ok = false;
           break;
         }
@@ -414,18 +460,32 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
                                      : make_desc_sw128(sa + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? make_desc_sw128(sb + kk * 2048, 8192, 1024)
                                      : make_desc_sw128(sb + kk * 32, 16, 1024);
-            tc_mma_f16(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if constexpr (CG == 2)
+              tc_mma_f16_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              tc_mma_f16(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          tc_commit(empty0 + 8 * s);
+          if constexpr (CG == 2)
+            tc_commit_pair_mc(empty0 + 8 * s, 0x3);  // both CTAs' producers may refill the stage
+          else
+            tc_commit(empty0 + 8 * s);
           if (++s == C::STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
-        if (ok) tc_commit(tfull0 + 8 * buf);
+        if (ok) {
+          if constexpr (CG == 2)
+            tc_commit_pair_mc(tfull0 + 8 * buf, 0x3);
+          else
+            tc_commit(tfull0 + 8 * buf);
+        }
       }
       // Make sure every MMA this thread issued has retired before TMEM is freed.
-      tc_commit(drain_bar);
+      if constexpr (CG == 2)
+        tc_commit_pair(drain_bar);
+      else
+        tc_commit(drain_bar);
       bounded_wait(drain_bar, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
     }
   } else if (AG && warp >= 6) {
@@ -438,9 +498,10 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
   } else {
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const int row_in_tile = (int)crank * GEMM_BM + q * 32 + lane;
+    const uint32_t tempty_leader = CG == 2 ? mapa_shared(tempty0, 0) : tempty0;
     int local = 0;
-    for (int t = blockIdx.x; t < T; t += gridDim.x, ++local) {
+    for (int t = t_first; t < T; t += t_step, ++local) {
       int tm, tn;
       gemm_tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
       tm = (tm + args.m_rot) % args.tiles_m;
@@ -450,7 +511,7 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
                              abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int row = tm * GEMM_BM + row_in_tile;
+      const int row = tm * BM_T + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
       const float alpha = args.alpha;
@@ -623,7 +684,12 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(tempty_leader + 8 * buf);
+        else
+          mbar_arrive(tempty0 + 8 * buf);
+      }
     }
     if constexpr (EPI == EPI_REMOTE) {
       if (lane == 0) bulk_wait<0>();  // every TMA store of this warp has landed in peer memory
@@ -632,16 +698,22 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync();  // the pair's MMAs, copies and TMEM reads are all done
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0>
+template <int BN, bool A_MN, bool B_MN, int EPI, int AG = 0, int CG = 1>
 int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
   GemmArgs args{};
   args.M = g.M;
   args.N = g.N;
@@ -654,16 +726,16 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   args.ldh = g.ldh;
   args.alpha = g.alpha;
   args.status = g.status;
-  args.tiles_m = cdiv(g.M, GEMM_BM);
+  args.tiles_m = cdiv(g.M, GEMM_BM * CG);
   args.tiles_n = cdiv(g.N, BN);
   CUtensorMap ta, tb, ta2, tb2;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   if (!make_tmap_2d(&ta, g.a, bf, 2, g.a_rows, g.a_cols, g.a_ld, A_MN ? 64 : GEMM_BM, 64)) return -1;
-  if (!make_tmap_2d(&tb, g.b, bf, 2, g.b_rows, g.b_cols, g.b_ld, B_MN ? 64 : BN, 64)) return -1;
+  if (!make_tmap_2d(&tb, g.b, bf, 2, g.b_rows, g.b_cols, g.b_ld, B_MN ? 64 : BN / CG, 64)) return -1;
   args.K2 = g.K2;
   if (g.K2 > 0) {
     if (!make_tmap_2d(&ta2, g.a2, bf, 2, g.a2_rows, g.a2_cols, g.a2_ld, A_MN ? 64 : GEMM_BM, 64)) return -1;
-    if (!make_tmap_2d(&tb2, g.b2, bf, 2, g.b2_rows, g.b2_cols, g.b2_ld, B_MN ? 64 : BN, 64)) return -1;
+    if (!make_tmap_2d(&tb2, g.b2, bf, 2, g.b2_rows, g.b2_cols, g.b2_ld, B_MN ? 64 : BN / CG, 64)) return -1;
   } else {
     ta2 = ta;
     tb2 = tb;
@@ -688,7 +760,7 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   args.gb_boff = g.gb_boff;
   args.gb_dst = reinterpret_cast<uint8_t*>(g.gb_dst);
   args.gb_count = g.gb_count;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, AG>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, AG, CG>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -699,6 +771,28 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
     attr_set |= 1ull << dev;
   }
   const int tiles = args.tiles_m * args.tiles_n;
+  if constexpr (CG == 2) {
+    // one cluster (CTA pair) per two SMs, persistent over the 256 x BN tiles
+    const int pairs = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, ta2, tb2, args);
+    if (e != cudaSuccess) {
+      last_error() = std::string("gemm pair launch: ") + cudaGetErrorString(e);
+      return -1;
+    }
+    return check_launch("gemm_tc_kernel_pair");
+  }
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if constexpr (AG != 0) {
     // CTAs wait on data copied by other CTAs: they must all be resident
@@ -718,6 +812,10 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
     return check_launch("gemm_tc_kernel");
   }
 }
+
+// CTA-pair policy (gemm_dispatch.cu): mode 0 off, 1 on where applicable.
+int& gemm_pair_mode();
+bool use_pair(const LkGemmDesc& g);
 
 // Per-epilogue dispatchers (each defined in its own translation unit).
 int gemm_dispatch_bf16(const LkGemmDesc& g, cudaStream_t s);

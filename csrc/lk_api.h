@@ -86,6 +86,10 @@ typedef struct LkGemmDesc {
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
+// CTA-pair tiles (tcgen05.mma.cta_group::2, 256 x 256) for plain GEMMs: 0 off, 1 on
+// (also LK_GEMM_PAIR in the environment at the first GEMM)
+void lk_gemm_set_pair(int mode);
+unsigned long long lk_gemm_pair_count(void);  // GEMMs that took the CTA-pair path so far
 // Encode the K18 store tensor maps of `world` receive buffers (bf16 [rows, cols],
 // pitch ld elements; 32 x 64 boxes, 128-byte swizzle) into host memory out
 // (world * 128 bytes, to be copied to the device by the caller).
@@ -137,6 +141,7 @@ int lk_rope(const LkRopeDesc* d, cudaStream_t s);
 // ------------------------------------------------------ K7 SwiGLU, K8 embedding
 int lk_swiglu_fwd(const void* gu, void* h, int M, int F, cudaStream_t s);
 int lk_swiglu_bwd(const void* gu, const void* dh, void* dgu, int M, int F, cudaStream_t s);
+int lk_cast_f32_bf16(const float* x, void* y, int64_t n, cudaStream_t s);
 int lk_embedding_fwd(const int64_t* ids, const void* W, void* out, int T, int D, int V,
                      int* status, cudaStream_t s);
 int lk_embedding_bwd(const int64_t* ids, const void* dy, float* dW, int T, int D, int V,

@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     const uint4* yr = reinterpret_cast<const uint4*>(dy + (int64_t)row * D);
     const uint4* gr = reinterpret_cast<const uint4*>(gamma);
     float dot = 0.f;
-#pragma unroll 2
+    // first pass: every load of the row in flight at once for widths <= 2048
+#pragma unroll(VPT <= 8 ? VPT : 2)
     for (int i = 0; i < VPT; ++i) {
       const int c = i * 32 + lane;
       const uint4 a = xr[c], b = yr[c], g = gr[c];

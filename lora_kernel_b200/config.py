@@ -34,6 +34,14 @@ class TransformerConfig:
     norm_eps: float = 1e-5
     tie_embeddings: bool = False
     init_std: float = 0.02
+    # LM head + cross-entropy in vocabulary chunks of this many columns, never
+    # materialising the [tokens, vocab] logits: 0 = chunks of 8192 when the
+    # logits would take more than 1 GiB, -1 = never
+    ce_vocab_chunk: int = 0
+    # stochastic depth (training): layer l (0-based) of L skips its attention and
+    # FFN branches with probability (l + 1) / L * stochastic_depth; a kept
+    # layer's branch outputs are scaled by 1 / (keep probability)
+    stochastic_depth: float = 0.0
 
     def __post_init__(self):
         if self.num_kv_heads <= 0:

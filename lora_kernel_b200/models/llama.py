@@ -103,6 +103,8 @@ class LlamaModel:
         # backward re-runs a layer's forward (same kernels, same values) right
         # before its backward
         self.recompute = False
+        self._saving = False
+        self._sd_scale = 1.0  # stochastic depth: 1 / keep probability of the current layer
         self.lora = None        # optional LoRAAdapters (models/lora.py)
         self.train_base = True  # False: frozen base weights (no base weight gradients)
         self._u: Dict[Tuple[int, str], torch.Tensor] = {}
@@ -115,6 +117,16 @@ class LlamaModel:
         self.ctx = None
 
     # -------------------------------------------------------------- helpers
+    def ce_chunk(self, T: int) -> int:
+        """Vocabulary columns per LM-head chunk in training (0: whole vocabulary)."""
+        c, V = self.cfg.ce_vocab_chunk, self.cfg.vocab_size
+        if c < 0:
+            return 0
+        if c == 0:
+            return 8192 if T * V * 2 > (1 << 30) and V > 8192 else 0
+        c = max(8, c // 8 * 8)
+        return c if c < V else 0
+
     def workspace(self, B: int, S: int, save: bool = True) -> _Workspace:
         key = (B, S, save, self.recompute and save)
         ws = self._ws.get(key)
@@ -123,7 +135,8 @@ class LlamaModel:
             if full > self.rope.shape[0]:
                 self.rope = E.rope_table(full, self.cfg.head_dim, self.cfg.rope_base, self.device)
             ws = _Workspace(self.cfg, B, S, self.device, save, recompute=self.recompute and save,
-                            dropout=save and self.cfg.dropout > 0)
+                            dropout=save and self.cfg.dropout > 0,
+                            logits=not (save and self.ce_chunk(B * S)))
             self._ws[key] = ws
         return ws
 
@@ -140,17 +153,21 @@ class LlamaModel:
         if self.hooks is not None:
             getattr(self.hooks, name)(*a)
 
-    def _wgrad(self, dy, x, name):
-        """Weight gradient: stored on the first micro-step of a window, else accumulated."""
+    def _wgrad(self, dy, x, name, rows: Optional[Tuple[int, int]] = None, alpha: float = 1.0):
+        """Weight gradient: stored on the first micro-step of a window, else
+        accumulated; rows = (r0, n): only those rows of the weight (dy holds
+        their output columns)."""
         if not self.train_base and not name.endswith("norm") and name != "embed":
             return
         g = self._g(name)
+        if rows is not None:
+            g = g[rows[0]:rows[0] + rows[1]]
         # a bf16 gradient view (ZeRO-3 slot, reduce-scattered every micro-batch)
         # is stored; an fp32 one is stored on the first micro-batch of a window
         # and accumulated afterwards
         epi = "bf16" if g.dtype == torch.bfloat16 else ("f32" if self._overwrite else "f32_acc")
         with ph("bwd.gemm_wgrad"):
-            G.gemm(dy.t(), x.t(), g, epi=epi)
+            G.gemm(dy.t(), x.t(), g, epi=epi, alpha=alpha)
 
     # ------------------------------------------------------ linear + LoRA
     def _lora_u(self, i: int, t: str, x: torch.Tensor, save: bool):
@@ -181,9 +198,10 @@ class LlamaModel:
             return out
         u = self._lora_u(i, t, x, save)
         B = self.lora.B(i, t) if u is not None else None
+        alpha = self._sd_scale if residual is not None else 1.0  # a residual branch's output projection
         with ph(f"fwd.gemm_{t}"):
             G.gemm(x, self._p(f"layers.{i}.{t}"), out, epi="bf16_resid" if residual is not None else "bf16",
-                   residual=residual, a2=u, b2=B)
+                   residual=residual, a2=u, b2=B, alpha=alpha)
         return out
 
     def _lin_swiglu(self, i: int, x, gu_out, h_out, save: bool = True):
@@ -205,13 +223,14 @@ class LlamaModel:
             G.gemm(dy.t(), self._u[(i, t)].t(), self.lora.gB(i, t), epi=acc)  # dB = dy^T (s u)
         else:
             fn = self._take_fused(i, t)
+            alpha = self._sd_scale if t in ("wo", "wdown") else 1.0
             if fn is not None:
                 with ph("bwd.gemm_dgrad+gather"):
                     fn(dy, self._p(name).t(), dx_out)
             else:
                 with ph("bwd.gemm_dgrad"):
-                    G.linear_dgrad(dy, self._p(name), out=dx_out)
-        self._wgrad(dy, x, name)
+                    G.gemm(dy, self._p(name).t(), dx_out, alpha=alpha)
+        self._wgrad(dy, x, name, alpha=alpha if self.lora is None or not self.lora.has(i, t) else 1.0)
 
     # -------------------------------------------------------------- dropout
     def _drop_seed(self, i: int, site: int) -> int:
@@ -220,10 +239,42 @@ class LlamaModel:
     def _dropping(self, ws: _Workspace) -> bool:
         return self.cfg.dropout > 0 and ws.od is not None
 
+    # ----------------------------------------------------- stochastic depth
+    def _layer_keep_prob(self, i: int) -> float:
+        return 1.0 - (i + 1) / self.cfg.num_layers * self.cfg.stochastic_depth
+
+    def _layer_dropped(self, i: int) -> bool:
+        """Training only: is layer i skipped in this micro-step?  A counter hash
+        of (seed, micro-step, layer), so the backward and the recomputation see
+        the forward's decision.  (Huang et al. 2016's linear decay; the
+        reference's StochasticDepth keeps layer l with p (1 - l / L), which
+        drops the deepest layers almost always.)"""
+        sd = self.cfg.stochastic_depth
+        if sd <= 0 or not self._saving:
+            return False
+        h = (self._drop_seed(i, 7) * 0x9E3779B97F4A7C15 + 0xD1B54A32D192ED03) & 0xFFFFFFFFFFFFFFFF
+        h ^= h >> 31
+        h = (h * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
+        h ^= h >> 29
+        return (h >> 11) / float(1 << 53) >= self._layer_keep_prob(i)
+
+    def _skip_layer_fwd(self, i: int, h_in: torch.Tensor, h_out: torch.Tensor) -> bool:
+        self._sd_scale = 1.0
+        if self.cfg.stochastic_depth <= 0 or not self._saving:
+            return False
+        if self._layer_dropped(i):
+            if h_out.data_ptr() != h_in.data_ptr():
+                h_out.copy_(h_in)  # identity layer
+            return True
+        self._sd_scale = 1.0 / self._layer_keep_prob(i)
+        return False
+
     # -------------------------------------------------------------- forward
     def _layer_fwd(self, i: int, ws: _Workspace, h_in: torch.Tensor, h_out: torch.Tensor, slot: int):
         cfg = self.cfg
         p = f"layers.{i}."
+        if self._skip_layer_fwd(i, h_in, h_out):
+            return
         drop = self._dropping(ws)
         xn1, rstd1 = ws.xn1[slot], ws.rstd1[slot]
         with ph("fwd.rmsnorm"):
@@ -267,8 +318,9 @@ class LlamaModel:
         h_last = ws.h[cfg.num_layers] if save else ws.h[cfg.num_layers % 2]
         with ph("fwd.rmsnorm"):
             N.rmsnorm_fwd(h_last, self._p("final_norm"), cfg.norm_eps, y=ws.xf, rstd=ws.rstdf)
-        with ph("fwd.gemm_lm_head"):
-            G.linear(ws.xf, self._p("lm_head"), out=ws.logits)
+        if ws.logits is not None:  # else: the vocabulary-chunked head runs in forward_backward
+            with ph("fwd.gemm_lm_head"):
+                G.linear(ws.xf, self._p("lm_head"), out=ws.logits)
         return ws.logits
 
     @torch.no_grad()
@@ -298,15 +350,18 @@ class LlamaModel:
         if loss_acc is None:
             acc.zero_()
         self._forward(ids, ws, save=True)
-        # K9: loss + dlogits in place (scaled)
-        with ph("fwd.cross_entropy"):
-            L.cross_entropy_(ws.logits, targets.reshape(-1), acc, scale=loss_scale, scale_mul=grad_scale,
-                             smoothing=label_smoothing, z_loss=z_loss)
-        dlogits = ws.logits
-        # LM head
-        with ph("bwd.gemm_dgrad"):
-            G.linear_dgrad(dlogits, self._p("lm_head"), out=ws.dx)
-        self._wgrad(dlogits, ws.xf, "lm_head")
+        if ws.logits is None:
+            self._lm_head_ce_chunked(ws, targets.reshape(-1), acc, loss_scale, grad_scale, label_smoothing, z_loss)
+        else:
+            # K9: loss + dlogits in place (scaled)
+            with ph("fwd.cross_entropy"):
+                L.cross_entropy_(ws.logits, targets.reshape(-1), acc, scale=loss_scale, scale_mul=grad_scale,
+                                 smoothing=label_smoothing, z_loss=z_loss)
+            dlogits = ws.logits
+            # LM head
+            with ph("bwd.gemm_dgrad"):
+                G.linear_dgrad(dlogits, self._p("lm_head"), out=ws.dx)
+            self._wgrad(dlogits, ws.xf, "lm_head")
         L_ = cfg.num_layers
         with ph("bwd.rmsnorm"):
             N.rmsnorm_bwd(ws.dx, ws.h[L_], self._p("final_norm"), ws.rstdf, self._g("final_norm"), dx=ws.dh,
@@ -331,12 +386,73 @@ class LlamaModel:
         self._drop_step += 1
         return acc
 
+    def _lm_head_ce_chunked(self, ws: _Workspace, targets: torch.Tensor, acc: torch.Tensor, loss_scale,
+                            grad_scale: float, smoothing: float, z_loss: float) -> None:
+        """LM head + cross-entropy without the [T, V] logits: pass 1 computes
+        each vocabulary chunk's logits into one reusable buffer and keeps per-row
+        statistics {max, sum exp, sum z, z[target]}; pass 2 recomputes each
+        chunk, turns it into its gradient slice with the combined statistics,
+        and feeds the dgrad GEMM (fp32 sum over chunks into dx) and the weight
+        gradient of the chunk's rows.  One extra LM-head GEMM buys the memory
+        of the logits (2.1 GB at 8192 tokens x 128256 words)."""
+        cfg = self.cfg
+        T, V, D = ws.T, cfg.vocab_size, cfg.hidden_dim
+        chunk = self.ce_chunk(T)
+        n = (V + chunk - 1) // chunk
+        W = self._p("lm_head")
+        # scratch: the logits chunk (bf16) and the fp32 input gradient, in the
+        # SwiGLU-gradient buffer (unused until the layers' backward) when it fits
+        need = T * chunk + 2 * T * D
+        buf = ws.dgu.view(-1)
+        if buf.numel() < need:
+            if getattr(ws, "ce_scratch", None) is None or ws.ce_scratch.numel() < need:
+                ws.ce_scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
+            buf = ws.ce_scratch
+        dx32 = buf[T * chunk:T * chunk + 2 * T * D].view(torch.float32).view(T, D)
+        if getattr(ws, "ce_stats", None) is None or ws.ce_stats.shape[0] != n:
+            ws.ce_stats = torch.empty(n, T, 4, dtype=torch.float32, device=self.device)
+            ws.ce_stat_ptrs = torch.tensor([ws.ce_stats[c].data_ptr() for c in range(n)], dtype=torch.int64,
+                                           device=self.device)
+            ws.ce_dummy = torch.zeros(2, dtype=torch.float32, device=self.device)
+
+        def logits_chunk(c):
+            v0 = c * chunk
+            vc = min(chunk, V - v0)
+            lg = buf[:T * vc].view(T, vc)
+            with ph("fwd.gemm_lm_head"):
+                G.linear(ws.xf, W[v0:v0 + vc], out=lg)
+            return v0, vc, lg
+
+        for c in range(n):
+            v0, vc, lg = logits_chunk(c)
+            with ph("fwd.cross_entropy"):
+                L.cross_entropy_chunk_stats(lg, targets, v0, V, ws.ce_stats[c], ws.ce_dummy, ws.ce_stat_ptrs)
+        for c in range(n):
+            v0, vc, lg = logits_chunk(c)  # recomputed: nothing of size [T, V] is kept
+            with ph("fwd.cross_entropy"):
+                L.cross_entropy_chunk_grad(lg, targets, v0, V, ws.ce_stats[c], ws.ce_stat_ptrs,
+                                           acc if c == 0 else ws.ce_dummy, scale=loss_scale, scale_mul=grad_scale,
+                                           smoothing=smoothing, z_loss=z_loss)
+            with ph("bwd.gemm_dgrad"):
+                G.gemm(lg, W[v0:v0 + vc].t(), dx32, epi="f32" if c == 0 else "f32_acc")
+            self._wgrad(lg, ws.xf, "lm_head", rows=(v0, vc))
+        E.cast_f32_bf16(dx32, out=ws.dx)
+
     def _layer_bwd(self, i: int, ws: _Workspace, slot: Optional[int] = None, hidx: Optional[int] = None):
         """Backward of layer i with the running residual gradient in ws.dh.
         slot: workspace slot of its intermediates; hidx: index of its input in
         ws.h (both default to the whole-model positions)."""
         cfg = self.cfg
         p = f"layers.{i}."
+        self._sd_scale = 1.0
+        if cfg.stochastic_depth > 0:
+            if self._layer_dropped(i):  # identity: dh passes through, the weights get no gradient
+                for t in ("wqkv", "wo", "wgu", "wdown", "attn_norm", "ffn_norm"):
+                    g = self._g(p + t)
+                    if self._overwrite or g.dtype == torch.bfloat16:
+                        g.zero_()
+                return
+            self._sd_scale = 1.0 / self._layer_keep_prob(i)
         s = slot if slot is not None else (0 if self.recompute else i)
         h_in = ws.h[i if hidx is None else hidx]
         dh = ws.dh

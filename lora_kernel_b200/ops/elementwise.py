@@ -105,3 +105,11 @@ def dropout_mask_reference(n: int, p: float, seed: int) -> torch.Tensor:
         h = (z >> np.uint64(32)).astype(np.uint64)
     thresh = min(4294967295, int(float(np.float32(p)) * 4294967296.0))  # the kernel gets p as float
     return torch.from_numpy(h >= np.uint64(thresh))
+
+
+def cast_f32_bf16(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 copy of an fp32 tensor (round to nearest even), on the device."""
+    require_device(x)
+    out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    C().cast_f32_bf16(x, out)
+    return out

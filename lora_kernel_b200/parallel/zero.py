@@ -159,6 +159,9 @@ class Zero3Trainer:
         self.rank = dist.get_rank(self.group)
         self.mode = comm
         self.fuse_gather = fuse_gather and comm == "p2p"
+        if self.fuse_gather and cfg.stochastic_depth > 0:
+            raise ValueError("stochastic depth skips layers whose gather the fused GEMM would do; "
+                             "use the prefetching gather (fuse_gather=False)")
         if grad_wire not in ("bf16", "fp32"):
             raise ValueError(grad_wire)
         self.grad_wire = grad_wire

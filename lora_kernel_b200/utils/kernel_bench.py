@@ -163,7 +163,12 @@ def main():
     ap.add_argument("--only", default="gemm,norm")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--small", action="store_true", help="one small GEMM (for profiling)")
+    ap.add_argument("--pair", type=int, default=-1,
+                    help="GEMMs on CTA pairs (cta_group::2, 256-row tiles): 1 on, 0 off, -1 the default")
     args = ap.parse_args()
+    if args.pair >= 0:
+        from lora_kernel_b200._ext import C
+        C().gemm_set_pair(args.pair)
     which = set(args.only.split(","))
     if "gemm" in which:
         if args.small:

@@ -11,7 +11,7 @@ mean there), ModelPruning (include/nn/model_pruning.hpp:8-37), GradientNoise
 """
 from __future__ import annotations
 
-from typing import Dict, List, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -82,3 +82,21 @@ def noise_seed(seed: int, step: int, rank: int = -1) -> int:
     rank holds a different shard."""
     z = (seed * 0x9E3779B97F4A7C15 + step * 0xBF58476D1CE4E5B9 + (rank + 1) * 0x94D049BB133111EB)
     return z & ((1 << 63) - 1)
+
+
+def fuse_conv_bn(conv_w: torch.Tensor, conv_b: Optional[torch.Tensor], bn_gamma: torch.Tensor,
+                 bn_beta: torch.Tensor, bn_mean: torch.Tensor, bn_var: torch.Tensor,
+                 eps: float = 1e-5) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Fold an inference-mode batch norm into the convolution (or linear layer)
+    before it: y = gamma (conv(x) - mean) / sqrt(var + eps) + beta becomes a
+    convolution with weight w * s (per output channel) and bias (b - mean) s +
+    beta, s = gamma / sqrt(var + eps).  Output channels are dimension 0 of
+    conv_w.  Returns (weight, bias) in conv_w's dtype, computed in fp32.
+
+    Reference: BatchNormFusion::fuse_conv_bn
+    (include/nn/training_enhancements.hpp:263-277), which uses eps = 1e-6."""
+    s = bn_gamma.float() / torch.sqrt(bn_var.float() + eps)
+    w = conv_w.float() * s.view(-1, *([1] * (conv_w.dim() - 1)))
+    b0 = conv_b.float() if conv_b is not None else torch.zeros_like(s)
+    b = (b0 - bn_mean.float()) * s + bn_beta.float()
+    return w.to(conv_w.dtype), b.to(conv_w.dtype)

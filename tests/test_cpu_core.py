@@ -292,3 +292,14 @@ def test_cpu_lora_trains_adapters_only(tmp_path):
     ad = load_lora_file(str(tmp_path / "lora_step_12.safetensors"), rc.model, "cpu")
     b = ad.state_dict()["layers.0.wqkv.B"]
     assert ad.lc.rank == 8 and float(b.abs().sum()) > 0      # B starts at zero and was trained
+
+
+def test_vocab_chunk_policy():
+    """Chunk the LM head only when the whole logits would be large."""
+    from lora_kernel_b200.models.llama import LlamaModel
+    from lora_kernel_b200.config import get_preset
+    big = get_preset("llama-8b-fsdp-dp8").model
+    small = get_preset("llama-1.1b-zero3").model
+    # the 1.1B logits at 8192 tokens (0.5 GB) stay whole; the 8B ones (2.1 GB) are chunked
+    assert LlamaModel.ce_chunk(type("M", (), {"cfg": small})(), 8192) == 0
+    assert LlamaModel.ce_chunk(type("M", (), {"cfg": big})(), 8192) == 8192

@@ -307,3 +307,66 @@ def test_peer_wait_gives_up_with_a_status_and_the_context_survives():
     assert int(status.item()) == 0
     x = torch.arange(1024, device="cuda", dtype=torch.float32)
     assert float(x.sum().item()) == 1023 * 1024 / 2
+
+
+@pytest.mark.parametrize("layout", ["tn", "dgrad", "wgrad", "nt"])
+def test_gemm_cta_pair_matches_fp32(layout):
+    """256 x 256 tiles computed by a CTA pair (tcgen05.mma.cta_group::2) with
+    ragged M, N and K edges, every operand layout and epilogue."""
+    from lora_kernel_b200._ext import C
+    from lora_kernel_b200.ops.gemm import gemm
+    torch.manual_seed(3)
+    M, N, K = 2600, 2056, 320
+    if layout == "tn":
+        a, b = _bf(M, K), _bf(N, K)
+    elif layout == "dgrad":
+        a, b = _bf(M, K), _mn(N, K)
+    elif layout == "wgrad":
+        a, b = _mn(M, K), _mn(N, K)
+    else:
+        a, b = _mn(M, K), _bf(N, K)
+    ref = a.float() @ b.float().t()
+    C().gemm_set_pair(1)
+    try:
+        n0 = C().gemm_pair_count()
+        out = gemm(a, b)
+        _close(out, ref, 2e-2, 2e-2 * math.sqrt(K) * 0.1 + 1e-2)
+        if layout != "nt":
+            out = gemm(a, b, epi="f32")
+            _close(out, ref, 1e-3, 1e-2)
+            acc = torch.ones(M, N, device=dev)
+            gemm(a, b, acc, epi="f32_acc", alpha=0.5)
+            _close(acc, 1 + 0.5 * ref, 1e-3, 1e-2)
+        if layout == "tn":
+            r = _bf(M, N)
+            r0 = r.float()
+            gemm(a, b, r, epi="bf16_resid", residual=r)  # in place
+            _close(r, ref + r0, 2e-2, 5e-2)
+        assert C().gemm_pair_count() > n0, "the CTA-pair path did not run"
+        _status_ok()
+    finally:
+        C().gemm_set_pair(0)
+
+
+def test_gemm_cta_pair_fused_epilogues():
+    from lora_kernel_b200._ext import C
+    from lora_kernel_b200.ops.gemm import gemm, interleave_gate_up, linear_swiglu
+    torch.manual_seed(4)
+    T, D, F = 2600, 256, 1536
+    x = _bf(T, D)
+    wg, wu = _bf(F, D, scale=0.1), _bf(F, D, scale=0.1)
+    w = _bf(2048, D)
+    r = _bf(T, 2048)
+    C().gemm_set_pair(1)
+    try:
+        n0 = C().gemm_pair_count()
+        gu, h = linear_swiglu(x, interleave_gate_up(wg, wu))
+        g = x.float() @ wg.float().t()
+        u = x.float() @ wu.float().t()
+        _close(h, torch.nn.functional.silu(g) * u, 3e-2, 3e-2)
+        out = gemm(x, w, epi="bf16_resid", residual=r)
+        _close(out, x.float() @ w.float().t() + r.float(), 2e-2, 5e-2)
+        assert C().gemm_pair_count() >= n0 + 2
+        _status_ok()
+    finally:
+        C().gemm_set_pair(0)

@@ -148,3 +148,74 @@ def test_cpu_demo_loss_curve_tracks_the_fp32_oracle():
     for k, (a, b) in enumerate(zip(got, want)):
         assert abs(a - b) <= 0.1 * b + 0.1, (k, got, want)
     assert got[-1] < got[0] - 2.0 and want[-1] < want[0] - 2.0
+
+
+@pytest.mark.parametrize("tie", [False, True])
+def test_vocab_chunked_lm_head_matches_the_materialised_logits(tie):
+    """The LM head + cross-entropy in vocabulary chunks (never holding the
+    [tokens, vocab] logits) gives the loss and gradients of the one-shot path,
+    with label smoothing and z-loss, a ragged last chunk and accumulation."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.models.llama import LlamaModel
+    torch.manual_seed(0)
+    B, S = 2, 256
+    ids = torch.randint(0, 1000, (2, B, S), device="cuda")
+    tgt = torch.randint(0, 1000, (2, B, S), device="cuda")
+    out = {}
+    for chunk in (-1, 256):
+        cfg = _tiny(vocab_size=1000, tie_embeddings=tie, ce_vocab_chunk=chunk)
+        eng = LlamaModel(cfg, "cuda", seed=7)
+        assert (eng.ce_chunk(B * S) > 0) == (chunk > 0)
+        scale = torch.full((1,), 64.0, device="cuda")
+        acc = torch.zeros(2, device="cuda")
+        for k in range(2):  # a two-micro-batch window: stored, then accumulated gradients
+            eng.forward_backward(ids[k], tgt[k], loss_scale=scale, grad_scale=1.0 / (2 * B * S),
+                                 label_smoothing=0.1, z_loss=1e-3, loss_acc=acc, overwrite_grads=(k == 0))
+        check_status()
+        ws = eng.workspace(B, S, save=True)
+        assert (ws.logits is None) == (chunk > 0)
+        out[chunk] = ((acc[0] / acc[1]).item(), {n: eng.grads[n].float().clone() for n in
+                                                 ("lm_head", "embed", "layers.1.wgu", "final_norm")})
+    (l0, g0), (l1, g1) = out[-1], out[256]
+    assert abs(l0 - l1) < 1e-3 * abs(l0), (l0, l1)
+    for n in g0:
+        assert _rel(g1[n], g0[n]) < 1e-2, (n, _rel(g1[n], g0[n]))
+
+
+
+def test_stochastic_depth_equals_a_rescaled_model():
+    """A micro-step with stochastic depth equals the plain engine whose dropped
+    layers have zero output projections and whose kept layers have theirs
+    scaled by 1 / keep probability; dropped layers get no gradient."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.models.llama import LlamaModel
+    torch.manual_seed(0)
+    B, S = 2, 128
+    ids = torch.randint(0, 512, (B, S), device="cuda")
+    tgt = torch.randint(0, 512, (B, S), device="cuda")
+    cfg = _tiny(num_layers=4, stochastic_depth=0.6)
+    eng = LlamaModel(cfg, "cuda", seed=7)
+    eng._saving = True
+    dropped = [eng._layer_dropped(i) for i in range(4)]
+    keep = [eng._layer_keep_prob(i) for i in range(4)]
+    acc = eng.forward_backward(ids, tgt, grad_scale=1.0 / (B * S), overwrite_grads=True)
+    ref = LlamaModel(_tiny(num_layers=4), "cuda", seed=7)
+    for i in range(4):
+        for t in ("wo", "wdown"):
+            w = ref.params[f"layers.{i}.{t}"]
+            w.copy_(torch.zeros_like(w) if dropped[i] else (w.float() / keep[i]).to(w.dtype))
+    acc_ref = ref.forward_backward(ids, tgt, grad_scale=1.0 / (B * S), overwrite_grads=True)
+    check_status()
+    l, lr = (acc[0] / acc[1]).item(), (acc_ref[0] / acc_ref[1]).item()
+    assert abs(l - lr) < 5e-3 * abs(lr), (l, lr, dropped)
+    for i in range(4):
+        for t in ("wqkv", "wo", "wgu", "wdown", "attn_norm", "ffn_norm"):
+            g = eng.grads[f"layers.{i}.{t}"].float()
+            if dropped[i]:
+                assert g.abs().max().item() == 0.0, (i, t)
+                continue
+            want = ref.grads[f"layers.{i}.{t}"].float()
+            if t in ("wo", "wdown"):  # d/dW of (W / p) x is (1 / p) times the rescaled model's
+                want = want / keep[i]
+            assert _rel(g, want) < 3e-2, (i, t, _rel(g, want))
+    assert _rel(eng.grads["embed"], ref.grads["embed"]) < 3e-2

@@ -272,3 +272,28 @@ def test_lora_merge_into_state_dict_matches_the_adapted_forward():
     ids = torch.randint(0, 64, (2, 9), generator=g)
     torch.testing.assert_close(llama_ref.forward(dict(merged.views), cfg, ids), llama_ref.forward(want, cfg, ids),
                                rtol=1e-5, atol=1e-5)
+
+
+def test_conv_bn_fusion_matches_conv_then_batch_norm():
+    from lora_kernel_b200.utils.model_ops import fuse_conv_bn
+    torch.manual_seed(0)
+    conv = torch.nn.Conv2d(6, 8, 3, padding=1)
+    bn = torch.nn.BatchNorm2d(8, eps=1e-5).eval()
+    bn.running_mean.uniform_(-1, 1)
+    bn.running_var.uniform_(0.5, 2.0)
+    bn.weight.data.uniform_(0.5, 1.5)
+    bn.bias.data.uniform_(-0.5, 0.5)
+    x = torch.randn(2, 6, 9, 9)
+    with torch.no_grad():
+        want = bn(conv(x))
+        w, b = fuse_conv_bn(conv.weight, conv.bias, bn.weight, bn.bias, bn.running_mean, bn.running_var, 1e-5)
+        got = torch.nn.functional.conv2d(x, w, b, padding=1)
+    assert torch.allclose(got, want, atol=1e-5, rtol=1e-5)
+    # a linear layer without bias folds the same way
+    lin = torch.nn.Linear(5, 4, bias=False)
+    bn1 = torch.nn.BatchNorm1d(4).eval()
+    bn1.running_mean.uniform_(-1, 1)
+    w, b = fuse_conv_bn(lin.weight, None, bn1.weight, bn1.bias, bn1.running_mean, bn1.running_var)
+    z = torch.randn(3, 5)
+    with torch.no_grad():
+        assert torch.allclose(torch.nn.functional.linear(z, w, b), bn1(lin(z)), atol=1e-5)
