@@ -238,7 +238,7 @@ def test_gradient_noise_units_and_seeding():
 
 def test_perf_regression_check(tmp_path):
     from lora_kernel_b200.utils.perf_check import compare, last_json, main
-    ref = last_json("profiles/bench_llama1b_2gpu.json")       # a log: JSON after torchrun banner lines
+    ref = last_json("profiles/bench_llama1b_2gpu_lk.json")
     assert ref["n_gpus"] == 2 and ref["value"] > 0
     new = dict(ref, value=ref["value"] * 0.97)
     assert compare(new, ref)["status"] == "ok"
@@ -248,7 +248,7 @@ def test_perf_regression_check(tmp_path):
     assert compare(hot, ref)["status"] == "not_comparable"
     p = tmp_path / "new.json"
     p.write_text("noise\n" + json.dumps(dict(ref, value=ref["value"] * 0.5)) + "\n")
-    assert main([str(p), "profiles/bench_llama1b_2gpu.json"]) == 1
+    assert main([str(p), "profiles/bench_llama1b_2gpu_lk.json"]) == 1
 
 
 def test_cpu_training_starts_from_pretrained_weights(tmp_path):
