@@ -22,11 +22,30 @@
 // (src/nn/transformer_blocks.cpp:50-97), FlashAttentionV2::forward
 // (include/nn/flash_attention.hpp:10-96, whose running-sum bug at :86 is not
 // reproduced) and GroupedQueryAttention (include/nn/attention_variants.hpp:59).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "lk_api.h"
 
 namespace lk {
+
+// 2^x on the FMA pipe (offloads the MUFU, which bounds the head_dim-64
+// softmax): round-to-nearest range reduction x = n + f, f in [-1/2, 1/2], by
+// adding 1.5 * 2^23; p(f) a cubic fitted here by iteratively reweighted least
+// squares to minimise the relative error of 2^f (max 9.1e-5 in fp32, far
+// below bf16's 2^-9 rounding of P); 2^n by adding n to the exponent bits.
+// Valid for x >= -126 (the caller clamps) and x < 128.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float n = t - 12582912.f;
+  const float f = x - n;
+  float p = fmaf(f, 0.055171433836221695f, 0.24261081218719482f);
+  p = fmaf(f, p, 0.6932609677314758f);
+  p = fmaf(f, p, 0.9999281167984009f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
 
 struct AttnFwdArgs {
   int B, S, Hq, Hkv;  // S = query length
@@ -41,6 +60,7 @@ struct AttnFwdArgs {
   float* lse;      // [B, Hq, S]
   int* status;
   int n_qtiles;  // CTAs per (head, batch): pairs of 128-query tiles
+  int emu;       // exponentials per 16 computed on the FMA pipe (0, 2 or 4)
 };
 
 template <int DH>
@@ -56,7 +76,7 @@ struct FwdCfg {
   static constexpr int THREADS = 320;    // TMA warp, MMA warp, two groups of 4 softmax warps
 };
 
-template <int DH>
+template <int DH, int EMU>
 __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_kv,
                     const AttnFwdArgs args) {
@@ -327,12 +347,22 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
       // over the first 64 columns of S (in key order, so no score is
       // overwritten before it is read); four independent partial sums
       float r4[4] = {0.f, 0.f, 0.f, 0.f};
+      // EMU of every 16 exponentials go to the FMA pipe on unmasked tiles (masked
+      // -inf scores need the exact 0 of ex2)
+      const bool emu = EMU > 0 && !need_mask;
       auto emit = [&](const uint32_t (&x)[32], int c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(x[e]), args.sl2, -mb));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(x[e + 1]), args.sl2, -mb));
+          const float a0 = fmaf(__uint_as_float(x[e]), args.sl2, -mb);
+          const float a1 = fmaf(__uint_as_float(x[e + 1]), args.sl2, -mb);
+          const float p0 = fast_exp2(a0);
+          float p1;
+          if (((e >> 1) & 7) < EMU) {
+            p1 = emu ? exp2_fma(a1) : fast_exp2(a1);
+          } else {
+            p1 = fast_exp2(a1);
+          }
           r4[(e >> 1) & 3] += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
@@ -444,7 +474,12 @@ static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
   a.lse = d.lse;
   a.status = d.status;
   a.n_qtiles = cdiv(d.S, 256);  // pairs of 128-query tiles, one per CTA
-  auto k = attn_fwd_kernel<DH>;
+  static const int emu = [] {
+    const char* e = getenv("LK_ATTN_EXP_EMU");
+    return e ? atoi(e) : 0;
+  }();
+  a.emu = emu;
+  auto k = a.emu >= 4 ? attn_fwd_kernel<DH, 4> : a.emu >= 2 ? attn_fwd_kernel<DH, 2> : attn_fwd_kernel<DH, 0>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   k<<<a.n_qtiles * d.Hq * d.B, C::THREADS, C::SMEM, s>>>(tm, tkv, a);
   return check_launch("attn_fwd");

@@ -44,7 +44,7 @@ namespace lk {
 int& gemm_pair_mode() {
   static int mode = [] {
     const char* e = getenv("LK_GEMM_PAIR");
-    return e ? atoi(e) : 0;
+    return e ? atoi(e) : 1;
   }();
   return mode;
 }

@@ -87,7 +87,7 @@ typedef struct LkGemmDesc {
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
 // CTA-pair tiles (tcgen05.mma.cta_group::2, 256 x 256) for plain GEMMs: 0 off, 1 on
-// (also LK_GEMM_PAIR in the environment at the first GEMM)
+// (the default; LK_GEMM_PAIR in the environment at the first GEMM overrides it)
 void lk_gemm_set_pair(int mode);
 unsigned long long lk_gemm_pair_count(void);  // GEMMs that took the CTA-pair path so far
 // Encode the K18 store tensor maps of `world` receive buffers (bf16 [rows, cols],
