@@ -369,6 +369,108 @@ void quant_128x128(torch::Tensor w, torch::Tensor q, c10::optional<torch::Tensor
                          qt.has_value() ? qt->data_ptr() : nullptr, scale.data_ptr<float>(), stream()));
 }
 
+// K2, MX form: hardware block-scaled fp8 GEMM (UE8M0 SF tiles) and its quantisers.
+static void mx_operand(const torch::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kUInt8 && t.dim() == 2 && t.stride(1) == 1, what,
+              " must be a row-major uint8 (fp8 bits) matrix");
+}
+
+static int64_t mx_sf_bytes(int64_t row_tiles, int64_t K) { return row_tiles * (K / 128) * 512; }
+
+void gemm_mxf8(torch::Tensor a8, torch::Tensor sfa, int64_t a_fmt, torch::Tensor b8, torch::Tensor sfb,
+               int64_t b_fmt, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> resid,
+               torch::Tensor status, int64_t rank, int64_t world, c10::optional<torch::Tensor> ag_rows,
+               c10::optional<torch::Tensor> ag_sf, int64_t rows_per_rank, c10::optional<torch::Tensor> count,
+               c10::optional<torch::Tensor> rptrs, int64_t rs_rows, int64_t ldd) {
+  const c10::cuda::CUDAGuard g(a8.device());
+  mx_operand(a8, "gemm_mxf8: a8");
+  mx_operand(b8, "gemm_mxf8: b8");
+  TORCH_CHECK(a8.size(1) == b8.size(1), "gemm_mxf8: K mismatch");
+  TORCH_CHECK(sfa.is_cuda() && sfa.is_contiguous() && sfa.scalar_type() == torch::kUInt8, "gemm_mxf8: sfa uint8");
+  TORCH_CHECK(sfb.is_cuda() && sfb.is_contiguous() && sfb.scalar_type() == torch::kUInt8, "gemm_mxf8: sfb uint8");
+  LkGemmMxf8Desc d{};
+  d.a = a8.data_ptr();
+  d.a_ld = a8.stride(0);
+  d.b = b8.data_ptr();
+  d.b_ld = b8.stride(0);
+  d.M = (int)a8.size(0);
+  d.N = (int)b8.size(0);
+  d.K = (int)a8.size(1);
+  d.a_fmt = (int)a_fmt;
+  d.b_fmt = (int)b_fmt;
+  TORCH_CHECK(sfa.numel() >= mx_sf_bytes((d.M + 127) / 128, d.K), "gemm_mxf8: sfa holds ceil(M/128) row tiles");
+  TORCH_CHECK(sfb.numel() >= mx_sf_bytes(2 * ((d.N + 255) / 256), d.K),
+              "gemm_mxf8: sfb holds 2 ceil(N/256) row tiles");
+  d.sfa = sfa.data_ptr();
+  d.sfb = sfb.data_ptr();
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  d.rank = (int)rank;
+  d.world = (int)world;
+  if (out.has_value()) {
+    need(*out, "out", torch::kBFloat16);
+    TORCH_CHECK(out->size(0) == d.M && out->size(1) == d.N && out->stride(1) == 1, "gemm_mxf8: out [M, N]");
+    d.d = out->data_ptr();
+    d.ldd = out->stride(0);
+  }
+  if (resid.has_value()) {
+    need(*resid, "resid", torch::kBFloat16);
+    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == d.N && resid->stride(1) == 1, "gemm_mxf8: resid");
+    d.r = resid->data_ptr();
+    d.ldr = resid->stride(0);
+  }
+  if (ag_rows.has_value()) {
+    TORCH_CHECK(ag_sf.has_value() && count.has_value() && out.has_value(), "gemm_mxf8 ag: missing args");
+    d.ag_rows = reinterpret_cast<const void* const*>(ag_rows->data_ptr());
+    d.ag_sf = reinterpret_cast<const void* const*>(ag_sf->data_ptr());
+    d.ag_rows_per_rank = (int)rows_per_rank;
+    d.ag_count = count->data_ptr<int>();
+  }
+  if (rptrs.has_value()) {
+    d.rptrs = reinterpret_cast<void* const*>(rptrs->data_ptr());
+    d.rs_rows = (int)rs_rows;
+    d.ldd = ldd;
+  } else {
+    TORCH_CHECK(out.has_value(), "gemm_mxf8: out required");
+  }
+  check(lk_gemm_mxf8(&d, stream()));
+}
+
+void quant_mx_rows(torch::Tensor x, int64_t fmt, torch::Tensor q, torch::Tensor sf, int64_t rows_pad) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need(x, "x", torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "quant_mx_rows: x row-major");
+  TORCH_CHECK(q.scalar_type() == torch::kUInt8 && q.stride(1) == 1 && q.size(0) == x.size(0) &&
+                  q.size(1) == x.size(1), "quant_mx_rows: q");
+  TORCH_CHECK(sf.is_contiguous() && sf.scalar_type() == torch::kUInt8 &&
+                  sf.numel() >= mx_sf_bytes(rows_pad / 128, x.size(1)), "quant_mx_rows: sf");
+  check(lk_quant_mx_rows(x.data_ptr(), x.stride(0), (int)x.size(0), (int)rows_pad, (int)x.size(1), (int)fmt,
+                         q.data_ptr(), q.stride(0), sf.data_ptr(), stream()));
+}
+
+void quant_mx_128x128(torch::Tensor w, torch::Tensor q, torch::Tensor sf, torch::Tensor scale,
+                      c10::optional<torch::Tensor> qt, c10::optional<torch::Tensor> sft) {
+  const c10::cuda::CUDAGuard g(w.device());
+  need(w, "w", torch::kBFloat16);
+  TORCH_CHECK(w.dim() == 2 && w.stride(1) == 1, "quant_mx_128x128: w row-major");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == torch::kUInt8 && q.numel() == w.numel(), "quant_mx_128x128: q");
+  TORCH_CHECK(sf.is_contiguous() && sf.scalar_type() == torch::kUInt8 && sf.numel() >= mx_sf_bytes((N + 127) / 128, K),
+              "quant_mx_128x128: sf");
+  need_contig(scale, "scale", torch::kFloat32);
+  TORCH_CHECK(scale.numel() >= ((N + 127) / 128) * (K / 128), "quant_mx_128x128: scale");
+  TORCH_CHECK(qt.has_value() == sft.has_value(), "quant_mx_128x128: qt and sft together");
+  if (qt.has_value()) {
+    TORCH_CHECK(qt->is_contiguous() && qt->scalar_type() == torch::kUInt8 && qt->numel() == w.numel(),
+                "quant_mx_128x128: qt");
+    TORCH_CHECK(sft->is_contiguous() && sft->scalar_type() == torch::kUInt8 &&
+                    sft->numel() >= mx_sf_bytes(K / 128, N), "quant_mx_128x128: sft");
+  }
+  check(lk_quant_mx_128x128(w.data_ptr(), w.stride(0), (int)N, (int)K, q.data_ptr(), sf.data_ptr(),
+                            scale.data_ptr<float>(), qt.has_value() ? qt->data_ptr() : nullptr,
+                            sft.has_value() ? sft->data_ptr() : nullptr, stream()));
+}
+
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
 void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
             c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> y,
@@ -1008,6 +1110,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8_comm", &gemm_fp8_comm);
   m.def("dequant_1x128", &dequant_1x128);
   m.def("quant_128x128", &quant_128x128);
+  m.def("gemm_mxf8", &gemm_mxf8);
+  m.def("quant_mx_rows", &quant_mx_rows);
+  m.def("quant_mx_128x128", &quant_mx_128x128);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);

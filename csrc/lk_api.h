@@ -188,6 +188,50 @@ int lk_dequant_1x128(const void* q, int M, int K, int fmt, const float* scale, v
 // w bf16 [N, K] -> q e4m3 [N, K], optional qt = q^T [K, N], scale [ceil(N/128)][K/128]
 int lk_quant_128x128(const void* w, int64_t ldw, int N, int K, void* q, void* qt, float* scale, cudaStream_t s);
 
+// ----------------------------------- K2, MX form: hardware block-scaled fp8 GEMM
+// D[M, N] (bf16) = sum_k 2^ea[m, k/32] 2^eb[n, k/32] A8[m, k] B8[n, k] [+ R].
+// A8 [M, K], B8 [N, K] fp8 bits (fmt 0 e4m3, 1 e5m2), K % 128 == 0.  Scales are
+// UE8M0 bytes in "SF tiles": an operand of R rows has ceil(R/128) x K/128 tiles
+// of 512 bytes, tile (rt, kb) at (rt K/128 + kb) 512, row r / 32-wide block j at
+// (r % 32) 16 + ((r % 128) / 32) 4 + j inside it.  sfa covers ceil(M/128) row
+// tiles, sfb 2 ceil(N/256) (rows past N: any finite exponent).
+typedef struct LkGemmMxf8Desc {
+  const void* a;
+  int64_t a_ld;
+  const void* b;
+  int64_t b_ld;
+  int M, N, K, a_fmt, b_fmt;
+  const void* sfa;
+  const void* sfb;
+  void* d;
+  int64_t ldd;
+  const void* r;  // optional residual (bf16, pitch ldr)
+  int64_t ldr;
+  int* status;
+  // Fused collectives (at most one, e4m3 operands): all-gather of A - every
+  // rank's ag_rows_per_rank rows (ag_rows[p], pitch K) and SF tiles (ag_sf[p])
+  // are copied into a / sfa (DEVICE pointer arrays of `world` entries; ag_count
+  // int scratch [M/128]); or reduce-scatter epilogue - bf16 row m goes to
+  // rptrs[m / rs_rows] at row rank * rs_rows + m % rs_rows (pitch ldd).
+  const void* const* ag_rows;
+  const void* const* ag_sf;
+  int ag_rows_per_rank;
+  int* ag_count;
+  void* const* rptrs;
+  int rs_rows;
+  int rank, world;
+} LkGemmMxf8Desc;
+int lk_gemm_mxf8(const LkGemmMxf8Desc* desc, cudaStream_t stream);
+// x bf16 [M, K] -> q fp8 [M, K] with one power-of-two scale per row and 128-wide
+// K block (UE8M0 SF tiles over rows_pad rows; rows >= M get exponent 0)
+int lk_quant_mx_rows(const void* x, int64_t ldx, int M, int rows_pad, int K, int fmt, void* q, int64_t ldq,
+                     void* sf, cudaStream_t s);
+// w bf16 [N, K] -> q e4m3 [N, K] with one power-of-two scale per 128 x 128 block:
+// SF tiles sf (ceil(N/128) row tiles), fp32 scales [ceil(N/128)][K/128], and
+// optionally qt = q^T [K, N] with its SF tiles sft (K/128 row tiles x N/128)
+int lk_quant_mx_128x128(const void* w, int64_t ldw, int N, int K, void* q, void* sf, float* scale, void* qt,
+                        void* sft, cudaStream_t s);
+
 // --------------------------------------------- K18 owner-side slot reduction
 typedef struct LkRsSumDesc {
   const void* recv;   // [world * rows, ld_recv] bf16: slot s = rank s's partial

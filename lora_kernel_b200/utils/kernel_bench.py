@@ -107,6 +107,34 @@ def bench_fp8(shapes, iters):
                           "peak_src": pk["src"]}), flush=True)
 
 
+def bench_mxf8(shapes, iters):
+    """K2 in MX form (tcgen05 block-scaled fp8, power-of-two scales) against the
+    bf16 tcgen05 GEMM and cuBLAS bf16 on the same shape; quantisation outside the
+    timed region (timed on its own as act_quant_ms)."""
+    from lora_kernel_b200.ops import fp8 as F
+    from lora_kernel_b200.ops.gemm import gemm
+    pk = peaks()
+    for (M, N, K) in shapes:
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        w8 = F.MXWeight(w, transpose=False)
+        q, sf = F.quantize_mx(x)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        t8 = time_fn(lambda: F.gemm_mxf8(q, sf, w8.q, w8.sf, out=out), iters)
+        tq = time_fn(lambda: F.quantize_mx(x), iters)
+        tb = time_fn(lambda: gemm(x, w, out), iters)
+        tc = time_fn(lambda: torch.matmul(x, w.t(), out=out), iters)
+        fl = 2.0 * M * N * K
+        print(json.dumps({"kernel": "gemm_mxf8", "M": M, "N": N, "K": K,
+                          "ms": round(t8, 4), "tflops": round(fl / t8 / 1e9, 1),
+                          "act_quant_ms": round(tq, 4),
+                          "bf16_tc_ms": round(tb, 4), "cublas_bf16_ms": round(tc, 4),
+                          "speedup_vs_bf16_tc": round(tb / t8, 3),
+                          "speedup_vs_cublas_bf16": round(tc / t8, 3),
+                          "frac_of_bf16_peak": round(fl / t8 / 1e9 / pk["bf16_tflops"], 3),
+                          "peak_src": pk["src"]}), flush=True)
+
+
 def bench_norm(iters):
     from lora_kernel_b200.ops.norm import rmsnorm_bwd, rmsnorm_fwd
     pk = peaks()
@@ -183,6 +211,9 @@ def main():
     if "fp8" in which:
         bench_fp8([(8192, 8192, 8192), (8192, 3584, 4096), (8192, 4096, 1792), (8192, 768, 4096)]
                   if not args.small else [(8192, 8192, 8192)], args.iters)
+    if "mx" in which:
+        bench_mxf8([(8192, 8192, 8192), (8192, 3584, 4096), (8192, 4096, 1792), (8192, 768, 4096),
+                    (8192, 4096, 512)] if not args.small else [(4096, 4096, 4096)], args.iters)
     if "norm" in which:
         bench_norm(args.iters)
     if "attn" in which:

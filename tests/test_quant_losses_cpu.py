@@ -297,3 +297,19 @@ def test_conv_bn_fusion_matches_conv_then_batch_norm():
     z = torch.randn(3, 5)
     with torch.no_grad():
         assert torch.allclose(torch.nn.functional.linear(z, w, b), bn1(lin(z)), atol=1e-5)
+
+
+def test_mx_scale_tiles_round_trip_cpu():
+    """The SF-tile layout helpers: exponents -> tiles -> exponents is exact, and a
+    row's four 32-wide blocks of one 128 block sit in one 4-byte word."""
+    import torch
+    from lora_kernel_b200.ops import fp8 as F
+    g = torch.Generator().manual_seed(0)
+    for rows, K, mult in [(128, 128, 128), (200, 512, 128), (300, 256, 256)]:
+        e = torch.randint(-20, 21, (rows, K // 32), generator=g, dtype=torch.int32)
+        sf = F.exponents_to_sf(e, mult)
+        assert sf.numel() == F.sf_tile_bytes(rows, K, mult)
+        assert torch.equal(F.sf_to_exponents(sf, rows, K), e)
+    idx = F._sf_index(256, 256, "cpu")
+    assert idx[37, 5].item() == ((0 * 2 + 1) * 512 + 5 * 16 + 1 * 4 + 1)
+    assert idx[200, 0].item() == ((1 * 2 + 0) * 512 + 8 * 16 + 2 * 4 + 0)
