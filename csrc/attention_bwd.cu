@@ -510,34 +510,42 @@ __global__ void __launch_bounds__(64 + 32 * bwd_softmax_warps<DH>(), 1)
   }
 }
 
-// D[b, h, q] = scale * sum_d dO[q, h, d] * O[q, h, d]  and  L2 = LSE * log2(e)
-// (one warp per (row, head)): both pre-scaled so the softmax backward spends
-// one FFMA per element on each instead of a multiply and a subtract.
+// D[b, h, q] = scale * sum_d dO[q, h, d] * O[q, h, d]  and  L2 = LSE * log2(e):
+// both pre-scaled so the softmax backward spends one FFMA per element on each
+// instead of a multiply and a subtract.  DH/8 lanes per (row, head), 16-byte
+// loads; the same lanes zero the (row, head)'s fp32 dQ accumulator, which the
+// main kernel reduce-adds into.
 template <int DH>
-__global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
-                                    const __nv_bfloat16* __restrict__ dout, int64_t lddo,
-                                    float* __restrict__ Dvec, const float* __restrict__ lse,
-                                    float* __restrict__ l2, float scale, int B, int S, int Hq,
-                                    float* __restrict__ dq_acc) {
-  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(256) attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
+                                                           const __nv_bfloat16* __restrict__ dout, int64_t lddo,
+                                                           float* __restrict__ Dvec, const float* __restrict__ lse,
+                                                           float* __restrict__ l2, float scale, int B, int S, int Hq,
+                                                           float* __restrict__ dq_acc) {
+  constexpr int LPR = DH / 8;  // lanes per (row, head)
+  const int64_t gt = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t w = gt / LPR;  // (row, head) index
+  const int sub = (int)(gt % LPR);
   const int64_t total = (int64_t)B * S * Hq;
-  if (w >= total) return;
-  const int h = (int)(w % Hq);
-  const int64_t row = w / Hq;  // b*S + s
-  const __nv_bfloat16* op = o + row * ldo + h * DH;
-  const __nv_bfloat16* dp = dout + row * lddo + h * DH;
+  const bool ok = w < total;
+  const int h = ok ? (int)(w % Hq) : 0;
+  const int64_t row = ok ? w / Hq : 0;  // b*S + s
   float s = 0.f;
-  for (int d = lane * 2; d < DH; d += 64) {
-    const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(op + d));
-    const float2 c = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dp + d));
-    s += a.x * c.x + a.y * c.y;
+  if (ok) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + row * ldo + h * DH + sub * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(dout + row * lddo + h * DH + sub * 8);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = unpack_bf16x2(aw[e]), y = unpack_bf16x2(cw[e]);
+      s += x.x * y.x + x.y * y.y;
+    }
+    float4* dqr = reinterpret_cast<float4*>(dq_acc + row * (int64_t)Hq * DH + h * DH + sub * 8);
+    dqr[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dqr[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  // zero this (row, head)'s fp32 dQ accumulator (the main kernel reduce-adds into it)
-  float* dqr = dq_acc + row * (int64_t)Hq * DH + h * DH;
-  for (int d = lane * 4; d < DH; d += 128) *reinterpret_cast<float4*>(dqr + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-  s = warp_sum(s);
-  if (lane == 0) {
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (ok && sub == 0) {
     const int bb = (int)(row / S), q = (int)(row % S);
     const int64_t idx = ((int64_t)bb * Hq + h) * S + q;
     Dvec[idx] = s * scale;
@@ -567,8 +575,8 @@ static int launch_bwd(const LkAttnBwdDesc& d, cudaStream_t s) {
   float* l2 = d.dvec + lk_attn_dvec_half(d.B, d.Hq, d.S);
   // D = rowsum(dO * O)
   {
-    const int64_t warps = T * d.Hq;
-    attn_bwd_dot_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
+    const int64_t threads = T * d.Hq * (DH / 8);
+    attn_bwd_dot_kernel<DH><<<(unsigned)cdiv(threads, 256), 256, 0, s>>>(
         (const __nv_bfloat16*)d.o, d.ld_o, (const __nv_bfloat16*)d.dout, d.ld_do, d.dvec, d.lse, l2, d.scale,
         d.B, d.S, d.Hq, d.dq_acc);
     if (check_launch("attn_bwd_dot")) return -1;

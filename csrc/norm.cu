@@ -78,33 +78,69 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(
   }
 }
 
-// Backward: one warp per row, grid-stride over rows, two passes over the row
-// (the second hits L1/L2).  dgamma partials accumulate per warp in shared
-// memory (float4 read-modify-write); each block then writes one partial row to
+// Backward: one warp per row, 4 warps per block, grid-stride over rows.  Rows
+// up to 2048 wide (VPT <= 8) come into registers with one pass of loads (every
+// load of the row in flight at once); wider rows read x and dy again in the
+// second pass (L1 hits).  dres is fetched into L2 during the first pass and the
+// warp's next row while the current one is processed, so the loads that wait are
+// L2 hits.  dgamma partial sums accumulate per warp in shared memory (float4
+// read-modify-write); at the end each block writes one partial row to
 // partial[blockIdx.x, :] (fp32 scratch, gridDim.x x D), summed by colsum_kernel.
+constexpr int NORM_BWD_WARPS = 4;
+
 template <int VPT>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
+__global__ void __launch_bounds__(32 * NORM_BWD_WARPS) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ rstd,
     const __nv_bfloat16* dres, __nv_bfloat16* dx, float* __restrict__ partial, int M, int D) {
-  extern __shared__ float red[];  // [warps][D]
-  const int warps = blockDim.x >> 5;
+  constexpr bool HOLD = VPT <= 8;
+  constexpr int NH = HOLD ? VPT : 1;  // row registers
+  extern __shared__ float red[];      // [warps][D]
   const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   float* my = red + (int64_t)w * D;
   for (int c = lane; c < D; c += 32) my[c] = 0.f;
   __syncwarp();
-  for (int row = blockIdx.x * warps + w; row < M; row += gridDim.x * warps) {
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  for (int row = blockIdx.x * NORM_BWD_WARPS + w; row < M; row += gridDim.x * NORM_BWD_WARPS) {
     const float rs = rstd[row];
     const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * D);
     const uint4* yr = reinterpret_cast<const uint4*>(dy + (int64_t)row * D);
-    const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+    const uint4* rr = dres ? reinterpret_cast<const uint4*>(dres + (int64_t)row * D) : nullptr;
+    uint4 xa[NH], ya[NH];
+    if constexpr (HOLD) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        xa[i] = xr[i * 32 + lane];
+        ya[i] = yr[i * 32 + lane];
+      }
+    }
+    {
+      // the warp's next row into L2 (one prefetch per 128-byte line)
+      const int nrow = row + gridDim.x * NORM_BWD_WARPS;
+      if (nrow < M) {
+        const int64_t o = (int64_t)nrow * D;
+        for (int c = lane * 8; c < VPT * 32; c += 256) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(x + o) + c));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(dy + o) + c));
+          if (dres) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(dres + o) + c));
+        }
+      }
+    }
     float dot = 0.f;
-    // first pass: every load of the row in flight at once for widths <= 2048
-#pragma unroll(VPT <= 8 ? VPT : 2)
+#pragma unroll(HOLD ? VPT : 4)
     for (int i = 0; i < VPT; ++i) {
       const int c = i * 32 + lane;
-      const uint4 a = xr[c], b = yr[c], g = gr[c];
+      uint4 a, b;
+      if constexpr (HOLD) {
+        a = xa[i];
+        b = ya[i];
+      } else {
+        a = xr[c];
+        b = yr[c];
+      }
+      if (rr && (lane & 7) == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(rr + c));
+      const uint4 g = gr[c];
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
       const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
@@ -115,17 +151,26 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
       }
     }
     dot = warp_sum(dot) * rs / (float)D;  // mean(dy*gamma*xhat)
-#pragma unroll 2
+    uint4* dxr = reinterpret_cast<uint4*>(dx + (int64_t)row * D);
+#pragma unroll(HOLD ? VPT : 4)
     for (int i = 0; i < VPT; ++i) {
       const int c = i * 32 + lane;
-      const uint4 a = xr[c], b = yr[c], g = gr[c];
-      const uint4 r = dres ? reinterpret_cast<const uint4*>(dres + (int64_t)row * D)[c] : make_uint4(0u, 0u, 0u, 0u);
+      uint4 a, b;
+      if constexpr (HOLD) {
+        a = xa[i];
+        b = ya[i];
+      } else {
+        a = xr[c];
+        b = yr[c];
+      }
+      const uint4 r = rr ? rr[c] : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 g = gr[c];
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
       const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
       const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
-      float4* acc4 = reinterpret_cast<float4*>(my + c * 8);
-      const float4 a0 = acc4[0], a1 = acc4[1];
+      float4* a4 = reinterpret_cast<float4*>(my + c * 8);
+      const float4 a0 = a4[0], a1 = a4[1];
       float accv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       uint32_t o[4];
 #pragma unroll
@@ -138,15 +183,16 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
         o[e] = pack_bf16x2(rs * (yf.x * gf.x - xh0 * dot) + rf.x,
                            rs * (yf.y * gf.y - xh1 * dot) + rf.y);
       }
-      acc4[0] = make_float4(accv[0], accv[1], accv[2], accv[3]);
-      acc4[1] = make_float4(accv[4], accv[5], accv[6], accv[7]);
-      reinterpret_cast<uint4*>(dx + (int64_t)row * D)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      a4[0] = make_float4(accv[0], accv[1], accv[2], accv[3]);
+      a4[1] = make_float4(accv[4], accv[5], accv[6], accv[7]);
+      dxr[c] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
   __syncthreads();
   for (int col = threadIdx.x; col < D; col += blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < warps; ++k) s += red[k * D + col];
+#pragma unroll
+    for (int k = 0; k < NORM_BWD_WARPS; ++k) s += red[k * D + col];
     partial[(int64_t)blockIdx.x * D + col] = s;
   }
 }
@@ -194,12 +240,12 @@ static void fwd_launch(const LkNormFwdDesc& d, cudaStream_t s) {
 
 template <int VPT>
 static void bwd_launch(const LkNormBwdDesc& d, int grid, cudaStream_t s) {
-  const int smem = 8 * d.D * sizeof(float);
+  const int smem = NORM_BWD_WARPS * d.D * (int)sizeof(float);
   auto k = rmsnorm_bwd_kernel<VPT>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  k<<<grid, 256, smem, s>>>((const __nv_bfloat16*)d.dy, (const __nv_bfloat16*)d.x,
-                            (const __nv_bfloat16*)d.gamma, d.rstd, (const __nv_bfloat16*)d.dres,
-                            (__nv_bfloat16*)d.dx, d.partial, d.M, d.D);
+  k<<<grid, 32 * NORM_BWD_WARPS, smem, s>>>(
+      (const __nv_bfloat16*)d.dy, (const __nv_bfloat16*)d.x, (const __nv_bfloat16*)d.gamma, d.rstd,
+      (const __nv_bfloat16*)d.dres, (__nv_bfloat16*)d.dx, d.partial, d.M, d.D);
 }
 
 int norm_bwd_grid(int M) {
