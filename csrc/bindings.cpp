@@ -71,16 +71,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
   d.M = (int)a.size(0);
   d.N = (int)b.size(0);
   d.K = (int)a.size(1);
-  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == d.M && out.size(1) == d.N &&
+  // the SwiGLU-backward epilogue writes gate|up gradients: [M, 2N]
+  const int64_t out_cols = epi == LK_EPI_SWIGLU_BWD ? 2 * (int64_t)d.N : d.N;
+  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == d.M && out.size(1) == out_cols &&
                   out.stride(1) == 1,
-              "gemm: out must be row-major [M, N]");
+              "gemm: out must be row-major [M, N] ([M, 2N] for swiglu_bwd)");
   const bool f32 = epi == LK_EPI_F32 || epi == LK_EPI_F32_ACC;
   TORCH_CHECK(out.scalar_type() == (f32 ? torch::kFloat32 : torch::kBFloat16), "gemm: out dtype");
   d.d = out.data_ptr();
   d.ldd = out.stride(0);
   if (resid.has_value()) {
     need(*resid, "resid", torch::kBFloat16);
-    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == d.N && resid->stride(1) == 1, "gemm: resid shape");
+    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == out_cols && resid->stride(1) == 1, "gemm: resid shape");
     d.r = resid->data_ptr();
     d.ldr = resid->stride(0);
   }
@@ -469,6 +471,17 @@ void quant_mx_128x128(torch::Tensor w, torch::Tensor q, torch::Tensor sf, torch:
   check(lk_quant_mx_128x128(w.data_ptr(), w.stride(0), (int)N, (int)K, q.data_ptr(), sf.data_ptr(),
                             scale.data_ptr<float>(), qt.has_value() ? qt->data_ptr() : nullptr,
                             sft.has_value() ? sft->data_ptr() : nullptr, stream()));
+}
+
+void dequant_mx_rows(torch::Tensor q, int64_t fmt, torch::Tensor sf, torch::Tensor x) {
+  const c10::cuda::CUDAGuard g(q.device());
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == torch::kUInt8 && q.dim() == 2, "dequant_mx_rows: q");
+  TORCH_CHECK(sf.is_contiguous() && sf.scalar_type() == torch::kUInt8 &&
+                  sf.numel() >= mx_sf_bytes((q.size(0) + 127) / 128, q.size(1)), "dequant_mx_rows: sf");
+  need(x, "x", torch::kBFloat16);
+  TORCH_CHECK(x.size(0) == q.size(0) && x.size(1) == q.size(1) && x.stride(1) == 1, "dequant_mx_rows: x");
+  check(lk_dequant_mx_rows(q.data_ptr(), (int)q.size(0), (int)q.size(1), (int)fmt, sf.data_ptr(), x.data_ptr(),
+                           x.stride(0), stream()));
 }
 
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
@@ -1002,7 +1015,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor block_tables, torch::Tensor ctx_lens, int64_t block_size, int64_t Hq,
                       int64_t Hkv, int64_t Dh, double scale, int64_t split_len, int64_t num_splits,
                       c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml,
-                      torch::Tensor out, int64_t kv_dtype) {
+                      torch::Tensor out, int64_t kv_dtype, c10::optional<torch::Tensor> status) {
   const c10::cuda::CUDAGuard g(q.device());
   need(q, "q", torch::kBFloat16);
   need(out, "out", torch::kBFloat16);
@@ -1020,19 +1033,22 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   d.part_o = optp<float>(part_o); d.part_ml = optp<float>(part_ml);
   d.out = out.data_ptr(); d.ldo = out.stride(0);
   d.kv_dtype = (int)kv_dtype;
+  d.num_blocks = (int)(k_cache.numel() / (Hkv * Dh) / block_size);
+  d.status = optp<int>(status);
   check(lk_decode_attention(&d, stream()));
 }
 
 void kv_gather(torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> k_scale,
                c10::optional<torch::Tensor> v_scale, torch::Tensor slots, int64_t Hkv, int64_t Dh,
-               torch::Tensor out, int64_t kv_dtype) {
+               torch::Tensor out, int64_t kv_dtype, c10::optional<torch::Tensor> status) {
   const c10::cuda::CUDAGuard g(out.device());
   need_contig(slots, "slots", torch::kInt32);
   need(out, "out", torch::kBFloat16);
   TORCH_CHECK(out.stride(1) == 1 && out.size(0) >= slots.numel(), "kv_gather: out shape");
-  check(lk_kv_gather(k_cache.data_ptr(), v_cache.data_ptr(), optp<float>(k_scale), optp<float>(v_scale),
-                     slots.data_ptr<int>(), (int)slots.numel(), (int)Hkv, (int)Dh, out.data_ptr(), out.stride(0),
-                     (int)kv_dtype, stream()));
+  check(lk_kv_gather_checked(k_cache.data_ptr(), v_cache.data_ptr(), optp<float>(k_scale), optp<float>(v_scale),
+                             slots.data_ptr<int>(), (int)slots.numel(), (int)Hkv, (int)Dh, out.data_ptr(),
+                             out.stride(0), (int)kv_dtype, (int)(k_cache.numel() / (Hkv * Dh)),
+                             optp<int>(status), stream()));
 }
 
 void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, int64_t seed, torch::Tensor out_tok,
@@ -1113,6 +1129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("quant_mx_rows", &quant_mx_rows);
   m.def("quant_mx_128x128", &quant_mx_128x128);
+  m.def("dequant_mx_rows", &dequant_mx_rows);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);

@@ -22,6 +22,16 @@
 
 namespace lk {
 
+// Bounds checks of data-dependent indices (block-table entries, cache slots,
+// positions): compiled only into the debug build (-DLK_BOUNDS_CHECK, module
+// _C_debug), where a failed check records `code` in *status and the caller
+// skips the access.  In the regular build LK_BOUNDS(...) is the constant true.
+#ifdef LK_BOUNDS_CHECK
+#define LK_BOUNDS(ok, status, code) (::lk::bounds_ok((ok), (status), (code)))
+#else
+#define LK_BOUNDS(ok, status, code) (true)
+#endif
+
 // Status codes written to the device status word (int32) on failure.
 enum Status : int {
   LK_OK = 0,
@@ -32,6 +42,12 @@ enum Status : int {
   LK_ERR_BAD_INDEX = 5,       // an index (token id, block id) was out of range
   LK_ERR_TIMEOUT_DRAIN = 6,   // copies in flight did not drain on abort
 };
+
+// A failed bounds check: record `code` (first failure wins) and report it.
+__device__ __forceinline__ bool bounds_ok(bool ok, int* status, int code) {
+  if (!ok && status) atomicCAS(status, 0, code);
+  return ok;
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

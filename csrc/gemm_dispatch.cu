@@ -26,6 +26,7 @@ extern "C" int lk_gemm(const LkGemmDesc* g, cudaStream_t stream) {
       return gemm_dispatch_f32(*g, stream);
     case LK_EPI_BF16_RESID:
     case LK_EPI_SWIGLU:
+    case LK_EPI_SWIGLU_BWD:
       return gemm_dispatch_fused(*g, stream);
     default:
       return fail("lk_gemm: unknown epilogue");

@@ -39,6 +39,7 @@ enum GemmEpi : int {
   EPI_BF16_RESID = 3,  // D(bf16) = alpha*acc + R(bf16) (residual add; D may alias R)
   EPI_SWIGLU = 4,      // D(bf16) = acc (gate|up), H(bf16) = silu(gate) * up
   EPI_REMOTE = 5,      // K18: bf16 tile stored into the owner rank's receive slot (peer memory)
+  EPI_SWIGLU_BWD = 6,  // acc = dh; D(bf16 [M, 2N] gate|up grads) from R (gate|up), dh not stored
 };
 
 struct GemmArgs {
@@ -637,7 +638,35 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
           tc_wait_ld();
           if (!row_ok) continue;
           const int col0 = tn * BN + c * 32;
-          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
+          if constexpr (EPI == EPI_SWIGLU_BWD) {
+            // columns [col0, col0 + 32) of dh lie in one 128-wide block b: gate
+            // at 256 b + j, up at 256 b + 128 + j of the gate|up row
+            if (col0 < args.N) {
+              const int64_t gcol = (int64_t)(col0 >> 7) * 256 + (col0 & 127);
+              const __nv_bfloat16* grow = args.R + (int64_t)row * args.ldr + gcol;
+              __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + gcol;
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const uint4 gv = *reinterpret_cast<const uint4*>(grow + v * 8);
+                const uint4 uv = *reinterpret_cast<const uint4*>(grow + 128 + v * 8);
+                const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+                const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+                uint32_t dg[4], du[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 g = unpack_bf16x2(gw[e]), u = unpack_bf16x2(uw[e]);
+                  const float d0 = __uint_as_float(r[v * 8 + 2 * e]) * alpha;
+                  const float d1 = __uint_as_float(r[v * 8 + 2 * e + 1]) * alpha;
+                  const float s0 = 1.0f / (1.0f + __expf(-g.x)), s1 = 1.0f / (1.0f + __expf(-g.y));
+                  dg[e] = pack_bf16x2(d0 * u.x * s0 * (1.f + g.x * (1.f - s0)),
+                                      d1 * u.y * s1 * (1.f + g.y * (1.f - s1)));
+                  du[e] = pack_bf16x2(d0 * g.x * s0, d1 * g.y * s1);
+                }
+                *reinterpret_cast<uint4*>(drow + v * 8) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+                *reinterpret_cast<uint4*>(drow + 128 + v * 8) = make_uint4(du[0], du[1], du[2], du[3]);
+              }
+            }
+          } else if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
             __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {

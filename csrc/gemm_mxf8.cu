@@ -409,31 +409,47 @@ __device__ __forceinline__ int64_t mx_sf_offset(int row, int kb, int nkb) {
   return ((int64_t)(row >> 7) * nkb + kb) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4;
 }
 
-// Activations / gradients, 1 x 128 blocks: one warp per (row, K block).  Rows
-// [M, rows_pad) get exponent 0 (byte 127) in the SF tiles and no data.
+// Activations / gradients, 1 x 128 blocks: a half-warp per (row, K block),
+// 8 elements (16 bytes) per lane, grid-stride.  Rows [M, rows_pad) get exponent
+// 0 (byte 127) in the SF tiles and no data.
 __global__ void __launch_bounds__(256) quant_mx_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M,
                                                             int rows_pad, int K, int fmt, uint8_t* __restrict__ q,
                                                             int64_t ldq, uint8_t* __restrict__ sf) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31, sub = lane & 15;
+  const uint32_t hmask = lane < 16 ? 0x0000FFFFu : 0xFFFF0000u;
   const int nkb = K / 128;
-  if (w >= (int64_t)rows_pad * nkb) return;
-  const int row = (int)(w / nkb), kb = (int)(w % nkb);
-  if (row >= M) {
-    if (lane == 0) *reinterpret_cast<uint32_t*>(sf + mx_sf_offset(row, kb, nkb)) = 0x7F7F7F7Fu;
-    return;
-  }
-  const uint2 v = *reinterpret_cast<const uint2*>(x + (int64_t)row * ldx + kb * 128 + lane * 4);
-  const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y);
-  float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
+  const int64_t units = (int64_t)rows_pad * nkb;
+  const int64_t stride = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4; u < units; u += stride) {
+    const int row = (int)(u / nkb), kb = (int)(u % nkb);
+    if (row >= M) {
+      if (sub == 0) *reinterpret_cast<uint32_t*>(sf + mx_sf_offset(row, kb, nkb)) = 0x7F7F7F7Fu;
+      continue;
+    }
+    const uint4 v = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + kb * 128 + sub * 8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const int e = mx_exponent(amax, fmt);
-  const float inv = mx_inv_scale(e);
-  const uint32_t packed = (uint32_t)mx_to_f8(a.x * inv, fmt) | ((uint32_t)mx_to_f8(a.y * inv, fmt) << 8) |
-                          ((uint32_t)mx_to_f8(b.x * inv, fmt) << 16) | ((uint32_t)mx_to_f8(b.y * inv, fmt) << 24);
-  *reinterpret_cast<uint32_t*>(q + (int64_t)row * ldq + kb * 128 + lane * 4) = packed;
-  if (lane == 0) *reinterpret_cast<uint32_t*>(sf + mx_sf_offset(row, kb, nkb)) = (uint32_t)(e + 127) * 0x01010101u;
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = unpack_bf16x2(w[e]);
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
+    const int ex = mx_exponent(amax, fmt);
+    const float inv = mx_inv_scale(ex);
+    uint32_t pk[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      pk[h] = (uint32_t)mx_to_f8(f[4 * h] * inv, fmt) | ((uint32_t)mx_to_f8(f[4 * h + 1] * inv, fmt) << 8) |
+              ((uint32_t)mx_to_f8(f[4 * h + 2] * inv, fmt) << 16) | ((uint32_t)mx_to_f8(f[4 * h + 3] * inv, fmt) << 24);
+    *reinterpret_cast<uint2*>(q + (int64_t)row * ldq + kb * 128 + sub * 8) = make_uint2(pk[0], pk[1]);
+    if (sub == 0) *reinterpret_cast<uint32_t*>(sf + mx_sf_offset(row, kb, nkb)) = (uint32_t)(ex + 127) * 0x01010101u;
+  }
 }
 
 // Weights, 128 x 128 blocks of e4m3: one block per tile.  Writes W8 [N, K], its
@@ -491,10 +507,49 @@ __global__ void __launch_bounds__(256) quant_mx_128x128_kernel(const __nv_bfloat
   }
 }
 
+// x = q * 2^e (SF tiles, one exponent per row and 128-wide K block: byte 0 of
+// the block's four) -> bf16; one thread per 8 elements.
+__global__ void __launch_bounds__(256) dequant_mx_rows_kernel(const uint8_t* __restrict__ q, int M, int K, int fmt,
+                                                              const uint8_t* __restrict__ sf,
+                                                              __nv_bfloat16* __restrict__ x, int64_t ldx) {
+  const int64_t n8 = (int64_t)M * K / 8;
+  const int nkb = K / 128;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < n8; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = u * 8;
+    const int row = (int)(e / K), col = (int)(e % K);
+    const int ex = (int)sf[mx_sf_offset(row, col / 128, nkb) + (col & 127) / 32] - 127;
+    const float sc = __uint_as_float((uint32_t)(ex + 127) << 23);
+    const uint2 v = *reinterpret_cast<const uint2*>(q + e);
+    const uint32_t w[2] = {v.x, v.y};
+    float f[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const __nv_fp8_storage_t bits = (__nv_fp8_storage_t)((w[h] >> (8 * b)) & 0xff);
+        const __half_raw hr = __nv_cvt_fp8_to_halfraw(bits, fmt == 0 ? __NV_E4M3 : __NV_E5M2);
+        f[h * 4 + b] = __half2float(__half(hr)) * sc;
+      }
+    *reinterpret_cast<uint4*>(x + (int64_t)row * ldx + col) =
+        make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+}
+
 }  // namespace
 }  // namespace lk
 
 using namespace lk;
+
+extern "C" int lk_dequant_mx_rows(const void* q, int M, int K, int fmt, const void* sf, void* x, int64_t ldx,
+                                  cudaStream_t s) {
+  LK_REQUIRE(K % 128 == 0 && ldx % 8 == 0, "dequant_mx_rows: K % 128, ldx % 8");
+  const int64_t n8 = (int64_t)M * K / 8;
+  if (n8 == 0) return 0;
+  const int grid = (int)std::min<int64_t>((n8 + 255) / 256, 8 * num_sms());
+  dequant_mx_rows_kernel<<<grid, 256, 0, s>>>((const uint8_t*)q, M, K, fmt, (const uint8_t*)sf,
+                                              (__nv_bfloat16*)x, ldx);
+  return check_launch("dequant_mx_rows");
+}
 
 extern "C" int lk_gemm_mxf8(const LkGemmMxf8Desc* g, cudaStream_t stream) {
   LK_REQUIRE(g->K % 128 == 0 && g->K > 0, "gemm_mxf8: K must be a positive multiple of 128");
@@ -549,15 +604,16 @@ extern "C" int lk_gemm_mxf8(const LkGemmMxf8Desc* g, cudaStream_t stream) {
   if (g->a_fmt == FA && g->b_fmt == FB && ag == AGV && remote == RV) kern = (void*)gemm_mxf8_kernel<FA, FB, AGV, RV>;
   LK_MX_PICK(0, 0, false, false) LK_MX_PICK(1, 0, false, false) LK_MX_PICK(0, 1, false, false)
   LK_MX_PICK(1, 1, false, false) LK_MX_PICK(0, 0, true, false) LK_MX_PICK(0, 0, false, true)
+  LK_MX_PICK(1, 0, true, false) LK_MX_PICK(1, 0, false, true)
 #undef LK_MX_PICK
-  LK_REQUIRE(kern != nullptr, "gemm_mxf8: fused collectives take e4m3 operands only");
-  static uint64_t attr_set[8] = {0};
+  LK_REQUIRE(kern != nullptr, "gemm_mxf8: fused collectives take an e4m3 B operand");
+  static uint64_t attr_set[12] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int variant = (g->a_fmt * 2 + g->b_fmt) + (ag ? 4 : 0) + (remote ? 5 : 0);
-  if (!(attr_set[variant & 7] & (1ull << dev))) {
+  const int variant = (g->a_fmt * 2 + g->b_fmt) + (ag ? 4 : 0) + (remote ? 8 : 0);
+  if (!(attr_set[variant] & (1ull << dev))) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MX_SMEM);
-    attr_set[variant & 7] |= 1ull << dev;
+    attr_set[variant] |= 1ull << dev;
   }
   void* params[] = {&ta, &tb, &a};
   if (ag) {
@@ -580,13 +636,16 @@ extern "C" int lk_gemm_mxf8(const LkGemmMxf8Desc* g, cudaStream_t stream) {
 
 extern "C" int lk_quant_mx_rows(const void* x, int64_t ldx, int M, int rows_pad, int K, int fmt, void* q,
                                 int64_t ldq, void* sf, cudaStream_t s) {
-  LK_REQUIRE(K % 128 == 0 && ldx % 4 == 0 && ldq % 4 == 0, "quant_mx_rows: K % 128, aligned pitches");
+  LK_REQUIRE(K % 128 == 0 && ldx % 8 == 0 && ldq % 8 == 0, "quant_mx_rows: K % 128, aligned pitches");
   LK_REQUIRE(rows_pad >= M && rows_pad % 128 == 0, "quant_mx_rows: rows_pad >= M, multiple of 128");
   LK_REQUIRE(fmt == 0 || fmt == 1, "quant_mx_rows: e4m3 (0) or e5m2 (1)");
-  const int64_t warps = (int64_t)rows_pad * (K / 128);
-  if (warps == 0) return 0;
-  quant_mx_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const __nv_bfloat16*)x, ldx, M, rows_pad, K,
-                                                                    fmt, (uint8_t*)q, ldq, (uint8_t*)sf);
+  LK_REQUIRE(ldq % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)q & 7) == 0,
+             "quant_mx_rows: 16-byte aligned x rows, 8-byte aligned q rows");
+  const int64_t units = (int64_t)rows_pad * (K / 128);
+  if (units == 0) return 0;
+  const int grid = (int)std::min<int64_t>((units + 15) / 16, (int64_t)num_sms() * 16);
+  quant_mx_rows_kernel<<<grid, 256, 0, s>>>((const __nv_bfloat16*)x, ldx, M, rows_pad, K, fmt, (uint8_t*)q, ldq,
+                                           (uint8_t*)sf);
   return check_launch("quant_mx_rows");
 }
 

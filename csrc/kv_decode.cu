@@ -96,56 +96,136 @@ __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t 
   if (KV != 0 && lane == 0) (which ? vs : ks)[(int64_t)slot * Hkv + h] = scale;
 }
 
-// Decode attention, split-KV.  grid (num_splits, Hkv, num_seqs), 128 threads.
-// Phase 1: each thread scores whole tokens against all G query heads of the
-// kv head (q in shared memory); phase 2: softmax statistics; phase 3: thread d
-// accumulates sum_t p[g][t] * v[t][d].  Writes unnormalised partial outputs
-// plus (max, sum) per (split, head) when num_splits > 1, else the final output.
+// Unpack N consecutive cache elements (N = 2, 4, 8, 16, 32; 16-byte aligned
+// for N * sizeof >= 16) at p into floats (scale not applied).
+template <int KV, int N>
+__device__ __forceinline__ void kv_load(const typename KvT<KV>::T* p, float (&x)[N]) {
+  constexpr int BYTES = N * (KV == 0 ? 2 : 1);
+  uint32_t w[BYTES / 4 > 0 ? BYTES / 4 : 1];
+  if constexpr (BYTES >= 16) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i) {
+      const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+      w[4 * i] = v.x;
+      w[4 * i + 1] = v.y;
+      w[4 * i + 2] = v.z;
+      w[4 * i + 3] = v.w;
+    }
+  } else if constexpr (BYTES == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x;
+    w[1] = v.y;
+  } else if constexpr (BYTES == 4) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else {
+    w[0] = *reinterpret_cast<const uint16_t*>(p);
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    if constexpr (KV == 0) {
+      const uint32_t h = (w[i / 2] >> (16 * (i & 1))) & 0xFFFFu;
+      x[i] = __uint_as_float(h << 16);
+    } else if constexpr (KV == 1) {
+      const __nv_fp8_storage_t b = (__nv_fp8_storage_t)((w[i / 4] >> (8 * (i & 3))) & 0xFFu);
+      x[i] = __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E4M3)));
+    } else {
+      x[i] = (float)(int8_t)((w[i / 4] >> (8 * (i & 3))) & 0xFFu);
+    }
+  }
+}
+
+// Decode attention, split-KV (flash-decoding).  grid (num_splits, Hkv,
+// num_seqs), 128 threads; a CTA handles the tokens [t0, t1) of one (sequence,
+// kv head) for its G query heads.
+//  phase 1  scores into shared memory: LPT lanes per token, each loading its
+//           DH / LPT contiguous cache elements with 16-byte loads (a warp reads
+//           32 / LPT whole K rows per step) against its slice of the G query
+//           rows, held in registers; LPT-lane shuffle reduction;
+//  phase 2  per-head max and sum over the split (block reductions);
+//  phase 3  P V: warp w takes tokens w, w + 4, ..., lane l owns dims
+//           [l DH/32, (l+1) DH/32) (one coalesced V row per warp and token),
+//           then the four warps' partial outputs are added in shared memory.
+// Writes unnormalised partial outputs plus (max, sum) per (split, head) when
+// num_splits > 1, else the final output.  A block id outside [0, num_blocks)
+// (bounds-checked builds) is reported in *status and its tokens are skipped.
 template <int KV, int DH, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(
     const __nv_bfloat16* __restrict__ q, int64_t ldq, const typename KvT<KV>::T* __restrict__ kc,
     const typename KvT<KV>::T* __restrict__ vc, const float* __restrict__ ks, const float* __restrict__ vs,
     const int* __restrict__ block_tables, int max_blocks, const int* __restrict__ ctx_lens,
     int block_size, int Hkv, float sl2, int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo,
-    float* __restrict__ part_o, float* __restrict__ part_ml, int num_splits) {
+    float* __restrict__ part_o, float* __restrict__ part_ml, int num_splits, int num_blocks, int* status) {
+  constexpr int LPT = G <= 4 ? 4 : 8;  // lanes per token in phase 1
+  constexpr int DPL = DH / LPT;        // dims per lane in phase 1
+  constexpr int TPI = 32 / LPT;        // tokens per warp step in phase 1
+  constexpr int D3 = DH / 32;          // dims per lane in phase 3
   extern __shared__ float sm[];
-  float* sq = sm;                 // [G][DH]
-  float* sp = sm + G * DH;        // [G][split_len] scores -> probabilities
+  float* sp = sm;  // [G][split_len] scores -> probabilities; reused for the phase-3 reduction
   __shared__ float red[G][4];
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const int ctx = ctx_lens[seq];
   const int t0 = split * split_len;
   const int t1 = min(ctx, t0 + split_len);
   const int n = max(0, t1 - t0);
-  const int tid = threadIdx.x;
-  for (int i = tid; i < G * DH; i += 128) {
-    const int g = i / DH, d = i % DH;
-    sq[i] = __bfloat162float(q[(int64_t)seq * ldq + (kvh * G + g) * DH + d]);
-  }
-  __syncthreads();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int* bt = block_tables + (int64_t)seq * max_blocks;
-  // phase 1: scores (log2 domain)
-  for (int tt = tid; tt < n; tt += 128) {
-    const int t = t0 + tt;
+  auto slot_of = [&](int t, bool& ok) -> int64_t {
     const int blk = bt[t / block_size];
-    const int64_t slot = (int64_t)blk * block_size + (t % block_size);
-    const typename KvT<KV>::T* kp = kc + (slot * Hkv + kvh) * DH;
-    const float kscale = KV == 0 ? 1.f : ks[slot * Hkv + kvh];
-    float acc[G];
+    ok = LK_BOUNDS(blk >= 0 && blk < num_blocks, status, LK_ERR_BAD_INDEX);
+    return (int64_t)blk * block_size + (t % block_size);
+  };
+  // ---------------------------------------------------------------- phase 1
+  {
+    const int grp = lane / LPT, sub = lane % LPT;
+    uint32_t qr[G][DPL / 2];  // this lane's dims of every query head, bf16 pairs
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < DH; ++d) {
-      const float kv = kv_decode<KV>(kp[d]);
+    for (int g = 0; g < G; ++g) {
+      const uint4* qp = reinterpret_cast<const uint4*>(q + (int64_t)seq * ldq + (kvh * G + g) * DH + sub * DPL);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] += sq[g * DH + d] * kv;
+      for (int i = 0; i < DPL / 8; ++i) {
+        const uint4 v = qp[i];
+        qr[g][4 * i] = v.x;
+        qr[g][4 * i + 1] = v.y;
+        qr[g][4 * i + 2] = v.z;
+        qr[g][4 * i + 3] = v.w;
+      }
     }
+#pragma unroll 2
+    for (int base = warp * TPI; base < n; base += 4 * TPI) {
+      const int tt = base + grp;
+      float sc[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) sp[g * split_len + tt] = acc[g] * kscale * sl2;
+      for (int g = 0; g < G; ++g) sc[g] = 0.f;
+      bool ok = tt < n;
+      if (ok) {
+        const int64_t slot = slot_of(t0 + tt, ok);
+        if (ok) {
+          float x[DPL];
+          kv_load<KV, DPL>(kc + (slot * Hkv + kvh) * DH + sub * DPL, x);
+          const float kscale = (KV == 0 ? 1.f : ks[slot * Hkv + kvh]) * sl2;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < DPL / 2; ++i) {
+              const float2 qf = unpack_bf16x2(qr[g][i]);
+              a = fmaf(qf.x, x[2 * i], fmaf(qf.y, x[2 * i + 1], a));
+            }
+            sc[g] = a * kscale;
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int o = LPT / 2; o > 0; o >>= 1) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+      if (tt < n && sub == 0)
+#pragma unroll
+        for (int g = 0; g < G; ++g) sp[g * split_len + tt] = ok ? sc[g] : -INFINITY;
+    }
   }
   __syncthreads();
-  // phase 2: max and sum per head
-  const int warp = tid >> 5, lane = tid & 31;
+  // ---------------------------------------------------------------- phase 2
   float mx[G], sum[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -160,41 +240,55 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float s = 0.f;
+    float sacc = 0.f;
     for (int tt = tid; tt < n; tt += 128) {
       const float p = mx[g] == -INFINITY ? 0.f : fast_exp2(sp[g * split_len + tt] - mx[g]);
       sp[g * split_len + tt] = p;
-      s += p;
+      sacc += p;
     }
-    s = warp_sum(s);
-    if (lane == 0) red[g][warp] = s;
+    sacc = warp_sum(sacc);
+    if (lane == 0) red[g][warp] = sacc;
   }
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) sum[g] = red[g][0] + red[g][1] + red[g][2] + red[g][3];
-  // phase 3: P V, thread d owns output column d (DH <= 128)
-  for (int d = tid; d < DH; d += 128) {
-    float acc[G];
+  // ---------------------------------------------------------------- phase 3
+  float acc[G][D3];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    for (int tt = 0; tt < n; ++tt) {
-      const int t = t0 + tt;
-      const int blk = bt[t / block_size];
-      const int64_t slot = (int64_t)blk * block_size + (t % block_size);
-      const float vscale = KV == 0 ? 1.f : vs[slot * Hkv + kvh];
-      const float vv = kv_decode<KV>(vc[(slot * Hkv + kvh) * DH + d]) * vscale;
+  for (int g = 0; g < G; ++g)
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] += sp[g * split_len + tt] * vv;
-    }
+    for (int j = 0; j < D3; ++j) acc[g][j] = 0.f;
+#pragma unroll 4
+  for (int tt = warp; tt < n; tt += 4) {
+    bool ok;
+    const int64_t slot = slot_of(t0 + tt, ok);
+    if (!ok) continue;
+    float v[D3];
+    kv_load<KV, D3>(vc + (slot * Hkv + kvh) * DH + lane * D3, v);
+    const float vscale = KV == 0 ? 1.f : vs[slot * Hkv + kvh];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const int h = kvh * G + g;
-      if (num_splits == 1) {
-        const float inv = sum[g] > 0.f ? 1.f / sum[g] : 0.f;
-        out[(int64_t)seq * ldo + h * DH + d] = __float2bfloat16(acc[g] * inv);
-      } else {
-        part_o[(((int64_t)seq * (Hkv * G) + h) * num_splits + split) * DH + d] = acc[g];
-      }
+      const float p = sp[g * split_len + tt] * vscale;
+#pragma unroll
+      for (int j = 0; j < D3; ++j) acc[g][j] = fmaf(p, v[j], acc[g][j]);
+    }
+  }
+  __syncthreads();  // sp is free: it holds the four warps' partial outputs now
+  float* po = sm;   // [4][G][DH]
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < D3; ++j) po[(warp * G + g) * DH + lane * D3 + j] = acc[g][j];
+  __syncthreads();
+  for (int i = tid; i < G * DH; i += 128) {
+    const int g = i / DH, d = i % DH;
+    const float o = po[i] + po[G * DH + i] + po[2 * G * DH + i] + po[3 * G * DH + i];
+    const int h = kvh * G + g;
+    if (num_splits == 1) {
+      const float inv = sum[g] > 0.f ? 1.f / sum[g] : 0.f;
+      out[(int64_t)seq * ldo + h * DH + d] = __float2bfloat16(o * inv);
+    } else {
+      part_o[(((int64_t)seq * (Hkv * G) + h) * num_splits + split) * DH + d] = o;
     }
   }
   if (num_splits > 1 && tid < G) {
@@ -242,7 +336,7 @@ template <int KV>
 __global__ void kv_gather_kernel(const typename KvT<KV>::T* __restrict__ kc, const typename KvT<KV>::T* __restrict__ vc,
                                  const float* __restrict__ ks, const float* __restrict__ vs,
                                  const int* __restrict__ slots, int n, int Hkv, int Dh,
-                                 __nv_bfloat16* __restrict__ out, int64_t ldo) {
+                                 __nv_bfloat16* __restrict__ out, int64_t ldo, int num_slots, int* status) {
   const int64_t total = (int64_t)n * 2 * Hkv * Dh;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -252,9 +346,12 @@ __global__ void kv_gather_kernel(const typename KvT<KV>::T* __restrict__ kc, con
     const int which = (int)((r / Hkv) & 1);
     const int t = (int)(r / (2 * Hkv));
     const int64_t slot = slots[t];
-    const int64_t src = (slot * Hkv + h) * Dh + d;
-    float v = kv_decode<KV>((which ? vc : kc)[src]);
-    if (KV != 0) v *= (which ? vs : ks)[slot * Hkv + h];
+    float v = 0.f;
+    if (LK_BOUNDS(slot >= 0 && slot < num_slots, status, LK_ERR_BAD_INDEX)) {
+      const int64_t src = (slot * Hkv + h) * Dh + d;
+      v = kv_decode<KV>((which ? vc : kc)[src]);
+      if (KV != 0) v *= (which ? vs : ks)[slot * Hkv + h];
+    }
     out[(int64_t)t * ldo + (which * Hkv + h) * Dh + d] = __float2bfloat16(v);
   }
 }
@@ -443,7 +540,7 @@ static int launch_decode_g(const LkDecodeDesc& d, int G, int nsplit, int smem, c
     k<<<grid, 128, smem, s>>>((const __nv_bfloat16*)d.q, d.ldq, (const T*)d.k_cache, (const T*)d.v_cache, \
                               d.k_scale, d.v_scale, d.block_tables, d.max_blocks, d.ctx_lens,        \
                               d.block_size, d.Hkv, sl2, d.split_len, (__nv_bfloat16*)d.out, d.ldo,   \
-                              d.part_o, d.part_ml, nsplit);                                          \
+                              d.part_o, d.part_ml, nsplit, d.num_blocks, d.status);                  \
     break;                                                                                           \
   }
   switch (G) {
@@ -504,7 +601,8 @@ extern "C" int lk_decode_attention(const LkDecodeDesc* d, cudaStream_t s) {
   const int G = d->Hq / d->Hkv;
   const int nsplit = d->num_splits;
   LK_REQUIRE(nsplit == 1 || (d->part_o && d->part_ml), "decode_attention: split partial buffers needed");
-  const int smem = (G * d->Dh + G * d->split_len) * (int)sizeof(float);
+  // scores [G][split_len], later the four warps' partial outputs [4][G][Dh]
+  const int smem = std::max(G * d->split_len, 4 * G * d->Dh) * (int)sizeof(float);
   if (d->kv_dtype == 0)
     return d->Dh == 64 ? launch_decode_g<0, 64>(*d, G, nsplit, smem, s) : launch_decode_g<0, 128>(*d, G, nsplit, smem, s);
   if (d->kv_dtype == 1)
@@ -514,22 +612,29 @@ extern "C" int lk_decode_attention(const LkDecodeDesc* d, cudaStream_t s) {
   return fail("decode_attention: bad kv_dtype");
 }
 
-extern "C" int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale,
-                            const float* v_scale, const int* slots, int n, int Hkv, int Dh, void* out,
-                            int64_t ldo, int kv_dtype, cudaStream_t s) {
+extern "C" int lk_kv_gather_checked(const void* k_cache, const void* v_cache, const float* k_scale,
+                                    const float* v_scale, const int* slots, int n, int Hkv, int Dh, void* out,
+                                    int64_t ldo, int kv_dtype, int num_slots, int* status, cudaStream_t s) {
   const int64_t work = (int64_t)n * 2 * Hkv * Dh;
   if (work == 0) return 0;
   const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms() * 8);
   if (kv_dtype == 0)
     kv_gather_kernel<0><<<grid, 256, 0, s>>>((const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, k_scale,
-                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo, num_slots, status);
   else if (kv_dtype == 1)
     kv_gather_kernel<1><<<grid, 256, 0, s>>>((const __nv_fp8_e4m3*)k_cache, (const __nv_fp8_e4m3*)v_cache, k_scale,
-                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+                                             v_scale, slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo, num_slots, status);
   else
     kv_gather_kernel<2><<<grid, 256, 0, s>>>((const int8_t*)k_cache, (const int8_t*)v_cache, k_scale, v_scale,
-                                             slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo);
+                                             slots, n, Hkv, Dh, (__nv_bfloat16*)out, ldo, num_slots, status);
   return check_launch("kv_gather");
+}
+
+extern "C" int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale,
+                            const float* v_scale, const int* slots, int n, int Hkv, int Dh, void* out,
+                            int64_t ldo, int kv_dtype, cudaStream_t s) {
+  return lk_kv_gather_checked(k_cache, v_cache, k_scale, v_scale, slots, n, Hkv, Dh, out, ldo, kv_dtype,
+                              INT32_MAX, nullptr, s);
 }
 
 extern "C" int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,

@@ -28,6 +28,11 @@ enum LkGemmEpi {
   LK_EPI_BF16_RESID = 3,
   LK_EPI_SWIGLU = 4,
   LK_EPI_REMOTE = 5,
+  // SwiGLU backward fused into the GEMM that produces dh = dL/d(silu(g) u):
+  // d is the bf16 gate|up gradient [M, 2N] (128-column blocks, pitch ldd) and r
+  // the forward gate|up activation in the same layout (pitch ldr); dh itself is
+  // not stored
+  LK_EPI_SWIGLU_BWD = 6,
 };
 
 typedef struct LkGemmDesc {
@@ -231,6 +236,8 @@ int lk_quant_mx_rows(const void* x, int64_t ldx, int M, int rows_pad, int K, int
 // optionally qt = q^T [K, N] with its SF tiles sft (K/128 row tiles x N/128)
 int lk_quant_mx_128x128(const void* w, int64_t ldw, int N, int K, void* q, void* sf, float* scale, void* qt,
                         void* sft, cudaStream_t s);
+// q fp8 [M, K] with SF tiles -> x bf16 [M, ldx]
+int lk_dequant_mx_rows(const void* q, int M, int K, int fmt, const void* sf, void* x, int64_t ldx, cudaStream_t s);
 
 // --------------------------------------------- K18 owner-side slot reduction
 typedef struct LkRsSumDesc {
@@ -409,11 +416,18 @@ typedef struct LkDecodeDesc {
   void* out;       // [num_seqs, Hq*Dh] bf16
   int64_t ldo;
   int kv_dtype;
+  int num_blocks;  // physical KV blocks (bounds-checked builds verify block-table entries)
+  int* status;     // optional device status word
 } LkDecodeDesc;
 int lk_decode_attention(const LkDecodeDesc* d, cudaStream_t s);
 int lk_kv_gather(const void* k_cache, const void* v_cache, const float* k_scale, const float* v_scale,
                  const int* slots, int n, int Hkv, int Dh, void* out, int64_t ldo, int kv_dtype,
                  cudaStream_t s);
+// Same, with the cache's slot count and a status word: bounds-checked builds
+// verify every slot and record an out-of-range one there (its row is zeroed).
+int lk_kv_gather_checked(const void* k_cache, const void* v_cache, const float* k_scale, const float* v_scale,
+                         const int* slots, int n, int Hkv, int Dh, void* out, int64_t ldo, int kv_dtype,
+                         int num_slots, int* status, cudaStream_t s);
 int lk_sample(const void* logits, int64_t ld, int rows, int V, const float* temperature,
               uint64_t seed, int64_t* out_tok, float* out_val, cudaStream_t s);
 int lk_sample_vp(const void* logits, int64_t ld, int rows, int V, int64_t v0, const float* temperature,

@@ -4,9 +4,15 @@ There is no fallback: every op of the B200 path calls into this extension and
 raises if it is missing or if the device is not an sm_100 GPU.  The per-device
 int32 status word is where kernels record bounded-wait timeouts and bad
 indices instead of trapping.
+
+LK_DEBUG_BOUNDS=1 loads the bounds-checked build `lora_kernel_b200._C_debug`
+instead (same sources compiled with -DLK_BOUNDS_CHECK): data-dependent indices
+(KV block-table entries, cache slots) are verified on the device, a bad one is
+recorded in the status word and the access is skipped.
 """
 from __future__ import annotations
 
+import os
 import threading
 
 import torch
@@ -36,12 +42,17 @@ def C():
     if _C is None:
         with _lock:
             if _C is None:
+                debug = os.environ.get("LK_DEBUG_BOUNDS", "0") == "1"
                 try:
-                    from lora_kernel_b200 import _C as mod  # noqa: F401
+                    if debug:
+                        from lora_kernel_b200 import _C_debug as mod  # noqa: F401
+                    else:
+                        from lora_kernel_b200 import _C as mod  # noqa: F401
                 except ImportError as e:  # pragma: no cover - depends on the build
                     raise RuntimeError(
-                        "lora_kernel_b200 CUDA extension is not built; run "
-                        "`python setup.py build_ext --inplace` in the repository root") from e
+                        "lora_kernel_b200 CUDA extension%s is not built; run "
+                        "`python setup.py build_ext --inplace` in the repository root"
+                        % (" (bounds-checked _C_debug)" if debug else "")) from e
                 _C = mod
     return _C
 

@@ -39,7 +39,7 @@ def _overrides(items):
 # train flags that are shorthands for dotted overrides (applied after --set)
 TRAIN_FLAGS = {
     "tp": "parallel.tp", "pp": "parallel.pp", "cp": "parallel.cp", "cp_mode": "parallel.cp_mode",
-    "zero": "parallel.zero_stage", "fp8": "parallel.fp8",
+    "zero": "parallel.zero_stage", "fp8": "parallel.fp8", "fp8_recipe": "parallel.fp8_recipe",
     "lr": "train.lr", "micro_batch": "train.micro_batch", "seq_len": "train.seq_len",
     "grad_accum": "train.grad_accum_steps", "metrics_file": "train.metrics_file",
     "init_from": "train.init_from", "init_format": "train.init_format",
@@ -265,6 +265,9 @@ def main(argv=None):
     t.add_argument("--device", choices=["cuda", "cpu"], default="cuda",
                    help="cpu: fp32 training on the host with the oracle model (no GPU needed)")
     t.add_argument("--fp8", action="store_true", help="block-scaled fp8 GEMMs (tensor parallel)")
+    t.add_argument("--fp8-recipe", choices=["mx", "exact"],
+                   help="mx (default): power-of-two scales applied by the tensor core, e5m2 data gradients; "
+                        "exact: fp32 scales, forward projections only")
     b = sub.add_parser("bench")
     b.add_argument("--gpus", type=int, default=1)
     b.add_argument("--kernels", action="store_true")

@@ -144,6 +144,10 @@ class ParallelConfig:
     fused_collectives: bool = True  # False: the same schedules on NCCL collectives (library baseline)
     fuse_gather: bool = False  # ZeRO-3: parameter all-gather inside the first consuming GEMM (K17)
     fp8: bool = False
+    # mx: power-of-two block scales applied by the tensor core (tcgen05 block-scaled
+    # MMA), e4m3 forward and e5m2 data gradients; exact: fp32 block scales promoted
+    # on the CUDA cores, forward projections only
+    fp8_recipe: str = "mx"
 
 
 @dataclass

@@ -457,12 +457,22 @@ class LlamaModel:
         h_in = ws.h[i if hidx is None else hidx]
         dh = ws.dh
         drop = self._dropping(ws)
-        # FFN
-        self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
-        if drop:
-            E.dropout(ws.dact, cfg.dropout, self._drop_seed(i, 1), out=ws.dact)
-        with ph("bwd.swiglu"):
-            E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
+        # FFN: the down projection's data gradient with the SwiGLU backward in its
+        # epilogue (gate|up gradients straight from the accumulator), unless
+        # dropout, a LoRA adapter or a fused parameter gather sits in between
+        fg = self.fused_gather
+        if (not drop and not (self.lora is not None and self.lora.has(i, "wdown"))
+                and not (fg is not None and fg[0] == i and fg[1] == "wdown")):
+            with ph("bwd.gemm_dgrad+swiglu"):
+                G.gemm(dh, self._p(p + "wdown").t(), ws.dgu, epi="swiglu_bwd", residual=ws.gu[s],
+                       alpha=self._sd_scale)
+            self._wgrad(dh, ws.act[s], p + "wdown", alpha=self._sd_scale)
+        else:
+            self._lin_bwd(i, "wdown", dh, ws.act[s], ws.dact)
+            if drop:
+                E.dropout(ws.dact, cfg.dropout, self._drop_seed(i, 1), out=ws.dact)
+            with ph("bwd.swiglu"):
+                E.swiglu_bwd(ws.gu[s], ws.dact, ws.dgu)
         self._lin_bwd(i, "wgu", ws.dgu, ws.xn2[s], ws.dx)
         with ph("bwd.rmsnorm"):
             N.rmsnorm_bwd(ws.dx, ws.hmid[s], self._p(p + "ffn_norm"), ws.rstd2[s], self._g(p + "ffn_norm"),

@@ -25,7 +25,8 @@ def kv_gather(k_cache, v_cache, k_scale, v_scale, slots: torch.Tensor, Hkv: int,
               kv_dtype: str = "bf16", out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(slots.numel(), 2 * Hkv * Dh, dtype=torch.bfloat16, device=slots.device)
-    C().kv_gather(k_cache, v_cache, k_scale, v_scale, slots, Hkv, Dh, out, KV_DTYPES[kv_dtype])
+    C().kv_gather(k_cache, v_cache, k_scale, v_scale, slots, Hkv, Dh, out, KV_DTYPES[kv_dtype],
+                  status(slots.device))
     return out
 
 
@@ -54,7 +55,8 @@ def decode_attention(q: torch.Tensor, k_cache, v_cache, k_scale, v_scale, block_
             _parts[key] = bufs
         po, pm = bufs
     C().decode_attention(q, k_cache, v_cache, k_scale, v_scale, block_tables, ctx_lens, block_size, Hq,
-                         Hkv, Dh, float(scale), split_len, nsplit, po, pm, out, KV_DTYPES[kv_dtype])
+                         Hkv, Dh, float(scale), split_len, nsplit, po, pm, out, KV_DTYPES[kv_dtype],
+                         status(q.device))
     return out
 
 

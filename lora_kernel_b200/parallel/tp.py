@@ -283,6 +283,45 @@ class TPComm:
         C().gemm_fp8_comm(q, sc, 0, w8.q, w8.scale, None, status(self.device), self.rank, self.tp,
                           None, None, 0, None, self.recv[k].ptrs, R, Nc)
 
+    # ------------------------------------- MX fp8 (hardware block scaling)
+    def _mx_bufs(self) -> None:
+        if not getattr(self, "stage_mx", None):
+            from ..ops.fp8 import sf_tile_bytes
+            R, D = self.max_tokens // self.tp, self.cfg.hidden_dim
+            # gathered operands are [R, D] rows: normalised inputs (e4m3) and residual gradients (e5m2)
+            self.stage_mx = [CM.SymBuffer(R * D, torch.uint8, self.device, self.group) for _ in range(2)]
+            self.ssf_mx = [CM.SymBuffer(sf_tile_bytes(R, D), torch.uint8, self.device, self.group)
+                           for _ in range(2)]
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)
+
+    def publish_mx(self, k: int, rows: torch.Tensor, fmt: int = 0) -> None:
+        """Quantise this rank's rows (bf16 [R, K]: e4m3 activations or e5m2 gradients,
+        one power-of-two scale per 128 block) into MX staging k."""
+        from ..ops.fp8 import sf_tile_bytes
+        self._mx_bufs()
+        R, K = rows.shape
+        q = self.stage_mx[k].local[:R * K].view(R, K)
+        sf = self.ssf_mx[k].local[:sf_tile_bytes(R, K)]
+        C().quant_mx_rows(rows, fmt, q, sf, R)
+
+    def ag_gemm_mx(self, k: int, dst8: torch.Tensor, dstsf: torch.Tensor, b8: torch.Tensor, bsf: torch.Tensor,
+                   out: torch.Tensor, a_fmt: int = 0) -> None:
+        """dst8 / dstsf <- all-gather of every rank's MX staging rows / SF tiles;
+        out = dst . B^T (tcgen05 block-scaled), the gather fused into the GEMM."""
+        T = dst8.shape[0]
+        C().gemm_mxf8(dst8, dstsf, int(a_fmt), b8, bsf, 0, out, None, status(self.device), self.rank, self.tp,
+                      self.stage_mx[k].ptrs, self.ssf_mx[k].ptrs, T // self.tp, self.count, None, 0, 0)
+
+    def gemm_rs_mx(self, k: int, a: torch.Tensor, b8: torch.Tensor, bsf: torch.Tensor, a_fmt: int = 0) -> None:
+        """a (bf16, quantised here) . B^T as a block-scaled fp8 GEMM whose epilogue
+        stores the bf16 rows into their owner's receive buffer k."""
+        from ..ops.fp8 import quantize_mx
+        T, Nc = a.shape[0], b8.shape[0]
+        q, sf = quantize_mx(a, a_fmt)
+        C().gemm_mxf8(q, sf, int(a_fmt), b8, bsf, 0, None, None, status(self.device), self.rank, self.tp,
+                      None, None, 0, None, self.recv[k].ptrs, T // self.tp, Nc)
+
     # --------------------------------------------------- K16 AG -> GEMM
     def ag_gemm(self, k: int, dst: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
                 epi: str = "bf16", h_out: Optional[torch.Tensor] = None) -> None:
@@ -384,7 +423,7 @@ class TPComm:
 
 # ------------------------------------------------------------------- model
 class _TPWorkspace:
-    def __init__(self, cfg: TransformerConfig, tp: int, B: int, S: int, device, fp8: bool = False):
+    def __init__(self, cfg: TransformerConfig, tp: int, B: int, S: int, device, fp8=False):
         T = B * S
         R = T // tp
         D = cfg.hidden_dim
@@ -400,7 +439,22 @@ class _TPWorkspace:
         self.rstd1 = [torch.empty(R, **f32) for _ in range(L)]
         self.rstd2 = [torch.empty(R, **f32) for _ in range(L)]
         self.rstdf = torch.empty(R, **f32)
-        if fp8:
+        if fp8 == "mx":
+            # gathered normalised inputs as e4m3 + SF tiles (power-of-two 1x128
+            # scales), gathered e5m2 gradients for the data-gradient GEMMs; bf16
+            # copies of the inputs are rebuilt right before each weight gradient
+            from ..ops.fp8 import sf_tile_bytes
+            u8 = dict(dtype=torch.uint8, device=device)
+            Fl = cfg.ff_dim_padded // tp
+            self.xn1_8 = [torch.empty(T, D, **u8) for _ in range(L)]
+            self.xn2_8 = [torch.empty(T, D, **u8) for _ in range(L)]
+            self.xn1_s = [torch.empty(sf_tile_bytes(T, D), **u8) for _ in range(L)]
+            self.xn2_s = [torch.empty(sf_tile_bytes(T, D), **u8) for _ in range(L)]
+            self.xn_deq = torch.empty(T, D, **bf)
+            self.dfull8 = torch.empty(T, D, **u8)
+            self.dfull_s = torch.empty(sf_tile_bytes(T, D), **u8)
+            self.xn1 = self.xn2 = None
+        elif fp8:
             # gathered normalised inputs as e4m3 + 1x128 scales; bf16 copies are
             # rebuilt (dequantised) right before each weight-gradient GEMM
             u8 = dict(dtype=torch.uint8, device=device)
@@ -437,14 +491,25 @@ class TPLlamaModel:
     accumulator [sum of token losses, count] - identical on every rank."""
 
     def __init__(self, cfg: TransformerConfig, comm: TPComm, params: Optional[TPParams] = None,
-                 seed: int = 1234, grads: Optional[TPParams] = None, fp8: bool = False):
+                 seed: int = 1234, grads: Optional[TPParams] = None, fp8=False):
         """fp8: the four projections of every layer run as block-scaled fp8 GEMMs
         (e4m3 activations in 1x128 blocks, e4m3 weights in 128x128 blocks) with the
         all-gather / reduce-scatter fused in (the gather moves fp8 rows + scales,
-        half the bf16 bytes); backward data-gradient GEMMs and weight gradients stay
-        bf16, the latter on the dequantised forward inputs."""
+        half the bf16 bytes).
+          "mx" (or True): power-of-two scales applied by the tensor core
+            (tcgen05 block-scaled MMA); the backward data-gradient GEMMs run the
+            same way on e5m2 gradients (gathered or reduce-scattered as fp8);
+            weight gradients are bf16 GEMMs on the dequantised fp8 operands.
+          "exact": fp32 scales, each 128-wide K block promoted on the CUDA cores;
+            backward data-gradient GEMMs and weight gradients stay bf16, the
+            latter on the dequantised forward inputs."""
         self.cfg = cfg
-        self.fp8 = fp8
+        if fp8 is True:
+            fp8 = "mx"
+        if fp8 not in (False, None, "mx", "exact"):
+            raise ValueError(f"fp8 must be False, 'mx' or 'exact', got {fp8!r}")
+        self.fp8 = fp8 or False
+        self.mx = fp8 == "mx"
         if fp8 and comm.comm != "p2p":
             raise ValueError("the fp8 tensor-parallel path runs on the peer-memory kernels (comm='p2p')")
         self.comm = comm
@@ -459,6 +524,8 @@ class TPLlamaModel:
         self.rope = E.rope_table(max(cfg.max_seq_len, 1), cfg.head_dim, cfg.rope_base, self.device)
         self._ws: Dict[Tuple[int, int], _TPWorkspace] = {}
         self._overwrite = False
+        self._w8 = None         # fp8 weight copies (see _forward)
+        self._w8_fresh = True
 
     def workspace(self, B: int, S: int) -> _TPWorkspace:
         ws = self._ws.get((B, S))
@@ -488,12 +555,20 @@ class TPLlamaModel:
         ids_local = ids.reshape(-1)[self.rank * R:(self.rank + 1) * R]
         E.embedding_fwd(ids_local, self._p("embed"), out=ws.h[0])
         N.rmsnorm_fwd(ws.h[0], self._p("layers.0.attn_norm"), eps, y=c.stage_view(0, R, D), rstd=ws.rstd1[0])
-        if self.fp8:
-            from ..ops.fp8 import Fp8Weight
-            self._w8 = {f"layers.{i}.{t}": Fp8Weight(self._p(f"layers.{i}.{t}"), transpose=False)
+        # fp8 copies of the projection weights: made on the first micro-step of an
+        # accumulation window (the weights only change between windows) and
+        # reused by the window's later micro-steps
+        if self.fp8 and (self._w8 is None or self._w8_fresh):
+            from ..ops.fp8 import Fp8Weight, MXWeight
+            make = (lambda w: MXWeight(w, transpose=True)) if self.mx else \
+                (lambda w: Fp8Weight(w, transpose=False))
+            self._w8 = {f"layers.{i}.{t}": make(self._p(f"layers.{i}.{t}"))
                         for i in range(cfg.num_layers) for t in ("wqkv", "wo", "wgu", "wdown")}
         for i in range(cfg.num_layers):
             p = f"layers.{i}."
+            if self.mx:
+                self._layer_fwd_mx(i, ws)
+                continue
             if self.fp8:
                 self._layer_fwd_fp8(i, ws)
                 continue
@@ -538,12 +613,63 @@ class TPLlamaModel:
         c.rs_sum(1, ws.h[i + 1], resid=ws.hmid[i], gamma=self._p(nxt), y=c.stage_view(0, R, D),
                  rstd=ws.rstdf if last else ws.rstd1[i + 1], eps=eps)
 
+    def _layer_fwd_mx(self, i: int, ws: _TPWorkspace) -> None:
+        cfg, c = self.cfg, self.comm
+        R, D, eps = ws.R, cfg.hidden_dim, cfg.norm_eps
+        Hl, Hkvl = cfg.num_heads // self.tp, cfg.num_kv_heads // self.tp
+        p = f"layers.{i}."
+        w = self._w8
+        c.publish_mx(0, c.stage_view(0, R, D))
+        c.barrier()
+        c.ag_gemm_mx(0, ws.xn1_8[i], ws.xn1_s[i], w[p + "wqkv"].q, w[p + "wqkv"].sf, ws.qkv[i])
+        E.rope_(ws.qkv[i], 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S)
+        A.attention_fwd(ws.qkv[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim, causal=True, out=ws.o[i], lse=ws.lse[i])
+        c.gemm_rs_mx(0, ws.o[i], w[p + "wo"].q, w[p + "wo"].sf)
+        c.rs_sum(0, ws.hmid[i], resid=ws.h[i], gamma=self._p(p + "ffn_norm"), y=c.stage_view(1, R, D),
+                 rstd=ws.rstd2[i], eps=eps)
+        c.publish_mx(1, c.stage_view(1, R, D))
+        c.barrier()
+        c.ag_gemm_mx(1, ws.xn2_8[i], ws.xn2_s[i], w[p + "wgu"].q, w[p + "wgu"].sf, ws.gu[i])
+        E.swiglu_fwd(ws.gu[i], ws.act[i])
+        c.gemm_rs_mx(1, ws.act[i], w[p + "wdown"].q, w[p + "wdown"].sf)
+        last = i == cfg.num_layers - 1
+        nxt = "final_norm" if last else f"layers.{i + 1}.attn_norm"
+        c.rs_sum(1, ws.h[i + 1], resid=ws.hmid[i], gamma=self._p(nxt), y=c.stage_view(0, R, D),
+                 rstd=ws.rstdf if last else ws.rstd1[i + 1], eps=eps)
+
+    def _ag_dgrad(self, k: int, ws: _TPWorkspace, name: str, out: torch.Tensor) -> torch.Tensor:
+        """out = gathered residual gradient . W (the column-parallel linear's data
+        gradient, all-gather fused); returns the gathered gradient (bf16) for the
+        weight gradient.  MX: the gradient travels as e5m2 and is dequantised after."""
+        c = self.comm
+        if not self.mx:
+            c.barrier()
+            c.ag_gemm(k, ws.dfull, self._p(name).t(), out)
+            return ws.dfull
+        w = self._w8[name]
+        c.publish_mx(k, c.stage_view(k, ws.R, self.cfg.hidden_dim), fmt=1)
+        c.barrier()
+        c.ag_gemm_mx(k, ws.dfull8, ws.dfull_s, w.qt, w.sft, out, a_fmt=1)
+        C().dequant_mx_rows(ws.dfull8, 1, ws.dfull_s, ws.dfull)
+        return ws.dfull
+
+    def _dgrad_rs(self, k: int, dy: torch.Tensor, name: str) -> None:
+        """Partial dy . W of a row-parallel input gradient, reduce-scattered to the owners."""
+        if self.mx:
+            w = self._w8[name]
+            self.comm.gemm_rs_mx(k, dy, w.qt, w.sft, a_fmt=1)
+        else:
+            self.comm.gemm_rs(k, dy, self._p(name).t())
+
     def _xn_bf16(self, ws: _TPWorkspace, which: int, i: int) -> torch.Tensor:
         """The gathered normalised input of layer i (1: attention, 2: FFN) as bf16."""
         if not self.fp8:
             return ws.xn1[i] if which == 1 else ws.xn2[i]
         q, sc = (ws.xn1_8[i], ws.xn1_s[i]) if which == 1 else (ws.xn2_8[i], ws.xn2_s[i])
-        C().dequant_1x128(q, 0, sc, ws.xn_deq)
+        if self.mx:
+            C().dequant_mx_rows(q, 0, sc, ws.xn_deq)
+        else:
+            C().dequant_1x128(q, 0, sc, ws.xn_deq)
         return ws.xn_deq
 
     # ----------------------------------------------------- forward+backward
@@ -555,6 +681,7 @@ class TPLlamaModel:
                          overwrite_grads: bool = False) -> torch.Tensor:
         cfg, c = self.cfg, self.comm
         self._overwrite = overwrite_grads
+        self._w8_fresh = overwrite_grads  # a new accumulation window: the weights may have changed
         B, S = ids.shape
         ws = self.workspace(B, S)
         R, D, L = ws.R, cfg.hidden_dim, cfg.num_layers
@@ -577,26 +704,24 @@ class TPLlamaModel:
         for i in reversed(range(L)):
             p = f"layers.{i}."
             # ---- FFN: dact = dh_full Wdown (all-gather fused), dgu, dxn2 -> owners
-            c.barrier()
-            c.ag_gemm(k, ws.dfull, self._p(p + "wdown").t(), ws.dact)
-            self._wgrad(ws.dfull, ws.act[i], p + "wdown")
+            dfull = self._ag_dgrad(k, ws, p + "wdown", ws.dact)
+            self._wgrad(dfull, ws.act[i], p + "wdown")
             E.swiglu_bwd(ws.gu[i], ws.dact, ws.dgu)
             self._wgrad(ws.dgu, self._xn_bf16(ws, 2, i), p + "wgu")
-            c.gemm_rs(0, ws.dgu, self._p(p + "wgu").t())
+            self._dgrad_rs(0, ws.dgu, p + "wgu")
             c.rs_sum(0, ws.dx)
             dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
             N.rmsnorm_bwd(ws.dx, ws.hmid[i], self._p(p + "ffn_norm"), ws.rstd2[i], self._g(p + "ffn_norm"),
                           dres=dh_in, dx=dh_out, accumulate=not overwrite_grads)
             k = 1 - k
             # ---- attention
-            c.barrier()
-            c.ag_gemm(k, ws.dfull, self._p(p + "wo").t(), ws.do)
-            self._wgrad(ws.dfull, ws.o[i], p + "wo")
+            dfull = self._ag_dgrad(k, ws, p + "wo", ws.do)
+            self._wgrad(dfull, ws.o[i], p + "wo")
             A.attention_bwd(ws.qkv[i], ws.o[i], ws.do, ws.lse[i], ws.B, ws.S, Hl, Hkvl, cfg.head_dim,
                             causal=True, dqkv=ws.dqkv)
             E.rope_(ws.dqkv, 0, Hl + Hkvl, cfg.head_dim, self.rope, seq_len=ws.S, inverse=True)
             self._wgrad(ws.dqkv, self._xn_bf16(ws, 1, i), p + "wqkv")
-            c.gemm_rs(1, ws.dqkv, self._p(p + "wqkv").t())
+            self._dgrad_rs(1, ws.dqkv, p + "wqkv")
             c.rs_sum(1, ws.dx)
             dh_in, dh_out = c.stage_view(k, R, D), c.stage_view(1 - k, R, D)
             N.rmsnorm_bwd(ws.dx, ws.h[i], self._p(p + "attn_norm"), ws.rstd1[i], self._g(p + "attn_norm"),
@@ -614,6 +739,7 @@ class TPLlamaModel:
         """Local vocabulary slice of the logits, [B*S, V/tp] (bf16)."""
         B, S = ids.shape
         ws = self.workspace(B, S)
+        self._w8_fresh = True
         self._forward(ids, ws)
         return ws.logits
 

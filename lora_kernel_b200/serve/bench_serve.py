@@ -26,6 +26,30 @@ import numpy as np
 import torch
 
 
+def _step_breakdown(log) -> dict:
+    """Where a step's time goes: decode-only steps (time, batch) and steps with
+    a prefill chunk (prefill time per token, decode part), host clock."""
+    def med(x):
+        return round(1e3 * statistics.median(x), 3) if x else None
+    dec_only = [r for r in log if r[3] == 0 and r[4] > 0]
+    mixed = [r for r in log if r[3] > 0]
+    out = {"steps": len(log), "decode_only_steps": len(dec_only), "steps_with_prefill": len(mixed),
+           "schedule_ms_p50": med([r[0] for r in log]),
+           "decode_only_ms_p50": med([r[2] for r in dec_only]),
+           "decode_only_batch_p50": statistics.median([r[4] for r in dec_only]) if dec_only else None,
+           "prefill_ms_p50": med([r[1] for r in mixed]),
+           "prefill_tokens_p50": statistics.median([r[3] for r in mixed]) if mixed else None,
+           "prefill_us_per_token_p50": (round(1e6 * statistics.median([r[1] / r[3] for r in mixed]), 2)
+                                        if mixed else None),
+           "decode_in_mixed_ms_p50": med([r[2] for r in mixed if r[4] > 0])}
+    busy = sum(r[0] + r[1] + r[2] for r in log)
+    if busy > 0:
+        out["share_schedule"] = round(sum(r[0] for r in log) / busy, 3)
+        out["share_prefill"] = round(sum(r[1] for r in log) / busy, 3)
+        out["share_decode"] = round(sum(r[2] for r in log) / busy, 3)
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="llama-8b-serve-int4")
@@ -39,6 +63,8 @@ def main(argv=None):
     ap.add_argument("--weights", default=None)
     ap.add_argument("--kv", default=None)
     ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--max-batched-tokens", type=int, default=0,
+                    help="token budget of a step (decode tokens + prefill chunk); 0 = the preset's")
     ap.add_argument("--layers", type=int, default=0, help="override (testing only)")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
@@ -55,6 +81,8 @@ def main(argv=None):
         cfg.num_layers = a.layers
     sc = rc.serve
     sc.max_num_seqs = a.max_num_seqs
+    if a.max_batched_tokens:
+        sc.max_num_batched_tokens = a.max_batched_tokens
     sc.max_model_len = max(sc.max_model_len, a.prompt_max + a.output_len + 16)
     weights = a.weights or rc.quant.weights
     kv = a.kv or rc.quant.kv_cache
@@ -104,6 +132,7 @@ def main(argv=None):
     torch.cuda.synchronize()
     eng.finished.clear()
 
+    eng.step_log = []
     t0 = time.perf_counter()
     nxt = 0
     ids = []
@@ -142,6 +171,8 @@ def main(argv=None):
         "data": "synthetic (random token ids, random-init weights)",
         "wall_s": round(t_end - t0, 2),
         "kv_blocks": eng.runner.num_blocks, "weight_gb": round(eng.runner.weight_bytes() / 1e9, 2),
+        "max_batched_tokens": sc.max_num_batched_tokens,
+        "step_breakdown": _step_breakdown(eng.step_log),
     }
     print(json.dumps(res), flush=True)
     if proxy is not None:

@@ -114,6 +114,10 @@ class LLMEngine:
         self.stats = {"prompt_tokens": 0, "generated_tokens": 0, "preemptions": 0, "steps": 0,
                       "prefill_tokens_computed": 0}
         self._seed = 1234
+        # when a list: one (schedule_s, prefill_s, decode_s, prefill_tokens,
+        # decode_seqs) record per step, host clock; the prefill and decode
+        # phases each end with the device read of their sampled tokens
+        self.step_log: Optional[list] = None
 
     # ---------------------------------------------------------- requests
     def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
@@ -257,9 +261,12 @@ class LLMEngine:
 
     def step(self) -> List[Request]:
         """Run one scheduling step; returns requests that finished during it."""
+        t0 = self.clock() if self.step_log is not None else 0.0
         decode, items = self._schedule()
         self.stats["steps"] += 1
         done_before = set(self.finished)
+        t1 = self.clock() if self.step_log is not None else 0.0
+        n_pre = sum(len(it.tokens) for _, it in items)
         if items:
             seq_ids, logits = self.runner.prefill([it for _, it in items])
             for r, it in items:
@@ -274,6 +281,7 @@ class LLMEngine:
                 now = self.clock()
                 for r, t in zip(reqs, toks):
                     self._emit(r, t, now)
+        t2 = self.clock() if self.step_log is not None else 0.0
         if decode:
             decode = [r for r in decode if not r.finished and r in self.running]
         if decode:
@@ -285,6 +293,9 @@ class LLMEngine:
             now = self.clock()
             for r, t in zip(decode, toks):
                 self._emit(r, t, now)
+        if self.step_log is not None:
+            t3 = self.clock()
+            self.step_log.append((t1 - t0, t2 - t1, t3 - t2, n_pre, len(decode)))
         return [self.finished[i] for i in self.finished if i not in done_before]
 
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:

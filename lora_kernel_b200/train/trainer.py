@@ -131,7 +131,7 @@ class Trainer:
             # tensor (+ sequence) parallelism over every rank: they share one batch
             from ..parallel.tp import TPTrainer
             self.pipe = TPTrainer(cfg, tc, micro_batch=tc.micro_batch, seq_len=tc.seq_len, device=self.device,
-                                  comm=comm, fp8=par.fp8, seed=tc.seed)
+                                  comm=comm, fp8=(par.fp8_recipe if par.fp8 else False), seed=tc.seed)
             self.align = 64
         elif plan["trainer"] == "dp":
             from ..parallel.dp import DataParallelTrainer

@@ -135,6 +135,55 @@ def bench_mxf8(shapes, iters):
                           "peak_src": pk["src"]}), flush=True)
 
 
+def bench_decode(iters):
+    """Serving kernels of the Llama 8B shape (TP=8 shard and the whole model on one
+    GPU): the int4 group-128 dequantising GEMV (K14 decode) and the paged decode
+    attention over an fp8 KV cache (K13), as fractions of the measured HBM copy
+    bandwidth (bytes: the int4 weights + scales once; the KV pages each sequence reads)."""
+    from lora_kernel_b200.ops import serving as SV
+    pk = peaks()
+    for (N, K, tag) in [(6144 // 8 * 8, 4096, "qkv_tp1"), (28672, 4096, "gate_up_tp1"),
+                        (4096, 14336, "down_tp1"), (3584, 4096, "gate_up_tp8")]:
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        qw = SV.QuantizedWeight(w, "int4", 128)
+        for M in (1, 8, 16):
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            t = time_fn(lambda: qw.matmul_t(x, out=out), iters)
+            by = qw.nbytes() + M * K * 2 + M * N * 2
+            print(json.dumps({"kernel": "int4_gemv", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
+                              "gbs": round(by / t / 1e6, 1), "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}),
+                  flush=True)
+        for M in (64, 256):  # decode batches above the GEMV's 16 rows
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            scratch = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
+            t = time_fn(lambda: qw.matmul_t(x, out=out, scratch=scratch), iters)
+            by = qw.nbytes() + M * K * 2 + M * N * 2
+            print(json.dumps({"kernel": "int4_matmul", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
+                              "gbs_of_int4_bytes": round(by / t / 1e6, 1),
+                              "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+        del w, qw
+    # paged decode attention: Llama 8B, 32 q / 8 kv heads (TP=8: 4 / 1), head_dim 128, fp8 pages of 16
+    for (nseq, ctx, Hq, Hkv) in [(256, 2048, 4, 1), (64, 2048, 32, 8), (256, 1024, 32, 8)]:
+        Dh, bs = 128, 16
+        nblk = nseq * ((ctx + bs - 1) // bs)
+        kc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
+        vc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
+        ks = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
+        vs = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
+        bt = torch.randperm(nblk, device="cuda", dtype=torch.int32).view(nseq, -1)
+        lens = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(nseq, Hq * Dh, device="cuda").to(torch.bfloat16)
+        out = torch.empty_like(q)
+        t = time_fn(lambda: SV.decode_attention(q, kc, vc, ks, vs, bt, lens, bs, Hq, Hkv, Dh, kv_dtype="fp8",
+                                                max_ctx=ctx, out=out), iters)
+        by = nseq * ctx * Hkv * (2 * Dh + 8) + 2 * q.numel() * 2
+        print(json.dumps({"kernel": "decode_attention_fp8", "seqs": nseq, "ctx": ctx, "Hq": Hq, "Hkv": Hkv,
+                          "Dh": Dh, "ms": round(t, 4), "gbs": round(by / t / 1e6, 1),
+                          "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+
+
 def bench_norm(iters):
     from lora_kernel_b200.ops.norm import rmsnorm_bwd, rmsnorm_fwd
     pk = peaks()
@@ -186,6 +235,19 @@ def bench_attention(iters, B=4, S=2048, Hq=32, Hkv=4, Dh=64):
           flush=True)
 
 
+def attention_once(B=4, S=2048, Hq=32, Hkv=4, Dh=64):
+    """One attention forward + backward and nothing else (the case ncu captures)."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.ops.attention import attention_bwd, attention_fwd
+    qkv = torch.randn(B * S, (Hq + 2 * Hkv) * Dh, device="cuda").to(torch.bfloat16)
+    o, lse = attention_fwd(qkv, B, S, Hq, Hkv, Dh)
+    dout = torch.randn_like(o)
+    attention_bwd(qkv, o, dout, lse, B, S, Hq, Hkv, Dh)
+    torch.cuda.synchronize()
+    check_status()
+    print(json.dumps({"kernel": "attention_once", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "Dh": Dh}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,norm")
@@ -214,10 +276,16 @@ def main():
     if "mx" in which:
         bench_mxf8([(8192, 8192, 8192), (8192, 3584, 4096), (8192, 4096, 1792), (8192, 768, 4096),
                     (8192, 4096, 512)] if not args.small else [(4096, 4096, 4096)], args.iters)
+    if "decode" in which:
+        bench_decode(args.iters)
     if "norm" in which:
         bench_norm(args.iters)
     if "attn" in which:
         bench_attention(args.iters)  # Llama 1.1B: B 4, S 2048, 32 / 4 heads, head_dim 64
+    if "attn_once" in which:
+        attention_once()
+    if "attn8b_once" in which:
+        attention_once(B=2, S=4096, Hq=32, Hkv=8, Dh=128)
     if "attn8b" in which:
         bench_attention(args.iters, B=2, S=4096, Hq=32, Hkv=8, Dh=128)  # Llama 8B shape
 

@@ -205,11 +205,15 @@ def bench_step(cfg, tc, B, S, accum, steps, warmup, comm, rank0, fp8=False):
     loss = (acc[0] / acc[1]).item()
     tokens = accum * B * S  # the TP group shares one batch
     res = {"metric": "train tokens/sec", "value": round(tokens / ms * 1e3, 1), "unit": "tokens/s",
-           "ms_per_step": round(ms, 2), "comm": comm + ("+fp8" if fp8 else ""), "n_gpus": dist.get_world_size(),
+           "ms_per_step": round(ms, 2), "comm": comm + (f"+fp8-{tr.model.fp8}" if fp8 else ""),
+           "n_gpus": dist.get_world_size(),
            "config": {"model": f"Llama-style {cfg.num_layers} layers d{cfg.hidden_dim}",
                       "global_batch": accum * B, "seq_len": S, "parallelism": f"tp{dist.get_world_size()}",
                       "micro_batch": B, "accum": accum},
-           "dtype": "fp8 e4m3 projections (1x128 / 128x128 scales), bf16 rest" if fp8 else "bf16",
+           "dtype": ("fp8 projections: e4m3 forward, e5m2 data gradients, power-of-two 1x128 / 128x128 scales "
+                     "applied by the tensor core (MX); bf16 weight gradients, attention and LM head"
+                     if tr.model.mx else
+                     "fp8 e4m3 forward projections (1x128 / 128x128 fp32 scales), bf16 rest") if fp8 else "bf16",
            "loss": round(loss, 4), "nvls": bool(tr.comm.pc.nvls)}
     if rank0:
         print(json.dumps(res), flush=True)
@@ -231,7 +235,8 @@ def main(argv=None):
     ap.add_argument("--step", action="store_true")
     ap.add_argument("--comm", default="p2p,nccl")
     ap.add_argument("--diag", action="store_true")
-    ap.add_argument("--fp8", action="store_true", help="also run the block-scaled fp8 TP step (p2p)")
+    ap.add_argument("--fp8", default="", help="also run the block-scaled fp8 TP step (p2p): "
+                    "comma list of recipes, mx (tensor-core scales) and/or exact (fp32 scales)")
     a = ap.parse_args(argv)
     from ..config import get_preset
     from ..parallel.comm import init_distributed
@@ -249,8 +254,8 @@ def main(argv=None):
     if a.step:
         for comm in a.comm.split(","):
             bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, comm, rank == 0)
-        if a.fp8:
-            bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, "p2p", rank == 0, fp8=True)
+        for recipe in [r for r in a.fp8.split(",") if r]:
+            bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, "p2p", rank == 0, fp8=recipe)
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()

@@ -165,7 +165,7 @@ def check_fp8(rank, world, res):
     tok = torch.randint(0, cfg.vocab_size, (B, S + 1), generator=gt).cuda()
     ids, tg = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
     outs = []
-    for fp8 in (False, True):
+    for fp8 in (False, "exact", "mx"):
         c2 = TP.TPComm(cfg, B * S, dev)
         params = TP.TPParams(cfg, world, rank, dev)
         params.init_(5, cfg.init_std)
@@ -176,6 +176,62 @@ def check_fp8(rank, world, res):
     check_status()
     res["fp8_model_loss_rel"] = abs(outs[1][0][0].item() - outs[0][0][0].item()) / outs[0][0][0].item()
     res["fp8_model_grad_rel"] = rel(outs[1][1], outs[0][1])
+    res["mx_model_loss_rel"] = abs(outs[2][0][0].item() - outs[0][0][0].item()) / outs[0][0][0].item()
+    res["mx_model_grad_rel"] = rel(outs[2][1], outs[0][1])
+
+
+def check_mx(rank, world, res):
+    """MX fp8 (tcgen05 block-scaled) with the collectives fused: the gather of e4m3
+    rows + SF tiles, the gather of e5m2 gradient rows against W^T, and the
+    reduce-scatter epilogue, against unfused MX GEMMs + NCCL."""
+    from lora_kernel_b200.ops import fp8 as F
+    cfg = TransformerConfig(**CFG)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    T = 256 * world
+    R, D = T // world, cfg.hidden_dim
+    comm = TP.TPComm(cfg, T, dev)
+    g = torch.Generator(device=dev).manual_seed(300 + rank)
+    gw = torch.Generator(device=dev).manual_seed(19)
+    mine = torch.randn(R, D, device=dev, generator=g).bfloat16()
+    w = F.MXWeight((torch.randn(384, D, device=dev, generator=gw) * 0.05).bfloat16())
+    comm.publish_mx(0, mine)
+    comm.barrier()
+    dst8 = torch.empty(T, D, dtype=torch.uint8, device=dev)
+    dstsf = torch.empty(F.sf_tile_bytes(T, D), dtype=torch.uint8, device=dev)
+    out = torch.empty(T, 384, dtype=torch.bfloat16, device=dev)
+    comm.ag_gemm_mx(0, dst8, dstsf, w.q, w.sf, out)
+    torch.cuda.synchronize()
+    q, sf = F.quantize_mx(mine)
+    allq = [torch.empty_like(q) for _ in range(world)]
+    allsf = [torch.empty_like(sf) for _ in range(world)]
+    dist.all_gather(allq, q)
+    dist.all_gather(allsf, sf)
+    fq, fsf = torch.cat(allq), torch.cat(allsf)
+    res["mx_ag_rows_exact"] = bool(torch.equal(dst8, fq)) and bool(torch.equal(dstsf, fsf))
+    res["mx_ag_gemm_err"] = rel(out, F.gemm_mxf8(fq, fsf, w.q, w.sf))
+    # e5m2 rows gathered into the data-gradient GEMM against W^T
+    w2 = F.MXWeight((torch.randn(D, 256, device=dev, generator=gw) * 0.05).bfloat16())
+    dmine = (torch.randn(R, D, device=dev, generator=g) * 1e-3).bfloat16()
+    comm.publish_mx(1, dmine, fmt=1)
+    comm.barrier()
+    out2 = torch.empty(T, 256, dtype=torch.bfloat16, device=dev)
+    comm.ag_gemm_mx(1, dst8, dstsf, w2.qt, w2.sft, out2, a_fmt=1)
+    torch.cuda.synchronize()
+    alld = [torch.empty_like(dmine) for _ in range(world)]
+    dist.all_gather(alld, dmine)
+    dfull = torch.cat(alld).float()
+    res["mx_ag_dgrad_err"] = rel(out2, dfull @ w2.dequantize())
+    # reduce-scatter epilogue (e5m2 input against W^T, the row-parallel data gradient)
+    a = (torch.randn(T, 256, device=dev, generator=g) * 1e-3).bfloat16()
+    comm.gemm_rs_mx(0, a, w2.q, w2.sf, a_fmt=1)
+    hout = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    comm.rs_sum(0, hout)
+    qa, sfa = F.quantize_mx(a, F.E5M2)
+    part = F.gemm_mxf8(qa, sfa, w2.q, w2.sf, a_fmt=F.E5M2).float()
+    dist.all_reduce(part)
+    torch.cuda.synchronize()
+    res["mx_rs_err"] = rel(hout, part[rank * R:(rank + 1) * R])
+    check_status()
 
 
 def _single_gpu(cfg, ids, tg, seed):
@@ -247,6 +303,7 @@ def main():
         check_model(rank, world, res, "nccl")
     elif what == "fp8":
         check_fp8(rank, world, res)
+        check_mx(rank, world, res)
     elif what == "train":
         check_train(rank, world, res, "p2p")
         check_train(rank, world, res, "nccl")

@@ -370,3 +370,25 @@ def test_gemm_cta_pair_fused_epilogues():
         _status_ok()
     finally:
         C().gemm_set_pair(0)
+
+
+@pytest.mark.parametrize("M,F,D", [(256, 256, 256), (1000, 640, 384), (4096, 1536, 1024)])
+def test_gemm_swiglu_bwd_epilogue(M, F, D):
+    """The down projection's data gradient with the SwiGLU backward in its
+    epilogue (gate|up in 128-column blocks) against fp32 PyTorch."""
+    from lora_kernel_b200.ops import gemm as G
+    g = torch.Generator(device="cuda").manual_seed(4)
+    dy = torch.randn(M, D, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(D, F, device="cuda", generator=g) * 0.05).bfloat16()
+    gu = torch.randn(M, 2 * F, device="cuda", generator=g).bfloat16()
+    dgu = G.gemm(dy, w.t(), epi="swiglu_bwd", residual=gu, alpha=0.5)
+    torch.cuda.synchronize()
+    dh = 0.5 * (dy.float() @ w.float())
+    blk = gu.float().view(M, F // 128, 2, 128)
+    gate, up = blk[:, :, 0].reshape(M, F), blk[:, :, 1].reshape(M, F)
+    s = torch.sigmoid(gate)
+    dgate = dh * up * s * (1 + gate * (1 - s))
+    dup = dh * gate * s
+    ref = torch.stack([dgate.view(M, F // 128, 128), dup.view(M, F // 128, 128)], 2).view(M, 2 * F)
+    err = (dgu.float() - ref).norm() / ref.norm()
+    assert err < 1e-2, err

@@ -15,7 +15,7 @@ def _close(out, ref, rtol, atol, what=""):
 
 
 @pytest.mark.parametrize("kv", ["bf16", "fp8", "int8"])
-@pytest.mark.parametrize("Hq,Hkv,Dh", [(8, 2, 64), (4, 1, 128), (8, 8, 128)])
+@pytest.mark.parametrize("Hq,Hkv,Dh", [(8, 2, 64), (4, 1, 128), (8, 8, 128), (8, 1, 64), (16, 2, 128)])
 def test_kv_append_gather_and_decode(kv, Hq, Hkv, Dh):
     from lora_kernel_b200.ops import serving as SV
     torch.manual_seed(0)

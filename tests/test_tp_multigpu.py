@@ -68,3 +68,9 @@ def test_tp_fp8_fused_paths(tmp_path):
         assert res["fp8_rs_err"] < 1e-2, res
         assert res["fp8_model_loss_rel"] < 3e-2, res
         assert res["fp8_model_grad_rel"] < 0.25, res
+        assert res["mx_ag_rows_exact"], res
+        assert res["mx_ag_gemm_err"] < 1e-3, res
+        assert res["mx_ag_dgrad_err"] < 0.1, res
+        assert res["mx_rs_err"] < 1e-2, res
+        assert res["mx_model_loss_rel"] < 3e-2, res
+        assert res["mx_model_grad_rel"] < 0.3, res
