@@ -173,8 +173,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="lk", choices=["lk", "reference", "torch"])
-    ap.add_argument("--micro-batch", type=int, default=4)
-    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--preset", default="llama-1.1b-zero3",
+                    help="workload: llama-1.1b-zero3 (the headline) or llama-8b-fsdp-dp8 (8B ZeRO-3, "
+                         "accumulation 8, EMA); a timed step is one optimizer step")
+    ap.add_argument("--micro-batch", type=int, default=0, help="0 = the preset's")
+    ap.add_argument("--seq", type=int, default=0, help="0 = the preset's")
     ap.add_argument("--layers", type=int, default=0, help="override (testing only; invalid for the headline)")
     ap.add_argument("--fuse-gather", action="store_true",
                     help="ZeRO-3: gather each layer inside its first GEMM instead of prefetching it")
@@ -199,9 +202,14 @@ def main():
         return
 
     from lora_kernel_b200.config import get_preset
-    rc = get_preset("llama-1.1b-zero3")
+    rc = get_preset(args.preset)
     cfg, tc = rc.model, rc.train
-    tc.micro_batch, tc.seq_len = args.micro_batch, args.seq
+    tc.micro_batch = args.micro_batch or tc.micro_batch
+    tc.seq_len = args.seq or tc.seq_len
+    accum = max(1, tc.grad_accum_steps)
+    model_name = MODEL_NAME if args.preset == "llama-1.1b-zero3" else (
+        f"Llama-style {cfg.num_parameters() / 1e9:.1f}B ({cfg.num_layers} layers, d {cfg.hidden_dim}, "
+        f"{cfg.num_heads} heads/{cfg.num_kv_heads} KV heads, ffn {cfg.ff_dim}, vocab {cfg.vocab_size})")
     if args.layers:
         cfg.num_layers = args.layers
     W = max(3, args.warmup)
@@ -220,8 +228,8 @@ def main():
     dev_ids = [h.to("cuda") for h in host_ids]
     dev_batches = [(d[:, :-1].contiguous(), d[:, 1:].contiguous()) for d in dev_ids]
 
-    # ---- warm-up
-    for i in range(W):
+    # ---- warm-up (optimizer steps of `accum` micro-batches each)
+    for i in range(W * accum):
         x, y = dev_batches[i % n_batches]
         trainer.micro_step_async(x, y)
     torch.cuda.synchronize()
@@ -236,7 +244,7 @@ def main():
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for i in range(K):
+    for i in range(K * accum):
         x, y = dev_batches[i % n_batches]
         trainer.micro_step_async(x, y)
     end.record()
@@ -246,7 +254,7 @@ def main():
     clocks = sampler.stop()
     ms = start.elapsed_time(end) / K
     ms = max_over_ranks(ms, world)
-    tokens_per_step = B * S * world
+    tokens_per_step = B * S * world * accum
     value = tokens_per_step / (ms / 1e3)
 
     # ---- end-to-end through the public API: the native loader fills page-locked
@@ -262,9 +270,13 @@ def main():
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
+        for _ in range(accum - 1):
+            x, y = loader.next_device("cuda")
+            h2d += loader.bytes_per_batch()
+            trainer.micro_step_async(x, y)
         x, y = loader.next_device("cuda")
         h2d += loader.bytes_per_batch()
-        loss = trainer.train_step(x, y)
+        loss = trainer.train_step(x, y)  # last micro-batch of the step; its loss read back
         d2h += 8
         losses.append(loss)
     torch.cuda.synchronize()
@@ -280,7 +292,7 @@ def main():
         P = max(1, args.phase_steps)
         barrier(world)
         with collecting(timer):
-            for i in range(P):
+            for i in range(P * accum):
                 x, y = dev_batches[i % n_batches]
                 trainer.micro_step_async(x, y)
         phases = timer.per_step_ms(P)
@@ -306,10 +318,12 @@ def main():
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids from the native loader, N(0,0.02) random-init weights)",
         "impl": args.impl,
-        "config": {"model": MODEL_NAME, "global_batch": B * world, "micro_batch_per_gpu": B,
+        "config": {"model": model_name, "global_batch": B * world * accum, "micro_batch_per_gpu": B,
                    "seq_len": S, "parallelism": parallelism,
                    "layers": cfg.num_layers,
-                   "optimizer": "AdamW+dynamic loss scale+global-norm clip 1.0",
+                   "optimizer": "AdamW+dynamic loss scale+global-norm clip 1.0"
+                                + (f"+EMA {tc.ema_decay}" if tc.ema_decay else ""),
+                   "grad_accum": accum,
                    "l2": "inputs larger than L2 (each step streams GBs of weights/activations)"},
         "clocks": clocks,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d // K,

@@ -313,30 +313,23 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
         for (int e = 0; e < 32; ++e)
           if (c * 32 + e > khi || c * 32 + e < klo) x[e] = __float_as_uint(-INFINITY);
       };
-      // pass 1: the row max over all 128 keys (four independent max chains, two
-      // TMEM round trips); chunks 2, 3 stay in registers, chunks 0, 1 are read
-      // again in pass 2 (168 registers hold 64 + 64 scores at once)
-      uint32_t s2[32], s3[32];
+      // pass 1: all 128 scores of the row in registers with one TMEM round trip,
+      // then the row max (four independent max chains)
+      uint32_t s0[32], s1[32], s2[32], s3[32];
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      {
-        uint32_t x0[32], x1[32];
-        tmem_ld32(tS, x0);
-        tmem_ld32(tS + 32, x1);
-        tc_wait_ld();
-        mask_chunk(x0, 0);
-        mask_chunk(x1, 1);
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          m4[e & 3] = fmaxf(m4[e & 3], fmaxf(__uint_as_float(x0[e]), __uint_as_float(x1[e])));
-      }
+      tmem_ld32(tS, s0);
+      tmem_ld32(tS + 32, s1);
       tmem_ld32(tS + 64, s2);
       tmem_ld32(tS + 96, s3);
       tc_wait_ld();
+      mask_chunk(s0, 0);
+      mask_chunk(s1, 1);
       mask_chunk(s2, 2);
       mask_chunk(s3, 3);
 #pragma unroll
       for (int e = 0; e < 32; ++e)
-        m4[e & 3] = fmaxf(m4[e & 3], fmaxf(__uint_as_float(s2[e]), __uint_as_float(s3[e])));
+        m4[e & 3] = fmaxf(m4[e & 3], fmaxf(fmaxf(__uint_as_float(s0[e]), __uint_as_float(s1[e])),
+                                           fmaxf(__uint_as_float(s2[e]), __uint_as_float(s3[e]))));
       // max of the raw scores (scale > 0 commutes with max)
       const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float mx = mraw * args.sl2;
@@ -344,8 +337,8 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
       const float alpha = (m_new != m_used) ? fast_exp2(m_used - m_new) : 1.f;
       const float mb = (m_new == -INFINITY) ? 0.f : m_new;
       // pass 2: P as bf16 pairs, 32 keys -> 16 TMEM columns at a time, written
-      // over the first 64 columns of S (in key order, so no score is
-      // overwritten before it is read); four independent partial sums
+      // over the first 64 columns of S (every score is already in registers);
+      // four independent partial sums
       float r4[4] = {0.f, 0.f, 0.f, 0.f};
       // EMU of every 16 exponentials go to the FMA pipe on unmasked tiles (masked
       // -inf scores need the exact 0 of ex2)
@@ -368,14 +361,8 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
         }
         tmem_st16(tS + c * 16, pk);
       };
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t x[32];
-        tmem_ld32(tS + c * 32, x);
-        tc_wait_ld();
-        mask_chunk(x, c);
-        emit(x, c);
-      }
+      emit(s0, 0);
+      emit(s1, 1);
       emit(s2, 2);
       emit(s3, 3);
       const float rowsum = (r4[0] + r4[1]) + (r4[2] + r4[3]);

@@ -61,7 +61,8 @@ Operand classify(const torch::Tensor& x, const char* name) {
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
           c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> h, double alpha,
           torch::Tensor status, int64_t bn, c10::optional<torch::Tensor> a2,
-          c10::optional<torch::Tensor> b2) {
+          c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> rope_table, int64_t rope_cols,
+          int64_t rope_dh, int64_t rope_seq, int64_t rope_off) {
   const c10::cuda::CUDAGuard g(a.device());
   TORCH_CHECK(a.size(1) == b.size(1), "gemm: K mismatch ", a.sizes(), " vs ", b.sizes());
   Operand A = classify(a, "a"), B = classify(b, "b");
@@ -95,6 +96,19 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
   d.alpha = (float)alpha;
   d.epi = (int)epi;
   d.bn = (int)bn;
+  if (rope_table.has_value()) {
+    need_contig(*rope_table, "rope_table", torch::kFloat32);
+    TORCH_CHECK(epi == LK_EPI_BF16_ROPE && rope_table->dim() == 3 && rope_table->size(1) * 2 == rope_dh,
+                "gemm: rope table [max_pos, Dh/2, 2] with the rope epilogue");
+    TORCH_CHECK(rope_seq + rope_off <= rope_table->size(0), "gemm: rope positions beyond the table");
+    d.rope_table = rope_table->data_ptr();
+    d.rope_cols = (int)rope_cols;
+    d.rope_dh = (int)rope_dh;
+    d.rope_seq = (int)rope_seq;
+    d.rope_off = (int)rope_off;
+  } else {
+    TORCH_CHECK(epi != LK_EPI_BF16_ROPE, "gemm: the rope epilogue needs its table");
+  }
   need(status, "status", torch::kInt32);
   d.status = status.data_ptr<int>();
   if (a2.has_value() && b2.has_value()) {
@@ -483,6 +497,49 @@ void dequant_mx_rows(torch::Tensor q, int64_t fmt, torch::Tensor sf, torch::Tens
   check(lk_dequant_mx_rows(q.data_ptr(), (int)q.size(0), (int)q.size(1), (int)fmt, sf.data_ptr(), x.data_ptr(),
                            x.stride(0), stream()));
 }
+
+// K14 decode form: weight-streaming dequant GEMM (tcgen05), M <= 256.
+void dq_gemm(torch::Tensor x, torch::Tensor q, torch::Tensor scale, c10::optional<torch::Tensor> zero, int64_t fmt,
+             int64_t N, int64_t K, int64_t group, torch::Tensor y, c10::optional<torch::Tensor> resid,
+             c10::optional<torch::Tensor> partial, int64_t splits, torch::Tensor status) {
+  const c10::cuda::CUDAGuard g(x.device());
+  need(x, "x", torch::kBFloat16);
+  need(y, "y", torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K, "dq_gemm: x [M, K] row-major");
+  TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(0) == x.size(0) && y.size(1) == N, "dq_gemm: y [M, N]");
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous(), "dq_gemm: q contiguous");
+  need_contig(scale, "scale", torch::kFloat32);
+  LkDqGemmDesc d{};
+  d.fmt = (int)fmt;
+  d.x = x.data_ptr();
+  d.ldx = x.stride(0);
+  d.M = (int)x.size(0);
+  d.q = q.data_ptr();
+  d.scale = scale.data_ptr<float>();
+  d.zero = optp<float>(zero);
+  d.N = (int)N;
+  d.K = (int)K;
+  d.group = (int)group;
+  d.y = y.data_ptr();
+  d.ldy = y.stride(0);
+  if (resid.has_value()) {
+    need(*resid, "resid", torch::kBFloat16);
+    TORCH_CHECK(resid->size(0) == d.M && resid->size(1) == N && resid->stride(1) == 1, "dq_gemm: resid");
+    d.r = resid->data_ptr();
+    d.ldr = resid->stride(0);
+  }
+  d.splits = (int)splits;
+  if (partial.has_value()) {
+    need_contig(*partial, "partial", torch::kFloat32);
+    TORCH_CHECK(partial->numel() >= (int64_t)std::max<int64_t>(splits, 1) * d.M * N, "dq_gemm: partial size");
+    d.partial = partial->data_ptr<float>();
+  }
+  need(status, "status", torch::kInt32);
+  d.status = status.data_ptr<int>();
+  check(lk_dq_gemm(&d, stream()));
+}
+
+int64_t dq_gemm_splits(int64_t M, int64_t N, int64_t K) { return lk_dq_gemm_splits((int)M, (int)N, (int)K); }
 
 // K18 owner side: sum of the received slots (+ residual, + RMSNorm).
 void rs_sum(torch::Tensor recv, int64_t world, torch::Tensor out, c10::optional<torch::Tensor> resid,
@@ -1130,6 +1187,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_mx_rows", &quant_mx_rows);
   m.def("quant_mx_128x128", &quant_mx_128x128);
   m.def("dequant_mx_rows", &dequant_mx_rows);
+  m.def("dq_gemm", &dq_gemm);
+  m.def("dq_gemm_splits", &dq_gemm_splits);
   m.def("allreduce_sum_nvls", &allreduce_sum_nvls);
   m.def("reduce_scatter_sum_nvls", &reduce_scatter_sum_nvls);
   m.def("cross_entropy_vp", &cross_entropy_vp);

@@ -27,6 +27,7 @@ extern "C" int lk_gemm(const LkGemmDesc* g, cudaStream_t stream) {
     case LK_EPI_BF16_RESID:
     case LK_EPI_SWIGLU:
     case LK_EPI_SWIGLU_BWD:
+    case LK_EPI_BF16_ROPE:
       return gemm_dispatch_fused(*g, stream);
     default:
       return fail("lk_gemm: unknown epilogue");

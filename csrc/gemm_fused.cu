@@ -15,6 +15,14 @@ int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s) {
                                : launch_gemm<256, false, true, EPI_SWIGLU_BWD>(g, s);
   }
   LK_REQUIRE(!g.a_mn && !g.b_mn, "lk_gemm: fused epilogues need K-major operands");
+  if (g.epi == LK_EPI_BF16_ROPE) {
+    LK_REQUIRE(g.rope_table != nullptr && g.rope_dh % 8 == 0 && g.rope_dh > 0 && g.rope_cols % g.rope_dh == 0 &&
+                   g.rope_seq > 0,
+               "lk_gemm: rope epilogue needs the table, head_dim % 8 == 0, whole heads and seq > 0");
+    if (use_pair(g)) return launch_gemm<256, false, false, EPI_BF16_ROPE, 0, 2>(g, s);
+    return choose_bn(g) == 128 ? launch_gemm<128, false, false, EPI_BF16_ROPE>(g, s)
+                               : launch_gemm<256, false, false, EPI_BF16_ROPE>(g, s);
+  }
   if (g.epi == LK_EPI_SWIGLU) {
     LK_REQUIRE(g.N % 256 == 0 && g.h != nullptr, "lk_gemm: swiglu needs N % 256 == 0 and h");
     if (use_pair(g)) return launch_gemm<256, false, false, EPI_SWIGLU, 0, 2>(g, s);

@@ -40,6 +40,7 @@ enum GemmEpi : int {
   EPI_SWIGLU = 4,      // D(bf16) = acc (gate|up), H(bf16) = silu(gate) * up
   EPI_REMOTE = 5,      // K18: bf16 tile stored into the owner rank's receive slot (peer memory)
   EPI_SWIGLU_BWD = 6,  // acc = dh; D(bf16 [M, 2N] gate|up grads) from R (gate|up), dh not stored
+  EPI_BF16_ROPE = 7,   // D(bf16) = alpha*acc, columns < rope_cols rotated (RoPE) first
 };
 
 struct GemmArgs {
@@ -79,6 +80,9 @@ struct GemmArgs {
   int64_t gb_chunk, gb_len, gb_boff;
   uint8_t* gb_dst;
   int* gb_count;
+  // EPI_BF16_ROPE: (cos, sin) table [max_pos, rope_dh / 2], rotated columns, position = row % seq + off
+  const float2* rope_table;
+  int rope_cols, rope_dh, rope_seq, rope_off;
 };
 
 constexpr int64_t GB_PIECE = 8192;  // elements per K17 copy piece (16 KB)
@@ -666,7 +670,7 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
                 *reinterpret_cast<uint4*>(drow + 128 + v * 8) = make_uint4(du[0], du[1], du[2], du[3]);
               }
             }
-          } else if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID) {
+          } else if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RESID || EPI == EPI_BF16_ROPE) {
             __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -675,6 +679,20 @@ __global__ void __launch_bounds__(AG ? GEMM_THREADS + 32 * AG_WARPS : GEMM_THREA
               float f[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]) * alpha;
+              if constexpr (EPI == EPI_BF16_ROPE) {
+                if (col < args.rope_cols) {
+                  // interleaved pairs (2i, 2i+1) of the head, angle index i = (col % Dh) / 2 + e
+                  const int pos = row % args.rope_seq + args.rope_off;
+                  const float2* tb = args.rope_table + (int64_t)pos * (args.rope_dh / 2) + (col % args.rope_dh) / 2;
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 cs = tb[e];
+                    const float x0 = f[2 * e], x1 = f[2 * e + 1];
+                    f[2 * e] = x0 * cs.x - x1 * cs.y;
+                    f[2 * e + 1] = x0 * cs.y + x1 * cs.x;
+                  }
+                }
+              }
               if constexpr (EPI == EPI_BF16_RESID) {
                 const uint4 rv = *reinterpret_cast<const uint4*>(args.R + (int64_t)row * args.ldr + col);
                 const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
@@ -789,6 +807,11 @@ int launch_gemm(const LkGemmDesc& g, cudaStream_t stream) {
   args.gb_boff = g.gb_boff;
   args.gb_dst = reinterpret_cast<uint8_t*>(g.gb_dst);
   args.gb_count = g.gb_count;
+  args.rope_table = reinterpret_cast<const float2*>(g.rope_table);
+  args.rope_cols = g.rope_cols;
+  args.rope_dh = g.rope_dh > 0 ? g.rope_dh : 64;
+  args.rope_seq = g.rope_seq > 0 ? g.rope_seq : (1 << 30);
+  args.rope_off = g.rope_off;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, AG, CG>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;

@@ -142,9 +142,9 @@ __device__ __forceinline__ void kv_load(const typename KvT<KV>::T* p, float (&x)
 //           32 / LPT whole K rows per step) against its slice of the G query
 //           rows, held in registers; LPT-lane shuffle reduction;
 //  phase 2  per-head max and sum over the split (block reductions);
-//  phase 3  P V: warp w takes tokens w, w + 4, ..., lane l owns dims
-//           [l DH/32, (l+1) DH/32) (one coalesced V row per warp and token),
-//           then the four warps' partial outputs are added in shared memory.
+//  phase 3  P V: 8 lanes per token (32 for G = 8) with 16-byte loads, four
+//           tokens per warp step and four steps in flight; token groups and
+//           then the four warps' partial outputs are added.
 // Writes unnormalised partial outputs plus (max, sum) per (split, head) when
 // num_splits > 1, else the final output.  A block id outside [0, num_blocks)
 // (bounds-checked builds) is reported in *status and its tokens are skipped.
@@ -158,7 +158,6 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
   constexpr int LPT = G <= 4 ? 4 : 8;  // lanes per token in phase 1
   constexpr int DPL = DH / LPT;        // dims per lane in phase 1
   constexpr int TPI = 32 / LPT;        // tokens per warp step in phase 1
-  constexpr int D3 = DH / 32;          // dims per lane in phase 3
   extern __shared__ float sm[];
   float* sp = sm;  // [G][split_len] scores -> probabilities; reused for the phase-3 reduction
   __shared__ float red[G][4];
@@ -253,32 +252,49 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
 #pragma unroll
   for (int g = 0; g < G; ++g) sum[g] = red[g][0] + red[g][1] + red[g][2] + red[g][3];
   // ---------------------------------------------------------------- phase 3
+  // LP3 lanes per token (16-byte loads for G <= 4), TP3 tokens per warp step;
+  // the token groups of a warp are added with shuffles at the end
+  constexpr int LP3 = G <= 4 ? 8 : 32;
+  constexpr int D3 = DH / LP3;
+  constexpr int TP3 = 32 / LP3;
+  const int g3 = lane / LP3, s3 = lane % LP3;
   float acc[G][D3];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int j = 0; j < D3; ++j) acc[g][j] = 0.f;
 #pragma unroll 4
-  for (int tt = warp; tt < n; tt += 4) {
-    bool ok;
-    const int64_t slot = slot_of(t0 + tt, ok);
-    if (!ok) continue;
-    float v[D3];
-    kv_load<KV, D3>(vc + (slot * Hkv + kvh) * DH + lane * D3, v);
-    const float vscale = KV == 0 ? 1.f : vs[slot * Hkv + kvh];
+  for (int base = warp * TP3; base < n; base += 4 * TP3) {
+    const int tt = base + g3;
+    if (tt < n) {
+      bool ok;
+      const int64_t slot = slot_of(t0 + tt, ok);
+      if (ok) {
+        float v[D3];
+        kv_load<KV, D3>(vc + (slot * Hkv + kvh) * DH + s3 * D3, v);
+        const float vscale = KV == 0 ? 1.f : vs[slot * Hkv + kvh];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float p = sp[g * split_len + tt] * vscale;
+        for (int g = 0; g < G; ++g) {
+          const float p = sp[g * split_len + tt] * vscale;
 #pragma unroll
-      for (int j = 0; j < D3; ++j) acc[g][j] = fmaf(p, v[j], acc[g][j]);
+          for (int j = 0; j < D3; ++j) acc[g][j] = fmaf(p, v[j], acc[g][j]);
+        }
+      }
     }
   }
-  __syncthreads();  // sp is free: it holds the four warps' partial outputs now
-  float* po = sm;   // [4][G][DH]
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int j = 0; j < D3; ++j) po[(warp * G + g) * DH + lane * D3 + j] = acc[g][j];
+    for (int j = 0; j < D3; ++j)
+#pragma unroll
+      for (int o = LP3; o < 32; o <<= 1) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], o);
+  __syncthreads();  // sp is free: it holds the four warps' partial outputs now
+  float* po = sm;   // [4][G][DH]
+  if (g3 == 0)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < D3; ++j) po[(warp * G + g) * DH + s3 * D3 + j] = acc[g][j];
   __syncthreads();
   for (int i = tid; i < G * DH; i += 128) {
     const int g = i / DH, d = i % DH;

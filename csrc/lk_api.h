@@ -33,6 +33,10 @@ enum LkGemmEpi {
   // the forward gate|up activation in the same layout (pitch ldr); dh itself is
   // not stored
   LK_EPI_SWIGLU_BWD = 6,
+  // bf16 output whose first rope_cols columns are rotary-embedded on the way
+  // out: heads of width rope_dh, interleaved pairs (2i, 2i+1), row m at position
+  // m % rope_seq + rope_off, (cos, sin) from rope_table float2 [max_pos, rope_dh/2]
+  LK_EPI_BF16_ROPE = 7,
 };
 
 typedef struct LkGemmDesc {
@@ -88,6 +92,9 @@ typedef struct LkGemmDesc {
   int64_t gb_chunk, gb_len, gb_boff;
   void* gb_dst;
   int* gb_count;
+  // LK_EPI_BF16_ROPE
+  const void* rope_table;
+  int rope_cols, rope_dh, rope_seq, rope_off;
 } LkGemmDesc;
 
 int lk_gemm(const LkGemmDesc* desc, cudaStream_t stream);
@@ -447,6 +454,30 @@ int lk_dequant_gemv(int fmt, const void* x, int64_t ldx, int M, const void* q, c
                     const float* zero, int N, int K, int group, void* y, int64_t ldy, cudaStream_t s);
 int lk_dequantize(int fmt, const void* q, const float* scale, const float* zero, int N, int K,
                   int group, void* w, cudaStream_t s);
+// Weight-streaming dequant GEMM for decode batches (tcgen05, 1 <= M <= 256):
+// y[M, N] (bf16) = x[M, K] (bf16, pitch ldx) . dequant(q)^T (+ r).  q / scale /
+// zero in the lk_quantize layouts (int4: K % 64 == 0, group % 64 == 0).  With
+// splits > 1 (0 = lk_dq_gemm_splits) each split writes an fp32 partial to
+// partial [splits, M, N], summed in split order into y.
+typedef struct LkDqGemmDesc {
+  int fmt;
+  const void* x;
+  int64_t ldx;
+  int M;
+  const void* q;
+  const float* scale;
+  const float* zero;
+  int N, K, group;
+  void* y;
+  int64_t ldy;
+  const void* r;
+  int64_t ldr;
+  float* partial;
+  int splits;
+  int* status;
+} LkDqGemmDesc;
+int lk_dq_gemm(const LkDqGemmDesc* d, cudaStream_t s);
+int lk_dq_gemm_splits(int M, int N, int K);
 
 // ---------------------------------------------- peer-memory collectives (comm.cu)
 // Pointer arguments named *_ptrs are DEVICE arrays of `world` peer pointers

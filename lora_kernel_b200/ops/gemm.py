@@ -16,7 +16,7 @@ import torch
 
 from .._ext import C, require_device, status
 
-EPI = {"bf16": 0, "f32": 1, "f32_acc": 2, "bf16_resid": 3, "swiglu": 4, "swiglu_bwd": 6}
+EPI = {"bf16": 0, "f32": 1, "f32_acc": 2, "bf16_resid": 3, "swiglu": 4, "swiglu_bwd": 6, "bf16_rope": 7}
 
 
 _cap = {}
@@ -56,10 +56,14 @@ def _check_device(t: torch.Tensor) -> None:
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *,
          epi: str = "bf16", residual: Optional[torch.Tensor] = None,
          h_out: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0,
-         a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None) -> torch.Tensor:
+         a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None,
+         rope: Optional[tuple] = None) -> torch.Tensor:
     """out = alpha * (a @ b.T [+ a2 @ b2.T]) with the requested epilogue.
     swiglu_bwd: a @ b.T is dh, the gradient of silu(gate) * up; residual is the
-    forward gate|up activation [M, 2N] and out receives its gradient [M, 2N]."""
+    forward gate|up activation [M, 2N] and out receives its gradient [M, 2N].
+    rope = (table, cols, head_dim, seq_len, pos_offset): the bf16 output's first
+    `cols` columns are rotated (interleaved-pair RoPE, row m at position
+    m % seq_len + pos_offset) in the epilogue (epi becomes "bf16_rope")."""
     _check_device(a)
     if bn == 0:
         bn = tuned_bn(a, b, epi)
@@ -68,7 +72,13 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
         dt = torch.float32 if epi in ("f32", "f32_acc") else torch.bfloat16
         cols = 2 * N if epi == "swiglu_bwd" else N  # gate|up gradients
         out = (torch.zeros if epi == "f32_acc" else torch.empty)(M, cols, dtype=dt, device=a.device)
-    C().gemm(a, b, out, EPI[epi], residual, h_out, float(alpha), status(a.device), int(bn), a2, b2)
+    if rope is not None:
+        table, cols, dh, seq, off = rope
+        C().gemm(a, b, out, EPI["bf16_rope"], None, None, float(alpha), status(a.device), int(bn), a2, b2,
+                 table, int(cols), int(dh), int(seq), int(off))
+    else:
+        C().gemm(a, b, out, EPI[epi], residual, h_out, float(alpha), status(a.device), int(bn), a2, b2,
+                 None, 0, 0, 0, 0)
     return out
 
 

@@ -124,15 +124,30 @@ class QuantizedWeight:
         return n + (self.zero.numel() * 4 if self.zero is not None else 0)
 
     def matmul_t(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
-                 scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """x [M, K] @ W^T -> [M, N]: dequantising GEMV for M <= 16, otherwise a
-        dequantise-to-bf16 pass followed by the tcgen05 GEMM."""
+                 scratch: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [M, K] @ W^T (+ residual) -> [M, N].  Decode batches (M <= 256): the
+        weight-streaming tcgen05 dequant GEMM (one pass over the packed weights
+        for the whole batch, split-K partials summed in order); prefill: a
+        dequantise-to-bf16 pass followed by the tcgen05 GEMM (the weight tile
+        would otherwise be dequantised once per 128-row block of x)."""
         M = x.shape[0]
         if out is None:
             out = torch.empty(M, self.N, dtype=torch.bfloat16, device=x.device)
-        if M <= 16:
-            C().dequant_gemv(QFMT[self.fmt], x, self.q, self.scale, self.zero, self.N, self.K, self.group, out)
+        if M <= 256 and self.K % 64 == 0 and self.N % 4 == 0 and (self.fmt != "int4" or self.group % 64 == 0):
+            splits = C().dq_gemm_splits(M, self.N, self.K)
+            part = None
+            if splits > 1:
+                key = (x.device, splits * M * self.N)
+                part = _dq_parts.get(key)
+                if part is None:
+                    part = torch.empty(splits * M * self.N, dtype=torch.float32, device=x.device)
+                    _dq_parts[key] = part
+            C().dq_gemm(x, self.q, self.scale, self.zero, QFMT[self.fmt], self.N, self.K, self.group, out,
+                        residual, part, splits, status(x.device))
             return out
         from .gemm import gemm
         w = self.dequantize(scratch)
-        return gemm(x, w, out)
+        return gemm(x, w, out, epi="bf16_resid" if residual is not None else "bf16", residual=residual)
+
+
+_dq_parts = {}

@@ -112,16 +112,13 @@ class ModelRunner:
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
         w = self.W[name]
         if isinstance(w, SV.QuantizedWeight):
-            if x.shape[0] > 16:
+            scratch = None
+            if x.shape[0] > 256:  # prefill: dequantise once, then the bf16 GEMM
                 need = w.N * w.K
                 if self._scratch is None or self._scratch.numel() < need:
                     self._scratch = torch.empty(need, dtype=torch.bfloat16, device=self.device)
-                y = w.matmul_t(x, out=out, scratch=self._scratch[:need].view(w.N, w.K))
-            else:
-                y = w.matmul_t(x, out=out)
-            if residual is not None:
-                y += residual
-            return y
+                scratch = self._scratch[:need].view(w.N, w.K)
+            return w.matmul_t(x, out=out, scratch=scratch, residual=residual)
         return G.linear(x, w, residual=residual, out=out)
 
     def _ffn(self, x: torch.Tensor, p: str, residual: torch.Tensor) -> torch.Tensor:

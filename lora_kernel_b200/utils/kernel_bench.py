@@ -142,27 +142,24 @@ def bench_decode(iters):
     bandwidth (bytes: the int4 weights + scales once; the KV pages each sequence reads)."""
     from lora_kernel_b200.ops import serving as SV
     pk = peaks()
-    for (N, K, tag) in [(6144 // 8 * 8, 4096, "qkv_tp1"), (28672, 4096, "gate_up_tp1"),
-                        (4096, 14336, "down_tp1"), (3584, 4096, "gate_up_tp8")]:
+    from lora_kernel_b200._ext import C
+    for (N, K, tag) in [(6144, 4096, "qkv_tp1"), (28672, 4096, "gate_up_tp1"),
+                        (4096, 14336, "down_tp1"), (3584, 4096, "gate_up_tp8"), (4096, 1792, "down_tp8")]:
         w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
         qw = SV.QuantizedWeight(w, "int4", 128)
-        for M in (1, 8, 16):
+        for M in (1, 8, 16, 64, 128, 256):
             x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
             out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
             t = time_fn(lambda: qw.matmul_t(x, out=out), iters)
             by = qw.nbytes() + M * K * 2 + M * N * 2
-            print(json.dumps({"kernel": "int4_gemv", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
-                              "gbs": round(by / t / 1e6, 1), "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}),
-                  flush=True)
-        for M in (64, 256):  # decode batches above the GEMV's 16 rows
-            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
-            out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-            scratch = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
-            t = time_fn(lambda: qw.matmul_t(x, out=out, scratch=scratch), iters)
-            by = qw.nbytes() + M * K * 2 + M * N * 2
-            print(json.dumps({"kernel": "int4_matmul", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
-                              "gbs_of_int4_bytes": round(by / t / 1e6, 1),
-                              "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+            rec = {"kernel": "int4_dq_gemm", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
+                   "splits": C().dq_gemm_splits(M, N, K), "gbs": round(by / t / 1e6, 1),
+                   "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}
+            if M <= 16:  # the CUDA-core GEMV it replaces
+                tg = time_fn(lambda: C().dequant_gemv(SV.QFMT["int4"], x, qw.q, qw.scale, qw.zero, N, K, 128, out),
+                             iters)
+                rec["cuda_core_gemv_ms"] = round(tg, 4)
+            print(json.dumps(rec), flush=True)
         del w, qw
     # paged decode attention: Llama 8B, 32 q / 8 kv heads (TP=8: 4 / 1), head_dim 128, fp8 pages of 16
     for (nseq, ctx, Hq, Hkv) in [(256, 2048, 4, 1), (64, 2048, 32, 8), (256, 1024, 32, 8)]:

@@ -392,3 +392,29 @@ def test_gemm_swiglu_bwd_epilogue(M, F, D):
     ref = torch.stack([dgate.view(M, F // 128, 128), dup.view(M, F // 128, 128)], 2).view(M, 2 * F)
     err = (dgu.float() - ref).norm() / ref.norm()
     assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("S,Dh,Hq,Hkv", [(256, 64, 4, 2), (512, 128, 2, 1)])
+def test_gemm_rope_epilogue(S, Dh, Hq, Hkv):
+    """The QKV GEMM with RoPE in its epilogue against fp32 PyTorch: x W^T, then the
+    interleaved-pair rotation of the q and k heads at position row % S; v untouched."""
+    from lora_kernel_b200.ops import gemm as G
+    from lora_kernel_b200.ops.elementwise import rope_table
+    g = torch.Generator(device="cuda").manual_seed(6)
+    B, D = 3, 256
+    N = (Hq + 2 * Hkv) * Dh
+    x = torch.randn(B * S, D, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, D, device="cuda", generator=g) * 0.05).bfloat16()
+    tab = rope_table(S, Dh, 10000.0, "cuda")
+    y = G.gemm(x, w, rope=(tab, (Hq + Hkv) * Dh, Dh, S, 0))
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    nrot = (Hq + Hkv) * Dh
+    r = ref[:, :nrot].view(B * S, Hq + Hkv, Dh // 2, 2)
+    pos = torch.arange(B * S, device="cuda") % S
+    c, s = tab[pos, :, 0][:, None, :], tab[pos, :, 1][:, None, :]
+    x0, x1 = r[..., 0], r[..., 1]
+    rot = torch.stack([x0 * c - x1 * s, x0 * s + x1 * c], -1).view(B * S, nrot)
+    ref = torch.cat([rot, ref[:, nrot:]], 1)
+    err = (y.float() - ref).norm() / ref.norm()
+    assert err < 1e-2, err

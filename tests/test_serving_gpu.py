@@ -67,7 +67,7 @@ def test_kv_append_gather_and_decode(kv, Hq, Hkv, Dh):
 
 
 @pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
-@pytest.mark.parametrize("M", [1, 5, 16, 40])
+@pytest.mark.parametrize("M", [1, 5, 16, 40, 130, 256, 300])
 def test_quantized_matmul(fmt, M):
     from lora_kernel_b200.ops.serving import QuantizedWeight
     torch.manual_seed(1)
@@ -88,6 +88,27 @@ def test_quantized_matmul(fmt, M):
     y = qw.matmul_t(x)
     ref = x.float() @ wd.float().t()
     _close(y, ref, 3e-2, 3e-2 * math.sqrt(K) * 0.05, f"{fmt} M={M}")
+
+
+@pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
+@pytest.mark.parametrize("M,N,K", [(7, 200, 512), (64, 3584, 4096), (200, 1000, 1536)])
+def test_dq_gemm_shapes_and_residual(fmt, M, N, K):
+    """The weight-streaming dequant GEMM: ragged N (rows past N read as zeros),
+    split-K partials, the residual epilogue, against the fp32 product of the
+    dequantised weights."""
+    from lora_kernel_b200.ops.serving import QuantizedWeight
+    g = torch.Generator(device=dev).manual_seed(2)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    qw = QuantizedWeight(w, fmt, 128)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    r = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    y = qw.matmul_t(x, residual=r)
+    y2 = qw.matmul_t(x, residual=r)
+    torch.cuda.synchronize()
+    ref = x.float() @ qw.dequantize().float().t() + r.float()
+    err = (y.float() - ref).norm() / ref.norm()
+    assert err < 1e-2, err
+    assert torch.equal(y, y2)  # split-K partials are summed in a fixed order
 
 
 def test_sampling():
