@@ -137,10 +137,10 @@ __device__ __forceinline__ void kv_load(const typename KvT<KV>::T* p, float (&x)
 // Decode attention, split-KV (flash-decoding).  grid (num_splits, Hkv,
 // num_seqs), 128 threads; a CTA handles the tokens [t0, t1) of one (sequence,
 // kv head) for its G query heads.
-//  phase 1  scores into shared memory: LPT lanes per token, each loading its
-//           DH / LPT contiguous cache elements with 16-byte loads (a warp reads
-//           32 / LPT whole K rows per step) against its slice of the G query
-//           rows, held in registers; LPT-lane shuffle reduction;
+//  phase 1  scores into shared memory: 8 lanes per token, each loading its
+//           DH / 8 contiguous cache elements with 16-byte loads (a warp reads 4
+//           whole K rows per step, four steps in flight) against its slice of
+//           the G query rows, held in registers; 8-lane shuffle reduction;
 //  phase 2  per-head max and sum over the split (block reductions);
 //  phase 3  P V: 8 lanes per token (32 for G = 8) with 16-byte loads, four
 //           tokens per warp step and four steps in flight; token groups and
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
     const int* __restrict__ block_tables, int max_blocks, const int* __restrict__ ctx_lens,
     int block_size, int Hkv, float sl2, int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo,
     float* __restrict__ part_o, float* __restrict__ part_ml, int num_splits, int num_blocks, int* status) {
-  constexpr int LPT = G <= 4 ? 4 : 8;  // lanes per token in phase 1
+  constexpr int LPT = 8;               // lanes per token in phase 1
   constexpr int DPL = DH / LPT;        // dims per lane in phase 1
   constexpr int TPI = 32 / LPT;        // tokens per warp step in phase 1
   extern __shared__ float sm[];
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
         qr[g][4 * i + 3] = v.w;
       }
     }
-#pragma unroll 2
+#pragma unroll(G <= 4 ? 4 : 2)
     for (int base = warp * TPI; base < n; base += 4 * TPI) {
       const int tt = base + grp;
       float sc[G];

@@ -45,9 +45,11 @@ struct DqRaw {
   static constexpr int TILE = DQ_BM * ROW_BYTES;
 };
 
+// Stage counts keep two CTAs resident per SM (up to MP = 128), so one CTA's
+// pipeline fill and epilogue overlap the other's stream of weights.
 template <int MP>
 struct DqCfg {
-  static constexpr int STAGES = MP >= 256 ? 3 : (MP >= 128 ? 4 : 6);
+  static constexpr int STAGES = MP >= 256 ? 2 : (MP >= 64 ? 3 : 4);
   static constexpr int A_BYTES = DQ_BM * DQ_BK * 2;  // dequantised bf16 tile
   static constexpr int X_BYTES = MP * DQ_BK * 2;
   static constexpr int TMEM_COLS = MP < 32 ? 32 : MP;
@@ -106,7 +108,7 @@ __device__ __forceinline__ uint4 dq_byte8(uint32_t lo, uint32_t hi, float s) {
 }
 
 template <int FMT, int MP>
-__global__ void __launch_bounds__(DQ_THREADS, 1)
+__global__ void __launch_bounds__(DQ_THREADS, 2)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const DqArgs args) {
   using C = DqCfg<MP>;

@@ -85,6 +85,15 @@ class Request:
     def tokens(self) -> List[int]:
         return self.prompt + self.output
 
+    # O(1) forms of len(tokens) and tokens[-1] for the per-step paths
+    @property
+    def n_tokens(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    @property
+    def last_token(self) -> int:
+        return self.output[-1] if self.output else self.prompt[-1]
+
     @property
     def in_prefill(self) -> bool:
         return self.computed < self.prefill_len
@@ -178,20 +187,23 @@ class LLMEngine:
 
     def _schedule(self):
         decode: List[Request] = []
+        preempted = set()  # request ids preempted during this pass
         for r in list(self.running):
-            if r.in_prefill or r not in self.running:
+            if r.in_prefill or r.req_id in preempted:
                 continue
             while True:
                 try:
-                    self.blocks.append_slot(r.table, len(r.tokens) - 1)
+                    self.blocks.append_slot(r.table, r.n_tokens - 1)
                     break
                 except MemoryError:
                     victims = [x for x in self.running if x is not r]
                     if not victims:
                         raise
+                    preempted.add(victims[-1].req_id)
                     self._preempt(victims[-1])
             decode.append(r)
-        decode = [r for r in decode if r in self.running]
+        if preempted:
+            decode = [r for r in decode if r.req_id not in preempted]
         budget = max(self.sc.max_num_batched_tokens - len(decode), 1)
         prefill: List[Request] = [r for r in self.running if r.in_prefill]
         admitted_tokens = sum(r.prefill_len - r.computed for r in prefill)
@@ -283,11 +295,13 @@ class LLMEngine:
                     self._emit(r, t, now)
         t2 = self.clock() if self.step_log is not None else 0.0
         if decode:
-            decode = [r for r in decode if not r.finished and r in self.running]
+            live = {x.req_id for x in self.running}
+            decode = [r for r in decode if not r.finished and r.req_id in live]
         if decode:
-            toks_in = [r.tokens[-1] for r in decode]
-            pos = [len(r.tokens) - 1 for r in decode]
-            slots = [self.blocks.slots_for(r.table, p, p + 1)[0] for r, p in zip(decode, pos)]
+            toks_in = [r.last_token for r in decode]
+            pos = [r.n_tokens - 1 for r in decode]
+            bs = self.blocks.block_size
+            slots = [r.table[p // bs] * bs + p % bs for r, p in zip(decode, pos)]
             logits = self.runner.decode(toks_in, pos, slots, [r.table for r in decode])
             toks = self._sample(decode, logits)
             now = self.clock()
