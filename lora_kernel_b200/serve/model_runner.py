@@ -21,6 +21,8 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
+
+import numpy as np
 from typing import Dict, List, Optional, Tuple
 
 import torch
@@ -265,7 +267,8 @@ class ModelRunner:
     @torch.no_grad()
     def decode(self, tokens: List[int], positions: List[int], slots: List[int],
                block_tables: List[List[int]]) -> torch.Tensor:
-        """One token per sequence; returns logits [n, vocab]."""
+        """One token per sequence; returns logits [n, vocab].  The arguments may
+        also be int32 numpy arrays (block_tables [n, max_blocks], zero padded)."""
         n = len(tokens)
         if self.use_graphs and n <= getattr(self, "graph_max_batch", self.GRAPH_BUCKETS[-1]):
             return self._decode_graph(tokens, positions, slots, block_tables)
@@ -273,13 +276,16 @@ class ModelRunner:
         ids_t = torch.tensor(tokens, dtype=torch.int64, device=dev)
         pos_t = torch.tensor(positions, dtype=torch.int32, device=dev)
         slots_t = torch.tensor(slots, dtype=torch.int32, device=dev)
-        mb = max(len(t) for t in block_tables)
-        bt = torch.zeros(n, mb, dtype=torch.int32)
-        for k, t in enumerate(block_tables):
-            bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        if isinstance(block_tables, np.ndarray):
+            bt = torch.from_numpy(np.ascontiguousarray(block_tables, dtype=np.int32))
+        else:
+            mb = max(len(t) for t in block_tables)
+            bt = torch.zeros(n, mb, dtype=torch.int32)
+            for k, t in enumerate(block_tables):
+                bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
         bt = bt.to(dev)
-        ctx = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=dev)
-        return self._decode_body(ids_t, pos_t, slots_t, bt, ctx, max(positions) + 1)
+        ctx = torch.tensor([int(p) + 1 for p in positions], dtype=torch.int32, device=dev)
+        return self._decode_body(ids_t, pos_t, slots_t, bt, ctx, int(max(positions)) + 1)
 
     def _decode_graph(self, tokens, positions, slots, block_tables) -> torch.Tensor:
         n = len(tokens)
@@ -297,11 +303,14 @@ class ModelRunner:
         hi[b:b + n] = positions
         hi[2 * b:2 * b + n] = slots
         hi[2 * b + n:3 * b] = self.dummy_block * self.block_size
-        hi[3 * b:3 * b + n] = [p + 1 for p in positions]
+        hi[3 * b:3 * b + n] = np.asarray(positions, dtype=np.int32) + 1
         hi[3 * b + n:4 * b] = 1
         btab = hi[4 * b:].reshape(b, mb)
-        for k, t in enumerate(block_tables):
-            btab[k, :len(t)] = t
+        if isinstance(block_tables, np.ndarray):
+            btab[:n, :block_tables.shape[1]] = block_tables
+        else:
+            for k, t in enumerate(block_tables):
+                btab[k, :len(t)] = t
         btab[n:, 0] = self.dummy_block
         dev_in.copy_(host, non_blocking=True)
         graph.replay()

@@ -26,6 +26,7 @@ from __future__ import annotations
 import dataclasses
 from typing import Dict, List, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -157,9 +158,73 @@ def pick_global(allp: torch.Tensor) -> torch.Tensor:
     return allp[best, torch.arange(allp.shape[1], device=allp.device), 1].long()
 
 
+# Runner calls travel rank 0 -> workers on the CPU (gloo) group as a 2-int64
+# header (op, payload length) and, for decode and sample, one flat int32 payload:
+#   decode  [n, max_blocks, tokens(n), positions(n), slots(n), block table (n x max_blocks)]
+#   sample  [seed low 32 bits, seed high 32 bits, has temperatures, temperatures as float32 bits (n)]
+# Prefill items (rarer, ragged) still go as one pickled object.
+OP_STOP, OP_DECODE, OP_SAMPLE, OP_PREFILL = 0, 1, 2, 3
+
+
+def pack_decode(tokens, positions, slots, block_tables) -> np.ndarray:
+    n = len(tokens)
+    mb = max(len(t) for t in block_tables)
+    pk = np.zeros(2 + 3 * n + n * mb, dtype=np.int32)
+    pk[0], pk[1] = n, mb
+    pk[2:2 + n] = tokens
+    pk[2 + n:2 + 2 * n] = positions
+    pk[2 + 2 * n:2 + 3 * n] = slots
+    bt = pk[2 + 3 * n:].reshape(n, mb)
+    for k, t in enumerate(block_tables):
+        bt[k, :len(t)] = t
+    return pk
+
+
+def unpack_decode(pk: np.ndarray):
+    n, mb = int(pk[0]), int(pk[1])
+    return (pk[2:2 + n], pk[2 + n:2 + 2 * n], pk[2 + 2 * n:2 + 3 * n], pk[2 + 3 * n:].reshape(n, mb))
+
+
+def pack_sample(temps, seed: int) -> np.ndarray:
+    n = 0 if temps is None else len(temps)
+    pk = np.zeros(3 + n, dtype=np.int32)
+    s = int(seed) & 0xFFFFFFFFFFFFFFFF
+    pk[0] = np.int64(s & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+    pk[1] = np.int64(s >> 32).astype(np.uint32).view(np.int32)
+    pk[2] = 0 if temps is None else 1
+    if n:
+        pk[3:] = np.asarray(temps, dtype=np.float32).view(np.int32)
+    return pk
+
+
+def unpack_sample(pk: np.ndarray):
+    seed = int(pk[0].view(np.uint32)) | (int(pk[1].view(np.uint32)) << 32)
+    temps = pk[3:].view(np.float32).tolist() if pk[2] else None
+    return temps, seed
+
+
+def _send(op: int, payload: Optional[np.ndarray], group) -> None:
+    hdr = torch.tensor([op, 0 if payload is None else payload.size], dtype=torch.int64)
+    dist.broadcast(hdr, src=0, group=group)
+    if payload is not None and payload.size:
+        dist.broadcast(torch.from_numpy(payload), src=0, group=group)
+
+
+def _recv(group):
+    hdr = torch.empty(2, dtype=torch.int64)
+    dist.broadcast(hdr, src=0, group=group)
+    op, n = int(hdr[0]), int(hdr[1])
+    payload = None
+    if n:
+        buf = torch.empty(n, dtype=torch.int32)
+        dist.broadcast(buf, src=0, group=group)
+        payload = buf.numpy()
+    return op, payload
+
+
 class RunnerProxy:
-    """Rank 0's stand-in for the runner: broadcasts every call to the workers
-    (CPU group) and runs it on its own shard."""
+    """Rank 0's stand-in for the runner: sends every call to the workers (CPU
+    group) and runs it on its own shard from the same message."""
 
     supports_top_p = False
 
@@ -170,48 +235,46 @@ class RunnerProxy:
         self.block_size = runner.block_size
         self._logits = None
 
-    def _bcast(self, msg) -> None:
-        obj = [msg]
-        dist.broadcast_object_list(obj, src=0, group=self.ctrl)
-
     def prefill(self, items):
-        self._bcast(("prefill", items))
+        _send(OP_PREFILL, None, self.ctrl)
+        dist.broadcast_object_list([items], src=0, group=self.ctrl)
         seq_ids, self._logits = self.runner.prefill(items)
         return seq_ids, self._logits
 
     def decode(self, tokens, positions, slots, block_tables):
-        self._bcast(("decode", (tokens, positions, slots, block_tables)))
-        self._logits = self.runner.decode(tokens, positions, slots, block_tables)
+        pk = pack_decode(tokens, positions, slots, block_tables)
+        _send(OP_DECODE, pk, self.ctrl)
+        self._logits = self.runner.decode(*unpack_decode(pk))
         return self._logits
 
     def sample(self, logits, temps, seed):
-        self._bcast(("sample", (temps, seed)))
+        _send(OP_SAMPLE, pack_sample(temps, seed), self.ctrl)
         return self.runner.sample(logits, temps, seed)
 
     def weight_bytes(self) -> int:
         return self.runner.weight_bytes()
 
     def stop(self) -> None:
-        self._bcast(("stop", None))
+        _send(OP_STOP, None, self.ctrl)
 
 
 def worker_loop(runner: TPModelRunner, ctrl_group) -> None:
     """Ranks > 0: execute rank 0's runner calls until it says stop."""
     logits = None
     while True:
-        obj = [None]
-        dist.broadcast_object_list(obj, src=0, group=ctrl_group)
-        op, arg = obj[0]
-        if op == "stop":
+        op, payload = _recv(ctrl_group)
+        if op == OP_STOP:
             return
-        if op == "prefill":
-            _, logits = runner.prefill(arg)
-        elif op == "decode":
-            logits = runner.decode(*arg)
-        elif op == "sample":
-            runner.sample(logits, *arg)
+        if op == OP_PREFILL:
+            obj = [None]
+            dist.broadcast_object_list(obj, src=0, group=ctrl_group)
+            _, logits = runner.prefill(obj[0])
+        elif op == OP_DECODE:
+            logits = runner.decode(*unpack_decode(payload))
+        elif op == OP_SAMPLE:
+            runner.sample(logits, *unpack_sample(payload))
         else:
-            raise RuntimeError(f"unknown runner call {op!r}")
+            raise RuntimeError(f"unknown runner call {op}")
 
 
 def tp_params_from_state_dict(cfg: TransformerConfig, sd: Dict[str, torch.Tensor], tp: int, rank: int,

@@ -217,3 +217,17 @@ def test_abort_request_frees_blocks_and_work():
     assert eng.finished[a].finish_reason == "abort"
     assert eng.blocks.num_free() == free0
     assert not eng.abort_request(a)  # already gone
+
+
+def test_tp_runner_messages_round_trip():
+    """The tensor-parallel serving control messages (decode inputs with ragged
+    block tables, sampling temperatures and 64-bit seeds) survive packing."""
+    import numpy as np
+    from lora_kernel_b200.serve.tp_runner import pack_decode, pack_sample, unpack_decode, unpack_sample
+    t, p, s, bt = unpack_decode(pack_decode([5, 6, 7], [10, 20, 30], [100, 200, 300], [[1], [3, 4, 5], [9, 8]]))
+    assert t.tolist() == [5, 6, 7] and p.tolist() == [10, 20, 30] and s.tolist() == [100, 200, 300]
+    assert bt.tolist() == [[1, 0, 0], [3, 4, 5], [9, 8, 0]] and bt.dtype == np.int32
+    for temps, seed in [(None, 0), ([0.7, 1.0], (1 << 64) - 1), ([0.5], 7)]:
+        got_t, got_s = unpack_sample(pack_sample(temps, seed))
+        assert got_s == seed
+        assert got_t is None if temps is None else np.allclose(got_t, temps)
