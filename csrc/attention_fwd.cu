@@ -71,13 +71,16 @@ struct FwdCfg {
   static constexpr int OFF_K = 2 * QB;
   static constexpr int OFF_V = OFF_K + NS * QB;
   static constexpr int OFF_BAR = OFF_V + NS * QB;
-  static constexpr int SMEM = OFF_BAR + 256;
+  static constexpr int OFF_XCH = OFF_BAR + 256;  // split softmax: row-max exchange slots (4 KB)
+  static constexpr int SMEM = OFF_XCH + 4096;
   static constexpr int TMEM_COLS = 512;  // S_a, S_b (P in their first 64 columns), O_a, O_b
-  static constexpr int THREADS = 320;    // TMA warp, MMA warp, two groups of 4 softmax warps
+  // TMA warp, MMA warp, two groups of 4 softmax warps (thread = query row) or,
+  // with split rows, two groups of 8 (two threads per row, 64 keys each)
+  static constexpr int threads(int split) { return 64 + 32 * 4 * split * 2; }
 };
 
-template <int DH, int EMU>
-__global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
+template <int DH, int EMU, int SPLIT>
+__global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_kv,
                     const AttnFwdArgs args) {
   using C = FwdCfg<DH>;
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + 8 * t, 1);
-      mbar_init(p_full + 8 * t, 4);
+      mbar_init(p_full + 8 * t, 4 * SPLIT);
       mbar_init(o_done + 8 * t, 1);
     }
     mbar_init(drain, 1);
@@ -140,6 +143,9 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_kv);
   }
+  if (SPLIT == 2)
+    for (int i = threadIdx.x; i < 512; i += blockDim.x)
+      reinterpret_cast<unsigned long long*>(smem + C::OFF_XCH)[i] = 0ull;  // sequence 0: never used
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -273,6 +279,160 @@ __global__ void __launch_bounds__(FwdCfg<DH>::THREADS, 1)
       }
       tc_commit(drain);
       bounded_wait(drain, 0, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+    }
+  } else if constexpr (SPLIT == 2) {
+    // ------------------------------------------------- softmax, split rows
+    // Group t (warps 2..9: tile a, 10..17: tile b), 8 warps: two threads per
+    // query row (the warps w and w + 4 share TMEM lane quarter w % 4), each
+    // owning 64 of the tile's 128 keys, so each SMSP has two softmax warps per
+    // group to hide TMEM and MUFU latency.  The partners exchange their row max
+    // through a 64-bit {sequence, value} slot in shared memory (a bounded poll,
+    // no named barrier); sums stay per half until the end.  A thread cannot
+    // write its next slot before its partner read the last one: the next S
+    // tile needs both halves' P of this one (p_full counts all 8 warps).
+    const int t = (warp - 2) >> 3;
+    const int hf = ((warp - 2) >> 2) & 1;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qt = 2 * qp + t;
+    const int ql = qt * 128 + r;
+    const int q = q_off + ql;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + DH * t + lane_off;
+    const int jbt = t == 0 ? jb0 : jb1;
+    const int n_t = (t == 0 ? je0 : je1) - jbt;
+    volatile unsigned long long* xch = reinterpret_cast<volatile unsigned long long*>(smem + C::OFF_XCH);
+    volatile unsigned long long* mine = xch + ((t * 4 + quarter) * 2 + hf) * 32 + lane;
+    volatile unsigned long long* theirs = xch + ((t * 4 + quarter) * 2 + (hf ^ 1)) * 32 + lane;
+    auto exchange = [&](uint32_t seq, float v, float& other) -> bool {
+      *mine = ((unsigned long long)seq << 32) | __float_as_uint(v);
+      const uint64_t t0 = globaltimer();
+      while (true) {
+        const unsigned long long x = *theirs;
+        if ((uint32_t)(x >> 32) == seq) {
+          other = __uint_as_float((uint32_t)x);
+          return true;
+        }
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > LK_WAIT_TIMEOUT_NS) {
+          atomicCAS(args.status, 0, LK_ERR_TIMEOUT_ACCUM);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    };
+    float m_used = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int jj = 0; jj < n_t; ++jj) {
+      const int j = jbt + jj;
+      bool w_ok = bounded_wait(s_full + 8 * t, jj & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool need_mask = (args.causal && j * 128 + 127 > q_off + qt * 128) || (j + 1) * 128 > Skv ||
+                             (args.window > 0 && j * 128 <= q - args.window + 127);
+      const int kbase = j * 128 + 64 * hf;  // this thread's 64 keys
+      const int khi = min(Skv - 1, args.causal ? q : Skv - 1) - kbase;
+      const int klo = (args.window > 0 ? q - args.window + 1 : 0) - kbase;
+      auto mask_chunk = [&](uint32_t (&x)[32], int c) {
+        if (!need_mask) return;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c * 32 + e > khi || c * 32 + e < klo) x[e] = __float_as_uint(-INFINITY);
+      };
+      uint32_t s0[32], s1[32];
+      tmem_ld32(tS + 64 * hf, s0);
+      tmem_ld32(tS + 64 * hf + 32, s1);
+      tc_wait_ld();
+      mask_chunk(s0, 0);
+      mask_chunk(s1, 1);
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        m4[e & 3] = fmaxf(m4[e & 3], fmaxf(__uint_as_float(s0[e]), __uint_as_float(s1[e])));
+      float mother = -INFINITY;
+      w_ok = exchange((uint32_t)jj + 1u, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])), mother);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      const float mraw = fmaxf(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])), mother);
+      const float mx = mraw * args.sl2;
+      const float m_new = (mx > m_used + 8.f) ? mx : m_used;
+      const float alpha = (m_new != m_used) ? fast_exp2(m_used - m_new) : 1.f;
+      const float mb = (m_new == -INFINITY) ? 0.f : m_new;
+      // P as bf16 pairs: keys [64 hf + 32 c, +32) -> TMEM columns 32 hf + 16 c (the
+      // partner's scores there are already in its registers: it exchanged its max)
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
+      auto emit = [&](const uint32_t (&x)[32], int c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(x[e]), args.sl2, -mb));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(x[e + 1]), args.sl2, -mb));
+          r4[(e >> 1) & 3] += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tS + 32 * hf + 16 * c, pk);
+      };
+      emit(s0, 0);
+      emit(s1, 1);
+      const float rowsum = (r4[0] + r4[1]) + (r4[2] + r4[3]);
+      // rescale this half of the O row (rare): PV(jj-1) must have finished
+      if (jj > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        w_ok = bounded_wait(o_done + 8 * t, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DH / 64; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(tO + hf * (DH / 2) + c * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(tO + hf * (DH / 2) + c * 32, ov);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + 8 * t);
+      l_run = l_run * alpha + rowsum;
+      m_used = m_new;
+    }
+    if (ok && n_t > 0) {
+      bool w_ok = bounded_wait(o_done + 8 * t, (n_t - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+      float lother = 0.f;
+      w_ok = w_ok && exchange(0x7FFFFFFFu, l_run, lother);
+      if (__all_sync(0xffffffffu, w_ok)) {
+        tc_fence_after();
+        const float l_tot = l_run + lother;
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        __nv_bfloat16* orow = args.o + (int64_t)(row0 + ql) * args.ldo + h * DH + hf * (DH / 2);
+#pragma unroll 1
+        for (int c = 0; c < DH / 64; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tO + hf * (DH / 2) + c * 32, v);
+          tc_wait_ld();
+          if (ql < S) {
+#pragma unroll
+            for (int d = 0; d < 32; d += 8)
+              *reinterpret_cast<uint4*>(orow + c * 32 + d) = make_uint4(
+                  pack_bf16x2(__uint_as_float(v[d]) * inv, __uint_as_float(v[d + 1]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 2]) * inv, __uint_as_float(v[d + 3]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 4]) * inv, __uint_as_float(v[d + 5]) * inv),
+                  pack_bf16x2(__uint_as_float(v[d + 6]) * inv, __uint_as_float(v[d + 7]) * inv));
+          }
+        }
+        if (ql < S && hf == 0)
+          args.lse[((int64_t)b * args.Hq + h) * S + ql] =
+              l_tot > 0.f ? (m_used + log2f(l_tot)) * 0.69314718055994531f : -INFINITY;
+      }
     }
   } else {
     // ---------------------------------------------------------- softmax
@@ -465,10 +625,17 @@ static int launch_fwd(const LkAttnDesc& d, cudaStream_t s) {
     const char* e = getenv("LK_ATTN_EXP_EMU");
     return e ? atoi(e) : 0;
   }();
+  // LK_ATTN_SPLIT=1: two threads per query row (16 softmax warps)
+  static const int split = [] {
+    const char* e = getenv("LK_ATTN_SPLIT");
+    return (e && atoi(e) == 1) ? 2 : 1;
+  }();
   a.emu = emu;
-  auto k = a.emu >= 4 ? attn_fwd_kernel<DH, 4> : a.emu >= 2 ? attn_fwd_kernel<DH, 2> : attn_fwd_kernel<DH, 0>;
+  auto k = split == 2 ? attn_fwd_kernel<DH, 0, 2>
+                      : (a.emu >= 4 ? attn_fwd_kernel<DH, 4, 1>
+                                    : a.emu >= 2 ? attn_fwd_kernel<DH, 2, 1> : attn_fwd_kernel<DH, 0, 1>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  k<<<a.n_qtiles * d.Hq * d.B, C::THREADS, C::SMEM, s>>>(tm, tkv, a);
+  k<<<a.n_qtiles * d.Hq * d.B, C::threads(split), C::SMEM, s>>>(tm, tkv, a);
   return check_launch("attn_fwd");
 }
 
