@@ -134,14 +134,18 @@ class QuantizedWeight:
         if out is None:
             out = torch.empty(M, self.N, dtype=torch.bfloat16, device=x.device)
         if M <= 256 and self.K % 64 == 0 and self.N % 4 == 0 and (self.fmt != "int4" or self.group % 64 == 0):
-            splits = C().dq_gemm_splits(M, self.N, self.K)
+            # split-K partials live in one fixed buffer per device (allocated once, so
+            # CUDA graphs captured against it stay valid); the split count shrinks
+            # to fit it
+            splits = min(C().dq_gemm_splits(M, self.N, self.K), DQ_PARTIAL_FLOATS // (M * self.N))
             part = None
             if splits > 1:
-                key = (x.device, splits * M * self.N)
-                part = _dq_parts.get(key)
+                part = _dq_parts.get(x.device)
                 if part is None:
-                    part = torch.empty(splits * M * self.N, dtype=torch.float32, device=x.device)
-                    _dq_parts[key] = part
+                    part = torch.empty(DQ_PARTIAL_FLOATS, dtype=torch.float32, device=x.device)
+                    _dq_parts[x.device] = part
+            else:
+                splits = 1
             C().dq_gemm(x, self.q, self.scale, self.zero, QFMT[self.fmt], self.N, self.K, self.group, out,
                         residual, part, splits, status(x.device))
             return out
@@ -150,4 +154,5 @@ class QuantizedWeight:
         return gemm(x, w, out, epi="bf16_resid" if residual is not None else "bf16", residual=residual)
 
 
+DQ_PARTIAL_FLOATS = 16 << 20  # 64 MB of fp32 split-K partials per device
 _dq_parts = {}
