@@ -501,7 +501,8 @@ void dequant_mx_rows(torch::Tensor q, int64_t fmt, torch::Tensor sf, torch::Tens
 // K14 decode form: weight-streaming dequant GEMM (tcgen05), M <= 256.
 void dq_gemm(torch::Tensor x, torch::Tensor q, torch::Tensor scale, c10::optional<torch::Tensor> zero, int64_t fmt,
              int64_t N, int64_t K, int64_t group, torch::Tensor y, c10::optional<torch::Tensor> resid,
-             c10::optional<torch::Tensor> partial, int64_t splits, torch::Tensor status) {
+             c10::optional<torch::Tensor> partial, int64_t splits, torch::Tensor status,
+             c10::optional<torch::Tensor> counters) {
   const c10::cuda::CUDAGuard g(x.device());
   need(x, "x", torch::kBFloat16);
   need(y, "y", torch::kBFloat16);
@@ -533,6 +534,11 @@ void dq_gemm(torch::Tensor x, torch::Tensor q, torch::Tensor scale, c10::optiona
     need_contig(*partial, "partial", torch::kFloat32);
     TORCH_CHECK(partial->numel() >= (int64_t)std::max<int64_t>(splits, 1) * d.M * N, "dq_gemm: partial size");
     d.partial = partial->data_ptr<float>();
+  }
+  if (counters.has_value()) {
+    need_contig(*counters, "counters", torch::kInt32);
+    TORCH_CHECK(counters->numel() >= LK_DQ_COUNTERS, "dq_gemm: counters need LK_DQ_COUNTERS entries");
+    d.counters = counters->data_ptr<int>();
   }
   need(status, "status", torch::kInt32);
   d.status = status.data_ptr<int>();

@@ -93,6 +93,35 @@ inline bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType d
   return true;
 }
 
+// 3-D tiled TMA map over [d2][d1][d0] (d0 contiguous) with byte strides s1
+// (between d1 entries) and s2 (between d2 entries), box [b2][b1][b0], no
+// swizzle.  Out-of-range boxes read zeros.  Returns false on error.
+inline bool make_tmap_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                         int64_t d0, int64_t d1, int64_t d2, int64_t s1, int64_t s2, int b0, int b1, int b2) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) {
+    last_error() = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || s1 % 16 != 0 || s2 % 16 != 0 || (b0 * elem_bytes) % 16 != 0) {
+    last_error() = "TMA operand is not 16-byte aligned";
+    return false;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1, (cuuint64_t)s2};
+  cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    last_error() = buf;
+    return false;
+  }
+  return true;
+}
+
 inline int num_sms() {
   static int n[64] = {0};
   int dev = 0;

@@ -346,6 +346,313 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
     out[(int64_t)seq * ldo + h * DH + lane + 32 * i] = __float2bfloat16(acc[i] * inv);
 }
 
+// ------------------------------------------------ decode attention, paged TMA form
+// Same contract as decode_attn_kernel (grid (num_splits, Hkv, num_seqs), same
+// partial layout for the combine pass), built around an asynchronous page ring:
+//   warp 4      producer: per KV page of the split, one 3-D TMA box for the
+//               page's K rows of this KV head, one for its V rows, and bulk
+//               copies of the page's K / V scales, into a ring of NS stages on
+//               one mbarrier each; the block table is read 32 entries at a time;
+//   warps 0-3   consumers, one pass with an online softmax per warp: LPT lanes
+//               per token (16-byte shared-memory loads of the cached row), the
+//               query slice in fp32 registers, packed f32x2 FMAs for q.k and
+//               p.v, the running max rescaling the warp's accumulators only
+//               when it grows; the four warps' (max, sum, output) are merged at
+//               the end through shared memory.
+// Pages are fetched whole; tokens outside [t0, t1) or past the context are
+// masked.  A block id outside [0, num_blocks) (bounds-checked builds) is
+// reported in *status and its page is skipped (no copy is issued).
+constexpr int DEC_CONSUMERS = 4;
+constexpr int DEC_THREADS = 32 * (DEC_CONSUMERS + 1);
+
+struct DecLayout {
+  int sk, ss, stage, ns, merge_off, bar_off, smem;
+};
+
+__host__ __device__ inline int dec_align128(int x) { return (x + 127) & ~127; }
+
+__host__ __device__ inline DecLayout dec_layout(int bs, int DH, int esize, int Hkv, int G, bool scaled) {
+  DecLayout L;
+  L.sk = dec_align128(bs * DH * esize);
+  L.ss = scaled ? dec_align128(bs * Hkv * 4) : 0;
+  L.stage = 2 * L.sk + 2 * L.ss;
+  int ns = (48 * 1024) / L.stage;
+  L.ns = ns < 2 ? 2 : (ns > 12 ? 12 : ns);
+  L.merge_off = L.ns * L.stage;
+  const int merge = DEC_CONSUMERS * G * DH * 4 + 2 * DEC_CONSUMERS * G * 4;
+  L.bar_off = dec_align128(L.merge_off + merge);
+  L.smem = L.bar_off + 2 * L.ns * 8 + 4 * L.ns + 16 + 128;
+  return L;
+}
+
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float x0, float x1, float y0, float y1) {
+  // (a0, a1) += (x0, x1) * (y0, y1) as one packed f32x2 FMA
+  uint64_t a, x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(x0), "f"(x1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(y0), "f"(y1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+}
+
+// N cached values at shared address p -> floats (scale not applied)
+template <int KV, int N>
+__device__ __forceinline__ void kv_load_smem(const uint8_t* p, float (&x)[N]) {
+  constexpr int BYTES = N * (KV == 0 ? 2 : 1);
+  static_assert(BYTES % 4 == 0, "kv_load_smem: 4-byte multiples");
+  uint32_t w[BYTES / 4];
+  if constexpr (BYTES >= 16) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i) {
+      const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+      w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+    }
+  } else if constexpr (BYTES == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x, w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+#pragma unroll
+  for (int i = 0; i < N; i += 2) {
+    if constexpr (KV == 0) {
+      const uint32_t u = w[i / 2];
+      x[i] = __uint_as_float(u << 16);
+      x[i + 1] = __uint_as_float(u & 0xFFFF0000u);
+    } else if constexpr (KV == 1) {
+      // two e4m3 codes -> f16x2 (exact) -> two floats
+      const uint16_t pair = (uint16_t)(w[i / 4] >> (8 * (i & 3)));
+      uint32_t h2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(pair));
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+      x[i] = f.x;
+      x[i + 1] = f.y;
+    } else {
+      x[i] = (float)(int8_t)((w[i / 4] >> (8 * (i & 3))) & 0xFFu);
+      x[i + 1] = (float)(int8_t)((w[i / 4] >> (8 * (i & 3) + 8)) & 0xFFu);
+    }
+  }
+}
+
+template <int KV, int DH, int G>
+__global__ void __launch_bounds__(DEC_THREADS) decode_attn_tma_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    const __nv_bfloat16* __restrict__ q, int64_t ldq, const float* __restrict__ ks, const float* __restrict__ vs,
+    const int* __restrict__ block_tables, int max_blocks, const int* __restrict__ ctx_lens, int block_size,
+    int Hkv, float sl2, int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo, float* __restrict__ part_o,
+    float* __restrict__ part_ml, int num_splits, int num_blocks, int* status) {
+  constexpr int ES = KV == 0 ? 2 : 1;
+  constexpr int LPT = G <= 4 ? 8 : 16;  // lanes per token
+  constexpr int DPL = DH / LPT;         // cached values per lane
+  constexpr int TPW = 32 / LPT;         // tokens per warp step
+  constexpr int TPS = TPW * DEC_CONSUMERS;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = dsm_raw + ((128 - (smem_u32(dsm_raw) & 127)) & 127);
+  const int bs = block_size;
+  const DecLayout L = dec_layout(bs, DH, ES, Hkv, G, KV != 0);
+  const uint32_t sbase = smem_u32(dsm);
+  const uint32_t full0 = sbase + L.bar_off, empty0 = full0 + 8 * L.ns;
+  volatile int* stage_ok = reinterpret_cast<volatile int*>(dsm + L.bar_off + 16 * L.ns);
+  volatile int* abort_flag = stage_ok + L.ns;
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int ctx = ctx_lens[seq];
+  const int t0 = split * split_len;
+  const int t1 = min(ctx, t0 + split_len);
+  const int pg0 = t0 / bs;
+  const int npg = t1 > t0 ? (t1 + bs - 1) / bs - pg0 : 0;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < L.ns; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, DEC_CONSUMERS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncthreads();
+
+  if (warp == DEC_CONSUMERS) {
+    // ------------------------------------------------------------ producer
+    const int* bt = block_tables + (int64_t)seq * max_blocks;
+    const uint32_t tx = 2u * bs * DH * ES + (KV != 0 ? 2u * bs * Hkv * 4 : 0u);
+    uint32_t pending = 0, par = 0;
+    int blk_lane = 0;
+    for (int i = 0; i < npg; ++i) {
+      if ((i & 31) == 0) blk_lane = i + lane < npg ? bt[pg0 + i + lane] : 0;
+      const int blk = __shfl_sync(0xffffffffu, blk_lane, i & 31);
+      const int s = i % L.ns;
+      const uint32_t ph = (uint32_t)(i / L.ns) & 1;
+      int ok = 1;
+      if (lane == 0) {
+        ok = bounded_wait(empty0 + 8 * s, ph ^ 1, status, LK_ERR_TIMEOUT_EMPTY, abort_flag);
+        if (ok) {
+          const bool valid = LK_BOUNDS(blk >= 0 && blk < num_blocks, status, LK_ERR_BAD_INDEX);
+          stage_ok[s] = valid;
+          if (valid) {
+            const uint32_t st = sbase + s * L.stage;
+            mbar_expect_tx(full0 + 8 * s, tx);
+            tma_load_3d(st, &tmK, full0 + 8 * s, 0, kvh, blk * bs);
+            tma_load_3d(st + L.sk, &tmV, full0 + 8 * s, 0, kvh, blk * bs);
+            if constexpr (KV != 0) {
+              bulk_load(st + 2 * L.sk, ks + (int64_t)blk * bs * Hkv, bs * Hkv * 4, full0 + 8 * s);
+              bulk_load(st + 2 * L.sk + L.ss, vs + (int64_t)blk * bs * Hkv, bs * Hkv * 4, full0 + 8 * s);
+            }
+            pending |= 1u << s;
+            par = (par & ~(1u << s)) | (ph << s);
+          } else {
+            mbar_arrive(full0 + 8 * s);
+          }
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        if (lane == 0)
+          for (int j = 0; j < L.ns; ++j)
+            if (pending & (1u << j))
+              bounded_wait(full0 + 8 * j, (par >> j) & 1, status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+        break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int grp = lane / LPT, sub = lane % LPT;
+  float qf[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint32_t* qp = reinterpret_cast<const uint32_t*>(q + (int64_t)seq * ldq + (kvh * G + g) * DH + sub * DPL);
+#pragma unroll
+    for (int i = 0; i < DPL / 2; ++i) {
+      const float2 f = unpack_bf16x2(qp[i]);
+      qf[g][2 * i] = f.x;
+      qf[g][2 * i + 1] = f.y;
+    }
+  }
+  float m[G], l[G], acc[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) acc[g][d] = 0.f;
+  }
+  for (int i = 0; i < npg; ++i) {
+    const int s = i % L.ns;
+    const bool ok = bounded_wait(full0 + 8 * s, (uint32_t)(i / L.ns) & 1, status, LK_ERR_TIMEOUT_FULL, abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const bool page_ok = stage_ok[s] != 0;
+    const uint8_t* st = dsm + s * L.stage;
+    const int tp = (pg0 + i) * bs;
+    for (int j0 = 0; j0 < bs; j0 += TPS) {
+      const int j = j0 + warp * TPW + grp;
+      const int tt = tp + j;
+      const bool tok = page_ok && j < bs && tt >= t0 && tt < t1;
+      float sc[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g] = 0.f;
+      if (tok) {
+        float x[DPL];
+        kv_load_smem<KV, DPL>(st + (j * DH + sub * DPL) * ES, x);
+        const float kscale = (KV == 0 ? 1.f : reinterpret_cast<const float*>(st + 2 * L.sk)[j * Hkv + kvh]) * sl2;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int d = 0; d < DPL; d += 2) ffma2(a0, a1, qf[g][d], qf[g][d + 1], x[d], x[d + 1]);
+          sc[g] = (a0 + a1) * kscale;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int o = LPT / 2; o > 0; o >>= 1) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+      }
+      float p[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float tmax = tok ? sc[g] : -INFINITY;
+#pragma unroll
+        for (int o = LPT; o < 32; o <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        if (tmax > m[g]) {  // warp-uniform: the running max grows
+          const float alpha = m[g] == -INFINITY ? 0.f : fast_exp2(m[g] - tmax);
+          l[g] *= alpha;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) acc[g][d] *= alpha;
+          m[g] = tmax;
+        }
+        p[g] = tok ? fast_exp2(sc[g] - m[g]) : 0.f;
+        l[g] += p[g];
+      }
+      if (tok) {
+        float v[DPL];
+        kv_load_smem<KV, DPL>(st + L.sk + (j * DH + sub * DPL) * ES, v);
+        const float vscale = KV == 0 ? 1.f : reinterpret_cast<const float*>(st + 2 * L.sk + L.ss)[j * Hkv + kvh];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pv = p[g] * vscale;
+#pragma unroll
+          for (int d = 0; d < DPL; d += 2) ffma2(acc[g][d], acc[g][d + 1], pv, pv, v[d], v[d + 1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+  }
+  // token groups of the warp -> one (sum, output) per warp
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int o = LPT; o < 32; o <<= 1) {
+      l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) acc[g][d] += __shfl_xor_sync(0xffffffffu, acc[g][d], o);
+    }
+  }
+  float* po = reinterpret_cast<float*>(dsm + L.merge_off);  // [4][G][DH]
+  float* pm = po + DEC_CONSUMERS * G * DH;                   // [4][G]
+  float* pl = pm + DEC_CONSUMERS * G;                        // [4][G]
+  if (grp == 0)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) po[(warp * G + g) * DH + sub * DPL + d] = acc[g][d];
+  if (lane == 0)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      pm[warp * G + g] = m[g];
+      pl[warp * G + g] = l[g];
+    }
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * DEC_CONSUMERS) : "memory");
+  for (int idx = tid; idx < G * DH; idx += 32 * DEC_CONSUMERS) {
+    const int g = idx / DH, d = idx % DH;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < DEC_CONSUMERS; ++w) M = fmaxf(M, pm[w * G + g]);
+    float o = 0.f, S = 0.f;
+#pragma unroll
+    for (int w = 0; w < DEC_CONSUMERS; ++w) {
+      const float mw = pm[w * G + g];
+      const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - M);
+      o += po[(w * G + g) * DH + d] * f;
+      S += pl[w * G + g] * f;
+    }
+    const int h = kvh * G + g;
+    if (num_splits == 1) {
+      out[(int64_t)seq * ldo + h * DH + d] = __float2bfloat16(S > 0.f ? o / S : 0.f);
+    } else {
+      part_o[(((int64_t)seq * (Hkv * G) + h) * num_splits + split) * DH + d] = o;
+      if (d == 0) {
+        float* ml = part_ml + (((int64_t)seq * (Hkv * G) + h) * num_splits + split) * 2;
+        ml[0] = M;
+        ml[1] = S;
+      }
+    }
+  }
+}
+
 // Gather a sequence's cached K/V (token t at slot slots[t]) into contiguous
 // bf16 rows [n, 2*Hkv*Dh]: keys in columns [0, Hkv*Dh), values after.
 template <int KV>
@@ -544,8 +851,61 @@ __global__ void sample_topp_kernel(const __nv_bfloat16* __restrict__ logits, int
   }
 }
 
+// Paged TMA form (default); false when this launch cannot use it.
+static bool decode_tma_ok(const LkDecodeDesc& d) {
+  static const bool v1 = [] {
+    const char* e = getenv("LK_DECODE_V1");
+    return e && e[0] == '1';
+  }();
+  return !v1 && d.block_size % 4 == 0 && d.block_size <= 256 && d.num_blocks > 0;
+}
+
+template <int KV, int DH>
+static int launch_decode_tma(const LkDecodeDesc& d, int G, int nsplit, cudaStream_t s) {
+  constexpr int ES = KV == 0 ? 2 : 1;
+  const DecLayout L = dec_layout(d.block_size, DH, ES, d.Hkv, G, KV != 0);
+  const CUtensorMapDataType dt = KV == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const int64_t slots = (int64_t)d.num_blocks * d.block_size;
+  CUtensorMap tk, tv;
+  if (!make_tmap_3d(&tk, d.k_cache, dt, ES, DH, d.Hkv, slots, (int64_t)DH * ES, (int64_t)d.Hkv * DH * ES, DH, 1,
+                    d.block_size) ||
+      !make_tmap_3d(&tv, d.v_cache, dt, ES, DH, d.Hkv, slots, (int64_t)DH * ES, (int64_t)d.Hkv * DH * ES, DH, 1,
+                    d.block_size))
+    return -1;
+  dim3 grid(nsplit, d.Hkv, d.num_seqs);
+  const float sl2 = d.scale * 1.4426950408889634f;
+#define LK_DEC2(GG)                                                                                        \
+  {                                                                                                        \
+    auto k = decode_attn_tma_kernel<KV, DH, GG>;                                                           \
+    if (L.smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem);  \
+    k<<<grid, DEC_THREADS, L.smem, s>>>(tk, tv, (const __nv_bfloat16*)d.q, d.ldq, d.k_scale, d.v_scale,    \
+                                        d.block_tables, d.max_blocks, d.ctx_lens, d.block_size, d.Hkv, sl2, \
+                                        d.split_len, (__nv_bfloat16*)d.out, d.ldo, d.part_o, d.part_ml,    \
+                                        nsplit, d.num_blocks, d.status);                                   \
+    break;                                                                                                 \
+  }
+  switch (G) {
+    case 1: LK_DEC2(1)
+    case 2: LK_DEC2(2)
+    case 4: LK_DEC2(4)
+    case 8: LK_DEC2(8)
+    default: return fail("decode_attention: GQA group must be 1, 2, 4 or 8");
+  }
+#undef LK_DEC2
+  if (check_launch("decode_attn_tma")) return -1;
+  if (nsplit > 1) {
+    const int64_t warps = (int64_t)d.num_seqs * d.Hkv * G;
+    decode_combine_kernel<DH><<<cdiv(warps * 32, 256), 256, 0, s>>>(
+        d.part_o, d.part_ml, d.num_seqs, d.Hkv * G, nsplit, d.ctx_lens, d.split_len,
+        (__nv_bfloat16*)d.out, d.ldo);
+    return check_launch("decode_combine");
+  }
+  return 0;
+}
+
 template <int KV, int DH>
 static int launch_decode_g(const LkDecodeDesc& d, int G, int nsplit, int smem, cudaStream_t s) {
+  if (decode_tma_ok(d)) return launch_decode_tma<KV, DH>(d, G, nsplit, s);
   dim3 grid(nsplit, d.Hkv, d.num_seqs);
   const float sl2 = d.scale * 1.4426950408889634f;
   using T = typename KvT<KV>::T;

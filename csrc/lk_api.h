@@ -475,7 +475,12 @@ typedef struct LkDqGemmDesc {
   float* partial;
   int splits;
   int* status;
+  // optional: LK_DQ_COUNTERS int32 zeros, one per 128-row weight tile; with it the
+  // last split of each tile sums the partials in the same launch (else a second
+  // kernel does); the kernel leaves them zero again
+  int* counters;
 } LkDqGemmDesc;
+#define LK_DQ_COUNTERS 16384
 int lk_dq_gemm(const LkDqGemmDesc* d, cudaStream_t s);
 int lk_dq_gemm_splits(int M, int N, int K);
 

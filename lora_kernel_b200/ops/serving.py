@@ -138,16 +138,13 @@ class QuantizedWeight:
             # CUDA graphs captured against it stay valid); the split count shrinks
             # to fit it
             splits = min(C().dq_gemm_splits(M, self.N, self.K), DQ_PARTIAL_FLOATS // (M * self.N))
-            part = None
+            part = counters = None
             if splits > 1:
-                part = _dq_parts.get(x.device)
-                if part is None:
-                    part = torch.empty(DQ_PARTIAL_FLOATS, dtype=torch.float32, device=x.device)
-                    _dq_parts[x.device] = part
+                part, counters = _dq_workspace(x.device)
             else:
                 splits = 1
             C().dq_gemm(x, self.q, self.scale, self.zero, QFMT[self.fmt], self.N, self.K, self.group, out,
-                        residual, part, splits, status(x.device))
+                        residual, part, splits, status(x.device), counters)
             return out
         from .gemm import gemm
         w = self.dequantize(scratch)
@@ -155,4 +152,17 @@ class QuantizedWeight:
 
 
 DQ_PARTIAL_FLOATS = 16 << 20  # 64 MB of fp32 split-K partials per device
+DQ_COUNTERS = 16384           # one per 128-row weight tile; the kernel leaves them zero
 _dq_parts = {}
+
+
+def _dq_workspace(device):
+    """The split-K partial buffer and tile counters of `device`, allocated once
+    (CUDA graphs captured against them stay valid; launches on one stream reuse
+    them in order)."""
+    ws = _dq_parts.get(device)
+    if ws is None:
+        ws = (torch.empty(DQ_PARTIAL_FLOATS, dtype=torch.float32, device=device),
+              torch.zeros(DQ_COUNTERS, dtype=torch.int32, device=device))
+        _dq_parts[device] = ws
+    return ws

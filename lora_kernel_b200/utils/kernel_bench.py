@@ -251,7 +251,8 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--small", action="store_true", help="one small GEMM (for profiling)")
     ap.add_argument("--pair", type=int, default=-1,
-                    help="GEMMs on CTA pairs (cta_group::2, 256-row tiles): 1 on, 0 off, -1 the default")
+                    help="GEMMs on CTA pairs (cta_group::2, 256-row tiles): 1 on (tile width by wave fill), "
+                         "2 on with 256x256 tiles, 3 on with 256x128 tiles, 0 off, -1 the default")
     args = ap.parse_args()
     if args.pair >= 0:
         from lora_kernel_b200._ext import C

@@ -309,10 +309,12 @@ def test_peer_wait_gives_up_with_a_status_and_the_context_survives():
     assert float(x.sum().item()) == 1023 * 1024 / 2
 
 
+@pytest.mark.parametrize("mode", [2, 3])
 @pytest.mark.parametrize("layout", ["tn", "dgrad", "wgrad", "nt"])
-def test_gemm_cta_pair_matches_fp32(layout):
-    """256 x 256 tiles computed by a CTA pair (tcgen05.mma.cta_group::2) with
-    ragged M, N and K edges, every operand layout and epilogue."""
+def test_gemm_cta_pair_matches_fp32(layout, mode):
+    """256 x 256 (mode 2) and 256 x 128 (mode 3) tiles computed by a CTA pair
+    (tcgen05.mma.cta_group::2) with ragged M, N and K edges, every operand
+    layout and epilogue."""
     from lora_kernel_b200._ext import C
     from lora_kernel_b200.ops.gemm import gemm
     torch.manual_seed(3)
@@ -326,7 +328,7 @@ def test_gemm_cta_pair_matches_fp32(layout):
     else:
         a, b = _mn(M, K), _bf(N, K)
     ref = a.float() @ b.float().t()
-    C().gemm_set_pair(1)
+    C().gemm_set_pair(mode)
     try:
         n0 = C().gemm_pair_count()
         out = gemm(a, b)
@@ -345,10 +347,11 @@ def test_gemm_cta_pair_matches_fp32(layout):
         assert C().gemm_pair_count() > n0, "the CTA-pair path did not run"
         _status_ok()
     finally:
-        C().gemm_set_pair(0)
+        C().gemm_set_pair(1)
 
 
-def test_gemm_cta_pair_fused_epilogues():
+@pytest.mark.parametrize("mode", [1, 2, 3])
+def test_gemm_cta_pair_fused_epilogues(mode):
     from lora_kernel_b200._ext import C
     from lora_kernel_b200.ops.gemm import gemm, interleave_gate_up, linear_swiglu
     torch.manual_seed(4)
@@ -357,7 +360,7 @@ def test_gemm_cta_pair_fused_epilogues():
     wg, wu = _bf(F, D, scale=0.1), _bf(F, D, scale=0.1)
     w = _bf(2048, D)
     r = _bf(T, 2048)
-    C().gemm_set_pair(1)
+    C().gemm_set_pair(mode)
     try:
         n0 = C().gemm_pair_count()
         gu, h = linear_swiglu(x, interleave_gate_up(wg, wu))
@@ -369,7 +372,7 @@ def test_gemm_cta_pair_fused_epilogues():
         assert C().gemm_pair_count() >= n0 + 2
         _status_ok()
     finally:
-        C().gemm_set_pair(0)
+        C().gemm_set_pair(1)
 
 
 @pytest.mark.parametrize("M,F,D", [(256, 256, 256), (1000, 640, 384), (4096, 1536, 1024)])

@@ -66,6 +66,52 @@ def test_kv_append_gather_and_decode(kv, Hq, Hkv, Dh):
     check_status()
 
 
+@pytest.mark.parametrize("bs", [8, 32])
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_decode_attention_block_sizes_and_unaligned_splits(bs, kv):
+    """Pages of 8 and 32 tokens and split boundaries that cut pages (split_len
+    40): the paged decode kernel masks tokens outside its split, against fp32."""
+    from lora_kernel_b200.ops import serving as SV
+    torch.manual_seed(3)
+    Hq, Hkv, Dh, nblk = 16, 4, 128, 96
+    slots_total = bs * nblk
+    kc = torch.zeros(slots_total, Hkv, Dh, dtype=SV.KV_TORCH[kv], device=dev)
+    vc = torch.zeros_like(kc)
+    ks = vs = None
+    if kv != "bf16":
+        ks = torch.zeros(slots_total, Hkv, device=dev)
+        vs = torch.zeros_like(ks)
+    ctxs = [5, 37, 300]
+    W = (Hq + 2 * Hkv) * Dh
+    perm = torch.randperm(nblk).tolist()
+    tables = [[perm.pop() for _ in range((c + bs - 1) // bs)] for c in ctxs]
+    kref, vref = [], []
+    for si, c in enumerate(ctxs):
+        qkv = torch.randn(c, W, device=dev).to(torch.bfloat16)
+        slots = torch.tensor([tables[si][t // bs] * bs + t % bs for t in range(c)], dtype=torch.int32, device=dev)
+        SV.kv_append(qkv, Hq, Hkv, Dh, slots, kc, vc, ks, vs, kv)
+        g = SV.kv_gather(kc, vc, ks, vs, slots, Hkv, Dh, kv).float()
+        kref.append(g[:, :Hkv * Dh].view(c, Hkv, Dh))
+        vref.append(g[:, Hkv * Dh:].view(c, Hkv, Dh))
+    q = torch.randn(len(ctxs), Hq * Dh, device=dev).to(torch.bfloat16)
+    bt = torch.zeros(len(ctxs), max(len(t) for t in tables), dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t)
+    ctx = torch.tensor(ctxs, dtype=torch.int32, device=dev)
+    for split in (40, 1024):
+        out = SV.decode_attention(q, kc, vc, ks, vs, bt.to(dev), ctx, bs, Hq, Hkv, Dh, kv_dtype=kv,
+                                  max_ctx=max(ctxs), split_len=split)
+        for i, c in enumerate(ctxs):
+            qi = q[i].float().view(Hq, Dh)
+            k = kref[i].repeat_interleave(Hq // Hkv, dim=1)
+            v = vref[i].repeat_interleave(Hq // Hkv, dim=1)
+            sc = torch.einsum("hd,thd->ht", qi, k) / math.sqrt(Dh)
+            ref = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), v).reshape(-1)
+            _close(out[i], ref, 2e-2, 2e-2, f"bs {bs} seq {i} split {split}")
+    from lora_kernel_b200._ext import check_status
+    check_status()
+
+
 @pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
 @pytest.mark.parametrize("M", [1, 5, 16, 40, 130, 256, 300])
 def test_quantized_matmul(fmt, M):
@@ -109,6 +155,56 @@ def test_dq_gemm_shapes_and_residual(fmt, M, N, K):
     err = (y.float() - ref).norm() / ref.norm()
     assert err < 1e-2, err
     assert torch.equal(y, y2)  # split-K partials are summed in a fixed order
+
+
+@pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
+@pytest.mark.parametrize("M", [1, 40, 130])
+def test_dq_gemm_fused_split_reduction(fmt, M):
+    """Split-K partials summed by the last split of each weight tile (tile
+    counters) give bit-identical results to the separate reduction kernel, and
+    leave the counters at zero for the next launch."""
+    from lora_kernel_b200._ext import C, status
+    from lora_kernel_b200.ops.serving import QFMT, QuantizedWeight
+    g = torch.Generator(device=dev).manual_seed(5)
+    N, K = 1000, 2048
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    qw = QuantizedWeight(w, fmt, 128)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    r = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    splits = 5
+    part = torch.empty(splits * M * N, device=dev)
+    cnt = torch.zeros(16384, dtype=torch.int32, device=dev)
+    ys = []
+    for counters in (None, cnt, cnt):
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        C().dq_gemm(x, qw.q, qw.scale, qw.zero, QFMT[fmt], N, K, 128, y, r, part, splits, status(x.device),
+                    counters)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert int(status(x.device).item()) == 0
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+    assert int(cnt.abs().sum().item()) == 0
+    ref = x.float() @ qw.dequantize().float().t() + r.float()
+    assert ((ys[1].float() - ref).norm() / ref.norm()).item() < 1e-2
+
+
+def test_dq_gemm_int4_zero_points_outside_the_bf16_exact_range():
+    """Groups whose zero point lies outside [-241, 128] (all-positive weights:
+    z = round(-min / s) far below zero) take the fp32 dequantisation path."""
+    from lora_kernel_b200.ops.serving import QuantizedWeight
+    g = torch.Generator(device=dev).manual_seed(6)
+    N, K = 256, 1024
+    w = (2.0 + 0.1 * torch.rand(N, K, device=dev, generator=g)).to(torch.bfloat16)
+    w[:128] -= 2.0  # rows 0..127 near zero (z ~ 0: bf16 path), the rest offset (z ~ -320: fp32 path)
+    qw = QuantizedWeight(w, "int4", 128)
+    assert float(qw.zero[128:].min()) < -241 and float(qw.zero[:128].max()) <= 128
+    x = torch.randn(16, K, device=dev, generator=g).to(torch.bfloat16)
+    y = qw.matmul_t(x)
+    torch.cuda.synchronize()
+    ref = x.float() @ qw.dequantize().float().t()
+    for rows in (slice(0, 128), slice(128, 256)):
+        err = (y[:, rows].float() - ref[:, rows]).norm() / ref[:, rows].norm()
+        assert err < 1e-2, (rows, err)
 
 
 def test_sampling():
