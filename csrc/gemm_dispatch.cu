@@ -2,7 +2,6 @@
 // Instantiations are spread over gemm_bf16.cu / gemm_f32.cu / gemm_fused.cu so
 // they compile in parallel.
 #include <atomic>
-#include <cmath>
 #include <cstdlib>
 
 #include "gemm_kernel.cuh"
@@ -66,21 +65,6 @@ bool use_pair(const LkGemmDesc& g) {
   if (tiles < num_sms() / 2) return false;
   ++gemm_pair_count();
   return true;
-}
-
-// Tile width of a CTA-pair GEMM: 256 x 256, or 256 x 128 when that fills the
-// last wave of pairs clearly better (fewer idle pairs at the tail).
-int pair_bn(const LkGemmDesc& g) {
-  if (gemm_pair_mode() == 2) return 256;  // LK_GEMM_PAIR=2: always 256 x 256
-  if (gemm_pair_mode() == 3) return 128;  // LK_GEMM_PAIR=3: always 256 x 128
-  if (g.bn == 256) return 256;
-  const int pairs = std::max(1, num_sms() / 2);
-  auto eff = [&](int bn) {
-    const double tiles = (double)cdiv(g.M, 256) * cdiv(g.N, bn);
-    const double waves = tiles / pairs;
-    return waves / std::ceil(waves);
-  };
-  return eff(128) > eff(256) + 0.05 ? 128 : 256;
 }
 
 int choose_bn(const LkGemmDesc& g) {

@@ -4,7 +4,6 @@
 
 namespace lk {
 int choose_bn(const LkGemmDesc& g);
-int pair_bn(const LkGemmDesc& g);
 
 int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s) {
   if (g.epi == LK_EPI_SWIGLU_BWD) {
@@ -30,9 +29,7 @@ int gemm_dispatch_fused(const LkGemmDesc& g, cudaStream_t s) {
     return launch_gemm<256, false, false, EPI_SWIGLU>(g, s);
   }
   LK_REQUIRE(g.r != nullptr && g.ldr % 8 == 0, "lk_gemm: residual epilogue needs r");
-  if (use_pair(g))
-    return pair_bn(g) == 128 ? launch_gemm<128, false, false, EPI_BF16_RESID, 0, 2>(g, s)
-                             : launch_gemm<256, false, false, EPI_BF16_RESID, 0, 2>(g, s);
+  if (use_pair(g)) return launch_gemm<256, false, false, EPI_BF16_RESID, 0, 2>(g, s);
   return choose_bn(g) == 128 ? launch_gemm<128, false, false, EPI_BF16_RESID>(g, s)
                              : launch_gemm<256, false, false, EPI_BF16_RESID>(g, s);
 }

@@ -376,7 +376,7 @@ __host__ __device__ inline DecLayout dec_layout(int bs, int DH, int esize, int H
   L.sk = dec_align128(bs * DH * esize);
   L.ss = scaled ? dec_align128(bs * Hkv * 4) : 0;
   L.stage = 2 * L.sk + 2 * L.ss;
-  int ns = (48 * 1024) / L.stage;
+  int ns = (40 * 1024) / L.stage;
   L.ns = ns < 2 ? 2 : (ns > 12 ? 12 : ns);
   L.merge_off = L.ns * L.stage;
   const int merge = DEC_CONSUMERS * G * DH * 4 + 2 * DEC_CONSUMERS * G * 4;
@@ -399,8 +399,8 @@ __device__ __forceinline__ void ffma2(float& a0, float& a1, float x0, float x1, 
 template <int KV, int N>
 __device__ __forceinline__ void kv_load_smem(const uint8_t* p, float (&x)[N]) {
   constexpr int BYTES = N * (KV == 0 ? 2 : 1);
-  static_assert(BYTES % 4 == 0, "kv_load_smem: 4-byte multiples");
-  uint32_t w[BYTES / 4];
+  static_assert(BYTES % 2 == 0, "kv_load_smem: 2-byte multiples");
+  uint32_t w[BYTES >= 4 ? BYTES / 4 : 1];
   if constexpr (BYTES >= 16) {
 #pragma unroll
     for (int i = 0; i < BYTES / 16; ++i) {
@@ -410,8 +410,10 @@ __device__ __forceinline__ void kv_load_smem(const uint8_t* p, float (&x)[N]) {
   } else if constexpr (BYTES == 8) {
     const uint2 v = *reinterpret_cast<const uint2*>(p);
     w[0] = v.x, w[1] = v.y;
-  } else {
+  } else if constexpr (BYTES == 4) {
     w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else {
+    w[0] = *reinterpret_cast<const uint16_t*>(p);
   }
 #pragma unroll
   for (int i = 0; i < N; i += 2) {
@@ -435,14 +437,16 @@ __device__ __forceinline__ void kv_load_smem(const uint8_t* p, float (&x)[N]) {
 }
 
 template <int KV, int DH, int G>
-__global__ void __launch_bounds__(DEC_THREADS) decode_attn_tma_kernel(
+__global__ void __launch_bounds__(DEC_THREADS, 4) decode_attn_tma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const __nv_bfloat16* __restrict__ q, int64_t ldq, const float* __restrict__ ks, const float* __restrict__ vs,
     const int* __restrict__ block_tables, int max_blocks, const int* __restrict__ ctx_lens, int block_size,
     int Hkv, float sl2, int split_len, __nv_bfloat16* __restrict__ out, int64_t ldo, float* __restrict__ part_o,
     float* __restrict__ part_ml, int num_splits, int num_blocks, int* status) {
   constexpr int ES = KV == 0 ? 2 : 1;
-  constexpr int LPT = G <= 4 ? 8 : 16;  // lanes per token
+  // lanes per token: the query slice and the accumulators stay at 2 * G * DH / LPT
+  // registers per lane, so four CTAs fit per SM
+  constexpr int LPT = G <= 2 ? 8 : (G == 4 ? 16 : 32);
   constexpr int DPL = DH / LPT;         // cached values per lane
   constexpr int TPW = 32 / LPT;         // tokens per warp step
   constexpr int TPS = TPW * DEC_CONSUMERS;
@@ -598,6 +602,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_tma_kernel(
         }
       }
     }
+    fence_proxy_async_smem();  // generic reads of the stage before its async-proxy (TMA) refill
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
   }

@@ -21,8 +21,10 @@
 //               warps 2..5 (one per TMEM lane quarter) drain the accumulator:
 //               thread = weight row, one coalesced store per batch row.
 // With one split the epilogue writes bf16 Y (+ R); with several, each split
-// writes an fp32 partial [split, M, N] and a reduction kernel sums them in
-// split order (deterministic, so a CUDA-graph replay equals an eager step).
+// writes an fp32 partial [split, M, N] and the partials are summed in split
+// order (deterministic, so a CUDA-graph replay equals an eager step): for
+// batches up to 4 rows by the last split of each weight tile to finish (tile
+// counters, same launch), else by a second, grid-wide kernel.
 // Every wait is bounded.
 //
 // Reference: QuantizedInferenceKernels (include/api/serving_production.hpp:211-226)
@@ -37,30 +39,22 @@ namespace {
 
 constexpr int DQ_BM = 128, DQ_BK = 64;
 constexpr int DQ_CONV_WARPS = 8;
-constexpr int DQ_THREADS = 96 + 32 * DQ_CONV_WARPS;  // raw TMA, MMA, X TMA, converters
+constexpr int DQ_THREADS = 64 + 32 * DQ_CONV_WARPS;
 
-// Ring sizes.  The raw weight ring is decoupled from the dequantised-tile ring
-// and is as deep as the shared-memory budget allows: the weights are the HBM
-// stream, so its loads run up to RAW_STAGES stages ahead of the converters.
-// The activation ring is deeper for small batches (its tiles come from L2).
-// Up to MP = 128 two CTAs stay resident per SM.
-template <int FMT, int MP>
+template <int FMT>  // 0 int8, 1 fp8 e4m3, 2 int4
+struct DqRaw {
+  static constexpr int ROW_BYTES = FMT == 2 ? DQ_BK / 2 : DQ_BK;  // raw bytes per weight row per stage
+  static constexpr int TILE = DQ_BM * ROW_BYTES;
+};
+
+// Stage counts keep two CTAs resident per SM (up to MP = 128), so one CTA's
+// pipeline fill and epilogue overlap the other's stream of weights.
+template <int MP>
 struct DqCfg {
-  static constexpr int RAW_ROW = FMT == 2 ? DQ_BK / 2 : DQ_BK;  // raw bytes per weight row per stage
-  static constexpr int RAW_TILE = DQ_BM * RAW_ROW;
+  static constexpr int STAGES = MP >= 256 ? 2 : (MP >= 64 ? 3 : 4);
   static constexpr int A_BYTES = DQ_BM * DQ_BK * 2;  // dequantised bf16 tile
-  static constexpr int A_STAGES = 2;
   static constexpr int X_BYTES = MP * DQ_BK * 2;
-  static constexpr int X_STAGES = MP <= 16 ? 8 : (MP <= 32 ? 6 : (MP <= 64 ? 4 : 3));
-  static constexpr int BUDGET = (MP <= 128 ? 104 : 200) * 1024;
-  static constexpr int RAW_LEFT = (BUDGET - A_STAGES * A_BYTES - X_STAGES * X_BYTES) / RAW_TILE;
-  static constexpr int RAW_STAGES = RAW_LEFT > 12 ? 12 : RAW_LEFT;
-  static_assert(RAW_STAGES >= 2, "dq_gemm: raw ring too shallow");
-  static constexpr int NBAR = 2 * (RAW_STAGES + A_STAGES + X_STAGES) + 2;
-  static constexpr int SMEM =
-      A_STAGES * A_BYTES + X_STAGES * X_BYTES + RAW_STAGES * RAW_TILE + NBAR * 8 + 16 + 1024;
   static constexpr int TMEM_COLS = MP < 32 ? 32 : MP;
-  static constexpr int MIN_BLOCKS = MP <= 128 ? 2 : 1;
 };
 
 struct DqArgs {
@@ -81,32 +75,6 @@ __device__ __forceinline__ uint32_t dq_sw128(int row, int chunk) {
   return (uint32_t)(row * 128 + (((chunk ^ (row & 7)) & 7) << 4));
 }
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-// (a & 0x000F000F) | 0x43004300: two 4-bit codes into the low mantissa bits of
-// a bf16 pair with exponent 2^7, i.e. the exact values 128 + q.
-__device__ __forceinline__ uint32_t nib_to_bf16x2(uint32_t a) {
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(0x000F000Fu), "r"(0x43004300u));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // 8 int4 values (one 32-bit word, low nibble first) -> 8 floats (q - z) * s, as 4 bf16 pairs
 __device__ __forceinline__ uint4 dq_int4x8(uint32_t v, float s, float zs) {
   uint32_t o[4];
@@ -116,23 +84,6 @@ __device__ __forceinline__ uint4 dq_int4x8(uint32_t v, float s, float zs) {
     const float a = __uint_as_float(0x4B000000u | ((v >> (8 * i)) & 0xFu)) - 8388608.f;
     const float b = __uint_as_float(0x4B000000u | ((v >> (8 * i + 4)) & 0xFu)) - 8388608.f;
     o[i] = pack_bf16x2(fmaf(a, s, -zs), fmaf(b, s, -zs));
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// The same in bf16x2 arithmetic, for zero points z in [-241, 128]: byte permutes
-// put codes 2i and 2i+1 into one word, 128 + q is formed exactly in the
-// mantissa, (128 + q) - (128 + z) = q - z is exact (|q - z| <= 256), and one
-// rounding multiply by s (s rounded to bf16) gives the value.
-// zz = bf16x2(128 + z), ss = bf16x2(s).
-__device__ __forceinline__ uint4 dq_int4x8_fast(uint32_t v, uint32_t zz, uint32_t ss) {
-  const uint32_t hi = v >> 4;
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // byte 0 <- byte i of v (code 2i in its low nibble), byte 2 <- byte i of v >> 4 (code 2i + 1)
-    const uint32_t w = nib_to_bf16x2(prmt(v, hi, 0x0400u + 0x0101u * (uint32_t)i));
-    o[i] = bf16x2_mul(bf16x2_sub(w, zz), ss);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -159,39 +110,25 @@ __device__ __forceinline__ uint4 dq_byte8(uint32_t lo, uint32_t hi, float s) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-__device__ __forceinline__ void conv_bar_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(32 * DQ_CONV_WARPS) : "memory");
-}
-
-// Wait for every load issued into a ring whose slots are flagged in `pending`
-// (slot i at parity bit i of `par`), so no copy lands after the CTA exits.
-__device__ __forceinline__ void drain_ring(uint32_t full0, uint32_t pending, uint32_t par, int stages,
-                                           int* status) {
-  for (int i = 0; i < stages; ++i)
-    if (pending & (1u << i)) bounded_wait(full0 + 8 * i, (par >> i) & 1, status, LK_ERR_TIMEOUT_DRAIN, nullptr);
-}
-
 template <int FMT, int MP>
-__global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
+__global__ void __launch_bounds__(DQ_THREADS, 2)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const DqArgs args) {
-  using C = DqCfg<FMT, MP>;
-  constexpr int RS = C::RAW_STAGES, AS = C::A_STAGES, XS = C::X_STAGES;
+  using C = DqCfg<MP>;
+  using RW = DqRaw<FMT>;
+  constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const uint32_t sA = smem_u32(smem);              // AS x 16 KB dequantised tiles
-  const uint32_t sX = sA + AS * C::A_BYTES;        // XS x X tiles
-  const uint32_t sR = sX + XS * C::X_BYTES;        // RS x raw weight tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AS * C::A_BYTES + XS * C::X_BYTES + RS * C::RAW_TILE);
-  const uint32_t rfull0 = smem_u32(bars);
-  const uint32_t rempty0 = rfull0 + 8 * RS;
-  const uint32_t afull0 = rempty0 + 8 * RS;
-  const uint32_t aempty0 = afull0 + 8 * AS;
-  const uint32_t xfull0 = aempty0 + 8 * AS;
-  const uint32_t xempty0 = xfull0 + 8 * XS;
-  const uint32_t accfull = xempty0 + 8 * XS;
+  const uint32_t sA = smem_u32(smem);                  // S x 16 KB dequantised tiles
+  const uint32_t sX = sA + S * C::A_BYTES;             // S x X tiles
+  const uint32_t sR = sX + S * C::X_BYTES;             // S x raw weight tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * (C::A_BYTES + C::X_BYTES + RW::TILE));
+  const uint32_t rawfull0 = smem_u32(bars);
+  const uint32_t full0 = rawfull0 + 8 * S;
+  const uint32_t empty0 = full0 + 8 * S;
+  const uint32_t accfull = empty0 + 8 * S;
   const uint32_t drain_bar = accfull + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -201,17 +138,10 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
   const int nk = min(args.k_split, args.K - k_begin) / DQ_BK;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < RS; ++i) {
-      mbar_init(rfull0 + 8 * i, 1);
-      mbar_init(rempty0 + 8 * i, DQ_CONV_WARPS);
-    }
-    for (int i = 0; i < AS; ++i) {
-      mbar_init(afull0 + 8 * i, DQ_CONV_WARPS);
-      mbar_init(aempty0 + 8 * i, 1);
-    }
-    for (int i = 0; i < XS; ++i) {
-      mbar_init(xfull0 + 8 * i, 1);
-      mbar_init(xempty0 + 8 * i, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(rawfull0 + 8 * s, 1);
+      mbar_init(full0 + 8 * s, 1 + DQ_CONV_WARPS);
+      mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accfull, 1);
     mbar_init(drain_bar, 1);
@@ -228,39 +158,30 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------- raw weight TMA
+    // ---------------------------------------------------------------- TMA
     if (lane == 0) {
-      uint32_t pending = 0, par = 0;
+      uint32_t pending = 0, parbits = 0;
+      bool ok = true;
       for (int kb = 0; kb < nk; ++kb) {
-        const int r = kb % RS;
-        const uint32_t ph = (uint32_t)(kb / RS) & 1;
-        if (!bounded_wait(rempty0 + 8 * r, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
-          drain_ring(rfull0, pending, par, RS, args.status);
+        const int s = kb % S;
+        const uint32_t ph = (uint32_t)(kb / S) & 1;
+        if (!bounded_wait(empty0 + 8 * s, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
+          ok = false;
           break;
         }
         const int k0 = k_begin + kb * DQ_BK;
-        mbar_expect_tx(rfull0 + 8 * r, C::RAW_TILE);
-        tma_load_2d(sR + r * C::RAW_TILE, &tmW, rfull0 + 8 * r, FMT == 2 ? k0 / 2 : k0, n0);
-        pending |= 1u << r;
-        par = (par & ~(1u << r)) | (ph << r);
+        mbar_expect_tx(rawfull0 + 8 * s, RW::TILE);
+        tma_load_2d(sR + s * RW::TILE, &tmW, rawfull0 + 8 * s, FMT == 2 ? k0 / 2 : k0, n0);
+        mbar_expect_tx(full0 + 8 * s, C::X_BYTES);
+        tma_load_2d(sX + s * C::X_BYTES, &tmX, full0 + 8 * s, k0, 0);
+        pending |= 1u << s;
+        parbits = (parbits & ~(1u << s)) | (ph << s);
       }
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------- activation TMA
-    if (lane == 0) {
-      uint32_t pending = 0, par = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int x = kb % XS;
-        const uint32_t ph = (uint32_t)(kb / XS) & 1;
-        if (!bounded_wait(xempty0 + 8 * x, ph ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY, abort_flag)) {
-          drain_ring(xfull0, pending, par, XS, args.status);
-          break;
-        }
-        mbar_expect_tx(xfull0 + 8 * x, C::X_BYTES);
-        tma_load_2d(sX + x * C::X_BYTES, &tmX, xfull0 + 8 * x, k_begin + kb * DQ_BK, 0);
-        pending |= 1u << x;
-        par = (par & ~(1u << x)) | (ph << x);
-      }
+      if (!ok)
+        for (int i = 0; i < S; ++i)
+          if (pending & (1u << i)) {
+            bounded_wait(rawfull0 + 8 * i, (parbits >> i) & 1, args.status, LK_ERR_TIMEOUT_DRAIN, nullptr);
+          }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -268,18 +189,18 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
       constexpr uint32_t idesc = make_idesc_bf16(DQ_BM, MP, false, false);
       bool ok = true;
       for (int kb = 0; kb < nk && ok; ++kb) {
-        const int s = kb % AS, x = kb % XS;
-        ok = bounded_wait(afull0 + 8 * s, (uint32_t)(kb / AS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag) &&
-             bounded_wait(xfull0 + 8 * x, (uint32_t)(kb / XS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
-        if (!ok) break;
+        const int s = kb % S;
+        if (!bounded_wait(full0 + 8 * s, (uint32_t)(kb / S) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t a = sA + s * C::A_BYTES, xb = sX + x * C::X_BYTES;
+        const uint32_t a = sA + s * C::A_BYTES, x = sX + s * C::X_BYTES;
 #pragma unroll
         for (int kk = 0; kk < DQ_BK / 16; ++kk)
-          tc_mma_f16(tmem, make_desc_sw128(a + kk * 32, 16, 1024), make_desc_sw128(xb + kk * 32, 16, 1024), idesc,
+          tc_mma_f16(tmem, make_desc_sw128(a + kk * 32, 16, 1024), make_desc_sw128(x + kk * 32, 16, 1024), idesc,
                      (kb | kk) != 0 ? 1u : 0u);
-        tc_commit(aempty0 + 8 * s);
-        tc_commit(xempty0 + 8 * x);
+        tc_commit(empty0 + 8 * s);
       }
       if (ok) tc_commit(accfull);
       tc_commit(drain_bar);
@@ -287,77 +208,45 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
     }
   } else {
     // ------------------------------------------------------- converters
-    const int t = threadIdx.x - 96;
+    const int t = threadIdx.x - 64;
     const int r = t & (DQ_BM - 1);  // weight row within the tile
     const int h = t >> 7;           // which 32 of the stage's 64 K values
     const int n = n0 + r;
     const bool row_ok = n < args.N;
     const int groups = FMT == 2 ? args.K / args.group : 1;
-    float s_cur = 0.f, z_cur = 0.f, s_nxt = 0.f, z_nxt = 0.f;
-    if (row_ok) {
-      if constexpr (FMT == 2) {
-        const int64_t gi = (int64_t)n * groups + (k_begin + h * 32) / args.group;
-        s_nxt = args.scale[gi];
-        z_nxt = args.zero[gi];
-      } else {
-        s_nxt = args.scale[n];
-      }
-    }
+    float s_cur = 0.f, z_cur = 0.f;
+    if (FMT != 2 && row_ok) s_cur = args.scale[n];
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
-      const int rs = kb % RS, s = kb % AS;
-      s_cur = s_nxt;
-      z_cur = z_nxt;
+      const int s = kb % S;
+      const int k0 = k_begin + kb * DQ_BK + h * 32;
       if constexpr (FMT == 2) {
-        // next stage's group scale and zero point, loaded a stage ahead
-        if (row_ok && kb + 1 < nk) {
-          const int64_t gi = (int64_t)n * groups + (k_begin + (kb + 1) * DQ_BK + h * 32) / args.group;
-          s_nxt = args.scale[gi];
-          z_nxt = args.zero[gi];
+        if (row_ok) {
+          const int g = k0 / args.group;
+          s_cur = args.scale[(int64_t)n * groups + g];
+          z_cur = args.zero[(int64_t)n * groups + g];
         }
       }
-      ok = bounded_wait(rfull0 + 8 * rs, (uint32_t)(kb / RS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
+      ok = bounded_wait(rawfull0 + 8 * s, (uint32_t)(kb / S) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
       }
-      const uint8_t* raw = smem + (sR - sA) + rs * C::RAW_TILE + r * C::RAW_ROW;
-      uint32_t w[FMT == 2 ? 4 : 8];
-      if constexpr (FMT == 2) {
-        const uint4 v = *reinterpret_cast<const uint4*>(raw + h * 16);
-        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
-      } else {
-        const uint4 v0 = *reinterpret_cast<const uint4*>(raw + h * 32);
-        const uint4 v1 = *reinterpret_cast<const uint4*>(raw + h * 32 + 16);
-        w[0] = v0.x, w[1] = v0.y, w[2] = v0.z, w[3] = v0.w, w[4] = v1.x, w[5] = v1.y, w[6] = v1.z, w[7] = v1.w;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(rempty0 + 8 * rs);  // the raw slot may be refilled
-      ok = bounded_wait(aempty0 + 8 * s, ((uint32_t)(kb / AS) & 1) ^ 1, args.status, LK_ERR_TIMEOUT_EMPTY,
-                        abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
+      const uint8_t* raw = smem + (sR - sA) + s * RW::TILE + r * RW::ROW_BYTES;
       uint8_t* a_tile = smem + s * C::A_BYTES;
       if constexpr (FMT == 2) {
-        if (z_cur >= -241.f && z_cur <= 128.f) {
-          const uint32_t zz = pack_bf16x2(128.f + z_cur, 128.f + z_cur);
-          const uint32_t ss = pack_bf16x2(s_cur, s_cur);
+        const uint4 v = row_ok ? *reinterpret_cast<const uint4*>(raw + h * 16) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const float zs = z_cur * s_cur;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 o = row_ok ? dq_int4x8_fast(w[c], zz, ss) : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(a_tile + dq_sw128(r, h * 4 + c)) = o;
-          }
-        } else {
-          const float zs = z_cur * s_cur;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 o = row_ok ? dq_int4x8(w[c], s_cur, zs) : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(a_tile + dq_sw128(r, h * 4 + c)) = o;
-          }
+        for (int c = 0; c < 4; ++c) {
+          const uint4 o = row_ok ? dq_int4x8(w[c], s_cur, zs) : make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(a_tile + dq_sw128(r, h * 4 + c)) = o;
         }
       } else {
+        const uint4 v0 = row_ok ? *reinterpret_cast<const uint4*>(raw + h * 32) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 v1 = row_ok ? *reinterpret_cast<const uint4*>(raw + h * 32 + 16) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint4 o = row_ok ? dq_byte8<FMT>(w[2 * c], w[2 * c + 1], s_cur) : make_uint4(0u, 0u, 0u, 0u);
@@ -366,17 +255,17 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
       }
       fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's async reads
       __syncwarp();
-      if (lane == 0) mbar_arrive(afull0 + 8 * s);
+      if (lane == 0) mbar_arrive(full0 + 8 * s);
     }
     // -------------------------------------------------------- epilogue
-    const bool split = gridDim.y > 1;
-    if (warp < 7) {  // warps 3..6: one per TMEM lane quarter
-      const int q = warp & 3;
+    if (warp < 6) {
+      const int q = warp & 3;  // TMEM lane quarter
       const int nrow = n0 + q * 32 + lane;
       ok = ok && bounded_wait(accfull, 0, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+        const bool split = gridDim.y > 1;
 #pragma unroll 1
         for (int c = 0; c < MP; c += (MP < 32 ? 16 : 32)) {
           float v[32];
@@ -410,26 +299,25 @@ __global__ void __launch_bounds__(DQ_THREADS, (DqCfg<FMT, MP>::MIN_BLOCKS))
         }
       }
     }
-    if (split && args.counters) {
+    if (gridDim.y > 1 && args.counters) {
       // Split-K: the last split of this weight tile to finish sums all the
       // partials in split order (deterministic) and writes Y (+ R).
-      conv_bar_sync();  // this CTA's partial stores precede the release below
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * DQ_CONV_WARPS) : "memory");  // partial stores first
       if (t == 0) {
         __threadfence();
         const int prev = atomicAdd(args.counters + blockIdx.x, 1);
         *last_flag = prev == (int)gridDim.y - 1;
       }
-      conv_bar_sync();
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * DQ_CONV_WARPS) : "memory");
       if (*last_flag) {
         __threadfence();
-        const int nn = n0 + r;
-        if (nn < args.N) {
+        if (n < args.N) {
           for (int m = h; m < args.M; m += 2) {
             float acc = 0.f;
             for (int sp = 0; sp < (int)gridDim.y; ++sp)
-              acc += __ldcg(args.partial + ((int64_t)sp * args.M + m) * args.N + nn);
-            if (args.r) acc += __bfloat162float(args.r[(int64_t)m * args.ldr + nn]);
-            args.y[(int64_t)m * args.ldy + nn] = __float2bfloat16(acc);
+              acc += __ldcg(args.partial + ((int64_t)sp * args.M + m) * args.N + n);
+            if (args.r) acc += __bfloat162float(args.r[(int64_t)m * args.ldr + n]);
+            args.y[(int64_t)m * args.ldy + n] = __float2bfloat16(acc);
           }
         }
         if (t == 0) args.counters[blockIdx.x] = 0;  // ready for the next launch
@@ -475,11 +363,17 @@ __global__ void dq_reduce_kernel(const float* __restrict__ partial, int splits, 
 
 template <int FMT, int MP>
 int launch_dq(const LkDqGemmDesc& d, int splits, int k_split, cudaStream_t s) {
-  using C = DqCfg<FMT, MP>;
+  using C = DqCfg<MP>;
+  using RW = DqRaw<FMT>;
   CUtensorMap tw, tx;
-  if (!make_tmap_2d(&tw, d.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.N, FMT == 2 ? d.K / 2 : d.K,
-                    FMT == 2 ? d.K / 2 : d.K, DQ_BM, C::RAW_ROW, CU_TENSOR_MAP_SWIZZLE_NONE))
+  if (FMT == 2) {
+    if (!make_tmap_2d(&tw, d.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.N, d.K / 2, d.K / 2, DQ_BM, RW::ROW_BYTES,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -1;
+  } else if (!make_tmap_2d(&tw, d.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.N, d.K, d.K, DQ_BM, RW::ROW_BYTES,
+                           CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return -1;
+  }
   if (!make_tmap_2d(&tx, d.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d.M, d.K, d.ldx, MP, DQ_BK)) return -1;
   DqArgs a{};
   a.M = d.M;
@@ -494,18 +388,22 @@ int launch_dq(const LkDqGemmDesc& d, int splits, int k_split, cudaStream_t s) {
   a.r = (const __nv_bfloat16*)d.r;
   a.ldr = d.ldr;
   a.partial = d.partial;
-  a.counters = splits > 1 ? d.counters : nullptr;
+  // the in-kernel reduction runs on one CTA per weight tile, so it only pays while
+  // the partials are few (measured: a gain at 1 row, a loss from 16); larger
+  // batches use the grid-wide reduction kernel
+  a.counters = (splits > 1 && d.M <= 4) ? d.counters : nullptr;
   a.status = d.status;
+  constexpr int SMEM = C::STAGES * (C::A_BYTES + C::X_BYTES + RW::TILE) + 3 * C::STAGES * 8 + 64 + 1024;
   auto k = dq_gemm_kernel<FMT, MP>;
   static uint64_t attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set & (1ull << dev))) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     attr_set |= 1ull << dev;
   }
   dim3 grid(cdiv(d.N, DQ_BM), splits);
-  k<<<grid, DQ_THREADS, C::SMEM, s>>>(tw, tx, a);
+  k<<<grid, DQ_THREADS, SMEM, s>>>(tw, tx, a);
   if (check_launch("dq_gemm")) return -1;
   if (splits > 1 && !a.counters) {
     const int64_t n4 = (int64_t)d.M * d.N / 4;
@@ -532,15 +430,12 @@ int launch_dq_fmt(const LkDqGemmDesc& d, int splits, int k_split, cudaStream_t s
 using namespace lk;
 
 extern "C" int lk_dq_gemm_splits(int M, int N, int K) {
-  // Split K until the grid fills the resident CTA slots (two per SM up to 128
-  // batch rows) without a second partial wave; every split keeps at least 4 K
-  // stages, and the fp32 partials (written and read back once) stay within
-  // about twice the int4 weight bytes.
+  // Split K until the grid fills the two resident CTA slots per SM without a
+  // second, partial wave; every split keeps at least 4 K stages.
   const int tiles = cdiv(N, DQ_BM);
-  const int slots = (M <= 128 ? 2 : 1) * num_sms();
-  int splits = std::max(1, slots / tiles);
+  int splits = std::max(1, 2 * num_sms() / tiles);
   splits = std::min(splits, std::max(1, K / (4 * DQ_BK)));
-  splits = std::min(splits, std::max(1, K / (8 * std::max(M, 1))));
+  (void)M;
   return splits;
 }
 

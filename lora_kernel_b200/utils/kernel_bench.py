@@ -135,50 +135,96 @@ def bench_mxf8(shapes, iters):
                           "peak_src": pk["src"]}), flush=True)
 
 
+def graph_time(calls, reps: int = 10) -> float:
+    """Median device milliseconds per call when `calls` (closures) replay back to
+    back from one CUDA graph: launch overhead is off the clock, as in the serving
+    engine's captured decode step.  Callers rotate the operands across enough
+    copies that one pass over them exceeds L2."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls:  # first use allocates workspaces outside the capture
+            c()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    g.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e) / len(calls))
+    times.sort()
+    del g
+    return times[len(times) // 2]
+
+
 def bench_decode(iters):
     """Serving kernels of the Llama 8B shape (TP=8 shard and the whole model on one
-    GPU): the int4 group-128 dequantising GEMV (K14 decode) and the paged decode
+    GPU): the int4 group-128 dequant GEMM (K14 decode) and the paged decode
     attention over an fp8 KV cache (K13), as fractions of the measured HBM copy
-    bandwidth (bytes: the int4 weights + scales once; the KV pages each sequence reads)."""
+    bandwidth (bytes: the int4 weights + scales once; the KV pages each sequence
+    reads).  Timed as CUDA-graph replays over rotating weight copies / KV block
+    sets (about 400 MB per pass, so L2 holds none of it)."""
     from lora_kernel_b200.ops import serving as SV
     pk = peaks()
     from lora_kernel_b200._ext import C
     for (N, K, tag) in [(6144, 4096, "qkv_tp1"), (28672, 4096, "gate_up_tp1"),
                         (4096, 14336, "down_tp1"), (3584, 4096, "gate_up_tp8"), (4096, 1792, "down_tp8")]:
         w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
-        qw = SV.QuantizedWeight(w, "int4", 128)
+        q0 = SV.QuantizedWeight(w, "int4", 128)
+        copies = max(2, min(48, -(-400 * 2 ** 20 // q0.nbytes())))
+        qws = [q0] + [SV.QuantizedWeight.from_parts("int4", 128, N, K, q0.q.clone(), q0.scale.clone(),
+                                                     q0.zero.clone()) for _ in range(copies - 1)]
+        del w
         for M in (1, 8, 16, 64, 128, 256):
             x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
             out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-            t = time_fn(lambda: qw.matmul_t(x, out=out), iters)
-            by = qw.nbytes() + M * K * 2 + M * N * 2
+            t = graph_time([(lambda qw=qw: qw.matmul_t(x, out=out)) for qw in qws], iters)
+            by = q0.nbytes() + M * K * 2 + M * N * 2
             rec = {"kernel": "int4_dq_gemm", "shape": tag, "M": M, "N": N, "K": K, "ms": round(t, 4),
                    "splits": C().dq_gemm_splits(M, N, K), "gbs": round(by / t / 1e6, 1),
-                   "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}
+                   "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3), "timing": "cuda graph"}
             if M <= 16:  # the CUDA-core GEMV it replaces
-                tg = time_fn(lambda: C().dequant_gemv(SV.QFMT["int4"], x, qw.q, qw.scale, qw.zero, N, K, 128, out),
-                             iters)
+                tg = graph_time([(lambda qw=qw: C().dequant_gemv(SV.QFMT["int4"], x, qw.q, qw.scale, qw.zero, N, K,
+                                                                 128, out)) for qw in qws], iters)
                 rec["cuda_core_gemv_ms"] = round(tg, 4)
             print(json.dumps(rec), flush=True)
-        del w, qw
+        del qws, q0
+        torch.cuda.empty_cache()
     # paged decode attention: Llama 8B, 32 q / 8 kv heads (TP=8: 4 / 1), head_dim 128, fp8 pages of 16
     for (nseq, ctx, Hq, Hkv) in [(256, 2048, 4, 1), (64, 2048, 32, 8), (256, 1024, 32, 8)]:
         Dh, bs = 128, 16
-        nblk = nseq * ((ctx + bs - 1) // bs)
+        per = nseq * ((ctx + bs - 1) // bs)  # blocks one call reads
+        pass_bytes = per * bs * Hkv * (2 * Dh + 8)
+        sets = max(2, min(16, -(-400 * 2 ** 20 // pass_bytes)))
+        nblk = sets * per
         kc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
         vc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
         ks = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
         vs = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
-        bt = torch.randperm(nblk, device="cuda", dtype=torch.int32).view(nseq, -1)
+        perm = torch.randperm(nblk, device="cuda", dtype=torch.int32)
+        bts = [perm[i * per:(i + 1) * per].view(nseq, -1).contiguous() for i in range(sets)]
         lens = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
         q = torch.randn(nseq, Hq * Dh, device="cuda").to(torch.bfloat16)
         out = torch.empty_like(q)
-        t = time_fn(lambda: SV.decode_attention(q, kc, vc, ks, vs, bt, lens, bs, Hq, Hkv, Dh, kv_dtype="fp8",
-                                                max_ctx=ctx, out=out), iters)
+        t = graph_time([(lambda bt=bt: SV.decode_attention(q, kc, vc, ks, vs, bt, lens, bs, Hq, Hkv, Dh,
+                                                           kv_dtype="fp8", max_ctx=ctx, out=out)) for bt in bts],
+                       iters)
         by = nseq * ctx * Hkv * (2 * Dh + 8) + 2 * q.numel() * 2
         print(json.dumps({"kernel": "decode_attention_fp8", "seqs": nseq, "ctx": ctx, "Hq": Hq, "Hkv": Hkv,
                           "Dh": Dh, "ms": round(t, 4), "gbs": round(by / t / 1e6, 1),
-                          "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3)}), flush=True)
+                          "frac_of_hbm": round(by / t / 1e6 / pk["hbm_gbs"], 3), "timing": "cuda graph"}),
+              flush=True)
+        del kc, vc, ks, vs
+        torch.cuda.empty_cache()
 
 
 def bench_norm(iters):
@@ -245,14 +291,38 @@ def attention_once(B=4, S=2048, Hq=32, Hkv=4, Dh=64):
     print(json.dumps({"kernel": "attention_once", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "Dh": Dh}), flush=True)
 
 
+def decode_once():
+    """One int4 dequant GEMM (Llama 8B qkv, 64 rows) and one paged fp8 decode
+    attention (256 sequences x 2048 tokens, 4 q / 1 kv heads) and nothing else
+    (the case ncu captures)."""
+    from lora_kernel_b200._ext import check_status
+    from lora_kernel_b200.ops import serving as SV
+    N, K, M = 6144, 4096, 64
+    qw = SV.QuantizedWeight((torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16), "int4", 128)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    qw.matmul_t(x)
+    nseq, ctx, Hq, Hkv, Dh, bs = 256, 2048, 4, 1, 128, 16
+    nblk = nseq * ctx // bs
+    kc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
+    vc = torch.randn(nblk * bs, Hkv, Dh, device="cuda").to(torch.float8_e4m3fn)
+    ks = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
+    vs = torch.full((nblk * bs, Hkv), 0.01, device="cuda")
+    bt = torch.randperm(nblk, device="cuda", dtype=torch.int32).view(nseq, -1)
+    lens = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+    q = torch.randn(nseq, Hq * Dh, device="cuda").to(torch.bfloat16)
+    SV.decode_attention(q, kc, vc, ks, vs, bt, lens, bs, Hq, Hkv, Dh, kv_dtype="fp8", max_ctx=ctx)
+    torch.cuda.synchronize()
+    check_status()
+    print(json.dumps({"kernel": "decode_once", "dq_gemm": [M, N, K], "decode": [nseq, ctx, Hq, Hkv, Dh]}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,norm")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--small", action="store_true", help="one small GEMM (for profiling)")
     ap.add_argument("--pair", type=int, default=-1,
-                    help="GEMMs on CTA pairs (cta_group::2, 256-row tiles): 1 on (tile width by wave fill), "
-                         "2 on with 256x256 tiles, 3 on with 256x128 tiles, 0 off, -1 the default")
+                    help="GEMMs on CTA pairs (cta_group::2, 256-row tiles): 1 on, 0 off, -1 the default")
     args = ap.parse_args()
     if args.pair >= 0:
         from lora_kernel_b200._ext import C
@@ -282,6 +352,8 @@ def main():
         bench_attention(args.iters)  # Llama 1.1B: B 4, S 2048, 32 / 4 heads, head_dim 64
     if "attn_once" in which:
         attention_once()
+    if "decode_once" in which:
+        decode_once()
     if "attn8b_once" in which:
         attention_once(B=2, S=4096, Hq=32, Hkv=8, Dh=128)
     if "attn8b" in which:
