@@ -93,9 +93,16 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
   }
   const uint32_t bar = sbase + C::OFF_BAR;
   // [0] q_full, [1..3] k_full, [4..6] k_empty, [7..9] v_full, [10..12] v_empty,
-  // [13,14] s_full[t], [15,16] p_full[t], [17,18] o_done[t], [19] drain
+  // [13,14] s_full[t], [15,16] p_full[t], [17,18] o_done[t], [19] drain, [20,21] s_free[t]
   const uint32_t q_full = bar, k_full = bar + 8, k_empty = bar + 32, v_full = bar + 56, v_empty = bar + 80,
-                 s_full = bar + 104, p_full = bar + 120, o_done = bar + 136, drain = bar + 152;
+                 s_full = bar + 104, p_full = bar + 120, o_done = bar + 136, drain = bar + 152,
+                 s_free = bar + 160;
+  // Head dim 64 (one thread per row): P gets its own TMEM columns instead of
+  // overwriting S, so S(j+1) is computed while the softmax still turns S(j) into
+  // P(j): TMEM = S_a, S_b (128 each) | P_a, P_b (64) | O_a, O_b (64).  Otherwise
+  // P is written over S: S_a, S_b | O_a, O_b (DH each).
+  constexpr bool SEP = DH == 64 && SPLIT == 1;
+  constexpr uint32_t P_COL = SEP ? 256 : 0, O_COL = SEP ? 384 : 256;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 192);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 196);
 
@@ -136,6 +143,7 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
       mbar_init(s_full + 8 * t, 1);
       mbar_init(p_full + 8 * t, 4 * SPLIT);
       mbar_init(o_done + 8 * t, 1);
+      mbar_init(s_free + 8 * t, 4 * SPLIT);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -231,10 +239,10 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
         tc_fence_after();
         const int st = u % NS;
         const uint32_t sv = sbase + C::OFF_V + st * C::QB;
-        const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + DH * t;
+        const uint32_t tP = SEP ? tmem + P_COL + 64 * t : tmem + 128 * t, tO = tmem + O_COL + DH * t;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P (bf16 pairs) from TMEM
-          tc_mma_f16_ta(tO, tS + kk * 8, make_desc_sw128(sv + kk * 2048, 16384, 1024), idesc_o,
+          tc_mma_f16_ta(tO, tP + kk * 8, make_desc_sw128(sv + kk * 2048, 16384, 1024), idesc_o,
                         (npv > 0 || kk > 0) ? 1u : 0u);
         tc_commit(o_done + 8 * t);
         ++npv;
@@ -249,7 +257,42 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
           tc_commit(k_empty);
         }
       }
-      for (int u = 0; u < nkv && ok; ++u) {
+      int n_s[2] = {active(0, j_lo) ? 1 : 0, active(1, j_lo) ? 1 : 0};  // S MMAs issued per tile
+      for (int u = 0; u < nkv && ok && SEP; ++u) {
+        // S_t(j+1) once the softmax of tile t has read S_t(j) (s_free), then the PVs
+        const int j = j_lo + u;
+        const int st = u % NS;
+        const bool nxt = u + 1 < nkv;
+        const int st1 = (u + 1) % NS;
+        if (nxt) {
+          if (!bounded_wait(k_full + 8 * st1, ((u + 1) / NS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!active(t, j + 1)) continue;
+            if (n_s[t] > 0)
+              ok = bounded_wait(s_free + 8 * t, (n_s[t] - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(t, u + 1);
+            ++n_s[t];
+          }
+          if (!ok) break;
+          tc_commit(k_empty + 8 * st1);
+        }
+        if (!bounded_wait(v_full + 8 * st, (u / NS) & 1, args.status, LK_ERR_TIMEOUT_FULL, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if ((active(0, j) && !issue_pv(0, u)) || (active(1, j) && !issue_pv(1, u))) {
+          ok = false;
+          break;
+        }
+        tc_commit(v_empty + 8 * st);
+      }
+      for (int u = 0; u < nkv && ok && !SEP; ++u) {
         const int j = j_lo + u;
         const int st = u % NS;
         const bool nxt = u + 1 < nkv;
@@ -298,7 +341,8 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
     const int ql = qt * 128 + r;
     const int q = q_off + ql;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + DH * t + lane_off;
+    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + O_COL + DH * t + lane_off;
+    const uint32_t tP = SEP ? tmem + P_COL + 64 * t + lane_off : tS;
     const int jbt = t == 0 ? jb0 : jb1;
     const int n_t = (t == 0 ? je0 : je1) - jbt;
     volatile unsigned long long* xch = reinterpret_cast<volatile unsigned long long*>(smem + C::OFF_XCH);
@@ -448,7 +492,8 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
     const int ql = qt * 128 + r;        // query row within the sequence
     const int q = q_off + ql;           // query position (keys are 0..Skv-1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + DH * t + lane_off;
+    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + O_COL + DH * t + lane_off;
+    const uint32_t tP = SEP ? tmem + P_COL + 64 * t + lane_off : tS;
     const int jbt = t == 0 ? jb0 : jb1;
     const int n_t = (t == 0 ? je0 : je1) - jbt;
     float m_used = -INFINITY, l_run = 0.f;
@@ -482,6 +527,12 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
       tmem_ld32(tS + 64, s2);
       tmem_ld32(tS + 96, s3);
       tc_wait_ld();
+      if constexpr (SEP) {
+        // S is in registers: the MMA warp may compute the next S into these columns
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free + 8 * t);
+      }
       mask_chunk(s0, 0);
       mask_chunk(s1, 1);
       mask_chunk(s2, 2);
@@ -503,6 +554,15 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
       // EMU of every 16 exponentials go to the FMA pipe on unmasked tiles (masked
       // -inf scores need the exact 0 of ex2)
       const bool emu = EMU > 0 && !need_mask;
+      if (SEP && jj > 0) {
+        // P(jj-1) in the P columns must have been read by its PV MMA
+        w_ok = bounded_wait(o_done + 8 * t, (jj - 1) & 1, args.status, LK_ERR_TIMEOUT_ACCUM, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       auto emit = [&](const uint32_t (&x)[32], int c) {
         uint32_t pk[16];
 #pragma unroll
@@ -519,7 +579,7 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
           r4[(e >> 1) & 3] += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(tS + c * 16, pk);
+        tmem_st16(tP + c * 16, pk);
       };
       emit(s0, 0);
       emit(s1, 1);

@@ -183,6 +183,94 @@ def bench_ops(cfg, B, S, iters, warmup, rank0):
     return results
 
 
+def bench_ops_mx(cfg, B, S, iters, warmup, rank0):
+    """The MX fp8 forms of the four fused ops as the MX TP step runs them
+    (quantise own rows -> device barrier -> gathered block-scaled GEMM; quantise
+    -> block-scaled GEMM storing into the owners' slots -> owner sum), forward
+    (e4m3 x e4m3) and data gradient (e5m2 x e4m3, the gathered gradient
+    dequantised for the weight gradient), against the bf16 fused ops."""
+    from .._ext import C
+    from ..ops import elementwise as E
+    from ..ops.fp8 import MXWeight
+    from ..parallel import tp as TP
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = dist.get_world_size(), dist.get_rank()
+    T = B * S
+    R, D = T // W, cfg.hidden_dim
+    ql, kvl, Fl = cfg.q_dim // W, cfg.kv_dim // W, cfg.ff_dim_padded // W
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(r)
+    bf = dict(dtype=torch.bfloat16, device=dev)
+
+    def rnd(*shape, s=0.02):
+        return (torch.randn(*shape, device=dev, generator=g) * s).to(torch.bfloat16)
+
+    w = {"qkv": rnd(ql + 2 * kvl, D), "gu": rnd(2 * Fl, D), "wo": rnd(D, ql), "down": rnd(D, Fl)}
+    w8 = {k: MXWeight(v, transpose=True) for k, v in w.items()}
+    a = {"wo": rnd(T, ql, s=1.0), "down": rnd(T, Fl, s=1.0)}
+    gamma = torch.ones(D, **bf)
+    resid = rnd(R, D, s=1.0)
+    out = {"qkv": torch.empty(T, ql + 2 * kvl, **bf), "gu": torch.empty(T, 2 * Fl, **bf)}
+    act = torch.empty(T, Fl, **bf)
+    hout = torch.empty(R, D, **bf)
+    rstd = torch.empty(R, dtype=torch.float32, device=dev)
+    x8 = torch.empty(T, D, dtype=torch.uint8, device=dev)
+    from ..ops.fp8 import sf_tile_bytes
+    xs = torch.empty(sf_tile_bytes(T, D), dtype=torch.uint8, device=dev)
+    dfull = torch.empty(T, D, **bf)
+    c = TP.TPComm(cfg, T, dev, comm="p2p")
+    rows = rnd(R, D, s=1.0)
+    c.stage_view(0, R, D).copy_(rows)
+    c.stage_view(1, R, D).copy_(rows)
+
+    def fwd_col(name, k):
+        def f():
+            c.publish_mx(k, c.stage_view(k, R, D))
+            c.barrier()
+            c.ag_gemm_mx(k, x8, xs, w8[name].q, w8[name].sf, out[name])
+            if name == "gu":
+                E.swiglu_fwd(out["gu"], act)
+        return f
+
+    def fwd_row(name, k):
+        def f():
+            c.gemm_rs_mx(k, a[name], w8[name].q, w8[name].sf)
+            c.rs_sum(k, hout, resid=resid, gamma=gamma, y=c.stage_view(1 - k, R, D), rstd=rstd)
+        return f
+
+    dx = {"wo": torch.empty(T, ql, **bf), "down": torch.empty(T, Fl, **bf)}
+    dy = {"qkv": rnd(T, ql + 2 * kvl, s=1.0), "gu": rnd(T, 2 * Fl, s=1.0)}
+
+    def bwd_ag(name, k):
+        # row-parallel layer: dX = gathered dY (e5m2) . W, dY dequantised for dW
+        def f():
+            c.publish_mx(k, c.stage_view(k, R, D), fmt=1)
+            c.barrier()
+            c.ag_gemm_mx(k, x8, xs, w8[name].qt, w8[name].sft, dx[name], a_fmt=1)
+            C().dequant_mx_rows(x8, 1, xs, dfull)
+        return f
+
+    def bwd_rs(name, k):
+        # column-parallel layer: partial dY . W reduce-scattered, summed by the owner
+        def f():
+            c.gemm_rs_mx(k, dy[name], w8[name].qt, w8[name].sft, a_fmt=1)
+            c.rs_sum(k, hout, resid=resid, gamma=None, y=None, rstd=None)
+        return f
+
+    res = {}
+    for name, fn in (("fwd.qkv", fwd_col("qkv", 0)), ("fwd.gu", fwd_col("gu", 1)),
+                     ("fwd.wo", fwd_row("wo", 0)), ("fwd.down", fwd_row("down", 1)),
+                     ("bwd.wo", bwd_ag("wo", 0)), ("bwd.down", bwd_ag("down", 1)),
+                     ("bwd.qkv", bwd_rs("qkv", 0)), ("bwd.gu", bwd_rs("gu", 1))):
+        res[name] = round(_time(fn, iters, warmup, flush), 4)
+    torch.cuda.synchronize()
+    dist.barrier()
+    del c
+    if rank0:
+        print(json.dumps({"mx_ops_ms": res, "shape": f"T={T} D={D} tp={W}"}), flush=True)
+    return res
+
+
 def bench_step(cfg, tc, B, S, accum, steps, warmup, comm, rank0, fp8=False):
     from ..parallel.tp import TPTrainer
     tr = TPTrainer(cfg, tc, micro_batch=B, seq_len=S, comm=comm, seed=tc.seed, fp8=fp8)
@@ -251,6 +339,8 @@ def main(argv=None):
         bench_diag(cfg, a.micro_batch, a.seq, a.iters, rank == 0)
     if a.ops:
         bench_ops(cfg, a.micro_batch, a.seq, a.iters, 3, rank == 0)
+        if "mx" in a.fp8.split(","):
+            bench_ops_mx(cfg, a.micro_batch, a.seq, a.iters, 3, rank == 0)
     if a.step:
         for comm in a.comm.split(","):
             bench_step(cfg, tc, a.micro_batch, a.seq, a.accum, a.steps, a.warmup, comm, rank == 0)
