@@ -51,7 +51,10 @@ constexpr int MX_SF_STAGE = MX_SFA + MX_SFB;
 constexpr int MX_EW = 8;                              // epilogue warps
 constexpr int MX_THREADS = 64 + 32 * MX_EW;
 constexpr int MX_AG_WARPS = 2;
-constexpr int MX_SMEM = MX_STAGES * (MX_STAGE + MX_SF_STAGE) + 256 + 1024;
+// peer-store staging of the reduce-scatter epilogue: 16 rows x 128 bytes per epilogue warp
+constexpr int MX_STG_OFF = MX_STAGES * (MX_STAGE + MX_SF_STAGE) + 256;
+constexpr int MX_STG_WARP = 16 * 128;
+constexpr int MX_SMEM = MX_STG_OFF + MX_EW * MX_STG_WARP + 1024;
 constexpr uint32_t MX_TMEM_COLS = 512;
 constexpr uint32_t MX_SF_COL0 = 256;  // scale columns: stage s at 256 + 16 s (A: +0..3, B: +8..15)
 
@@ -342,35 +345,68 @@ __global__ void __launch_bounds__(MX_THREADS + (AG ? 32 * MX_AG_WARPS : 0), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);  // the MMAs of the next tile may start
       const int row = tm * MX_BM + row_in_tile;
-      if (row < args.M) {
-        __nv_bfloat16* drow;
-        if constexpr (REMOTE) {
-          const int owner = row / args.rs_rows;
-          drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
-                 (int64_t)(args.rs_rank * args.rs_rows + row - owner * args.rs_rows) * args.ldd;
-        } else {
-          drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
+      // bf16 values of this lane's row, 16 chunks of 8 columns (+ residual)
+      uint4 pk[16];
+#pragma unroll
+      for (int v = 0; v < 16; ++v) {
+        const int col = tn * MX_BN + h * 128 + v * 8;
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v >> 2][(v & 3) * 8 + e]);
+        if (args.R && row < args.M && col < args.N) {
+          const uint4 rv = *reinterpret_cast<const uint4*>(args.R + (int64_t)row * args.ldr + col);
+          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x = unpack_bf16x2(rw[e]);
+            f[2 * e] += x.x;
+            f[2 * e + 1] += x.y;
+          }
         }
+        pk[v] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                           pack_bf16x2(f[6], f[7]));
+      }
+      if constexpr (REMOTE) {
+        // Rows go to their owners over NVLink.  Stored thread-per-row, each
+        // instruction would send 32 separate 16-byte pieces; instead 16 rows x
+        // 128 bytes at a time pass through this warp's shared-memory slot
+        // (16-byte chunks XOR-swizzled by row) and leave as whole 128-byte row
+        // segments, 8 lanes per row.
+        uint8_t* stg = smem + MX_STG_OFF + (warp - 2) * MX_STG_WARP;
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            if ((lane >> 4) == rh) {
+              const int rl = lane & 15;
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(stg + rl * 128 + ((c ^ (rl & 7)) << 4)) = pk[ch * 8 + c];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int rl = k * 4 + (lane >> 3), j = lane & 7;
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + rl * 128 + ((j ^ (rl & 7)) << 4));
+              const int grow = tm * MX_BM + q * 32 + rh * 16 + rl;
+              const int col = tn * MX_BN + h * 128 + ch * 64 + j * 8;
+              if (grow < args.M && col < args.N) {
+                const int owner = grow / args.rs_rows;
+                __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.rptrs[owner]) +
+                                      (int64_t)(args.rs_rank * args.rs_rows + grow - owner * args.rs_rows) * args.ldd;
+                *reinterpret_cast<uint4*>(drow + col) = val;
+              }
+            }
+            __syncwarp();
+          }
+        }
+      } else if (row < args.M) {
+        __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd;
 #pragma unroll
         for (int v = 0; v < 16; ++v) {
           const int col = tn * MX_BN + h * 128 + v * 8;
           if (col >= args.N) break;
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v >> 2][(v & 3) * 8 + e]);
-          if (args.R) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(args.R + (int64_t)row * args.ldr + col);
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 x = unpack_bf16x2(rw[e]);
-              f[2 * e] += x.x;
-              f[2 * e + 1] += x.y;
-            }
-          }
-          *reinterpret_cast<uint4*>(drow + col) =
-              make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                         pack_bf16x2(f[6], f[7]));
+          *reinterpret_cast<uint4*>(drow + col) = pk[v];
         }
       }
     }
