@@ -10,14 +10,15 @@
 //               shared by the two tiles (no multicast);
 //   warp 1      one thread issues S_t = Q_t K_j^T (M=128, N=128) into TMEM and,
 //               once P_t is back in TMEM, O_t += P_t V_j with P_t as the
-//               tensor-memory A operand; order PV_a(j), S_a(j+1), PV_b(j),
-//               S_b(j+1), so the tensor cores serve one softmax group while the
-//               other works (ping-pong);
+//               tensor-memory A operand; the tensor cores serve one softmax
+//               group while the other works (ping-pong).  Head dim 128: order
+//               PV_a(j), S_a(j+1), PV_b(j), S_b(j+1), P over S.  Head dim 64: P
+//               has its own columns, so S_t(j+1) goes out as soon as group t has
+//               read S_t(j), ahead of the PVs;
 //   warps 2..9  two softmax groups of 4 warps (tile a, tile b): thread = query
 //               row = TMEM lane; it reads its 128 scores, keeps the running
-//               max / sum in registers, writes P as bf16 pairs over the first 64
-//               columns of its S and rescales its O row in TMEM only when the
-//               max grew by more than 2^8.
+//               max / sum in registers, writes P as bf16 pairs and rescales its
+//               O row in TMEM only when the max grew by more than 2^8.
 // Replaces the reference's CPU attention: MultiHeadAttention::forward
 // (src/nn/transformer_blocks.cpp:50-97), FlashAttentionV2::forward
 // (include/nn/flash_attention.hpp:10-96, whose running-sum bug at :86 is not
@@ -73,7 +74,7 @@ struct FwdCfg {
   static constexpr int OFF_BAR = OFF_V + NS * QB;
   static constexpr int OFF_XCH = OFF_BAR + 256;  // split softmax: row-max exchange slots (4 KB)
   static constexpr int SMEM = OFF_XCH + 4096;
-  static constexpr int TMEM_COLS = 512;  // S_a, S_b (P in their first 64 columns), O_a, O_b
+  static constexpr int TMEM_COLS = 512;  // S_a, S_b, O_a, O_b (+ P_a, P_b at head dim 64)
   // TMA warp, MMA warp, two groups of 4 softmax warps (thread = query row) or,
   // with split rows, two groups of 8 (two threads per row, 64 keys each)
   static constexpr int threads(int split) { return 64 + 32 * 4 * split * 2; }
@@ -342,7 +343,6 @@ __global__ void __launch_bounds__(FwdCfg<DH>::threads(SPLIT), 1)
     const int q = q_off + ql;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + O_COL + DH * t + lane_off;
-    const uint32_t tP = SEP ? tmem + P_COL + 64 * t + lane_off : tS;
     const int jbt = t == 0 ? jb0 : jb1;
     const int n_t = (t == 0 ? je0 : je1) - jbt;
     volatile unsigned long long* xch = reinterpret_cast<volatile unsigned long long*>(smem + C::OFF_XCH);
